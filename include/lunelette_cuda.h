@@ -1,0 +1,119 @@
+/* Additive C-ABI of the B200 backend (lunelette_b200/liblunelette_cuda.so),
+ * next to the drop-in contract in metal.h. Nothing here is needed by callers of
+ * metal.h. Device pointers are CUDA global memory of the current device;
+ * `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ * All functions return 0 on success and -1 on invalid arguments or a CUDA
+ * launch error; they launch asynchronously on `stream` unless noted.
+ */
+#ifndef LUNELETTE_CUDA_H
+#define LUNELETTE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "metal.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------- kernel-level entry points (parity tests, microbenchmarks) */
+
+/* Set per-device kernel attributes; the model runtime does this itself. */
+int lunelette_cuda_kernels_init(void);
+
+/* out[i] = decode_e4m3(codes[i]) * scale, through the GEMV's in-register
+ * conversion. Replaces convert_fp8 (src/metal_kernels.metal:145-152); the
+ * decode itself restates st_f8_e4m3_to_f32 (src/safetensors.c:505-519). */
+int lunelette_cuda_fp8_decode(const uint8_t *codes, size_t n, float scale, float *out,
+    void *stream);
+
+/* y[t][r] = scale * sum_c decode(W[r][c]) * x[t][c]  (+ res[t][r] when res).
+ * W row-major [rows][cols] E4M3, cols % 16 == 0, cols <= 9216; any count.
+ * Replaces project_fp8 / project_fp8_lookup (src/metal_kernels.metal:154-177,
+ * 249-272) and, with res, the residual element op (:47-57). */
+int lunelette_cuda_gemv_fp8(const uint8_t *W, size_t rows, size_t cols, float scale,
+    const float *x, const float *res, size_t count, float *y, void *stream);
+
+/* Fused input RMSNorm + q/k/v projection + YaRN RoPE (+ query scale) + KV store
+ * for `count` tokens at positions length..length+count-1. W is [6144][3072]
+ * (q rows, then k, then v); scales = {q, k, v}; q_out [count][4096];
+ * kv_pool is the paged BF16 pool [layer][page][K|V][8][64][128].
+ * Replaces norm + 3x project_fp8 + 2x rope + the KV blit
+ * (src/metal_encode.m:129-153, src/metal_kernels.metal:29-78). */
+int lunelette_cuda_qkv_rope(const uint8_t *W, const float *scales, const float *gain,
+    const float *x, size_t count, size_t length, const float *rope_cos, const float *rope_sin,
+    float *q_out, uint16_t *kv_pool, const int *page_table, size_t num_pages, size_t layer,
+    void *stream);
+
+/* Fused post-attention RMSNorm + gate/up projection + SwiGLU. W is [18432][3072]
+ * with 128-row gate and up blocks alternating; act [count][9216].
+ * Replaces norm + 2x project_fp8 + SiLU + multiply (src/metal_encode.m:162-172). */
+int lunelette_cuda_gateup_swiglu(const uint8_t *W, float scale_gate, float scale_up,
+    const float *gain, const float *x, size_t count, float *act, void *stream);
+
+/* out = gain * (x * rsqrt(mean(x^2) + 1e-5)) per row (src/metal_kernels.metal:29-44). */
+int lunelette_cuda_rmsnorm(const float *gain, const float *x, size_t width, size_t count,
+    float *out, void *stream);
+
+/* Final RMSNorm + tied BF16 head over one hidden row: logits[rows]; *nonfinite
+ * (device int) is OR-ed with 1 when a logit is NaN/Inf. cols % 8 == 0.
+ * Replaces norm + project on the last row (src/metal_encode.m:204-210). */
+int lunelette_cuda_head_bf16(const uint16_t *W, size_t rows, size_t cols, const float *x,
+    const float *gain, float *logits, int *nonfinite, void *stream);
+
+/* Causal GQA attention (32 query heads over 8 KV heads, head dim 128) of `count`
+ * query rows at positions length..length+count-1 against KV layer `layer` of the
+ * paged pool; out [count][4096]. part_acc (slots*128 floats) and part_ml
+ * (slots*2 floats) are caller scratch, slots >= 32*count.
+ * Replaces scores + attend (src/metal_kernels.metal:81-132). */
+int lunelette_cuda_attention(const float *q, const uint16_t *kv_pool, const int *page_table,
+    size_t num_pages, size_t layer, size_t length, size_t count, float *out, float *part_acc,
+    float *part_ml, size_t slots, void *stream);
+
+/* ---------------- model-level test support */
+
+/* Keep every layer's output rows (which 0..25) and the final-norm rows (26) of
+ * the most recent call; host copy of count*3072 floats. Host-synchronous. */
+int lunelette_cuda_trace(lunelette_metal *context, int enable);
+int lunelette_cuda_trace_copy(lunelette_metal *context, int which, float *out, size_t floats);
+/* Device-resident greedy decode for throughput measurement: decode `first_token`
+ * and then keep feeding each step's argmax (strict '>', lowest id on ties, as
+ * src/generation.c:8-34) back on the GPU, `steps` steps in all, each one replay
+ * of a captured CUDA graph; no host round trip between steps. On success the
+ * sequence length grows by `steps`, tokens[0..steps) holds the generated ids,
+ * *milliseconds the CUDA-event time of the replays and *launches_per_step the
+ * kernel launches in one step. Host logits are not refreshed, so no endpoint is
+ * published (checkpoint_create needs another prefill/append/decode first). */
+int lunelette_cuda_decode_loop(lunelette_metal *context, int64_t first_token, size_t steps,
+    int64_t *tokens, float *milliseconds, int *launches_per_step, char *error, size_t capacity);
+
+/* Current sequence length (0 for NULL). */
+size_t lunelette_cuda_length(const lunelette_metal *context);
+
+/* The host YaRN table row the runtime uploads for `position` (128 cos, 128
+ * sin, split-half duplicated); -1 for position >= 262144. Restates
+ * lunelette_metal_yarn (src/metal_yarn.c:8-33). */
+int lunelette_cuda_yarn(uint32_t position, float *cosine, float *sine);
+
+/* Host-only admission of a checkpoint: the same name/dtype/shape/companion
+ * validation and FP8 payload admission that create() applies for `strategy`,
+ * without touching a GPU (src/metal_weights.c:51-231). */
+int lunelette_cuda_validate_checkpoint(const char *path, lunelette_metal_strategy strategy,
+    char *error, size_t capacity);
+
+/* ---------------- synthetic checkpoint */
+
+/* Write a seeded random-init checkpoint in the reference's tensor contract
+ * (3.8 GB): FP8 linears N(0,0.02) with BF16 per-tensor scales, BF16 embedding,
+ * unit norm gains. Host-only; deterministic for a seed. */
+int lunelette_cuda_synth_checkpoint(const char *path, uint64_t seed, char *error,
+    size_t capacity);
+/* FP32 -> E4M3FN code, round-to-nearest-even, saturating at +-448. */
+unsigned char lunelette_cuda_e4m3_encode(float value);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

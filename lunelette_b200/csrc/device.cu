@@ -1,0 +1,627 @@
+// CUDA layer of the B200 backend: device allocations, weight upload and the
+// per-call launch sequence that replaces the reference's command-buffer encoder
+// (src/metal_encode.m:124-215) and execute() commit/wait (src/metal_runtime.m:349-432).
+#include "device.h"
+#include "kernels.h"
+
+#include <new>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+using namespace lun;
+
+namespace {
+
+constexpr size_t kLayerQKV = (size_t)kQKVRows * kHidden;            // 18,874,368
+constexpr size_t kLayerO = (size_t)kHidden * kQuery;                // 12,582,912
+constexpr size_t kLayerGateUp = (size_t)kGateUpRows * kHidden;      // 56,623,104
+constexpr size_t kLayerDown = (size_t)kHidden * kInner;             // 28,311,552
+constexpr size_t kLayerBytes = kLayerQKV + kLayerO + kLayerGateUp + kLayerDown;
+constexpr size_t kStagingBytes = (size_t)32 << 20;
+constexpr size_t kPartSlots = 8192;  // (token, head, split) partial slots
+
+size_t pages_for(size_t context) { return (context + kPage - 1) / kPage; }
+
+}  // namespace
+
+struct lun_device {
+    int ordinal = -1;
+    int sm_count = 0;
+    size_t context = 0, block = 0;
+    int num_pages = 0;
+    cudaStream_t stream = nullptr;
+    uint8_t *w8 = nullptr;
+    float scales[kLayers][LUN_SLOT_COUNT] = {};
+    uint16_t *embedding = nullptr;
+    float *norms = nullptr, *final_norm = nullptr;
+    uint16_t *kv = nullptr;
+    int *page_table = nullptr;
+    float *rope_cos = nullptr, *rope_sin = nullptr;
+    StepParams *d_step = nullptr, *h_step = nullptr;
+    float *x = nullptr, *h = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
+    float *logits = nullptr, *part_acc = nullptr, *part_ml = nullptr;
+    int *d_flag = nullptr, *h_flag = nullptr;
+    float *h_logits = nullptr;
+    void *staging[2] = {nullptr, nullptr};
+    cudaEvent_t staging_done[2] = {nullptr, nullptr};
+    int trace = 0;
+    float *trace_buf = nullptr;
+    size_t trace_count = 0;
+    // device greedy decode loop (benchmarks): one captured step, replayed
+    int *d_tokens = nullptr, *d_partials = nullptr;
+    cudaGraphExec_t decode_graph = nullptr;
+    int launches_per_step = 0;
+    lun_device_bytes owned = {};
+};
+
+static int fail(char *error, size_t capacity, const char *what, cudaError_t e)
+{
+    if (error && capacity) snprintf(error, capacity, "%s: %s", what, cudaGetErrorString(e));
+    return -1;
+}
+
+extern "C" void lun_device_plan(size_t context, size_t block, lun_device_bytes *bytes)
+{
+    bytes->weight_bytes = (uint64_t)kLayerBytes * kLayers + (uint64_t)kVocab * kHidden * 2 +
+                          (uint64_t)(2 * kLayers + 1) * kHidden * 4;
+    bytes->kv_bytes = (uint64_t)kLayers * pages_for(context) * 2 * kPageKind * 2;
+    uint64_t scratch = 0;
+    scratch += sizeof(StepParams);
+    scratch += (uint64_t)block * (2 * kHidden + 2 * kQuery + kInner) * 4;  // x h q attn act
+    scratch += (uint64_t)kVocab * 4;                                       // logits
+    scratch += (uint64_t)kPartSlots * (kHeadDim + 2) * 4;                  // attention partials
+    scratch += (uint64_t)context * kHeadDim * 2 * 4;                       // rope tables
+    scratch += (uint64_t)pages_for(context) * 4 + 4;                        // page table + flag
+    bytes->scratch_bytes = scratch;
+}
+
+template <class T>
+static cudaError_t dalloc(T **p, size_t bytes, uint64_t *counter)
+{
+    cudaError_t e = cudaMalloc((void **)p, bytes);
+    if (e == cudaSuccess && counter) *counter += bytes;
+    return e;
+}
+
+extern "C" lun_device *lun_device_create(size_t context, size_t block, char *error, size_t capacity)
+{
+    lun_device_bytes plan;
+    lun_device_plan(context, block, &plan);
+    int ordinal = 0;
+    cudaError_t e = cudaGetDevice(&ordinal);
+    if (e != cudaSuccess) {
+        fail(error, capacity, "CUDA device unavailable", e);
+        return nullptr;
+    }
+    cudaDeviceProp prop;
+    e = cudaGetDeviceProperties(&prop, ordinal);
+    if (e != cudaSuccess) {
+        fail(error, capacity, "CUDA device query failed", e);
+        return nullptr;
+    }
+    if (prop.major != 10) {
+        if (error && capacity)
+            snprintf(error, capacity, "requires an sm_100 (B200) device, found sm_%d%d", prop.major,
+                     prop.minor);
+        return nullptr;
+    }
+    size_t free_bytes = 0, total_bytes = 0;
+    e = cudaMemGetInfo(&free_bytes, &total_bytes);
+    uint64_t need = plan.weight_bytes + plan.kv_bytes + plan.scratch_bytes + ((uint64_t)1 << 30);
+    if (e != cudaSuccess || free_bytes < need) {
+        if (error && capacity)
+            snprintf(error, capacity, "insufficient device memory: need %llu bytes, %zu free",
+                     (unsigned long long)need, free_bytes);
+        return nullptr;
+    }
+    lun_device *d = new (std::nothrow) lun_device();
+    if (!d) {
+        if (error && capacity) snprintf(error, capacity, "device context allocation failed");
+        return nullptr;
+    }
+    d->ordinal = ordinal;
+    d->sm_count = prop.multiProcessorCount;
+    d->context = context;
+    d->block = block;
+    d->num_pages = (int)pages_for(context);
+    uint64_t *wc = &d->owned.weight_bytes, *kc = &d->owned.kv_bytes, *sc = &d->owned.scratch_bytes;
+    const char *what = "stream";
+    if ((e = cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking)) != cudaSuccess) goto bad;
+    what = "weights";
+    if ((e = dalloc(&d->w8, kLayerBytes * kLayers, wc)) != cudaSuccess ||
+        (e = dalloc(&d->embedding, (size_t)kVocab * kHidden * 2, wc)) != cudaSuccess ||
+        (e = dalloc(&d->norms, (size_t)(2 * kLayers + 1) * kHidden * 4, wc)) != cudaSuccess)
+        goto bad;
+    d->final_norm = d->norms + (size_t)2 * kLayers * kHidden;
+    what = "KV cache";
+    if ((e = dalloc(&d->kv, (size_t)kLayers * d->num_pages * 2 * kPageKind * 2, kc)) != cudaSuccess)
+        goto bad;
+    what = "scratch";
+    if ((e = dalloc(&d->d_step, sizeof(StepParams), sc)) != cudaSuccess ||
+        (e = dalloc(&d->x, block * kHidden * 4, sc)) != cudaSuccess ||
+        (e = dalloc(&d->h, block * kHidden * 4, sc)) != cudaSuccess ||
+        (e = dalloc(&d->q, block * kQuery * 4, sc)) != cudaSuccess ||
+        (e = dalloc(&d->attn, block * kQuery * 4, sc)) != cudaSuccess ||
+        (e = dalloc(&d->act, block * kInner * 4, sc)) != cudaSuccess ||
+        (e = dalloc(&d->logits, (size_t)kVocab * 4, sc)) != cudaSuccess ||
+        (e = dalloc(&d->part_acc, kPartSlots * kHeadDim * 4, sc)) != cudaSuccess ||
+        (e = dalloc(&d->part_ml, kPartSlots * 2 * 4, sc)) != cudaSuccess ||
+        (e = dalloc(&d->rope_cos, context * kHeadDim * 4, sc)) != cudaSuccess ||
+        (e = dalloc(&d->rope_sin, context * kHeadDim * 4, sc)) != cudaSuccess ||
+        (e = dalloc(&d->page_table, (size_t)d->num_pages * 4, sc)) != cudaSuccess ||
+        (e = dalloc(&d->d_flag, 4, sc)) != cudaSuccess)
+        goto bad;
+    what = "pinned host buffers";
+    if ((e = cudaMallocHost((void **)&d->h_step, sizeof(StepParams))) != cudaSuccess ||
+        (e = cudaMallocHost((void **)&d->h_logits, (size_t)kVocab * 4)) != cudaSuccess ||
+        (e = cudaMallocHost((void **)&d->h_flag, 4)) != cudaSuccess ||
+        (e = cudaMallocHost(&d->staging[0], kStagingBytes)) != cudaSuccess ||
+        (e = cudaMallocHost(&d->staging[1], kStagingBytes)) != cudaSuccess ||
+        (e = cudaEventCreateWithFlags(&d->staging_done[0], cudaEventDisableTiming)) != cudaSuccess ||
+        (e = cudaEventCreateWithFlags(&d->staging_done[1], cudaEventDisableTiming)) != cudaSuccess)
+        goto bad;
+    {
+        // single-sequence context: identity page table
+        int *table = (int *)malloc((size_t)d->num_pages * sizeof(int));
+        if (!table) {
+            e = cudaErrorMemoryAllocation;
+            goto bad;
+        }
+        for (int i = 0; i < d->num_pages; i++) table[i] = i;
+        e = cudaMemcpy(d->page_table, table, (size_t)d->num_pages * 4, cudaMemcpyHostToDevice);
+        free(table);
+        if (e != cudaSuccess) goto bad;
+    }
+    what = "kernel setup";
+    if ((e = lun_kernels_ensure()) != cudaSuccess) goto bad;
+    return d;
+bad:
+    fail(error, capacity, what, e);
+    lun_device_destroy(d);
+    return nullptr;
+}
+
+extern "C" void lun_device_destroy(lun_device *d)
+{
+    if (!d) return;
+    if (d->stream) cudaStreamSynchronize(d->stream);
+    cudaFree(d->w8);
+    cudaFree(d->embedding);
+    cudaFree(d->norms);
+    cudaFree(d->kv);
+    cudaFree(d->d_step);
+    cudaFree(d->x);
+    cudaFree(d->h);
+    cudaFree(d->q);
+    cudaFree(d->attn);
+    cudaFree(d->act);
+    cudaFree(d->logits);
+    cudaFree(d->part_acc);
+    cudaFree(d->part_ml);
+    cudaFree(d->rope_cos);
+    cudaFree(d->rope_sin);
+    cudaFree(d->page_table);
+    cudaFree(d->d_flag);
+    cudaFree(d->trace_buf);
+    cudaFree(d->d_tokens);
+    cudaFree(d->d_partials);
+    if (d->decode_graph) cudaGraphExecDestroy(d->decode_graph);
+    cudaFreeHost(d->h_step);
+    cudaFreeHost(d->h_logits);
+    cudaFreeHost(d->h_flag);
+    cudaFreeHost(d->staging[0]);
+    cudaFreeHost(d->staging[1]);
+    for (int i = 0; i < 2; i++)
+        if (d->staging_done[i]) cudaEventDestroy(d->staging_done[i]);
+    if (d->stream) cudaStreamDestroy(d->stream);
+    delete d;
+}
+
+extern "C" int lun_device_ordinal(const lun_device *d) { return d->ordinal; }
+
+extern "C" void lun_device_bytes_owned(const lun_device *d, lun_device_bytes *bytes)
+{
+    *bytes = d->owned;
+}
+
+extern "C" size_t lun_device_staging_bytes(void) { return kStagingBytes; }
+
+extern "C" void *lun_device_staging(lun_device *d, int index) { return d->staging[index & 1]; }
+
+extern "C" int lun_device_staging_wait(lun_device *d, int index)
+{
+    return cudaEventSynchronize(d->staging_done[index & 1]) == cudaSuccess ? 0 : -1;
+}
+
+static uint8_t *layer_base(lun_device *d, int layer) { return d->w8 + (size_t)layer * kLayerBytes; }
+
+extern "C" int lun_device_upload_linear(lun_device *d, int index, int layer, int slot, size_t rows,
+                                        size_t cols, float scale)
+{
+    const uint8_t *src = (const uint8_t *)d->staging[index & 1];
+    uint8_t *base = layer_base(d, layer);
+    cudaError_t e;
+    d->scales[layer][slot] = scale;
+    switch (slot) {
+    case LUN_SLOT_Q:
+    case LUN_SLOT_K:
+    case LUN_SLOT_V: {
+        size_t row0 = slot == LUN_SLOT_Q ? 0 : (slot == LUN_SLOT_K ? kQuery : kQuery + kKV);
+        e = cudaMemcpyAsync(base + row0 * kHidden, src, rows * cols, cudaMemcpyHostToDevice, d->stream);
+        break;
+    }
+    case LUN_SLOT_O:
+        e = cudaMemcpyAsync(base + kLayerQKV, src, rows * cols, cudaMemcpyHostToDevice, d->stream);
+        break;
+    case LUN_SLOT_GATE:
+    case LUN_SLOT_UP: {
+        // 128-row blocks interleave gate and up: block b of gate -> 2b, of up -> 2b+1
+        size_t block_bytes = (size_t)128 * cols;
+        uint8_t *dst = base + kLayerQKV + kLayerO + (slot == LUN_SLOT_UP ? block_bytes : 0);
+        e = cudaMemcpy2DAsync(dst, 2 * block_bytes, src, block_bytes, block_bytes, rows / 128,
+                              cudaMemcpyHostToDevice, d->stream);
+        break;
+    }
+    case LUN_SLOT_DOWN:
+        e = cudaMemcpyAsync(base + kLayerQKV + kLayerO + kLayerGateUp, src, rows * cols,
+                            cudaMemcpyHostToDevice, d->stream);
+        break;
+    default:
+        return -1;
+    }
+    if (e != cudaSuccess) return -1;
+    return cudaEventRecord(d->staging_done[index & 1], d->stream) == cudaSuccess ? 0 : -1;
+}
+
+extern "C" int lun_device_upload_embedding(lun_device *d, int index, size_t offset, size_t bytes)
+{
+    if (cudaMemcpyAsync((uint8_t *)d->embedding + offset, d->staging[index & 1], bytes,
+                        cudaMemcpyHostToDevice, d->stream) != cudaSuccess)
+        return -1;
+    return cudaEventRecord(d->staging_done[index & 1], d->stream) == cudaSuccess ? 0 : -1;
+}
+
+extern "C" int lun_device_upload_norms(lun_device *d, const float *norms, const float *final_norm)
+{
+    if (cudaMemcpy(d->norms, norms, (size_t)2 * kLayers * kHidden * 4, cudaMemcpyHostToDevice) !=
+        cudaSuccess)
+        return -1;
+    return cudaMemcpy(d->final_norm, final_norm, (size_t)kHidden * 4, cudaMemcpyHostToDevice) ==
+                   cudaSuccess
+               ? 0
+               : -1;
+}
+
+extern "C" int lun_device_upload_rope(lun_device *d, const float *cosine, const float *sine,
+                                      size_t positions)
+{
+    if (positions > d->context) return -1;
+    if (cudaMemcpy(d->rope_cos, cosine, positions * kHeadDim * 4, cudaMemcpyHostToDevice) !=
+        cudaSuccess)
+        return -1;
+    return cudaMemcpy(d->rope_sin, sine, positions * kHeadDim * 4, cudaMemcpyHostToDevice) ==
+                   cudaSuccess
+               ? 0
+               : -1;
+}
+
+extern "C" int lun_device_upload_finish(lun_device *d, char *error, size_t capacity)
+{
+    cudaError_t e = cudaStreamSynchronize(d->stream);
+    if (e != cudaSuccess) return fail(error, capacity, "weight upload failed", e);
+    return 0;
+}
+
+extern "C" float *lun_device_host_logits(lun_device *d) { return d->h_logits; }
+
+// ---------------------------------------------------------------------------
+
+static GemvParams layer_gemv(lun_device *d, int layer, int which)
+{
+    GemvParams p;
+    memset(&p, 0, sizeof p);
+    uint8_t *base = layer_base(d, layer);
+    const float *s = d->scales[layer];
+    p.step = d->d_step;
+    p.kv = d->kv;
+    p.page_table = d->page_table;
+    p.num_pages = d->num_pages;
+    p.layer = layer;
+    p.rope_cos = d->rope_cos;
+    p.rope_sin = d->rope_sin;
+    p.bound[0] = p.bound[1] = 1 << 30;
+    p.scale[0] = p.scale[1] = p.scale[2] = 1.0f;
+    switch (which) {
+    case 0:  // qkv with input norm
+        p.W = base;
+        p.rows = kQKVRows;
+        p.cols = kHidden;
+        p.gain = d->norms + (size_t)(2 * layer) * kHidden;
+        p.scale[0] = s[LUN_SLOT_Q];
+        p.scale[1] = s[LUN_SLOT_K];
+        p.scale[2] = s[LUN_SLOT_V];
+        p.bound[0] = kQuery;
+        p.bound[1] = kQuery + kKV;
+        break;
+    case 1:  // o + residual
+        p.W = base + kLayerQKV;
+        p.rows = kHidden;
+        p.cols = kQuery;
+        p.scale[0] = s[LUN_SLOT_O];
+        break;
+    case 2:  // gate/up with post-attention norm, SwiGLU
+        p.W = base + kLayerQKV + kLayerO;
+        p.rows = kGateUpRows;
+        p.cols = kHidden;
+        p.gain = d->norms + (size_t)(2 * layer + 1) * kHidden;
+        p.scale[0] = s[LUN_SLOT_GATE];
+        p.scale[1] = s[LUN_SLOT_UP];
+        break;
+    default:  // down + residual
+        p.W = base + kLayerQKV + kLayerO + kLayerGateUp;
+        p.rows = kHidden;
+        p.cols = kInner;
+        p.scale[0] = s[LUN_SLOT_DOWN];
+        break;
+    }
+    return p;
+}
+
+// Launch `which` projection of `layer` over all `count` tokens in groups of <= 4.
+static cudaError_t run_projection(lun_device *d, int layer, int which, int count)
+{
+    static const int epi[4] = {kEpiQKV, kEpiResidual, kEpiSwiGLU, kEpiResidual};
+    for (int t0 = 0; t0 < count; t0 += 4) {
+        int m = count - t0 < 4 ? count - t0 : 4;
+        GemvParams p = layer_gemv(d, layer, which);
+        p.token_offset = t0;
+        switch (which) {
+        case 0:
+            p.x = d->x + (size_t)t0 * kHidden;
+            p.x_stride = kHidden;
+            p.y = d->q + (size_t)t0 * kQuery;
+            p.y_stride = kQuery;
+            break;
+        case 1:
+            p.x = d->attn + (size_t)t0 * kQuery;
+            p.x_stride = kQuery;
+            p.res = d->x + (size_t)t0 * kHidden;
+            p.res_stride = kHidden;
+            p.y = d->h + (size_t)t0 * kHidden;
+            p.y_stride = kHidden;
+            break;
+        case 2:
+            p.x = d->h + (size_t)t0 * kHidden;
+            p.x_stride = kHidden;
+            p.y = d->act + (size_t)t0 * kInner;
+            p.y_stride = kInner;
+            break;
+        default:
+            p.x = d->act + (size_t)t0 * kInner;
+            p.x_stride = kInner;
+            p.res = d->h + (size_t)t0 * kHidden;
+            p.res_stride = kHidden;
+            p.y = d->x + (size_t)t0 * kHidden;
+            p.y_stride = kHidden;
+            break;
+        }
+        cudaError_t e = lun_launch_gemv(p, m, epi[which], d->sm_count, d->stream);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+static cudaError_t run_attention(lun_device *d, int layer, int count, size_t length,
+                                 bool fixed_plan = false)
+{
+    AttnParams a;
+    memset(&a, 0, sizeof a);
+    a.q = d->q;
+    a.kv = d->kv;
+    a.page_table = d->page_table;
+    a.num_pages = d->num_pages;
+    a.layer = layer;
+    a.step = d->d_step;
+    a.out = d->attn;
+    a.part_acc = d->part_acc;
+    a.part_ml = d->part_ml;
+    // A captured graph serves every length, so it plans for the full context;
+    // splits past the current length find no positions and contribute nothing.
+    int total = fixed_plan ? (int)d->context : (int)(length + count);
+    lun_attention_plan(&a, total, count, d->sm_count, (int)kPartSlots);
+    return lun_launch_attention(a, count, d->stream);
+}
+
+// One decode step reading length/ids from d_step, ending with device greedy
+// selection that advances d_step; capturable.
+static cudaError_t enqueue_decode_step(lun_device *d, int *launches)
+{
+    int n = 0;
+    embed_kernel<<<1, 256, 0, d->stream>>>(d->embedding, d->d_step, d->x, 1);
+    cudaError_t e = cudaGetLastError();
+    n++;
+    for (int layer = 0; e == cudaSuccess && layer < kLayers; layer++) {
+        if ((e = run_projection(d, layer, 0, 1)) != cudaSuccess ||
+            (e = run_attention(d, layer, 1, 0, true)) != cudaSuccess ||
+            (e = run_projection(d, layer, 1, 1)) != cudaSuccess ||
+            (e = run_projection(d, layer, 2, 1)) != cudaSuccess ||
+            (e = run_projection(d, layer, 3, 1)) != cudaSuccess)
+            break;
+        AttnParams a;
+        lun_attention_plan(&a, (int)d->context, 1, d->sm_count, (int)kPartSlots);
+        n += 5 + (a.splits > 1 ? 1 : 0);
+    }
+    if (e != cudaSuccess) return e;
+    HeadParams hp;
+    hp.W = d->embedding;
+    hp.rows = kVocab;
+    hp.cols = kHidden;
+    hp.x = d->x;
+    hp.gain = d->final_norm;
+    hp.logits = d->logits;
+    hp.nonfinite = d->d_flag;
+    if ((e = lun_launch_head(hp, d->sm_count, d->stream)) != cudaSuccess) return e;
+    if ((e = lun_launch_greedy(d->logits, kVocab, d->d_partials, d->d_step, d->d_tokens,
+                               d->stream)) != cudaSuccess)
+        return e;
+    *launches = n + 3;
+    return cudaSuccess;
+}
+
+extern "C" int lun_device_decode_loop(lun_device *d, int64_t first_token, size_t length,
+                                      size_t steps, int64_t *tokens, float *milliseconds,
+                                      int *launches, char *error, size_t capacity)
+{
+    cudaError_t e = cudaSetDevice(d->ordinal);
+    if (e != cudaSuccess) return fail(error, capacity, "cudaSetDevice", e);
+    if (!steps || length == 0 || length + steps > d->context || first_token < 0 ||
+        first_token >= kVocab) {
+        if (error && capacity) snprintf(error, capacity, "decode loop: bad length/steps/token");
+        return -1;
+    }
+    const char *what = "decode loop setup";
+    cudaEvent_t start = nullptr, stop = nullptr;
+    int *host_tokens = nullptr;
+    if (!d->d_tokens) {
+        if ((e = cudaMalloc((void **)&d->d_tokens, d->context * sizeof(int))) != cudaSuccess ||
+            (e = cudaMalloc((void **)&d->d_partials, 2 * kArgmaxBlocks * sizeof(int))) != cudaSuccess)
+            goto bad;
+    }
+    if (!d->decode_graph) {
+        what = "decode graph capture";
+        cudaGraph_t graph = nullptr;
+        if ((e = cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeRelaxed)) != cudaSuccess)
+            goto bad;
+        cudaError_t ce = enqueue_decode_step(d, &d->launches_per_step);
+        e = cudaStreamEndCapture(d->stream, &graph);
+        if (ce != cudaSuccess) e = ce;
+        if (e == cudaSuccess) e = cudaGraphInstantiate(&d->decode_graph, graph, 0);
+        if (graph) cudaGraphDestroy(graph);
+        if (e != cudaSuccess) {
+            d->decode_graph = nullptr;
+            goto bad;
+        }
+    }
+    what = "decode loop";
+    d->h_step->length = (int)length;
+    d->h_step->count = 1;
+    d->h_step->generated = 0;
+    d->h_step->ids[0] = (int)first_token;
+    if ((e = cudaEventCreate(&start)) != cudaSuccess || (e = cudaEventCreate(&stop)) != cudaSuccess ||
+        (e = cudaMemcpyAsync(d->d_step, d->h_step, sizeof(StepParams), cudaMemcpyHostToDevice,
+                             d->stream)) != cudaSuccess ||
+        (e = cudaEventRecord(start, d->stream)) != cudaSuccess)
+        goto bad;
+    for (size_t s = 0; s < steps; s++)
+        if ((e = cudaGraphLaunch(d->decode_graph, d->stream)) != cudaSuccess) goto bad;
+    if ((e = cudaEventRecord(stop, d->stream)) != cudaSuccess ||
+        (e = cudaStreamSynchronize(d->stream)) != cudaSuccess)
+        goto bad;
+    if (milliseconds && (e = cudaEventElapsedTime(milliseconds, start, stop)) != cudaSuccess) goto bad;
+    host_tokens = (int *)malloc(steps * sizeof(int));
+    if (!host_tokens) {
+        e = cudaErrorMemoryAllocation;
+        goto bad;
+    }
+    if ((e = cudaMemcpy(host_tokens, d->d_tokens, steps * sizeof(int), cudaMemcpyDeviceToHost)) !=
+        cudaSuccess)
+        goto bad;
+    for (size_t s = 0; s < steps; s++) tokens[s] = host_tokens[s];
+    free(host_tokens);
+    if (launches) *launches = d->launches_per_step;
+    cudaEventDestroy(start);
+    cudaEventDestroy(stop);
+    return 0;
+bad:
+    free(host_tokens);
+    if (start) cudaEventDestroy(start);
+    if (stop) cudaEventDestroy(stop);
+    return fail(error, capacity, what, e);
+}
+
+extern "C" int lun_device_run(lun_device *d, const int64_t *ids, size_t count, size_t length,
+                              const float **logits, int *nonfinite, char *error, size_t capacity)
+{
+    cudaError_t e = cudaSetDevice(d->ordinal);
+    if (e != cudaSuccess) return fail(error, capacity, "cudaSetDevice", e);
+    if (!count || count > d->block || length + count > d->context) {
+        if (error && capacity) snprintf(error, capacity, "device run: block/context exceeded");
+        return -1;
+    }
+    d->h_step->length = (int)length;
+    d->h_step->count = (int)count;
+    for (size_t i = 0; i < count; i++) d->h_step->ids[i] = (int)ids[i];
+    const int n = (int)count;
+    const char *what = "step upload";
+    if ((e = cudaMemcpyAsync(d->d_step, d->h_step, sizeof(StepParams), cudaMemcpyHostToDevice,
+                             d->stream)) != cudaSuccess ||
+        (e = cudaMemsetAsync(d->d_flag, 0, 4, d->stream)) != cudaSuccess)
+        goto bad;
+    what = "kernel launch";
+    embed_kernel<<<n, 256, 0, d->stream>>>(d->embedding, d->d_step, d->x, n);
+    if ((e = cudaGetLastError()) != cudaSuccess) goto bad;
+    for (int layer = 0; layer < kLayers; layer++) {
+        if ((e = run_projection(d, layer, 0, n)) != cudaSuccess ||
+            (e = run_attention(d, layer, n, length)) != cudaSuccess ||
+            (e = run_projection(d, layer, 1, n)) != cudaSuccess ||
+            (e = run_projection(d, layer, 2, n)) != cudaSuccess ||
+            (e = run_projection(d, layer, 3, n)) != cudaSuccess)
+            goto bad;
+        if (d->trace && (e = cudaMemcpyAsync(d->trace_buf + (size_t)layer * count * kHidden, d->x,
+                                             count * kHidden * 4, cudaMemcpyDeviceToDevice,
+                                             d->stream)) != cudaSuccess)
+            goto bad;
+    }
+    if (d->trace) {
+        if ((e = lun_launch_rmsnorm(d->final_norm, d->x, d->trace_buf + (size_t)kLayers * count * kHidden,
+                                    kHidden, n, d->stream)) != cudaSuccess)
+            goto bad;
+        d->trace_count = count;
+    }
+    {
+        HeadParams hp;
+        hp.W = d->embedding;
+        hp.rows = kVocab;
+        hp.cols = kHidden;
+        hp.x = d->x + (size_t)(count - 1) * kHidden;
+        hp.gain = d->final_norm;
+        hp.logits = d->logits;
+        hp.nonfinite = d->d_flag;
+        if ((e = lun_launch_head(hp, d->sm_count, d->stream)) != cudaSuccess) goto bad;
+    }
+    what = "logits download";
+    if ((e = cudaMemcpyAsync(d->h_logits, d->logits, (size_t)kVocab * 4, cudaMemcpyDeviceToHost,
+                             d->stream)) != cudaSuccess ||
+        (e = cudaMemcpyAsync(d->h_flag, d->d_flag, 4, cudaMemcpyDeviceToHost, d->stream)) !=
+            cudaSuccess)
+        goto bad;
+    what = "execution";
+    if ((e = cudaStreamSynchronize(d->stream)) != cudaSuccess) goto bad;
+    *logits = d->h_logits;
+    *nonfinite = *d->h_flag != 0;
+    return 0;
+bad:
+    return fail(error, capacity, what, e);
+}
+
+extern "C" int lun_device_trace(lun_device *d, int enable)
+{
+    if (enable && !d->trace_buf) {
+        if (cudaMalloc((void **)&d->trace_buf, (size_t)(kLayers + 1) * d->block * kHidden * 4) !=
+            cudaSuccess)
+            return -1;
+    }
+    d->trace = enable != 0;
+    return 0;
+}
+
+extern "C" int lun_device_trace_copy(lun_device *d, int which, float *out, size_t floats)
+{
+    if (!d->trace_buf || which < 0 || which > kLayers || floats != d->trace_count * kHidden)
+        return -1;
+    return cudaMemcpy(out, d->trace_buf + (size_t)which * d->trace_count * kHidden, floats * 4,
+                      cudaMemcpyDeviceToHost) == cudaSuccess
+               ? 0
+               : -1;
+}

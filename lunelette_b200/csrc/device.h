@@ -1,0 +1,77 @@
+/* Thin C-ABI between the plain-C host runtime (runtime.c) and the CUDA layer
+ * (device.cu). Plain pointers and sizes only. This is the seam that takes the
+ * place of the reference's Objective-C owner and encoder
+ * (src/metal_internal.h:412-457, src/metal_encode.m). */
+#ifndef LUN_DEVICE_H
+#define LUN_DEVICE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct lun_device lun_device;
+
+/* Linear slots within a layer (storage order on the device). */
+enum { LUN_SLOT_Q, LUN_SLOT_K, LUN_SLOT_V, LUN_SLOT_O, LUN_SLOT_GATE, LUN_SLOT_UP,
+    LUN_SLOT_DOWN, LUN_SLOT_COUNT };
+
+/* Byte sizes of what lun_device_create would allocate for a (context, block)
+ * profile; used for preflight and get_memory. */
+typedef struct {
+    uint64_t weight_bytes, scratch_bytes, kv_bytes;
+} lun_device_bytes;
+void lun_device_plan(size_t context, size_t block, lun_device_bytes *bytes);
+
+/* Allocates weights, KV, scratch, tables and pinned staging on the current
+ * device. Fails (NULL + diagnostic) before allocating when cudaMemGetInfo shows
+ * too little free memory. */
+lun_device *lun_device_create(size_t context, size_t block, char *error, size_t capacity);
+void lun_device_destroy(lun_device *d);
+int lun_device_ordinal(const lun_device *d);
+void lun_device_bytes_owned(const lun_device *d, lun_device_bytes *bytes);
+
+/* Upload path. Two pinned staging buffers of lun_device_staging_bytes() each;
+ * wait before refilling a buffer that an earlier upload may still read. */
+size_t lun_device_staging_bytes(void);
+void *lun_device_staging(lun_device *d, int index);
+int lun_device_staging_wait(lun_device *d, int index);
+/* A whole FP8 tensor from staging buffer `index` (rows*cols bytes). */
+int lun_device_upload_linear(lun_device *d, int index, int layer, int slot, size_t rows,
+    size_t cols, float scale);
+/* Bytes [offset, offset+bytes) of the BF16 embedding from staging buffer `index`. */
+int lun_device_upload_embedding(lun_device *d, int index, size_t offset, size_t bytes);
+/* norms: [26][2][3072] FP32 (input, post-attention), final: [3072] FP32. */
+int lun_device_upload_norms(lun_device *d, const float *norms, const float *final_norm);
+int lun_device_upload_rope(lun_device *d, const float *cosine, const float *sine,
+    size_t positions);
+int lun_device_upload_finish(lun_device *d, char *error, size_t capacity);
+
+/* One prefill/append/decode block at sequence length `length`. On success
+ * *logits points to the context's pinned host copy of the 131072 logits and
+ * *nonfinite is 1 when the device saw a NaN/Inf logit. */
+int lun_device_run(lun_device *d, const int64_t *ids, size_t count, size_t length,
+    const float **logits, int *nonfinite, char *error, size_t capacity);
+float *lun_device_host_logits(lun_device *d);
+
+/* Device-resident greedy decode: `steps` decode steps starting from token
+ * `first_token` at sequence length `length` (a valid prefix must already be in
+ * the KV cache), each step one replay of a captured CUDA graph whose last
+ * kernels pick the argmax and feed it to the next step. Writes the generated
+ * ids, the CUDA-event time of all replays and the kernel launches per step. */
+int lun_device_decode_loop(lun_device *d, int64_t first_token, size_t length, size_t steps,
+    int64_t *tokens, float *milliseconds, int *launches, char *error, size_t capacity);
+
+/* Test support: keep each layer's output hidden rows and the final-norm rows of
+ * the most recent call (eager launches while enabled). */
+int lun_device_trace(lun_device *d, int enable);
+/* which: 0..25 = layer output [count][3072]; 26 = final norm [count][3072]. */
+int lun_device_trace_copy(lun_device *d, int which, float *out, size_t floats);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,182 @@
+// Kernel-level C-ABI: the product kernels on caller-provided device pointers,
+// so tests can check each one against the CPU oracle on awkward shapes.
+// Return 0 on success, -1 on invalid arguments or a CUDA launch error.
+#include "kernels.h"
+
+#include <string.h>
+
+#define LUN_API extern "C" __attribute__((visibility("default")))
+
+using namespace lun;
+
+static int sm_count_of_current()
+{
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+    return sms;
+}
+
+static int ok(cudaError_t e) { return e == cudaSuccess ? 0 : -1; }
+
+LUN_API int lunelette_cuda_kernels_init(void) { return ok(lun_kernels_init()); }
+
+LUN_API int lunelette_cuda_fp8_decode(const uint8_t *codes, size_t n, float scale, float *out,
+                                      void *stream)
+{
+    if ((!codes || !out) && n) return -1;
+    return ok(lun_launch_fp8_decode(codes, n, scale, out, (cudaStream_t)stream));
+}
+
+static GemvParams plain(const uint8_t *W, size_t rows, size_t cols, float scale)
+{
+    GemvParams p;
+    memset(&p, 0, sizeof p);
+    p.W = W;
+    p.rows = (int)rows;
+    p.cols = (int)cols;
+    p.scale[0] = p.scale[1] = p.scale[2] = scale;
+    p.bound[0] = p.bound[1] = 1 << 30;
+    p.length = 0;
+    return p;
+}
+
+// y[t][r] = scale * sum_c decode(W[r][c]) * x[t][c] (+ res[t][r]), any count
+// (processed in groups of 4 rows of x). cols must be a multiple of 16.
+LUN_API int lunelette_cuda_gemv_fp8(const uint8_t *W, size_t rows, size_t cols, float scale,
+                                    const float *x, const float *res, size_t count, float *y,
+                                    void *stream)
+{
+    if (!W || !x || !y || !rows || !cols || (cols % 16) || !count || rows > (1u << 28) ||
+        cols * 4 * 4 > 4 * 9216 * 4)
+        return -1;
+    int sms = sm_count_of_current();
+    for (size_t t0 = 0; t0 < count; t0 += 4) {
+        int m = (int)(count - t0 < 4 ? count - t0 : 4);
+        GemvParams p = plain(W, rows, cols, scale);
+        p.x = x + t0 * cols;
+        p.x_stride = (int)cols;
+        p.y = y + t0 * rows;
+        p.y_stride = (int)rows;
+        if (res) {
+            p.res = res + t0 * rows;
+            p.res_stride = (int)rows;
+        }
+        if (lun_launch_gemv(p, m, res ? kEpiResidual : kEpiStore, sms, (cudaStream_t)stream) !=
+            cudaSuccess)
+            return -1;
+    }
+    return 0;
+}
+
+// Fused input-norm + q/k/v projection + RoPE (+query scale) + KV store for
+// tokens at positions length..length+count-1. W is [6144][3072] (q|k|v rows).
+LUN_API int lunelette_cuda_qkv_rope(const uint8_t *W, const float *scales, const float *gain,
+                                    const float *x, size_t count, size_t length,
+                                    const float *rope_cos, const float *rope_sin, float *q_out,
+                                    uint16_t *kv_pool, const int *page_table, size_t num_pages,
+                                    size_t layer, void *stream)
+{
+    if (!W || !scales || !gain || !x || !count || !rope_cos || !rope_sin || !q_out || !kv_pool ||
+        !page_table || !num_pages || length + count > num_pages * kPage)
+        return -1;
+    int sms = sm_count_of_current();
+    for (size_t t0 = 0; t0 < count; t0 += 4) {
+        int m = (int)(count - t0 < 4 ? count - t0 : 4);
+        GemvParams p = plain(W, kQKVRows, kHidden, 1.0f);
+        p.scale[0] = scales[0];
+        p.scale[1] = scales[1];
+        p.scale[2] = scales[2];
+        p.bound[0] = kQuery;
+        p.bound[1] = kQuery + kKV;
+        p.gain = gain;
+        p.x = x + t0 * kHidden;
+        p.x_stride = kHidden;
+        p.y = q_out + t0 * kQuery;
+        p.y_stride = kQuery;
+        p.length = (int)length;
+        p.token_offset = (int)t0;
+        p.rope_cos = rope_cos;
+        p.rope_sin = rope_sin;
+        p.kv = kv_pool;
+        p.page_table = page_table;
+        p.num_pages = (int)num_pages;
+        p.layer = (int)layer;
+        if (lun_launch_gemv(p, m, kEpiQKV, sms, (cudaStream_t)stream) != cudaSuccess) return -1;
+    }
+    return 0;
+}
+
+// Fused post-attention norm + interleaved gate/up projection + SwiGLU.
+// W is [18432][3072] with 128-row gate and up blocks alternating.
+LUN_API int lunelette_cuda_gateup_swiglu(const uint8_t *W, float scale_gate, float scale_up,
+                                         const float *gain, const float *x, size_t count,
+                                         float *act, void *stream)
+{
+    if (!W || !gain || !x || !act || !count) return -1;
+    int sms = sm_count_of_current();
+    for (size_t t0 = 0; t0 < count; t0 += 4) {
+        int m = (int)(count - t0 < 4 ? count - t0 : 4);
+        GemvParams p = plain(W, kGateUpRows, kHidden, 1.0f);
+        p.scale[0] = scale_gate;
+        p.scale[1] = scale_up;
+        p.gain = gain;
+        p.x = x + t0 * kHidden;
+        p.x_stride = kHidden;
+        p.y = act + t0 * kInner;
+        p.y_stride = kInner;
+        if (lun_launch_gemv(p, m, kEpiSwiGLU, sms, (cudaStream_t)stream) != cudaSuccess) return -1;
+    }
+    return 0;
+}
+
+LUN_API int lunelette_cuda_rmsnorm(const float *gain, const float *x, size_t width, size_t count,
+                                   float *out, void *stream)
+{
+    if (!gain || !x || !out || !width || !count) return -1;
+    return ok(lun_launch_rmsnorm(gain, x, out, (int)width, (int)count, (cudaStream_t)stream));
+}
+
+// Final norm + BF16 head over one hidden row; *nonfinite (device int) is OR-ed.
+LUN_API int lunelette_cuda_head_bf16(const uint16_t *W, size_t rows, size_t cols, const float *x,
+                                     const float *gain, float *logits, int *nonfinite, void *stream)
+{
+    if (!W || !x || !gain || !logits || !nonfinite || !rows || !cols || (cols % 8) ||
+        cols > 9216)
+        return -1;
+    HeadParams p;
+    p.W = W;
+    p.rows = (int)rows;
+    p.cols = (int)cols;
+    p.x = x;
+    p.gain = gain;
+    p.logits = logits;
+    p.nonfinite = nonfinite;
+    return ok(lun_launch_head(p, sm_count_of_current(), (cudaStream_t)stream));
+}
+
+// Causal GQA attention of `count` query rows (positions length..length+count-1)
+// over KV layer `layer` of a paged BF16 pool. part_acc/part_ml are caller scratch
+// of (slots*128) and (slots*2) floats; slots >= count*32.
+LUN_API int lunelette_cuda_attention(const float *q, const uint16_t *kv_pool, const int *page_table,
+                                     size_t num_pages, size_t layer, size_t length, size_t count,
+                                     float *out, float *part_acc, float *part_ml, size_t slots,
+                                     void *stream)
+{
+    if (!q || !kv_pool || !page_table || !out || !count || !part_acc || !part_ml ||
+        slots < count * kQueryHeads || length + count > num_pages * kPage)
+        return -1;
+    AttnParams a;
+    memset(&a, 0, sizeof a);
+    a.q = q;
+    a.kv = kv_pool;
+    a.page_table = page_table;
+    a.num_pages = (int)num_pages;
+    a.layer = (int)layer;
+    a.length = (int)length;
+    a.out = out;
+    a.part_acc = part_acc;
+    a.part_ml = part_ml;
+    lun_attention_plan(&a, (int)(length + count), (int)count, sm_count_of_current(), (int)slots);
+    return ok(lun_launch_attention(a, (int)count, (cudaStream_t)stream));
+}

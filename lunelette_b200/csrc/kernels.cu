@@ -1,0 +1,258 @@
+#include "kernels.h"
+
+using namespace lun;
+
+namespace {
+
+constexpr int kMaxGemvSmem = 4 * kInner * 4;  // 4 rows x 9216 FP32
+
+template <int M, int EPI>
+cudaError_t setup_one()
+{
+    return cudaFuncSetAttribute(gemv_fp8_kernel<M, EPI>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxGemvSmem);
+}
+
+template <int EPI>
+cudaError_t setup_epi()
+{
+    cudaError_t e;
+    if ((e = setup_one<1, EPI>()) != cudaSuccess) return e;
+    if ((e = setup_one<2, EPI>()) != cudaSuccess) return e;
+    if ((e = setup_one<3, EPI>()) != cudaSuccess) return e;
+    return setup_one<4, EPI>();
+}
+
+template <int M, int EPI>
+cudaError_t launch_one(const GemvParams &p, int sm_count, cudaStream_t stream)
+{
+    const size_t smem = (size_t)M * p.cols * 4;
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_fp8_kernel<M, EPI>,
+                                                                  256, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) per_sm = 1;
+    int groups = (p.rows + 3) / 4;
+    int blocks = (groups + 7) / 8;
+    int limit = sm_count * per_sm;
+    if (blocks > limit) blocks = limit;
+    gemv_fp8_kernel<M, EPI><<<blocks, 256, smem, stream>>>(p);
+    return cudaGetLastError();
+}
+
+template <int EPI>
+cudaError_t launch_epi(const GemvParams &p, int m, int sm_count, cudaStream_t stream)
+{
+    switch (m) {
+    case 1: return launch_one<1, EPI>(p, sm_count, stream);
+    case 2: return launch_one<2, EPI>(p, sm_count, stream);
+    case 3: return launch_one<3, EPI>(p, sm_count, stream);
+    case 4: return launch_one<4, EPI>(p, sm_count, stream);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+__global__ void rmsnorm_kernel(const float *gain, const float *x, float *out, int width)
+{
+    __shared__ float red[32];
+    const float *xr = x + (size_t)blockIdx.x * width;
+    float ss = 0.0f;
+    for (int c = threadIdx.x; c < width; c += blockDim.x) ss += xr[c] * xr[c];
+    ss = block_sum(ss, red);
+    float rs = rsqrtf(ss / (float)width + kNormEps);
+    for (int c = threadIdx.x; c < width; c += blockDim.x)
+        out[(size_t)blockIdx.x * width + c] = gain[c] * (xr[c] * rs);
+}
+
+__global__ void fp8_decode_kernel(const uint8_t *codes, size_t n, float scale, float *out)
+{
+    size_t i = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) * 2;
+    if (i >= n) return;
+    uint32_t two = codes[i] | (i + 1 < n ? (uint32_t)codes[i + 1] << 8 : 0u);
+    float2 v = e4m3x2_to_float2(two);
+    out[i] = v.x * scale;
+    if (i + 1 < n) out[i + 1] = v.y * scale;
+}
+
+// Better of two (value, index) candidates: larger value, then lower index.
+__device__ __forceinline__ void better(float &v, int &i, float v2, int i2)
+{
+    if (v2 > v || (v2 == v && i2 < i)) {
+        v = v2;
+        i = i2;
+    }
+}
+
+__device__ __forceinline__ void block_best(float &v, int &i)
+{
+    __shared__ float sv[32];
+    __shared__ int si[32];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+        int i2 = __shfl_xor_sync(0xffffffffu, i, o);
+        better(v, i, v2, i2);
+    }
+    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sv[warp] = v;
+        si[warp] = i;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int warps = blockDim.x >> 5;
+        v = lane < warps ? sv[lane] : -INFINITY;
+        i = lane < warps ? si[lane] : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+            int i2 = __shfl_xor_sync(0xffffffffu, i, o);
+            better(v, i, v2, i2);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) argmax_partial_kernel(const float *logits, int n, int *partials)
+{
+    int per = (n + gridDim.x - 1) / gridDim.x;
+    int begin = blockIdx.x * per, end = min(begin + per, n);
+    float v = -INFINITY;
+    int i = 0x7fffffff;
+    for (int k = begin + threadIdx.x; k < end; k += blockDim.x) better(v, i, logits[k], k);
+    block_best(v, i);
+    if (threadIdx.x == 0) {
+        partials[2 * blockIdx.x] = __float_as_int(v);
+        partials[2 * blockIdx.x + 1] = i;
+    }
+}
+
+__global__ void __launch_bounds__(256) argmax_final_kernel(const int *partials, int blocks,
+                                                           StepParams *step, int *tokens)
+{
+    float v = -INFINITY;
+    int i = 0x7fffffff;
+    for (int k = threadIdx.x; k < blocks; k += blockDim.x)
+        better(v, i, __int_as_float(partials[2 * k]), partials[2 * k + 1]);
+    block_best(v, i);
+    if (threadIdx.x == 0) {
+        int id = i == 0x7fffffff ? 0 : i;
+        step->ids[0] = id;
+        tokens[step->generated] = id;
+        step->generated += 1;
+        step->length += 1;
+    }
+}
+
+}  // namespace
+
+cudaError_t lun_launch_greedy(const float *logits, int n, int *partials, StepParams *step,
+                              int *tokens, cudaStream_t stream)
+{
+    argmax_partial_kernel<<<kArgmaxBlocks, 256, 0, stream>>>(logits, n, partials);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    argmax_final_kernel<<<1, 256, 0, stream>>>(partials, kArgmaxBlocks, step, tokens);
+    return cudaGetLastError();
+}
+
+// Function attributes apply to the current device; calling again is cheap.
+cudaError_t lun_kernels_init()
+{
+    cudaError_t e;
+    if ((e = setup_epi<kEpiStore>()) != cudaSuccess) return e;
+    if ((e = setup_epi<kEpiResidual>()) != cudaSuccess) return e;
+    if ((e = setup_epi<kEpiQKV>()) != cudaSuccess) return e;
+    return setup_epi<kEpiSwiGLU>();
+}
+
+// Dynamic shared memory above 48 KB needs a per-device opt-in; do it on first use.
+cudaError_t lun_kernels_ensure()
+{
+    static bool done[128] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 128 && done[dev]) return cudaSuccess;
+    e = lun_kernels_init();
+    if (e == cudaSuccess && dev >= 0 && dev < 128) done[dev] = true;
+    return e;
+}
+
+cudaError_t lun_launch_gemv(const GemvParams &p, int m, int epilogue, int sm_count,
+                            cudaStream_t stream)
+{
+    if (p.cols <= 0 || (p.cols & 15) || p.rows <= 0 || (size_t)m * p.cols * 4 > (size_t)kMaxGemvSmem)
+        return cudaErrorInvalidValue;
+    cudaError_t ie = lun_kernels_ensure();
+    if (ie != cudaSuccess) return ie;
+    switch (epilogue) {
+    case kEpiStore: return launch_epi<kEpiStore>(p, m, sm_count, stream);
+    case kEpiResidual: return launch_epi<kEpiResidual>(p, m, sm_count, stream);
+    case kEpiQKV: return launch_epi<kEpiQKV>(p, m, sm_count, stream);
+    case kEpiSwiGLU: return launch_epi<kEpiSwiGLU>(p, m, sm_count, stream);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t lun_launch_head(const HeadParams &p, int sm_count, cudaStream_t stream)
+{
+    if (p.cols <= 0 || (p.cols & 7)) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)p.cols * 4;
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, head_bf16_kernel, 256, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) per_sm = 1;
+    int groups = (p.rows + 3) / 4;
+    int blocks = (groups + 7) / 8;
+    if (blocks > sm_count * per_sm) blocks = sm_count * per_sm;
+    head_bf16_kernel<<<blocks, 256, smem, stream>>>(p);
+    return cudaGetLastError();
+}
+
+void lun_attention_plan(AttnParams *a, int total, int count, int sm_count, int slots)
+{
+    int wanted = (2 * sm_count + 8 * count - 1) / (8 * count);  // splits per (token, kv head)
+    if (wanted < 1) wanted = 1;
+    int split_len = (total + wanted - 1) / wanted;
+    split_len = (split_len + kTile - 1) / kTile * kTile;
+    if (split_len < kTile) split_len = kTile;
+    int splits = (total + split_len - 1) / split_len;
+    int cap = slots / (count * kQueryHeads);
+    if (cap < 1) cap = 1;
+    if (splits > cap) {
+        splits = cap;
+        split_len = (total + splits - 1) / splits;
+        split_len = (split_len + kTile - 1) / kTile * kTile;
+        splits = (total + split_len - 1) / split_len;
+    }
+    a->split_len = split_len;
+    a->splits = splits;
+}
+
+cudaError_t lun_launch_attention(const AttnParams &a, int count, cudaStream_t stream)
+{
+    if (a.splits < 1 || a.split_len < kTile || (a.split_len % kTile)) return cudaErrorInvalidValue;
+    dim3 grid(a.splits, kKVHeads, count);
+    attention_split_kernel<<<grid, 128, 0, stream>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || a.splits == 1) return e;
+    attention_combine_kernel<<<dim3(kQueryHeads, count), 128, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t lun_launch_rmsnorm(const float *gain, const float *x, float *out, int width, int count,
+                               cudaStream_t stream)
+{
+    if (width <= 0 || count <= 0) return cudaErrorInvalidValue;
+    rmsnorm_kernel<<<count, 256, 0, stream>>>(gain, x, out, width);
+    return cudaGetLastError();
+}
+
+cudaError_t lun_launch_fp8_decode(const uint8_t *codes, size_t n, float scale, float *out,
+                                  cudaStream_t stream)
+{
+    if (!n) return cudaSuccess;
+    size_t pairs = (n + 1) / 2;
+    fp8_decode_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0, stream>>>(codes, n, scale, out);
+    return cudaGetLastError();
+}

@@ -1,0 +1,36 @@
+// Launch helpers shared by the runtime (device.cu) and the kernel-level C-ABI
+// (kernel_api.cu). C++ only; nothing here crosses the public boundary.
+#pragma once
+#include "attention.cuh"
+#include "gemv.cuh"
+
+// One-time per-process kernel attribute setup (dynamic shared memory limits).
+cudaError_t lun_kernels_init();
+// lun_kernels_init() once per device (cached); call before any graph capture.
+cudaError_t lun_kernels_ensure();
+
+// GEMV family: m token rows (1..4), epilogue kind lun::GemvEpilogue.
+cudaError_t lun_launch_gemv(const lun::GemvParams &p, int m, int epilogue, int sm_count,
+                            cudaStream_t stream);
+cudaError_t lun_launch_head(const lun::HeadParams &p, int sm_count, cudaStream_t stream);
+
+// Choose split_len/splits for `total` positions (max over the call's tokens),
+// `count` query tokens and `slots` partial slots available.
+void lun_attention_plan(lun::AttnParams *a, int total, int count, int sm_count, int slots);
+cudaError_t lun_launch_attention(const lun::AttnParams &a, int count, cudaStream_t stream);
+
+// out[t][c] = gain[c] * (x[t][c] * rsqrt(mean(x[t]^2) + eps))
+cudaError_t lun_launch_rmsnorm(const float *gain, const float *x, float *out, int width, int count,
+                               cudaStream_t stream);
+
+// Greedy selection on the device for the decode loop: argmax over logits with
+// the reference's rule (strict '>', lowest id wins ties, src/generation.c:8-34);
+// writes the id into step->ids[0], appends it to tokens[step->generated++] and
+// advances step->length by one. partials: 2*kArgmaxBlocks ints.
+constexpr int kArgmaxBlocks = 256;
+cudaError_t lun_launch_greedy(const float *logits, int n, int *partials, lun::StepParams *step,
+                              int *tokens, cudaStream_t stream);
+
+// FP8 codes -> FP32 * scale through the same in-register conversion as the GEMV.
+cudaError_t lun_launch_fp8_decode(const uint8_t *codes, size_t n, float scale, float *out,
+                                  cudaStream_t stream);

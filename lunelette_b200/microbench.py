@@ -1,0 +1,105 @@
+"""Decode GEMV microbenchmark on the current GPU.
+
+Shapes: the model's FP8 linears q 3072->4096, k/v 3072->1024, o 4096->3072,
+gate/up 3072->9216, down 9216->3072, and the BF16 lm_head 3072->131072, at token
+batch M = 1, 2, 4, 8. Weights are random E4M3 codes (several copies rotated so
+that the working set exceeds L2), activations N(0,1). Time per launch from CUDA
+events on the launching stream; GB/s counts weight bytes + activations in and
+outputs once per launch (the algorithmic bytes), against the measured HBM peak.
+M = 8 runs as two launches of 4 rows (weights are streamed twice) — the GB/s
+reported is still algorithmic bytes over total time.
+
+    python -m lunelette_b200.microbench [--shapes q,gate,...] [--m 1,2,4,8] [--iters N]
+"""
+import argparse
+import json
+import os
+
+import numpy as np
+
+SHAPES = {
+    "q": (4096, 3072), "k": (1024, 3072), "v": (1024, 3072), "o": (3072, 4096),
+    "gate": (9216, 3072), "up": (9216, 3072), "down": (3072, 9216), "lm_head": (131072, 3072),
+}
+L2_BYTES = 126 << 20
+
+
+def hbm_peak():
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    try:
+        return float(json.load(open(path))["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def run(shapes, ms_list, iters, warmup=3):
+    import torch
+    import lunelette_b200 as L
+    lib = L.library()
+    stream = torch.cuda.current_stream()
+    peak, kind = hbm_peak()
+    rows_out = []
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    for name in shapes:
+        rows, cols = SHAPES[name]
+        bf16 = name == "lm_head"
+        wbytes = rows * cols * (2 if bf16 else 1)
+        copies = max(1, min(8, (2 * L2_BYTES) // wbytes + 1))
+        ws = []
+        for _ in range(copies):
+            if bf16:
+                w = (torch.randn(rows, cols, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+            else:
+                w = torch.randint(0, 256, (rows, cols), device="cuda", dtype=torch.uint8, generator=gen)
+                w[(w & 127) == 127] = 0
+            ws.append(w)
+        gain = torch.ones(cols, device="cuda")
+        flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+        for m in ms_list:
+            if bf16 and m != 1:
+                continue
+            x = torch.randn(m, cols, device="cuda", generator=gen)
+            y = torch.empty(m, rows, device="cuda")
+
+            def launch(i):
+                w = ws[i % copies]
+                if bf16:
+                    rc = lib.lunelette_cuda_head_bf16(w.data_ptr(), rows, cols, x.data_ptr(), gain.data_ptr(),
+                                                      y.data_ptr(), flag.data_ptr(), stream.cuda_stream)
+                else:
+                    rc = lib.lunelette_cuda_gemv_fp8(w.data_ptr(), rows, cols, 1e-3, x.data_ptr(), None, m,
+                                                     y.data_ptr(), stream.cuda_stream)
+                assert rc == 0
+
+            for i in range(warmup):
+                launch(i)
+            torch.cuda.synchronize()
+            start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            for i in range(iters):
+                launch(i)
+            stop.record(stream)
+            torch.cuda.synchronize()
+            ms = start.elapsed_time(stop) / iters
+            nbytes = wbytes + m * cols * 4 + m * rows * 4
+            gbs = nbytes / (ms / 1000) / 1e9
+            rows_out.append({"shape": name, "rows": rows, "cols": cols, "m": m, "us": ms * 1000,
+                             "algorithmic_bytes": nbytes, "gbs": gbs, "frac_hbm": gbs / peak,
+                             "peak_gbs": peak, "peak_kind": kind})
+    return rows_out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--shapes", default=",".join(SHAPES))
+    ap.add_argument("--m", default="1,2,4,8")
+    ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=3)
+    args = ap.parse_args()
+    out = run(args.shapes.split(","), [int(v) for v in args.m.split(",")], args.iters, args.warmup)
+    for r in out:
+        print(json.dumps(r))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,317 @@
+"""Kernel parity on the B200: each product kernel, called through the C-ABI on
+device buffers, against the CPU oracle (or a float64 restatement of the
+reference's own analytic expectations) on awkward and model shapes."""
+import json
+import os
+import struct
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.fixture(scope="module")
+def torch_cuda():
+    import torch
+    torch.cuda.init()
+    return torch
+
+
+def dev(torch, array):
+    return torch.from_numpy(np.ascontiguousarray(array)).cuda()
+
+
+def ptr(t):
+    return t.data_ptr()
+
+
+def stream(torch):
+    return torch.cuda.current_stream().cuda_stream
+
+
+def e4m3_table(oracle):
+    return np.array([oracle.fp8_decode(c) for c in range(256)], np.float32)
+
+
+def finite_codes(rng, shape):
+    codes = rng.integers(0, 256, size=shape).astype(np.uint8)
+    codes[(codes & 127) == 127] = 0x3A  # never NaN
+    return codes
+
+
+def bf16_round(x):
+    b = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    b = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16) << 16
+    return b.astype(np.uint32).view(np.float32)
+
+
+def test_fp8_decode_bit_exact_all_codes(lib, torch_cuda):
+    torch = torch_cuda
+    golden = json.load(open(os.path.join(GOLDEN, "fp8_golden.json")))
+    table = np.array(golden["bits"], np.uint32).view(np.float32)
+    n = 1031  # odd: exercises the tail of the pair conversion
+    codes = ((np.arange(n) * 37 + 11) % 256).astype(np.uint8)
+    scales = [1.0, struct.unpack("<f", struct.pack("<I", 0x39FB << 16))[0], float.fromhex("0x1.f6p-12"),
+              float.fromhex("0x1.02p+5"), 2.0 ** -110, 2.0 ** 100, 0.251953125, 3.140625]
+    d_codes = dev(torch, codes)
+    out = torch.empty(n, dtype=torch.float32, device="cuda")
+    for scale in scales:
+        assert lib.lunelette_cuda_fp8_decode(ptr(d_codes), n, scale, ptr(out), stream(torch)) == 0
+        got = out.cpu().numpy()
+        want = table[codes] * np.float32(scale)
+        nan = (codes & 127) == 127
+        assert np.all(np.isnan(got[nan]))
+        assert np.array_equal(got[~nan].view(np.uint32), want[~nan].view(np.uint32)), scale
+
+
+def gemv_check(lib, oracle, torch, rows, cols, count, seed, residual=False):
+    rng = np.random.default_rng(seed)
+    codes = finite_codes(rng, (rows, cols))
+    scale = float(bf16_round(np.float32(0.0003 + rng.random() * 0.01)))
+    x = rng.standard_normal((count, cols)).astype(np.float32)
+    res = rng.standard_normal((count, rows)).astype(np.float32) if residual else None
+    d_w, d_x = dev(torch, codes), dev(torch, x)
+    d_r = dev(torch, res) if residual else None
+    y = torch.empty((count, rows), dtype=torch.float32, device="cuda")
+    rc = lib.lunelette_cuda_gemv_fp8(ptr(d_w), rows, cols, scale, ptr(d_x),
+                                     ptr(d_r) if residual else None, count, ptr(y), stream(torch))
+    assert rc == 0
+    got = y.cpu().numpy()
+    w64 = e4m3_table(oracle)[codes].astype(np.float64) * scale
+    exact = x.astype(np.float64) @ w64.T
+    bound = np.abs(x.astype(np.float64)) @ np.abs(w64).T
+    if residual:
+        exact = exact + res
+        bound = bound + np.abs(res)
+    assert np.all(np.abs(got - exact) <= 1e-5 * bound + 1e-30)
+    ref = oracle.project_fp8(codes, scale, x)
+    if residual:
+        ref = ref + res
+    # same arithmetic within FP32 summation-order noise of the reference's lane loop
+    assert np.all(np.abs(got - ref) <= 1e-5 * bound + 1e-30)
+
+
+@pytest.mark.parametrize("rows,cols,count", [
+    (7, 16, 1), (259, 48, 3), (65, 3072, 1), (1024, 3072, 2), (4096, 3072, 1),
+    (3072, 4096, 4), (3072, 9216, 1), (3072, 9216, 5), (1, 9216, 4), (33, 112, 9)])
+def test_gemv_fp8_matches_oracle(lib, oracle, torch_cuda, rows, cols, count):
+    gemv_check(lib, oracle, torch_cuda, rows, cols, count, seed=rows * 7 + cols + count)
+
+
+def test_gemv_fp8_residual(lib, oracle, torch_cuda):
+    gemv_check(lib, oracle, torch_cuda, 3072, 4096, 3, seed=11, residual=True)
+
+
+@pytest.mark.parametrize("k", [16, 32, 48, 64, 3072, 9216])
+def test_gemv_exact_integer_dots(lib, torch_cuda, k):
+    # all-ones weights (E4M3 0x38 = 1.0) and inputs give exactly K
+    torch = torch_cuda
+    rows, count = 5, 3
+    d_w = dev(torch, np.full((rows, k), 0x38, np.uint8))
+    d_x = dev(torch, np.ones((count, k), np.float32))
+    y = torch.empty((count, rows), dtype=torch.float32, device="cuda")
+    assert lib.lunelette_cuda_gemv_fp8(ptr(d_w), rows, k, 1.0, ptr(d_x), None, count, ptr(y),
+                                       stream(torch)) == 0
+    assert torch.all(y == float(k)).item()
+
+
+def test_gemv_rejects_unsupported_shapes(lib, torch_cuda):
+    torch = torch_cuda
+    d = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    f = torch.zeros(4096, dtype=torch.float32, device="cuda")
+    assert lib.lunelette_cuda_gemv_fp8(ptr(d), 7, 67, 1.0, ptr(f), None, 3, ptr(f), stream(torch)) == -1
+    assert lib.lunelette_cuda_gemv_fp8(ptr(d), 7, 0, 1.0, ptr(f), None, 3, ptr(f), stream(torch)) == -1
+    assert lib.lunelette_cuda_gemv_fp8(None, 7, 16, 1.0, ptr(f), None, 3, ptr(f), stream(torch)) == -1
+
+
+def test_rmsnorm_matches_oracle(lib, oracle, torch_cuda):
+    torch = torch_cuda
+    rng = np.random.default_rng(5)
+    for width, count in [(67 * 16, 2), (3072, 7)]:
+        x = (rng.standard_normal((count, width)) * 3).astype(np.float32)
+        g = (0.5 + rng.random(width)).astype(np.float32)
+        out = torch.empty((count, width), dtype=torch.float32, device="cuda")
+        assert lib.lunelette_cuda_rmsnorm(ptr(dev(torch, g)), ptr(dev(torch, x)), width, count,
+                                          ptr(out), stream(torch)) == 0
+        assert np.abs(out.cpu().numpy() - oracle.norm(g, x)).max() < 2e-6 * 3 * 3
+
+
+def pool_view(pool, num_pages):
+    return pool.reshape(-1, num_pages, 2, 8, 64, 128)
+
+
+def kv_rows(pool_np, page_table, num_pages, layer, kind, positions):
+    v = pool_view(pool_np, num_pages)
+    out = []
+    for p in positions:
+        page = page_table[p // 64]
+        out.append(v[layer, page, kind, :, p % 64, :].reshape(1024))
+    return np.stack(out)
+
+
+def bf16_to_f32(u16):
+    return (np.asarray(u16, np.uint32) << 16).view(np.float32)
+
+
+def test_qkv_rope_kv_store_matches_oracle(lib, oracle, torch_cuda):
+    torch = torch_cuda
+    rng = np.random.default_rng(21)
+    count, length, layer = 6, 61, 1  # positions 61..66 cross a page boundary
+    num_pages = 4
+    page_table = np.array([2, 0, 3, 1], np.int32)
+    codes = finite_codes(rng, (6144, 3072))
+    scales = np.array([bf16_round(np.float32(s)) for s in (0.0007, 0.0011, 0.0005)], np.float32)
+    gain = (0.5 + rng.random(3072)).astype(np.float32)
+    x = rng.standard_normal((count, 3072)).astype(np.float32)
+    positions = np.arange(length, length + count)
+    cos = np.zeros((num_pages * 64, 128), np.float32)
+    sin = np.zeros((num_pages * 64, 128), np.float32)
+    for p in range(num_pages * 64):
+        cos[p], sin[p] = oracle.yarn(p)
+    pool = torch.zeros((layer + 1) * num_pages * 2 * 8 * 64 * 128, dtype=torch.int16, device="cuda")
+    q_out = torch.empty((count, 4096), dtype=torch.float32, device="cuda")
+    rc = lib.lunelette_cuda_qkv_rope(
+        ptr(dev(torch, codes)), ptr(dev(torch, scales)), ptr(dev(torch, gain)), ptr(dev(torch, x)),
+        count, length, ptr(dev(torch, cos)), ptr(dev(torch, sin)), ptr(q_out), ptr(pool),
+        ptr(dev(torch, page_table)), num_pages, layer, stream(torch))
+    assert rc == 0
+    normed = oracle.norm(gain, x)
+    q = oracle.project_fp8(codes[:4096], scales[0], normed)
+    k = oracle.project_fp8(codes[4096:5120], scales[1], normed)
+    v = oracle.project_fp8(codes[5120:], scales[2], normed)
+    rq = oracle.rope(q, cos[positions], sin[positions], positions, 1)
+    rk = oracle.rope(k, cos[positions], sin[positions], positions, 0)
+    got_q = q_out.cpu().numpy()
+    assert np.abs(got_q - rq).max() <= 1e-5 * np.abs(rq).max()
+    pool_np = pool.cpu().numpy().view(np.uint16)
+    got_k = bf16_to_f32(kv_rows(pool_np, page_table, num_pages, layer, 0, positions))
+    got_v = bf16_to_f32(kv_rows(pool_np, page_table, num_pages, layer, 1, positions))
+    # BF16 storage: within one BF16 rounding of the oracle's FP32 values
+    assert np.all(np.abs(got_k - rk) <= 2.0 ** -8 * np.abs(rk) + 1e-6 * np.abs(rk).max())
+    assert np.all(np.abs(got_v - v) <= 2.0 ** -8 * np.abs(v) + 1e-6 * np.abs(v).max())
+    # layer 0 untouched
+    assert not pool_view(pool_np, num_pages)[0].any()
+
+
+def test_gateup_swiglu_matches_oracle(lib, oracle, torch_cuda):
+    torch = torch_cuda
+    rng = np.random.default_rng(31)
+    count = 3
+    gate = finite_codes(rng, (9216, 3072))
+    up = finite_codes(rng, (9216, 3072))
+    inter = np.empty((18432, 3072), np.uint8)
+    for b in range(72):
+        inter[256 * b:256 * b + 128] = gate[128 * b:128 * (b + 1)]
+        inter[256 * b + 128:256 * (b + 1)] = up[128 * b:128 * (b + 1)]
+    sg, su = float(bf16_round(np.float32(0.0004))), float(bf16_round(np.float32(0.0006)))
+    gain = (0.5 + rng.random(3072)).astype(np.float32)
+    x = rng.standard_normal((count, 3072)).astype(np.float32)
+    act = torch.empty((count, 9216), dtype=torch.float32, device="cuda")
+    assert lib.lunelette_cuda_gateup_swiglu(ptr(dev(torch, inter)), sg, su, ptr(dev(torch, gain)),
+                                            ptr(dev(torch, x)), count, ptr(act), stream(torch)) == 0
+    normed = oracle.norm(gain, x)
+    g = oracle.project_fp8(gate, sg, normed)
+    u = oracle.project_fp8(up, su, normed)
+    want = oracle.element(oracle.element(g, g, 1), u, 2)
+    got = act.cpu().numpy()
+    assert np.abs(got - want).max() <= 2e-5 * np.abs(want).max()
+
+
+def test_head_bf16_matches_oracle_and_flags_nonfinite(lib, oracle, torch_cuda):
+    torch = torch_cuda
+    rng = np.random.default_rng(41)
+    rows, cols = 4099, 3072
+    w = bf16_round((rng.standard_normal((rows, cols)) * 0.02).astype(np.float32))
+    w16 = (w.view(np.uint32) >> 16).astype(np.uint16)
+    x = (rng.standard_normal(cols) * 5).astype(np.float32)
+    gain = (0.5 + rng.random(cols)).astype(np.float32)
+    logits = torch.empty(rows, dtype=torch.float32, device="cuda")
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+    d_w = dev(torch, w16.view(np.int16))
+    assert lib.lunelette_cuda_head_bf16(ptr(d_w), rows, cols, ptr(dev(torch, x)), ptr(dev(torch, gain)),
+                                        ptr(logits), ptr(flag), stream(torch)) == 0
+    normed = oracle.norm(gain, x[None])
+    want = oracle.project(w, normed)[0]
+    got = logits.cpu().numpy()
+    assert np.abs(got - want).max() <= 1e-5 * np.abs(want).max()
+    assert flag.item() == 0
+    w16[1234, 17] = 0x7FC0  # NaN weight -> NaN logit
+    d_w = dev(torch, w16.view(np.int16))
+    assert lib.lunelette_cuda_head_bf16(ptr(d_w), rows, cols, ptr(dev(torch, x)), ptr(dev(torch, gain)),
+                                        ptr(logits), ptr(flag), stream(torch)) == 0
+    assert flag.item() == 1
+    assert np.isnan(logits.cpu().numpy()[1234])
+
+
+def write_pool(k_rows, v_rows, page_table, num_pages, layer, layers):
+    """Lay FP32 K/V rows [positions][1024] into a BF16 pool (returns uint16)."""
+    pool = np.zeros((layers, num_pages, 2, 8, 64, 128), np.uint16)
+    for p in range(k_rows.shape[0]):
+        page = page_table[p // 64]
+        pool[layer, page, 0, :, p % 64, :] = (bf16_round(k_rows[p]).view(np.uint32) >> 16).reshape(8, 128)
+        pool[layer, page, 1, :, p % 64, :] = (bf16_round(v_rows[p]).view(np.uint32) >> 16).reshape(8, 128)
+    return pool.reshape(-1)
+
+
+def run_attention(lib, torch, q, pool, page_table, num_pages, layer, length, count, slots=8192):
+    out = torch.empty((count, 4096), dtype=torch.float32, device="cuda")
+    acc = torch.empty(slots * 128, dtype=torch.float32, device="cuda")
+    ml = torch.empty(slots * 2, dtype=torch.float32, device="cuda")
+    rc = lib.lunelette_cuda_attention(ptr(dev(torch, q)), ptr(dev(torch, pool.view(np.int16))),
+                                      ptr(dev(torch, page_table)), num_pages, layer, length, count,
+                                      ptr(out), ptr(acc), ptr(ml), slots, stream(torch))
+    assert rc == 0
+    return out.cpu().numpy()
+
+
+def test_attention_prefix_matches_reference_expectation(lib, oracle, torch_cuda):
+    # tests/test_metal.m:532-578 inputs (exactly representable in BF16)
+    torch = torch_cuda
+    count, prefix = 2, 3
+    total = count + prefix
+    q = (((np.arange(count * 4096) % 11) - 5) * 0.03125).astype(np.float32).reshape(count, 4096)
+    k = (((np.arange(total * 1024) % 17) - 8) * 0.03125).astype(np.float32).reshape(total, 1024)
+    v = (((np.arange(total * 1024) % 23) - 11) * 0.0625).astype(np.float32).reshape(total, 1024)
+    table = np.array([0], np.int32)
+    pool = write_pool(k, v, table, 1, 0, 1)
+    got = run_attention(lib, torch, q, pool, table, 1, 0, prefix, count)
+    want = oracle.attention(q, k, v, prefix)
+    assert np.abs(got - want).max() < 2e-6
+
+
+def test_attention_long_causal_sentinel(lib, torch_cuda):
+    # tests/test_metal.m:956-997 at C = 4352: row 0 masks the last value row, row 1 includes it
+    torch = torch_cuda
+    total, count = 4352, 2
+    num_pages = total // 64
+    table = np.arange(num_pages, dtype=np.int32)[::-1].copy()
+    k = np.zeros((total, 1024), np.float32)
+    v = np.ones((total, 1024), np.float32)
+    v[total - 1] = 4352.0
+    pool = write_pool(k, v, table, num_pages, 0, 1)
+    got = run_attention(lib, torch, np.zeros((count, 4096), np.float32), pool, table, num_pages, 0,
+                        total - count, count)
+    assert np.abs(got[0] - 1.0).max() < 2e-4
+    assert np.abs(got[1] - 8703.0 / 4352).max() < 2e-4
+
+
+@pytest.mark.parametrize("length,count,slots", [(0, 1, 8192), (255, 1, 8192), (300, 1, 8192),
+                                                (4351, 1, 8192), (100, 37, 8192), (0, 256, 8192),
+                                                (1000, 5, 160), (2000, 3, 96)])
+def test_attention_random_matches_oracle(lib, oracle, torch_cuda, length, count, slots):
+    torch = torch_cuda
+    rng = np.random.default_rng(length * 3 + count)
+    total = length + count
+    num_pages = (total + 63) // 64 + 1
+    table = rng.permutation(num_pages).astype(np.int32)
+    k = bf16_round(rng.standard_normal((total, 1024)).astype(np.float32))
+    v = bf16_round(rng.standard_normal((total, 1024)).astype(np.float32))
+    q = rng.standard_normal((count, 4096)).astype(np.float32)
+    layer = 2
+    pool = write_pool(k, v, table, num_pages, layer, 3)
+    got = run_attention(lib, torch, q, pool, table, num_pages, layer, length, count, slots)
+    want = oracle.attention(q, k, v, length)
+    assert np.abs(got - want).max() < 1e-5 * max(1.0, np.abs(want).max())

@@ -1,0 +1,170 @@
+"""Full-model parity on the B200 through the drop-in C-ABI (include/metal.h),
+against the CPU oracle on the same seeded synthetic checkpoint.
+
+Gates: per-layer hidden states and final logits within
+2e-2 max-abs and 1e-2 relative L2; greedy tokens identical over 32 decode
+steps; bitwise-identical logits across reset cycles (tests/compare_native.c
+demands this of the reference)."""
+import numpy as np
+import pytest
+
+import lunelette_b200 as L
+from tests.oracle_lib import greedy
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-2
+REL_L2 = 1e-2
+
+
+def rel_l2(a, b):
+    return float(np.linalg.norm((a - b).ravel()) / max(np.linalg.norm(b.ravel()), 1e-30))
+
+
+def assert_close(got, want, what):
+    err = float(np.abs(got - want).max())
+    rel = rel_l2(got, want)
+    assert err <= MAX_ABS and rel <= REL_L2, "%s: max-abs %.3g rel-L2 %.3g" % (what, err, rel)
+    return err, rel
+
+
+def prompt(seed, n):
+    return np.random.default_rng(seed).integers(1000, 131072, n).astype(np.int64)
+
+
+@pytest.fixture(scope="module")
+def runtime(lib, checkpoint_path):
+    rt = L.Runtime(checkpoint_path)
+    yield rt
+    rt.close()
+
+
+@pytest.fixture(scope="module")
+def oracle_model(oracle, checkpoint_path):
+    m = oracle.open_model(checkpoint_path, 256)
+    yield m
+    m.close()
+
+
+def test_memory_and_limits(runtime):
+    mem = runtime.memory()
+    assert mem["strategy"] == L.COMPACT_FP8_ARITHMETIC  # NULL options -> product default
+    assert mem["weight_bytes"] == 3026190336 + 805306368 + 53 * 3072 * 4
+    assert mem["conversion_stage_bytes"] == 0
+    assert mem["kv_bytes"] == 26 * 2 * 256 * 1024 * 2
+    assert mem["total_bytes"] == mem["weight_bytes"] + mem["scratch_bytes"] + mem["kv_bytes"]
+    assert runtime.limits() == (256, 256)
+
+
+def test_c0_prefill_per_layer_and_greedy_32(runtime, oracle_model):
+    ids = prompt(1234, 32)
+    runtime.reset()
+    oracle_model.reset()
+    runtime.trace(True)
+    try:
+        logits = runtime.prefill(ids).copy()
+        layers = [runtime.trace_copy(l, len(ids)) for l in range(27)]
+    finally:
+        runtime.trace(False)
+    want, trace, final = oracle_model.forward(ids, trace=True, final_norm=True)
+    for l in range(26):
+        assert_close(layers[l], trace[l], "layer %d hidden" % l)
+    assert_close(layers[26], final, "final norm")
+    assert_close(logits, want, "prefill logits")
+    tokens_gpu, tokens_cpu = [greedy(logits)], [greedy(want)]
+    assert tokens_gpu == tokens_cpu
+    for step in range(31):
+        logits = runtime.decode(tokens_gpu[-1]).copy()
+        want, _, _ = oracle_model.forward([tokens_cpu[-1]])
+        assert_close(logits, want, "decode step %d logits" % step)
+        tokens_gpu.append(greedy(logits))
+        tokens_cpu.append(greedy(want))
+        assert tokens_gpu == tokens_cpu, "greedy divergence at step %d" % step
+
+
+def test_reset_cycles_are_bitwise_identical(runtime):
+    ids = prompt(77, 24)
+    runs = []
+    for cycle in range(2):
+        runtime.reset()
+        seq = [runtime.prefill(ids).copy()]
+        for step in range(6):
+            seq.append(runtime.decode(int(seq[-1].argmax())).copy())
+        runs.append(seq)
+    for a, b in zip(*runs):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_chunked_append_matches_single_prefill(runtime):
+    ids = prompt(99, 40)
+    runtime.reset()
+    whole = runtime.prefill(ids).copy()
+    runtime.reset()
+    runtime.prefill(ids[:13])
+    runtime.append(ids[13:30])
+    part = runtime.append(ids[30:]).copy()
+    assert runtime.length() == 40
+    assert np.abs(part - whole).max() < 1e-3
+    runtime.reset()
+    runtime.prefill(ids[:39])
+    last = runtime.decode(int(ids[39])).copy()
+    assert np.abs(last - whole).max() < 1e-3
+
+
+def test_checkpoint_restore_and_prefix_reuse(runtime):
+    ids = prompt(5, 20)
+    runtime.reset()
+    saved_logits = runtime.prefill(ids).copy()
+    cp = runtime.checkpoint_create()
+    try:
+        t1 = int(saved_logits.argmax())
+        first = runtime.decode(t1).copy()
+        runtime.decode(int(first.argmax()))
+        assert runtime.length() == 22
+        restored = runtime.checkpoint_restore(cp).copy()
+        assert runtime.length() == 20
+        assert np.array_equal(restored.view(np.uint32), saved_logits.view(np.uint32))
+        again = runtime.decode(t1).copy()  # overwrites the stale KV row 20
+        assert np.array_equal(again.view(np.uint32), first.view(np.uint32))
+        runtime.checkpoint_restore(cp)  # restore repeats
+        cp2 = runtime.checkpoint_create()
+        with pytest.raises(L.LuneletteError):
+            runtime.checkpoint_restore(cp)  # replaced handle is stale
+        cp2.destroy()
+        runtime.reset()
+        with pytest.raises(L.LuneletteError):
+            runtime.checkpoint_restore(cp)
+    finally:
+        cp.destroy()
+
+
+def test_argument_errors_do_not_mutate(runtime):
+    ids = prompt(6, 8)
+    runtime.reset()
+    with pytest.raises(L.LuneletteError):
+        runtime.decode(5)  # empty sequence
+    with pytest.raises(L.LuneletteError):
+        runtime.prefill([])
+    with pytest.raises(L.LuneletteError):
+        runtime.prefill([131072])
+    runtime.prefill(ids)
+    with pytest.raises(L.LuneletteError):
+        runtime.prefill(ids)  # non-empty
+    with pytest.raises(L.LuneletteError):
+        runtime.decode(-1)
+    with pytest.raises(L.LuneletteError):
+        runtime.append(np.zeros(257, np.int64))
+    assert runtime.length() == 8
+    runtime.decode(3)
+    assert runtime.length() == 9
+
+
+def test_capacity_256_fill_then_reject(runtime):
+    runtime.reset()
+    runtime.prefill(prompt(8, 250))
+    for _ in range(6):
+        runtime.decode(11)
+    assert runtime.length() == 256
+    with pytest.raises(L.LuneletteError):
+        runtime.decode(11)
+    assert runtime.length() == 256

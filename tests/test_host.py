@@ -1,0 +1,259 @@
+"""Host-side product tests that need no GPU: the C-ABI exports, argument
+rejection before any I/O, the E4M3 encoder, the YaRN table, checkpoint
+admission (including agreement with the reference's own loader and parser)."""
+import ctypes
+import json
+import os
+import re
+import shutil
+import struct
+import tempfile
+
+import numpy as np
+import pytest
+
+import lunelette_b200 as L
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = set()
+    for header in ("metal.h", "lunelette_cuda.h"):
+        text = open(os.path.join(REPO, "include", header)).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names.update(re.findall(r"\b(lunelette_\w+)\s*\(", text))
+    return names
+
+
+def exported_functions():
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", L.LIBRARY_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    return {line.split()[-1] for line in out.splitlines() if " T " in line}
+
+
+def test_library_exports_exactly_the_declared_abi(lib):
+    declared = declared_functions()
+    exported = exported_functions()
+    assert len([n for n in declared if n.startswith("lunelette_metal_")]) == 13
+    assert declared <= exported, declared - exported
+    assert exported <= declared, exported - declared
+    for name in declared:
+        assert name in L.SIGNATURES, name
+
+
+def test_create_rejects_before_io(lib):
+    err = ctypes.create_string_buffer(512)
+    bad_limits = L.Limits(4352, 64)
+    assert not lib.lunelette_metal_create_configured(b"/no-model", None, ctypes.byref(bad_limits), err, 512)
+    assert b"unsupported context/block" in err.value
+    bad = L.Options(7, 1)
+    assert not lib.lunelette_metal_create_with_options(b"/no-model", ctypes.byref(bad), err, 512)
+    assert b"invalid prefill option" in err.value
+    bad = L.Options(0, 9)
+    assert not lib.lunelette_metal_create_with_options(b"/no-model", ctypes.byref(bad), err, 512)
+    assert b"invalid strategy" in err.value
+    assert not lib.lunelette_metal_create(None, err, 512)
+    assert b"explicit FP8 safetensors path" in err.value
+    assert not lib.lunelette_metal_create(b"/no-model", None, 0)  # NULL error buffer allowed
+    lim = L.Limits(1, 2)
+    assert lib.lunelette_metal_get_limits(None, ctypes.byref(lim)) == -1
+    assert (lim.context, lim.block) == (1, 2)
+    assert lib.lunelette_metal_get_memory(None, None) == -1
+    lib.lunelette_metal_destroy(None)
+    assert lib.lunelette_metal_reset(None, err, 512) == -1
+    logits = ctypes.c_void_p(1)
+    ids = (ctypes.c_int64 * 1)(0)
+    assert lib.lunelette_metal_prefill(None, ids, 1, ctypes.byref(logits), err, 512) == -1
+    assert logits.value is None
+    lib.lunelette_metal_checkpoint_destroy(None)
+
+
+def test_e4m3_encoder_round_trips_and_matches_torch(lib, oracle):
+    import torch
+    for code in range(256):
+        if code & 127 == 127:
+            continue
+        assert lib.lunelette_cuda_e4m3_encode(oracle.fp8_decode(code)) == code
+    rng = np.random.default_rng(3)
+    x = np.concatenate([rng.standard_normal(20000) * s for s in (1e-3, 0.1, 3.0, 100.0)]).astype(np.float32)
+    x = np.clip(x, -448, 448)
+    # include exact ties between neighbouring codes
+    decoded = np.array([oracle.fp8_decode(c) for c in range(126)], np.float32)
+    mids = ((decoded[:-1].astype(np.float64) + decoded[1:]) / 2).astype(np.float32)
+    x = np.concatenate([x, mids, -mids])
+    ours = np.array([lib.lunelette_cuda_e4m3_encode(float(v)) for v in x], np.uint8)
+    theirs = torch.from_numpy(x).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(ours, theirs)
+    assert lib.lunelette_cuda_e4m3_encode(1000.0) == 0x7E
+    assert lib.lunelette_cuda_e4m3_encode(-1000.0) == 0xFE
+
+
+def test_product_yarn_bitwise_equals_reference(lib):
+    g = json.load(open(os.path.join(REPO, "tests", "golden", "yarn_ref.json")))
+    c = np.zeros(128, np.float32)
+    s = np.zeros(128, np.float32)
+    for pos in g["positions"]:
+        assert lib.lunelette_cuda_yarn(pos, c.ctypes.data, s.ctypes.data) == 0
+        assert [int(b) for b in c.view(np.uint32)] == g["tables"][str(pos)]["cos"]
+        assert [int(b) for b in s.view(np.uint32)] == g["tables"][str(pos)]["sin"]
+    assert lib.lunelette_cuda_yarn(262144, c.ctypes.data, s.ctypes.data) == -1
+
+
+def test_synthetic_checkpoint_admitted(checkpoint_path):
+    for strategy in (L.RESIDENT_FP32, L.COMPACT_FP8_ARITHMETIC, L.COMPACT_FP8_LOOKUP):
+        L.validate_checkpoint(checkpoint_path, strategy)
+
+
+def test_reference_loader_accepts_synthetic_checkpoint(checkpoint_path, ref_lib):
+    """The reference's own metadata validation and compact raw admission
+    (src/metal_weights.c:51-231) accept the generated file."""
+    ref_lib.lunelette_metal_weights_open.argtypes = [ctypes.c_void_p, ctypes.c_char_p,
+                                                     ctypes.c_char_p, ctypes.c_size_t]
+    ref_lib.lunelette_metal_weights_load_raw.argtypes = [ctypes.c_void_p, ctypes.c_size_t,
+                                                         ctypes.c_void_p, ctypes.c_size_t,
+                                                         ctypes.c_char_p, ctypes.c_size_t]
+    ref_lib.lunelette_metal_weights_close.argtypes = [ctypes.c_void_p]
+    state = ctypes.create_string_buffer(1 << 16)
+    err = ctypes.create_string_buffer(512)
+    assert ref_lib.lunelette_metal_weights_open(state, checkpoint_path.encode(), err, 512) == 0, err.value
+    try:
+        out = np.empty(9216 * 3072, np.uint8)
+        sizes = [4096 * 3072, 1024 * 3072, 1024 * 3072, 3072 * 4096, 9216 * 3072, 9216 * 3072,
+                 3072 * 9216]
+        for layer in (0, 13, 25):
+            for slot, size in zip((1, 2, 3, 4, 6, 7, 8), sizes):
+                index = 2 + layer * 9 + slot
+                rc = ref_lib.lunelette_metal_weights_load_raw(state, index, out.ctypes.data, size, err, 512)
+                assert rc == 0, err.value
+    finally:
+        ref_lib.lunelette_metal_weights_close(state)
+
+
+@pytest.fixture(scope="module")
+def corrupt_copy(checkpoint_path):
+    path = os.path.join(tempfile.gettempdir(), "lunelette_corrupt_%d.safetensors" % os.getpid())
+    shutil.copyfile(checkpoint_path, path)
+    yield path
+    os.unlink(path)
+
+
+def header_of(path):
+    with open(path, "rb") as f:
+        n = struct.unpack("<Q", f.read(8))[0]
+        return n, f.read(n).decode()
+
+
+def patch(path, offset, data):
+    with open(path, "r+b") as f:
+        f.seek(offset)
+        old = f.read(len(data))
+        f.seek(offset)
+        f.write(data)
+    return old
+
+
+def tensor_offset(path, name):
+    n, header = header_of(path)
+    meta = json.loads(header)[name]
+    return 8 + n + meta["data_offsets"][0]
+
+
+def test_admission_rejects_planted_faults(corrupt_copy):
+    q = "language_model.model.layers.3.self_attn.q_proj.weight"
+    base = tensor_offset(corrupt_copy, q)
+    old = patch(corrupt_copy, base + 1000, b"\x7f")
+    try:
+        for strategy in (L.RESIDENT_FP32, L.COMPACT_FP8_ARITHMETIC):
+            with pytest.raises(L.LuneletteError):
+                L.validate_checkpoint(corrupt_copy, strategy)
+        with pytest.raises(L.LuneletteError, match="byte 1000 code 0x7f"):
+            L.validate_checkpoint(corrupt_copy, L.COMPACT_FP8_ARITHMETIC)
+    finally:
+        patch(corrupt_copy, base + 1000, old)
+    scale = q[:-6] + "weight_scale_inv"
+    at = tensor_offset(corrupt_copy, scale)
+    old = patch(corrupt_copy, at, struct.pack("<H", 0x0001))  # subnormal BF16 scale
+    try:
+        with pytest.raises(L.LuneletteError, match="FP32-normal widened BF16"):
+            L.validate_checkpoint(corrupt_copy, L.COMPACT_FP8_ARITHMETIC)
+        L.validate_checkpoint(corrupt_copy, L.RESIDENT_FP32)  # resident admits it
+    finally:
+        patch(corrupt_copy, at, old)
+    act = q[:-6] + "activation_scale"
+    at = tensor_offset(corrupt_copy, act)
+    old = patch(corrupt_copy, at, struct.pack("<H", 0xBF80))  # -1.0
+    try:
+        with pytest.raises(L.LuneletteError, match="positive finite BF16"):
+            L.validate_checkpoint(corrupt_copy, L.RESIDENT_FP32)
+    finally:
+        patch(corrupt_copy, at, old)
+    n, header = header_of(corrupt_copy)
+    at = 8 + header.index("embed_tokens") + len("embed_token")
+    old = patch(corrupt_copy, at, b"z")
+    try:
+        with pytest.raises(L.LuneletteError, match="embed_tokens.weight: expected BF16"):
+            L.validate_checkpoint(corrupt_copy, L.COMPACT_FP8_ARITHMETIC)
+    finally:
+        patch(corrupt_copy, at, old)
+    L.validate_checkpoint(corrupt_copy, L.COMPACT_FP8_ARITHMETIC)
+
+
+# ---- parser corpus: same accept/reject verdict as the reference's st_open ----
+
+def small_file(header, data=b""):
+    fd, path = tempfile.mkstemp(suffix=".safetensors")
+    raw = header.encode() if isinstance(header, str) else header
+    with os.fdopen(fd, "wb") as f:
+        f.write(struct.pack("<Q", len(raw)) + raw + data)
+    return path
+
+
+PARSER_CASES = [
+    ('{"w":{"dtype":"BF16","shape":[2,2],"data_offsets":[0,8]}}', b"\0" * 8, True),
+    ('{"__metadata__":{"a":"b"},"w":{"dtype":"F32","shape":[],"data_offsets":[0,4]}}', b"\0" * 4, True),
+    ('{}', b"", True),
+    ('  {}', b"", False),  # first byte must be '{'
+    ('{"w":{"dtype":"F16","shape":[1],"data_offsets":[0,2]}}', b"\0" * 2, False),
+    ('{"w":{"dtype":"BF16","shape":[2],"data_offsets":[0,2]}}', b"\0" * 2, False),
+    ('{"w":{"dtype":"BF16","shape":[1],"data_offsets":[0,2]},"w":{"dtype":"BF16","shape":[1],"data_offsets":[2,4]}}', b"\0" * 4, False),
+    ('{"a":{"dtype":"BF16","shape":[1],"data_offsets":[0,2]},"b":{"dtype":"BF16","shape":[1],"data_offsets":[4,6]}}', b"\0" * 6, False),
+    ('{"a":{"dtype":"BF16","shape":[1],"data_offsets":[0,2]}}', b"\0" * 4, False),  # trailing bytes
+    ('{"a":{"dtype":"I64","shape":[1,1,1,1,1,1,1,1,1],"data_offsets":[0,8]}}', b"\0" * 8, False),
+    ('{"a":{"dtype":"I64","shape":[1],"shape":[1],"data_offsets":[0,8]}}', b"\0" * 8, False),
+    ('{"a":{"dtype":"I64","shape":[01],"data_offsets":[0,8]}}', b"\0" * 8, False),
+    ('{"__metadata__":{"a":1}}', b"", False),
+    ('{"e":{"dtype":"BF16","shape":[0],"data_offsets":[0,0]},"a":{"dtype":"F8_E4M3","shape":[1],"data_offsets":[0,1]}}', b"\0", True),
+    ('{"e":{"dtype":"BF16","shape":[0],"data_offsets":[1,1]},"a":{"dtype":"BF16","shape":[1],"data_offsets":[0,2]}}', b"\0\0", False),
+    ('{"a\\u0041":{"dtype":"F8_E4M3","shape":[],"data_offsets":[0,1]}}', b"\0", True),
+    ('{"a":{"dtype":"F8_E4M3","shape":[],"data_offsets":[0,1]}} ', b"\0", True),
+    ('{"a":{"dtype":"F8_E4M3","shape":[],"data_offsets":[0,1]}}x', b"\0", False),
+]
+
+
+def st_open_verdicts(ref_lib, path):
+    ref_lib.st_open.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t]
+    ref_lib.st_close.argtypes = [ctypes.c_void_p]
+    state = ctypes.create_string_buffer(256)
+    err = ctypes.create_string_buffer(512)
+    ok = ref_lib.st_open(state, path.encode(), err, 512) == 0
+    if ok:
+        ref_lib.st_close(state)
+    return ok
+
+
+@pytest.mark.parametrize("case", range(len(PARSER_CASES)))
+def test_parser_corpus(lib, case, request):
+    header, data, accepted = PARSER_CASES[case]
+    path = small_file(header, data)
+    try:
+        err = ctypes.create_string_buffer(512)
+        lib.lunelette_cuda_validate_checkpoint(path.encode(), 1, err, 512)
+        parsed = b"tensor language_model.model.embed_tokens.weight" in err.value
+        assert parsed == accepted, err.value
+        if os.path.exists(os.path.join(REPO, "oracle", "_ref", "libref.so")):
+            ref = request.getfixturevalue("ref_lib")
+            assert st_open_verdicts(ref, path) == accepted
+    finally:
+        os.unlink(path)

@@ -1,0 +1,183 @@
+"""Pin the CPU oracle before trusting it: golden vectors from the reference's
+tests (fp8_golden.h, rope_golden.h), bit-for-bit agreement with the
+reference's own compiled C (oracle/_ref), and the analytic expectations of the
+reference's Metal operator tests (tests/test_metal.m, test_metal_reference.m)."""
+import ctypes
+import json
+import os
+import struct
+
+import numpy as np
+import pytest
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def bits(x):
+    return struct.unpack("<I", struct.pack("<f", float(x)))[0]
+
+
+def load(name):
+    with open(os.path.join(GOLDEN, name)) as f:
+        return json.load(f)
+
+
+def test_fp8_decode_matches_frozen_pytorch_table(oracle):
+    g = load("fp8_golden.json")
+    for code in range(256):
+        v = oracle.fp8_decode(code)
+        if code in g["nan_codes"]:
+            assert np.isnan(v)
+        else:
+            assert bits(v) == g["bits"][code], code
+
+
+def test_yarn_matches_transformers_golden(oracle):
+    g = load("rope_golden.json")
+    for p, pos in enumerate(g["positions"]):
+        c, s = oracle.yarn(pos)
+        for j, idx in enumerate(g["indices"]):
+            assert abs(c[idx] - g["cos_sin"][p][j][0]) < g["tolerance"]
+            assert abs(s[idx] - g["cos_sin"][p][j][1]) < g["tolerance"]
+    assert oracle.yarn(262144) is None
+
+
+def test_yarn_bitwise_equals_reference_c(oracle):
+    g = load("yarn_ref.json")
+    for pos in g["positions"]:
+        c, s = oracle.yarn(pos)
+        assert [bits(v) for v in c] == g["tables"][str(pos)]["cos"], pos
+        assert [bits(v) for v in s] == g["tables"][str(pos)]["sin"], pos
+
+
+def test_oracle_against_live_reference_c(oracle, ref_lib):
+    ref_lib.lunelette_metal_yarn.argtypes = [ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p]
+    ref_lib.st_f8_e4m3_to_f32.argtypes = [ctypes.c_ubyte]
+    ref_lib.st_f8_e4m3_to_f32.restype = ctypes.c_float
+    for code in range(256):
+        a, b = oracle.fp8_decode(code), ref_lib.st_f8_e4m3_to_f32(code)
+        assert (np.isnan(a) and np.isnan(b)) or bits(a) == bits(b)
+    c = np.zeros(128, np.float32)
+    s = np.zeros(128, np.float32)
+    for pos in list(range(0, 4352, 7)) + [4351, 16383, 16384, 16385, 262143]:
+        assert ref_lib.lunelette_metal_yarn(pos, c.ctypes.data, s.ctypes.data) == 0
+        oc, os_ = oracle.yarn(pos)
+        assert np.array_equal(oc.view(np.uint32), c.view(np.uint32)), pos
+        assert np.array_equal(os_.view(np.uint32), s.view(np.uint32)), pos
+
+
+def test_projection_odd_shape(oracle):
+    # tests/test_metal.m:169-198: 7 rows x 67 cols x 3 tokens within 1e-6
+    rows, cols, tokens = 7, 67, 3
+    w = ((np.arange(rows * cols) % 19) - 9).astype(np.float32) * 0.03125
+    x = ((np.arange(tokens * cols) % 13) - 6).astype(np.float32) * 0.0625
+    w, x = w.reshape(rows, cols), x.reshape(tokens, cols)
+    out = oracle.project(w, x)
+    expect = x.astype(np.float64) @ w.astype(np.float64).T
+    assert np.abs(out - expect).max() < 1e-6
+
+
+def test_norm_and_elements(oracle):
+    # tests/test_metal.m:490-530: width 67, 2 tokens, within 2e-6
+    width, tokens = 67, 2
+    w = (0.5 + np.arange(width) * 0.001).astype(np.float32)
+    x = (((np.arange(width * tokens) % 17) - 8) * 0.125).astype(np.float32).reshape(tokens, width)
+    out = oracle.norm(w, x)
+    xd = x.astype(np.float64)
+    expect = w * xd / np.sqrt((xd * xd).mean(axis=1, keepdims=True) + 1e-5)
+    assert np.abs(out - expect).max() < 2e-6
+    flat = x.reshape(-1)
+    for mode, ref in [(0, 2 * flat.astype(np.float64)),
+                      (1, flat / (1 + np.exp(-flat.astype(np.float64)))),
+                      (2, flat.astype(np.float64) ** 2)]:
+        assert np.abs(oracle.element(flat, flat, mode) - ref).max() < 2e-6
+
+
+def attention_reference(q, k, v, prefix):
+    count = q.shape[0]
+    out = np.zeros((count, 4096))
+    for t in range(count):
+        for h in range(32):
+            n = prefix + t + 1
+            qd = q[t, h * 128:(h + 1) * 128].astype(np.float64)
+            kd = k[:n, (h // 4) * 128:(h // 4 + 1) * 128].astype(np.float64)
+            vd = v[:n, (h // 4) * 128:(h // 4 + 1) * 128].astype(np.float64)
+            p = np.exp(kd @ qd / np.sqrt(128))
+            out[t, h * 128:(h + 1) * 128] = (p / p.sum()) @ vd
+    return out
+
+
+def test_attention_prefix(oracle):
+    # tests/test_metal.m:532-578: prefix 3 + 2 tokens within 2e-6
+    count, prefix = 2, 3
+    total = count + prefix
+    q = (((np.arange(count * 4096) % 11) - 5) * 0.03125).astype(np.float32).reshape(count, 4096)
+    k = (((np.arange(total * 1024) % 17) - 8) * 0.03125).astype(np.float32).reshape(total, 1024)
+    v = (((np.arange(total * 1024) % 23) - 11) * 0.0625).astype(np.float32).reshape(total, 1024)
+    out = oracle.attention(q, k, v, prefix)
+    assert np.abs(out - attention_reference(q, k, v, prefix)).max() < 2e-6
+
+
+def test_long_causal_sentinel(oracle):
+    # tests/test_metal.m:956-997: zero q/k, values 1 except the last row 4352
+    total, count = 4352, 2
+    q = np.zeros((count, 4096), np.float32)
+    k = np.zeros((total, 1024), np.float32)
+    v = np.ones((total, 1024), np.float32)
+    v[total - 1] = 4352.0
+    out = oracle.attention(q, k, v, total - count)
+    assert np.abs(out[0] - 1.0).max() < 2e-4
+    assert np.abs(out[1] - 8703.0 / 4352).max() < 2e-4
+
+
+def test_rope_with_query_scale(oracle):
+    # tests/test_metal.m:580-627
+    positions = np.array([0, 1, 16383, 16384, 16385], np.uint32)
+    count = len(positions)
+    x = (((np.arange(count * 128) % 23) - 11) * 0.125).astype(np.float32).reshape(count, 128)
+    cos = np.stack([oracle.yarn(int(p))[0] for p in positions])
+    sin = np.stack([oracle.yarn(int(p))[1] for p in positions])
+    for query in (0, 1):
+        out = oracle.rope(x, cos, sin, positions, query)
+        rot = np.concatenate([-x[:, 64:], x[:, :64]], axis=1).astype(np.float64)
+        expect = x * cos.astype(np.float64) + rot * sin
+        if query:
+            expect *= (1 + 0.1 * np.log(1 + positions // 16384))[:, None]
+        assert np.abs(out - expect).max() < 2e-6
+
+
+@pytest.mark.parametrize("k", [1, 7, 31, 32, 33, 63, 65, 3072])
+def test_frozen_exact_integer_dots(oracle, k):
+    # tests/test_metal_reference.m:121-127: all-ones weights and inputs give exactly K
+    rows, tokens = 3, 2
+    out = oracle.project(np.ones((rows, k), np.float32), np.ones((tokens, k), np.float32))
+    assert np.all(out == np.float32(k))
+    codes = np.full((rows, k), 0x38, np.uint8)  # E4M3 1.0
+    out8 = oracle.project_fp8(codes, 1.0, np.ones((tokens, k), np.float32))
+    assert np.all(out8 == np.float32(k))
+
+
+def test_greedy_rule_matches_reference(oracle):
+    from tests.oracle_lib import greedy
+    g = load("greedy_ref.json")
+    rng = np.random.default_rng(20261201)
+    for case in g["cases"]:
+        v = rng.standard_normal(131072).astype(np.float32)
+        plant = case["plant"]
+        if "tie" in plant:
+            top = float(v.max()) + 1.0
+            v[plant["tie"]] = top
+        if "signed_zero" in plant:
+            v[:] = -1.0
+            v[10] = -0.0
+            v[5] = 0.0
+        if "inf" in plant:
+            v[plant["inf"]] = np.inf
+        if "nan" in plant:
+            v[plant["nan"]] = np.nan
+        if case["seed_case"] == 5:
+            v[131071] = float(v.max()) + 0.5
+        if case["rc"] != 0:
+            assert not np.all(np.isfinite(v))
+        else:
+            assert greedy(v) == case["token"]
