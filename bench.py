@@ -337,7 +337,7 @@ def run_ours(args, rank, world, local_rank):
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps,
             "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None,
-            "dtype": "fp8-e4m3 weights, fp32 activations/accumulation, bf16 kv",
+            "dtype": "fp8-e4m3 weights, fp32 activations/accumulation/kv",
             "data": "synthetic (seeded random-init checkpoint in the reference's tensor layout, seeded ids)",
             "config": {"workload": "C0: batch-1 greedy decode after a 32-token prompt, context profile 256",
                        "prompt": PROMPT, "decode_per_round": per_round, "rounds": rounds,

@@ -37,13 +37,13 @@ int lunelette_cuda_gemv_fp8(const uint8_t *W, size_t rows, size_t cols, float sc
 
 /* Fused input RMSNorm + q/k/v projection + YaRN RoPE (+ query scale) + KV store
  * for `count` tokens at positions length..length+count-1. W is [6144][3072]
- * (q rows, then k, then v); scales = {q, k, v}; q_out [count][4096];
- * kv_pool is the paged BF16 pool [layer][page][K|V][8][64][128].
+ * (q rows, then k, then v); scales is a HOST array {q, k, v}; q_out [count][4096];
+ * kv_pool is the paged FP32 pool [layer][page][K|V][8 heads][64 slots][128].
  * Replaces norm + 3x project_fp8 + 2x rope + the KV blit
  * (src/metal_encode.m:129-153, src/metal_kernels.metal:29-78). */
 int lunelette_cuda_qkv_rope(const uint8_t *W, const float *scales, const float *gain,
     const float *x, size_t count, size_t length, const float *rope_cos, const float *rope_sin,
-    float *q_out, uint16_t *kv_pool, const int *page_table, size_t num_pages, size_t layer,
+    float *q_out, float *kv_pool, const int *page_table, size_t num_pages, size_t layer,
     void *stream);
 
 /* Fused post-attention RMSNorm + gate/up projection + SwiGLU. W is [18432][3072]
@@ -67,7 +67,7 @@ int lunelette_cuda_head_bf16(const uint16_t *W, size_t rows, size_t cols, const 
  * paged pool; out [count][4096]. part_acc (slots*128 floats) and part_ml
  * (slots*2 floats) are caller scratch, slots >= 32*count.
  * Replaces scores + attend (src/metal_kernels.metal:81-132). */
-int lunelette_cuda_attention(const float *q, const uint16_t *kv_pool, const int *page_table,
+int lunelette_cuda_attention(const float *q, const float *kv_pool, const int *page_table,
     size_t num_pages, size_t layer, size_t length, size_t count, float *out, float *part_acc,
     float *part_ml, size_t slots, void *stream);
 

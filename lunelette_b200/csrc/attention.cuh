@@ -1,4 +1,4 @@
-// Causal GQA attention over the paged BF16 KV pool, split over positions.
+// Causal GQA attention over the paged FP32 KV pool, split over positions.
 //
 // Replaces scores + attend (src/metal_kernels.metal:81-132), which materialise a
 // [count,32,C] probability matrix; here each block streams K/V tiles of 32
@@ -18,7 +18,7 @@ namespace lun {
 
 struct AttnParams {
     const float *q;          // [count][4096], RoPE'd and query-scaled
-    const uint16_t *kv;      // BF16 pool
+    const float *kv;         // FP32 pool
     const int *page_table;
     int num_pages, layer;
     const StepParams *step;  // length before this call (device), or nullptr to
@@ -32,15 +32,15 @@ struct AttnParams {
 };
 
 constexpr int kTile = 32;
-constexpr int kKPad = 136;  // padded K row (BF16 elements): conflict-free 16-byte reads
+constexpr int kKPad = 132;  // padded K row (floats): conflict-free 16-byte reads across lanes
 
 // Kernels defined in headers have internal linkage: each translation unit that
 // launches one compiles its own copy.
 static __global__ void __launch_bounds__(128) attention_split_kernel(AttnParams p)
 {
-    __shared__ float qs[4][kHeadDim];
-    __shared__ __align__(16) uint16_t ks[kTile][kKPad];
-    __shared__ __align__(16) uint16_t vs[kTile][kHeadDim];
+    __shared__ __align__(16) float qs[4][kHeadDim];
+    __shared__ __align__(16) float ks[kTile][kKPad];
+    __shared__ __align__(16) float vs[kTile][kHeadDim];
     const int split = blockIdx.x, kvh = blockIdx.y, t = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int head = kvh * 4 + warp;
@@ -55,19 +55,19 @@ static __global__ void __launch_bounds__(128) attention_split_kernel(AttnParams 
     float o[4] = {0.f, 0.f, 0.f, 0.f};
     for (int p0 = begin; p0 < end; p0 += kTile) {
         __syncthreads();
-        // cooperative tile load: 32 rows x 256 B for K and for V = 1024 16-byte chunks
-        for (int c = threadIdx.x; c < 2 * kTile * 16; c += blockDim.x) {
-            int kind = c >> 9, row = (c >> 4) & 31, chunk = c & 15;
+        // cooperative tile load: 32 rows x 512 B for K and for V = 2048 16-byte chunks
+        for (int c = threadIdx.x; c < 2 * kTile * 32; c += blockDim.x) {
+            int kind = c >> 10, row = (c >> 5) & 31, chunk = c & 31;
             int pos = p0 + row;
-            uint4 v = make_uint4(0, 0, 0, 0);
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
             if (pos < end) {
                 int page = p.page_table[pos / kPage];
-                const uint16_t *src = p.kv + kv_offset(p.layer, p.num_pages, page, kind, kvh,
-                                                       pos % kPage);
-                v = *reinterpret_cast<const uint4 *>(src + chunk * 8);
+                const float *src = p.kv + kv_offset(p.layer, p.num_pages, page, kind, kvh,
+                                                    pos % kPage);
+                v = *reinterpret_cast<const float4 *>(src + chunk * 4);
             }
-            if (kind == 0) *reinterpret_cast<uint4 *>(&ks[row][chunk * 8]) = v;
-            else *reinterpret_cast<uint4 *>(&vs[row][chunk * 8]) = v;
+            if (kind == 0) *reinterpret_cast<float4 *>(&ks[row][chunk * 4]) = v;
+            else *reinterpret_cast<float4 *>(&vs[row][chunk * 4]) = v;
         }
         __syncthreads();
         // scores: lane -> position p0 + lane
@@ -75,18 +75,13 @@ static __global__ void __launch_bounds__(128) attention_split_kernel(AttnParams 
         if (p0 + lane < end) {
             float dot = 0.0f;
 #pragma unroll
-            for (int c = 0; c < 16; c++) {
-                uint4 kk = *reinterpret_cast<const uint4 *>(&ks[lane][c * 8]);
-                float4 qa = *reinterpret_cast<const float4 *>(&qs[warp][c * 8]);
-                float4 qb = *reinterpret_cast<const float4 *>(&qs[warp][c * 8 + 4]);
-                dot = fmaf(qa.x, bf16_lo(kk.x), dot);
-                dot = fmaf(qa.y, bf16_hi(kk.x), dot);
-                dot = fmaf(qa.z, bf16_lo(kk.y), dot);
-                dot = fmaf(qa.w, bf16_hi(kk.y), dot);
-                dot = fmaf(qb.x, bf16_lo(kk.z), dot);
-                dot = fmaf(qb.y, bf16_hi(kk.z), dot);
-                dot = fmaf(qb.z, bf16_lo(kk.w), dot);
-                dot = fmaf(qb.w, bf16_hi(kk.w), dot);
+            for (int c = 0; c < 32; c++) {
+                float4 kk = *reinterpret_cast<const float4 *>(&ks[lane][c * 4]);
+                float4 qa = *reinterpret_cast<const float4 *>(&qs[warp][c * 4]);
+                dot = fmaf(qa.x, kk.x, dot);
+                dot = fmaf(qa.y, kk.y, dot);
+                dot = fmaf(qa.z, kk.z, dot);
+                dot = fmaf(qa.w, kk.w, dot);
             }
             s = dot * kScoreScale;
         }
@@ -100,11 +95,11 @@ static __global__ void __launch_bounds__(128) attention_split_kernel(AttnParams 
         const int rows = min(kTile, end - p0);
         for (int j = 0; j < rows; j++) {
             float pj = __shfl_sync(0xffffffffu, prob, j);
-            uint2 vv = *reinterpret_cast<const uint2 *>(&vs[j][lane * 4]);
-            o[0] = fmaf(pj, bf16_lo(vv.x), o[0]);
-            o[1] = fmaf(pj, bf16_hi(vv.x), o[1]);
-            o[2] = fmaf(pj, bf16_lo(vv.y), o[2]);
-            o[3] = fmaf(pj, bf16_hi(vv.y), o[3]);
+            float4 vv = *reinterpret_cast<const float4 *>(&vs[j][lane * 4]);
+            o[0] = fmaf(pj, vv.x, o[0]);
+            o[1] = fmaf(pj, vv.y, o[1]);
+            o[2] = fmaf(pj, vv.z, o[2]);
+            o[3] = fmaf(pj, vv.w, o[3]);
         }
     }
     if (p.splits == 1) {

@@ -35,7 +35,7 @@ struct lun_device {
     float scales[kLayers][LUN_SLOT_COUNT] = {};
     uint16_t *embedding = nullptr;
     float *norms = nullptr, *final_norm = nullptr;
-    uint16_t *kv = nullptr;
+    float *kv = nullptr;
     int *page_table = nullptr;
     float *rope_cos = nullptr, *rope_sin = nullptr;
     StepParams *d_step = nullptr, *h_step = nullptr;
@@ -65,7 +65,7 @@ extern "C" void lun_device_plan(size_t context, size_t block, lun_device_bytes *
 {
     bytes->weight_bytes = (uint64_t)kLayerBytes * kLayers + (uint64_t)kVocab * kHidden * 2 +
                           (uint64_t)(2 * kLayers + 1) * kHidden * 4;
-    bytes->kv_bytes = (uint64_t)kLayers * pages_for(context) * 2 * kPageKind * 2;
+    bytes->kv_bytes = (uint64_t)kLayers * pages_for(context) * 2 * kPageKind * sizeof(float);
     uint64_t scratch = 0;
     scratch += sizeof(StepParams);
     scratch += (uint64_t)block * (2 * kHidden + 2 * kQuery + kInner) * 4;  // x h q attn act
@@ -135,7 +135,8 @@ extern "C" lun_device *lun_device_create(size_t context, size_t block, char *err
         goto bad;
     d->final_norm = d->norms + (size_t)2 * kLayers * kHidden;
     what = "KV cache";
-    if ((e = dalloc(&d->kv, (size_t)kLayers * d->num_pages * 2 * kPageKind * 2, kc)) != cudaSuccess)
+    if ((e = dalloc(&d->kv, (size_t)kLayers * d->num_pages * 2 * kPageKind * sizeof(float), kc)) !=
+        cudaSuccess)
         goto bad;
     what = "scratch";
     if ((e = dalloc(&d->d_step, sizeof(StepParams), sc)) != cudaSuccess ||

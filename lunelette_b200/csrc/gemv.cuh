@@ -3,6 +3,7 @@
 // Replaces project_fp8 / project_fp8_lookup (src/metal_kernels.metal:136-177,
 // 249-272) and, by fusion, the norm, rope, element and KV-blit steps that the
 // reference encodes around each projection (src/metal_encode.m:124-187).
+// K and V rows are stored in FP32, the reference's KV precision.
 //
 // Layout: W is row-major [rows][cols] E4M3 bytes; one warp owns a group of four
 // rows and streams them with 16-byte loads (16 codes per lane per load, two
@@ -43,7 +44,7 @@ struct GemvParams {
     const StepParams *step;            // device: sequence length before this call, or
     int length;                        //   nullptr to use this value instead
     int token_offset;                  // first token of this launch within the call
-    uint16_t *kv;                      // BF16 KV pool
+    float *kv;                         // FP32 KV pool
     const int *page_table;
     int num_pages, layer;
 };
@@ -152,9 +153,9 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, int g, int la
                     int kind = ra < kQuery + kKV ? 0 : 1;
                     int head = (ra - kQuery - kind * kKV) >> 7;
                     int page = p.page_table[pos / kPage], slot = pos % kPage;
-                    uint16_t *dst = p.kv + kv_offset(p.layer, p.num_pages, page, kind, head, slot);
-                    dst[j] = __bfloat16_as_ushort(__float2bfloat16_rn(a));
-                    dst[j + 64] = __bfloat16_as_ushort(__float2bfloat16_rn(b));
+                    float *dst = p.kv + kv_offset(p.layer, p.num_pages, page, kind, head, slot);
+                    dst[j] = a;
+                    dst[j + 64] = b;
                 }
             }
         }

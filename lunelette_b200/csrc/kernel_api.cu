@@ -74,7 +74,7 @@ LUN_API int lunelette_cuda_gemv_fp8(const uint8_t *W, size_t rows, size_t cols, 
 LUN_API int lunelette_cuda_qkv_rope(const uint8_t *W, const float *scales, const float *gain,
                                     const float *x, size_t count, size_t length,
                                     const float *rope_cos, const float *rope_sin, float *q_out,
-                                    uint16_t *kv_pool, const int *page_table, size_t num_pages,
+                                    float *kv_pool, const int *page_table, size_t num_pages,
                                     size_t layer, void *stream)
 {
     if (!W || !scales || !gain || !x || !count || !rope_cos || !rope_sin || !q_out || !kv_pool ||
@@ -156,9 +156,9 @@ LUN_API int lunelette_cuda_head_bf16(const uint16_t *W, size_t rows, size_t cols
 }
 
 // Causal GQA attention of `count` query rows (positions length..length+count-1)
-// over KV layer `layer` of a paged BF16 pool. part_acc/part_ml are caller scratch
+// over KV layer `layer` of a paged FP32 pool. part_acc/part_ml are caller scratch
 // of (slots*128) and (slots*2) floats; slots >= count*32.
-LUN_API int lunelette_cuda_attention(const float *q, const uint16_t *kv_pool, const int *page_table,
+LUN_API int lunelette_cuda_attention(const float *q, const float *kv_pool, const int *page_table,
                                      size_t num_pages, size_t layer, size_t length, size_t count,
                                      float *out, float *part_acc, float *part_ml, size_t slots,
                                      void *stream)

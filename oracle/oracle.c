@@ -24,6 +24,41 @@
 
 #define LANES 32
 
+/* Precision-study knobs (default 0 = the reference's FP32 everywhere). They let
+ * tests measure what a narrower storage format for KV rows (kv_rounding) or for
+ * projection inputs (input_rounding) does to per-layer drift: 1 rounds to BF16,
+ * 2 to FP16, both round-to-nearest-even. Never used as a reference result. */
+static int kv_rounding, input_rounding;
+
+void oracle_set_rounding(int kv, int input)
+{
+    kv_rounding = kv;
+    input_rounding = input;
+}
+
+static float round_to(float v, int mode)
+{
+    if (mode == 1) {
+        uint32_t bits;
+        memcpy(&bits, &v, 4);
+        bits = (bits + 0x7fffu + ((bits >> 16) & 1u)) & 0xffff0000u;
+        memcpy(&v, &bits, 4);
+    } else if (mode == 2) {
+        _Float16 h = (_Float16)v;
+        v = (float)h;
+    }
+    return v;
+}
+
+static void round_rows(float *v, size_t n, int mode)
+{
+    if (mode) {
+        for (size_t i = 0; i < n; i++) {
+            v[i] = round_to(v[i], mode);
+        }
+    }
+}
+
 void oracle_set_threads(int threads)
 {
 #ifdef _OPENMP
@@ -599,20 +634,26 @@ int oracle_forward(oracle_model *m, const int64_t *ids, size_t count, float *log
         float *keys = m->keys + (size_t)layer * m->context * KV;
         float *values = m->values + (size_t)layer * m->context * KV;
         oracle_norm(m->norms[layer][0], x, normed, H, count);
+        round_rows(normed, count * H, input_rounding);
         oracle_project_fp8(m->linear[layer][0], m->scale[layer][0], normed, q, Q, H, count);
         oracle_project_fp8(m->linear[layer][1], m->scale[layer][1], normed, k, KV, H, count);
         oracle_project_fp8(m->linear[layer][2], m->scale[layer][2], normed, v, KV, H, count);
         oracle_rope(q, cosine, sine, positions, rq, Q, count, 1);
         oracle_rope(k, cosine, sine, positions, keys + m->length * KV, KV, count, 0);
         memcpy(values + m->length * KV, v, count * KV * sizeof(float));
+        round_rows(keys + m->length * KV, count * KV, kv_rounding);
+        round_rows(values + m->length * KV, count * KV, kv_rounding);
         oracle_attention(rq, keys, values, attn, count, m->length, NULL);
+        round_rows(attn, count * Q, input_rounding);
         oracle_project_fp8(m->linear[layer][3], m->scale[layer][3], attn, o, H, Q, count);
         oracle_element(x, o, residual, count * H, 0);
         oracle_norm(m->norms[layer][1], residual, normed, H, count);
+        round_rows(normed, count * H, input_rounding);
         oracle_project_fp8(m->linear[layer][4], m->scale[layer][4], normed, gate, F, H, count);
         oracle_project_fp8(m->linear[layer][5], m->scale[layer][5], normed, up, F, H, count);
         oracle_element(gate, gate, gated, count * F, 1);
         oracle_element(gated, up, gated, count * F, 2);
+        round_rows(gated, count * F, input_rounding);
         oracle_project_fp8(m->linear[layer][6], m->scale[layer][6], gated, down, H, F, count);
         oracle_element(residual, down, x, count * H, 0);
         if (trace) {

@@ -48,6 +48,9 @@ void oracle_attention(const float *query, const float *keys, const float *values
     float *output, size_t count, size_t prefix, float *probabilities);
 void oracle_set_threads(int threads);
 int oracle_threads(void);
+/* Precision study only (default 0,0 = FP32 as the reference): round stored KV
+ * rows and/or projection inputs to 1 = BF16 or 2 = FP16 to measure drift. */
+void oracle_set_rounding(int kv, int input);
 
 /* ---- model level ---- */
 typedef struct oracle_model oracle_model;

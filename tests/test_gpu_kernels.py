@@ -20,8 +20,24 @@ def torch_cuda():
     return torch
 
 
+_KEEP = []  # device copies stay referenced until the test's kernels finished
+
+
+@pytest.fixture(autouse=True)
+def _release_device_copies():
+    yield
+    import torch
+    torch.cuda.synchronize()
+    _KEEP.clear()
+
+
 def dev(torch, array):
-    return torch.from_numpy(np.ascontiguousarray(array)).cuda()
+    """Device copy that outlives the (asynchronous) launches of this test.
+    A temporary would go back to torch's caching allocator at once and could be
+    handed to the next copy before the kernel reads it."""
+    t = torch.from_numpy(np.ascontiguousarray(array)).cuda()
+    _KEEP.append(t)
+    return t
 
 
 def ptr(t):
@@ -152,8 +168,6 @@ def kv_rows(pool_np, page_table, num_pages, layer, kind, positions):
     return np.stack(out)
 
 
-def bf16_to_f32(u16):
-    return (np.asarray(u16, np.uint32) << 16).view(np.float32)
 
 
 def test_qkv_rope_kv_store_matches_oracle(lib, oracle, torch_cuda):
@@ -171,10 +185,10 @@ def test_qkv_rope_kv_store_matches_oracle(lib, oracle, torch_cuda):
     sin = np.zeros((num_pages * 64, 128), np.float32)
     for p in range(num_pages * 64):
         cos[p], sin[p] = oracle.yarn(p)
-    pool = torch.zeros((layer + 1) * num_pages * 2 * 8 * 64 * 128, dtype=torch.int16, device="cuda")
+    pool = torch.zeros((layer + 1) * num_pages * 2 * 8 * 64 * 128, dtype=torch.float32, device="cuda")
     q_out = torch.empty((count, 4096), dtype=torch.float32, device="cuda")
     rc = lib.lunelette_cuda_qkv_rope(
-        ptr(dev(torch, codes)), ptr(dev(torch, scales)), ptr(dev(torch, gain)), ptr(dev(torch, x)),
+        ptr(dev(torch, codes)), scales.ctypes.data, ptr(dev(torch, gain)), ptr(dev(torch, x)),
         count, length, ptr(dev(torch, cos)), ptr(dev(torch, sin)), ptr(q_out), ptr(pool),
         ptr(dev(torch, page_table)), num_pages, layer, stream(torch))
     assert rc == 0
@@ -186,12 +200,12 @@ def test_qkv_rope_kv_store_matches_oracle(lib, oracle, torch_cuda):
     rk = oracle.rope(k, cos[positions], sin[positions], positions, 0)
     got_q = q_out.cpu().numpy()
     assert np.abs(got_q - rq).max() <= 1e-5 * np.abs(rq).max()
-    pool_np = pool.cpu().numpy().view(np.uint16)
-    got_k = bf16_to_f32(kv_rows(pool_np, page_table, num_pages, layer, 0, positions))
-    got_v = bf16_to_f32(kv_rows(pool_np, page_table, num_pages, layer, 1, positions))
-    # BF16 storage: within one BF16 rounding of the oracle's FP32 values
-    assert np.all(np.abs(got_k - rk) <= 2.0 ** -8 * np.abs(rk) + 1e-6 * np.abs(rk).max())
-    assert np.all(np.abs(got_v - v) <= 2.0 ** -8 * np.abs(v) + 1e-6 * np.abs(v).max())
+    pool_np = pool.cpu().numpy()
+    got_k = kv_rows(pool_np, page_table, num_pages, layer, 0, positions)
+    got_v = kv_rows(pool_np, page_table, num_pages, layer, 1, positions)
+    # FP32 storage, as the reference's KV blit: only summation-order noise remains
+    assert np.abs(got_k - rk).max() <= 1e-5 * np.abs(rk).max()
+    assert np.abs(got_v - v).max() <= 1e-5 * np.abs(v).max()
     # layer 0 untouched
     assert not pool_view(pool_np, num_pages)[0].any()
 
@@ -247,12 +261,12 @@ def test_head_bf16_matches_oracle_and_flags_nonfinite(lib, oracle, torch_cuda):
 
 
 def write_pool(k_rows, v_rows, page_table, num_pages, layer, layers):
-    """Lay FP32 K/V rows [positions][1024] into a BF16 pool (returns uint16)."""
-    pool = np.zeros((layers, num_pages, 2, 8, 64, 128), np.uint16)
+    """Lay FP32 K/V rows [positions][1024] into the paged FP32 pool layout."""
+    pool = np.zeros((layers, num_pages, 2, 8, 64, 128), np.float32)
     for p in range(k_rows.shape[0]):
         page = page_table[p // 64]
-        pool[layer, page, 0, :, p % 64, :] = (bf16_round(k_rows[p]).view(np.uint32) >> 16).reshape(8, 128)
-        pool[layer, page, 1, :, p % 64, :] = (bf16_round(v_rows[p]).view(np.uint32) >> 16).reshape(8, 128)
+        pool[layer, page, 0, :, p % 64, :] = k_rows[p].reshape(8, 128)
+        pool[layer, page, 1, :, p % 64, :] = v_rows[p].reshape(8, 128)
     return pool.reshape(-1)
 
 
@@ -260,7 +274,7 @@ def run_attention(lib, torch, q, pool, page_table, num_pages, layer, length, cou
     out = torch.empty((count, 4096), dtype=torch.float32, device="cuda")
     acc = torch.empty(slots * 128, dtype=torch.float32, device="cuda")
     ml = torch.empty(slots * 2, dtype=torch.float32, device="cuda")
-    rc = lib.lunelette_cuda_attention(ptr(dev(torch, q)), ptr(dev(torch, pool.view(np.int16))),
+    rc = lib.lunelette_cuda_attention(ptr(dev(torch, q)), ptr(dev(torch, pool)),
                                       ptr(dev(torch, page_table)), num_pages, layer, length, count,
                                       ptr(out), ptr(acc), ptr(ml), slots, stream(torch))
     assert rc == 0
@@ -268,7 +282,7 @@ def run_attention(lib, torch, q, pool, page_table, num_pages, layer, length, cou
 
 
 def test_attention_prefix_matches_reference_expectation(lib, oracle, torch_cuda):
-    # tests/test_metal.m:532-578 inputs (exactly representable in BF16)
+    # tests/test_metal.m:532-578 inputs
     torch = torch_cuda
     count, prefix = 2, 3
     total = count + prefix
@@ -307,8 +321,8 @@ def test_attention_random_matches_oracle(lib, oracle, torch_cuda, length, count,
     total = length + count
     num_pages = (total + 63) // 64 + 1
     table = rng.permutation(num_pages).astype(np.int32)
-    k = bf16_round(rng.standard_normal((total, 1024)).astype(np.float32))
-    v = bf16_round(rng.standard_normal((total, 1024)).astype(np.float32))
+    k = rng.standard_normal((total, 1024)).astype(np.float32)
+    v = rng.standard_normal((total, 1024)).astype(np.float32)
     q = rng.standard_normal((count, 4096)).astype(np.float32)
     layer = 2
     pool = write_pool(k, v, table, num_pages, layer, 3)

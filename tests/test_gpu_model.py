@@ -51,7 +51,7 @@ def test_memory_and_limits(runtime):
     assert mem["strategy"] == L.COMPACT_FP8_ARITHMETIC  # NULL options -> product default
     assert mem["weight_bytes"] == 3026190336 + 805306368 + 53 * 3072 * 4
     assert mem["conversion_stage_bytes"] == 0
-    assert mem["kv_bytes"] == 26 * 2 * 256 * 1024 * 2
+    assert mem["kv_bytes"] == 26 * 2 * 256 * 1024 * 4  # FP32 KV, as the reference
     assert mem["total_bytes"] == mem["weight_bytes"] + mem["scratch_bytes"] + mem["kv_bytes"]
     assert runtime.limits() == (256, 256)
 
