@@ -71,6 +71,21 @@ int lunelette_cuda_attention(const float *q, const float *kv_pool, const int *pa
     size_t num_pages, size_t layer, size_t length, size_t count, float *out, float *part_acc,
     float *part_ml, size_t slots, void *stream);
 
+/* Same attention as lunelette_cuda_attention, for callers that cannot allocate
+ * device memory (an engine that has already reserved the whole device for its
+ * own pool, or a latency-critical loop where cudaMalloc/cudaFree would
+ * synchronise the device). It allocates nothing: its partial results live in a
+ * fixed array inside the library, 4096 slots (2,129,920 bytes) per GPU, held
+ * until the process exits, so count may be at most 128; larger counts are
+ * rejected with a message in error[0..capacity). The first call on a device
+ * looks up that array's device address, so make it before any stream capture.
+ * Every call shares the array: calls that overlap on the GPU (other streams,
+ * other threads) race and must be serialised by the caller.
+ * No counterpart in the reference (its Metal runtime owns all scratch). */
+int lunelette_cuda_attention_noalloc(const float *q, const float *kv_pool, const int *page_table,
+    size_t num_pages, size_t layer, size_t length, size_t count, float *out, void *stream,
+    char *error, size_t capacity);
+
 /* ---------------- model-level test support */
 
 /* Keep every layer's output rows (which 0..25) and the final-norm rows (26) of

@@ -70,6 +70,7 @@ SIGNATURES = {
     "lunelette_cuda_rmsnorm": (ctypes.c_int, [P, P, SZ, SZ, P, P]),
     "lunelette_cuda_head_bf16": (ctypes.c_int, [P, SZ, SZ, P, P, P, P, P]),
     "lunelette_cuda_attention": (ctypes.c_int, [P, P, P, SZ, SZ, SZ, SZ, P, P, P, SZ, P]),
+    "lunelette_cuda_attention_noalloc": (ctypes.c_int, [P, P, P, SZ, SZ, SZ, SZ, P, P, ERR, SZ]),
     "lunelette_cuda_trace": (ctypes.c_int, [P, ctypes.c_int]),
     "lunelette_cuda_trace_copy": (ctypes.c_int, [P, ctypes.c_int, P, SZ]),
     "lunelette_cuda_length": (SZ, [P]),
