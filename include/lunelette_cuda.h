@@ -36,8 +36,10 @@ int lunelette_cuda_gemv_fp8(const uint8_t *W, size_t rows, size_t cols, float sc
     const float *x, const float *res, size_t count, float *y, void *stream);
 
 /* Fused input RMSNorm + q/k/v projection + YaRN RoPE (+ query scale) + KV store
- * for `count` tokens at positions length..length+count-1. W is [6144][3072]
- * (q rows, then k, then v); scales is a HOST array {q, k, v}; q_out [count][4096];
+ * for `count` tokens at positions length..length+count-1. W is [6144][3072]:
+ * q rows, then k, then v, and inside every 128-row head row j < 64 stored at
+ * 2j and row j + 64 at 2j + 1 (RoPE pairs adjacent); scales is a HOST array
+ * {q, k, v}; q_out [count][4096] in the checkpoint's (unpermuted) order;
  * kv_pool is the paged FP32 pool [layer][page][K|V][8 heads][64 slots][128].
  * Replaces norm + 3x project_fp8 + 2x rope + the KV blit
  * (src/metal_encode.m:129-153, src/metal_kernels.metal:29-78). */
@@ -47,7 +49,7 @@ int lunelette_cuda_qkv_rope(const uint8_t *W, const float *scales, const float *
     void *stream);
 
 /* Fused post-attention RMSNorm + gate/up projection + SwiGLU. W is [18432][3072]
- * with 128-row gate and up blocks alternating; act [count][9216].
+ * with gate row f at row 2f and up row f at row 2f+1; act [count][9216].
  * Replaces norm + 2x project_fp8 + SiLU + multiply (src/metal_encode.m:162-172). */
 int lunelette_cuda_gateup_swiglu(const uint8_t *W, float scale_gate, float scale_up,
     const float *gain, const float *x, size_t count, float *act, void *stream);
@@ -102,6 +104,13 @@ int lunelette_cuda_trace_copy(lunelette_metal *context, int which, float *out, s
  * published (checkpoint_create needs another prefill/append/decode first). */
 int lunelette_cuda_decode_loop(lunelette_metal *context, int64_t first_token, size_t steps,
     int64_t *tokens, float *milliseconds, int *launches_per_step, char *error, size_t capacity);
+
+/* Phase timing of the persistent decode kernel: while enabled, each single-token
+ * step records %globaltimer (ns) at its start and after each of its 132 grid
+ * barriers (26 layers x {qkv, attention, o, gate/up, down}, head, greedy pick);
+ * copy up to 133 entries of the most recent launch's first step. */
+int lunelette_cuda_timeline(lunelette_metal *context, int enable);
+int lunelette_cuda_timeline_copy(lunelette_metal *context, unsigned long long *out, size_t entries);
 
 /* Current sequence length (0 for NULL). */
 size_t lunelette_cuda_length(const lunelette_metal *context);

@@ -76,6 +76,8 @@ SIGNATURES = {
     "lunelette_cuda_length": (SZ, [P]),
     "lunelette_cuda_decode_loop": (ctypes.c_int, [P, ctypes.c_int64, SZ, P, P, P, ERR, SZ]),
     "lunelette_cuda_yarn": (ctypes.c_int, [ctypes.c_uint32, P, P]),
+    "lunelette_cuda_timeline": (ctypes.c_int, [P, ctypes.c_int]),
+    "lunelette_cuda_timeline_copy": (ctypes.c_int, [P, P, SZ]),
     "lunelette_cuda_validate_checkpoint": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int, ERR, SZ]),
     "lunelette_cuda_synth_checkpoint": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_uint64, ERR, SZ]),
     "lunelette_cuda_e4m3_encode": (ctypes.c_ubyte, [ctypes.c_float]),
@@ -228,6 +230,16 @@ class Runtime:
                                                 ctypes.byref(ms), ctypes.byref(launches), err, 512):
             raise LuneletteError(err.value.decode())
         return tokens, ms.value, launches.value
+
+    def timeline(self, enable=True):
+        if library().lunelette_cuda_timeline(self.handle, 1 if enable else 0):
+            raise LuneletteError("timeline enable failed")
+
+    def timeline_copy(self, entries=133):
+        out = np.zeros(entries, dtype=np.uint64)
+        if library().lunelette_cuda_timeline_copy(self.handle, out.ctypes.data, entries):
+            raise LuneletteError("timeline copy failed")
+        return out
 
     def trace(self, enable=True):
         if library().lunelette_cuda_trace(self.handle, 1 if enable else 0):

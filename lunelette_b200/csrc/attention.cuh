@@ -33,51 +33,80 @@ struct AttnParams {
 
 constexpr int kTile = 32;
 constexpr int kKPad = 132;  // padded K row (floats): conflict-free 16-byte reads across lanes
+constexpr int kStageFloats = kTile * kKPad + kTile * kHeadDim;
+// dynamic shared memory: q for 4 heads + two K/V tile stages
+constexpr int kAttnSmemBytes = (4 * kHeadDim + 2 * kStageFloats) * 4;
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool full)
+{
+    unsigned dst = (unsigned)__cvta_generic_to_shared(smem);
+    int bytes = full ? 16 : 0;  // 0: no global read, zero-fill
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(gmem), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// Issue the copies of one 32-position K/V tile (2 x 16 KB) into a stage.
+__device__ __forceinline__ void attention_issue_tile(const AttnParams &p, float *stage, int kvh, int p0,
+                                                     int end)
+{
+    float *ks = stage, *vs = stage + kTile * kKPad;
+    for (int c = threadIdx.x; c < 2 * kTile * 32; c += blockDim.x) {
+        int kind = c >> 10, row = (c >> 5) & 31, chunk = c & 31;
+        int pos = p0 + row;
+        bool in = pos < end;
+        const float *src = p.kv;
+        if (in) {
+            int page = p.page_table[pos / kPage];
+            src = p.kv + kv_offset(p.layer, p.num_pages, page, kind, kvh, pos % kPage) + chunk * 4;
+        }
+        float *dst = kind == 0 ? ks + row * kKPad + chunk * 4 : vs + row * kHeadDim + chunk * 4;
+        cp_async16(dst, src, in);
+    }
+    cp_async_commit();
+}
 
 // Kernels defined in headers have internal linkage: each translation unit that
 // launches one compiles its own copy.
 static __global__ void __launch_bounds__(128) attention_split_kernel(AttnParams p)
 {
-    __shared__ __align__(16) float qs[4][kHeadDim];
-    __shared__ __align__(16) float ks[kTile][kKPad];
-    __shared__ __align__(16) float vs[kTile][kHeadDim];
+    extern __shared__ float4 attn_smem4[];
+    float *sm = reinterpret_cast<float *>(attn_smem4);
+    float *qs = sm;  // [4][128]
+    float *stages = sm + 4 * kHeadDim;
     const int split = blockIdx.x, kvh = blockIdx.y, t = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int head = kvh * 4 + warp;
+    pdl_wait();  // q and the newest K/V rows come from the previous kernel
+    pdl_launch_dependents();
     const int total = (p.step ? p.step->length : p.length) + p.token_offset + t + 1;
     const int begin = split * p.split_len;
     const int end = min(begin + p.split_len, total);
+    const int tiles = end > begin ? (end - begin + kTile - 1) / kTile : 0;
+    if (tiles > 0) attention_issue_tile(p, stages, kvh, begin, end);
 
     for (int i = threadIdx.x; i < 4 * kHeadDim; i += blockDim.x)
-        qs[i / kHeadDim][i % kHeadDim] = p.q[(size_t)t * kQuery + kvh * 4 * kHeadDim + i];
+        qs[i] = p.q[(size_t)t * kQuery + kvh * 4 * kHeadDim + i];
 
     float m_run = -INFINITY, l_run = 0.0f;
     float o[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int p0 = begin; p0 < end; p0 += kTile) {
+    for (int it = 0; it < tiles; it++) {
+        const int p0 = begin + it * kTile;
+        if (it + 1 < tiles) attention_issue_tile(p, stages + ((it + 1) & 1) * kStageFloats, kvh, p0 + kTile, end);
+        else cp_async_commit();  // empty group keeps the wait count uniform
+        cp_async_wait_one();
         __syncthreads();
-        // cooperative tile load: 32 rows x 512 B for K and for V = 2048 16-byte chunks
-        for (int c = threadIdx.x; c < 2 * kTile * 32; c += blockDim.x) {
-            int kind = c >> 10, row = (c >> 5) & 31, chunk = c & 31;
-            int pos = p0 + row;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (pos < end) {
-                int page = p.page_table[pos / kPage];
-                const float *src = p.kv + kv_offset(p.layer, p.num_pages, page, kind, kvh,
-                                                    pos % kPage);
-                v = *reinterpret_cast<const float4 *>(src + chunk * 4);
-            }
-            if (kind == 0) *reinterpret_cast<float4 *>(&ks[row][chunk * 4]) = v;
-            else *reinterpret_cast<float4 *>(&vs[row][chunk * 4]) = v;
-        }
-        __syncthreads();
+        const float *ks = stages + (it & 1) * kStageFloats;
+        const float *vs = ks + kTile * kKPad;
         // scores: lane -> position p0 + lane
         float s = -INFINITY;
         if (p0 + lane < end) {
             float dot = 0.0f;
 #pragma unroll
             for (int c = 0; c < 32; c++) {
-                float4 kk = *reinterpret_cast<const float4 *>(&ks[lane][c * 4]);
-                float4 qa = *reinterpret_cast<const float4 *>(&qs[warp][c * 4]);
+                float4 kk = *reinterpret_cast<const float4 *>(ks + lane * kKPad + c * 4);
+                float4 qa = *reinterpret_cast<const float4 *>(qs + warp * kHeadDim + c * 4);
                 dot = fmaf(qa.x, kk.x, dot);
                 dot = fmaf(qa.y, kk.y, dot);
                 dot = fmaf(qa.z, kk.z, dot);
@@ -95,12 +124,13 @@ static __global__ void __launch_bounds__(128) attention_split_kernel(AttnParams 
         const int rows = min(kTile, end - p0);
         for (int j = 0; j < rows; j++) {
             float pj = __shfl_sync(0xffffffffu, prob, j);
-            float4 vv = *reinterpret_cast<const float4 *>(&vs[j][lane * 4]);
+            float4 vv = *reinterpret_cast<const float4 *>(vs + j * kHeadDim + lane * 4);
             o[0] = fmaf(pj, vv.x, o[0]);
             o[1] = fmaf(pj, vv.y, o[1]);
             o[2] = fmaf(pj, vv.z, o[2]);
             o[3] = fmaf(pj, vv.w, o[3]);
         }
+        __syncthreads();  // this stage is refilled two iterations later
     }
     if (p.splits == 1) {
         float inv = 1.0f / l_run;
@@ -121,6 +151,8 @@ static __global__ void __launch_bounds__(128) attention_split_kernel(AttnParams 
 static __global__ void __launch_bounds__(128) attention_combine_kernel(AttnParams p)
 {
     const int head = blockIdx.x, t = blockIdx.y, d = threadIdx.x;
+    pdl_wait();
+    pdl_launch_dependents();
     const size_t base = ((size_t)t * kQueryHeads + head) * p.splits;
     float m = -INFINITY;
     for (int s = 0; s < p.splits; s++) {
@@ -143,6 +175,8 @@ static __global__ void embed_kernel(const uint16_t *embedding, const StepParams 
                              int count)
 {
     const int t = blockIdx.x;
+    pdl_wait();  // ids come from the host copy or the previous step's greedy kernel
+    pdl_launch_dependents();
     if (t >= count) return;
     const uint16_t *row = embedding + (size_t)step->ids[t] * kHidden;
     for (int c = threadIdx.x; c < kHidden / 2; c += blockDim.x) {

@@ -22,7 +22,7 @@ constexpr int kPageKind = kKVHeads * kPage * kHeadDim;  // elements of K (or V) 
 constexpr float kNormEps = 1e-5f;
 constexpr float kScoreScale = 0.08838834764831845f;  // 1/sqrt(128) as the reference rounds it
 constexpr int kQKVRows = kQuery + 2 * kKV;       // 6144
-constexpr int kGateUpRows = 2 * kInner;          // 18432, 128-row gate/up blocks interleaved
+constexpr int kGateUpRows = 2 * kInner;          // 18432: gate and up rows alternate (2f, 2f+1)
 
 // Per-call parameters that kernels read from device memory, so that one
 // captured graph serves every step: the sequence length before the call.
@@ -33,6 +33,32 @@ struct StepParams {
     int pad;
     int ids[256];
 };
+
+// Programmatic dependent launch: the next kernel in the stream may start before
+// this one finishes; pdl_wait() blocks until the previous kernel completed and
+// its writes are visible (a no-op when launched without the attribute).
+// Everything before pdl_wait() may only read immutable data (weights).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Ask L2 to fetch this block's share of [base, base+bytes) (bytes and base
+// 16-byte aligned), in 16 KB bulk prefetches spread over the block's threads.
+// Fire-and-forget: nothing waits for it; a later read finds the lines in L2.
+__device__ __forceinline__ void l2_prefetch_share(const void *base, size_t bytes)
+{
+    if (!base || !bytes) return;
+    size_t per = ((bytes + gridDim.x - 1) / gridDim.x + 15) & ~(size_t)15;
+    size_t begin = (size_t)blockIdx.x * per;
+    size_t end = begin + per < bytes ? begin + per : bytes;
+    const char *p = static_cast<const char *>(base);
+    for (size_t off = begin + (size_t)threadIdx.x * 16384; off < end; off += (size_t)blockDim.x * 16384) {
+        uint32_t n = (uint32_t)(end - off < 16384 ? end - off : 16384);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p + off), "r"(n) : "memory");
+    }
+}
 
 // 16-byte streaming load that bypasses L1 allocation (weights are read once).
 __device__ __forceinline__ uint4 ld_stream(const void *p)

@@ -3,6 +3,7 @@
 // (src/metal_encode.m:124-215) and execute() commit/wait (src/metal_runtime.m:349-432).
 #include "device.h"
 #include "kernels.h"
+#include "mega_params.cuh"
 
 #include <new>
 #include <stdio.h>
@@ -52,6 +53,17 @@ struct lun_device {
     int *d_tokens = nullptr, *d_partials = nullptr;
     cudaGraphExec_t decode_graph = nullptr;
     int launches_per_step = 0;
+    // persistent decode kernel state
+    bool use_mega = true;
+    float *d_scales = nullptr;          // [26][7]
+    unsigned *mega_barrier = nullptr;   // [2], zeroed before every launch
+    unsigned *attn_count = nullptr;     // [8], self-resetting
+    int *mega_error = nullptr, *h_error = nullptr;
+    float *arg_val = nullptr;
+    int *arg_idx = nullptr;
+    bool prefetch = true;                        // next-matrix L2 prefetch
+    unsigned long long *timeline = nullptr;      // per-barrier timestamps (optional)
+    bool record_timeline = false;
     lun_device_bytes owned = {};
 };
 
@@ -151,12 +163,29 @@ extern "C" lun_device *lun_device_create(size_t context, size_t block, char *err
         (e = dalloc(&d->rope_cos, context * kHeadDim * 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->rope_sin, context * kHeadDim * 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->page_table, (size_t)d->num_pages * 4, sc)) != cudaSuccess ||
-        (e = dalloc(&d->d_flag, 4, sc)) != cudaSuccess)
+        (e = dalloc(&d->d_flag, 4, sc)) != cudaSuccess ||
+        (e = dalloc(&d->d_scales, (size_t)kLayers * LUN_SLOT_COUNT * 4, sc)) != cudaSuccess ||
+        (e = dalloc(&d->mega_barrier, 2 * sizeof(unsigned), sc)) != cudaSuccess ||
+        (e = dalloc(&d->attn_count, kKVHeads * sizeof(unsigned), sc)) != cudaSuccess ||
+        (e = dalloc(&d->mega_error, sizeof(int), sc)) != cudaSuccess ||
+        (e = dalloc(&d->arg_val, (size_t)d->sm_count * 4, sc)) != cudaSuccess ||
+        (e = dalloc(&d->arg_idx, (size_t)d->sm_count * 4, sc)) != cudaSuccess ||
+        (e = dalloc(&d->d_tokens, context * sizeof(int), sc)) != cudaSuccess)
         goto bad;
+    if ((e = cudaMemset(d->attn_count, 0, kKVHeads * sizeof(unsigned))) != cudaSuccess ||
+        (e = cudaMemset(d->mega_error, 0, sizeof(int))) != cudaSuccess)
+        goto bad;
+    {
+        const char *mega = getenv("LUNELETTE_MEGA");
+        d->use_mega = !(mega && mega[0] == '0');
+        const char *prefetch = getenv("LUNELETTE_PREFETCH");
+        d->prefetch = !(prefetch && prefetch[0] == '0');
+    }
     what = "pinned host buffers";
     if ((e = cudaMallocHost((void **)&d->h_step, sizeof(StepParams))) != cudaSuccess ||
         (e = cudaMallocHost((void **)&d->h_logits, (size_t)kVocab * 4)) != cudaSuccess ||
         (e = cudaMallocHost((void **)&d->h_flag, 4)) != cudaSuccess ||
+        (e = cudaMallocHost((void **)&d->h_error, 4)) != cudaSuccess ||
         (e = cudaMallocHost(&d->staging[0], kStagingBytes)) != cudaSuccess ||
         (e = cudaMallocHost(&d->staging[1], kStagingBytes)) != cudaSuccess ||
         (e = cudaEventCreateWithFlags(&d->staging_done[0], cudaEventDisableTiming)) != cudaSuccess ||
@@ -207,6 +236,14 @@ extern "C" void lun_device_destroy(lun_device *d)
     cudaFree(d->trace_buf);
     cudaFree(d->d_tokens);
     cudaFree(d->d_partials);
+    cudaFree(d->d_scales);
+    cudaFree(d->mega_barrier);
+    cudaFree(d->attn_count);
+    cudaFree(d->mega_error);
+    cudaFree(d->arg_val);
+    cudaFree(d->arg_idx);
+    cudaFree(d->timeline);
+    cudaFreeHost(d->h_error);
     if (d->decode_graph) cudaGraphExecDestroy(d->decode_graph);
     cudaFreeHost(d->h_step);
     cudaFreeHost(d->h_logits);
@@ -248,8 +285,18 @@ extern "C" int lun_device_upload_linear(lun_device *d, int index, int layer, int
     case LUN_SLOT_Q:
     case LUN_SLOT_K:
     case LUN_SLOT_V: {
+        // group-major: within each 128-row head, row j < 64 goes to 2j and row
+        // j + 64 to 2j + 1, so the RoPE pairs (j, j+64) sit in adjacent rows
         size_t row0 = slot == LUN_SLOT_Q ? 0 : (slot == LUN_SLOT_K ? kQuery : kQuery + kKV);
-        e = cudaMemcpyAsync(base + row0 * kHidden, src, rows * cols, cudaMemcpyHostToDevice, d->stream);
+        e = cudaSuccess;
+        for (size_t head = 0; e == cudaSuccess && head < rows / 128; head++) {
+            uint8_t *dst = base + (row0 + head * 128) * cols;
+            const uint8_t *s0 = src + head * 128 * cols;
+            e = cudaMemcpy2DAsync(dst, 2 * cols, s0, cols, cols, 64, cudaMemcpyHostToDevice, d->stream);
+            if (e == cudaSuccess)
+                e = cudaMemcpy2DAsync(dst + cols, 2 * cols, s0 + 64 * cols, cols, cols, 64,
+                                      cudaMemcpyHostToDevice, d->stream);
+        }
         break;
     }
     case LUN_SLOT_O:
@@ -257,11 +304,9 @@ extern "C" int lun_device_upload_linear(lun_device *d, int index, int layer, int
         break;
     case LUN_SLOT_GATE:
     case LUN_SLOT_UP: {
-        // 128-row blocks interleave gate and up: block b of gate -> 2b, of up -> 2b+1
-        size_t block_bytes = (size_t)128 * cols;
-        uint8_t *dst = base + kLayerQKV + kLayerO + (slot == LUN_SLOT_UP ? block_bytes : 0);
-        e = cudaMemcpy2DAsync(dst, 2 * block_bytes, src, block_bytes, block_bytes, rows / 128,
-                              cudaMemcpyHostToDevice, d->stream);
+        // group-major: gate row f goes to 2f and up row f to 2f + 1
+        uint8_t *dst = base + kLayerQKV + kLayerO + (slot == LUN_SLOT_UP ? cols : 0);
+        e = cudaMemcpy2DAsync(dst, 2 * cols, src, cols, cols, rows, cudaMemcpyHostToDevice, d->stream);
         break;
     }
     case LUN_SLOT_DOWN:
@@ -311,6 +356,8 @@ extern "C" int lun_device_upload_finish(lun_device *d, char *error, size_t capac
 {
     cudaError_t e = cudaStreamSynchronize(d->stream);
     if (e != cudaSuccess) return fail(error, capacity, "weight upload failed", e);
+    e = cudaMemcpy(d->d_scales, d->scales, sizeof d->scales, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return fail(error, capacity, "scale upload failed", e);
     return 0;
 }
 
@@ -365,6 +412,14 @@ static GemvParams layer_gemv(lun_device *d, int layer, int which)
         p.cols = kInner;
         p.scale[0] = s[LUN_SLOT_DOWN];
         break;
+    }
+    // The step reads the FP8 weights front to back (qkv, o, gate/up, down, next
+    // layer's qkv): each projection prefetches the next matrix into L2.
+    static const size_t next_bytes[4] = {kLayerO, kLayerGateUp, kLayerDown, kLayerQKV};
+    if (which < 3 || layer + 1 < kLayers) {
+        p.prefetch = p.W + (which == 0 ? kLayerQKV : which == 1 ? kLayerO
+                            : which == 2 ? kLayerGateUp : kLayerDown);
+        p.prefetch_bytes = next_bytes[which];
     }
     return p;
 }
@@ -434,13 +489,56 @@ static cudaError_t run_attention(lun_device *d, int layer, int count, size_t len
     return lun_launch_attention(a, count, d->stream);
 }
 
+// The persistent decode kernel for `steps` batch-1 steps starting from d_step
+// (length and ids[0]); it advances d_step and logs the greedy ids in d_tokens.
+static cudaError_t launch_mega(lun_device *d, int steps)
+{
+    MegaParams p;
+    memset(&p, 0, sizeof p);
+    p.w8 = d->w8;
+    p.scales = d->d_scales;
+    p.embedding = d->embedding;
+    p.norms = d->norms;
+    p.final_norm = d->final_norm;
+    p.kv = d->kv;
+    p.page_table = d->page_table;
+    p.num_pages = d->num_pages;
+    p.rope_cos = d->rope_cos;
+    p.rope_sin = d->rope_sin;
+    p.step = d->d_step;
+    p.x = d->x;
+    p.h = d->h;
+    p.q = d->q;
+    p.attn = d->attn;
+    p.act = d->act;
+    p.part_acc = d->part_acc;
+    p.part_ml = d->part_ml;
+    p.attn_count = d->attn_count;
+    AttnParams plan;
+    lun_attention_plan(&plan, (int)d->context, 1, d->sm_count, (int)kPartSlots);
+    p.split_len = plan.split_len;
+    p.splits = plan.splits;
+    p.logits = d->logits;
+    p.nonfinite = d->d_flag;
+    p.arg_val = d->arg_val;
+    p.arg_idx = d->arg_idx;
+    p.tokens = d->d_tokens;
+    p.barrier = d->mega_barrier;
+    p.error = d->mega_error;
+    p.steps = steps;
+    p.timeline = d->record_timeline ? d->timeline : nullptr;
+    p.prefetch = d->prefetch ? 1 : 0;
+    cudaError_t e = cudaMemsetAsync(d->mega_barrier, 0, 2 * sizeof(unsigned), d->stream);
+    if (e != cudaSuccess) return e;
+    return lun_launch_decode_mega(p, d->sm_count, d->stream);
+}
+
 // One decode step reading length/ids from d_step, ending with device greedy
 // selection that advances d_step; capturable.
 static cudaError_t enqueue_decode_step(lun_device *d, int *launches)
 {
     int n = 0;
-    embed_kernel<<<1, 256, 0, d->stream>>>(d->embedding, d->d_step, d->x, 1);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = lun_launch_embed(d->embedding, d->d_step, d->x, 1, d->stream);
     n++;
     for (int layer = 0; e == cudaSuccess && layer < kLayers; layer++) {
         if ((e = run_projection(d, layer, 0, 1)) != cudaSuccess ||
@@ -484,12 +582,35 @@ extern "C" int lun_device_decode_loop(lun_device *d, int64_t first_token, size_t
     const char *what = "decode loop setup";
     cudaEvent_t start = nullptr, stop = nullptr;
     int *host_tokens = nullptr;
-    if (!d->d_tokens) {
-        if ((e = cudaMalloc((void **)&d->d_tokens, d->context * sizeof(int))) != cudaSuccess ||
-            (e = cudaMalloc((void **)&d->d_partials, 2 * kArgmaxBlocks * sizeof(int))) != cudaSuccess)
+    if (!d->d_partials &&
+        (e = cudaMalloc((void **)&d->d_partials, 2 * kArgmaxBlocks * sizeof(int))) != cudaSuccess)
+        goto bad;
+    if (d->use_mega) {
+        what = "decode loop (persistent kernel)";
+        d->h_step->length = (int)length;
+        d->h_step->count = 1;
+        d->h_step->generated = 0;
+        d->h_step->ids[0] = (int)first_token;
+        if ((e = cudaEventCreate(&start)) != cudaSuccess || (e = cudaEventCreate(&stop)) != cudaSuccess ||
+            (e = cudaMemcpyAsync(d->d_step, d->h_step, sizeof(StepParams), cudaMemcpyHostToDevice,
+                                 d->stream)) != cudaSuccess ||
+            (e = cudaEventRecord(start, d->stream)) != cudaSuccess ||
+            (e = launch_mega(d, (int)steps)) != cudaSuccess ||
+            (e = cudaEventRecord(stop, d->stream)) != cudaSuccess ||
+            (e = cudaMemcpyAsync(d->h_error, d->mega_error, 4, cudaMemcpyDeviceToHost, d->stream)) !=
+                cudaSuccess ||
+            (e = cudaStreamSynchronize(d->stream)) != cudaSuccess)
             goto bad;
-    }
-    if (!d->decode_graph) {
+        if (*d->h_error) {
+            cudaMemset(d->mega_error, 0, sizeof(int));
+            cudaMemset(d->attn_count, 0, kKVHeads * sizeof(unsigned));
+            e = cudaErrorLaunchTimeout;
+            what = "decode loop: grid barrier wait gave up";
+            goto bad;
+        }
+        if (milliseconds && (e = cudaEventElapsedTime(milliseconds, start, stop)) != cudaSuccess) goto bad;
+        d->launches_per_step = 1;
+    } else if (!d->decode_graph) {
         what = "decode graph capture";
         cudaGraph_t graph = nullptr;
         if ((e = cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeRelaxed)) != cudaSuccess)
@@ -504,22 +625,25 @@ extern "C" int lun_device_decode_loop(lun_device *d, int64_t first_token, size_t
             goto bad;
         }
     }
-    what = "decode loop";
-    d->h_step->length = (int)length;
-    d->h_step->count = 1;
-    d->h_step->generated = 0;
-    d->h_step->ids[0] = (int)first_token;
-    if ((e = cudaEventCreate(&start)) != cudaSuccess || (e = cudaEventCreate(&stop)) != cudaSuccess ||
-        (e = cudaMemcpyAsync(d->d_step, d->h_step, sizeof(StepParams), cudaMemcpyHostToDevice,
-                             d->stream)) != cudaSuccess ||
-        (e = cudaEventRecord(start, d->stream)) != cudaSuccess)
-        goto bad;
-    for (size_t s = 0; s < steps; s++)
-        if ((e = cudaGraphLaunch(d->decode_graph, d->stream)) != cudaSuccess) goto bad;
-    if ((e = cudaEventRecord(stop, d->stream)) != cudaSuccess ||
-        (e = cudaStreamSynchronize(d->stream)) != cudaSuccess)
-        goto bad;
-    if (milliseconds && (e = cudaEventElapsedTime(milliseconds, start, stop)) != cudaSuccess) goto bad;
+    if (!d->use_mega) {
+        what = "decode loop";
+        d->h_step->length = (int)length;
+        d->h_step->count = 1;
+        d->h_step->generated = 0;
+        d->h_step->ids[0] = (int)first_token;
+        if ((e = cudaEventCreate(&start)) != cudaSuccess || (e = cudaEventCreate(&stop)) != cudaSuccess ||
+            (e = cudaMemcpyAsync(d->d_step, d->h_step, sizeof(StepParams), cudaMemcpyHostToDevice,
+                                 d->stream)) != cudaSuccess ||
+            (e = cudaEventRecord(start, d->stream)) != cudaSuccess)
+            goto bad;
+        for (size_t s = 0; s < steps; s++)
+            if ((e = cudaGraphLaunch(d->decode_graph, d->stream)) != cudaSuccess) goto bad;
+        if ((e = cudaEventRecord(stop, d->stream)) != cudaSuccess ||
+            (e = cudaStreamSynchronize(d->stream)) != cudaSuccess)
+            goto bad;
+        if (milliseconds && (e = cudaEventElapsedTime(milliseconds, start, stop)) != cudaSuccess)
+            goto bad;
+    }
     host_tokens = (int *)malloc(steps * sizeof(int));
     if (!host_tokens) {
         e = cudaErrorMemoryAllocation;
@@ -553,15 +677,24 @@ extern "C" int lun_device_run(lun_device *d, const int64_t *ids, size_t count, s
     d->h_step->length = (int)length;
     d->h_step->count = (int)count;
     for (size_t i = 0; i < count; i++) d->h_step->ids[i] = (int)ids[i];
+    d->h_step->generated = 0;
     const int n = (int)count;
+    // single-token calls run the persistent decode kernel (one launch); blocks of
+    // several tokens and traced calls run the per-projection kernels
+    const bool mega = count == 1 && !d->trace && d->use_mega;
     const char *what = "step upload";
     if ((e = cudaMemcpyAsync(d->d_step, d->h_step, sizeof(StepParams), cudaMemcpyHostToDevice,
                              d->stream)) != cudaSuccess ||
         (e = cudaMemsetAsync(d->d_flag, 0, 4, d->stream)) != cudaSuccess)
         goto bad;
     what = "kernel launch";
-    embed_kernel<<<n, 256, 0, d->stream>>>(d->embedding, d->d_step, d->x, n);
-    if ((e = cudaGetLastError()) != cudaSuccess) goto bad;
+    if (mega) {
+        if ((e = launch_mega(d, 1)) != cudaSuccess ||
+            (e = cudaMemcpyAsync(d->h_error, d->mega_error, 4, cudaMemcpyDeviceToHost, d->stream)) !=
+                cudaSuccess)
+            goto bad;
+    } else {
+    if ((e = lun_launch_embed(d->embedding, d->d_step, d->x, n, d->stream)) != cudaSuccess) goto bad;
     for (int layer = 0; layer < kLayers; layer++) {
         if ((e = run_projection(d, layer, 0, n)) != cudaSuccess ||
             (e = run_attention(d, layer, n, length)) != cudaSuccess ||
@@ -591,6 +724,7 @@ extern "C" int lun_device_run(lun_device *d, const int64_t *ids, size_t count, s
         hp.nonfinite = d->d_flag;
         if ((e = lun_launch_head(hp, d->sm_count, d->stream)) != cudaSuccess) goto bad;
     }
+    }
     what = "logits download";
     if ((e = cudaMemcpyAsync(d->h_logits, d->logits, (size_t)kVocab * 4, cudaMemcpyDeviceToHost,
                              d->stream)) != cudaSuccess ||
@@ -599,11 +733,36 @@ extern "C" int lun_device_run(lun_device *d, const int64_t *ids, size_t count, s
         goto bad;
     what = "execution";
     if ((e = cudaStreamSynchronize(d->stream)) != cudaSuccess) goto bad;
+    if (mega && *d->h_error) {
+        cudaMemset(d->mega_error, 0, sizeof(int));
+        cudaMemset(d->attn_count, 0, kKVHeads * sizeof(unsigned));
+        if (error && capacity) snprintf(error, capacity, "decode: grid barrier wait gave up");
+        return -1;
+    }
     *logits = d->h_logits;
     *nonfinite = *d->h_flag != 0;
     return 0;
 bad:
     return fail(error, capacity, what, e);
+}
+
+extern "C" int lun_device_timeline(lun_device *d, int enable)
+{
+    if (enable && !d->timeline &&
+        cudaMalloc((void **)&d->timeline, (kMegaTimelineEntries) * sizeof(unsigned long long)) !=
+            cudaSuccess)
+        return -1;
+    d->record_timeline = enable != 0;
+    return 0;
+}
+
+extern "C" int lun_device_timeline_copy(lun_device *d, unsigned long long *out, size_t entries)
+{
+    if (!d->timeline || entries > kMegaTimelineEntries) return -1;
+    return cudaMemcpy(out, d->timeline, entries * sizeof(unsigned long long), cudaMemcpyDeviceToHost) ==
+                   cudaSuccess
+               ? 0
+               : -1;
 }
 
 extern "C" int lun_device_trace(lun_device *d, int enable)

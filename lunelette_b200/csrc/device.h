@@ -64,6 +64,11 @@ float *lun_device_host_logits(lun_device *d);
 int lun_device_decode_loop(lun_device *d, int64_t first_token, size_t length, size_t steps,
     int64_t *tokens, float *milliseconds, int *launches, char *error, size_t capacity);
 
+/* Measurement: record %globaltimer at the start and after every grid barrier of
+ * the first step of each persistent-kernel launch (133 entries). */
+int lun_device_timeline(lun_device *d, int enable);
+int lun_device_timeline_copy(lun_device *d, unsigned long long *out, size_t entries);
+
 /* Test support: keep each layer's output hidden rows and the final-norm rows of
  * the most recent call (eager launches while enabled). */
 int lun_device_trace(lun_device *d, int enable);

@@ -24,7 +24,7 @@ enum GemvEpilogue : int {
     kEpiStore = 0,     // y[m][r] = acc * scale(r)
     kEpiResidual = 1,  // y[m][r] = res[m][r] + acc * scale(r)
     kEpiQKV = 2,       // rows [q|k|v]: RoPE on q,k (+query scale); q -> y, k/v -> KV pool
-    kEpiSwiGLU = 3,    // interleaved gate/up blocks: y[m][f] = silu(g) * u
+    kEpiSwiGLU = 3,    // alternating gate/up rows: y[m][f] = silu(g) * u
 };
 
 struct GemvParams {
@@ -47,6 +47,10 @@ struct GemvParams {
     float *kv;                         // FP32 KV pool
     const int *page_table;
     int num_pages, layer;
+    // Weights of the next projection in the step, fetched into L2 while this one
+    // runs so that HBM keeps streaming across kernel boundaries (or nullptr).
+    const uint8_t *prefetch;
+    size_t prefetch_bytes;
 };
 
 template <int M>
@@ -73,30 +77,30 @@ __device__ __forceinline__ void gemv_load_x(const GemvParams &p, float4 *xs, flo
     }
 }
 
-// Per-tensor scale of row r. For the interleaved gate/up matrix, bit 7 of the
-// row index selects up (scale[1]) over gate (scale[0]).
+// Storage is group-major: group g occupies rows 4g..4g+3 of the matrix on the
+// device. For q/k/v a group is two RoPE pairs of one 128-row head, stored as
+// (j, j+64, j+1, j+65); for gate/up it is (gate f, up f, gate f+1, up f+1) with
+// f = 2g. logical_row() maps element i of group g back to the row index of the
+// checkpoint's tensor (q|k|v concatenated) for scales, RoPE and outputs.
 template <int EPI>
-__device__ __forceinline__ float row_scale(const GemvParams &p, int r)
-{
-    if (EPI == kEpiSwiGLU) return (r & 128) ? p.scale[1] : p.scale[0];
-    return r < p.bound[0] ? p.scale[0] : (r < p.bound[1] ? p.scale[1] : p.scale[2]);
-}
-
-// Row of element i (0..3) of row-group g for each epilogue.
-template <int EPI>
-__device__ __forceinline__ int group_row(int g, int i)
+__device__ __forceinline__ int logical_row(int g, int i)
 {
     if (EPI == kEpiQKV) {
-        // (j, j+64, j+1, j+65) of one 128-row head: two RoPE pairs
         int head = g >> 5, j = (g & 31) * 2;
         return head * 128 + j + (i & 1) * 64 + (i >> 1);
-    } else if (EPI == kEpiSwiGLU) {
-        // (gate f, up f, gate f+1, up f+1) inside one 256-row interleaved block
-        int blk = g >> 6, f = (g & 63) * 2;
-        return blk * 256 + f + (i & 1) * 128 + (i >> 1);
     } else {
         return g * 4 + i;
     }
+}
+
+// Per-tensor scale of element i of group g: gate/up alternate (odd = up);
+// otherwise by logical row range (q, k, v).
+template <int EPI>
+__device__ __forceinline__ float elem_scale(const GemvParams &p, int g, int i)
+{
+    if (EPI == kEpiSwiGLU) return (i & 1) ? p.scale[1] : p.scale[0];
+    int r = logical_row<EPI>(g, i);
+    return r < p.bound[0] ? p.scale[0] : (r < p.bound[1] ? p.scale[1] : p.scale[2]);
 }
 
 template <int M, int EPI>
@@ -110,10 +114,10 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, int g, int la
 #pragma unroll
             for (int m = 0; m < M; m++) {
                 if (lane == i * M + m) {
-                    int r = group_row<EPI>(g, i);
+                    int r = logical_row<EPI>(g, i);
                     if (r < p.rows) {
-                        float v = acc[i][m] * row_scale<EPI>(p, r);
-                        if (EPI == kEpiResidual) v = p.res[(size_t)m * p.res_stride + r] + v;
+                        float v = acc[i][m] * elem_scale<EPI>(p, g, i);
+                        if (EPI == kEpiResidual) v = __ldcg(&p.res[(size_t)m * p.res_stride + r]) + v;
                         p.y[(size_t)m * p.y_stride + r] = v;
                     }
                 }
@@ -125,12 +129,12 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, int g, int la
 #pragma unroll
         for (int m = 0; m < M; m++) {
             if (lane != pair * M + m) continue;
-            int ra = group_row<EPI>(g, pair * 2), rb = group_row<EPI>(g, pair * 2 + 1);
-            float a = acc[pair * 2][m] * row_scale<EPI>(p, ra);
-            float b = acc[pair * 2 + 1][m] * row_scale<EPI>(p, rb);
+            int ra = logical_row<EPI>(g, pair * 2), rb = logical_row<EPI>(g, pair * 2 + 1);
+            float a = acc[pair * 2][m] * elem_scale<EPI>(p, g, pair * 2);
+            float b = acc[pair * 2 + 1][m] * elem_scale<EPI>(p, g, pair * 2 + 1);
             if (EPI == kEpiSwiGLU) {
-                // a = gate, b = up (same feature)
-                int f = (ra >> 8) * 128 + (ra & 127);
+                // a = gate, b = up of feature 2g + pair
+                int f = 2 * g + pair;
                 float silu = a / (1.0f + expf(-a));
                 p.y[(size_t)m * p.y_stride + f] = silu * b;
             } else {
@@ -163,73 +167,85 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, int g, int la
     }
 }
 
+// Dot products of the four rows of group g against the M activation rows in
+// shared memory; every lane ends with the full (butterfly-reduced) sums.
+template <int M, int EPI>
+__device__ __forceinline__ void gemv_group(const GemvParams &p, const float4 *xs, int g, int lane,
+                                           float (&acc)[4][M])
+{
+    const int NQ = p.cols >> 4;
+    const uint8_t *wr[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        int r = 4 * g + i;  // storage row
+        wr[i] = p.W + (size_t)(r < p.rows ? r : p.rows - 1) * p.cols;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int m = 0; m < M; m++) acc[i][m] = 0.0f;
+
+    for (int q0 = lane; q0 < NQ; q0 += 64) {
+        uint4 w[2][4];
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            int q = q0 + 32 * u;
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                w[u][i] = q < NQ ? ld_stream(wr[i] + (size_t)q * 16) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            int q = q0 + 32 * u;
+            if (q >= NQ) break;
+#pragma unroll
+            for (int piece = 0; piece < 4; piece++) {
+                float4 xv[M];
+#pragma unroll
+                for (int m = 0; m < M; m++) xv[m] = xs[(size_t)m * 4 * NQ + (size_t)piece * NQ + q];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    uint32_t word = piece == 0 ? w[u][i].x : piece == 1 ? w[u][i].y
+                                  : piece == 2 ? w[u][i].z : w[u][i].w;
+                    float2 lo = e4m3x2_to_float2(word);
+                    float2 hi = e4m3x2_to_float2(word >> 16);
+#pragma unroll
+                    for (int m = 0; m < M; m++) {
+                        float a = acc[i][m];
+                        a = fmaf(lo.x, xv[m].x, a);
+                        a = fmaf(lo.y, xv[m].y, a);
+                        a = fmaf(hi.x, xv[m].z, a);
+                        a = fmaf(hi.y, xv[m].w, a);
+                        acc[i][m] = a;
+                    }
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int m = 0; m < M; m++) acc[i][m] = warp_sum(acc[i][m]);
+}
+
 // One launch: blockDim 256 (8 warps); grid-stride over row groups of 4.
 template <int M, int EPI>
 __global__ void __launch_bounds__(256) gemv_fp8_kernel(GemvParams p)
 {
     extern __shared__ float4 xs[];
     __shared__ float red[32];
+    l2_prefetch_share(p.prefetch, p.prefetch_bytes);
+    pdl_wait();
+    pdl_launch_dependents();
     gemv_load_x<M>(p, xs, red);
     __syncthreads();
 
     const int lane = threadIdx.x & 31;
-    const int NQ = p.cols >> 4;
     const int groups = (p.rows + 3) >> 2;
     const int warps = gridDim.x * (blockDim.x >> 5);
     for (int g = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); g < groups; g += warps) {
-        const uint8_t *wr[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            int r = group_row<EPI>(g, i);
-            wr[i] = p.W + (size_t)(r < p.rows ? r : p.rows - 1) * p.cols;
-        }
         float acc[4][M];
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-#pragma unroll
-            for (int m = 0; m < M; m++) acc[i][m] = 0.0f;
-
-        for (int q0 = lane; q0 < NQ; q0 += 64) {
-            uint4 w[2][4];
-#pragma unroll
-            for (int u = 0; u < 2; u++) {
-                int q = q0 + 32 * u;
-#pragma unroll
-                for (int i = 0; i < 4; i++)
-                    w[u][i] = q < NQ ? ld_stream(wr[i] + (size_t)q * 16) : make_uint4(0, 0, 0, 0);
-            }
-#pragma unroll
-            for (int u = 0; u < 2; u++) {
-                int q = q0 + 32 * u;
-                if (q >= NQ) break;
-#pragma unroll
-                for (int piece = 0; piece < 4; piece++) {
-                    float4 xv[M];
-#pragma unroll
-                    for (int m = 0; m < M; m++) xv[m] = xs[(size_t)m * 4 * NQ + (size_t)piece * NQ + q];
-#pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        uint32_t word = piece == 0 ? w[u][i].x : piece == 1 ? w[u][i].y
-                                      : piece == 2 ? w[u][i].z : w[u][i].w;
-                        float2 lo = e4m3x2_to_float2(word);
-                        float2 hi = e4m3x2_to_float2(word >> 16);
-#pragma unroll
-                        for (int m = 0; m < M; m++) {
-                            float a = acc[i][m];
-                            a = fmaf(lo.x, xv[m].x, a);
-                            a = fmaf(lo.y, xv[m].y, a);
-                            a = fmaf(hi.x, xv[m].z, a);
-                            a = fmaf(hi.y, xv[m].w, a);
-                            acc[i][m] = a;
-                        }
-                    }
-                }
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-#pragma unroll
-            for (int m = 0; m < M; m++) acc[i][m] = warp_sum(acc[i][m]);
+        gemv_group<M, EPI>(p, xs, g, lane, acc);
         gemv_epilogue<M, EPI>(p, g, lane, acc);
     }
 }
@@ -252,6 +268,8 @@ static __global__ void __launch_bounds__(256) head_bf16_kernel(HeadParams p)
     extern __shared__ float4 xs[];
     __shared__ float red[32];
     const int cols = p.cols, NQ = cols >> 3;  // 8-column chunks (16 bytes of BF16)
+    pdl_wait();
+    pdl_launch_dependents();
     {
         float ss = 0.0f;
         for (int c = threadIdx.x; c < cols; c += blockDim.x) ss += p.x[c] * p.x[c];

@@ -107,8 +107,8 @@ LUN_API int lunelette_cuda_qkv_rope(const uint8_t *W, const float *scales, const
     return 0;
 }
 
-// Fused post-attention norm + interleaved gate/up projection + SwiGLU.
-// W is [18432][3072] with 128-row gate and up blocks alternating.
+// Fused post-attention norm + gate/up projection + SwiGLU.
+// W is [18432][3072] with gate row f at 2f and up row f at 2f + 1.
 LUN_API int lunelette_cuda_gateup_swiglu(const uint8_t *W, float scale_gate, float scale_up,
                                          const float *gain, const float *x, size_t count,
                                          float *act, void *stream)

@@ -1,10 +1,40 @@
 #include "kernels.h"
 
+#include <stdlib.h>
+
 using namespace lun;
 
 namespace {
 
 constexpr int kMaxGemvSmem = 4 * kInner * 4;  // 4 rows x 9216 FP32
+
+// Programmatic dependent launch for every kernel of the decode/prefill sequence
+// (LUNELETTE_PDL=0 turns it off for comparisons).
+bool pdl_enabled()
+{
+    static const bool on = [] {
+        const char *v = getenv("LUNELETTE_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
+template <typename... Params, typename... Args>
+cudaError_t launch(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                   cudaStream_t stream, Args &&...args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...);
+}
 
 template <int M, int EPI>
 cudaError_t setup_one()
@@ -36,8 +66,7 @@ cudaError_t launch_one(const GemvParams &p, int sm_count, cudaStream_t stream)
     int blocks = (groups + 7) / 8;
     int limit = sm_count * per_sm;
     if (blocks > limit) blocks = limit;
-    gemv_fp8_kernel<M, EPI><<<blocks, 256, smem, stream>>>(p);
-    return cudaGetLastError();
+    return launch(gemv_fp8_kernel<M, EPI>, dim3(blocks), dim3(256), smem, stream, p);
 }
 
 template <int EPI>
@@ -55,6 +84,8 @@ cudaError_t launch_epi(const GemvParams &p, int m, int sm_count, cudaStream_t st
 __global__ void rmsnorm_kernel(const float *gain, const float *x, float *out, int width)
 {
     __shared__ float red[32];
+    pdl_wait();
+    pdl_launch_dependents();
     const float *xr = x + (size_t)blockIdx.x * width;
     float ss = 0.0f;
     for (int c = threadIdx.x; c < width; c += blockDim.x) ss += xr[c] * xr[c];
@@ -114,6 +145,8 @@ __device__ __forceinline__ void block_best(float &v, int &i)
 
 __global__ void __launch_bounds__(256) argmax_partial_kernel(const float *logits, int n, int *partials)
 {
+    pdl_wait();
+    pdl_launch_dependents();
     int per = (n + gridDim.x - 1) / gridDim.x;
     int begin = blockIdx.x * per, end = min(begin + per, n);
     float v = -INFINITY;
@@ -129,6 +162,8 @@ __global__ void __launch_bounds__(256) argmax_partial_kernel(const float *logits
 __global__ void __launch_bounds__(256) argmax_final_kernel(const int *partials, int blocks,
                                                            StepParams *step, int *tokens)
 {
+    pdl_wait();
+    pdl_launch_dependents();
     float v = -INFINITY;
     int i = 0x7fffffff;
     for (int k = threadIdx.x; k < blocks; k += blockDim.x)
@@ -148,17 +183,26 @@ __global__ void __launch_bounds__(256) argmax_final_kernel(const int *partials, 
 cudaError_t lun_launch_greedy(const float *logits, int n, int *partials, StepParams *step,
                               int *tokens, cudaStream_t stream)
 {
-    argmax_partial_kernel<<<kArgmaxBlocks, 256, 0, stream>>>(logits, n, partials);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch(argmax_partial_kernel, dim3(kArgmaxBlocks), dim3(256), 0, stream, logits, n,
+                           partials);
     if (e != cudaSuccess) return e;
-    argmax_final_kernel<<<1, 256, 0, stream>>>(partials, kArgmaxBlocks, step, tokens);
-    return cudaGetLastError();
+    return launch(argmax_final_kernel, dim3(1), dim3(256), 0, stream, (const int *)partials,
+                  (int)kArgmaxBlocks, step, tokens);
+}
+
+cudaError_t lun_launch_embed(const uint16_t *embedding, const StepParams *step, float *x, int count,
+                             cudaStream_t stream)
+{
+    return launch(embed_kernel, dim3(count), dim3(256), 0, stream, embedding, step, x, count);
 }
 
 // Function attributes apply to the current device; calling again is cheap.
 cudaError_t lun_kernels_init()
 {
     cudaError_t e;
+    if ((e = cudaFuncSetAttribute(attention_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  kAttnSmemBytes)) != cudaSuccess)
+        return e;
     if ((e = setup_epi<kEpiStore>()) != cudaSuccess) return e;
     if ((e = setup_epi<kEpiResidual>()) != cudaSuccess) return e;
     if ((e = setup_epi<kEpiQKV>()) != cudaSuccess) return e;
@@ -205,8 +249,7 @@ cudaError_t lun_launch_head(const HeadParams &p, int sm_count, cudaStream_t stre
     int groups = (p.rows + 3) / 4;
     int blocks = (groups + 7) / 8;
     if (blocks > sm_count * per_sm) blocks = sm_count * per_sm;
-    head_bf16_kernel<<<blocks, 256, smem, stream>>>(p);
-    return cudaGetLastError();
+    return launch(head_bf16_kernel, dim3(blocks), dim3(256), smem, stream, p);
 }
 
 void lun_attention_plan(AttnParams *a, int total, int count, int sm_count, int slots)
@@ -233,19 +276,18 @@ cudaError_t lun_launch_attention(const AttnParams &a, int count, cudaStream_t st
 {
     if (a.splits < 1 || a.split_len < kTile || (a.split_len % kTile)) return cudaErrorInvalidValue;
     dim3 grid(a.splits, kKVHeads, count);
-    attention_split_kernel<<<grid, 128, 0, stream>>>(a);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = lun_kernels_ensure();
+    if (e != cudaSuccess) return e;
+    e = launch(attention_split_kernel, grid, dim3(128), kAttnSmemBytes, stream, a);
     if (e != cudaSuccess || a.splits == 1) return e;
-    attention_combine_kernel<<<dim3(kQueryHeads, count), 128, 0, stream>>>(a);
-    return cudaGetLastError();
+    return launch(attention_combine_kernel, dim3(kQueryHeads, count), dim3(128), 0, stream, a);
 }
 
 cudaError_t lun_launch_rmsnorm(const float *gain, const float *x, float *out, int width, int count,
                                cudaStream_t stream)
 {
     if (width <= 0 || count <= 0) return cudaErrorInvalidValue;
-    rmsnorm_kernel<<<count, 256, 0, stream>>>(gain, x, out, width);
-    return cudaGetLastError();
+    return launch(rmsnorm_kernel, dim3(count), dim3(256), 0, stream, gain, x, out, width);
 }
 
 cudaError_t lun_launch_fp8_decode(const uint8_t *codes, size_t n, float scale, float *out,

@@ -19,6 +19,10 @@ cudaError_t lun_launch_head(const lun::HeadParams &p, int sm_count, cudaStream_t
 void lun_attention_plan(lun::AttnParams *a, int total, int count, int sm_count, int slots);
 cudaError_t lun_launch_attention(const lun::AttnParams &a, int count, cudaStream_t stream);
 
+// x[t] = widen(embedding[step->ids[t]]) for t < count.
+cudaError_t lun_launch_embed(const uint16_t *embedding, const lun::StepParams *step, float *x, int count,
+                             cudaStream_t stream);
+
 // out[t][c] = gain[c] * (x[t][c] * rsqrt(mean(x[t]^2) + eps))
 cudaError_t lun_launch_rmsnorm(const float *gain, const float *x, float *out, int width, int count,
                                cudaStream_t stream);
@@ -30,6 +34,13 @@ cudaError_t lun_launch_rmsnorm(const float *gain, const float *x, float *out, in
 constexpr int kArgmaxBlocks = 256;
 cudaError_t lun_launch_greedy(const float *logits, int n, int *partials, lun::StepParams *step,
                               int *tokens, cudaStream_t stream);
+
+// Persistent decode kernel (decode_mega.cuh): cooperative launch of one CTA per
+// SM; the barrier words in p must be zero at launch.
+namespace lun {
+struct MegaParams;
+}
+cudaError_t lun_launch_decode_mega(const lun::MegaParams &p, int sm_count, cudaStream_t stream);
 
 // FP8 codes -> FP32 * scale through the same in-register conversion as the GEMV.
 cudaError_t lun_launch_fp8_decode(const uint8_t *codes, size_t n, float scale, float *out,

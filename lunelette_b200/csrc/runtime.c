@@ -556,6 +556,18 @@ LUN_API int lunelette_cuda_decode_loop(lunelette_metal *context, int64_t first_t
     return 0;
 }
 
+LUN_API int lunelette_cuda_timeline(lunelette_metal *context, int enable)
+{
+    return context && context->device ? lun_device_timeline(context->device, enable) : -1;
+}
+
+LUN_API int lunelette_cuda_timeline_copy(lunelette_metal *context, unsigned long long *out,
+    size_t entries)
+{
+    return context && context->device && out ?
+        lun_device_timeline_copy(context->device, out, entries) : -1;
+}
+
 LUN_API int lunelette_cuda_yarn(uint32_t position, float *cosine, float *sine)
 {
     return cosine && sine ? lun_yarn(position, cosine, sine) : -1;

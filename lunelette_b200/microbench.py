@@ -89,13 +89,59 @@ def run(shapes, ms_list, iters, warmup=3):
     return rows_out
 
 
+PHASES = ["qkv", "attention", "o", "gate_up", "down"]
+PHASE_BYTES = {"qkv": 6144 * 3072, "attention": 0, "o": 3072 * 4096, "gate_up": 18432 * 3072,
+               "down": 3072 * 9216}
+
+
+def decode_phases(checkpoint, steps=8, prompt=32):
+    """Per-phase durations of the persistent decode kernel (single-token steps
+    through lunelette_metal_decode), from its %globaltimer timeline: the mean over
+    `steps` steps and 26 layers of each phase, plus the head+pick tail."""
+    import lunelette_b200 as L
+    peak, kind = hbm_peak()
+    rows = {name: [] for name in PHASES + ["head", "pick", "step"]}
+    with L.Runtime(checkpoint) as rt:
+        ids = np.random.default_rng(7).integers(1000, 131072, prompt)
+        tok = int(np.argmax(rt.prefill(ids)))
+        rt.timeline(True)
+        for _ in range(steps):
+            tok = int(np.argmax(rt.decode(tok)))
+            t = rt.timeline_copy().astype(np.float64) / 1000.0  # us
+            d = np.diff(t)
+            for layer in range(26):
+                for k, name in enumerate(PHASES):
+                    rows[name].append(d[layer * 5 + k])
+            rows["head"].append(d[130])
+            rows["pick"].append(d[131])
+            rows["step"].append(t[132] - t[0])
+        rt.timeline(False)
+    out = []
+    for name, vals in rows.items():
+        us = float(np.mean(vals))
+        nbytes = PHASE_BYTES.get(name, 131072 * 3072 * 2 if name == "head" else 0)
+        rec = {"phase": name, "mean_us": us, "min_us": float(np.min(vals)), "max_us": float(np.max(vals))}
+        if nbytes:
+            rec["weight_bytes"] = nbytes
+            rec["gbs"] = nbytes / (us * 1e-6) / 1e9
+            rec["frac_hbm"] = rec["gbs"] / peak
+        out.append(rec)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--shapes", default=",".join(SHAPES))
     ap.add_argument("--m", default="1,2,4,8")
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--decode-phases", metavar="CHECKPOINT", default=None,
+                    help="time the persistent decode kernel's phases on this checkpoint instead")
     args = ap.parse_args()
+    if args.decode_phases:
+        for r in decode_phases(args.decode_phases):
+            print(json.dumps(r))
+        return
     out = run(args.shapes.split(","), [int(v) for v in args.m.split(",")], args.iters, args.warmup)
     for r in out:
         print(json.dumps(r))

@@ -155,6 +155,17 @@ def test_rmsnorm_matches_oracle(lib, oracle, torch_cuda):
         assert np.abs(out.cpu().numpy() - oracle.norm(g, x)).max() < 2e-6 * 3 * 3
 
 
+def qkv_storage_order(codes):
+    """Checkpoint-order q|k|v rows -> the device's group-major order: inside
+    every 128-row head, row j < 64 to 2j and row j + 64 to 2j + 1."""
+    out = np.empty_like(codes)
+    for head in range(codes.shape[0] // 128):
+        block = codes[head * 128:(head + 1) * 128]
+        out[head * 128:(head + 1) * 128:2] = block[:64]
+        out[head * 128 + 1:(head + 1) * 128:2] = block[64:]
+    return out
+
+
 def pool_view(pool, num_pages):
     return pool.reshape(-1, num_pages, 2, 8, 64, 128)
 
@@ -188,7 +199,8 @@ def test_qkv_rope_kv_store_matches_oracle(lib, oracle, torch_cuda):
     pool = torch.zeros((layer + 1) * num_pages * 2 * 8 * 64 * 128, dtype=torch.float32, device="cuda")
     q_out = torch.empty((count, 4096), dtype=torch.float32, device="cuda")
     rc = lib.lunelette_cuda_qkv_rope(
-        ptr(dev(torch, codes)), scales.ctypes.data, ptr(dev(torch, gain)), ptr(dev(torch, x)),
+        ptr(dev(torch, qkv_storage_order(codes))), scales.ctypes.data, ptr(dev(torch, gain)),
+        ptr(dev(torch, x)),
         count, length, ptr(dev(torch, cos)), ptr(dev(torch, sin)), ptr(q_out), ptr(pool),
         ptr(dev(torch, page_table)), num_pages, layer, stream(torch))
     assert rc == 0
@@ -216,10 +228,9 @@ def test_gateup_swiglu_matches_oracle(lib, oracle, torch_cuda):
     count = 3
     gate = finite_codes(rng, (9216, 3072))
     up = finite_codes(rng, (9216, 3072))
-    inter = np.empty((18432, 3072), np.uint8)
-    for b in range(72):
-        inter[256 * b:256 * b + 128] = gate[128 * b:128 * (b + 1)]
-        inter[256 * b + 128:256 * (b + 1)] = up[128 * b:128 * (b + 1)]
+    inter = np.empty((18432, 3072), np.uint8)  # device order: gate f at 2f, up f at 2f+1
+    inter[0::2] = gate
+    inter[1::2] = up
     sg, su = float(bf16_round(np.float32(0.0004))), float(bf16_round(np.float32(0.0006)))
     gain = (0.5 + rng.random(3072)).astype(np.float32)
     x = rng.standard_normal((count, 3072)).astype(np.float32)
