@@ -28,17 +28,30 @@ int lunelette_cuda_kernels_init(void);
 int lunelette_cuda_fp8_decode(const uint8_t *codes, size_t n, float scale, float *out,
     void *stream);
 
+/* Row-major E4M3 codes [rows][cols] (cols % 16 == 0) -> the tiled layout that
+ * the GEMV entry points below read: 16-row tiles of 1 KB blocks (16 rows x 64
+ * columns) in tensor-core fragment order, rows padded to 16 and columns to 64
+ * with zeros; dst holds ceil(rows/16)*16 * ceil(cols/64)*64 bytes. order 0 keeps
+ * the row order; 1 takes q|k|v rows (rows % 128 == 0) and stores the RoPE pair
+ * rows (j, j + 64) of each 128-row head adjacently (2j, 2j + 1); 2 takes the gate
+ * rows followed by the up rows (rows even) and interleaves them (gate f at 2f,
+ * up f at 2f + 1). The runtime stores its weights this way at upload, in place
+ * of the reference's row-major MTLBuffers (src/metal_weights.c:150-231). */
+int lunelette_cuda_tile_fp8(const uint8_t *src, size_t rows, size_t cols, int order, uint8_t *dst,
+    void *stream);
+
 /* y[t][r] = scale * sum_c decode(W[r][c]) * x[t][c]  (+ res[t][r] when res).
- * W row-major [rows][cols] E4M3, cols % 16 == 0, cols <= 9216; any count.
+ * W tiled (order 0) from [rows][cols] E4M3, cols % 16 == 0, cols <= 9216; any
+ * count. FP32 activations enter the tensor core as FP16 hi + lo halves after an
+ * exact power-of-two scaling; products are exact and accumulate in FP32.
  * Replaces project_fp8 / project_fp8_lookup (src/metal_kernels.metal:154-177,
  * 249-272) and, with res, the residual element op (:47-57). */
 int lunelette_cuda_gemv_fp8(const uint8_t *W, size_t rows, size_t cols, float scale,
     const float *x, const float *res, size_t count, float *y, void *stream);
 
 /* Fused input RMSNorm + q/k/v projection + YaRN RoPE (+ query scale) + KV store
- * for `count` tokens at positions length..length+count-1. W is [6144][3072]:
- * q rows, then k, then v, and inside every 128-row head row j < 64 stored at
- * 2j and row j + 64 at 2j + 1 (RoPE pairs adjacent); scales is a HOST array
+ * for `count` tokens at positions length..length+count-1. W is the [6144][3072]
+ * q|k|v matrix tiled with order 1 (RoPE pairs adjacent); scales is a HOST array
  * {q, k, v}; q_out [count][4096] in the checkpoint's (unpermuted) order;
  * kv_pool is the paged FP32 pool [layer][page][K|V][8 heads][64 slots][128].
  * Replaces norm + 3x project_fp8 + 2x rope + the KV blit
@@ -48,8 +61,9 @@ int lunelette_cuda_qkv_rope(const uint8_t *W, const float *scales, const float *
     float *q_out, float *kv_pool, const int *page_table, size_t num_pages, size_t layer,
     void *stream);
 
-/* Fused post-attention RMSNorm + gate/up projection + SwiGLU. W is [18432][3072]
- * with gate row f at row 2f and up row f at row 2f+1; act [count][9216].
+/* Fused post-attention RMSNorm + gate/up projection + SwiGLU. W is the gate
+ * rows followed by the up rows ([18432][3072]) tiled with order 2; act
+ * [count][9216].
  * Replaces norm + 2x project_fp8 + SiLU + multiply (src/metal_encode.m:162-172). */
 int lunelette_cuda_gateup_swiglu(const uint8_t *W, float scale_gate, float scale_up,
     const float *gain, const float *x, size_t count, float *act, void *stream);
@@ -105,10 +119,12 @@ int lunelette_cuda_trace_copy(lunelette_metal *context, int which, float *out, s
 int lunelette_cuda_decode_loop(lunelette_metal *context, int64_t first_token, size_t steps,
     int64_t *tokens, float *milliseconds, int *launches_per_step, char *error, size_t capacity);
 
-/* Phase timing of the persistent decode kernel: while enabled, each single-token
- * step records %globaltimer (ns) at its start and after each of its 132 grid
- * barriers (26 layers x {qkv, attention, o, gate/up, down}, head, greedy pick);
- * copy up to 133 entries of the most recent launch's first step. */
+/* Phase timing of the persistent decode kernel: while enabled, the first step of
+ * each launch records %globaltimer (ns) at its start (entry 0) and as CTA 0
+ * leaves each of its 131 grid barriers (entry 1 + k: 26 layers x {qkv,
+ * attention, o, gate/up, down}, then head + greedy pick); CTA b's arrival at
+ * barrier k is entry 132 + k * ctas + b, ctas = the device's SM count. Copy up to
+ * 132 + 131 * ctas entries. */
 int lunelette_cuda_timeline(lunelette_metal *context, int enable);
 int lunelette_cuda_timeline_copy(lunelette_metal *context, unsigned long long *out, size_t entries);
 

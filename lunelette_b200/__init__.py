@@ -64,6 +64,7 @@ SIGNATURES = {
     "lunelette_metal_checkpoint_destroy": (None, [P]),
     "lunelette_cuda_kernels_init": (ctypes.c_int, []),
     "lunelette_cuda_fp8_decode": (ctypes.c_int, [P, SZ, ctypes.c_float, P, P]),
+    "lunelette_cuda_tile_fp8": (ctypes.c_int, [P, SZ, SZ, ctypes.c_int, P, P]),
     "lunelette_cuda_gemv_fp8": (ctypes.c_int, [P, SZ, SZ, ctypes.c_float, P, P, SZ, P, P]),
     "lunelette_cuda_qkv_rope": (ctypes.c_int, [P, P, P, P, SZ, SZ, P, P, P, P, P, SZ, SZ, P]),
     "lunelette_cuda_gateup_swiglu": (ctypes.c_int, [P, ctypes.c_float, ctypes.c_float, P, P, SZ, P, P]),
@@ -235,7 +236,7 @@ class Runtime:
         if library().lunelette_cuda_timeline(self.handle, 1 if enable else 0):
             raise LuneletteError("timeline enable failed")
 
-    def timeline_copy(self, entries=133):
+    def timeline_copy(self, entries=132):
         out = np.zeros(entries, dtype=np.uint64)
         if library().lunelette_cuda_timeline_copy(self.handle, out.ctypes.data, entries):
             raise LuneletteError("timeline copy failed")

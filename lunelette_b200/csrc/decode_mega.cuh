@@ -1,19 +1,31 @@
 // Persistent cooperative decode kernel: one CTA per SM runs whole batch-1
-// decode steps (26 layers, final norm, tied head, greedy pick) with grid-wide
-// barriers between the phases of the reference's layer graph
-// (src/metal_encode.m:124-215). Per layer:
-//   qkv   input norm + q/k/v GEMV + RoPE + KV store          (prefetches o)
-//   attn  split-K attention; the last split of a KV head combines (fixed order)
-//   o     o GEMV + residual                                  (prefetches gate/up)
-//   ffn   post norm + gate/up GEMV + SwiGLU                  (prefetches down)
-//   down  down GEMV + residual                               (prefetches next qkv)
-// Each phase issues an L2 prefetch of the next matrix before computing, so HBM
-// keeps streaming weights through the barriers; the weights themselves never
-// depend on activations. Activations produced by other CTAs are read through L2
-// (ld.cg / cp.async.cg), never from a possibly stale L1.
+// decode steps (26 layers, final norm, tied head, greedy pick) of the
+// reference's layer graph (src/metal_encode.m:124-215).
 //
-// Barrier waits are bounded: past kSpinLimit polls a CTA sets *error and stops
-// waiting for the rest of the launch; the host then reports a failed call.
+// Warp roles per CTA (256 threads):
+//   producer (lane 0 of warp 7): walks this CTA's share of every weight matrix
+//     in the order the step consumes it and copies it, 8-12 KB items at a time,
+//     into shared-memory slots with bulk async copies (cp.async.bulk + mbarrier
+//     complete_tx). Weights never depend on activations, so the producer runs
+//     ahead across phases and grid barriers, bounded by free slots; it also
+//     keeps a short stretch of the stream (p.l2_ahead bytes) prefetched into L2.
+//   consumers (warps 0-6): per phase, wait at a grid barrier for the previous
+//     phase's activations, stage the activation row as FP16 hi/lo MMA fragments
+//     (and the epilogue's residual rows), then take items (16 rows x 512 or 768
+//     columns of the tiled layout of gemv.cuh), run the tensor-core dot
+//     products, leave 16 partial row sums per item in shared memory, and
+//     finally add each tile's partials in a fixed order and run the fused
+//     epilogue. Attention and the greedy pick run on consumers only.
+// Item i of the CTA's stream goes to consumer warp i mod 7, which owns
+// kSlotsPerWarp private slots and takes its items strictly in order, so every
+// slot's full and empty barriers are waited on in phase order by one waiter.
+// Phases per layer: qkv (norm + q/k/v + RoPE + KV store), attention (split
+// over positions, the last split of a KV head merges), o (+ residual), gate/up
+// (norm + SwiGLU), down (+ residual); then the head (final norm + tied BF16
+// GEMV) with a per-CTA argmax whose last CTA picks the token.
+//
+// Every wait is bounded (kSpinLimit polls): a CTA that gives up sets *error and
+// later waits return at once, so a failed launch ends and the host reports it.
 #pragma once
 #include "attention.cuh"
 #include "gemv.cuh"
@@ -21,207 +33,395 @@
 
 namespace lun {
 
-constexpr int kMegaThreads = 512;
-constexpr int kMegaWarps = kMegaThreads / 32;
-constexpr int kMegaAttnWorkers = kMegaThreads / 128;  // 4-warp workers (one warp per query head)
-constexpr int kMegaWorkerFloats = 4 * kHeadDim + kTile * kKPad + kTile * kHeadDim;
-constexpr int kMegaSmemBytes = kMegaAttnWorkers * kMegaWorkerFloats * 4;  // >= 9216 floats for x
+constexpr int kMegaConsumerWarps = 7;
+constexpr int kMegaConsumers = kMegaConsumerWarps * 32;
+constexpr int kMegaThreads = kMegaConsumers + 32;
+constexpr int kSlotsPerWarp = 2;
+constexpr int kRingSlots = kMegaConsumerWarps * kSlotsPerWarp;
+constexpr int kSlotBytes = 12288;
+constexpr int kFragBytes = (kInner / kBlockCols) * 256;  // hi/lo fragments of a 9216-column row
+constexpr int kMegaMaxItems = 48;                         // FP8 items of one phase per CTA
+constexpr int kMegaMaxTiles = 16;                         // tiles of one phase per CTA
+constexpr int kMegaSmemBytes =
+    kRingSlots * kSlotBytes + kFragBytes + kMegaMaxItems * 16 * 4 + 2 * kRingSlots * 8;
 constexpr unsigned kSpinLimit = 1u << 22;
-static_assert(kMegaSmemBytes >= kInner * 4, "x buffer must fit in the attention buffers");
+constexpr int kPhasesPerStep = kLayers * 4 + 1;  // 4 FP8 phases per layer, then the head
+constexpr int kAttnMaxSplits = 32;               // position ranges per KV head
+constexpr int kQStride = 36;                     // floats per staged query quarter (32 + pad)
 
+// ---- small PTX wrappers -----------------------------------------------------
+__device__ __forceinline__ unsigned smem_u32(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
 
-
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, unsigned bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity)
+{
+    unsigned ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void l2_prefetch(const void *src, unsigned bytes)
+{
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p)
 {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-
-__device__ __forceinline__ int ld_cg_int(const int *p) { return __ldcg(p); }
-
 __device__ __forceinline__ unsigned long long globaltimer_ns()
 {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kMegaConsumers) : "memory"); }
 
-// Grid-wide barrier number `target` (1, 2, ...) of this launch.
-__device__ __forceinline__ void mega_sync(const MegaParams &p, unsigned target)
+// Bounded wait on an mbarrier phase; false when the launch already failed or
+// this wait gave up (then *error is set).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, int *error)
 {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        unsigned arrived = atomicAdd(&p.barrier[0], 1u);
-        if (arrived == gridDim.x - 1) {
-            p.barrier[0] = 0;
-            __threadfence();
-            atomicExch(&p.barrier[1], target);
-        } else {
-            unsigned spins = 0;
-            while ((int)(ld_acquire_u32(&p.barrier[1]) - target) < 0) {
-                if (*(volatile int *)p.error) break;
-                if (++spins > kSpinLimit) {
-                    atomicExch(p.error, 1);
-                    break;
-                }
-                __nanosleep(32);
-            }
+    unsigned spins = 0;
+    while (!mbar_try_wait(bar, parity)) {
+        if (++spins > kSpinLimit) {
+            atomicExch(error, 1);
+            return false;
         }
-        __threadfence();
-        if (p.timeline && blockIdx.x == 0 && target <= (unsigned)kMegaBarriersPerStep)
-            p.timeline[target] = globaltimer_ns();
+        if ((spins & 255u) == 0 && *(volatile int *)error) return false;
     }
-    __syncthreads();
+    return true;
 }
 
-__device__ __forceinline__ void named_sync(int id, int threads)
+// ---- the stream: which bytes each CTA needs, in consumption order -----------
+enum { kPhQKV, kPhO, kPhGateUp, kPhDown, kPhHead };
+
+// This CTA's share of one phase: `items` consecutive items of `item_bytes`
+// starting at src. FP8 phases: whole 16-row tiles from tile `first`, each
+// split into K-chunks; head: 2-row items of the BF16 embedding from row `first`.
+struct PhaseSpan {
+    const uint8_t *src;
+    int items;
+    int item_bytes;
+    int first;
+};
+
+__device__ __forceinline__ void cta_range(int units, int &u0, int &u1)
 {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+    u0 = (int)(((long long)units * blockIdx.x) / gridDim.x);
+    u1 = (int)(((long long)units * (blockIdx.x + 1)) / gridDim.x);
 }
 
-// One activation row into the GEMV's permuted shared layout (16-column chunks),
-// optionally RMS-normalised; src rows come from other CTAs (read through L2) or
-// from the BF16 embedding.
-__device__ __forceinline__ void mega_load_row(float4 *xs, const float *src, const uint16_t *emb,
-                                              const float *gain, int cols, float *red)
+// blocks per item: qkv, o, gate/up, down
+__host__ __device__ constexpr int item_blocks(int ph) { return ph == kPhO ? 8 : 12; }
+
+__device__ __forceinline__ PhaseSpan phase_span(const MegaParams &p, int layer, int ph)
 {
-    const int NQ = cols >> 4;
-    float *xf = reinterpret_cast<float *>(xs);
-    float rs = 1.0f;
-    if (gain) {
-        float ss = 0.0f;
-        for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-            float v = emb ? bf16_lo((uint32_t)emb[c]) : __ldcg(&src[c]);
-            ss += v * v;
-        }
-        ss = block_sum(ss, red);
-        rs = rsqrtf(ss / (float)cols + kNormEps);
+    constexpr size_t lq = (size_t)kQKVRows * kHidden, lo = (size_t)kHidden * kQuery,
+                     lg = (size_t)kGateUpRows * kHidden, ld = (size_t)kHidden * kInner;
+    if (ph == kPhHead) {
+        int g0, g1;
+        cta_range(kVocab / 4, g0, g1);  // 4-row groups, two items each
+        return {reinterpret_cast<const uint8_t *>(p.embedding) + (size_t)g0 * 4 * kHidden * 2, 2 * (g1 - g0),
+                2 * kHidden * 2, 4 * g0};
     }
-    for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-        float v = emb ? bf16_lo((uint32_t)emb[c]) : __ldcg(&src[c]);
-        if (gain) v = gain[c] * (v * rs);
-        xf[((size_t)((c >> 2) & 3) * NQ + (c >> 4)) * 4 + (c & 3)] = v;
+    const uint8_t *base = p.w8 + (size_t)layer * (lq + lo + lg + ld);
+    const uint8_t *m;
+    int tiles, nb;
+    switch (ph) {
+    case kPhQKV: m = base; tiles = kQKVRows / kTileRows; nb = kHidden / kBlockCols; break;
+    case kPhO: m = base + lq; tiles = kHidden / kTileRows; nb = kQuery / kBlockCols; break;
+    case kPhGateUp: m = base + lq + lo; tiles = kGateUpRows / kTileRows; nb = kHidden / kBlockCols; break;
+    default: m = base + lq + lo + lg; tiles = kHidden / kTileRows; nb = kInner / kBlockCols; break;
     }
-    __syncthreads();
+    const int cb = item_blocks(ph);
+    int t0, t1;
+    cta_range(tiles, t0, t1);
+    return {m + (size_t)t0 * nb * kBlockBytes, (t1 - t0) * (nb / cb), cb * kBlockBytes, t0};
 }
 
-template <int EPI>
-__device__ __forceinline__ void mega_gemv(const GemvParams &gp, const float4 *xs)
+// Phase k of the launch's stream (steps repeat the same weights).
+__device__ __forceinline__ PhaseSpan stream_span(const MegaParams &p, int k)
 {
-    const int lane = threadIdx.x & 31;
-    const int groups = (gp.rows + 3) >> 2;
-    const int warps = gridDim.x * kMegaWarps;
-    for (int g = blockIdx.x * kMegaWarps + (threadIdx.x >> 5); g < groups; g += warps) {
-        float acc[4][1];
-        gemv_group<1, EPI>(gp, xs, g, lane, acc);
-        gemv_epilogue<1, EPI>(gp, g, lane, acc);
-    }
+    k %= kPhasesPerStep;
+    if (k == kLayers * 4) return phase_span(p, 0, kPhHead);
+    return phase_span(p, k >> 2, k & 3);
 }
 
-// Split-K attention of the step's single query row; worker = 4 warps.
-__device__ __forceinline__ void mega_attention(const MegaParams &p, int layer, int length,
-                                               float *smem)
+struct Ring {
+    uint8_t *slots;
+    uint64_t *full, *empty;
+};
+
+// Slot of the k-th item taken by consumer warp w.
+__device__ __forceinline__ unsigned slot_of(int w, unsigned k) { return w * kSlotsPerWarp + k % kSlotsPerWarp; }
+
+// First item of a phase that belongs to this consumer warp, given the number
+// of items the CTA's stream held before the phase.
+__device__ __forceinline__ int first_item(unsigned seq0)
 {
-    const int worker = threadIdx.x >> 7, wt = threadIdx.x & 127;
-    const int warp = wt >> 5, lane = threadIdx.x & 31;
-    float *qs = smem + worker * kMegaWorkerFloats;
-    float *ks = qs + 4 * kHeadDim;
-    float *vs = ks + kTile * kKPad;
-    __shared__ int last_flag[kMegaAttnWorkers];
-    const int total = length + 1;
-    const int live = (total + p.split_len - 1) / p.split_len;  // splits holding positions
-    const int items = kKVHeads * live;
-    for (int item = blockIdx.x * kMegaAttnWorkers + worker; item < items;
-         item += gridDim.x * kMegaAttnWorkers) {
-        const int kvh = item % kKVHeads, split = item / kKVHeads;
-        const int head = kvh * 4 + warp;
-        const int begin = split * p.split_len, end = min(begin + p.split_len, total);
-        for (int i = wt; i < 4 * kHeadDim; i += 128) qs[i] = __ldcg(&p.q[kvh * 4 * kHeadDim + i]);
-        float m_run = -INFINITY, l_run = 0.0f;
-        float o[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int p0 = begin; p0 < end; p0 += kTile) {
-            named_sync(1 + worker, 128);
-            for (int c = wt; c < 2 * kTile * 32; c += 128) {
-                int kind = c >> 10, row = (c >> 5) & 31, chunk = c & 31;
-                int pos = p0 + row;
-                bool in = pos < end;
-                const float *src = p.kv;
-                if (in)
-                    src = p.kv + kv_offset(layer, p.num_pages, p.page_table[pos / kPage], kind, kvh,
-                                           pos % kPage) + chunk * 4;
-                float *dst = kind == 0 ? ks + row * kKPad + chunk * 4 : vs + row * kHeadDim + chunk * 4;
-                cp_async16(dst, src, in);
-            }
-            cp_async_commit();
-            asm volatile("cp.async.wait_group 0;" ::: "memory");
-            named_sync(1 + worker, 128);
-            float s = -INFINITY;
-            if (p0 + lane < end) {
-                float dot = 0.0f;
-#pragma unroll
-                for (int c = 0; c < 32; c++) {
-                    float4 kk = *reinterpret_cast<const float4 *>(ks + lane * kKPad + c * 4);
-                    float4 qa = *reinterpret_cast<const float4 *>(qs + warp * kHeadDim + c * 4);
-                    dot = fmaf(qa.x, kk.x, dot);
-                    dot = fmaf(qa.y, kk.y, dot);
-                    dot = fmaf(qa.z, kk.z, dot);
-                    dot = fmaf(qa.w, kk.w, dot);
-                }
-                s = dot * kScoreScale;
-            }
-            float m_new = fmaxf(m_run, warp_max(s));
-            float correction = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
-            float prob = s == -INFINITY ? 0.0f : expf(s - m_new);
-            l_run = l_run * correction + warp_sum(prob);
-            m_run = m_new;
-#pragma unroll
-            for (int d = 0; d < 4; d++) o[d] *= correction;
-            const int rows = min(kTile, end - p0);
-            for (int j = 0; j < rows; j++) {
-                float pj = __shfl_sync(0xffffffffu, prob, j);
-                float4 vv = *reinterpret_cast<const float4 *>(vs + j * kHeadDim + lane * 4);
-                o[0] = fmaf(pj, vv.x, o[0]);
-                o[1] = fmaf(pj, vv.y, o[1]);
-                o[2] = fmaf(pj, vv.z, o[2]);
-                o[3] = fmaf(pj, vv.w, o[3]);
-            }
-        }
-        size_t slot = (size_t)head * p.splits + split;
-        *reinterpret_cast<float4 *>(&p.part_acc[slot * kHeadDim + lane * 4]) =
-            make_float4(o[0], o[1], o[2], o[3]);
-        if (lane == 0) {
-            p.part_ml[slot * 2] = m_run;
-            p.part_ml[slot * 2 + 1] = l_run;
-        }
-        __threadfence();
-        named_sync(1 + worker, 128);
-        if (wt == 0) last_flag[worker] = atomicAdd(&p.attn_count[kvh], 1u) == (unsigned)(live - 1);
-        named_sync(1 + worker, 128);
-        if (last_flag[worker]) {
-            // every split of this KV head has written its partials: merge them in
-            // split order for the four query heads (thread = head-dim column)
-            __threadfence();
-            for (int hq = 0; hq < 4; hq++) {
-                const size_t base = (size_t)(kvh * 4 + hq) * p.splits;
-                float m = -INFINITY;
-                for (int s2 = 0; s2 < live; s2++)
-                    if (__ldcg(&p.part_ml[(base + s2) * 2 + 1]) > 0.0f)
-                        m = fmaxf(m, __ldcg(&p.part_ml[(base + s2) * 2]));
-                float l = 0.0f, acc = 0.0f;
-                for (int s2 = 0; s2 < live; s2++) {
-                    float ls = __ldcg(&p.part_ml[(base + s2) * 2 + 1]);
-                    if (ls > 0.0f) {
-                        float w = expf(__ldcg(&p.part_ml[(base + s2) * 2]) - m);
-                        l += ls * w;
-                        acc += __ldcg(&p.part_acc[(base + s2) * kHeadDim + wt]) * w;
+    const int warp = threadIdx.x >> 5;
+    return (warp + kMegaConsumerWarps - (int)(seq0 % kMegaConsumerWarps)) % kMegaConsumerWarps;
+}
+
+// Producer (one thread): every item of the launch, in stream order, plus an L2
+// prefetch that runs p.l2_ahead bytes ahead of the ring.
+__device__ __forceinline__ void produce(const MegaParams &p, const Ring &r)
+{
+    unsigned issued[kMegaConsumerWarps] = {};
+    unsigned seq = 0;
+    const int total = p.steps * kPhasesPerStep;
+    int pk = 0;  // L2 lookahead cursor: phase and byte offset in it
+    unsigned pf_off = 0;
+    PhaseSpan pf = stream_span(p, 0);
+    unsigned long long ring_bytes = 0, pf_bytes = 0;
+    for (int k = 0; k < total; k++) {
+        const PhaseSpan sp = stream_span(p, k);
+        for (int i = 0; i < sp.items; i++, seq++) {
+            while (pk < total && pf_bytes < ring_bytes + p.l2_ahead) {
+                const unsigned span = (unsigned)pf.items * (unsigned)pf.item_bytes;
+                if (pf_off >= span) {
+                    if (++pk < total) {
+                        pf = stream_span(p, pk);
+                        pf_off = 0;
                     }
+                    continue;
                 }
-                p.attn[(kvh * 4 + hq) * kHeadDim + wt] = acc / l;
+                const unsigned n = span - pf_off < 16384u ? span - pf_off : 16384u;
+                l2_prefetch(pf.src + pf_off, n);
+                pf_off += n;
+                pf_bytes += n;
             }
-            if (wt == 0) p.attn_count[kvh] = 0;
+            const int w = (int)(seq % kMegaConsumerWarps);
+            const unsigned u = issued[w]++;
+            const unsigned slot = slot_of(w, u), use = u / kSlotsPerWarp;
+            if (use && !mbar_wait(&r.empty[slot], (use - 1) & 1, p.error)) return;
+            mbar_expect_tx(&r.full[slot], (unsigned)sp.item_bytes);
+            bulk_g2s(r.slots + (size_t)slot * kSlotBytes, sp.src + (size_t)i * sp.item_bytes, (unsigned)sp.item_bytes,
+                     &r.full[slot]);
+            ring_bytes += (unsigned)sp.item_bytes;
         }
+    }
+}
+
+// ---- synchronisation --------------------------------------------------------
+__device__ __forceinline__ unsigned *sync_word(const MegaParams &p, int index)
+{
+    return p.sync + (size_t)index * kSyncStride;
+}
+
+// Bounded wait of one thread until *word >= target (acquire).
+__device__ __forceinline__ void thread_wait(const unsigned *word, unsigned target, int *error)
+{
+    unsigned spins = 0;
+    while (ld_acquire_u32(word) < target) {
+        if (++spins > kSpinLimit) {
+            atomicExch(error, 1);
+            return;
+        }
+        if ((spins & 255u) == 0 && *(volatile int *)error) return;
+    }
+}
+
+// Grid barrier `target` (1, 2, ...) of this launch among all CTAs' consumers;
+// with rec, this CTA's arrival and CTA 0's exit go to the timeline.
+__device__ __forceinline__ void grid_sync(const MegaParams &p, unsigned target, bool rec)
+{
+    consumers_sync();
+    if (threadIdx.x == 0) {
+        if (rec) p.timeline[kMegaTimelineHead + (size_t)(target - 1) * gridDim.x + blockIdx.x] = globaltimer_ns();
+        __threadfence();
+        if (!*(volatile int *)p.error) {
+            // barrier k is passed once the arrival count reaches k * gridDim.x
+            unsigned *word = sync_word(p, kSyncBarrier);
+            asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(word), "r"(1u) : "memory");
+            thread_wait(word, target * gridDim.x, p.error);
+        }
+        __threadfence();
+        if (rec && blockIdx.x == 0) p.timeline[target] = globaltimer_ns();
+    }
+    consumers_sync();
+}
+
+// ---- consumer helpers -------------------------------------------------------
+__device__ __forceinline__ float consumers_sum(float v, float *red)
+{
+    v = warp_sum(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    consumers_sync();
+    if (lane == 0) red[warp] = v;
+    consumers_sync();
+    float t = lane < kMegaConsumerWarps ? red[lane] : 0.0f;
+    return warp_sum(t);
+}
+
+// Rows [row0, row0 + n) of a vector another CTA wrote -> shared memory, for an
+// epilogue; the loads overlap the fragment staging that follows.
+__device__ __forceinline__ void stage_rows(float *dst, const float *src, int row0, int n)
+{
+    for (int i = threadIdx.x; i < n; i += kMegaConsumers) dst[i] = __ldcg(&src[row0 + i]);
+}
+
+// Activation row -> hi/lo FP16 B fragments (lanes 0-7 of every half block, the
+// layout of gemv_stage with one token), optionally RMS-normalised, in one pass:
+// every consumer thread holds its float4s in registers while the sum of squares
+// and the magnitude bound are reduced. src is another CTA's output (read through
+// L2) or, with emb, the BF16 embedding row. Returns 2^-e, the inverse scale.
+template <int K>
+__device__ __forceinline__ float stage_frag(uint32_t *frag, const float *src, const uint16_t *emb, const float *gain,
+                                            float *red)
+{
+    constexpr int kF4 = K / 4;
+    constexpr int kPer = (kF4 + kMegaConsumers - 1) / kMegaConsumers;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float4 v[kPer];
+#pragma unroll
+    for (int u = 0; u < kPer; u++) {
+        const int idx = threadIdx.x + u * kMegaConsumers;
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (idx < kF4) {
+            if (emb) {
+                const uint2 e = *reinterpret_cast<const uint2 *>(emb + 4 * idx);
+                v[u] = make_float4(bf16_lo(e.x), bf16_hi(e.x), bf16_lo(e.y), bf16_hi(e.y));
+            } else {
+                v[u] = __ldcg(reinterpret_cast<const float4 *>(src) + idx);
+            }
+        }
+    }
+    const float4 *gain4 = reinterpret_cast<const float4 *>(gain);
+    float ss = 0.0f, mx = 0.0f;
+#pragma unroll
+    for (int u = 0; u < kPer; u++) {
+        const int idx = threadIdx.x + u * kMegaConsumers;
+        if (idx < kF4) {
+            const float4 x = v[u];
+            ss += x.x * x.x;
+            ss += x.y * x.y;
+            ss += x.z * x.z;
+            ss += x.w * x.w;
+            const float4 g = gain ? __ldg(gain4 + idx) : make_float4(1.f, 1.f, 1.f, 1.f);
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(g.x * x.x), fabsf(g.y * x.y)), fmaxf(fabsf(g.z * x.z), fabsf(g.w * x.w))));
+        }
+    }
+    ss = warp_sum(ss);
+    mx = warp_max(mx);
+    if (lane == 0) {
+        red[warp * 2] = ss;
+        red[warp * 2 + 1] = mx;
+    }
+    consumers_sync();
+    float tss = 0.0f, tmx = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kMegaConsumerWarps; w++) {
+        tss += red[w * 2];
+        tmx = fmaxf(tmx, red[w * 2 + 1]);
+    }
+    const float rs = gain ? rsqrtf(tss / (float)K + kNormEps) : 1.0f;
+    const int e = frag_exponent(tmx * rs * 1.0001f);
+    const float sc = exp2i(e);
+#pragma unroll
+    for (int u = 0; u < kPer; u++) {
+        const int idx = threadIdx.x + u * kMegaConsumers;
+        if (idx < kF4) {
+            float4 x = v[u];
+            if (gain) {
+                const float4 g = __ldg(gain4 + idx);
+                x.x = g.x * (x.x * rs);
+                x.y = g.y * (x.y * rs);
+                x.z = g.z * (x.z * rs);
+                x.w = g.w * (x.w * rs);
+            }
+            uint32_t hi, lo;
+            split_hilo(x.x * sc, x.y * sc, hi, lo);
+            frag_store_pair(frag, 8, 4 * idx, 0, hi);
+            frag_store_pair(frag, 8, 4 * idx, 1, lo);
+            split_hilo(x.z * sc, x.w * sc, hi, lo);
+            frag_store_pair(frag, 8, 4 * idx + 2, 0, hi);
+            frag_store_pair(frag, 8, 4 * idx + 2, 1, lo);
+        }
+    }
+    consumers_sync();
+    return exp2i(-e);
+}
+
+// One FP8 phase's items on this warp: CB blocks per item, NB blocks per row.
+// Leaves the item's 16 partial row sums (hi + lo columns) in partial[item][16].
+template <int CB, int NB>
+__device__ __forceinline__ void consume_fp8(const Ring &r, const PhaseSpan &sp, unsigned seq0, unsigned &taken,
+                                            const uint4 *frag, float *partial, int *error)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int kChunks = NB / CB;
+    for (int i = first_item(seq0); i < sp.items; i += kMegaConsumerWarps) {
+        const unsigned k = taken++;
+        const unsigned slot = slot_of(warp, k), use = k / kSlotsPerWarp;
+        mbar_wait(&r.full[slot], use & 1, error);
+        const uint8_t *s = r.slots + (size_t)slot * kSlotBytes;
+        const uint4 *xf = frag + (size_t)(i % kChunks) * CB * 16;
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+        for (int b = 0; b < CB; b++) {
+            const uint4 wa = *reinterpret_cast<const uint4 *>(s + b * kBlockBytes + lane * 16);
+            const uint4 wb = *reinterpret_cast<const uint4 *>(s + b * kBlockBytes + 512 + lane * 16);
+            uint4 x0 = make_uint4(0, 0, 0, 0), x1 = x0;
+            if (lane < 8) {
+                x0 = xf[(b * 2) * 8 + lane];
+                x1 = xf[(b * 2 + 1) * 8 + lane];
+            }
+            mma_block(c, wa, wb, x0, x1);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&r.empty[slot]);
+        if ((lane & 3) == 0) {
+            partial[i * 16 + (lane >> 2)] = c[0] + c[1];
+            partial[i * 16 + 8 + (lane >> 2)] = c[2] + c[3];
+        }
+    }
+}
+
+// Sum each tile's chunk partials in chunk order and run the phase epilogue on
+// its four row groups (groups spread over the consumer warps).
+template <int EPI>
+__device__ __forceinline__ void fp8_epilogue(const GemvParams &gp, const PhaseSpan &sp, int chunks,
+                                             const float *partial, float inv_scale)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int groups = (sp.items / chunks) * 4;
+    for (int gi = warp; gi < groups; gi += kMegaConsumerWarps) {
+        const int tl = gi >> 2, gq = gi & 3;
+        float acc[4][1];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            float s = 0.0f;
+            for (int c = 0; c < chunks; c++) s += partial[(tl * chunks + c) * 16 + gq * 4 + i];
+            acc[i][0] = s * inv_scale;
+        }
+        gemv_epilogue<1, EPI>(gp, (sp.first + tl) * 4 + gq, lane, acc);
     }
 }
 
@@ -233,103 +433,266 @@ __device__ __forceinline__ void arg_better(float &v, int &i, float v2, int i2)
     }
 }
 
-// Final norm + tied BF16 head over this CTA's rows, then a per-CTA argmax.
-__device__ __forceinline__ void mega_head(const MegaParams &p, float4 *xs, float *red)
+// Head phase: final-normed row staged with 8-column chunks; items of 2 BF16
+// rows; logits, non-finite flag and per-warp best.
+__device__ __forceinline__ void consume_head(const Ring &r, const PhaseSpan &sp, unsigned seq0, unsigned &taken,
+                                             const MegaParams &p, const float4 *xs, float &best, int &best_i,
+                                             int *error)
 {
-    const int cols = kHidden, NQ = cols >> 3;
-    {
-        float ss = 0.0f;
-        for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-            float v = __ldcg(&p.x[c]);
-            ss += v * v;
-        }
-        ss = block_sum(ss, red);
-        float rs = rsqrtf(ss / (float)cols + kNormEps);
-        float *xf = reinterpret_cast<float *>(xs);
-        for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-            float v = p.final_norm[c] * (__ldcg(&p.x[c]) * rs);
-            xf[((size_t)((c >> 2) & 1) * NQ + (c >> 3)) * 4 + (c & 3)] = v;
-        }
-        __syncthreads();
-    }
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int groups = kVocab / 4;
-    const int warps = gridDim.x * kMegaWarps;
-    float best = -INFINITY;
-    int best_i = 0x7fffffff, bad = 0;
-    for (int g = blockIdx.x * kMegaWarps + warp; g < groups; g += warps) {
-        const uint16_t *wr[4];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int NQ = kHidden >> 3;  // 8-column chunks of a row
+    int bad = 0;
+    for (int i = first_item(seq0); i < sp.items; i += kMegaConsumerWarps) {
+        const unsigned k = taken++;
+        const unsigned slot = slot_of(warp, k), use = k / kSlotsPerWarp;
+        mbar_wait(&r.full[slot], use & 1, error);
+        const uint8_t *s = r.slots + (size_t)slot * kSlotBytes;
+        float acc[2] = {0.f, 0.f};
+#pragma unroll 4
+        for (int qq = lane; qq < NQ; qq += 32) {
+            const float4 x0 = xs[qq], x1 = xs[NQ + qq];
 #pragma unroll
-        for (int i = 0; i < 4; i++) wr[i] = p.embedding + (size_t)(g * 4 + i) * cols;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int q0 = lane; q0 < NQ; q0 += 64) {
-            uint4 w[2][4];
-#pragma unroll
-            for (int u = 0; u < 2; u++)
-#pragma unroll
-                for (int i = 0; i < 4; i++) w[u][i] = ld_stream(wr[i] + (size_t)(q0 + 32 * u) * 8);
-#pragma unroll
-            for (int u = 0; u < 2; u++) {
-                int q = q0 + 32 * u;
-                float4 x0 = xs[q], x1 = xs[NQ + q];
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    float a = acc[i];
-                    a = fmaf(bf16_lo(w[u][i].x), x0.x, a);
-                    a = fmaf(bf16_hi(w[u][i].x), x0.y, a);
-                    a = fmaf(bf16_lo(w[u][i].y), x0.z, a);
-                    a = fmaf(bf16_hi(w[u][i].y), x0.w, a);
-                    a = fmaf(bf16_lo(w[u][i].z), x1.x, a);
-                    a = fmaf(bf16_hi(w[u][i].z), x1.y, a);
-                    a = fmaf(bf16_lo(w[u][i].w), x1.z, a);
-                    a = fmaf(bf16_hi(w[u][i].w), x1.w, a);
-                    acc[i] = a;
-                }
+            for (int rr = 0; rr < 2; rr++) {
+                const uint4 w = *reinterpret_cast<const uint4 *>(s + rr * kHidden * 2 + qq * 16);
+                float a = acc[rr];
+                a = fmaf(bf16_lo(w.x), x0.x, a);
+                a = fmaf(bf16_hi(w.x), x0.y, a);
+                a = fmaf(bf16_lo(w.y), x0.z, a);
+                a = fmaf(bf16_hi(w.y), x0.w, a);
+                a = fmaf(bf16_lo(w.z), x1.x, a);
+                a = fmaf(bf16_hi(w.z), x1.y, a);
+                a = fmaf(bf16_lo(w.w), x1.z, a);
+                a = fmaf(bf16_hi(w.w), x1.w, a);
+                acc[rr] = a;
             }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&r.empty[slot]);
+        const int row = sp.first + 2 * i;
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            float v = warp_sum(acc[i]);
-            if (lane == i) {
-                p.logits[g * 4 + i] = v;
+        for (int rr = 0; rr < 2; rr++) {
+            const float v = warp_sum(acc[rr]);
+            if (lane == rr) {
+                p.logits[row + rr] = v;
                 bad |= !isfinite(v);
             }
-            arg_better(best, best_i, v, g * 4 + i);
+            arg_better(best, best_i, v, row + rr);
         }
     }
     if (bad) atomicOr(p.nonfinite, 1);
-    // CTA argmax over its warps (value, then lowest id)
-    __shared__ float bv[kMegaWarps];
-    __shared__ int bi[kMegaWarps];
-    if (lane == 0) {
-        bv[warp] = best;
-        bi[warp] = best_i;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float v = bv[0];
-        int i = bi[0];
-        for (int w = 1; w < kMegaWarps; w++) arg_better(v, i, bv[w], bi[w]);
-        p.arg_val[blockIdx.x] = v;
-        p.arg_idx[blockIdx.x] = i;
+}
+
+// Position ranges per KV head for `total` positions (8-position multiples).
+__device__ __forceinline__ void attention_plan(int total, int &splits, int &per)
+{
+    splits = (total + 7) >> 3;
+    if (splits > kAttnMaxSplits) splits = kAttnMaxSplits;
+    per = (total + splits - 1) / splits;
+    per = (per + 7) & ~7;
+    splits = (total + per - 1) / per;
+}
+
+// Attention of the step's query row. Work item = (KV head, position range):
+// one warp scores the range for the KV head's four query heads in sub-tiles of
+// 8 positions — lanes (position, dim quarter) for the scores, lanes = dims for
+// P.V, with all 16 K/V loads of a sub-tile in flight at once — and keeps an
+// online softmax per query head. With several ranges, each writes (m, l, o)
+// partials and the warp that finishes a KV head's last range merges them in
+// range order (a ticket counter per KV head, `tickets` before this layer).
+// Replaces scores + attend (src/metal_kernels.metal:81-132).
+__device__ __forceinline__ void mega_attention(const MegaParams &p, int layer, int length, unsigned tickets,
+                                               float *qs_all)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, pp = lane >> 2, qd = lane & 3;
+    const int total = length + 1;
+    int splits, per;
+    attention_plan(total, splits, per);
+    const int items = kKVHeads * splits;
+    float *qs = qs_all + warp * (16 * kQStride);
+    for (int item = warp * (int)gridDim.x + blockIdx.x; item < items; item += gridDim.x * kMegaConsumerWarps) {
+        const int kvh = item / splits, split = item - kvh * splits;
+        const int begin = split * per, end = min(begin + per, total);
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int f4 = lane + 32 * u, hq = f4 >> 5, d4 = f4 & 31;
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(p.q + (size_t)(kvh * 4 + hq) * kHeadDim) + d4);
+            *reinterpret_cast<float4 *>(qs + (hq * 4 + (d4 >> 3)) * kQStride + (d4 & 7) * 4) = v;
+        }
+        __syncwarp();
+        float m_run[4], l_run[4];
+        float4 o[4];
+#pragma unroll
+        for (int hq = 0; hq < 4; hq++) {
+            m_run[hq] = -INFINITY;
+            l_run[hq] = 0.0f;
+            o[hq] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        for (int p0 = begin; p0 < end; p0 += 8) {
+            const int n = min(8, end - p0);
+            const int page = p.page_table[p0 / kPage];
+            const float *kb = p.kv + kv_offset(layer, p.num_pages, page, 0, kvh, p0 % kPage);
+            const float *vb = p.kv + kv_offset(layer, p.num_pages, page, 1, kvh, p0 % kPage);
+            const bool valid = pp < n;
+            float4 kk[8], vv[8];
+            const float4 *krow = reinterpret_cast<const float4 *>(kb + pp * kHeadDim + qd * 32);
+#pragma unroll
+            for (int c = 0; c < 8; c++) kk[c] = valid ? __ldcg(krow + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int t = 0; t < 8; t++)
+                vv[t] = t < n ? __ldcg(reinterpret_cast<const float4 *>(vb + t * kHeadDim) + lane)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+            float pr[4];
+#pragma unroll
+            for (int hq = 0; hq < 4; hq++) {
+                const float4 *qv = reinterpret_cast<const float4 *>(qs + (hq * 4 + qd) * kQStride);
+                float d = 0.0f;
+#pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    const float4 q4 = qv[c];
+                    d = fmaf(q4.x, kk[c].x, d);
+                    d = fmaf(q4.y, kk[c].y, d);
+                    d = fmaf(q4.z, kk[c].z, d);
+                    d = fmaf(q4.w, kk[c].w, d);
+                }
+                d += __shfl_xor_sync(0xffffffffu, d, 1);
+                d += __shfl_xor_sync(0xffffffffu, d, 2);
+                const float s = valid ? d * kScoreScale : -INFINITY;
+                float tmax = s;
+                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
+                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
+                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
+                const float m_new = fmaxf(m_run[hq], tmax);
+                const float corr = m_run[hq] == -INFINITY ? 0.0f : expf(m_run[hq] - m_new);
+                pr[hq] = valid ? expf(s - m_new) : 0.0f;
+                float ps = pr[hq];
+                ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+                ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+                ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+                l_run[hq] = l_run[hq] * corr + ps;
+                m_run[hq] = m_new;
+                o[hq].x *= corr;
+                o[hq].y *= corr;
+                o[hq].z *= corr;
+                o[hq].w *= corr;
+            }
+#pragma unroll
+            for (int t = 0; t < 8; t++) {
+#pragma unroll
+                for (int hq = 0; hq < 4; hq++) {
+                    const float pt = __shfl_sync(0xffffffffu, pr[hq], t * 4);
+                    o[hq].x = fmaf(pt, vv[t].x, o[hq].x);
+                    o[hq].y = fmaf(pt, vv[t].y, o[hq].y);
+                    o[hq].z = fmaf(pt, vv[t].z, o[hq].z);
+                    o[hq].w = fmaf(pt, vv[t].w, o[hq].w);
+                }
+            }
+        }
+        if (splits == 1) {
+#pragma unroll
+            for (int hq = 0; hq < 4; hq++) {
+                const float inv = 1.0f / l_run[hq];
+                reinterpret_cast<float4 *>(p.attn + (size_t)(kvh * 4 + hq) * kHeadDim)[lane] =
+                    make_float4(o[hq].x * inv, o[hq].y * inv, o[hq].z * inv, o[hq].w * inv);
+            }
+            __syncwarp();
+            continue;
+        }
+        const size_t base = (size_t)(kvh * splits + split) * 4;
+#pragma unroll
+        for (int hq = 0; hq < 4; hq++) {
+            reinterpret_cast<float4 *>(p.part_acc + (base + hq) * kHeadDim)[lane] = o[hq];
+            if (lane == 0) {
+                p.part_ml[(base + hq) * 2] = m_run[hq];
+                p.part_ml[(base + hq) * 2 + 1] = l_run[hq];
+            }
+        }
+        __syncwarp();
+        unsigned ticket = 0;
+        if (lane == 0) {
+            __threadfence();
+            ticket = atomicAdd(sync_word(p, kSyncTicket + kvh), 1u);
+        }
+        ticket = __shfl_sync(0xffffffffu, ticket, 0);
+        if (ticket == tickets + (unsigned)(splits - 1)) {
+            // last range of this KV head: merge every range in order
+            __threadfence();
+#pragma unroll 1
+            for (int hq = 0; hq < 4; hq++) {
+                float ms = -INFINITY, ls = 0.0f;
+                if (lane < splits) {
+                    const size_t at = ((size_t)(kvh * splits + lane) * 4 + hq) * 2;
+                    ms = __ldcg(&p.part_ml[at]);
+                    ls = __ldcg(&p.part_ml[at + 1]);
+                }
+                const float M = warp_max(ls > 0.0f ? ms : -INFINITY);
+                const float w = ls > 0.0f ? expf(ms - M) : 0.0f;
+                const float L = warp_sum(w * ls);
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+                for (int s2 = 0; s2 < splits; s2++) {
+                    const float ws = __shfl_sync(0xffffffffu, w, s2);
+                    const float4 v = __ldcg(
+                        reinterpret_cast<const float4 *>(p.part_acc + ((size_t)(kvh * splits + s2) * 4 + hq) * kHeadDim) +
+                        lane);
+                    acc.x = fmaf(ws, v.x, acc.x);
+                    acc.y = fmaf(ws, v.y, acc.y);
+                    acc.z = fmaf(ws, v.z, acc.z);
+                    acc.w = fmaf(ws, v.w, acc.w);
+                }
+                const float inv = 1.0f / L;
+                reinterpret_cast<float4 *>(p.attn + (size_t)(kvh * 4 + hq) * kHeadDim)[lane] =
+                    make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+            }
+        }
+        __syncwarp();
     }
 }
 
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams p)
 {
-    extern __shared__ float4 mega_smem[];
-    float4 *xs = mega_smem;
+    extern __shared__ __align__(128) uint8_t mega_smem[];
     __shared__ float red[32];
-    unsigned barrier = 0;
-    if (p.timeline && blockIdx.x == 0 && threadIdx.x == 0) p.timeline[0] = globaltimer_ns();
-    const size_t layer_bytes = (size_t)kQKVRows * kHidden + (size_t)kHidden * kQuery +
-                               (size_t)kGateUpRows * kHidden + (size_t)kHidden * kInner;
+    __shared__ float best_v[kMegaConsumerWarps];
+    __shared__ int best_i[kMegaConsumerWarps];
+    __shared__ int last_cta;
+    __shared__ float rope_s[2 * kHeadDim];       // cos | sin of the step's position
+    __shared__ float res_s[kMegaMaxTiles * 16];  // residual rows of this CTA's tiles
+    Ring ring;
+    ring.slots = mega_smem;
+    uint32_t *frag = reinterpret_cast<uint32_t *>(mega_smem + (size_t)kRingSlots * kSlotBytes);
+    float *partial = reinterpret_cast<float *>(mega_smem + (size_t)kRingSlots * kSlotBytes + kFragBytes);
+    ring.full = reinterpret_cast<uint64_t *>(partial + kMegaMaxItems * 16);
+    ring.empty = ring.full + kRingSlots;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kRingSlots; s++) {
+            mbar_init(&ring.full[s], 1);
+            mbar_init(&ring.empty[s], 1);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        if (p.timeline && blockIdx.x == 0) p.timeline[0] = globaltimer_ns();
+    }
+    __syncthreads();
+
+    if (threadIdx.x >= kMegaConsumers) {
+        if (threadIdx.x == kMegaConsumers) produce(p, ring);
+        return;
+    }
+
+    const uint4 *frag4 = reinterpret_cast<const uint4 *>(frag);
+    float *xs_head = reinterpret_cast<float *>(frag);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    unsigned barrier = 0, taken = 0, seq = 0, tickets = 0;
     for (int s = 0; s < p.steps; s++) {
-        const int length = ld_cg_int(&p.step->length);
-        const int id = ld_cg_int(&p.step->ids[0]);
+        const bool rec = p.timeline && s == 0;
+        const int length = __ldcg(&p.step->length);
+        const int id = __ldcg(&p.step->ids[0]);
         const uint16_t *emb_row = p.embedding + (size_t)id * kHidden;
+        for (int i = threadIdx.x; i < 2 * kHeadDim; i += kMegaConsumers)
+            rope_s[i] = i < kHeadDim ? p.rope_cos[(size_t)length * kHeadDim + i]
+                                     : p.rope_sin[(size_t)length * kHeadDim + i - kHeadDim];
+        int splits, per;
+        attention_plan(length + 1, splits, per);
         for (int layer = 0; layer < kLayers; layer++) {
-            const uint8_t *base = p.w8 + (size_t)layer * layer_bytes;
             const float *sc = p.scales + layer * 7;
             GemvParams gp;
             memset(&gp, 0, sizeof gp);
@@ -337,12 +700,10 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
             gp.page_table = p.page_table;
             gp.num_pages = p.num_pages;
             gp.layer = layer;
-            gp.rope_cos = p.rope_cos;
-            gp.rope_sin = p.rope_sin;
+            gp.rope_row = rope_s;
             gp.length = length;
-            gp.bound[0] = gp.bound[1] = 1 << 30;
-            // qkv
-            gp.W = base;
+            // qkv: input norm, RoPE, KV store
+            PhaseSpan sp = phase_span(p, layer, kPhQKV);
             gp.rows = kQKVRows;
             gp.cols = kHidden;
             gp.scale[0] = sc[0];
@@ -351,66 +712,124 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
             gp.bound[0] = kQuery;
             gp.bound[1] = kQuery + kKV;
             gp.y = p.q;
-            if (p.prefetch) l2_prefetch_share(base + (size_t)kQKVRows * kHidden, (size_t)kHidden * kQuery);
-            mega_load_row(xs, p.x, layer == 0 ? emb_row : nullptr, p.norms + (size_t)(2 * layer) * kHidden,
-                          kHidden, red);
+            gp.y_stride = kQuery;
+            float inv = stage_frag<kHidden>(frag, p.x, layer == 0 ? emb_row : nullptr,
+                                            p.norms + (size_t)(2 * layer) * kHidden, red);
             if (layer == 0 && blockIdx.x == 0)
-                for (int c = threadIdx.x; c < kHidden; c += blockDim.x) p.x[c] = bf16_lo((uint32_t)emb_row[c]);
-            mega_gemv<kEpiQKV>(gp, xs);
-            mega_sync(p, ++barrier);
-            // attention
-            mega_attention(p, layer, length, reinterpret_cast<float *>(mega_smem));
-            mega_sync(p, ++barrier);
-            // o + residual
-            gp.W = base + (size_t)kQKVRows * kHidden;
+                for (int c = threadIdx.x; c < kHidden; c += kMegaConsumers) p.x[c] = bf16_lo((uint32_t)emb_row[c]);
+            consume_fp8<item_blocks(kPhQKV), kHidden / kBlockCols>(ring, sp, seq, taken, frag4, partial, p.error);
+            seq += sp.items;
+            consumers_sync();
+            fp8_epilogue<kEpiQKV>(gp, sp, kHidden / kBlockCols / item_blocks(kPhQKV), partial, inv);
+            grid_sync(p, ++barrier, rec);
+            mega_attention(p, layer, length, tickets, reinterpret_cast<float *>(frag));
+            if (splits > 1) tickets += (unsigned)splits;
+            grid_sync(p, ++barrier, rec);
+            // o + residual (x)
+            sp = phase_span(p, layer, kPhO);
             gp.rows = kHidden;
             gp.cols = kQuery;
             gp.scale[0] = gp.scale[1] = gp.scale[2] = sc[3];
             gp.bound[0] = gp.bound[1] = 1 << 30;
-            gp.res = p.x;
+            gp.res_shared = res_s;
+            gp.res_base = sp.first * kTileRows;
             gp.y = p.h;
-            if (p.prefetch) l2_prefetch_share(gp.W + (size_t)kHidden * kQuery, (size_t)kGateUpRows * kHidden);
-            mega_load_row(xs, p.attn, nullptr, nullptr, kQuery, red);
-            mega_gemv<kEpiResidual>(gp, xs);
-            mega_sync(p, ++barrier);
+            gp.y_stride = kHidden;
+            stage_rows(res_s, p.x, gp.res_base, sp.items / (kQuery / kBlockCols / item_blocks(kPhO)) * kTileRows);
+            inv = stage_frag<kQuery>(frag, p.attn, nullptr, nullptr, red);
+            consume_fp8<item_blocks(kPhO), kQuery / kBlockCols>(ring, sp, seq, taken, frag4, partial, p.error);
+            seq += sp.items;
+            consumers_sync();
+            fp8_epilogue<kEpiResidual>(gp, sp, kQuery / kBlockCols / item_blocks(kPhO), partial, inv);
+            grid_sync(p, ++barrier, rec);
             // post norm + gate/up + SwiGLU
-            gp.W = base + (size_t)kQKVRows * kHidden + (size_t)kHidden * kQuery;
+            sp = phase_span(p, layer, kPhGateUp);
             gp.rows = kGateUpRows;
             gp.cols = kHidden;
             gp.scale[0] = sc[4];
             gp.scale[1] = sc[5];
             gp.y = p.act;
-            if (p.prefetch) l2_prefetch_share(gp.W + (size_t)kGateUpRows * kHidden, (size_t)kHidden * kInner);
-            mega_load_row(xs, p.h, nullptr, p.norms + (size_t)(2 * layer + 1) * kHidden, kHidden, red);
-            mega_gemv<kEpiSwiGLU>(gp, xs);
-            mega_sync(p, ++barrier);
-            // down + residual
-            gp.W = base + (size_t)kQKVRows * kHidden + (size_t)kHidden * kQuery +
-                   (size_t)kGateUpRows * kHidden;
+            gp.y_stride = kInner;
+            inv = stage_frag<kHidden>(frag, p.h, nullptr, p.norms + (size_t)(2 * layer + 1) * kHidden, red);
+            consume_fp8<item_blocks(kPhGateUp), kHidden / kBlockCols>(ring, sp, seq, taken, frag4, partial, p.error);
+            seq += sp.items;
+            consumers_sync();
+            fp8_epilogue<kEpiSwiGLU>(gp, sp, kHidden / kBlockCols / item_blocks(kPhGateUp), partial, inv);
+            grid_sync(p, ++barrier, rec);
+            // down + residual (h)
+            sp = phase_span(p, layer, kPhDown);
             gp.rows = kHidden;
             gp.cols = kInner;
             gp.scale[0] = gp.scale[1] = gp.scale[2] = sc[6];
-            gp.res = p.h;
+            gp.res_base = sp.first * kTileRows;
             gp.y = p.x;
-            if (layer + 1 < kLayers) if (p.prefetch) l2_prefetch_share(base + layer_bytes, (size_t)kQKVRows * kHidden);
-            mega_load_row(xs, p.act, nullptr, nullptr, kInner, red);
-            mega_gemv<kEpiResidual>(gp, xs);
-            mega_sync(p, ++barrier);
+            gp.y_stride = kHidden;
+            stage_rows(res_s, p.h, gp.res_base, sp.items / (kInner / kBlockCols / item_blocks(kPhDown)) * kTileRows);
+            inv = stage_frag<kInner>(frag, p.act, nullptr, nullptr, red);
+            consume_fp8<item_blocks(kPhDown), kInner / kBlockCols>(ring, sp, seq, taken, frag4, partial, p.error);
+            seq += sp.items;
+            consumers_sync();
+            fp8_epilogue<kEpiResidual>(gp, sp, kInner / kBlockCols / item_blocks(kPhDown), partial, inv);
+            grid_sync(p, ++barrier, rec);
         }
-        mega_head(p, xs, red);
-        mega_sync(p, ++barrier);
-        if (blockIdx.x == 0 && threadIdx.x == 0) {
-            float v = __ldcg(&p.arg_val[0]);
-            int i = __ldcg(&p.arg_idx[0]);
-            for (int b = 1; b < (int)gridDim.x; b++) arg_better(v, i, __ldcg(&p.arg_val[b]), __ldcg(&p.arg_idx[b]));
-            int next = (i < 0 || i >= kVocab) ? 0 : i;
-            int generated = ld_cg_int(&p.step->generated);
-            p.tokens[generated] = next;
-            p.step->generated = generated + 1;
-            p.step->ids[0] = next;
-            p.step->length = length + 1;
+        // final norm + tied head, 8-column staging
+        {
+            float ss = 0.0f;
+            for (int c = threadIdx.x; c < kHidden; c += kMegaConsumers) {
+                float v = __ldcg(&p.x[c]);
+                ss += v * v;
+            }
+            ss = consumers_sum(ss, red);
+            const float rs = rsqrtf(ss / (float)kHidden + kNormEps);
+            const int NQ = kHidden >> 3;
+            for (int c = threadIdx.x; c < kHidden; c += kMegaConsumers)
+                xs_head[((size_t)((c >> 2) & 1) * NQ + (c >> 3)) * 4 + (c & 3)] =
+                    p.final_norm[c] * (__ldcg(&p.x[c]) * rs);
+            consumers_sync();
         }
-        mega_sync(p, ++barrier);
+        float best = -INFINITY;
+        int bi = 0x7fffffff;
+        const PhaseSpan hs = phase_span(p, 0, kPhHead);
+        consume_head(ring, hs, seq, taken, p, reinterpret_cast<const float4 *>(xs_head), best, bi, p.error);
+        seq += hs.items;
+        if (lane == 0) {
+            best_v[warp] = best;
+            best_i[warp] = bi;
+        }
+        consumers_sync();
+        if (threadIdx.x == 0) {
+            float v = best_v[0];
+            int i = best_i[0];
+            for (int w = 1; w < kMegaConsumerWarps; w++) arg_better(v, i, best_v[w], best_i[w]);
+            p.arg_val[blockIdx.x] = v;
+            p.arg_idx[blockIdx.x] = i;
+            __threadfence();
+            last_cta = atomicAdd(sync_word(p, kSyncPick), 1u) == gridDim.x * (unsigned)(s + 1) - 1;
+        }
+        consumers_sync();
+        if (last_cta && warp == 0) {
+            // the last CTA to finish the head picks the token (strict '>', lowest id)
+            __threadfence();
+            float v = -INFINITY;
+            int i = 0x7fffffff;
+            for (int b = lane; b < (int)gridDim.x; b += 32)
+                arg_better(v, i, __ldcg(&p.arg_val[b]), __ldcg(&p.arg_idx[b]));
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+                int i2 = __shfl_xor_sync(0xffffffffu, i, o);
+                arg_better(v, i, v2, i2);
+            }
+            if (lane == 0) {
+                const int next = (i < 0 || i >= kVocab) ? 0 : i;
+                const int generated = __ldcg(&p.step->generated);
+                p.tokens[generated] = next;
+                p.step->generated = generated + 1;
+                p.step->ids[0] = next;
+                p.step->length = length + 1;
+            }
+        }
+        grid_sync(p, ++barrier, rec);
     }
 }
 

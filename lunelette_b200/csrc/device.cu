@@ -46,6 +46,7 @@ struct lun_device {
     float *h_logits = nullptr;
     void *staging[2] = {nullptr, nullptr};
     cudaEvent_t staging_done[2] = {nullptr, nullptr};
+    uint8_t *upload_raw = nullptr;  // row-major tensor on its way to the tiled layout (upload only)
     int trace = 0;
     float *trace_buf = nullptr;
     size_t trace_count = 0;
@@ -56,8 +57,8 @@ struct lun_device {
     // persistent decode kernel state
     bool use_mega = true;
     float *d_scales = nullptr;          // [26][7]
-    unsigned *mega_barrier = nullptr;   // [2], zeroed before every launch
-    unsigned *attn_count = nullptr;     // [8], self-resetting
+    unsigned *mega_sync = nullptr;      // kSyncWords lines, zeroed before every launch
+    unsigned l2_ahead = 0;              // persistent kernel's L2 lookahead (bytes per CTA)
     int *mega_error = nullptr, *h_error = nullptr;
     float *arg_val = nullptr;
     int *arg_idx = nullptr;
@@ -165,21 +166,23 @@ extern "C" lun_device *lun_device_create(size_t context, size_t block, char *err
         (e = dalloc(&d->page_table, (size_t)d->num_pages * 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->d_flag, 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->d_scales, (size_t)kLayers * LUN_SLOT_COUNT * 4, sc)) != cudaSuccess ||
-        (e = dalloc(&d->mega_barrier, 2 * sizeof(unsigned), sc)) != cudaSuccess ||
-        (e = dalloc(&d->attn_count, kKVHeads * sizeof(unsigned), sc)) != cudaSuccess ||
+        (e = dalloc(&d->mega_sync, kSyncWords * kSyncStride * sizeof(unsigned), sc)) != cudaSuccess ||
         (e = dalloc(&d->mega_error, sizeof(int), sc)) != cudaSuccess ||
         (e = dalloc(&d->arg_val, (size_t)d->sm_count * 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->arg_idx, (size_t)d->sm_count * 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->d_tokens, context * sizeof(int), sc)) != cudaSuccess)
         goto bad;
-    if ((e = cudaMemset(d->attn_count, 0, kKVHeads * sizeof(unsigned))) != cudaSuccess ||
-        (e = cudaMemset(d->mega_error, 0, sizeof(int))) != cudaSuccess)
+    if ((e = cudaMemset(d->mega_error, 0, sizeof(int))) != cudaSuccess)
         goto bad;
     {
         const char *mega = getenv("LUNELETTE_MEGA");
-        d->use_mega = !(mega && mega[0] == '0');
+        d->use_mega = !(mega && mega[0] == '0') && lun_mega_supported(d->sm_count);
         const char *prefetch = getenv("LUNELETTE_PREFETCH");
         d->prefetch = !(prefetch && prefetch[0] == '0');
+        // L2 lookahead of the persistent kernel's weight stream, per CTA; longer
+        // lookaheads measured slower (prefetched lines evicted before use)
+        const char *ahead = getenv("LUNELETTE_L2_AHEAD_KB");
+        d->l2_ahead = (ahead ? (unsigned)strtoul(ahead, nullptr, 10) : 128u) << 10;
     }
     what = "pinned host buffers";
     if ((e = cudaMallocHost((void **)&d->h_step, sizeof(StepParams))) != cudaSuccess ||
@@ -237,12 +240,12 @@ extern "C" void lun_device_destroy(lun_device *d)
     cudaFree(d->d_tokens);
     cudaFree(d->d_partials);
     cudaFree(d->d_scales);
-    cudaFree(d->mega_barrier);
-    cudaFree(d->attn_count);
+    cudaFree(d->mega_sync);
     cudaFree(d->mega_error);
     cudaFree(d->arg_val);
     cudaFree(d->arg_idx);
     cudaFree(d->timeline);
+    cudaFree(d->upload_raw);
     cudaFreeHost(d->h_error);
     if (d->decode_graph) cudaGraphExecDestroy(d->decode_graph);
     cudaFreeHost(d->h_step);
@@ -274,50 +277,45 @@ extern "C" int lun_device_staging_wait(lun_device *d, int index)
 
 static uint8_t *layer_base(lun_device *d, int layer) { return d->w8 + (size_t)layer * kLayerBytes; }
 
+// FP8 linears are stored tiled (gemv.cuh): the row-major tensor is copied to a
+// device buffer and a tile kernel writes it into its matrix, placing q/k/v rows
+// so that RoPE pairs are adjacent and interleaving gate/up rows (gate f -> 2f,
+// up f -> 2f + 1), which the fused epilogues rely on.
 extern "C" int lun_device_upload_linear(lun_device *d, int index, int layer, int slot, size_t rows,
                                         size_t cols, float scale)
 {
-    const uint8_t *src = (const uint8_t *)d->staging[index & 1];
+    if (rows * cols > kStagingBytes || (cols % 64) || (rows % 16)) return -1;
     uint8_t *base = layer_base(d, layer);
-    cudaError_t e;
     d->scales[layer][slot] = scale;
+    uint8_t *matrix;
+    int order = kOrderRows, row0 = 0;
     switch (slot) {
     case LUN_SLOT_Q:
     case LUN_SLOT_K:
-    case LUN_SLOT_V: {
-        // group-major: within each 128-row head, row j < 64 goes to 2j and row
-        // j + 64 to 2j + 1, so the RoPE pairs (j, j+64) sit in adjacent rows
-        size_t row0 = slot == LUN_SLOT_Q ? 0 : (slot == LUN_SLOT_K ? kQuery : kQuery + kKV);
-        e = cudaSuccess;
-        for (size_t head = 0; e == cudaSuccess && head < rows / 128; head++) {
-            uint8_t *dst = base + (row0 + head * 128) * cols;
-            const uint8_t *s0 = src + head * 128 * cols;
-            e = cudaMemcpy2DAsync(dst, 2 * cols, s0, cols, cols, 64, cudaMemcpyHostToDevice, d->stream);
-            if (e == cudaSuccess)
-                e = cudaMemcpy2DAsync(dst + cols, 2 * cols, s0 + 64 * cols, cols, cols, 64,
-                                      cudaMemcpyHostToDevice, d->stream);
-        }
+    case LUN_SLOT_V:
+        matrix = base;
+        order = kOrderRopePairs;
+        row0 = slot == LUN_SLOT_Q ? 0 : (slot == LUN_SLOT_K ? kQuery : kQuery + kKV);
         break;
-    }
-    case LUN_SLOT_O:
-        e = cudaMemcpyAsync(base + kLayerQKV, src, rows * cols, cudaMemcpyHostToDevice, d->stream);
-        break;
+    case LUN_SLOT_O: matrix = base + kLayerQKV; break;
     case LUN_SLOT_GATE:
-    case LUN_SLOT_UP: {
-        // group-major: gate row f goes to 2f and up row f to 2f + 1
-        uint8_t *dst = base + kLayerQKV + kLayerO + (slot == LUN_SLOT_UP ? cols : 0);
-        e = cudaMemcpy2DAsync(dst, 2 * cols, src, cols, cols, rows, cudaMemcpyHostToDevice, d->stream);
+    case LUN_SLOT_UP:
+        matrix = base + kLayerQKV + kLayerO;
+        order = kOrderInterleave;
+        row0 = slot == LUN_SLOT_UP ? 1 : 0;
         break;
+    case LUN_SLOT_DOWN: matrix = base + kLayerQKV + kLayerO + kLayerGateUp; break;
+    default: return -1;
     }
-    case LUN_SLOT_DOWN:
-        e = cudaMemcpyAsync(base + kLayerQKV + kLayerO + kLayerGateUp, src, rows * cols,
-                            cudaMemcpyHostToDevice, d->stream);
-        break;
-    default:
+    if (!d->upload_raw && cudaMalloc((void **)&d->upload_raw, kStagingBytes) != cudaSuccess) return -1;
+    if (cudaMemcpyAsync(d->upload_raw, d->staging[index & 1], rows * cols, cudaMemcpyHostToDevice, d->stream) !=
+            cudaSuccess ||
+        cudaEventRecord(d->staging_done[index & 1], d->stream) != cudaSuccess)
         return -1;
-    }
-    if (e != cudaSuccess) return -1;
-    return cudaEventRecord(d->staging_done[index & 1], d->stream) == cudaSuccess ? 0 : -1;
+    return lun_launch_tile_fp8(d->upload_raw, (int)rows, (int)cols, matrix, (int)(cols / 64), order, row0,
+                               d->stream) == cudaSuccess
+               ? 0
+               : -1;
 }
 
 extern "C" int lun_device_upload_embedding(lun_device *d, int index, size_t offset, size_t bytes)
@@ -355,6 +353,8 @@ extern "C" int lun_device_upload_rope(lun_device *d, const float *cosine, const 
 extern "C" int lun_device_upload_finish(lun_device *d, char *error, size_t capacity)
 {
     cudaError_t e = cudaStreamSynchronize(d->stream);
+    cudaFree(d->upload_raw);
+    d->upload_raw = nullptr;
     if (e != cudaSuccess) return fail(error, capacity, "weight upload failed", e);
     e = cudaMemcpy(d->d_scales, d->scales, sizeof d->scales, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return fail(error, capacity, "scale upload failed", e);
@@ -513,22 +513,17 @@ static cudaError_t launch_mega(lun_device *d, int steps)
     p.act = d->act;
     p.part_acc = d->part_acc;
     p.part_ml = d->part_ml;
-    p.attn_count = d->attn_count;
-    AttnParams plan;
-    lun_attention_plan(&plan, (int)d->context, 1, d->sm_count, (int)kPartSlots);
-    p.split_len = plan.split_len;
-    p.splits = plan.splits;
     p.logits = d->logits;
     p.nonfinite = d->d_flag;
     p.arg_val = d->arg_val;
     p.arg_idx = d->arg_idx;
     p.tokens = d->d_tokens;
-    p.barrier = d->mega_barrier;
+    p.sync = d->mega_sync;
     p.error = d->mega_error;
     p.steps = steps;
     p.timeline = d->record_timeline ? d->timeline : nullptr;
-    p.prefetch = d->prefetch ? 1 : 0;
-    cudaError_t e = cudaMemsetAsync(d->mega_barrier, 0, 2 * sizeof(unsigned), d->stream);
+    p.l2_ahead = d->l2_ahead;
+    cudaError_t e = cudaMemsetAsync(d->mega_sync, 0, kSyncWords * kSyncStride * sizeof(unsigned), d->stream);
     if (e != cudaSuccess) return e;
     return lun_launch_decode_mega(p, d->sm_count, d->stream);
 }
@@ -603,7 +598,6 @@ extern "C" int lun_device_decode_loop(lun_device *d, int64_t first_token, size_t
             goto bad;
         if (*d->h_error) {
             cudaMemset(d->mega_error, 0, sizeof(int));
-            cudaMemset(d->attn_count, 0, kKVHeads * sizeof(unsigned));
             e = cudaErrorLaunchTimeout;
             what = "decode loop: grid barrier wait gave up";
             goto bad;
@@ -735,7 +729,6 @@ extern "C" int lun_device_run(lun_device *d, const int64_t *ids, size_t count, s
     if ((e = cudaStreamSynchronize(d->stream)) != cudaSuccess) goto bad;
     if (mega && *d->h_error) {
         cudaMemset(d->mega_error, 0, sizeof(int));
-        cudaMemset(d->attn_count, 0, kKVHeads * sizeof(unsigned));
         if (error && capacity) snprintf(error, capacity, "decode: grid barrier wait gave up");
         return -1;
     }
@@ -746,11 +739,16 @@ bad:
     return fail(error, capacity, what, e);
 }
 
+// CTA 0's barrier exits, then every CTA's barrier arrivals (mega_params.cuh)
+static size_t timeline_entries(const lun_device *d)
+{
+    return (size_t)kMegaTimelineHead + (size_t)kMegaBarriersPerStep * d->sm_count;
+}
+
 extern "C" int lun_device_timeline(lun_device *d, int enable)
 {
     if (enable && !d->timeline &&
-        cudaMalloc((void **)&d->timeline, (kMegaTimelineEntries) * sizeof(unsigned long long)) !=
-            cudaSuccess)
+        cudaMalloc((void **)&d->timeline, timeline_entries(d) * sizeof(unsigned long long)) != cudaSuccess)
         return -1;
     d->record_timeline = enable != 0;
     return 0;
@@ -758,7 +756,7 @@ extern "C" int lun_device_timeline(lun_device *d, int enable)
 
 extern "C" int lun_device_timeline_copy(lun_device *d, unsigned long long *out, size_t entries)
 {
-    if (!d->timeline || entries > kMegaTimelineEntries) return -1;
+    if (!d->timeline || entries > timeline_entries(d)) return -1;
     return cudaMemcpy(out, d->timeline, entries * sizeof(unsigned long long), cudaMemcpyDeviceToHost) ==
                    cudaSuccess
                ? 0

@@ -1,20 +1,27 @@
-// FP8-E4M3 weight GEMV family for decode (M = 1..4 token rows).
+// FP8-E4M3 weight GEMV family for decode and short chunks (M = 1..4 token rows).
 //
 // Replaces project_fp8 / project_fp8_lookup (src/metal_kernels.metal:136-177,
 // 249-272) and, by fusion, the norm, rope, element and KV-blit steps that the
 // reference encodes around each projection (src/metal_encode.m:124-187).
 // K and V rows are stored in FP32, the reference's KV precision.
 //
-// Layout: W is row-major [rows][cols] E4M3 bytes; one warp owns a group of four
-// rows and streams them with 16-byte loads (16 codes per lane per load, two
-// loads in flight per row), dequantises in registers (cvt e4m3x2 -> f16x2 ->
-// f32, exact), and accumulates in FP32 against the activation rows held in
-// shared memory. The per-tensor scale multiplies the reduced sum. The warp
-// reduction is a fixed xor butterfly, so results are run-to-run deterministic.
+// Tiled weight layout. Every FP8 matrix [rows][K] lives on the device as
+// 16-row tiles; a tile is ceil(K/64) blocks of 1 KB (16 rows x 64 columns),
+// stored in the order the m16n8k16 tensor-core MMA consumes them: byte
+// h*512 + lane*16 + j*4 + i of a block holds tile row 8h + (lane >> 2) and block
+// column 16j + 2(lane & 3) + (i & 1) + 8(i >> 1). One coalesced 16-byte load per
+// lane per half block yields the A fragments (rows g and g+8) of the block's four
+// k16 MMAs. Rows past the matrix and columns past K are zero.
 //
-// Shared-memory activation layout: row m, 16-column chunk q, 4-column piece p
-// lives at float4 index m*4*NQ + p*NQ + q (NQ = cols/16). Consecutive lanes read
-// consecutive float4s, so the loads are bank-conflict free.
+// Arithmetic. E4M3 codes become FP16 exactly (cvt.rn.f16x2.e4m3x2). The FP32
+// activation row is scaled by an exact power of two 2^e (so its largest value
+// sits in [2^14, 2^15)) and split into FP16 hi + lo halves (hi = rn(x),
+// lo = rn(x - hi): 22 significant bits). The MMA's B operand carries hi and lo
+// of each token as two columns; FP16 x FP16 products are exact and accumulate in
+// FP32 on the tensor core, and the row sum is (hi column + lo column) * 2^-e,
+// times the per-tensor scale in the epilogue. This keeps the projections within
+// FP32 summation noise of the reference's FP32 dot products while replacing ten
+// CUDA-core instructions per four weights with two conversions and a quarter MMA.
 #pragma once
 #include "common.cuh"
 
@@ -27,8 +34,129 @@ enum GemvEpilogue : int {
     kEpiSwiGLU = 3,    // alternating gate/up rows: y[m][f] = silu(g) * u
 };
 
+constexpr int kTileRows = 16;
+constexpr int kBlockCols = 64;
+constexpr int kBlockBytes = 1024;
+
+// Bytes of a matrix in the tiled layout (rows padded to 16, columns to 64).
+__host__ __device__ constexpr size_t tiled_bytes(size_t rows, size_t cols)
+{
+    return ((rows + 15) / 16) * 16 * ((cols + 63) / 64) * 64;
+}
+
+// Row orders the upload applies before tiling (storage row of source row r):
+//   kOrderRows       row0 + r
+//   kOrderRopePairs  inside every 128-row head, row j < 64 -> 2j, j + 64 -> 2j + 1
+//                    (RoPE pairs adjacent), offset by row0
+//   kOrderInterleave 2r + row0 (gate rows even, up rows odd)
+enum TileOrder : int { kOrderRows = 0, kOrderRopePairs = 1, kOrderInterleave = 2 };
+
+__host__ __device__ __forceinline__ int tile_storage_row(int order, int row0, int r)
+{
+    if (order == kOrderRopePairs) {
+        const int j = r & 127;
+        return row0 + (r & ~127) + (j < 64 ? 2 * j : 2 * (j - 64) + 1);
+    }
+    if (order == kOrderInterleave) return 2 * r + row0;
+    return row0 + r;
+}
+
+// Row-major [rows][cols] codes (cols % 16 == 0) -> tiled matrix of dst_nb blocks
+// per tile; one thread per 16-column chunk. Padding is the caller's (zeroed) memory.
+static __global__ void tile_fp8_kernel(const uint8_t *src, int rows, int cols, uint8_t *dst, int dst_nb,
+                                       int order, int row0)
+{
+    const int chunks_per_row = cols >> 4;
+    const size_t chunks = (size_t)rows * chunks_per_row;
+    for (size_t u = (size_t)blockIdx.x * blockDim.x + threadIdx.x; u < chunks; u += (size_t)gridDim.x * blockDim.x) {
+        const int r = (int)(u / chunks_per_row), q = (int)(u % chunks_per_row);
+        const uint4 v = *reinterpret_cast<const uint4 *>(src + (size_t)r * cols + (size_t)q * 16);
+        const int s = tile_storage_row(order, row0, r);
+        const int tile = s >> 4, h = (s >> 3) & 1, g = s & 7, kb = q >> 2, j = q & 3;
+        uint8_t *blk = dst + ((size_t)tile * dst_nb + kb) * kBlockBytes + h * 512 + j * 4;
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int t4 = 0; t4 < 4; t4++) {
+            const int sh = 16 * (t4 & 1);
+            const uint32_t lo = (w[t4 >> 1] >> sh) & 0xffffu, hi = (w[2 + (t4 >> 1)] >> sh) & 0xffffu;
+            *reinterpret_cast<uint32_t *>(blk + (g * 4 + t4) * 16) = lo | (hi << 16);
+        }
+    }
+}
+
+// ---- MMA helpers -------------------------------------------------------------
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two_codes)
+{
+    uint32_t h;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"((uint16_t)(two_codes & 0xffffu)));
+    return h;
+}
+
+__device__ __forceinline__ void mma_f16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1)
+{
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// The four k16 MMAs of one block: wa/wb are this lane's 16 bytes of rows g and
+// g+8, x0/x1 its B fragments (zero on lanes past the activation columns).
+__device__ __forceinline__ void mma_block(float (&c)[4], const uint4 &wa, const uint4 &wb, const uint4 &x0,
+                                          const uint4 &x1)
+{
+    mma_f16_16816(c, e4m3x2_to_f16x2(wa.x), e4m3x2_to_f16x2(wb.x), e4m3x2_to_f16x2(wa.x >> 16),
+                  e4m3x2_to_f16x2(wb.x >> 16), x0.x, x0.y);
+    mma_f16_16816(c, e4m3x2_to_f16x2(wa.y), e4m3x2_to_f16x2(wb.y), e4m3x2_to_f16x2(wa.y >> 16),
+                  e4m3x2_to_f16x2(wb.y >> 16), x0.z, x0.w);
+    mma_f16_16816(c, e4m3x2_to_f16x2(wa.z), e4m3x2_to_f16x2(wb.z), e4m3x2_to_f16x2(wa.z >> 16),
+                  e4m3x2_to_f16x2(wb.z >> 16), x1.x, x1.y);
+    mma_f16_16816(c, e4m3x2_to_f16x2(wa.w), e4m3x2_to_f16x2(wb.w), e4m3x2_to_f16x2(wa.w >> 16),
+                  e4m3x2_to_f16x2(wb.w >> 16), x1.z, x1.w);
+}
+
+// ---- activation fragments ------------------------------------------------------
+// B fragments of `lanes` = 8 * tokens lanes per half block, as uint4 index
+// (kb * 2 + half) * lanes + lane; lane 4n + t4 carries B column n (token n / 2,
+// hi for even n, lo for odd n). Word (j & 1) * 2 + b of that uint4 holds MMA j
+// (j >> 1 == half) register b: columns 16j + 2t4 + 8b and the next one.
+__device__ __forceinline__ void frag_store_pair(uint32_t *frag, int lanes, int c, int n, uint32_t pair)
+{
+    const int kb = c >> 6, w = c & 63, j = w >> 4, ww = w & 15;
+    const int t4 = (ww & 7) >> 1, b = ww >> 3;
+    frag[((size_t)(kb * 2 + (j >> 1)) * lanes + n * 4 + t4) * 4 + (j & 1) * 2 + b] = pair;
+}
+
+__device__ __forceinline__ uint32_t half2_bits(__half a, __half b)
+{
+    __half2 h = __halves2half2(a, b);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// hi/lo FP16 split of two (already scaled) values.
+__device__ __forceinline__ void split_hilo(float a, float b, uint32_t &hi, uint32_t &lo)
+{
+    const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+    hi = half2_bits(ha, hb);
+    lo = half2_bits(__float2half_rn(a - __half2float(ha)), __float2half_rn(b - __half2float(hb)));
+}
+
+// Exponent e with bound * 2^e < 2^15 for an upper bound of the row's magnitudes
+// (0 for an all-zero or non-finite row, whose NaN/Inf then propagate).
+__device__ __forceinline__ int frag_exponent(float bound)
+{
+    if (!(bound > 0.0f) || !isfinite(bound)) return 0;
+    const int e = 14 - ((int)((__float_as_uint(bound) >> 23) & 0xffu) - 127);
+    return e < -100 ? -100 : (e > 100 ? 100 : e);
+}
+
+__device__ __forceinline__ float exp2i(int e) { return __uint_as_float((uint32_t)(127 + e) << 23); }
+
+// ---- multi-token GEMV ------------------------------------------------------------
 struct GemvParams {
-    const uint8_t *W;
+    const uint8_t *W;    // tiled matrix
     int rows, cols;
     const float *x;      // [M][x_stride] activations (pre-norm when gain != nullptr)
     int x_stride;
@@ -51,28 +179,74 @@ struct GemvParams {
     // runs so that HBM keeps streaming across kernel boundaries (or nullptr).
     const uint8_t *prefetch;
     size_t prefetch_bytes;
+    // One-token callers may stage epilogue operands in shared memory: the RoPE
+    // row of the position (cos[128] then sin[128]) and residual rows
+    // [res_base, ...) of token 0; nullptr reads the global arrays above.
+    const float *rope_row;
+    const float *res_shared;
+    int res_base;
 };
 
+// Stage M activation rows (normed when p.gain) as hi/lo B fragments for the
+// whole block; inv_scale[m] = 2^-e of row m. red: 16 * M floats of scratch.
 template <int M>
-__device__ __forceinline__ void gemv_load_x(const GemvParams &p, float4 *xs, float *red)
+__device__ __forceinline__ void gemv_stage(const GemvParams &p, uint32_t *frag, float *inv_scale, float *red)
 {
-    const int cols = p.cols, NQ = cols >> 4;
-    float *xf = reinterpret_cast<float *>(xs);
+    const int cols = p.cols, NB = (cols + 63) >> 6, lanes = 8 * M;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+    float ss[M], mx[M];
 #pragma unroll
     for (int m = 0; m < M; m++) {
+        ss[m] = 0.0f;
+        mx[m] = 0.0f;
         const float *xr = p.x + (size_t)m * p.x_stride;
-        float rs = 1.0f;
-        if (p.gain) {
-            float ss = 0.0f;
-            for (int c = threadIdx.x; c < cols; c += blockDim.x) ss += xr[c] * xr[c];
-            ss = block_sum(ss, red);
-            rs = rsqrtf(ss / (float)cols + kNormEps);
-        }
         for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-            float v = xr[c];
-            if (p.gain) v = p.gain[c] * (v * rs);
-            int q = c >> 4, piece = (c >> 2) & 3, e = c & 3;
-            xf[((size_t)m * 4 * NQ + (size_t)piece * NQ + q) * 4 + e] = v;
+            const float v = xr[c];
+            ss[m] += v * v;
+            mx[m] = fmaxf(mx[m], fabsf(p.gain ? p.gain[c] * v : v));
+        }
+        ss[m] = warp_sum(ss[m]);
+        mx[m] = warp_max(mx[m]);
+        if (lane == 0) {
+            red[(warp * M + m) * 2] = ss[m];
+            red[(warp * M + m) * 2 + 1] = mx[m];
+        }
+    }
+    __syncthreads();
+    float rs[M], sc[M];
+#pragma unroll
+    for (int m = 0; m < M; m++) {
+        float s = 0.0f, x = 0.0f;
+        for (int w = 0; w < warps; w++) {
+            s += red[(w * M + m) * 2];
+            x = fmaxf(x, red[(w * M + m) * 2 + 1]);
+        }
+        rs[m] = p.gain ? rsqrtf(s / (float)cols + kNormEps) : 1.0f;
+        const int e = frag_exponent(x * rs[m] * 1.0001f);
+        sc[m] = exp2i(e);
+        if (threadIdx.x == 0) inv_scale[m] = exp2i(-e);
+    }
+    // column pairs (c, c+1); columns in [cols, 64 * NB) are zero
+    for (int c = 2 * threadIdx.x; c < 64 * NB; c += 2 * blockDim.x) {
+        float g0 = 1.0f, g1 = 1.0f;
+        if (p.gain && c < cols) {
+            g0 = p.gain[c];
+            g1 = p.gain[c + 1];
+        }
+#pragma unroll
+        for (int m = 0; m < M; m++) {
+            uint32_t hi = 0, lo = 0;
+            if (c < cols) {
+                const float *xr = p.x + (size_t)m * p.x_stride;
+                float a = xr[c], b = xr[c + 1];
+                if (p.gain) {
+                    a = g0 * (a * rs[m]);
+                    b = g1 * (b * rs[m]);
+                }
+                split_hilo(a * sc[m], b * sc[m], hi, lo);
+            }
+            frag_store_pair(frag, lanes, c, 2 * m, hi);
+            frag_store_pair(frag, lanes, c, 2 * m + 1, lo);
         }
     }
 }
@@ -117,7 +291,10 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, int g, int la
                     int r = logical_row<EPI>(g, i);
                     if (r < p.rows) {
                         float v = acc[i][m] * elem_scale<EPI>(p, g, i);
-                        if (EPI == kEpiResidual) v = __ldcg(&p.res[(size_t)m * p.res_stride + r]) + v;
+                        if (EPI == kEpiResidual)
+                            v = (p.res_shared ? p.res_shared[r - p.res_base]
+                                              : __ldcg(&p.res[(size_t)m * p.res_stride + r])) +
+                                v;
                         p.y[(size_t)m * p.y_stride + r] = v;
                     }
                 }
@@ -142,8 +319,8 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, int g, int la
                 int pos = (p.step ? p.step->length : p.length) + p.token_offset + m;
                 int j = ra & 127;
                 if (ra < kQuery + kKV) {
-                    const float *cs = p.rope_cos + (size_t)pos * 128;
-                    const float *sn = p.rope_sin + (size_t)pos * 128;
+                    const float *cs = p.rope_row ? p.rope_row : p.rope_cos + (size_t)pos * 128;
+                    const float *sn = p.rope_row ? p.rope_row + 128 : p.rope_sin + (size_t)pos * 128;
                     float lo = a * cs[j] + (-b) * sn[j];
                     float hi = b * cs[j + 64] + a * sn[j + 64];
                     a = lo;
@@ -167,86 +344,58 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, int g, int la
     }
 }
 
-// Dot products of the four rows of group g against the M activation rows in
-// shared memory; every lane ends with the full (butterfly-reduced) sums.
+// One launch: 8 warps per block, grid-stride over 16-row tiles. The warps
+// split a tile's blocks (warp w takes blocks w, w+8, ...), then their partial
+// row sums are added in warp order (deterministic) and warps 0-3 run the
+// epilogue of the tile's four row groups.
 template <int M, int EPI>
-__device__ __forceinline__ void gemv_group(const GemvParams &p, const float4 *xs, int g, int lane,
-                                           float (&acc)[4][M])
+__global__ void __launch_bounds__(256) gemv_tiled_kernel(GemvParams p)
 {
-    const int NQ = p.cols >> 4;
-    const uint8_t *wr[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        int r = 4 * g + i;  // storage row
-        wr[i] = p.W + (size_t)(r < p.rows ? r : p.rows - 1) * p.cols;
-    }
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-#pragma unroll
-        for (int m = 0; m < M; m++) acc[i][m] = 0.0f;
-
-    for (int q0 = lane; q0 < NQ; q0 += 64) {
-        uint4 w[2][4];
-#pragma unroll
-        for (int u = 0; u < 2; u++) {
-            int q = q0 + 32 * u;
-#pragma unroll
-            for (int i = 0; i < 4; i++)
-                w[u][i] = q < NQ ? ld_stream(wr[i] + (size_t)q * 16) : make_uint4(0, 0, 0, 0);
-        }
-#pragma unroll
-        for (int u = 0; u < 2; u++) {
-            int q = q0 + 32 * u;
-            if (q >= NQ) break;
-#pragma unroll
-            for (int piece = 0; piece < 4; piece++) {
-                float4 xv[M];
-#pragma unroll
-                for (int m = 0; m < M; m++) xv[m] = xs[(size_t)m * 4 * NQ + (size_t)piece * NQ + q];
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    uint32_t word = piece == 0 ? w[u][i].x : piece == 1 ? w[u][i].y
-                                  : piece == 2 ? w[u][i].z : w[u][i].w;
-                    float2 lo = e4m3x2_to_float2(word);
-                    float2 hi = e4m3x2_to_float2(word >> 16);
-#pragma unroll
-                    for (int m = 0; m < M; m++) {
-                        float a = acc[i][m];
-                        a = fmaf(lo.x, xv[m].x, a);
-                        a = fmaf(lo.y, xv[m].y, a);
-                        a = fmaf(hi.x, xv[m].z, a);
-                        a = fmaf(hi.y, xv[m].w, a);
-                        acc[i][m] = a;
-                    }
-                }
-            }
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-#pragma unroll
-        for (int m = 0; m < M; m++) acc[i][m] = warp_sum(acc[i][m]);
-}
-
-// One launch: blockDim 256 (8 warps); grid-stride over row groups of 4.
-template <int M, int EPI>
-__global__ void __launch_bounds__(256) gemv_fp8_kernel(GemvParams p)
-{
-    extern __shared__ float4 xs[];
-    __shared__ float red[32];
+    extern __shared__ uint4 frag4[];
+    __shared__ float part[8][16][M];
+    __shared__ float inv_scale[M];
+    __shared__ float red[16 * M];
     l2_prefetch_share(p.prefetch, p.prefetch_bytes);
     pdl_wait();
     pdl_launch_dependents();
-    gemv_load_x<M>(p, xs, red);
+    gemv_stage<M>(p, reinterpret_cast<uint32_t *>(frag4), inv_scale, red);
     __syncthreads();
 
-    const int lane = threadIdx.x & 31;
-    const int groups = (p.rows + 3) >> 2;
-    const int warps = gridDim.x * (blockDim.x >> 5);
-    for (int g = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); g < groups; g += warps) {
-        float acc[4][M];
-        gemv_group<M, EPI>(p, xs, g, lane, acc);
-        gemv_epilogue<M, EPI>(p, g, lane, acc);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+    const int NB = (p.cols + 63) >> 6, tiles = (p.rows + 15) >> 4, lanes = 8 * M;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+        const uint8_t *tw = p.W + (size_t)tile * NB * kBlockBytes;
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
+        for (int kb = warp; kb < NB; kb += 8) {
+            const uint4 wa = ld_stream(tw + (size_t)kb * kBlockBytes + lane * 16);
+            const uint4 wb = ld_stream(tw + (size_t)kb * kBlockBytes + 512 + lane * 16);
+            uint4 x0 = make_uint4(0, 0, 0, 0), x1 = x0;
+            if (lane < lanes) {
+                x0 = frag4[(kb * 2) * lanes + lane];
+                x1 = frag4[(kb * 2 + 1) * lanes + lane];
+            }
+            mma_block(c, wa, wb, x0, x1);
+        }
+        if (t4 < M) {
+            part[warp][g][t4] = c[0] + c[1];
+            part[warp][g + 8][t4] = c[2] + c[3];
+        }
+        __syncthreads();
+        if (warp < 4) {
+            float acc[4][M];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int m = 0; m < M; m++) {
+                    float s = 0.0f;
+#pragma unroll
+                    for (int w = 0; w < 8; w++) s += part[w][warp * 4 + i][m];
+                    acc[i][m] = s * inv_scale[m];
+                }
+            gemv_epilogue<M, EPI>(p, tile * 4 + warp, lane, acc);
+        }
+        __syncthreads();
     }
 }
 

@@ -41,8 +41,33 @@ static GemvParams plain(const uint8_t *W, size_t rows, size_t cols, float scale)
     return p;
 }
 
+// Row-major FP8 codes -> the tiled layout that every GEMV entry point reads.
+// order 0 keeps the rows; 1 takes q|k|v rows (rows % 128 == 0) and places the
+// RoPE pairs (j, j + 64) of every 128-row head in adjacent rows; 2 takes gate
+// rows followed by up rows (rows even) and interleaves them (gate f -> 2f,
+// up f -> 2f + 1). Padding rows/columns of dst are zeroed.
+LUN_API int lunelette_cuda_tile_fp8(const uint8_t *src, size_t rows, size_t cols, int order, uint8_t *dst,
+                                    void *stream)
+{
+    if (!src || !dst || !rows || !cols || (cols % 16) || rows > (1u << 24) || cols > (1u << 16) || order < 0 ||
+        order > 2 || (order == 1 && rows % 128) || (order == 2 && rows % 2))
+        return -1;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int nb = (int)((cols + 63) / 64);
+    if (tiled_bytes(rows, cols) != rows * cols && cudaMemsetAsync(dst, 0, tiled_bytes(rows, cols), st) != cudaSuccess)
+        return -1;
+    if (order == 2) {
+        const int half = (int)(rows / 2);
+        if (lun_launch_tile_fp8(src, half, (int)cols, dst, nb, kOrderInterleave, 0, st) != cudaSuccess) return -1;
+        return ok(lun_launch_tile_fp8(src + (size_t)half * cols, half, (int)cols, dst, nb, kOrderInterleave, 1, st));
+    }
+    return ok(lun_launch_tile_fp8(src, (int)rows, (int)cols, dst, nb, order == 1 ? kOrderRopePairs : kOrderRows, 0,
+                                  st));
+}
+
 // y[t][r] = scale * sum_c decode(W[r][c]) * x[t][c] (+ res[t][r]), any count
-// (processed in groups of 4 rows of x). cols must be a multiple of 16.
+// (processed in groups of 4 rows of x). W is tiled (lunelette_cuda_tile_fp8,
+// order 0); cols must be a multiple of 16.
 LUN_API int lunelette_cuda_gemv_fp8(const uint8_t *W, size_t rows, size_t cols, float scale,
                                     const float *x, const float *res, size_t count, float *y,
                                     void *stream)
@@ -70,7 +95,8 @@ LUN_API int lunelette_cuda_gemv_fp8(const uint8_t *W, size_t rows, size_t cols, 
 }
 
 // Fused input-norm + q/k/v projection + RoPE (+query scale) + KV store for
-// tokens at positions length..length+count-1. W is [6144][3072] (q|k|v rows).
+// tokens at positions length..length+count-1. W is the tiled [6144][3072] q|k|v
+// matrix (lunelette_cuda_tile_fp8, order 1).
 LUN_API int lunelette_cuda_qkv_rope(const uint8_t *W, const float *scales, const float *gain,
                                     const float *x, size_t count, size_t length,
                                     const float *rope_cos, const float *rope_sin, float *q_out,
@@ -108,7 +134,8 @@ LUN_API int lunelette_cuda_qkv_rope(const uint8_t *W, const float *scales, const
 }
 
 // Fused post-attention norm + gate/up projection + SwiGLU.
-// W is [18432][3072] with gate row f at 2f and up row f at 2f + 1.
+// W is the tiled [18432][3072] gate/up matrix (lunelette_cuda_tile_fp8, order 2:
+// gate row f at 2f, up row f at 2f + 1).
 LUN_API int lunelette_cuda_gateup_swiglu(const uint8_t *W, float scale_gate, float scale_up,
                                          const float *gain, const float *x, size_t count,
                                          float *act, void *stream)

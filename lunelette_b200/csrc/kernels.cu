@@ -6,7 +6,7 @@ using namespace lun;
 
 namespace {
 
-constexpr int kMaxGemvSmem = 4 * kInner * 4;  // 4 rows x 9216 FP32
+constexpr int kMaxGemvSmem = (kInner / 64) * 256 * 4;  // B fragments of 4 rows x 9216 columns
 
 // Programmatic dependent launch for every kernel of the decode/prefill sequence
 // (LUNELETTE_PDL=0 turns it off for comparisons).
@@ -39,7 +39,7 @@ cudaError_t launch(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem
 template <int M, int EPI>
 cudaError_t setup_one()
 {
-    return cudaFuncSetAttribute(gemv_fp8_kernel<M, EPI>,
+    return cudaFuncSetAttribute(gemv_tiled_kernel<M, EPI>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxGemvSmem);
 }
 
@@ -53,20 +53,20 @@ cudaError_t setup_epi()
     return setup_one<4, EPI>();
 }
 
+// B fragments: 256 bytes per token per 64-column block.
 template <int M, int EPI>
 cudaError_t launch_one(const GemvParams &p, int sm_count, cudaStream_t stream)
 {
-    const size_t smem = (size_t)M * p.cols * 4;
+    const size_t smem = (size_t)((p.cols + 63) / 64) * 256 * M;
     int per_sm = 0;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_fp8_kernel<M, EPI>,
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_tiled_kernel<M, EPI>,
                                                                   256, smem);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) per_sm = 1;
-    int groups = (p.rows + 3) / 4;
-    int blocks = (groups + 7) / 8;
+    int blocks = (p.rows + 15) / 16;
     int limit = sm_count * per_sm;
     if (blocks > limit) blocks = limit;
-    return launch(gemv_fp8_kernel<M, EPI>, dim3(blocks), dim3(256), smem, stream, p);
+    return launch(gemv_tiled_kernel<M, EPI>, dim3(blocks), dim3(256), smem, stream, p);
 }
 
 template <int EPI>
@@ -288,6 +288,17 @@ cudaError_t lun_launch_rmsnorm(const float *gain, const float *x, float *out, in
 {
     if (width <= 0 || count <= 0) return cudaErrorInvalidValue;
     return launch(rmsnorm_kernel, dim3(count), dim3(256), 0, stream, gain, x, out, width);
+}
+
+cudaError_t lun_launch_tile_fp8(const uint8_t *src, int rows, int cols, uint8_t *dst, int dst_nb, int order,
+                                int row0, cudaStream_t stream)
+{
+    if (rows <= 0 || cols <= 0 || (cols & 15) || dst_nb < (cols + 63) / 64) return cudaErrorInvalidValue;
+    const size_t chunks = (size_t)rows * (cols / 16);
+    size_t blocks = (chunks + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    tile_fp8_kernel<<<(unsigned)blocks, 256, 0, stream>>>(src, rows, cols, dst, dst_nb, order, row0);
+    return cudaGetLastError();
 }
 
 cudaError_t lun_launch_fp8_decode(const uint8_t *codes, size_t n, float scale, float *out,

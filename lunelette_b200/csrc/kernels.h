@@ -9,7 +9,13 @@ cudaError_t lun_kernels_init();
 // lun_kernels_init() once per device (cached); call before any graph capture.
 cudaError_t lun_kernels_ensure();
 
-// GEMV family: m token rows (1..4), epilogue kind lun::GemvEpilogue.
+// Row-major FP8 [rows][cols] (cols % 16 == 0) -> the tiled layout of gemv.cuh
+// with dst_nb blocks per tile, rows placed by lun::TileOrder from row0. Padding
+// rows/columns of dst are left as they are (zero them first).
+cudaError_t lun_launch_tile_fp8(const uint8_t *src, int rows, int cols, uint8_t *dst, int dst_nb, int order,
+                                int row0, cudaStream_t stream);
+
+// GEMV family over a tiled matrix: m token rows (1..4), epilogue kind lun::GemvEpilogue.
 cudaError_t lun_launch_gemv(const lun::GemvParams &p, int m, int epilogue, int sm_count,
                             cudaStream_t stream);
 cudaError_t lun_launch_head(const lun::HeadParams &p, int sm_count, cudaStream_t stream);
@@ -41,6 +47,8 @@ namespace lun {
 struct MegaParams;
 }
 cudaError_t lun_launch_decode_mega(const lun::MegaParams &p, int sm_count, cudaStream_t stream);
+// Whether the persistent kernel's per-CTA work fits on a grid of sm_count CTAs.
+bool lun_mega_supported(int sm_count);
 
 // FP8 codes -> FP32 * scale through the same in-register conversion as the GEMV.
 cudaError_t lun_launch_fp8_decode(const uint8_t *codes, size_t n, float scale, float *out,

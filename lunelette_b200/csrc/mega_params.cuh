@@ -5,11 +5,28 @@
 
 namespace lun {
 
-constexpr int kMegaBarriersPerStep = kLayers * 5 + 2;
-constexpr int kMegaTimelineEntries = 1 + kMegaBarriersPerStep;
+// grid barriers per decode step: 5 per layer, one after the head and the pick
+constexpr int kMegaBarriersPerStep = kLayers * 5 + 1;
+// Timeline of the first step of a launch: [0] start, [1 + k] CTA 0 leaving
+// barrier k (k = 0..130), then from kMegaTimelineHead every CTA b's arrival at
+// barrier k in entry kMegaTimelineHead + k * gridDim.x + b.
+constexpr int kMegaTimelineHead = 1 + kMegaBarriersPerStep;
+
+// Synchronisation words of one launch, each on its own 128-byte line, zero at
+// launch and only ever increased:
+//   kSyncBarrier        grid barrier arrivals (gridDim per barrier)
+//   kSyncTicket + kvh   attention ranges of KV head kvh finished
+//   kSyncPick           CTAs done with the head (gridDim per step)
+constexpr int kSyncStride = 32;
+enum : int {
+    kSyncBarrier = 0,
+    kSyncTicket = 1,
+    kSyncPick = kSyncTicket + kKVHeads,
+    kSyncWords = kSyncPick + 1,
+};
 
 struct MegaParams {
-    const uint8_t *w8;       // [26][qkv | o | gate/up | down]
+    const uint8_t *w8;       // [26][qkv | o | gate/up | down], tiled (gemv.cuh)
     const float *scales;     // [26][7]: q k v o gate up down
     const uint16_t *embedding;
     const float *norms;      // [26][2][3072]
@@ -20,21 +37,17 @@ struct MegaParams {
     const float *rope_cos, *rope_sin;
     StepParams *step;        // length and ids[0] advance on the device each step
     float *x, *h, *q, *attn, *act;
-    float *part_acc, *part_ml;  // [32 heads][splits][128] and [..][2]
-    unsigned *attn_count;       // [8] self-resetting arrival counters
-    int split_len, splits;
+    float *part_acc, *part_ml;  // [8 KV heads][ranges][4 query heads][128] and [..][2]
     float *logits;
     int *nonfinite;
     float *arg_val;
     int *arg_idx;               // [gridDim.x] per-CTA argmax partials
     int *tokens;                // generated ids
-    unsigned *barrier;          // [0] arrivals, [1] generation; zero at launch
+    unsigned *sync;             // kSyncWords * kSyncStride words, zero at launch
     int *error;
     int steps;
-    // optional: CTA 0 records %globaltimer (ns) at kernel start and after every
-    // grid barrier of the first step ([1 + barriers per step] entries)
-    unsigned long long *timeline;
-    int prefetch;  // 0 disables the next-matrix L2 prefetch (measurement only)
+    unsigned l2_ahead;          // bytes of a CTA's weight stream kept prefetched into L2 ahead of its ring
+    unsigned long long *timeline;  // optional %globaltimer (ns) record, layout above
 };
 
 }  // namespace lun

@@ -2,8 +2,10 @@
 
 Shapes: the model's FP8 linears q 3072->4096, k/v 3072->1024, o 4096->3072,
 gate/up 3072->9216, down 9216->3072, and the BF16 lm_head 3072->131072, at token
-batch M = 1, 2, 4, 8. Weights are random E4M3 codes (several copies rotated so
-that the working set exceeds L2), activations N(0,1). Time per launch from CUDA
+batch M = 1, 2, 4, 8. Weights are random E4M3 codes, read as the tiled layout
+the runtime stores (any random bytes are a valid tiled matrix of the same
+size); several copies rotate so that the working set exceeds L2; activations
+N(0,1). Time per launch from CUDA
 events on the launching stream; GB/s counts weight bytes + activations in and
 outputs once per launch (the algorithmic bytes), against the measured HBM peak.
 M = 8 runs as two launches of 4 rows (weights are streamed twice) — the GB/s
@@ -97,24 +99,31 @@ PHASE_BYTES = {"qkv": 6144 * 3072, "attention": 0, "o": 3072 * 4096, "gate_up": 
 def decode_phases(checkpoint, steps=8, prompt=32):
     """Per-phase durations of the persistent decode kernel (single-token steps
     through lunelette_metal_decode), from its %globaltimer timeline: the mean over
-    `steps` steps and 26 layers of each phase, plus the head+pick tail."""
+    `steps` steps and 26 layers of each phase, plus `head` (head GEMV and greedy
+    pick). Each phase runs from one grid barrier to the next. Per phase also
+    `<phase>_spread`, first to last CTA reaching the barrier that closes it, and
+    `<phase>_release`, the last arrival to CTA 0 leaving that barrier."""
+    import torch
     import lunelette_b200 as L
     peak, kind = hbm_peak()
-    rows = {name: [] for name in PHASES + ["head", "pick", "step"]}
+    ctas = torch.cuda.get_device_properties(0).multi_processor_count
+    names = PHASES + ["head"]
+    rows = {n: [] for n in names + [m + "_spread" for m in names] + [m + "_release" for m in names] + ["step"]}
     with L.Runtime(checkpoint) as rt:
         ids = np.random.default_rng(7).integers(1000, 131072, prompt)
         tok = int(np.argmax(rt.prefill(ids)))
         rt.timeline(True)
         for _ in range(steps):
             tok = int(np.argmax(rt.decode(tok)))
-            t = rt.timeline_copy().astype(np.float64) / 1000.0  # us
-            d = np.diff(t)
-            for layer in range(26):
-                for k, name in enumerate(PHASES):
-                    rows[name].append(d[layer * 5 + k])
-            rows["head"].append(d[130])
-            rows["pick"].append(d[131])
-            rows["step"].append(t[132] - t[0])
+            full = rt.timeline_copy(132 + 131 * ctas).astype(np.float64) / 1000.0  # us
+            t = full[:132]
+            arrive = full[132:].reshape(131, ctas)
+            for k in range(131):
+                name = names[k % 5] if k < 130 else "head"
+                rows[name].append(t[k + 1] - t[k])
+                rows[name + "_spread"].append(arrive[k].max() - arrive[k].min())
+                rows[name + "_release"].append(t[k + 1] - arrive[k].max())
+            rows["step"].append(t[131] - t[0])
         rt.timeline(False)
     out = []
     for name, vals in rows.items():

@@ -8,6 +8,8 @@ import struct
 import numpy as np
 import pytest
 
+from tests.tiling import ORDER_INTERLEAVE, ORDER_ROPE_PAIRS, ORDER_ROWS, tile_reference, tiled_bytes
+
 pytestmark = pytest.mark.gpu
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
@@ -44,6 +46,16 @@ def ptr(t):
     return t.data_ptr()
 
 
+def tiled(lib, torch, codes, order=ORDER_ROWS):
+    """Row-major codes -> the device's tiled layout, through the tile kernel."""
+    rows, cols = codes.shape
+    raw = dev(torch, codes)
+    out = torch.full((tiled_bytes(rows, cols),), 0xAB, dtype=torch.uint8, device="cuda")
+    _KEEP.append(out)
+    assert lib.lunelette_cuda_tile_fp8(ptr(raw), rows, cols, order, ptr(out), stream(torch)) == 0
+    return out
+
+
 def stream(torch):
     return torch.cuda.current_stream().cuda_stream
 
@@ -59,7 +71,7 @@ def finite_codes(rng, shape):
 
 
 def bf16_round(x):
-    b = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    b = np.array(x, np.float32).view(np.uint32).astype(np.uint64)
     b = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16) << 16
     return b.astype(np.uint32).view(np.float32)
 
@@ -89,7 +101,7 @@ def gemv_check(lib, oracle, torch, rows, cols, count, seed, residual=False):
     scale = float(bf16_round(np.float32(0.0003 + rng.random() * 0.01)))
     x = rng.standard_normal((count, cols)).astype(np.float32)
     res = rng.standard_normal((count, rows)).astype(np.float32) if residual else None
-    d_w, d_x = dev(torch, codes), dev(torch, x)
+    d_w, d_x = tiled(lib, torch, codes), dev(torch, x)
     d_r = dev(torch, res) if residual else None
     y = torch.empty((count, rows), dtype=torch.float32, device="cuda")
     rc = lib.lunelette_cuda_gemv_fp8(ptr(d_w), rows, cols, scale, ptr(d_x),
@@ -126,12 +138,55 @@ def test_gemv_exact_integer_dots(lib, torch_cuda, k):
     # all-ones weights (E4M3 0x38 = 1.0) and inputs give exactly K
     torch = torch_cuda
     rows, count = 5, 3
-    d_w = dev(torch, np.full((rows, k), 0x38, np.uint8))
+    d_w = tiled(lib, torch, np.full((rows, k), 0x38, np.uint8))
     d_x = dev(torch, np.ones((count, k), np.float32))
     y = torch.empty((count, rows), dtype=torch.float32, device="cuda")
     assert lib.lunelette_cuda_gemv_fp8(ptr(d_w), rows, k, 1.0, ptr(d_x), None, count, ptr(y),
                                        stream(torch)) == 0
     assert torch.all(y == float(k)).item()
+
+
+@pytest.mark.parametrize("rows,cols,order", [(7, 16, ORDER_ROWS), (33, 112, ORDER_ROWS), (259, 48, ORDER_ROWS),
+                                             (6144, 3072, ORDER_ROPE_PAIRS), (1024, 3072, ORDER_ROPE_PAIRS),
+                                             (18432, 3072, ORDER_INTERLEAVE), (3072, 9216, ORDER_ROWS)])
+def test_tile_kernel_matches_layout(lib, torch_cuda, rows, cols, order):
+    torch = torch_cuda
+    codes = np.random.default_rng(rows * 3 + cols + order).integers(0, 256, (rows, cols)).astype(np.uint8)
+    got = tiled(lib, torch, codes, order).cpu().numpy()
+    assert np.array_equal(got, tile_reference(codes, order))
+
+
+def test_tile_rejects_bad_arguments(lib, torch_cuda):
+    torch = torch_cuda
+    d = torch.zeros(1 << 16, dtype=torch.uint8, device="cuda")
+    assert lib.lunelette_cuda_tile_fp8(ptr(d), 16, 24, 0, ptr(d), stream(torch)) == -1   # cols % 16
+    assert lib.lunelette_cuda_tile_fp8(ptr(d), 100, 64, 1, ptr(d), stream(torch)) == -1  # rows % 128
+    assert lib.lunelette_cuda_tile_fp8(ptr(d), 15, 64, 2, ptr(d), stream(torch)) == -1   # odd rows
+    assert lib.lunelette_cuda_tile_fp8(ptr(d), 16, 64, 3, ptr(d), stream(torch)) == -1   # order
+    assert lib.lunelette_cuda_tile_fp8(None, 16, 64, 0, ptr(d), stream(torch)) == -1
+
+
+def test_gemv_hi_lo_split_keeps_fp32_accuracy_over_wide_ranges(lib, oracle, torch_cuda):
+    # activations spanning 2^-30..2^30 within one row: the power-of-two staging
+    # scale follows the largest value, tiny ones ride in the lo half or vanish
+    # below FP32 summation noise of the large ones
+    torch = torch_cuda
+    rng = np.random.default_rng(77)
+    rows, cols, count = 48, 3072, 3
+    codes = finite_codes(rng, (rows, cols))
+    x = (rng.standard_normal((count, cols)) * np.exp2(rng.integers(-30, 31, (count, cols)))).astype(np.float32)
+    x[1] *= np.float32(1e-20)
+    x[2] = 0.0
+    d_w, d_x = tiled(lib, torch, codes), dev(torch, x)
+    y = torch.empty((count, rows), dtype=torch.float32, device="cuda")
+    assert lib.lunelette_cuda_gemv_fp8(ptr(d_w), rows, cols, 0.001, ptr(d_x), None, count, ptr(y),
+                                       stream(torch)) == 0
+    got = y.cpu().numpy()
+    w64 = e4m3_table(oracle)[codes].astype(np.float64) * 0.001
+    exact = x.astype(np.float64) @ w64.T
+    bound = np.abs(x.astype(np.float64)) @ np.abs(w64).T
+    assert np.all(np.abs(got - exact) <= 1e-5 * bound + 1e-38)
+    assert not got[2].any()
 
 
 def test_gemv_rejects_unsupported_shapes(lib, torch_cuda):
@@ -153,17 +208,6 @@ def test_rmsnorm_matches_oracle(lib, oracle, torch_cuda):
         assert lib.lunelette_cuda_rmsnorm(ptr(dev(torch, g)), ptr(dev(torch, x)), width, count,
                                           ptr(out), stream(torch)) == 0
         assert np.abs(out.cpu().numpy() - oracle.norm(g, x)).max() < 2e-6 * 3 * 3
-
-
-def qkv_storage_order(codes):
-    """Checkpoint-order q|k|v rows -> the device's group-major order: inside
-    every 128-row head, row j < 64 to 2j and row j + 64 to 2j + 1."""
-    out = np.empty_like(codes)
-    for head in range(codes.shape[0] // 128):
-        block = codes[head * 128:(head + 1) * 128]
-        out[head * 128:(head + 1) * 128:2] = block[:64]
-        out[head * 128 + 1:(head + 1) * 128:2] = block[64:]
-    return out
 
 
 def pool_view(pool, num_pages):
@@ -199,7 +243,7 @@ def test_qkv_rope_kv_store_matches_oracle(lib, oracle, torch_cuda):
     pool = torch.zeros((layer + 1) * num_pages * 2 * 8 * 64 * 128, dtype=torch.float32, device="cuda")
     q_out = torch.empty((count, 4096), dtype=torch.float32, device="cuda")
     rc = lib.lunelette_cuda_qkv_rope(
-        ptr(dev(torch, qkv_storage_order(codes))), scales.ctypes.data, ptr(dev(torch, gain)),
+        ptr(tiled(lib, torch, codes, ORDER_ROPE_PAIRS)), scales.ctypes.data, ptr(dev(torch, gain)),
         ptr(dev(torch, x)),
         count, length, ptr(dev(torch, cos)), ptr(dev(torch, sin)), ptr(q_out), ptr(pool),
         ptr(dev(torch, page_table)), num_pages, layer, stream(torch))
@@ -228,14 +272,12 @@ def test_gateup_swiglu_matches_oracle(lib, oracle, torch_cuda):
     count = 3
     gate = finite_codes(rng, (9216, 3072))
     up = finite_codes(rng, (9216, 3072))
-    inter = np.empty((18432, 3072), np.uint8)  # device order: gate f at 2f, up f at 2f+1
-    inter[0::2] = gate
-    inter[1::2] = up
+    inter = tiled(lib, torch, np.concatenate([gate, up]), ORDER_INTERLEAVE)  # gate f at 2f, up f at 2f+1
     sg, su = float(bf16_round(np.float32(0.0004))), float(bf16_round(np.float32(0.0006)))
     gain = (0.5 + rng.random(3072)).astype(np.float32)
     x = rng.standard_normal((count, 3072)).astype(np.float32)
     act = torch.empty((count, 9216), dtype=torch.float32, device="cuda")
-    assert lib.lunelette_cuda_gateup_swiglu(ptr(dev(torch, inter)), sg, su, ptr(dev(torch, gain)),
+    assert lib.lunelette_cuda_gateup_swiglu(ptr(inter), sg, su, ptr(dev(torch, gain)),
                                             ptr(dev(torch, x)), count, ptr(act), stream(torch)) == 0
     normed = oracle.norm(gain, x)
     g = oracle.project_fp8(gate, sg, normed)

@@ -168,3 +168,26 @@ def test_capacity_256_fill_then_reject(runtime):
     with pytest.raises(L.LuneletteError):
         runtime.decode(11)
     assert runtime.length() == 256
+
+
+def test_long_context_decode_matches_multi_kernel_path(lib, checkpoint_path, monkeypatch):
+    # 700 positions: the persistent kernel splits each KV head's attention into
+    # position ranges and merges them; the multi-kernel path (LUNELETTE_MEGA=0)
+    # is itself checked against the oracle at long contexts by the attention
+    # kernel tests.
+    ids = prompt(99, 700)
+    runs = []
+    for mega in ("1", "0"):
+        monkeypatch.setenv("LUNELETTE_MEGA", mega)
+        with L.Runtime(checkpoint_path, limits=(4352, 256)) as rt:
+            rt.prefill(ids[:256])
+            rt.append(ids[256:512])
+            tok = int(np.argmax(rt.append(ids[512:])))
+            steps = []
+            for _ in range(3):
+                logits = rt.decode(tok).copy()
+                steps.append(logits)
+                tok = int(np.argmax(logits))
+            runs.append(np.stack(steps))
+    assert_close(runs[0], runs[1], "persistent vs multi-kernel decode at 700 positions")
+    assert [int(np.argmax(s)) for s in runs[0]] == [int(np.argmax(s)) for s in runs[1]]
