@@ -19,8 +19,8 @@
 // Item i of the CTA's stream goes to consumer warp i mod 7, which owns
 // kSlotsPerWarp private slots and takes its items strictly in order, so every
 // slot's full and empty barriers are waited on in phase order by one waiter.
-// Phases per layer: qkv (norm + q/k/v + RoPE + KV store), attention (split
-// over positions, the last split of a KV head merges), o (+ residual), gate/up
+// Phases per layer: qkv (norm + q/k/v + RoPE + KV store), attention (one CTA
+// per KV head and position range), o (+ residual), gate/up
 // (norm + SwiGLU), down (+ residual); then the head (final norm + tied BF16
 // GEMV) with a per-CTA argmax whose last CTA picks the token.
 //
@@ -46,8 +46,11 @@ constexpr int kMegaSmemBytes =
     kRingSlots * kSlotBytes + kFragBytes + kMegaMaxItems * 16 * 4 + 2 * kRingSlots * 8;
 constexpr unsigned kSpinLimit = 1u << 22;
 constexpr int kPhasesPerStep = kLayers * 4 + 1;  // 4 FP8 phases per layer, then the head
-constexpr int kAttnMaxSplits = 32;               // position ranges per KV head
+constexpr int kAttnMaxRanges = 18;               // position ranges per KV head (8 x 18 <= CTAs)
 constexpr int kQStride = 36;                     // floats per staged query quarter (32 + pad)
+constexpr int kCmbStride = 132;                  // floats per (warp, head) attention partial
+static_assert(16 * kQStride * 4 + kMegaConsumerWarps * 4 * kCmbStride * 4 <= kFragBytes,
+              "attention staging fits the fragment area");
 
 // ---- small PTX wrappers -----------------------------------------------------
 __device__ __forceinline__ unsigned smem_u32(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
@@ -482,170 +485,207 @@ __device__ __forceinline__ void consume_head(const Ring &r, const PhaseSpan &sp,
     if (bad) atomicOr(p.nonfinite, 1);
 }
 
-// Position ranges per KV head for `total` positions (8-position multiples).
-__device__ __forceinline__ void attention_plan(int total, int &splits, int &per)
+// Position ranges per KV head for `total` positions: at most 256 positions
+// per range, at most one range per CTA.
+__device__ __forceinline__ int attention_ranges(int total)
 {
-    splits = (total + 7) >> 3;
-    if (splits > kAttnMaxSplits) splits = kAttnMaxSplits;
-    per = (total + splits - 1) / splits;
-    per = (per + 7) & ~7;
-    splits = (total + per - 1) / per;
+    int r = (total + 255) / 256;
+    const int cap = min(kAttnMaxRanges, (int)gridDim.x / kKVHeads);
+    return r < 1 ? 1 : (r > cap ? cap : r);
 }
 
-// Attention of the step's query row. Work item = (KV head, position range):
-// one warp scores the range for the KV head's four query heads in sub-tiles of
-// 8 positions — lanes (position, dim quarter) for the scores, lanes = dims for
-// P.V, with all 16 K/V loads of a sub-tile in flight at once — and keeps an
-// online softmax per query head. With several ranges, each writes (m, l, o)
-// partials and the warp that finishes a KV head's last range merges them in
-// range order (a ticket counter per KV head, `tickets` before this layer).
-// Replaces scores + attend (src/metal_kernels.metal:81-132).
-__device__ __forceinline__ void mega_attention(const MegaParams &p, int layer, int length, unsigned tickets,
-                                               float *qs_all)
+// The attention unit (KV head, range) of this CTA, or -1: unit u runs on CTA
+// floor(u * gridDim / units), so units land on distinct CTAs spread over the grid.
+__device__ __forceinline__ int attention_unit(int units)
+{
+    const long long G = gridDim.x, b = blockIdx.x;
+    const int u = (int)((b * units + G - 1) / G);
+    return (u < units && (int)((long long)u * G / units) == (int)b) ? u : -1;
+}
+
+// K (lanes = position x dim quarter) and V (lanes = dims) of one 8-position
+// sub-tile into registers; positions past `end` read as zero.
+__device__ __forceinline__ void attention_load(const MegaParams &p, int layer, int kvh, int p0, int end, float4 (&kk)[8],
+                                               float4 (&vv)[8])
+{
+    const int lane = threadIdx.x & 31, pp = lane >> 2, qd = lane & 3;
+    const int n = min(8, end - p0);
+    const int page = p.page_table[p0 / kPage];
+    const float *kb = p.kv + kv_offset(layer, p.num_pages, page, 0, kvh, p0 % kPage);
+    const float *vb = p.kv + kv_offset(layer, p.num_pages, page, 1, kvh, p0 % kPage);
+    const float4 *krow = reinterpret_cast<const float4 *>(kb + pp * kHeadDim + qd * 32);
+#pragma unroll
+    for (int c = 0; c < 8; c++) kk[c] = pp < n ? __ldcg(krow + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int t = 0; t < 8; t++)
+        vv[t] = t < n ? __ldcg(reinterpret_cast<const float4 *>(vb + t * kHeadDim) + lane)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// One attention unit on the whole CTA: the four query heads of KV head kvh
+// over one position range. Each warp takes sub-tiles of 8 positions (its first
+// sub-tile's K/V loads are issued before the query rows are staged, so one
+// memory round trip precedes the arithmetic), scores them with lanes =
+// position x dim quarter, accumulates P.V with lanes = dims and keeps an online
+// softmax per query head; the warps' (m, l, o) are merged in warp order in
+// shared memory. With one range the result goes straight to attn; with several,
+// each range leaves (m, l, unnormalised o) in global memory and the CTA that
+// finishes a KV head's last range (ticket counter, `tickets` before this layer)
+// merges them in range order. Replaces scores + attend
+// (src/metal_kernels.metal:81-132).
+__device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, int length, int unit, int ranges,
+                                              unsigned tickets, float *qs, float *cmb, int *flag)
 {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, pp = lane >> 2, qd = lane & 3;
     const int total = length + 1;
-    int splits, per;
-    attention_plan(total, splits, per);
-    const int items = kKVHeads * splits;
-    float *qs = qs_all + warp * (16 * kQStride);
-    for (int item = warp * (int)gridDim.x + blockIdx.x; item < items; item += gridDim.x * kMegaConsumerWarps) {
-        const int kvh = item / splits, split = item - kvh * splits;
-        const int begin = split * per, end = min(begin + per, total);
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-            const int f4 = lane + 32 * u, hq = f4 >> 5, d4 = f4 & 31;
-            const float4 v = __ldcg(reinterpret_cast<const float4 *>(p.q + (size_t)(kvh * 4 + hq) * kHeadDim) + d4);
-            *reinterpret_cast<float4 *>(qs + (hq * 4 + (d4 >> 3)) * kQStride + (d4 & 7) * 4) = v;
-        }
-        __syncwarp();
-        float m_run[4], l_run[4];
-        float4 o[4];
-#pragma unroll
-        for (int hq = 0; hq < 4; hq++) {
-            m_run[hq] = -INFINITY;
-            l_run[hq] = 0.0f;
-            o[hq] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        for (int p0 = begin; p0 < end; p0 += 8) {
-            const int n = min(8, end - p0);
-            const int page = p.page_table[p0 / kPage];
-            const float *kb = p.kv + kv_offset(layer, p.num_pages, page, 0, kvh, p0 % kPage);
-            const float *vb = p.kv + kv_offset(layer, p.num_pages, page, 1, kvh, p0 % kPage);
-            const bool valid = pp < n;
-            float4 kk[8], vv[8];
-            const float4 *krow = reinterpret_cast<const float4 *>(kb + pp * kHeadDim + qd * 32);
-#pragma unroll
-            for (int c = 0; c < 8; c++) kk[c] = valid ? __ldcg(krow + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int t = 0; t < 8; t++)
-                vv[t] = t < n ? __ldcg(reinterpret_cast<const float4 *>(vb + t * kHeadDim) + lane)
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
-            float pr[4];
-#pragma unroll
-            for (int hq = 0; hq < 4; hq++) {
-                const float4 *qv = reinterpret_cast<const float4 *>(qs + (hq * 4 + qd) * kQStride);
-                float d = 0.0f;
-#pragma unroll
-                for (int c = 0; c < 8; c++) {
-                    const float4 q4 = qv[c];
-                    d = fmaf(q4.x, kk[c].x, d);
-                    d = fmaf(q4.y, kk[c].y, d);
-                    d = fmaf(q4.z, kk[c].z, d);
-                    d = fmaf(q4.w, kk[c].w, d);
-                }
-                d += __shfl_xor_sync(0xffffffffu, d, 1);
-                d += __shfl_xor_sync(0xffffffffu, d, 2);
-                const float s = valid ? d * kScoreScale : -INFINITY;
-                float tmax = s;
-                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
-                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
-                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
-                const float m_new = fmaxf(m_run[hq], tmax);
-                const float corr = m_run[hq] == -INFINITY ? 0.0f : expf(m_run[hq] - m_new);
-                pr[hq] = valid ? expf(s - m_new) : 0.0f;
-                float ps = pr[hq];
-                ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-                ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-                ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-                l_run[hq] = l_run[hq] * corr + ps;
-                m_run[hq] = m_new;
-                o[hq].x *= corr;
-                o[hq].y *= corr;
-                o[hq].z *= corr;
-                o[hq].w *= corr;
-            }
-#pragma unroll
-            for (int t = 0; t < 8; t++) {
-#pragma unroll
-                for (int hq = 0; hq < 4; hq++) {
-                    const float pt = __shfl_sync(0xffffffffu, pr[hq], t * 4);
-                    o[hq].x = fmaf(pt, vv[t].x, o[hq].x);
-                    o[hq].y = fmaf(pt, vv[t].y, o[hq].y);
-                    o[hq].z = fmaf(pt, vv[t].z, o[hq].z);
-                    o[hq].w = fmaf(pt, vv[t].w, o[hq].w);
-                }
-            }
-        }
-        if (splits == 1) {
-#pragma unroll
-            for (int hq = 0; hq < 4; hq++) {
-                const float inv = 1.0f / l_run[hq];
-                reinterpret_cast<float4 *>(p.attn + (size_t)(kvh * 4 + hq) * kHeadDim)[lane] =
-                    make_float4(o[hq].x * inv, o[hq].y * inv, o[hq].z * inv, o[hq].w * inv);
-            }
-            __syncwarp();
-            continue;
-        }
-        const size_t base = (size_t)(kvh * splits + split) * 4;
-#pragma unroll
-        for (int hq = 0; hq < 4; hq++) {
-            reinterpret_cast<float4 *>(p.part_acc + (base + hq) * kHeadDim)[lane] = o[hq];
-            if (lane == 0) {
-                p.part_ml[(base + hq) * 2] = m_run[hq];
-                p.part_ml[(base + hq) * 2 + 1] = l_run[hq];
-            }
-        }
-        __syncwarp();
-        unsigned ticket = 0;
-        if (lane == 0) {
-            __threadfence();
-            ticket = atomicAdd(sync_word(p, kSyncTicket + kvh), 1u);
-        }
-        ticket = __shfl_sync(0xffffffffu, ticket, 0);
-        if (ticket == tickets + (unsigned)(splits - 1)) {
-            // last range of this KV head: merge every range in order
-            __threadfence();
-#pragma unroll 1
-            for (int hq = 0; hq < 4; hq++) {
-                float ms = -INFINITY, ls = 0.0f;
-                if (lane < splits) {
-                    const size_t at = ((size_t)(kvh * splits + lane) * 4 + hq) * 2;
-                    ms = __ldcg(&p.part_ml[at]);
-                    ls = __ldcg(&p.part_ml[at + 1]);
-                }
-                const float M = warp_max(ls > 0.0f ? ms : -INFINITY);
-                const float w = ls > 0.0f ? expf(ms - M) : 0.0f;
-                const float L = warp_sum(w * ls);
-                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-                for (int s2 = 0; s2 < splits; s2++) {
-                    const float ws = __shfl_sync(0xffffffffu, w, s2);
-                    const float4 v = __ldcg(
-                        reinterpret_cast<const float4 *>(p.part_acc + ((size_t)(kvh * splits + s2) * 4 + hq) * kHeadDim) +
-                        lane);
-                    acc.x = fmaf(ws, v.x, acc.x);
-                    acc.y = fmaf(ws, v.y, acc.y);
-                    acc.z = fmaf(ws, v.z, acc.z);
-                    acc.w = fmaf(ws, v.w, acc.w);
-                }
-                const float inv = 1.0f / L;
-                reinterpret_cast<float4 *>(p.attn + (size_t)(kvh * 4 + hq) * kHeadDim)[lane] =
-                    make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-            }
-        }
-        __syncwarp();
+    const int kvh = unit / ranges, range = unit - kvh * ranges;
+    int per = (total + ranges - 1) / ranges;
+    per = (per + 7) & ~7;
+    const int begin = range * per, end = min(begin + per, total);
+    int p0 = begin + 8 * warp;
+    float4 kk[8], vv[8];
+    if (p0 < end) attention_load(p, layer, kvh, p0, end, kk, vv);
+    if (threadIdx.x < 128) {
+        const int hq = threadIdx.x >> 5, d4 = threadIdx.x & 31;
+        const float4 v = __ldcg(reinterpret_cast<const float4 *>(p.q + (size_t)(kvh * 4 + hq) * kHeadDim) + d4);
+        *reinterpret_cast<float4 *>(qs + (hq * 4 + (d4 >> 3)) * kQStride + (d4 & 7) * 4) = v;
     }
+    consumers_sync();
+    float m_run[4], l_run[4];
+    float4 o[4];
+#pragma unroll
+    for (int hq = 0; hq < 4; hq++) {
+        m_run[hq] = -INFINITY;
+        l_run[hq] = 0.0f;
+        o[hq] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    for (; p0 < end; p0 += 8 * kMegaConsumerWarps) {
+        if (p0 != begin + 8 * warp) attention_load(p, layer, kvh, p0, end, kk, vv);
+        const bool valid = pp < min(8, end - p0);
+        float pr[4];
+#pragma unroll
+        for (int hq = 0; hq < 4; hq++) {
+            const float4 *qv = reinterpret_cast<const float4 *>(qs + (hq * 4 + qd) * kQStride);
+            float d = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                const float4 q4 = qv[c];
+                d = fmaf(q4.x, kk[c].x, d);
+                d = fmaf(q4.y, kk[c].y, d);
+                d = fmaf(q4.z, kk[c].z, d);
+                d = fmaf(q4.w, kk[c].w, d);
+            }
+            d += __shfl_xor_sync(0xffffffffu, d, 1);
+            d += __shfl_xor_sync(0xffffffffu, d, 2);
+            const float s = valid ? d * kScoreScale : -INFINITY;
+            float tmax = s;
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
+            const float m_new = fmaxf(m_run[hq], tmax);
+            const float corr = m_run[hq] == -INFINITY ? 0.0f : expf(m_run[hq] - m_new);
+            pr[hq] = valid ? expf(s - m_new) : 0.0f;
+            float ps = pr[hq];
+            ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+            l_run[hq] = l_run[hq] * corr + ps;
+            m_run[hq] = m_new;
+            o[hq].x *= corr;
+            o[hq].y *= corr;
+            o[hq].z *= corr;
+            o[hq].w *= corr;
+        }
+#pragma unroll
+        for (int t = 0; t < 8; t++) {
+#pragma unroll
+            for (int hq = 0; hq < 4; hq++) {
+                const float pt = __shfl_sync(0xffffffffu, pr[hq], t * 4);
+                o[hq].x = fmaf(pt, vv[t].x, o[hq].x);
+                o[hq].y = fmaf(pt, vv[t].y, o[hq].y);
+                o[hq].z = fmaf(pt, vv[t].z, o[hq].z);
+                o[hq].w = fmaf(pt, vv[t].w, o[hq].w);
+            }
+        }
+    }
+    // the warps' partials -> shared memory: [warp][head] o[128], m, l
+#pragma unroll
+    for (int hq = 0; hq < 4; hq++) {
+        float *slot = cmb + (warp * 4 + hq) * kCmbStride;
+        reinterpret_cast<float4 *>(slot)[lane] = o[hq];
+        if (lane == 0) {
+            slot[128] = m_run[hq];
+            slot[129] = l_run[hq];
+        }
+    }
+    consumers_sync();
+    if (warp < 4) {
+        const int hq = warp;
+        float M = -INFINITY;
+        for (int w = 0; w < kMegaConsumerWarps; w++) {
+            const float *slot = cmb + (w * 4 + hq) * kCmbStride;
+            if (slot[129] > 0.0f) M = fmaxf(M, slot[128]);
+        }
+        float L = 0.0f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int w = 0; w < kMegaConsumerWarps; w++) {
+            const float *slot = cmb + (w * 4 + hq) * kCmbStride;
+            if (!(slot[129] > 0.0f)) continue;
+            const float wt = expf(slot[128] - M);
+            const float4 v = reinterpret_cast<const float4 *>(slot)[lane];
+            L = fmaf(wt, slot[129], L);
+            acc.x = fmaf(wt, v.x, acc.x);
+            acc.y = fmaf(wt, v.y, acc.y);
+            acc.z = fmaf(wt, v.z, acc.z);
+            acc.w = fmaf(wt, v.w, acc.w);
+        }
+        if (ranges == 1) {
+            const float inv = 1.0f / L;
+            reinterpret_cast<float4 *>(p.attn + (size_t)(kvh * 4 + hq) * kHeadDim)[lane] =
+                make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        } else {
+            const size_t at = (size_t)(kvh * ranges + range) * 4 + hq;
+            reinterpret_cast<float4 *>(p.part_acc + at * kHeadDim)[lane] = acc;
+            if (lane == 0) {
+                p.part_ml[at * 2] = M;
+                p.part_ml[at * 2 + 1] = L;
+            }
+        }
+    }
+    if (ranges == 1) return;
+    consumers_sync();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned old = atomicAdd(sync_word(p, kSyncTicket + kvh), 1u);
+        *flag = old == tickets + (unsigned)ranges - 1;
+        __threadfence();
+    }
+    consumers_sync();
+    if (!*flag || warp >= 4) return;
+    // last range of this KV head: merge all ranges in order
+    const int hq = warp;
+    float ms = -INFINITY, ls = 0.0f;
+    if (lane < ranges) {
+        const size_t at = ((size_t)(kvh * ranges + lane) * 4 + hq) * 2;
+        ms = __ldcg(&p.part_ml[at]);
+        ls = __ldcg(&p.part_ml[at + 1]);
+    }
+    const float M = warp_max(ls > 0.0f ? ms : -INFINITY);
+    const float w = ls > 0.0f ? expf(ms - M) : 0.0f;
+    const float L = warp_sum(w * ls);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s2 = 0; s2 < ranges; s2++) {
+        const float ws = __shfl_sync(0xffffffffu, w, s2);
+        const float4 v = __ldcg(
+            reinterpret_cast<const float4 *>(p.part_acc + ((size_t)(kvh * ranges + s2) * 4 + hq) * kHeadDim) + lane);
+        acc.x = fmaf(ws, v.x, acc.x);
+        acc.y = fmaf(ws, v.y, acc.y);
+        acc.z = fmaf(ws, v.z, acc.z);
+        acc.w = fmaf(ws, v.w, acc.w);
+    }
+    const float inv = 1.0f / L;
+    reinterpret_cast<float4 *>(p.attn + (size_t)(kvh * 4 + hq) * kHeadDim)[lane] =
+        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
 }
 
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams p)
@@ -654,7 +694,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
     __shared__ float red[32];
     __shared__ float best_v[kMegaConsumerWarps];
     __shared__ int best_i[kMegaConsumerWarps];
-    __shared__ int last_cta;
+    __shared__ int last_cta, flag;
     __shared__ float rope_s[2 * kHeadDim];       // cos | sin of the step's position
     __shared__ float res_s[kMegaMaxTiles * 16];  // residual rows of this CTA's tiles
     Ring ring;
@@ -690,8 +730,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
         for (int i = threadIdx.x; i < 2 * kHeadDim; i += kMegaConsumers)
             rope_s[i] = i < kHeadDim ? p.rope_cos[(size_t)length * kHeadDim + i]
                                      : p.rope_sin[(size_t)length * kHeadDim + i - kHeadDim];
-        int splits, per;
-        attention_plan(length + 1, splits, per);
+        const int ranges = attention_ranges(length + 1);
+        const int unit = attention_unit(kKVHeads * ranges);
         for (int layer = 0; layer < kLayers; layer++) {
             const float *sc = p.scales + layer * 7;
             GemvParams gp;
@@ -722,8 +762,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
             consumers_sync();
             fp8_epilogue<kEpiQKV>(gp, sp, kHidden / kBlockCols / item_blocks(kPhQKV), partial, inv);
             grid_sync(p, ++barrier, rec);
-            mega_attention(p, layer, length, tickets, reinterpret_cast<float *>(frag));
-            if (splits > 1) tickets += (unsigned)splits;
+            if (unit >= 0) {
+                float *qs = reinterpret_cast<float *>(frag);
+                cta_attention(p, layer, length, unit, ranges, tickets, qs, qs + 16 * kQStride, &flag);
+            }
+            if (ranges > 1) tickets += (unsigned)ranges;
             grid_sync(p, ++barrier, rec);
             // o + residual (x)
             sp = phase_span(p, layer, kPhO);
