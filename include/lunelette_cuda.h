@@ -121,10 +121,13 @@ int lunelette_cuda_decode_loop(lunelette_metal *context, int64_t first_token, si
 
 /* Phase timing of the persistent decode kernel: while enabled, the first step of
  * each launch records %globaltimer (ns) at its start (entry 0) and as CTA 0
- * leaves each of its 131 grid barriers (entry 1 + k: 26 layers x {qkv,
- * attention, o, gate/up, down}, then head + greedy pick); CTA b's arrival at
- * barrier k is entry 132 + k * ctas + b, ctas = the device's SM count. Copy up to
- * 132 + 131 * ctas entries. */
+ * leaves each of its 79 grid barriers (entry 1 + k; per layer one after the o
+ * projection, one after gate/up and one after down, then one after the greedy
+ * pick). From entry 80, CTA b's marks m at 80 + m * ctas + b (ctas = the
+ * device's SM count): per layer L, mark 5L when it published its q/k/v tiles,
+ * 5L + 1 when it published an attention result (CTAs that own one, else 0),
+ * 5L + 2..4 its arrivals at the o, gate/up and down barriers; mark 130 its
+ * arrival at the last barrier. Copy up to 80 + 131 * ctas entries. */
 int lunelette_cuda_timeline(lunelette_metal *context, int enable);
 int lunelette_cuda_timeline_copy(lunelette_metal *context, unsigned long long *out, size_t entries);
 

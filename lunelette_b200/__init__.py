@@ -236,7 +236,7 @@ class Runtime:
         if library().lunelette_cuda_timeline(self.handle, 1 if enable else 0):
             raise LuneletteError("timeline enable failed")
 
-    def timeline_copy(self, entries=132):
+    def timeline_copy(self, entries=80):
         out = np.zeros(entries, dtype=np.uint64)
         if library().lunelette_cuda_timeline_copy(self.handle, out.ctypes.data, entries):
             raise LuneletteError("timeline copy failed")

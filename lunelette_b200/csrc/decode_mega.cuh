@@ -19,8 +19,10 @@
 // Item i of the CTA's stream goes to consumer warp i mod 7, which owns
 // kSlotsPerWarp private slots and takes its items strictly in order, so every
 // slot's full and empty barriers are waited on in phase order by one waiter.
-// Phases per layer: qkv (norm + q/k/v + RoPE + KV store), attention (one CTA
-// per KV head and position range), o (+ residual), gate/up
+// Phases per layer: qkv (norm + q/k/v + RoPE + KV store; each CTA then counts
+// its tiles into their KV-head groups), attention (one CTA per KV head and
+// position range, started by its group's count), o (+ residual; starts once the
+// eight attention results are counted, ends at a grid barrier), gate/up
 // (norm + SwiGLU), down (+ residual); then the head (final norm + tied BF16
 // GEMV) with a per-CTA argmax whose last CTA picks the token.
 //
@@ -251,13 +253,26 @@ __device__ __forceinline__ void thread_wait(const unsigned *word, unsigned targe
     }
 }
 
+__device__ __forceinline__ void record_mark(const MegaParams &p, bool rec, int mark)
+{
+    if (rec) p.timeline[kMegaTimelineHead + (size_t)mark * gridDim.x + blockIdx.x] = globaltimer_ns();
+}
+
+// Publish the CTA's global writes (callers synchronise the consumers first),
+// then add n to *word (release). One thread.
+__device__ __forceinline__ void signal_word(unsigned *word, unsigned n)
+{
+    __threadfence();
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(word), "r"(n) : "memory");
+}
+
 // Grid barrier `target` (1, 2, ...) of this launch among all CTAs' consumers;
-// with rec, this CTA's arrival and CTA 0's exit go to the timeline.
-__device__ __forceinline__ void grid_sync(const MegaParams &p, unsigned target, bool rec)
+// with rec, this CTA's arrival goes to `mark` and CTA 0's exit to entry target.
+__device__ __forceinline__ void grid_sync(const MegaParams &p, unsigned target, bool rec, int mark)
 {
     consumers_sync();
     if (threadIdx.x == 0) {
-        if (rec) p.timeline[kMegaTimelineHead + (size_t)(target - 1) * gridDim.x + blockIdx.x] = globaltimer_ns();
+        record_mark(p, rec, mark);
         __threadfence();
         if (!*(volatile int *)p.error) {
             // barrier k is passed once the arrival count reaches k * gridDim.x
@@ -272,6 +287,9 @@ __device__ __forceinline__ void grid_sync(const MegaParams &p, unsigned target, 
 }
 
 // ---- consumer helpers -------------------------------------------------------
+// KV-head group of a q|k|v tile: q tiles 0-255 (8 per query head), k 256-319, v 320-383.
+__device__ __forceinline__ int qkv_group(int tile) { return tile < 256 ? tile >> 5 : ((tile - 256) & 63) >> 3; }
+
 __device__ __forceinline__ float consumers_sum(float v, float *red)
 {
     v = warp_sum(v);
@@ -522,6 +540,37 @@ __device__ __forceinline__ void attention_load(const MegaParams &p, int layer, i
                       : make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
+// Merge the ranges of KV head kvh in range order (warps 0-3, one query head each).
+__device__ __forceinline__ void merge_ranges(const MegaParams &p, int kvh, int ranges)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp >= 4) return;
+    // last range of this KV head: merge all ranges in order
+    const int hq = warp;
+    float ms = -INFINITY, ls = 0.0f;
+    if (lane < ranges) {
+        const size_t at = ((size_t)(kvh * ranges + lane) * 4 + hq) * 2;
+        ms = __ldcg(&p.part_ml[at]);
+        ls = __ldcg(&p.part_ml[at + 1]);
+    }
+    const float M = warp_max(ls > 0.0f ? ms : -INFINITY);
+    const float w = ls > 0.0f ? expf(ms - M) : 0.0f;
+    const float L = warp_sum(w * ls);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s2 = 0; s2 < ranges; s2++) {
+        const float ws = __shfl_sync(0xffffffffu, w, s2);
+        const float4 v = __ldcg(
+            reinterpret_cast<const float4 *>(p.part_acc + ((size_t)(kvh * ranges + s2) * 4 + hq) * kHeadDim) + lane);
+        acc.x = fmaf(ws, v.x, acc.x);
+        acc.y = fmaf(ws, v.y, acc.y);
+        acc.z = fmaf(ws, v.z, acc.z);
+        acc.w = fmaf(ws, v.w, acc.w);
+    }
+    const float inv = 1.0f / L;
+    reinterpret_cast<float4 *>(p.attn + (size_t)(kvh * 4 + hq) * kHeadDim)[lane] =
+        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+}
+
 // One attention unit on the whole CTA: the four query heads of KV head kvh
 // over one position range. Each warp takes sub-tiles of 8 positions (its first
 // sub-tile's K/V loads are issued before the query rows are staged, so one
@@ -534,7 +583,8 @@ __device__ __forceinline__ void attention_load(const MegaParams &p, int layer, i
 // merges them in range order. Replaces scores + attend
 // (src/metal_kernels.metal:81-132).
 __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, int length, int unit, int ranges,
-                                              unsigned tickets, float *qs, float *cmb, int *flag)
+                                              unsigned epoch, unsigned tickets, float *qs, float *cmb, int *flag,
+                                              bool rec)
 {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, pp = lane >> 2, qd = lane & 3;
     const int total = length + 1;
@@ -542,6 +592,9 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
     int per = (total + ranges - 1) / ranges;
     per = (per + 7) & ~7;
     const int begin = range * per, end = min(begin + per, total);
+    // q/k/v of this KV head's group (its 48 tiles) stored by the qkv phase
+    if (threadIdx.x == 0) thread_wait(sync_word(p, kSyncQKV + kvh), 48u * epoch, p.error);
+    consumers_sync();
     int p0 = begin + 8 * warp;
     float4 kk[8], vv[8];
     if (p0 < end) attention_load(p, layer, kvh, p0, end, kk, vv);
@@ -652,8 +705,14 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
             }
         }
     }
-    if (ranges == 1) return;
     consumers_sync();
+    if (ranges == 1) {
+        if (threadIdx.x == 0) {
+            signal_word(sync_word(p, kSyncAttn), 1);
+            record_mark(p, rec, layer * 5 + 1);
+        }
+        return;
+    }
     if (threadIdx.x == 0) {
         __threadfence();
         const unsigned old = atomicAdd(sync_word(p, kSyncTicket + kvh), 1u);
@@ -661,31 +720,13 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
         __threadfence();
     }
     consumers_sync();
-    if (!*flag || warp >= 4) return;
-    // last range of this KV head: merge all ranges in order
-    const int hq = warp;
-    float ms = -INFINITY, ls = 0.0f;
-    if (lane < ranges) {
-        const size_t at = ((size_t)(kvh * ranges + lane) * 4 + hq) * 2;
-        ms = __ldcg(&p.part_ml[at]);
-        ls = __ldcg(&p.part_ml[at + 1]);
+    if (!*flag) return;
+    merge_ranges(p, kvh, ranges);
+    consumers_sync();
+    if (threadIdx.x == 0) {
+        signal_word(sync_word(p, kSyncAttn), 1);
+        record_mark(p, rec, layer * 5 + 1);
     }
-    const float M = warp_max(ls > 0.0f ? ms : -INFINITY);
-    const float w = ls > 0.0f ? expf(ms - M) : 0.0f;
-    const float L = warp_sum(w * ls);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s2 = 0; s2 < ranges; s2++) {
-        const float ws = __shfl_sync(0xffffffffu, w, s2);
-        const float4 v = __ldcg(
-            reinterpret_cast<const float4 *>(p.part_acc + ((size_t)(kvh * ranges + s2) * 4 + hq) * kHeadDim) + lane);
-        acc.x = fmaf(ws, v.x, acc.x);
-        acc.y = fmaf(ws, v.y, acc.y);
-        acc.z = fmaf(ws, v.z, acc.z);
-        acc.w = fmaf(ws, v.w, acc.w);
-    }
-    const float inv = 1.0f / L;
-    reinterpret_cast<float4 *>(p.attn + (size_t)(kvh * 4 + hq) * kHeadDim)[lane] =
-        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
 }
 
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams p)
@@ -733,6 +774,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
         const int ranges = attention_ranges(length + 1);
         const int unit = attention_unit(kKVHeads * ranges);
         for (int layer = 0; layer < kLayers; layer++) {
+            const unsigned epoch = (unsigned)(s * kLayers + layer) + 1;  // layers run by the launch, this one included
             const float *sc = p.scales + layer * 7;
             GemvParams gp;
             memset(&gp, 0, sizeof gp);
@@ -761,13 +803,24 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
             seq += sp.items;
             consumers_sync();
             fp8_epilogue<kEpiQKV>(gp, sp, kHidden / kBlockCols / item_blocks(kPhQKV), partial, inv);
-            grid_sync(p, ++barrier, rec);
+            consumers_sync();
+            if (threadIdx.x == 0) {
+                // publish this CTA's tiles to their KV-head groups (runs of equal group)
+                const int t1 = sp.first + sp.items / (kHidden / kBlockCols / item_blocks(kPhQKV));
+                for (int t = sp.first; t < t1;) {
+                    const int g = qkv_group(t);
+                    int n = 0;
+                    for (; t < t1 && qkv_group(t) == g; t++) n++;
+                    signal_word(sync_word(p, kSyncQKV + g), (unsigned)n);
+                }
+                record_mark(p, rec, layer * 5);
+            }
             if (unit >= 0) {
                 float *qs = reinterpret_cast<float *>(frag);
-                cta_attention(p, layer, length, unit, ranges, tickets, qs, qs + 16 * kQStride, &flag);
+                cta_attention(p, layer, length, unit, ranges, epoch, tickets, qs, qs + 16 * kQStride, &flag, rec);
+                consumers_sync();
             }
             if (ranges > 1) tickets += (unsigned)ranges;
-            grid_sync(p, ++barrier, rec);
             // o + residual (x)
             sp = phase_span(p, layer, kPhO);
             gp.rows = kHidden;
@@ -779,12 +832,15 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
             gp.y = p.h;
             gp.y_stride = kHidden;
             stage_rows(res_s, p.x, gp.res_base, sp.items / (kQuery / kBlockCols / item_blocks(kPhO)) * kTileRows);
+            // every KV head's attention output stored
+            if (threadIdx.x == 0) thread_wait(sync_word(p, kSyncAttn), (unsigned)kKVHeads * epoch, p.error);
+            consumers_sync();
             inv = stage_frag<kQuery>(frag, p.attn, nullptr, nullptr, red);
             consume_fp8<item_blocks(kPhO), kQuery / kBlockCols>(ring, sp, seq, taken, frag4, partial, p.error);
             seq += sp.items;
             consumers_sync();
             fp8_epilogue<kEpiResidual>(gp, sp, kQuery / kBlockCols / item_blocks(kPhO), partial, inv);
-            grid_sync(p, ++barrier, rec);
+            grid_sync(p, ++barrier, rec, layer * 5 + 2);
             // post norm + gate/up + SwiGLU
             sp = phase_span(p, layer, kPhGateUp);
             gp.rows = kGateUpRows;
@@ -798,7 +854,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
             seq += sp.items;
             consumers_sync();
             fp8_epilogue<kEpiSwiGLU>(gp, sp, kHidden / kBlockCols / item_blocks(kPhGateUp), partial, inv);
-            grid_sync(p, ++barrier, rec);
+            grid_sync(p, ++barrier, rec, layer * 5 + 3);
             // down + residual (h)
             sp = phase_span(p, layer, kPhDown);
             gp.rows = kHidden;
@@ -813,7 +869,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
             seq += sp.items;
             consumers_sync();
             fp8_epilogue<kEpiResidual>(gp, sp, kInner / kBlockCols / item_blocks(kPhDown), partial, inv);
-            grid_sync(p, ++barrier, rec);
+            grid_sync(p, ++barrier, rec, layer * 5 + 4);
         }
         // final norm + tied head, 8-column staging
         {
@@ -872,7 +928,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
                 p.step->length = length + 1;
             }
         }
-        grid_sync(p, ++barrier, rec);
+        grid_sync(p, ++barrier, rec, kLayers * 5);
     }
 }
 

@@ -739,10 +739,10 @@ bad:
     return fail(error, capacity, what, e);
 }
 
-// CTA 0's barrier exits, then every CTA's barrier arrivals (mega_params.cuh)
+// CTA 0's barrier exits, then every CTA's marks (mega_params.cuh)
 static size_t timeline_entries(const lun_device *d)
 {
-    return (size_t)kMegaTimelineHead + (size_t)kMegaBarriersPerStep * d->sm_count;
+    return (size_t)kMegaTimelineHead + (size_t)kMegaMarksPerStep * d->sm_count;
 }
 
 extern "C" int lun_device_timeline(lun_device *d, int enable)

@@ -5,22 +5,32 @@
 
 namespace lun {
 
-// grid barriers per decode step: 5 per layer, one after the head and the pick
-constexpr int kMegaBarriersPerStep = kLayers * 5 + 1;
+// Grid barriers per decode step: three per layer (after o, once h is whole;
+// after gate/up; after down, once x is whole) and one after the head and the
+// pick. qkv -> attention -> o use counters instead (kSyncQKV, kSyncAttn).
+constexpr int kMegaBarriersPerStep = kLayers * 3 + 1;
 // Timeline of the first step of a launch: [0] start, [1 + k] CTA 0 leaving
-// barrier k (k = 0..130), then from kMegaTimelineHead every CTA b's arrival at
-// barrier k in entry kMegaTimelineHead + k * gridDim.x + b.
+// barrier k, then from kMegaTimelineHead one entry per CTA b for each mark m at
+// kMegaTimelineHead + m * gridDim.x + b. Marks per layer L: 5L qkv results
+// published, 5L + 1 attention published (CTAs that own a unit, else 0),
+// 5L + 2..4 arrival at the o, gate/up and down barriers; mark 5 * 26 the
+// arrival at the barrier after the pick.
+constexpr int kMegaMarksPerStep = kLayers * 5 + 1;
 constexpr int kMegaTimelineHead = 1 + kMegaBarriersPerStep;
 
 // Synchronisation words of one launch, each on its own 128-byte line, zero at
-// launch and only ever increased:
+// launch and only ever increased (targets grow with the layers the launch ran):
 //   kSyncBarrier        grid barrier arrivals (gridDim per barrier)
+//   kSyncQKV + kvh      q/k/v tiles of KV head kvh's group stored (48 per layer)
+//   kSyncAttn           KV heads whose attention output is stored (8 per layer)
 //   kSyncTicket + kvh   attention ranges of KV head kvh finished
 //   kSyncPick           CTAs done with the head (gridDim per step)
 constexpr int kSyncStride = 32;
 enum : int {
     kSyncBarrier = 0,
-    kSyncTicket = 1,
+    kSyncQKV = 1,
+    kSyncAttn = kSyncQKV + kKVHeads,
+    kSyncTicket = kSyncAttn + 1,
     kSyncPick = kSyncTicket + kKVHeads,
     kSyncWords = kSyncPick + 1,
 };

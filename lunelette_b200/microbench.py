@@ -91,44 +91,59 @@ def run(shapes, ms_list, iters, warmup=3):
     return rows_out
 
 
-PHASES = ["qkv", "attention", "o", "gate_up", "down"]
-PHASE_BYTES = {"qkv": 6144 * 3072, "attention": 0, "o": 3072 * 4096, "gate_up": 18432 * 3072,
-               "down": 3072 * 9216}
+PHASE_BYTES = {"qkv": 6144 * 3072, "attn_o": (6144 + 4096) * 3072, "gate_up": 18432 * 3072, "down": 3072 * 9216,
+               "head": 131072 * 3072 * 2}
 
 
 def decode_phases(checkpoint, steps=8, prompt=32):
-    """Per-phase durations of the persistent decode kernel (single-token steps
-    through lunelette_metal_decode), from its %globaltimer timeline: the mean over
-    `steps` steps and 26 layers of each phase, plus `head` (head GEMV and greedy
-    pick). Each phase runs from one grid barrier to the next. Per phase also
-    `<phase>_spread`, first to last CTA reaching the barrier that closes it, and
-    `<phase>_release`, the last arrival to CTA 0 leaving that barrier."""
+    """Phase durations of the persistent decode kernel (single-token steps through
+    lunelette_metal_decode), from its %globaltimer timeline, as means over `steps`
+    steps and 26 layers, each measured from the barrier that opens the layer
+    (or from the previous phase's barrier): `qkv` until the last CTA published its
+    q/k/v tiles, `attention` until the last attention result was published,
+    `attn_o` until CTA 0 left the barrier after the o projection, `gate_up` and
+    `down` barrier to barrier, and `head` (head GEMV and greedy pick). For each
+    barrier phase also `<phase>_spread`, first to last CTA arriving, and
+    `<phase>_release`, the last arrival to CTA 0 leaving the barrier."""
     import torch
     import lunelette_b200 as L
     peak, kind = hbm_peak()
     ctas = torch.cuda.get_device_properties(0).multi_processor_count
-    names = PHASES + ["head"]
-    rows = {n: [] for n in names + [m + "_spread" for m in names] + [m + "_release" for m in names] + ["step"]}
+    barriers, marks = 79, 131
+    closing = ["attn_o", "gate_up", "down"]
+    names = ["qkv", "attention"] + closing + ["head"]
+    rows = {n: [] for n in names + [m + "_spread" for m in closing + ["head"]] +
+            [m + "_release" for m in closing + ["head"]] + ["step"]}
     with L.Runtime(checkpoint) as rt:
         ids = np.random.default_rng(7).integers(1000, 131072, prompt)
         tok = int(np.argmax(rt.prefill(ids)))
         rt.timeline(True)
         for _ in range(steps):
             tok = int(np.argmax(rt.decode(tok)))
-            full = rt.timeline_copy(132 + 131 * ctas).astype(np.float64) / 1000.0  # us
-            t = full[:132]
-            arrive = full[132:].reshape(131, ctas)
-            for k in range(131):
-                name = names[k % 5] if k < 130 else "head"
-                rows[name].append(t[k + 1] - t[k])
-                rows[name + "_spread"].append(arrive[k].max() - arrive[k].min())
-                rows[name + "_release"].append(t[k + 1] - arrive[k].max())
-            rows["step"].append(t[131] - t[0])
+            full = rt.timeline_copy(1 + barriers + marks * ctas).astype(np.float64) / 1000.0  # us
+            start, exits = full[0], full[1:1 + barriers]
+            mark = full[1 + barriers:].reshape(marks, ctas)
+
+            def closed(name, prev, b, arrivals):
+                rows[name].append(exits[b] - prev)
+                rows[name + "_spread"].append(arrivals.max() - arrivals.min())
+                rows[name + "_release"].append(exits[b] - arrivals.max())
+
+            opened = start
+            for layer in range(26):
+                rows["qkv"].append(mark[5 * layer].max() - opened)
+                published = mark[5 * layer + 1][mark[5 * layer + 1] > 0]
+                rows["attention"].append(published.max() - opened)
+                for k, name in enumerate(closing):
+                    closed(name, opened if k == 0 else exits[3 * layer + k - 1], 3 * layer + k, mark[5 * layer + 2 + k])
+                opened = exits[3 * layer + 2]
+            closed("head", opened, 78, mark[130])
+            rows["step"].append(exits[78] - start)
         rt.timeline(False)
     out = []
     for name, vals in rows.items():
         us = float(np.mean(vals))
-        nbytes = PHASE_BYTES.get(name, 131072 * 3072 * 2 if name == "head" else 0)
+        nbytes = PHASE_BYTES.get(name, 0)
         rec = {"phase": name, "mean_us": us, "min_us": float(np.min(vals)), "max_us": float(np.max(vals))}
         if nbytes:
             rec["weight_bytes"] = nbytes
