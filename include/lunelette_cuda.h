@@ -29,9 +29,9 @@ int lunelette_cuda_fp8_decode(const uint8_t *codes, size_t n, float scale, float
     void *stream);
 
 /* Row-major E4M3 codes [rows][cols] (cols % 16 == 0) -> the tiled layout that
- * the GEMV entry points below read: 16-row tiles of 1 KB blocks (16 rows x 64
- * columns) in tensor-core fragment order, rows padded to 16 and columns to 64
- * with zeros; dst holds ceil(rows/16)*16 * ceil(cols/64)*64 bytes. order 0 keeps
+ * the GEMV entry points below read: 8-row tiles of 1 KB blocks (8 rows x 128
+ * columns) in tensor-core fragment order, rows padded to 8 and columns to 128
+ * with zeros; dst holds ceil(rows/8)*8 * ceil(cols/128)*128 bytes. order 0 keeps
  * the row order; 1 takes q|k|v rows (rows % 128 == 0) and stores the RoPE pair
  * rows (j, j + 64) of each 128-row head adjacently (2j, 2j + 1); 2 takes the gate
  * rows followed by the up rows (rows even) and interleaves them (gate f at 2f,

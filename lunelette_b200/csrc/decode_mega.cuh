@@ -11,9 +11,9 @@
 //     keeps a short stretch of the stream (p.l2_ahead bytes) prefetched into L2.
 //   consumers (warps 0-6): per phase, wait at a grid barrier for the previous
 //     phase's activations, stage the activation row as FP16 hi/lo MMA fragments
-//     (and the epilogue's residual rows), then take items (16 rows x 512 or 768
-//     columns of the tiled layout of gemv.cuh), run the tensor-core dot
-//     products, leave 16 partial row sums per item in shared memory, and
+//     (and the epilogue's residual rows), then take items (8 rows x 1024 or
+//     1536 columns of the tiled layout of gemv.cuh), run the tensor-core dot
+//     products, leave 8 partial row sums per item in shared memory, and
 //     finally add each tile's partials in a fixed order and run the fused
 //     epilogue. Attention and the greedy pick run on consumers only.
 // Item i of the CTA's stream goes to consumer warp i mod 7, which owns
@@ -41,7 +41,7 @@ constexpr int kMegaThreads = kMegaConsumers + 32;
 constexpr int kSlotsPerWarp = 2;
 constexpr int kRingSlots = kMegaConsumerWarps * kSlotsPerWarp;
 constexpr int kSlotBytes = 12288;
-constexpr int kFragBytes = (kInner / kBlockCols) * 256;  // hi/lo fragments of a 9216-column row
+constexpr int kFragBytes = (kInner / 64) * 256;          // hi/lo fragments of a 9216-column row
 constexpr int kMegaMaxItems = 48;                         // FP8 items of one phase per CTA
 constexpr int kMegaMaxTiles = 16;                         // tiles of one phase per CTA
 constexpr int kMegaSmemBytes =
@@ -127,7 +127,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, int *e
 enum { kPhQKV, kPhO, kPhGateUp, kPhDown, kPhHead };
 
 // This CTA's share of one phase: `items` consecutive items of `item_bytes`
-// starting at src. FP8 phases: whole 16-row tiles from tile `first`, each
+// starting at src. FP8 phases: whole 8-row tiles from tile `first`, each
 // split into K-chunks; head: 2-row items of the BF16 embedding from row `first`.
 struct PhaseSpan {
     const uint8_t *src;
@@ -287,8 +287,9 @@ __device__ __forceinline__ void grid_sync(const MegaParams &p, unsigned target, 
 }
 
 // ---- consumer helpers -------------------------------------------------------
-// KV-head group of a q|k|v tile: q tiles 0-255 (8 per query head), k 256-319, v 320-383.
-__device__ __forceinline__ int qkv_group(int tile) { return tile < 256 ? tile >> 5 : ((tile - 256) & 63) >> 3; }
+// KV-head group of a q|k|v tile: q tiles 0-511 (16 per query head), k 512-639, v 640-767.
+__device__ __forceinline__ int qkv_group(int tile) { return tile < 512 ? tile >> 6 : ((tile - 512) & 127) >> 4; }
+constexpr unsigned kGroupTiles = 96;  // q/k/v tiles of one KV-head group
 
 __device__ __forceinline__ float consumers_sum(float v, float *red)
 {
@@ -391,7 +392,9 @@ __device__ __forceinline__ float stage_frag(uint32_t *frag, const float *src, co
 }
 
 // One FP8 phase's items on this warp: CB blocks per item, NB blocks per row.
-// Leaves the item's 16 partial row sums (hi + lo columns) in partial[item][16].
+// Leaves the item's 8 partial row sums (hi + lo columns of both block halves)
+// in partial[item][8]. B column n of lane (n, t4) is half (n >> 1) & 1, hi/lo n & 1
+// of the token: lanes 0-15 load fragments, the rest stay zero.
 template <int CB, int NB>
 __device__ __forceinline__ void consume_fp8(const Ring &r, const PhaseSpan &sp, unsigned seq0, unsigned &taken,
                                             const uint4 *frag, float *partial, int *error)
@@ -403,25 +406,26 @@ __device__ __forceinline__ void consume_fp8(const Ring &r, const PhaseSpan &sp, 
         const unsigned slot = slot_of(warp, k), use = k / kSlotsPerWarp;
         mbar_wait(&r.full[slot], use & 1, error);
         const uint8_t *s = r.slots + (size_t)slot * kSlotBytes;
-        const uint4 *xf = frag + (size_t)(i % kChunks) * CB * 16;
+        const uint4 *xf = frag + (size_t)(i % kChunks) * CB * 32;  // two 64-column pieces per block
         float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
         for (int b = 0; b < CB; b++) {
             const uint4 wa = *reinterpret_cast<const uint4 *>(s + b * kBlockBytes + lane * 16);
             const uint4 wb = *reinterpret_cast<const uint4 *>(s + b * kBlockBytes + 512 + lane * 16);
             uint4 x0 = make_uint4(0, 0, 0, 0), x1 = x0;
-            if (lane < 8) {
-                x0 = xf[(b * 2) * 8 + lane];
-                x1 = xf[(b * 2 + 1) * 8 + lane];
+            if (lane < 16) {
+                const int piece = 2 * b + (lane >> 3);
+                x0 = xf[(piece * 2) * 8 + (lane & 7)];
+                x1 = xf[(piece * 2 + 1) * 8 + (lane & 7)];
             }
             mma_block(c, wa, wb, x0, x1);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&r.empty[slot]);
-        if ((lane & 3) == 0) {
-            partial[i * 16 + (lane >> 2)] = c[0] + c[1];
-            partial[i * 16 + 8 + (lane >> 2)] = c[2] + c[3];
-        }
+        // lane (g, t4): t4 = 0 holds half 0 of row g (A rows g), t4 = 1 half 1 (A rows g + 8)
+        float v = (lane & 1) ? c[2] + c[3] : c[0] + c[1];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        if ((lane & 3) == 0) partial[i * 8 + (lane >> 2)] = v;
     }
 }
 
@@ -432,17 +436,17 @@ __device__ __forceinline__ void fp8_epilogue(const GemvParams &gp, const PhaseSp
                                              const float *partial, float inv_scale)
 {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int groups = (sp.items / chunks) * 4;
+    const int groups = (sp.items / chunks) * 2;
     for (int gi = warp; gi < groups; gi += kMegaConsumerWarps) {
-        const int tl = gi >> 2, gq = gi & 3;
+        const int tl = gi >> 1, gq = gi & 1;
         float acc[4][1];
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             float s = 0.0f;
-            for (int c = 0; c < chunks; c++) s += partial[(tl * chunks + c) * 16 + gq * 4 + i];
+            for (int c = 0; c < chunks; c++) s += partial[(tl * chunks + c) * 8 + gq * 4 + i];
             acc[i][0] = s * inv_scale;
         }
-        gemv_epilogue<1, EPI>(gp, (sp.first + tl) * 4 + gq, lane, acc);
+        gemv_epilogue<1, EPI>(gp, (sp.first + tl) * 2 + gq, lane, acc);
     }
 }
 
@@ -592,8 +596,8 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
     int per = (total + ranges - 1) / ranges;
     per = (per + 7) & ~7;
     const int begin = range * per, end = min(begin + per, total);
-    // q/k/v of this KV head's group (its 48 tiles) stored by the qkv phase
-    if (threadIdx.x == 0) thread_wait(sync_word(p, kSyncQKV + kvh), 48u * epoch, p.error);
+    // q/k/v of this KV head's group stored by the qkv phase
+    if (threadIdx.x == 0) thread_wait(sync_word(p, kSyncQKV + kvh), kGroupTiles * epoch, p.error);
     consumers_sync();
     int p0 = begin + 8 * warp;
     float4 kk[8], vv[8];

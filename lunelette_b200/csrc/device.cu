@@ -284,7 +284,7 @@ static uint8_t *layer_base(lun_device *d, int layer) { return d->w8 + (size_t)la
 extern "C" int lun_device_upload_linear(lun_device *d, int index, int layer, int slot, size_t rows,
                                         size_t cols, float scale)
 {
-    if (rows * cols > kStagingBytes || (cols % 64) || (rows % 16)) return -1;
+    if (rows * cols > kStagingBytes || (cols % 128) || (rows % 8)) return -1;
     uint8_t *base = layer_base(d, layer);
     d->scales[layer][slot] = scale;
     uint8_t *matrix;
@@ -312,7 +312,7 @@ extern "C" int lun_device_upload_linear(lun_device *d, int index, int layer, int
             cudaSuccess ||
         cudaEventRecord(d->staging_done[index & 1], d->stream) != cudaSuccess)
         return -1;
-    return lun_launch_tile_fp8(d->upload_raw, (int)rows, (int)cols, matrix, (int)(cols / 64), order, row0,
+    return lun_launch_tile_fp8(d->upload_raw, (int)rows, (int)cols, matrix, (int)(cols / 128), order, row0,
                                d->stream) == cudaSuccess
                ? 0
                : -1;

@@ -6,20 +6,24 @@
 // K and V rows are stored in FP32, the reference's KV precision.
 //
 // Tiled weight layout. Every FP8 matrix [rows][K] lives on the device as
-// 16-row tiles; a tile is ceil(K/64) blocks of 1 KB (16 rows x 64 columns),
+// 8-row tiles; a tile is ceil(K/128) blocks of 1 KB (8 rows x 128 columns),
 // stored in the order the m16n8k16 tensor-core MMA consumes them: byte
-// h*512 + lane*16 + j*4 + i of a block holds tile row 8h + (lane >> 2) and block
-// column 16j + 2(lane & 3) + (i & 1) + 8(i >> 1). One coalesced 16-byte load per
-// lane per half block yields the A fragments (rows g and g+8) of the block's four
-// k16 MMAs. Rows past the matrix and columns past K are zero.
+// h*512 + lane*16 + j*4 + i of a block holds tile row lane >> 2 and block column
+// 64h + 16j + 2(lane & 3) + (i & 1) + 8(i >> 1). The MMA's 16 A rows are the
+// tile's 8 rows twice, over the block's two 64-column halves (A row g: half 0,
+// A row g + 8: half 1), so one coalesced 16-byte load per lane per half yields
+// the A fragments of the block's four k16 MMAs. Rows past the matrix and
+// columns past K are zero. Eight-row tiles split a 3072-row matrix over 148
+// SMs as 2-3 tiles each instead of 1-2 sixteen-row tiles.
 //
 // Arithmetic. E4M3 codes become FP16 exactly (cvt.rn.f16x2.e4m3x2). The FP32
 // activation row is scaled by an exact power of two 2^e (so its largest value
 // sits in [2^14, 2^15)) and split into FP16 hi + lo halves (hi = rn(x),
 // lo = rn(x - hi): 22 significant bits). The MMA's B operand carries hi and lo
-// of each token as two columns; FP16 x FP16 products are exact and accumulate in
-// FP32 on the tensor core, and the row sum is (hi column + lo column) * 2^-e,
-// times the per-tensor scale in the epilogue. This keeps the projections within
+// of each token and half as four columns (n = 4 * (token & 1) + 2 * half + lo);
+// FP16 x FP16 products are exact and accumulate in FP32 on the tensor core, and
+// a row's sum is its hi and lo columns of both halves times 2^-e, times the
+// per-tensor scale in the epilogue. This keeps the projections within
 // FP32 summation noise of the reference's FP32 dot products while replacing ten
 // CUDA-core instructions per four weights with two conversions and a quarter MMA.
 #pragma once
@@ -34,14 +38,14 @@ enum GemvEpilogue : int {
     kEpiSwiGLU = 3,    // alternating gate/up rows: y[m][f] = silu(g) * u
 };
 
-constexpr int kTileRows = 16;
-constexpr int kBlockCols = 64;
+constexpr int kTileRows = 8;
+constexpr int kBlockCols = 128;
 constexpr int kBlockBytes = 1024;
 
-// Bytes of a matrix in the tiled layout (rows padded to 16, columns to 64).
+// Bytes of a matrix in the tiled layout (rows padded to 8, columns to 128).
 __host__ __device__ constexpr size_t tiled_bytes(size_t rows, size_t cols)
 {
-    return ((rows + 15) / 16) * 16 * ((cols + 63) / 64) * 64;
+    return ((rows + 7) / 8) * 8 * ((cols + 127) / 128) * 128;
 }
 
 // Row orders the upload applies before tiling (storage row of source row r):
@@ -72,7 +76,7 @@ static __global__ void tile_fp8_kernel(const uint8_t *src, int rows, int cols, u
         const int r = (int)(u / chunks_per_row), q = (int)(u % chunks_per_row);
         const uint4 v = *reinterpret_cast<const uint4 *>(src + (size_t)r * cols + (size_t)q * 16);
         const int s = tile_storage_row(order, row0, r);
-        const int tile = s >> 4, h = (s >> 3) & 1, g = s & 7, kb = q >> 2, j = q & 3;
+        const int tile = s >> 3, g = s & 7, kb = q >> 3, h = (q >> 2) & 1, j = q & 3;
         uint8_t *blk = dst + ((size_t)tile * dst_nb + kb) * kBlockBytes + h * 512 + j * 4;
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -102,8 +106,8 @@ __device__ __forceinline__ void mma_f16_16816(float (&c)[4], uint32_t a0, uint32
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// The four k16 MMAs of one block: wa/wb are this lane's 16 bytes of rows g and
-// g+8, x0/x1 its B fragments (zero on lanes past the activation columns).
+// The four k16 MMAs of one block: wa/wb are this lane's 16 bytes of tile row g
+// in the block's two halves, x0/x1 its B fragments (zero on unused lanes).
 __device__ __forceinline__ void mma_block(float (&c)[4], const uint4 &wa, const uint4 &wb, const uint4 &x0,
                                           const uint4 &x1)
 {
@@ -118,10 +122,11 @@ __device__ __forceinline__ void mma_block(float (&c)[4], const uint4 &wa, const 
 }
 
 // ---- activation fragments ------------------------------------------------------
-// B fragments of `lanes` = 8 * tokens lanes per half block, as uint4 index
-// (kb * 2 + half) * lanes + lane; lane 4n + t4 carries B column n (token n / 2,
-// hi for even n, lo for odd n). Word (j & 1) * 2 + b of that uint4 holds MMA j
-// (j >> 1 == half) register b: columns 16j + 2t4 + 8b and the next one.
+// Staged per 64-column piece c64 of the activation rows: `lanes` = 8 * tokens
+// lanes per half piece, as uint4 index (c64 * 2 + half) * lanes + 4u + t4 for
+// u = 2 * token + (0 hi, 1 lo). Word (j & 1) * 2 + b of that uint4 holds MMA j
+// (j >> 1 == half) register b: columns 16j + 2t4 + 8b and the next one. An MMA
+// lane with B column n reads piece 2 * block + ((n >> 1) & 1), u = 2 * token + (n & 1).
 __device__ __forceinline__ void frag_store_pair(uint32_t *frag, int lanes, int c, int n, uint32_t pair)
 {
     const int kb = c >> 6, w = c & 63, j = w >> 4, ww = w & 15;
@@ -192,7 +197,7 @@ struct GemvParams {
 template <int M>
 __device__ __forceinline__ void gemv_stage(const GemvParams &p, uint32_t *frag, float *inv_scale, float *red)
 {
-    const int cols = p.cols, NB = (cols + 63) >> 6, lanes = 8 * M;
+    const int cols = p.cols, NB = 2 * ((cols + 127) >> 7), lanes = 8 * M;  // 64-column pieces
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
     float ss[M], mx[M];
 #pragma unroll
@@ -344,15 +349,16 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, int g, int la
     }
 }
 
-// One launch: 8 warps per block, grid-stride over 16-row tiles. The warps
-// split a tile's blocks (warp w takes blocks w, w+8, ...), then their partial
-// row sums are added in warp order (deterministic) and warps 0-3 run the
-// epilogue of the tile's four row groups.
+// One launch: 8 warps per block, grid-stride over 8-row tiles. The warps split
+// a tile's blocks (warp w takes blocks w, w+8, ...), one MMA per token pair and
+// k16 step; their partial row sums are added in warp order (deterministic) and
+// warps 0-1 run the epilogue of the tile's two row groups.
 template <int M, int EPI>
 __global__ void __launch_bounds__(256) gemv_tiled_kernel(GemvParams p)
 {
+    constexpr int kPairs = (M + 1) / 2;
     extern __shared__ uint4 frag4[];
-    __shared__ float part[8][16][M];
+    __shared__ float part[8][8][M];
     __shared__ float inv_scale[M];
     __shared__ float red[16 * M];
     l2_prefetch_share(p.prefetch, p.prefetch_bytes);
@@ -362,27 +368,40 @@ __global__ void __launch_bounds__(256) gemv_tiled_kernel(GemvParams p)
     __syncthreads();
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
-    const int NB = (p.cols + 63) >> 6, tiles = (p.rows + 15) >> 4, lanes = 8 * M;
+    const int NB = (p.cols + 127) >> 7, tiles = (p.rows + 7) >> 3, lanes = 8 * M;
+    // this lane's B column g: token 2 * pair + (g >> 2), half (g >> 1) & 1, hi/lo g & 1
+    const int slot = (2 * (g >> 2) + (g & 1)) * 4 + t4;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
         const uint8_t *tw = p.W + (size_t)tile * NB * kBlockBytes;
-        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        float c[kPairs][4];
+#pragma unroll
+        for (int tp = 0; tp < kPairs; tp++) c[tp][0] = c[tp][1] = c[tp][2] = c[tp][3] = 0.0f;
 #pragma unroll 2
         for (int kb = warp; kb < NB; kb += 8) {
             const uint4 wa = ld_stream(tw + (size_t)kb * kBlockBytes + lane * 16);
             const uint4 wb = ld_stream(tw + (size_t)kb * kBlockBytes + 512 + lane * 16);
-            uint4 x0 = make_uint4(0, 0, 0, 0), x1 = x0;
-            if (lane < lanes) {
-                x0 = frag4[(kb * 2) * lanes + lane];
-                x1 = frag4[(kb * 2 + 1) * lanes + lane];
+            const int piece = 2 * kb + ((g >> 1) & 1);
+#pragma unroll
+            for (int tp = 0; tp < kPairs; tp++) {
+                uint4 x0 = make_uint4(0, 0, 0, 0), x1 = x0;
+                if (2 * tp + (g >> 2) < M) {
+                    const int l = slot + 16 * tp;
+                    x0 = frag4[(piece * 2) * lanes + l];
+                    x1 = frag4[(piece * 2 + 1) * lanes + l];
+                }
+                mma_block(c[tp], wa, wb, x0, x1);
             }
-            mma_block(c, wa, wb, x0, x1);
         }
-        if (t4 < M) {
-            part[warp][g][t4] = c[0] + c[1];
-            part[warp][g + 8][t4] = c[2] + c[3];
+        // lane (g, t4) holds token 2 * pair + (t4 >> 1), half t4 & 1 of row g
+#pragma unroll
+        for (int tp = 0; tp < kPairs; tp++) {
+            float v = (t4 & 1) ? c[tp][2] + c[tp][3] : c[tp][0] + c[tp][1];
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            const int m = 2 * tp + (t4 >> 1);
+            if (!(t4 & 1) && m < M) part[warp][g][m] = v;
         }
         __syncthreads();
-        if (warp < 4) {
+        if (warp < 2) {
             float acc[4][M];
 #pragma unroll
             for (int i = 0; i < 4; i++)
@@ -393,7 +412,7 @@ __global__ void __launch_bounds__(256) gemv_tiled_kernel(GemvParams p)
                     for (int w = 0; w < 8; w++) s += part[w][warp * 4 + i][m];
                     acc[i][m] = s * inv_scale[m];
                 }
-            gemv_epilogue<M, EPI>(p, tile * 4 + warp, lane, acc);
+            gemv_epilogue<M, EPI>(p, tile * 2 + warp, lane, acc);
         }
         __syncthreads();
     }

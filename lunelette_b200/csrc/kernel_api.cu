@@ -53,7 +53,7 @@ LUN_API int lunelette_cuda_tile_fp8(const uint8_t *src, size_t rows, size_t cols
         order > 2 || (order == 1 && rows % 128) || (order == 2 && rows % 2))
         return -1;
     cudaStream_t st = (cudaStream_t)stream;
-    const int nb = (int)((cols + 63) / 64);
+    const int nb = (int)((cols + 127) / 128);
     if (tiled_bytes(rows, cols) != rows * cols && cudaMemsetAsync(dst, 0, tiled_bytes(rows, cols), st) != cudaSuccess)
         return -1;
     if (order == 2) {

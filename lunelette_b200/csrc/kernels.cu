@@ -53,17 +53,17 @@ cudaError_t setup_epi()
     return setup_one<4, EPI>();
 }
 
-// B fragments: 256 bytes per token per 64-column block.
+// B fragments: 256 bytes per token per 64-column piece (columns padded to 128).
 template <int M, int EPI>
 cudaError_t launch_one(const GemvParams &p, int sm_count, cudaStream_t stream)
 {
-    const size_t smem = (size_t)((p.cols + 63) / 64) * 256 * M;
+    const size_t smem = (size_t)((p.cols + 127) / 128) * 2 * 256 * M;
     int per_sm = 0;
     cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_tiled_kernel<M, EPI>,
                                                                   256, smem);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) per_sm = 1;
-    int blocks = (p.rows + 15) / 16;
+    int blocks = (p.rows + 7) / 8;
     int limit = sm_count * per_sm;
     if (blocks > limit) blocks = limit;
     return launch(gemv_tiled_kernel<M, EPI>, dim3(blocks), dim3(256), smem, stream, p);
@@ -293,7 +293,7 @@ cudaError_t lun_launch_rmsnorm(const float *gain, const float *x, float *out, in
 cudaError_t lun_launch_tile_fp8(const uint8_t *src, int rows, int cols, uint8_t *dst, int dst_nb, int order,
                                 int row0, cudaStream_t stream)
 {
-    if (rows <= 0 || cols <= 0 || (cols & 15) || dst_nb < (cols + 63) / 64) return cudaErrorInvalidValue;
+    if (rows <= 0 || cols <= 0 || (cols & 15) || dst_nb < (cols + 127) / 128) return cudaErrorInvalidValue;
     const size_t chunks = (size_t)rows * (cols / 16);
     size_t blocks = (chunks + 255) / 256;
     if (blocks > 4096) blocks = 4096;

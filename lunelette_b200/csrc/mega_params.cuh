@@ -21,7 +21,7 @@ constexpr int kMegaTimelineHead = 1 + kMegaBarriersPerStep;
 // Synchronisation words of one launch, each on its own 128-byte line, zero at
 // launch and only ever increased (targets grow with the layers the launch ran):
 //   kSyncBarrier        grid barrier arrivals (gridDim per barrier)
-//   kSyncQKV + kvh      q/k/v tiles of KV head kvh's group stored (48 per layer)
+//   kSyncQKV + kvh      q/k/v tiles of KV head kvh's group stored (96 per layer)
 //   kSyncAttn           KV heads whose attention output is stored (8 per layer)
 //   kSyncTicket + kvh   attention ranges of KV head kvh finished
 //   kSyncPick           CTAs done with the head (gridDim per step)

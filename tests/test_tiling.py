@@ -9,13 +9,13 @@ from tests.tiling import ORDER_INTERLEAVE, ORDER_ROPE_PAIRS, ORDER_ROWS, storage
 def element_reference(codes, order):
     rows, cols = codes.shape
     out = np.zeros(tiled_bytes(rows, cols), np.uint8)
-    nb = -(-cols // 64)
+    nb = -(-cols // 128)
     srow = storage_rows(rows, order)
     for r in range(rows):
         s = int(srow[r])
         for c in range(cols):
-            tile, h, g = s // 16, (s // 8) % 2, s % 8
-            kb, w = c // 64, c % 64
+            tile, g = s // 8, s % 8
+            kb, h, w = c // 128, (c // 64) % 2, c % 64
             j, ww = w // 16, w % 16
             t4 = (ww % 8) // 2
             i = (ww & 1) | ((ww >> 3) << 1)
