@@ -258,11 +258,11 @@ __device__ __forceinline__ void record_mark(const MegaParams &p, bool rec, int m
     if (rec) p.timeline[kMegaTimelineHead + (size_t)mark * gridDim.x + blockIdx.x] = globaltimer_ns();
 }
 
-// Publish the CTA's global writes (callers synchronise the consumers first),
-// then add n to *word (release). One thread.
+// Publish the CTA's global writes and add n to *word. One thread, after the
+// consumers synchronised (bar.sync): the release add orders every write that
+// happened before it in the CTA, so a reader that acquires the new count sees them.
 __device__ __forceinline__ void signal_word(unsigned *word, unsigned n)
 {
-    __threadfence();
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(word), "r"(n) : "memory");
 }
 
@@ -273,14 +273,13 @@ __device__ __forceinline__ void grid_sync(const MegaParams &p, unsigned target, 
     consumers_sync();
     if (threadIdx.x == 0) {
         record_mark(p, rec, mark);
-        __threadfence();
         if (!*(volatile int *)p.error) {
-            // barrier k is passed once the arrival count reaches k * gridDim.x
+            // barrier k is passed once the arrival count reaches k * gridDim.x;
+            // release add and acquire polls order the CTAs' writes around it
             unsigned *word = sync_word(p, kSyncBarrier);
-            asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(word), "r"(1u) : "memory");
+            signal_word(word, 1u);
             thread_wait(word, target * gridDim.x, p.error);
         }
-        __threadfence();
         if (rec && blockIdx.x == 0) p.timeline[target] = globaltimer_ns();
     }
     consumers_sync();
