@@ -124,10 +124,11 @@ int lunelette_cuda_decode_loop(lunelette_metal *context, int64_t first_token, si
  * leaves each of its 79 grid barriers (entry 1 + k; per layer one after the o
  * projection, one after gate/up and one after down, then one after the greedy
  * pick). From entry 80, CTA b's marks m at 80 + m * ctas + b (ctas = the
- * device's SM count): per layer L, mark 5L when it published its q/k/v tiles,
- * 5L + 1 when it published an attention result (CTAs that own one, else 0),
- * 5L + 2..4 its arrivals at the o, gate/up and down barriers; mark 130 its
- * arrival at the last barrier. Copy up to 80 + 131 * ctas entries. */
+ * device's SM count): per layer L at 13L + 0 qkv row staged, 1 qkv items done,
+ * 2 q/k/v published, 3 attention published (CTAs that own one, else 0), 4 o row
+ * staged, 5 o items done, 6 arrival at the o barrier, 7-9 the same three for
+ * gate/up, 10-12 for down; mark 338 the arrival at the last barrier. Copy up
+ * to 80 + 339 * ctas entries. */
 int lunelette_cuda_timeline(lunelette_metal *context, int enable);
 int lunelette_cuda_timeline_copy(lunelette_metal *context, unsigned long long *out, size_t entries);
 

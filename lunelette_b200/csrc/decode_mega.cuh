@@ -3,12 +3,13 @@
 // reference's layer graph (src/metal_encode.m:124-215).
 //
 // Warp roles per CTA (256 threads):
-//   producer (lane 0 of warp 7): walks this CTA's share of every weight matrix
-//     in the order the step consumes it and copies it, 8-12 KB items at a time,
-//     into shared-memory slots with bulk async copies (cp.async.bulk + mbarrier
-//     complete_tx). Weights never depend on activations, so the producer runs
-//     ahead across phases and grid barriers, bounded by free slots; it also
-//     keeps a short stretch of the stream (p.l2_ahead bytes) prefetched into L2.
+//   producers (lanes 0-6 of warp 7, lane w serving consumer warp w): walk this
+//     CTA's share of every weight matrix in the order the step consumes it and
+//     copy it, 8-12 KB items at a time, into shared-memory slots with bulk async
+//     copies (cp.async.bulk + mbarrier complete_tx). Weights never depend on
+//     activations, so the producers run ahead across phases and grid barriers,
+//     bounded by free slots; they also keep a short stretch of the stream
+//     (p.l2_ahead bytes) prefetched into L2 while the layers run.
 //   consumers (warps 0-6): per phase, wait at a grid barrier for the previous
 //     phase's activations, stage the activation row as FP16 hi/lo MMA fragments
 //     (and the epilogue's residual rows), then take items (8 rows x 1024 or
@@ -194,43 +195,57 @@ __device__ __forceinline__ int first_item(unsigned seq0)
     return (warp + kMegaConsumerWarps - (int)(seq0 % kMegaConsumerWarps)) % kMegaConsumerWarps;
 }
 
-// Producer (one thread): every item of the launch, in stream order, plus an L2
-// prefetch that runs p.l2_ahead bytes ahead of the ring.
-__device__ __forceinline__ void produce(const MegaParams &p, const Ring &r)
+// Position of one consumer warp's next item in the launch's stream: phase k,
+// item i of that phase, seq0 items in the stream before phase k.
+struct WarpCursor {
+    int k, i;
+    unsigned seq0;
+    PhaseSpan sp;
+};
+
+// Move c to warp w's first item at or after c.i (item i of the stream belongs to
+// warp (seq0 + i) mod 7); false past the launch's last phase.
+__device__ __forceinline__ bool cursor_settle(const MegaParams &p, WarpCursor &c, int w, int total)
 {
-    unsigned issued[kMegaConsumerWarps] = {};
-    unsigned seq = 0;
+    while (c.i >= c.sp.items) {
+        c.seq0 += (unsigned)c.sp.items;
+        if (++c.k >= total) return false;
+        c.sp = stream_span(p, c.k);
+        c.i = (w + kMegaConsumerWarps - (int)(c.seq0 % kMegaConsumerWarps)) % kMegaConsumerWarps;
+    }
+    return true;
+}
+
+// Producer lane w (one per consumer warp): every item of warp w in stream
+// order, each as one bulk copy into the warp's next slot once the warp released
+// it; the lanes issue independently, so a slow warp holds back only its own
+// stream. Each lane also keeps its next items (p.l2_ahead / 7 bytes) prefetched
+// into L2 while the layers run; the head streams without waits and reads
+// nothing ahead.
+__device__ __forceinline__ void produce(const MegaParams &p, const Ring &r, int w)
+{
     const int total = p.steps * kPhasesPerStep;
-    int pk = 0;  // L2 lookahead cursor: phase and byte offset in it
-    unsigned pf_off = 0;
-    PhaseSpan pf = stream_span(p, 0);
+    WarpCursor rc = {0, w, 0u, stream_span(p, 0)}, pc = rc;
+    bool more = cursor_settle(p, rc, w, total), pf_more = cursor_settle(p, pc, w, total);
+    const unsigned budget = p.l2_ahead / kMegaConsumerWarps;
     unsigned long long ring_bytes = 0, pf_bytes = 0;
-    for (int k = 0; k < total; k++) {
-        const PhaseSpan sp = stream_span(p, k);
-        for (int i = 0; i < sp.items; i++, seq++) {
-            while (pk < total && pf_bytes < ring_bytes + p.l2_ahead) {
-                const unsigned span = (unsigned)pf.items * (unsigned)pf.item_bytes;
-                if (pf_off >= span) {
-                    if (++pk < total) {
-                        pf = stream_span(p, pk);
-                        pf_off = 0;
-                    }
-                    continue;
-                }
-                const unsigned n = span - pf_off < 16384u ? span - pf_off : 16384u;
-                l2_prefetch(pf.src + pf_off, n);
-                pf_off += n;
-                pf_bytes += n;
-            }
-            const int w = (int)(seq % kMegaConsumerWarps);
-            const unsigned u = issued[w]++;
-            const unsigned slot = slot_of(w, u), use = u / kSlotsPerWarp;
-            if (use && !mbar_wait(&r.empty[slot], (use - 1) & 1, p.error)) return;
-            mbar_expect_tx(&r.full[slot], (unsigned)sp.item_bytes);
-            bulk_g2s(r.slots + (size_t)slot * kSlotBytes, sp.src + (size_t)i * sp.item_bytes, (unsigned)sp.item_bytes,
-                     &r.full[slot]);
-            ring_bytes += (unsigned)sp.item_bytes;
+    for (unsigned u = 0; more; u++) {
+        const unsigned ahead = rc.k % kPhasesPerStep == kLayers * 4 ? 0u : budget;
+        while (pf_more && pf_bytes < ring_bytes + ahead) {
+            const unsigned n = (unsigned)pc.sp.item_bytes;
+            if (pf_bytes >= ring_bytes) l2_prefetch(pc.sp.src + (size_t)pc.i * n, n);  // not yet in the ring
+            pf_bytes += n;
+            pc.i += kMegaConsumerWarps;
+            pf_more = cursor_settle(p, pc, w, total);
         }
+        const unsigned slot = slot_of(w, u), use = u / kSlotsPerWarp;
+        if (use && !mbar_wait(&r.empty[slot], (use - 1) & 1, p.error)) return;
+        const unsigned n = (unsigned)rc.sp.item_bytes;
+        mbar_expect_tx(&r.full[slot], n);
+        bulk_g2s(r.slots + (size_t)slot * kSlotBytes, rc.sp.src + (size_t)rc.i * n, n, &r.full[slot]);
+        ring_bytes += n;
+        rc.i += kMegaConsumerWarps;
+        more = cursor_settle(p, rc, w, total);
     }
 }
 
@@ -712,7 +727,7 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
     if (ranges == 1) {
         if (threadIdx.x == 0) {
             signal_word(sync_word(p, kSyncAttn), 1);
-            record_mark(p, rec, layer * 5 + 1);
+            record_mark(p, rec, layer * kMarksPerLayer + 3);
         }
         return;
     }
@@ -728,7 +743,7 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
     consumers_sync();
     if (threadIdx.x == 0) {
         signal_word(sync_word(p, kSyncAttn), 1);
-        record_mark(p, rec, layer * 5 + 1);
+        record_mark(p, rec, layer * kMarksPerLayer + 3);
     }
 }
 
@@ -758,7 +773,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
     __syncthreads();
 
     if (threadIdx.x >= kMegaConsumers) {
-        if (threadIdx.x == kMegaConsumers) produce(p, ring);
+        const int lane = threadIdx.x & 31;
+        if (lane < kMegaConsumerWarps) produce(p, ring, lane);
         return;
     }
 
@@ -798,13 +814,16 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
             gp.bound[1] = kQuery + kKV;
             gp.y = p.q;
             gp.y_stride = kQuery;
+            const int mk = layer * kMarksPerLayer;
             float inv = stage_frag<kHidden>(frag, p.x, layer == 0 ? emb_row : nullptr,
                                             p.norms + (size_t)(2 * layer) * kHidden, red);
+            if (threadIdx.x == 0) record_mark(p, rec, mk);
             if (layer == 0 && blockIdx.x == 0)
                 for (int c = threadIdx.x; c < kHidden; c += kMegaConsumers) p.x[c] = bf16_lo((uint32_t)emb_row[c]);
             consume_fp8<item_blocks(kPhQKV), kHidden / kBlockCols>(ring, sp, seq, taken, frag4, partial, p.error);
             seq += sp.items;
             consumers_sync();
+            if (threadIdx.x == 0) record_mark(p, rec, mk + 1);
             fp8_epilogue<kEpiQKV>(gp, sp, kHidden / kBlockCols / item_blocks(kPhQKV), partial, inv);
             consumers_sync();
             if (threadIdx.x == 0) {
@@ -816,7 +835,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
                     for (; t < t1 && qkv_group(t) == g; t++) n++;
                     signal_word(sync_word(p, kSyncQKV + g), (unsigned)n);
                 }
-                record_mark(p, rec, layer * 5);
+                record_mark(p, rec, mk + 2);
             }
             if (unit >= 0) {
                 float *qs = reinterpret_cast<float *>(frag);
@@ -839,11 +858,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
             if (threadIdx.x == 0) thread_wait(sync_word(p, kSyncAttn), (unsigned)kKVHeads * epoch, p.error);
             consumers_sync();
             inv = stage_frag<kQuery>(frag, p.attn, nullptr, nullptr, red);
+            if (threadIdx.x == 0) record_mark(p, rec, mk + 4);
             consume_fp8<item_blocks(kPhO), kQuery / kBlockCols>(ring, sp, seq, taken, frag4, partial, p.error);
             seq += sp.items;
             consumers_sync();
+            if (threadIdx.x == 0) record_mark(p, rec, mk + 5);
             fp8_epilogue<kEpiResidual>(gp, sp, kQuery / kBlockCols / item_blocks(kPhO), partial, inv);
-            grid_sync(p, ++barrier, rec, layer * 5 + 2);
+            grid_sync(p, ++barrier, rec, mk + 6);
             // post norm + gate/up + SwiGLU
             sp = phase_span(p, layer, kPhGateUp);
             gp.rows = kGateUpRows;
@@ -853,11 +874,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
             gp.y = p.act;
             gp.y_stride = kInner;
             inv = stage_frag<kHidden>(frag, p.h, nullptr, p.norms + (size_t)(2 * layer + 1) * kHidden, red);
+            if (threadIdx.x == 0) record_mark(p, rec, mk + 7);
             consume_fp8<item_blocks(kPhGateUp), kHidden / kBlockCols>(ring, sp, seq, taken, frag4, partial, p.error);
             seq += sp.items;
             consumers_sync();
+            if (threadIdx.x == 0) record_mark(p, rec, mk + 8);
             fp8_epilogue<kEpiSwiGLU>(gp, sp, kHidden / kBlockCols / item_blocks(kPhGateUp), partial, inv);
-            grid_sync(p, ++barrier, rec, layer * 5 + 3);
+            grid_sync(p, ++barrier, rec, mk + 9);
             // down + residual (h)
             sp = phase_span(p, layer, kPhDown);
             gp.rows = kHidden;
@@ -868,11 +891,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
             gp.y_stride = kHidden;
             stage_rows(res_s, p.h, gp.res_base, sp.items / (kInner / kBlockCols / item_blocks(kPhDown)) * kTileRows);
             inv = stage_frag<kInner>(frag, p.act, nullptr, nullptr, red);
+            if (threadIdx.x == 0) record_mark(p, rec, mk + 10);
             consume_fp8<item_blocks(kPhDown), kInner / kBlockCols>(ring, sp, seq, taken, frag4, partial, p.error);
             seq += sp.items;
             consumers_sync();
+            if (threadIdx.x == 0) record_mark(p, rec, mk + 11);
             fp8_epilogue<kEpiResidual>(gp, sp, kInner / kBlockCols / item_blocks(kPhDown), partial, inv);
-            grid_sync(p, ++barrier, rec, layer * 5 + 4);
+            grid_sync(p, ++barrier, rec, mk + 12);
         }
         // final norm + tied head, 8-column staging
         {
@@ -931,7 +956,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
                 p.step->length = length + 1;
             }
         }
-        grid_sync(p, ++barrier, rec, kLayers * 5);
+        grid_sync(p, ++barrier, rec, kLayers * kMarksPerLayer);
     }
 }
 

@@ -11,11 +11,15 @@ namespace lun {
 constexpr int kMegaBarriersPerStep = kLayers * 3 + 1;
 // Timeline of the first step of a launch: [0] start, [1 + k] CTA 0 leaving
 // barrier k, then from kMegaTimelineHead one entry per CTA b for each mark m at
-// kMegaTimelineHead + m * gridDim.x + b. Marks per layer L: 5L qkv results
-// published, 5L + 1 attention published (CTAs that own a unit, else 0),
-// 5L + 2..4 arrival at the o, gate/up and down barriers; mark 5 * 26 the
-// arrival at the barrier after the pick.
-constexpr int kMegaMarksPerStep = kLayers * 5 + 1;
+// kMegaTimelineHead + m * gridDim.x + b. Marks per layer L, at 13L + :
+//   0 qkv row staged, 1 qkv items done, 2 q/k/v tiles published,
+//   3 attention published (CTAs that own a unit, else 0),
+//   4 o row staged, 5 o items done, 6 arrival at the o barrier,
+//   7 gate/up row staged, 8 items done, 9 arrival at the gate/up barrier,
+//   10 down row staged, 11 items done, 12 arrival at the down barrier;
+// mark 13 * 26 is the arrival at the barrier after the pick.
+constexpr int kMarksPerLayer = 13;
+constexpr int kMegaMarksPerStep = kLayers * kMarksPerLayer + 1;
 constexpr int kMegaTimelineHead = 1 + kMegaBarriersPerStep;
 
 // Synchronisation words of one launch, each on its own 128-byte line, zero at

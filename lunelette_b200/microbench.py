@@ -98,22 +98,27 @@ PHASE_BYTES = {"qkv": 6144 * 3072, "attn_o": (6144 + 4096) * 3072, "gate_up": 18
 def decode_phases(checkpoint, steps=8, prompt=32):
     """Phase durations of the persistent decode kernel (single-token steps through
     lunelette_metal_decode), from its %globaltimer timeline, as means over `steps`
-    steps and 26 layers, each measured from the barrier that opens the layer
-    (or from the previous phase's barrier): `qkv` until the last CTA published its
-    q/k/v tiles, `attention` until the last attention result was published,
-    `attn_o` until CTA 0 left the barrier after the o projection, `gate_up` and
-    `down` barrier to barrier, and `head` (head GEMV and greedy pick). For each
-    barrier phase also `<phase>_spread`, first to last CTA arriving, and
-    `<phase>_release`, the last arrival to CTA 0 leaving the barrier."""
+    steps and 26 layers. Barrier phases, from CTA 0 leaving one barrier to
+    leaving the next: `attn_o` (qkv, attention, o), `gate_up`, `down`, `head`
+    (head GEMV and greedy pick); with `<phase>_spread`, first to last CTA
+    arriving, and `<phase>_release`, last arrival to CTA 0 leaving. Milestones
+    within a layer, measured from the barrier that opened the phase to the last
+    CTA reaching them (`@max`) and to the median CTA (`@med`): row staged, items
+    done, q/k/v published, attention published."""
     import torch
     import lunelette_b200 as L
     peak, kind = hbm_peak()
     ctas = torch.cuda.get_device_properties(0).multi_processor_count
-    barriers, marks = 79, 131
-    closing = ["attn_o", "gate_up", "down"]
-    names = ["qkv", "attention"] + closing + ["head"]
-    rows = {n: [] for n in names + [m + "_spread" for m in closing + ["head"]] +
-            [m + "_release" for m in closing + ["head"]] + ["step"]}
+    barriers, per_layer = 79, 13
+    marks = 26 * per_layer + 1
+    milestones = {0: "qkv_staged", 1: "qkv_items", 2: "qkv_published", 3: "attention", 4: "o_staged",
+                  5: "o_items", 7: "gate_up_staged", 8: "gate_up_items", 10: "down_staged", 11: "down_items"}
+    closing = {6: "attn_o", 9: "gate_up", 12: "down"}
+    rows = {}
+
+    def add(name, v):
+        rows.setdefault(name, []).append(v)
+
     with L.Runtime(checkpoint) as rt:
         ids = np.random.default_rng(7).integers(1000, 131072, prompt)
         tok = int(np.argmax(rt.prefill(ids)))
@@ -123,22 +128,27 @@ def decode_phases(checkpoint, steps=8, prompt=32):
             full = rt.timeline_copy(1 + barriers + marks * ctas).astype(np.float64) / 1000.0  # us
             start, exits = full[0], full[1:1 + barriers]
             mark = full[1 + barriers:].reshape(marks, ctas)
-
-            def closed(name, prev, b, arrivals):
-                rows[name].append(exits[b] - prev)
-                rows[name + "_spread"].append(arrivals.max() - arrivals.min())
-                rows[name + "_release"].append(exits[b] - arrivals.max())
-
             opened = start
             for layer in range(26):
-                rows["qkv"].append(mark[5 * layer].max() - opened)
-                published = mark[5 * layer + 1][mark[5 * layer + 1] > 0]
-                rows["attention"].append(published.max() - opened)
-                for k, name in enumerate(closing):
-                    closed(name, opened if k == 0 else exits[3 * layer + k - 1], 3 * layer + k, mark[5 * layer + 2 + k])
-                opened = exits[3 * layer + 2]
-            closed("head", opened, 78, mark[130])
-            rows["step"].append(exits[78] - start)
+                base = layer * per_layer
+                for k in range(per_layer):
+                    arr = mark[base + k]
+                    if k in milestones:
+                        arr = arr[arr > 0]
+                        add(milestones[k] + "@max", arr.max() - opened)
+                        add(milestones[k] + "@med", float(np.median(arr)) - opened)
+                    else:
+                        b = 3 * layer + (k - 6) // 3
+                        name = closing[k]
+                        add(name, exits[b] - opened)
+                        add(name + "_spread", arr.max() - arr.min())
+                        add(name + "_release", exits[b] - arr.max())
+                        opened = exits[b]
+            arr = mark[marks - 1]
+            add("head", exits[78] - opened)
+            add("head_spread", arr.max() - arr.min())
+            add("head_release", exits[78] - arr.max())
+            add("step", exits[78] - start)
         rt.timeline(False)
     out = []
     for name, vals in rows.items():
