@@ -52,7 +52,7 @@ constexpr int kPhasesPerStep = kLayers * 4 + 1;  // 4 FP8 phases per layer, then
 constexpr int kAttnMaxRanges = 18;               // position ranges per KV head (8 x 18 <= CTAs)
 constexpr int kQStride = 36;                     // floats per staged query quarter (32 + pad)
 constexpr int kCmbStride = 132;                  // floats per (warp, head) attention partial
-static_assert(16 * kQStride * 4 + kMegaConsumerWarps * 4 * kCmbStride * 4 <= kFragBytes,
+static_assert((16 * kQStride + 2 * kHeadDim + kMegaConsumerWarps * 4 * kCmbStride) * 4 <= kFragBytes,
               "attention staging fits the fragment area");
 
 // ---- small PTX wrappers -----------------------------------------------------
@@ -301,9 +301,35 @@ __device__ __forceinline__ void grid_sync(const MegaParams &p, unsigned target, 
 }
 
 // ---- consumer helpers -------------------------------------------------------
-// KV-head group of a q|k|v tile: q tiles 0-511 (16 per query head), k 512-639, v 640-767.
-__device__ __forceinline__ int qkv_group(int tile) { return tile < 512 ? tile >> 6 : ((tile - 512) & 127) >> 4; }
-constexpr unsigned kGroupTiles = 96;  // q/k/v tiles of one KV-head group
+// ---- tagged words (store_tagged) --------------------------------------------
+__device__ __forceinline__ ulonglong2 ld_cg_u64x2(const unsigned long long *p)
+{
+    ulonglong2 v;
+    asm volatile("ld.global.cg.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+    return v;
+}
+
+// Four tagged words at src -> v; true when all carry `want`.
+__device__ __forceinline__ bool load_tagged4(const unsigned long long *src, unsigned want, float4 &v)
+{
+    const ulonglong2 a = ld_cg_u64x2(src), b = ld_cg_u64x2(src + 2);
+    v = make_float4(__uint_as_float((unsigned)a.x), __uint_as_float((unsigned)a.y), __uint_as_float((unsigned)b.x),
+                    __uint_as_float((unsigned)b.y));
+    return (unsigned)(a.x >> 32) == want && (unsigned)(a.y >> 32) == want && (unsigned)(b.x >> 32) == want &&
+           (unsigned)(b.y >> 32) == want;
+}
+
+// Poll four tagged words until they carry `want` (bounded).
+__device__ __forceinline__ float4 poll_tagged4(const unsigned long long *src, unsigned want, int *error)
+{
+    float4 v;
+    for (unsigned spins = 0; !load_tagged4(src, want, v);)
+        if (++spins > kSpinLimit || ((spins & 255u) == 0 && *(volatile int *)error)) {
+            atomicExch(error, 1);
+            break;
+        }
+    return v;
+}
 
 __device__ __forceinline__ float consumers_sum(float v, float *red)
 {
@@ -558,6 +584,21 @@ __device__ __forceinline__ void attention_load(const MegaParams &p, int layer, i
                       : make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
+// The step's own position `cur` inside the sub-tile at p0: its k/v rows come
+// from shared memory (staged from the tagged words), not from the pool.
+__device__ __forceinline__ void attention_patch(int p0, int cur, const float *kcur, const float *vcur, float4 (&kk)[8],
+                                                float4 (&vv)[8])
+{
+    if (cur < p0 || cur >= p0 + 8) return;
+    const int lane = threadIdx.x & 31, pp = lane >> 2, qd = lane & 3;
+    if (p0 + pp == cur)
+#pragma unroll
+        for (int c = 0; c < 8; c++) kk[c] = reinterpret_cast<const float4 *>(kcur + qd * 32)[c];
+#pragma unroll
+    for (int t = 0; t < 8; t++)
+        if (p0 + t == cur) vv[t] = reinterpret_cast<const float4 *>(vcur)[lane];
+}
+
 // Merge the ranges of KV head kvh in range order (warps 0-3, one query head each).
 __device__ __forceinline__ void merge_ranges(const MegaParams &p, int kvh, int ranges)
 {
@@ -601,8 +642,8 @@ __device__ __forceinline__ void merge_ranges(const MegaParams &p, int kvh, int r
 // merges them in range order. Replaces scores + attend
 // (src/metal_kernels.metal:81-132).
 __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, int length, int unit, int ranges,
-                                              unsigned epoch, unsigned tickets, float *qs, float *cmb, int *flag,
-                                              bool rec)
+                                              unsigned epoch, unsigned tag, unsigned tickets, float *qs, float *cmb,
+                                              int *flag, bool rec)
 {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, pp = lane >> 2, qd = lane & 3;
     const int total = length + 1;
@@ -610,18 +651,34 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
     int per = (total + ranges - 1) / ranges;
     per = (per + 7) & ~7;
     const int begin = range * per, end = min(begin + per, total);
-    // q/k/v of this KV head's group stored by the qkv phase
-    if (threadIdx.x == 0) thread_wait(sync_word(p, kSyncQKV + kvh), kGroupTiles * epoch, p.error);
-    consumers_sync();
+    float *kcur = qs + 16 * kQStride, *vcur = kcur + kHeadDim;
+    // K/V of earlier steps' positions are in memory already: loaded first
     int p0 = begin + 8 * warp;
     float4 kk[8], vv[8];
     if (p0 < end) attention_load(p, layer, kvh, p0, end, kk, vv);
-    if (threadIdx.x < 128) {
-        const int hq = threadIdx.x >> 5, d4 = threadIdx.x & 31;
-        const float4 v = __ldcg(reinterpret_cast<const float4 *>(p.q + (size_t)(kvh * 4 + hq) * kHeadDim) + d4);
-        *reinterpret_cast<float4 *>(qs + (hq * 4 + (d4 >> 3)) * kQStride + (d4 & 7) * 4) = v;
+    // this layer's q rows of the four query heads and the position's k, v rows,
+    // polled from the tagged words the qkv epilogues write (224 threads, 4 words each)
+    {
+        const unsigned long long *src;
+        float *dst;
+        if (threadIdx.x < 128) {
+            const int hq = threadIdx.x >> 5, d4 = threadIdx.x & 31;
+            src = p.qkvt + (size_t)(kvh * 4 + hq) * kHeadDim + 4 * d4;
+            dst = qs + (hq * 4 + (d4 >> 3)) * kQStride + (d4 & 7) * 4;
+        } else if (threadIdx.x < 160) {
+            src = p.qkvt + kQuery + kvh * kHeadDim + 4 * (threadIdx.x - 128);
+            dst = kcur + 4 * (threadIdx.x - 128);
+        } else if (threadIdx.x < 192) {
+            src = p.qkvt + kQuery + kKV + kvh * kHeadDim + 4 * (threadIdx.x - 160);
+            dst = vcur + 4 * (threadIdx.x - 160);
+        } else {
+            src = nullptr;
+            dst = nullptr;
+        }
+        if (src) *reinterpret_cast<float4 *>(dst) = poll_tagged4(src, tag, p.error);
     }
     consumers_sync();
+    attention_patch(p0, length, kcur, vcur, kk, vv);
     float m_run[4], l_run[4];
     float4 o[4];
 #pragma unroll
@@ -631,7 +688,10 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
         o[hq] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     for (; p0 < end; p0 += 8 * kMegaConsumerWarps) {
-        if (p0 != begin + 8 * warp) attention_load(p, layer, kvh, p0, end, kk, vv);
+        if (p0 != begin + 8 * warp) {
+            attention_load(p, layer, kvh, p0, end, kk, vv);
+            attention_patch(p0, length, kcur, vcur, kk, vv);
+        }
         const bool valid = pp < min(8, end - p0);
         float pr[4];
 #pragma unroll
@@ -812,8 +872,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
             gp.scale[2] = sc[2];
             gp.bound[0] = kQuery;
             gp.bound[1] = kQuery + kKV;
-            gp.y = p.q;
-            gp.y_stride = kQuery;
+            gp.qkv_tagged = p.qkvt;
+            gp.ytag = p.tag_base + epoch - 1;
             const int mk = layer * kMarksPerLayer;
             float inv = stage_frag<kHidden>(frag, p.x, layer == 0 ? emb_row : nullptr,
                                             p.norms + (size_t)(2 * layer) * kHidden, red);
@@ -825,21 +885,15 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
             consumers_sync();
             if (threadIdx.x == 0) record_mark(p, rec, mk + 1);
             fp8_epilogue<kEpiQKV>(gp, sp, kHidden / kBlockCols / item_blocks(kPhQKV), partial, inv);
-            consumers_sync();
-            if (threadIdx.x == 0) {
-                // publish this CTA's tiles to their KV-head groups (runs of equal group)
-                const int t1 = sp.first + sp.items / (kHidden / kBlockCols / item_blocks(kPhQKV));
-                for (int t = sp.first; t < t1;) {
-                    const int g = qkv_group(t);
-                    int n = 0;
-                    for (; t < t1 && qkv_group(t) == g; t++) n++;
-                    signal_word(sync_word(p, kSyncQKV + g), (unsigned)n);
-                }
-                record_mark(p, rec, mk + 2);
+            gp.qkv_tagged = nullptr;
+            if (rec) {
+                consumers_sync();
+                if (threadIdx.x == 0) record_mark(p, rec, mk + 2);
             }
             if (unit >= 0) {
                 float *qs = reinterpret_cast<float *>(frag);
-                cta_attention(p, layer, length, unit, ranges, epoch, tickets, qs, qs + 16 * kQStride, &flag, rec);
+                cta_attention(p, layer, length, unit, ranges, epoch, gp.ytag, tickets, qs,
+                              qs + 16 * kQStride + 2 * kHeadDim, &flag, rec);
                 consumers_sync();
             }
             if (ranges > 1) tickets += (unsigned)ranges;

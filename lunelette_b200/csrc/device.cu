@@ -58,6 +58,8 @@ struct lun_device {
     bool use_mega = true;
     float *d_scales = nullptr;          // [26][7]
     unsigned *mega_sync = nullptr;      // kSyncWords lines, zeroed before every launch
+    unsigned long long *mega_qkvt = nullptr;  // tagged q/k/v words the persistent kernel exchanges
+    unsigned mega_tag = 1;                    // tag of the next launch's first layer (never 0)
     unsigned l2_ahead = 0;              // persistent kernel's L2 lookahead (bytes per CTA)
     int *mega_error = nullptr, *h_error = nullptr;
     float *arg_val = nullptr;
@@ -167,12 +169,14 @@ extern "C" lun_device *lun_device_create(size_t context, size_t block, char *err
         (e = dalloc(&d->d_flag, 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->d_scales, (size_t)kLayers * LUN_SLOT_COUNT * 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->mega_sync, kSyncWords * kSyncStride * sizeof(unsigned), sc)) != cudaSuccess ||
+        (e = dalloc(&d->mega_qkvt, (size_t)kQKVRows * sizeof(unsigned long long), sc)) != cudaSuccess ||
         (e = dalloc(&d->mega_error, sizeof(int), sc)) != cudaSuccess ||
         (e = dalloc(&d->arg_val, (size_t)d->sm_count * 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->arg_idx, (size_t)d->sm_count * 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->d_tokens, context * sizeof(int), sc)) != cudaSuccess)
         goto bad;
-    if ((e = cudaMemset(d->mega_error, 0, sizeof(int))) != cudaSuccess)
+    if ((e = cudaMemset(d->mega_error, 0, sizeof(int))) != cudaSuccess ||
+        (e = cudaMemset(d->mega_qkvt, 0, (size_t)kQKVRows * sizeof(unsigned long long))) != cudaSuccess)
         goto bad;
     {
         const char *mega = getenv("LUNELETTE_MEGA");
@@ -241,6 +245,7 @@ extern "C" void lun_device_destroy(lun_device *d)
     cudaFree(d->d_partials);
     cudaFree(d->d_scales);
     cudaFree(d->mega_sync);
+    cudaFree(d->mega_qkvt);
     cudaFree(d->mega_error);
     cudaFree(d->arg_val);
     cudaFree(d->arg_idx);
@@ -508,7 +513,17 @@ static cudaError_t launch_mega(lun_device *d, int steps)
     p.step = d->d_step;
     p.x = d->x;
     p.h = d->h;
-    p.q = d->q;
+    // tags of this launch's layers: mega_tag .. mega_tag + 26 * steps - 1; a
+    // wrap restarts from 1 over freshly zeroed words, so no old word matches
+    const unsigned long long span = (unsigned long long)steps * kLayers;
+    if ((unsigned long long)d->mega_tag + span >= 0xffffffffull) {
+        cudaError_t z = cudaMemsetAsync(d->mega_qkvt, 0, (size_t)kQKVRows * sizeof(unsigned long long), d->stream);
+        if (z != cudaSuccess) return z;
+        d->mega_tag = 1;
+    }
+    p.qkvt = d->mega_qkvt;
+    p.tag_base = d->mega_tag;
+    d->mega_tag += (unsigned)span;
     p.attn = d->attn;
     p.act = d->act;
     p.part_acc = d->part_acc;

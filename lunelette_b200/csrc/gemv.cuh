@@ -190,7 +190,22 @@ struct GemvParams {
     const float *rope_row;
     const float *res_shared;
     int res_base;
+    // One-token QKV epilogue for readers on other CTAs: q rows and the
+    // position's k and v rows also go out as tagged words (store_tagged) to
+    // qkv_tagged[0..4096) (q), [4096..5120) (k), [5120..6144) (v), tag ytag;
+    // q then skips y.
+    unsigned long long *qkv_tagged;
+    unsigned ytag;
 };
+
+// A value and the tag of the phase that produced it in one 64-bit word: a
+// reader that sees the expected tag sees the value written with it (a single
+// aligned 8-byte store), so no separate flag, fence or counter is needed.
+__device__ __forceinline__ void store_tagged(unsigned long long *dst, float v, unsigned tag)
+{
+    const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
+    asm volatile("st.global.u64 [%0], %1;" ::"l"(dst), "l"(w) : "memory");
+}
 
 // Stage M activation rows (normed when p.gain) as hi/lo B fragments for the
 // whole block; inv_scale[m] = 2^-e of row m. red: 16 * M floats of scratch.
@@ -333,8 +348,13 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, int g, int la
                 }
                 if (ra < kQuery) {
                     float qs = query_scale(pos);
-                    p.y[(size_t)m * p.y_stride + ra] = a * qs;
-                    p.y[(size_t)m * p.y_stride + rb] = b * qs;
+                    if (p.qkv_tagged) {
+                        store_tagged(p.qkv_tagged + ra, a * qs, p.ytag);
+                        store_tagged(p.qkv_tagged + rb, b * qs, p.ytag);
+                    } else {
+                        p.y[(size_t)m * p.y_stride + ra] = a * qs;
+                        p.y[(size_t)m * p.y_stride + rb] = b * qs;
+                    }
                 } else {
                     int kind = ra < kQuery + kKV ? 0 : 1;
                     int head = (ra - kQuery - kind * kKV) >> 7;
@@ -342,6 +362,10 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, int g, int la
                     float *dst = p.kv + kv_offset(p.layer, p.num_pages, page, kind, head, slot);
                     dst[j] = a;
                     dst[j + 64] = b;
+                    if (p.qkv_tagged) {
+                        store_tagged(p.qkv_tagged + ra, a, p.ytag);
+                        store_tagged(p.qkv_tagged + rb, b, p.ytag);
+                    }
                 }
             }
         }

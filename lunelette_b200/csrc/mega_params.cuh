@@ -7,12 +7,13 @@ namespace lun {
 
 // Grid barriers per decode step: three per layer (after o, once h is whole;
 // after gate/up; after down, once x is whole) and one after the head and the
-// pick. qkv -> attention -> o use counters instead (kSyncQKV, kSyncAttn).
+// pick. qkv -> attention goes through tagged words (the attention CTAs poll the
+// q, k and v values themselves), attention -> o through a counter (kSyncAttn).
 constexpr int kMegaBarriersPerStep = kLayers * 3 + 1;
 // Timeline of the first step of a launch: [0] start, [1 + k] CTA 0 leaving
 // barrier k, then from kMegaTimelineHead one entry per CTA b for each mark m at
 // kMegaTimelineHead + m * gridDim.x + b. Marks per layer L, at 13L + :
-//   0 qkv row staged, 1 qkv items done, 2 q/k/v tiles published,
+//   0 qkv row staged, 1 qkv items done, 2 q/k/v stored (tagged),
 //   3 attention published (CTAs that own a unit, else 0),
 //   4 o row staged, 5 o items done, 6 arrival at the o barrier,
 //   7 gate/up row staged, 8 items done, 9 arrival at the gate/up barrier,
@@ -25,15 +26,13 @@ constexpr int kMegaTimelineHead = 1 + kMegaBarriersPerStep;
 // Synchronisation words of one launch, each on its own 128-byte line, zero at
 // launch and only ever increased (targets grow with the layers the launch ran):
 //   kSyncBarrier        grid barrier arrivals (gridDim per barrier)
-//   kSyncQKV + kvh      q/k/v tiles of KV head kvh's group stored (96 per layer)
 //   kSyncAttn           KV heads whose attention output is stored (8 per layer)
 //   kSyncTicket + kvh   attention ranges of KV head kvh finished
 //   kSyncPick           CTAs done with the head (gridDim per step)
 constexpr int kSyncStride = 32;
 enum : int {
     kSyncBarrier = 0,
-    kSyncQKV = 1,
-    kSyncAttn = kSyncQKV + kKVHeads,
+    kSyncAttn = 1,
     kSyncTicket = kSyncAttn + 1,
     kSyncPick = kSyncTicket + kKVHeads,
     kSyncWords = kSyncPick + 1,
@@ -50,7 +49,9 @@ struct MegaParams {
     int num_pages;
     const float *rope_cos, *rope_sin;
     StepParams *step;        // length and ids[0] advance on the device each step
-    float *x, *h, *q, *attn, *act;
+    float *x, *h, *attn, *act;
+    unsigned long long *qkvt;  // the step's q (4096) and k, v (1024 each) of the current layer, tagged
+    unsigned tag_base;         // tag of this launch's first layer (step s, layer L: tag_base + 26 s + L)
     float *part_acc, *part_ml;  // [8 KV heads][ranges][4 query heads][128] and [..][2]
     float *logits;
     int *nonfinite;
