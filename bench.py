@@ -5,11 +5,14 @@ seeded random-init checkpoint, batch 1, a 32-token prompt of ids ~ U[1000,
 131072), greedy decode at context profile 256. A "step" is one greedy decode
 token. The timed region is R rounds of: restore the 32-token prompt checkpoint
 (host-only, no device work) and decode 31 greedy tokens on the device
-(lunelette_cuda_decode_loop: one captured CUDA graph per token, argmax fed back
-on the GPU). `value` = decode tokens/s from CUDA events (max over ranks, all
-ranks' tokens summed); `e2e` = the same metric through the drop-in C-ABI with
-host buffers (lunelette_metal_decode + host greedy each token, H2D of the step
-parameters and D2H of the 131072 logits inside the timed region).
+(lunelette_cuda_decode_loop: one launch of the persistent decode kernel for the
+31 tokens, argmax fed back on the GPU). `value` = decode tokens/s from CUDA
+events (max over ranks, all ranks' tokens summed); `e2e` = the same metric
+through the drop-in C-ABI with host buffers (lunelette_metal_decode + host
+greedy each token: one persistent-kernel launch per token, H2D of the step
+parameters and D2H of the 131072 logits inside the timed region). `roofline`
+is the persistent kernel's: the algorithmic bytes of a launch (FP8 linears,
+BF16 head, norm gains and the FP32 KV rows read) over its CUDA-event time.
 
 Multi-GPU: one process per GPU (torchrun), each an independent weight replica
 and session ("replicas only": the model has no collective), so scaling is weak.
@@ -36,9 +39,13 @@ METRIC = "decode tok/s (batch 1 and aggregate) + prefill tok/s, % of HBM/FP8 roo
 PROMPT = 32
 CONTEXT = 256
 WEIGHT_BYTES_PER_TOKEN = 3026190336 + 805306368 + 53 * 3072 * 4  # FP8 linears + BF16 head + norms
-KV_BYTES_PER_POSITION = 26 * 2 * 1024 * 2                         # BF16 K and V, all layers
+KV_BYTES_PER_POSITION = 26 * 2 * 1024 * 4                         # FP32 K and V, all layers
 GATEUP_BYTES = 18432 * 3072                                       # one fused gate/up launch
 HEAD_BYTES = 131072 * 3072 * 2
+# DRAM read + write bytes of one C0 decode token: ncu capture of a one-token
+# launch of decode_mega_kernel at context 34 (profiles/decode_mega_c0_token.md:
+# 3,839,687,168 read + 7,772,160 written)
+DRAM_BYTES_PER_TOKEN = 3839687168 + 7772160
 
 
 def env_int(name, default):
@@ -163,6 +170,15 @@ def gateup_roofline(lib, torch, checkpoint, launches=40):
     return ms, algorithmic
 
 
+def traffic_per_launch(steps):
+    """DRAM bytes (read + write) of a persistent-kernel launch of `steps` tokens,
+    from the ncu capture summarised in profiles/ (one single-token launch on the
+    C0 workload, scaled by the token count: the kernel's traffic is per token),
+    or None when no capture has been summarised."""
+    per_token = DRAM_BYTES_PER_TOKEN
+    return None if per_token is None else per_token * steps
+
+
 def cpu_baseline(checkpoint, prompt, decode_steps=6):
     """The CPU oracle (C restatement of the reference kernels, OpenMP) on this
     box's host cores: the C0 prompt, then `decode_steps` greedy decode steps."""
@@ -275,9 +291,9 @@ def run_ours(args, rank, world, local_rank):
     with ClockSampler(local_rank) as clocks:
         t0 = time.perf_counter()
         for r in range(rounds):
-            tokens, ms, per_step = rt.decode_loop(first, per_round)
+            tokens, ms, n = rt.decode_loop(first, per_round)
             device_ms += ms
-            launches += per_step * per_round
+            launches += n
             rt.checkpoint_restore(cp)
             tokens_seen = tokens
         torch.cuda.synchronize()
@@ -326,12 +342,13 @@ def run_ours(args, rank, world, local_rank):
     rt.close()
 
     hbm, bf16, peak_kind = measured_peaks()
-    kernel_ms, algorithmic = gateup_roofline(lib, torch, checkpoint)
-    achieved = algorithmic / (kernel_ms / 1000) / 1e9
+    gemv_ms, gemv_bytes = gateup_roofline(lib, torch, checkpoint)
     ms_per_step = device_ms / steps
     mean_ctx = PROMPT + (per_round + 1) / 2
     step_bytes = WEIGHT_BYTES_PER_TOKEN + KV_BYTES_PER_POSITION * mean_ctx
-    step_gbs = step_bytes / (ms_per_step / 1000) / 1e9
+    launch_ms = device_ms / launches            # one persistent-kernel launch per round
+    launch_bytes = step_bytes * steps / launches
+    achieved = launch_bytes / (launch_ms / 1000) / 1e9
 
     if rank == 0:
         line = {
@@ -350,11 +367,15 @@ def run_ours(args, rank, world, local_rank):
             "prefill_tok_s": {"chunk_256": 256 / prefill_256, "prompt_32": PROMPT / prefill_32,
                               "note": "lunelette_metal_prefill wall time, host ids and logits"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "traffic": None, "peak_kind": peak_kind,
-                         "kernel": "gemv_tiled_kernel<1,kEpiSwiGLU> (fused norm + gate/up + SwiGLU)",
-                         "algorithmic_bytes": algorithmic, "avg_launch_ms": kernel_ms},
-            "step_roofline": {"bytes_per_token": step_bytes, "achieved_gbs": step_gbs, "peak": hbm,
-                              "frac": step_gbs / hbm, "peak_kind": peak_kind},
+                         "frac": achieved / hbm, "traffic": traffic_per_launch(per_round), "peak_kind": peak_kind,
+                         "kernel": "decode_mega_kernel (persistent: %d greedy tokens per launch)" % per_round,
+                         "algorithmic_bytes": launch_bytes, "avg_launch_ms": launch_ms,
+                         "bytes_per_token": step_bytes},
+            "gemv_roofline": {"kernel": "gemv_tiled_kernel<1,kEpiSwiGLU> (fused norm + gate/up + SwiGLU, "
+                                        "standalone launches, weights > L2)",
+                              "achieved": gemv_bytes / (gemv_ms / 1000) / 1e9, "unit": "GB/s",
+                              "frac": gemv_bytes / (gemv_ms / 1000) / 1e9 / hbm, "algorithmic_bytes": gemv_bytes,
+                              "avg_launch_ms": gemv_ms},
             "clocks": clocks.summary(),
             "gpu_launches": launches,
             "greedy_device_matches_host": same_tokens,

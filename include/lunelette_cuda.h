@@ -110,14 +110,16 @@ int lunelette_cuda_trace(lunelette_metal *context, int enable);
 int lunelette_cuda_trace_copy(lunelette_metal *context, int which, float *out, size_t floats);
 /* Device-resident greedy decode for throughput measurement: decode `first_token`
  * and then keep feeding each step's argmax (strict '>', lowest id on ties, as
- * src/generation.c:8-34) back on the GPU, `steps` steps in all, each one replay
- * of a captured CUDA graph; no host round trip between steps. On success the
- * sequence length grows by `steps`, tokens[0..steps) holds the generated ids,
- * *milliseconds the CUDA-event time of the replays and *launches_per_step the
- * kernel launches in one step. Host logits are not refreshed, so no endpoint is
- * published (checkpoint_create needs another prefill/append/decode first). */
+ * src/generation.c:8-34) back on the GPU, `steps` steps in all, with no host
+ * round trip between steps: one launch of the persistent decode kernel for all
+ * steps, or (LUNELETTE_MEGA=0) one replay of a captured CUDA graph per step.
+ * On success the sequence length grows by `steps`, tokens[0..steps) holds the
+ * generated ids, *milliseconds the CUDA-event time of the call's device work
+ * and *launches the kernel launches it made. Host logits are not refreshed, so
+ * no endpoint is published (checkpoint_create needs another prefill/append/decode
+ * first). */
 int lunelette_cuda_decode_loop(lunelette_metal *context, int64_t first_token, size_t steps,
-    int64_t *tokens, float *milliseconds, int *launches_per_step, char *error, size_t capacity);
+    int64_t *tokens, float *milliseconds, int *launches, char *error, size_t capacity);
 
 /* Phase timing of the persistent decode kernel: while enabled, the first step of
  * each launch records %globaltimer (ns) at its start (entry 0) and as CTA 0

@@ -222,7 +222,7 @@ class Runtime:
 
     def decode_loop(self, first_token, steps):
         """Device-resident greedy decode; returns (tokens, device milliseconds,
-        kernel launches per step)."""
+        kernel launches the call made)."""
         tokens = np.empty(steps, np.int64)
         ms = ctypes.c_float()
         launches = ctypes.c_int()

@@ -663,7 +663,7 @@ extern "C" int lun_device_decode_loop(lun_device *d, int64_t first_token, size_t
         goto bad;
     for (size_t s = 0; s < steps; s++) tokens[s] = host_tokens[s];
     free(host_tokens);
-    if (launches) *launches = d->launches_per_step;
+    if (launches) *launches = d->use_mega ? 1 : d->launches_per_step * (int)steps;
     cudaEventDestroy(start);
     cudaEventDestroy(stop);
     return 0;

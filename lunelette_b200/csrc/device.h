@@ -60,7 +60,7 @@ float *lun_device_host_logits(lun_device *d);
  * `first_token` at sequence length `length` (a valid prefix must already be in
  * the KV cache), each step one replay of a captured CUDA graph whose last
  * kernels pick the argmax and feed it to the next step. Writes the generated
- * ids, the CUDA-event time of all replays and the kernel launches per step. */
+ * ids, the CUDA-event time of the call and the kernel launches it made. */
 int lun_device_decode_loop(lun_device *d, int64_t first_token, size_t length, size_t steps,
     int64_t *tokens, float *milliseconds, int *launches, char *error, size_t capacity);
 

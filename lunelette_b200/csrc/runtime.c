@@ -526,7 +526,7 @@ LUN_API size_t lunelette_cuda_length(const lunelette_metal *context)
 }
 
 LUN_API int lunelette_cuda_decode_loop(lunelette_metal *context, int64_t first_token, size_t steps,
-    int64_t *tokens, float *milliseconds, int *launches_per_step, char *error, size_t capacity)
+    int64_t *tokens, float *milliseconds, int *launches, char *error, size_t capacity)
 {
     char fallback[512];
     if (!error || !capacity) {
@@ -545,7 +545,7 @@ LUN_API int lunelette_cuda_decode_loop(lunelette_metal *context, int64_t first_t
     context->endpoint_valid = false;
     context->valid = false;
     if (lun_device_decode_loop(context->device, first_token, context->length, steps, tokens,
-            milliseconds, launches_per_step, error, capacity)) {
+            milliseconds, launches, error, capacity)) {
         return -1;
     }
     /* The KV cache now holds `steps` more positions; the host logits were not

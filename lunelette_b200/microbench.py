@@ -163,15 +163,32 @@ def decode_phases(checkpoint, steps=8, prompt=32):
     return out
 
 
+def decode_tokens(checkpoint, steps, prompt=32):
+    """A small profiling target: the C0 prompt, then `steps` greedy tokens through
+    lunelette_metal_decode (one persistent-kernel launch each)."""
+    import lunelette_b200 as L
+    with L.Runtime(checkpoint) as rt:
+        ids = np.random.default_rng(7).integers(1000, 131072, prompt)
+        tok = int(np.argmax(rt.prefill(ids)))
+        for _ in range(steps):
+            tok = int(np.argmax(rt.decode(tok)))
+    return tok
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--shapes", default=",".join(SHAPES))
     ap.add_argument("--m", default="1,2,4,8")
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--decode-tokens", nargs=2, metavar=("CHECKPOINT", "N"), default=None,
+                    help="run the C0 prompt and N single-token decode launches (a profiling target)")
     ap.add_argument("--decode-phases", metavar="CHECKPOINT", default=None,
                     help="time the persistent decode kernel's phases on this checkpoint instead")
     args = ap.parse_args()
+    if args.decode_tokens:
+        print(json.dumps({"last_token": decode_tokens(args.decode_tokens[0], int(args.decode_tokens[1]))}))
+        return
     if args.decode_phases:
         for r in decode_phases(args.decode_phases):
             print(json.dumps(r))
