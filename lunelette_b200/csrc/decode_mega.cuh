@@ -20,9 +20,10 @@
 // Item i of the CTA's stream goes to consumer warp i mod 7, which owns
 // kSlotsPerWarp private slots and takes its items strictly in order, so every
 // slot's full and empty barriers are waited on in phase order by one waiter.
-// Phases per layer: qkv (norm + q/k/v + RoPE + KV store; each CTA then counts
-// its tiles into their KV-head groups), attention (one CTA per KV head and
-// position range, started by its group's count), o (+ residual; starts once the
+// Phases per layer: qkv (norm + q/k/v + RoPE + KV store; the epilogue also
+// writes q and the new k/v as 64-bit words tagged with the layer's tag),
+// attention (one CTA per KV head and position range, started when the tagged
+// q/k/v words it polls carry the current tag), o (+ residual; starts once the
 // eight attention results are counted, ends at a grid barrier), gate/up
 // (norm + SwiGLU), down (+ residual); then the head (final norm + tied BF16
 // GEMV) with a per-CTA argmax whose last CTA picks the token.
