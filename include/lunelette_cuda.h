@@ -68,6 +68,23 @@ int lunelette_cuda_qkv_rope(const uint8_t *W, const float *scales, const float *
 int lunelette_cuda_gateup_swiglu(const uint8_t *W, float scale_gate, float scale_up,
     const float *gain, const float *x, size_t count, float *act, void *stream);
 
+/* The same three projections on the tcgen05 tensor cores, the runtime's path
+ * for blocks of more than four tokens (prefill, append): activations split
+ * into FP16 hi + lo parts as above, FP8 weights converted to FP16 in shared
+ * memory, tcgen05.mma (M = 128 tokens, N = 256 rows, K = 16) accumulating both
+ * parts in TMEM (FP32), K ranges added in a fixed order. Same arguments and
+ * results as lunelette_cuda_gemv_fp8 / _qkv_rope / _gateup_swiglu (rows % 8 == 0
+ * here); each call allocates its workspace on the stream and synchronises it.
+ * Replaces the MPS prefill GEMMs (src/metal_mps.m:26-111). */
+int lunelette_cuda_gemm_fp8(const uint8_t *W, size_t rows, size_t cols, float scale,
+    const float *x, const float *res, size_t count, float *y, void *stream);
+int lunelette_cuda_gemm_qkv_rope(const uint8_t *W, const float *scales, const float *gain,
+    const float *x, size_t count, size_t length, const float *rope_cos, const float *rope_sin,
+    float *q_out, float *kv_pool, const int *page_table, size_t num_pages, size_t layer,
+    void *stream);
+int lunelette_cuda_gemm_gateup_swiglu(const uint8_t *W, float scale_gate, float scale_up,
+    const float *gain, const float *x, size_t count, float *act, void *stream);
+
 /* out = gain * (x * rsqrt(mean(x^2) + 1e-5)) per row (src/metal_kernels.metal:29-44). */
 int lunelette_cuda_rmsnorm(const float *gain, const float *x, size_t width, size_t count,
     float *out, void *stream);

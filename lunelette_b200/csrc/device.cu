@@ -65,6 +65,10 @@ struct lun_device {
     float *arg_val = nullptr;
     int *arg_idx = nullptr;
     bool prefetch = true;                        // next-matrix L2 prefetch
+    // blocks of more than kGemvMaxTokens tokens: tcgen05 GEMM projections
+    PrefillWorkspace pf = {};
+    bool use_gemm = true;
+    int *h_pf_error = nullptr;
     unsigned long long *timeline = nullptr;      // per-barrier timestamps (optional)
     bool record_timeline = false;
     lun_device_bytes owned = {};
@@ -88,6 +92,11 @@ extern "C" void lun_device_plan(size_t context, size_t block, lun_device_bytes *
     scratch += (uint64_t)kPartSlots * (kHeadDim + 2) * 4;                  // attention partials
     scratch += (uint64_t)context * kHeadDim * 2 * 4;                       // rope tables
     scratch += (uint64_t)pages_for(context) * 4 + 4;                        // page table + flag
+    if (block > kGemvMaxTokens) {  // prefill GEMM workspace (sized for a 148-SM B200)
+        size_t xs, inv, ws;
+        lun_prefill_workspace_bytes((int)block, 148, &xs, &inv, &ws);
+        scratch += xs + inv + ws + 4;
+    }
     bytes->scratch_bytes = scratch;
 }
 
@@ -175,12 +184,23 @@ extern "C" lun_device *lun_device_create(size_t context, size_t block, char *err
         (e = dalloc(&d->arg_idx, (size_t)d->sm_count * 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->d_tokens, context * sizeof(int), sc)) != cudaSuccess)
         goto bad;
+    if (block > kGemvMaxTokens) {
+        lun_prefill_workspace_bytes((int)block, d->sm_count, &d->pf.xs_bytes, &d->pf.inv_bytes, &d->pf.ws_bytes);
+        if ((e = dalloc(&d->pf.xs, d->pf.xs_bytes, sc)) != cudaSuccess ||
+            (e = dalloc(&d->pf.inv_scale, d->pf.inv_bytes, sc)) != cudaSuccess ||
+            (e = dalloc(&d->pf.ws, d->pf.ws_bytes, sc)) != cudaSuccess ||
+            (e = dalloc(&d->pf.error, sizeof(int), sc)) != cudaSuccess ||
+            (e = cudaMemset(d->pf.error, 0, sizeof(int))) != cudaSuccess)
+            goto bad;
+    }
     if ((e = cudaMemset(d->mega_error, 0, sizeof(int))) != cudaSuccess ||
         (e = cudaMemset(d->mega_qkvt, 0, (size_t)kQKVRows * sizeof(unsigned long long))) != cudaSuccess)
         goto bad;
     {
         const char *mega = getenv("LUNELETTE_MEGA");
         d->use_mega = !(mega && mega[0] == '0') && lun_mega_supported(d->sm_count);
+        const char *gemm = getenv("LUNELETTE_PREFILL_GEMM");
+        d->use_gemm = !(gemm && gemm[0] == '0') && d->pf.ws;
         const char *prefetch = getenv("LUNELETTE_PREFETCH");
         d->prefetch = !(prefetch && prefetch[0] == '0');
         // L2 lookahead of the persistent kernel's weight stream, per CTA; longer
@@ -193,6 +213,7 @@ extern "C" lun_device *lun_device_create(size_t context, size_t block, char *err
         (e = cudaMallocHost((void **)&d->h_logits, (size_t)kVocab * 4)) != cudaSuccess ||
         (e = cudaMallocHost((void **)&d->h_flag, 4)) != cudaSuccess ||
         (e = cudaMallocHost((void **)&d->h_error, 4)) != cudaSuccess ||
+        (e = cudaMallocHost((void **)&d->h_pf_error, 4)) != cudaSuccess ||
         (e = cudaMallocHost(&d->staging[0], kStagingBytes)) != cudaSuccess ||
         (e = cudaMallocHost(&d->staging[1], kStagingBytes)) != cudaSuccess ||
         (e = cudaEventCreateWithFlags(&d->staging_done[0], cudaEventDisableTiming)) != cudaSuccess ||
@@ -251,6 +272,11 @@ extern "C" void lun_device_destroy(lun_device *d)
     cudaFree(d->arg_idx);
     cudaFree(d->timeline);
     cudaFree(d->upload_raw);
+    cudaFree(d->pf.xs);
+    cudaFree(d->pf.inv_scale);
+    cudaFree(d->pf.ws);
+    cudaFree(d->pf.error);
+    cudaFreeHost(d->h_pf_error);
     cudaFreeHost(d->h_error);
     if (d->decode_graph) cudaGraphExecDestroy(d->decode_graph);
     cudaFreeHost(d->h_step);
@@ -433,8 +459,9 @@ static GemvParams layer_gemv(lun_device *d, int layer, int which)
 static cudaError_t run_projection(lun_device *d, int layer, int which, int count)
 {
     static const int epi[4] = {kEpiQKV, kEpiResidual, kEpiSwiGLU, kEpiResidual};
-    for (int t0 = 0; t0 < count; t0 += 4) {
-        int m = count - t0 < 4 ? count - t0 : 4;
+    const bool gemm = count > kGemvMaxTokens && d->use_gemm;
+    for (int t0 = 0; t0 < count; t0 += gemm ? count : kGemvMaxTokens) {
+        int m = count - t0 < kGemvMaxTokens ? count - t0 : kGemvMaxTokens;
         GemvParams p = layer_gemv(d, layer, which);
         p.token_offset = t0;
         switch (which) {
@@ -466,6 +493,10 @@ static cudaError_t run_projection(lun_device *d, int layer, int which, int count
             p.y = d->x + (size_t)t0 * kHidden;
             p.y_stride = kHidden;
             break;
+        }
+        if (gemm) {
+            p.prefetch = nullptr;  // the GEMM is tensor-bound; no next-matrix prefetch
+            return lun_launch_prefill(p, count, epi[which], d->pf, d->sm_count, d->stream);
         }
         cudaError_t e = lun_launch_gemv(p, m, epi[which], d->sm_count, d->stream);
         if (e != cudaSuccess) return e;
@@ -740,8 +771,16 @@ extern "C" int lun_device_run(lun_device *d, const int64_t *ids, size_t count, s
         (e = cudaMemcpyAsync(d->h_flag, d->d_flag, 4, cudaMemcpyDeviceToHost, d->stream)) !=
             cudaSuccess)
         goto bad;
+    if (d->pf.error &&
+        (e = cudaMemcpyAsync(d->h_pf_error, d->pf.error, 4, cudaMemcpyDeviceToHost, d->stream)) != cudaSuccess)
+        goto bad;
     what = "execution";
     if ((e = cudaStreamSynchronize(d->stream)) != cudaSuccess) goto bad;
+    if (d->pf.error && *d->h_pf_error) {
+        cudaMemset(d->pf.error, 0, sizeof(int));
+        if (error && capacity) snprintf(error, capacity, "prefill: GEMM pipeline wait gave up");
+        return -1;
+    }
     if (mega && *d->h_error) {
         cudaMemset(d->mega_error, 0, sizeof(int));
         if (error && capacity) snprintf(error, capacity, "decode: grid barrier wait gave up");

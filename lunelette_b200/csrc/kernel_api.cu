@@ -2,6 +2,7 @@
 // so tests can check each one against the CPU oracle on awkward shapes.
 // Return 0 on success, -1 on invalid arguments or a CUDA launch error.
 #include "kernels.h"
+#include "prefill_gemm.cuh"
 
 #include <string.h>
 
@@ -155,6 +156,99 @@ LUN_API int lunelette_cuda_gateup_swiglu(const uint8_t *W, float scale_gate, flo
         if (lun_launch_gemv(p, m, kEpiSwiGLU, sms, (cudaStream_t)stream) != cudaSuccess) return -1;
     }
     return 0;
+}
+
+// One projection through the tcgen05 prefill path with workspace allocated
+// for this call (stream-ordered); -1 also when a bounded wait inside the GEMM
+// gave up. Synchronises the stream.
+static int run_prefill(const GemvParams &p, size_t count, int epilogue, cudaStream_t stream)
+{
+    if (!count || count > 65536) return -1;
+    const int sms = sm_count_of_current();
+    const PrefillPlan pl = lun_prefill_plan(p.rows, p.cols, (int)count, sms);
+    PrefillWorkspace w;
+    memset(&w, 0, sizeof w);
+    w.xs_bytes = (size_t)pl.token_tiles * pl.kchunks * 2 * kPgATile;
+    w.inv_bytes = (size_t)pl.token_tiles * kPgM * sizeof(float);
+    w.ws_bytes = (size_t)pl.splits * pl.token_tiles * kPgM * pl.row_tiles * kPgN * sizeof(float);
+    int rc = -1, error = 0;
+    if (cudaMallocAsync((void **)&w.xs, w.xs_bytes, stream) == cudaSuccess &&
+        cudaMallocAsync((void **)&w.inv_scale, w.inv_bytes, stream) == cudaSuccess &&
+        cudaMallocAsync((void **)&w.ws, w.ws_bytes, stream) == cudaSuccess &&
+        cudaMallocAsync((void **)&w.error, sizeof(int), stream) == cudaSuccess &&
+        cudaMemsetAsync(w.error, 0, sizeof(int), stream) == cudaSuccess &&
+        lun_launch_prefill(p, (int)count, epilogue, w, sms, stream) == cudaSuccess &&
+        cudaMemcpyAsync(&error, w.error, sizeof(int), cudaMemcpyDeviceToHost, stream) == cudaSuccess &&
+        cudaStreamSynchronize(stream) == cudaSuccess)
+        rc = error ? -1 : 0;
+    if (w.xs) cudaFreeAsync(w.xs, stream);
+    if (w.inv_scale) cudaFreeAsync(w.inv_scale, stream);
+    if (w.ws) cudaFreeAsync(w.ws, stream);
+    if (w.error) cudaFreeAsync(w.error, stream);
+    return rc;
+}
+
+// lunelette_cuda_gemv_fp8 through the tcgen05 prefill GEMM.
+LUN_API int lunelette_cuda_gemm_fp8(const uint8_t *W, size_t rows, size_t cols, float scale, const float *x,
+                                    const float *res, size_t count, float *y, void *stream)
+{
+    if (!W || !x || !y || !rows || (rows % 8) || !cols || (cols % 16) || rows > (1u << 24) || cols > 65536)
+        return -1;
+    GemvParams p = plain(W, rows, cols, scale);
+    p.x = x;
+    p.x_stride = (int)cols;
+    p.y = y;
+    p.y_stride = (int)rows;
+    p.res = res;
+    p.res_stride = (int)rows;
+    return run_prefill(p, count, res ? kEpiResidual : kEpiStore, (cudaStream_t)stream);
+}
+
+// lunelette_cuda_qkv_rope through the tcgen05 prefill GEMM.
+LUN_API int lunelette_cuda_gemm_qkv_rope(const uint8_t *W, const float *scales, const float *gain,
+                                         const float *x, size_t count, size_t length, const float *rope_cos,
+                                         const float *rope_sin, float *q_out, float *kv_pool,
+                                         const int *page_table, size_t num_pages, size_t layer, void *stream)
+{
+    if (!W || !scales || !gain || !x || !count || !rope_cos || !rope_sin || !q_out || !kv_pool ||
+        !page_table || !num_pages || length + count > num_pages * kPage)
+        return -1;
+    GemvParams p = plain(W, kQKVRows, kHidden, 1.0f);
+    p.scale[0] = scales[0];
+    p.scale[1] = scales[1];
+    p.scale[2] = scales[2];
+    p.bound[0] = kQuery;
+    p.bound[1] = kQuery + kKV;
+    p.gain = gain;
+    p.x = x;
+    p.x_stride = kHidden;
+    p.y = q_out;
+    p.y_stride = kQuery;
+    p.length = (int)length;
+    p.rope_cos = rope_cos;
+    p.rope_sin = rope_sin;
+    p.kv = kv_pool;
+    p.page_table = page_table;
+    p.num_pages = (int)num_pages;
+    p.layer = (int)layer;
+    return run_prefill(p, count, kEpiQKV, (cudaStream_t)stream);
+}
+
+// lunelette_cuda_gateup_swiglu through the tcgen05 prefill GEMM.
+LUN_API int lunelette_cuda_gemm_gateup_swiglu(const uint8_t *W, float scale_gate, float scale_up,
+                                              const float *gain, const float *x, size_t count, float *act,
+                                              void *stream)
+{
+    if (!W || !gain || !x || !act || !count) return -1;
+    GemvParams p = plain(W, kGateUpRows, kHidden, 1.0f);
+    p.scale[0] = scale_gate;
+    p.scale[1] = scale_up;
+    p.gain = gain;
+    p.x = x;
+    p.x_stride = kHidden;
+    p.y = act;
+    p.y_stride = kInner;
+    return run_prefill(p, count, kEpiSwiGLU, (cudaStream_t)stream);
 }
 
 LUN_API int lunelette_cuda_rmsnorm(const float *gain, const float *x, size_t width, size_t count,

@@ -15,7 +15,8 @@ cudaError_t lun_kernels_ensure();
 cudaError_t lun_launch_tile_fp8(const uint8_t *src, int rows, int cols, uint8_t *dst, int dst_nb, int order,
                                 int row0, cudaStream_t stream);
 
-// GEMV family over a tiled matrix: m token rows (1..4), epilogue kind lun::GemvEpilogue.
+// GEMV family over a tiled matrix: m token rows (1..kGemvMaxTokens), epilogue kind lun::GemvEpilogue.
+constexpr int kGemvMaxTokens = 4;
 cudaError_t lun_launch_gemv(const lun::GemvParams &p, int m, int epilogue, int sm_count,
                             cudaStream_t stream);
 cudaError_t lun_launch_head(const lun::HeadParams &p, int sm_count, cudaStream_t stream);
@@ -53,3 +54,25 @@ bool lun_mega_supported(int sm_count);
 // FP8 codes -> FP32 * scale through the same in-register conversion as the GEMV.
 cudaError_t lun_launch_fp8_decode(const uint8_t *codes, size_t n, float scale, float *out,
                                   cudaStream_t stream);
+
+// Prefill projections on the tcgen05 tensor cores (prefill_gemm.cuh): split
+// activations, GEMM into per-K-range partials, ordered finish + fused epilogue.
+struct PrefillPlan {
+    int row_tiles, token_tiles, kchunks, splits;
+};
+PrefillPlan lun_prefill_plan(int rows, int cols, int count, int sm_count);
+struct PrefillWorkspace {
+    uint8_t *xs;        // split activation tiles
+    float *inv_scale;   // per-token 2^-e
+    float *ws;          // FP32 partials
+    int *error;         // set when a bounded wait inside the GEMM gave up
+    size_t xs_bytes, inv_bytes, ws_bytes;
+};
+// Workspace sizes covering the model's four projections for up to max_count tokens.
+void lun_prefill_workspace_bytes(int max_count, int sm_count, size_t *xs_bytes, size_t *inv_bytes,
+                                 size_t *ws_bytes);
+// The projection of p (GemvParams fields: W tiled, rows % 8 == 0, cols % 16 == 0,
+// x, gain, scales, y, res, RoPE/KV fields) for `count` tokens with a
+// lun::GemvEpilogue, positions from p.step->length (or p.length + p.token_offset).
+cudaError_t lun_launch_prefill(const lun::GemvParams &p, int count, int epilogue, const PrefillWorkspace &w,
+                               int sm_count, cudaStream_t stream);

@@ -95,7 +95,7 @@ def test_fp8_decode_bit_exact_all_codes(lib, torch_cuda):
         assert np.array_equal(got[~nan].view(np.uint32), want[~nan].view(np.uint32)), scale
 
 
-def gemv_check(lib, oracle, torch, rows, cols, count, seed, residual=False):
+def gemv_check(lib, oracle, torch, rows, cols, count, seed, residual=False, entry="lunelette_cuda_gemv_fp8"):
     rng = np.random.default_rng(seed)
     codes = finite_codes(rng, (rows, cols))
     scale = float(bf16_round(np.float32(0.0003 + rng.random() * 0.01)))
@@ -104,8 +104,8 @@ def gemv_check(lib, oracle, torch, rows, cols, count, seed, residual=False):
     d_w, d_x = tiled(lib, torch, codes), dev(torch, x)
     d_r = dev(torch, res) if residual else None
     y = torch.empty((count, rows), dtype=torch.float32, device="cuda")
-    rc = lib.lunelette_cuda_gemv_fp8(ptr(d_w), rows, cols, scale, ptr(d_x),
-                                     ptr(d_r) if residual else None, count, ptr(y), stream(torch))
+    rc = getattr(lib, entry)(ptr(d_w), rows, cols, scale, ptr(d_x),
+                             ptr(d_r) if residual else None, count, ptr(y), stream(torch))
     assert rc == 0
     got = y.cpu().numpy()
     w64 = e4m3_table(oracle)[codes].astype(np.float64) * scale
@@ -131,6 +131,31 @@ def test_gemv_fp8_matches_oracle(lib, oracle, torch_cuda, rows, cols, count):
 
 def test_gemv_fp8_residual(lib, oracle, torch_cuda):
     gemv_check(lib, oracle, torch_cuda, 3072, 4096, 3, seed=11, residual=True)
+
+
+# The tcgen05 prefill GEMM: one and two 128-token tiles, partial row tiles
+# (rows % 256 != 0), K ranges split across CTAs, K not a multiple of 64.
+@pytest.mark.parametrize("rows,cols,count", [
+    (256, 64, 1), (264, 3072, 5), (40, 112, 7), (3072, 4096, 130), (6144, 3072, 256),
+    (3072, 9216, 37), (18432, 3072, 200), (1024, 3072, 128), (512, 9216, 129)])
+def test_gemm_fp8_matches_oracle(lib, oracle, torch_cuda, rows, cols, count):
+    gemv_check(lib, oracle, torch_cuda, rows, cols, count, seed=rows * 5 + cols + count,
+               entry="lunelette_cuda_gemm_fp8")
+
+
+def test_gemm_fp8_residual(lib, oracle, torch_cuda):
+    gemv_check(lib, oracle, torch_cuda, 3072, 4096, 77, seed=12, residual=True, entry="lunelette_cuda_gemm_fp8")
+
+
+def test_gemm_rejects_unsupported_shapes(lib, torch_cuda):
+    torch = torch_cuda
+    w = torch.zeros(1 << 16, dtype=torch.uint8, device="cuda")
+    x = torch.zeros(1 << 16, dtype=torch.float32, device="cuda")
+    y = torch.zeros(1 << 16, dtype=torch.float32, device="cuda")
+    s = stream(torch)
+    assert lib.lunelette_cuda_gemm_fp8(ptr(w), 12, 64, 1.0, ptr(x), None, 1, ptr(y), s) == -1  # rows % 8
+    assert lib.lunelette_cuda_gemm_fp8(ptr(w), 16, 24, 1.0, ptr(x), None, 1, ptr(y), s) == -1  # cols % 16
+    assert lib.lunelette_cuda_gemm_fp8(ptr(w), 16, 64, 1.0, ptr(x), None, 0, ptr(y), s) == -1  # no tokens
 
 
 @pytest.mark.parametrize("k", [16, 32, 48, 64, 3072, 9216])
@@ -225,10 +250,15 @@ def kv_rows(pool_np, page_table, num_pages, layer, kind, positions):
 
 
 
-def test_qkv_rope_kv_store_matches_oracle(lib, oracle, torch_cuda):
+@pytest.mark.parametrize("entry,count,length", [
+    ("lunelette_cuda_qkv_rope", 6, 61),        # positions 61..66 cross a page boundary
+    ("lunelette_cuda_gemm_qkv_rope", 6, 61),
+    ("lunelette_cuda_gemm_qkv_rope", 150, 30),  # two token tiles over three pages
+])
+def test_qkv_rope_kv_store_matches_oracle(lib, oracle, torch_cuda, entry, count, length):
     torch = torch_cuda
-    rng = np.random.default_rng(21)
-    count, length, layer = 6, 61, 1  # positions 61..66 cross a page boundary
+    rng = np.random.default_rng(21 + count)
+    layer = 1
     num_pages = 4
     page_table = np.array([2, 0, 3, 1], np.int32)
     codes = finite_codes(rng, (6144, 3072))
@@ -242,7 +272,7 @@ def test_qkv_rope_kv_store_matches_oracle(lib, oracle, torch_cuda):
         cos[p], sin[p] = oracle.yarn(p)
     pool = torch.zeros((layer + 1) * num_pages * 2 * 8 * 64 * 128, dtype=torch.float32, device="cuda")
     q_out = torch.empty((count, 4096), dtype=torch.float32, device="cuda")
-    rc = lib.lunelette_cuda_qkv_rope(
+    rc = getattr(lib, entry)(
         ptr(tiled(lib, torch, codes, ORDER_ROPE_PAIRS)), scales.ctypes.data, ptr(dev(torch, gain)),
         ptr(dev(torch, x)),
         count, length, ptr(dev(torch, cos)), ptr(dev(torch, sin)), ptr(q_out), ptr(pool),
@@ -266,10 +296,12 @@ def test_qkv_rope_kv_store_matches_oracle(lib, oracle, torch_cuda):
     assert not pool_view(pool_np, num_pages)[0].any()
 
 
-def test_gateup_swiglu_matches_oracle(lib, oracle, torch_cuda):
+@pytest.mark.parametrize("entry,count", [
+    ("lunelette_cuda_gateup_swiglu", 3), ("lunelette_cuda_gemm_gateup_swiglu", 3),
+    ("lunelette_cuda_gemm_gateup_swiglu", 131)])
+def test_gateup_swiglu_matches_oracle(lib, oracle, torch_cuda, entry, count):
     torch = torch_cuda
-    rng = np.random.default_rng(31)
-    count = 3
+    rng = np.random.default_rng(31 + count)
     gate = finite_codes(rng, (9216, 3072))
     up = finite_codes(rng, (9216, 3072))
     inter = tiled(lib, torch, np.concatenate([gate, up]), ORDER_INTERLEAVE)  # gate f at 2f, up f at 2f+1
@@ -277,7 +309,7 @@ def test_gateup_swiglu_matches_oracle(lib, oracle, torch_cuda):
     gain = (0.5 + rng.random(3072)).astype(np.float32)
     x = rng.standard_normal((count, 3072)).astype(np.float32)
     act = torch.empty((count, 9216), dtype=torch.float32, device="cuda")
-    assert lib.lunelette_cuda_gateup_swiglu(ptr(inter), sg, su, ptr(dev(torch, gain)),
+    assert getattr(lib, entry)(ptr(inter), sg, su, ptr(dev(torch, gain)),
                                             ptr(dev(torch, x)), count, ptr(act), stream(torch)) == 0
     normed = oracle.norm(gain, x)
     g = oracle.project_fp8(gate, sg, normed)
