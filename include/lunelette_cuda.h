@@ -74,7 +74,7 @@ int lunelette_cuda_gateup_swiglu(const uint8_t *W, float scale_gate, float scale
  * memory, tcgen05.mma (M = 128 tokens, N = 256 rows, K = 16) accumulating both
  * parts in TMEM (FP32), K ranges added in a fixed order. Same arguments and
  * results as lunelette_cuda_gemv_fp8 / _qkv_rope / _gateup_swiglu (rows % 8 == 0
- * here); each call allocates its workspace on the stream and synchronises it.
+ * here, cols <= 16384); each call allocates its workspace on the stream and synchronises it.
  * Replaces the MPS prefill GEMMs (src/metal_mps.m:26-111). */
 int lunelette_cuda_gemm_fp8(const uint8_t *W, size_t rows, size_t cols, float scale,
     const float *x, const float *res, size_t count, float *y, void *stream);
@@ -84,6 +84,14 @@ int lunelette_cuda_gemm_qkv_rope(const uint8_t *W, const float *scales, const fl
     void *stream);
 int lunelette_cuda_gemm_gateup_swiglu(const uint8_t *W, float scale_gate, float scale_up,
     const float *gain, const float *x, size_t count, float *act, void *stream);
+
+/* Microbenchmark of the tensor-core path: runs lunelette_cuda_gemm_fp8 (no
+ * residual) `reps` times back to back, run r on the tiled matrix copy r % copies
+ * of `copies` consecutive ones at W, and writes the mean device time in ms of
+ * its three kernels from CUDA events on the stream: ms[0] activation split,
+ * ms[1] the tcgen05 GEMM, ms[2] the ordered K-range finish. */
+int lunelette_cuda_gemm_fp8_timed(const uint8_t *W, size_t copies, size_t rows, size_t cols, float scale,
+    const float *x, size_t count, float *y, int reps, float *ms, void *stream);
 
 /* out = gain * (x * rsqrt(mean(x^2) + 1e-5)) per row (src/metal_kernels.metal:29-44). */
 int lunelette_cuda_rmsnorm(const float *gain, const float *x, size_t width, size_t count,

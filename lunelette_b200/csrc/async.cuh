@@ -40,6 +40,29 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned by
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
+// Non-blocking probe of an mbarrier phase (mbarrier.try_wait may suspend the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, unsigned parity)
+{
+    unsigned ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Tiled 4-D tensor load (no multicast) of the box at {c0, c1, c2, c3}, completing on *bar.
+__device__ __forceinline__ void tma_load_4d(void *dst, const void *tmap, int c0, int c1, int c2, int c3,
+                                            uint64_t *bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+        "[%6];" ::"r"(smem_u32(dst)),
+        "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+        : "memory");
+}
 __device__ __forceinline__ void l2_prefetch(const void *src, unsigned bytes)
 {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");

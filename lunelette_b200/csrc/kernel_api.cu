@@ -4,6 +4,7 @@
 #include "kernels.h"
 #include "prefill_gemm.cuh"
 
+#include <stdlib.h>
 #include <string.h>
 
 #define LUN_API extern "C" __attribute__((visibility("default")))
@@ -168,9 +169,9 @@ static int run_prefill(const GemvParams &p, size_t count, int epilogue, cudaStre
     const PrefillPlan pl = lun_prefill_plan(p.rows, p.cols, (int)count, sms);
     PrefillWorkspace w;
     memset(&w, 0, sizeof w);
-    w.xs_bytes = (size_t)pl.token_tiles * pl.kchunks * 2 * kPgATile;
-    w.inv_bytes = (size_t)pl.token_tiles * kPgM * sizeof(float);
-    w.ws_bytes = (size_t)pl.splits * pl.token_tiles * kPgM * pl.row_tiles * kPgN * sizeof(float);
+    w.xs_bytes = pl.xs_bytes;
+    w.inv_bytes = pl.inv_bytes;
+    w.ws_bytes = pl.ws_bytes;
     int rc = -1, error = 0;
     if (cudaMallocAsync((void **)&w.xs, w.xs_bytes, stream) == cudaSuccess &&
         cudaMallocAsync((void **)&w.inv_scale, w.inv_bytes, stream) == cudaSuccess &&
@@ -188,11 +189,72 @@ static int run_prefill(const GemvParams &p, size_t count, int epilogue, cudaStre
     return rc;
 }
 
+// Mean device time of each prefill kernel (ms[0] split, ms[1] GEMM, ms[2]
+// finish) over `reps` back-to-back runs of lunelette_cuda_gemm_fp8 (store
+// epilogue), from CUDA events on the stream; run r reads weight copy r % copies
+// of `copies` consecutive tiled matrices at W. A microbenchmark of the
+// tensor-core path.
+LUN_API int lunelette_cuda_gemm_fp8_timed(const uint8_t *W, size_t copies, size_t rows, size_t cols, float scale,
+                                          const float *x, size_t count, float *y, int reps, float *ms,
+                                          void *stream)
+{
+    if (!W || !copies || !x || !y || !ms || reps <= 0 || reps > 4096 || !rows || (rows % 8) || !cols ||
+        (cols % 16) || !count || count > 65536 || rows > (1u << 24) || cols > kSplitMaxCols)
+        return -1;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int sms = sm_count_of_current();
+    const size_t matrix = tiled_bytes(rows, cols);
+    GemvParams p = plain(W, rows, cols, scale);
+    p.x = x;
+    p.x_stride = (int)cols;
+    p.y = y;
+    p.y_stride = (int)rows;
+    const PrefillPlan pl = lun_prefill_plan(p.rows, p.cols, (int)count, sms);
+    PrefillWorkspace w;
+    memset(&w, 0, sizeof w);
+    w.xs_bytes = pl.xs_bytes;
+    w.inv_bytes = pl.inv_bytes;
+    w.ws_bytes = pl.ws_bytes;
+    cudaEvent_t *ev = (cudaEvent_t *)calloc((size_t)4 * reps, sizeof(cudaEvent_t));
+    if (!ev) return -1;
+    int rc = -1, error = 0;
+    double sum[3] = {0, 0, 0};
+    bool good = cudaMalloc((void **)&w.xs, w.xs_bytes) == cudaSuccess &&
+                cudaMalloc((void **)&w.inv_scale, w.inv_bytes) == cudaSuccess &&
+                cudaMalloc((void **)&w.ws, w.ws_bytes) == cudaSuccess &&
+                cudaMalloc((void **)&w.error, sizeof(int)) == cudaSuccess &&
+                cudaMemsetAsync(w.error, 0, sizeof(int), st) == cudaSuccess;
+    for (int i = 0; i < 4 * reps && good; i++) good = cudaEventCreate(&ev[i]) == cudaSuccess;
+    for (int r = 0; r < reps && good; r++) {
+        p.W = W + (size_t)(r % copies) * matrix;
+        good = lun_launch_prefill_marked(p, (int)count, kEpiStore, w, sms, st, ev + 4 * r) == cudaSuccess;
+    }
+    good = good && cudaStreamSynchronize(st) == cudaSuccess;
+    for (int r = 0; r < reps && good; r++)
+        for (int k = 0; k < 3 && good; k++) {
+            float t = 0.0f;
+            good = cudaEventElapsedTime(&t, ev[4 * r + k], ev[4 * r + k + 1]) == cudaSuccess;
+            sum[k] += t;
+        }
+    if (good && cudaMemcpy(&error, w.error, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess && !error) {
+        for (int k = 0; k < 3; k++) ms[k] = (float)(sum[k] / reps);
+        rc = 0;
+    }
+    for (int i = 0; i < 4 * reps; i++)
+        if (ev[i]) cudaEventDestroy(ev[i]);
+    free(ev);
+    cudaFree(w.xs);
+    cudaFree(w.inv_scale);
+    cudaFree(w.ws);
+    cudaFree(w.error);
+    return rc;
+}
+
 // lunelette_cuda_gemv_fp8 through the tcgen05 prefill GEMM.
 LUN_API int lunelette_cuda_gemm_fp8(const uint8_t *W, size_t rows, size_t cols, float scale, const float *x,
                                     const float *res, size_t count, float *y, void *stream)
 {
-    if (!W || !x || !y || !rows || (rows % 8) || !cols || (cols % 16) || rows > (1u << 24) || cols > 65536)
+    if (!W || !x || !y || !rows || (rows % 8) || !cols || (cols % 16) || rows > (1u << 24) || cols > kSplitMaxCols)
         return -1;
     GemvParams p = plain(W, rows, cols, scale);
     p.x = x;

@@ -58,7 +58,8 @@ cudaError_t lun_launch_fp8_decode(const uint8_t *codes, size_t n, float scale, f
 // Prefill projections on the tcgen05 tensor cores (prefill_gemm.cuh): split
 // activations, GEMM into per-K-range partials, ordered finish + fused epilogue.
 struct PrefillPlan {
-    int row_tiles, token_tiles, kchunks, splits;
+    int row_tiles, token_tiles, kchunks, splits;  // 512-row tiles, 128-token tiles, 64-column chunks, K ranges
+    size_t xs_bytes, inv_bytes, ws_bytes;         // workspace this projection needs
 };
 PrefillPlan lun_prefill_plan(int rows, int cols, int count, int sm_count);
 struct PrefillWorkspace {
@@ -76,3 +77,8 @@ void lun_prefill_workspace_bytes(int max_count, int sm_count, size_t *xs_bytes, 
 // lun::GemvEpilogue, positions from p.step->length (or p.length + p.token_offset).
 cudaError_t lun_launch_prefill(const lun::GemvParams &p, int count, int epilogue, const PrefillWorkspace &w,
                                int sm_count, cudaStream_t stream);
+// The same with events recorded before the split, between the kernels and after
+// the finish (marks[0..3]), for per-kernel timing.
+cudaError_t lun_launch_prefill_marked(const lun::GemvParams &p, int count, int epilogue,
+                                      const PrefillWorkspace &w, int sm_count, cudaStream_t stream,
+                                      cudaEvent_t *marks);

@@ -1,22 +1,28 @@
 // Launchers of the tcgen05 prefill projections (prefill_gemm.cuh).
+#include <cudaTypedefs.h>
+
 #include "kernels.h"
 #include "prefill_gemm.cuh"
+
 
 using namespace lun;
 
 PrefillPlan lun_prefill_plan(int rows, int cols, int count, int sm_count)
 {
     PrefillPlan pl;
-    pl.row_tiles = (rows + kPgN - 1) / kPgN;
+    pl.row_tiles = (rows + kP2N - 1) / kP2N;
     pl.token_tiles = (count + kPgM - 1) / kPgM;
     pl.kchunks = (cols + kPgK - 1) / kPgK;
-    // K ranges fill the SMs when the output tiles alone do not; every range
-    // keeps at least two stages
-    const int tiles = pl.row_tiles * pl.token_tiles;
-    int splits = sm_count / (tiles > 0 ? tiles : 1);
+    // K ranges fill the SMs when the output tiles alone do not (a CTA pair per
+    // 512 rows x 256 tokens); every range keeps at least two stages
+    const int pairs = pl.row_tiles * ((pl.token_tiles + 1) / 2);
+    int splits = sm_count / (2 * (pairs > 0 ? pairs : 1));
     splits = splits < 1 ? 1 : splits;
     const int max_splits = pl.kchunks / 2 > 0 ? pl.kchunks / 2 : 1;
     pl.splits = splits > max_splits ? max_splits : splits;
+    pl.xs_bytes = (size_t)pl.token_tiles * pl.kchunks * 2 * kPgATile;
+    pl.inv_bytes = (size_t)pl.token_tiles * kPgM * sizeof(float);
+    pl.ws_bytes = (size_t)pl.splits * pl.token_tiles * kPgM * pl.row_tiles * kP2N * sizeof(float);
     return pl;
 }
 
@@ -24,17 +30,46 @@ void lun_prefill_workspace_bytes(int max_count, int sm_count, size_t *xs_bytes, 
                                  size_t *ws_bytes)
 {
     static const int shapes[4][2] = {{kQKVRows, kHidden}, {kHidden, kQuery}, {kGateUpRows, kHidden}, {kHidden, kInner}};
-    size_t xs = 0, ws = 0;
+    size_t xs = 0, ws = 0, inv = 0;
     for (const auto &s : shapes) {
         const PrefillPlan pl = lun_prefill_plan(s[0], s[1], max_count, sm_count);
-        const size_t x = (size_t)pl.token_tiles * pl.kchunks * 2 * kPgATile;
-        const size_t w = (size_t)pl.splits * pl.token_tiles * kPgM * pl.row_tiles * kPgN * sizeof(float);
-        xs = x > xs ? x : xs;
-        ws = w > ws ? w : ws;
+        xs = pl.xs_bytes > xs ? pl.xs_bytes : xs;
+        ws = pl.ws_bytes > ws ? pl.ws_bytes : ws;
+        inv = pl.inv_bytes > inv ? pl.inv_bytes : inv;
     }
     *xs_bytes = xs;
-    *inv_bytes = (size_t)((max_count + kPgM - 1) / kPgM) * kPgM * sizeof(float);
+    *inv_bytes = inv;
     *ws_bytes = ws;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return (PFN_cuTensorMapEncodeTiled_v12000)f;
+    }();
+    return fn;
+}
+
+// The tiled FP8 matrix as the GEMM's 4-D weight tensor (prefill_gemm_pair_kernel).
+static cudaError_t weight_tensor_map(CUtensorMap *map, const uint8_t *W, int rows, int nb)
+{
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (!encode || ((uintptr_t)W & 15)) return cudaErrorInvalidValue;
+    const cuuint64_t dims[4] = {256, 2, (cuuint64_t)(2 * nb), (cuuint64_t)(rows / kTileRows)};
+    const cuuint64_t strides[3] = {256, 512, (cuuint64_t)nb * kBlockBytes};
+    const cuuint32_t box[4] = {256, 2, 1, kP2Rows / kTileRows};
+    const cuuint32_t elem[4] = {1, 1, 1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, (void *)W, dims, strides, box, elem,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
 static cudaError_t prefill_setup()
@@ -45,7 +80,7 @@ static cudaError_t prefill_setup()
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
     if (done[dev]) return cudaSuccess;
-    e = cudaFuncSetAttribute(prefill_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPgSmemBytes);
+    e = cudaFuncSetAttribute(prefill_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kP2SmemBytes);
     if (e == cudaSuccess) done[dev] = true;
     return e;
 }
@@ -61,16 +96,21 @@ static cudaError_t launch_finish(const PrefillFinishParams &f, cudaStream_t stre
 cudaError_t lun_launch_prefill(const GemvParams &p, int count, int epilogue, const PrefillWorkspace &w,
                                int sm_count, cudaStream_t stream)
 {
-    if (count <= 0 || p.rows <= 0 || (p.rows % kTileRows) || p.cols <= 0 || (p.cols & 15) || !w.xs ||
+    return lun_launch_prefill_marked(p, count, epilogue, w, sm_count, stream, nullptr);
+}
+
+cudaError_t lun_launch_prefill_marked(const GemvParams &p, int count, int epilogue, const PrefillWorkspace &w,
+                                      int sm_count, cudaStream_t stream, cudaEvent_t *marks)
+{
+    if (count <= 0 || p.rows <= 0 || (p.rows % kTileRows) || p.cols <= 0 || (p.cols & 15) ||
+        p.cols > kSplitMaxCols || (p.x_stride & 3) || ((uintptr_t)p.x & 15) || ((uintptr_t)p.gain & 15) || !w.xs ||
         !w.inv_scale || !w.ws || !w.error)
         return cudaErrorInvalidValue;
     if ((epilogue == kEpiQKV && (p.rows != kQKVRows || p.cols != kHidden)) || (epilogue == kEpiSwiGLU && (p.rows & 1)))
         return cudaErrorInvalidValue;
     const PrefillPlan pl = lun_prefill_plan(p.rows, p.cols, count, sm_count);
-    const size_t xs = (size_t)pl.token_tiles * pl.kchunks * 2 * kPgATile;
-    const size_t inv = (size_t)pl.token_tiles * kPgM * sizeof(float);
-    const size_t ws = (size_t)pl.splits * pl.token_tiles * kPgM * pl.row_tiles * kPgN * sizeof(float);
-    if (xs > w.xs_bytes || inv > w.inv_bytes || ws > w.ws_bytes) return cudaErrorInvalidValue;
+    if (pl.xs_bytes > w.xs_bytes || pl.inv_bytes > w.inv_bytes || pl.ws_bytes > w.ws_bytes)
+        return cudaErrorInvalidValue;
     cudaError_t e = prefill_setup();
     if (e != cudaSuccess) return e;
 
@@ -83,8 +123,10 @@ cudaError_t lun_launch_prefill(const GemvParams &p, int count, int epilogue, con
     sp.count = count;
     sp.xs = w.xs;
     sp.inv_scale = w.inv_scale;
-    prefill_split_kernel<<<pl.token_tiles * kPgM, 256, 0, stream>>>(sp);
+    if (marks && (e = cudaEventRecord(marks[0], stream)) != cudaSuccess) return e;
+    prefill_split_kernel<<<pl.token_tiles * kPgM, kSplitThreads, 0, stream>>>(sp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if (marks && (e = cudaEventRecord(marks[1], stream)) != cudaSuccess) return e;
 
     PrefillGemmParams g;
     g.W = p.W;
@@ -97,10 +139,14 @@ cudaError_t lun_launch_prefill(const GemvParams &p, int count, int epilogue, con
     g.splits = pl.splits;
     g.inv_scale = w.inv_scale;
     g.ws = w.ws;
-    g.ws_rows = pl.row_tiles * kPgN;
+    g.ws_rows = pl.row_tiles * kP2N;
     g.error = w.error;
-    prefill_gemm_kernel<<<dim3(pl.row_tiles, pl.token_tiles, pl.splits), kPgThreads, kPgSmemBytes, stream>>>(g);
+    CUtensorMap wmap;
+    if ((e = weight_tensor_map(&wmap, p.W, p.rows, g.nb)) != cudaSuccess) return e;
+    prefill_gemm_pair_kernel<<<dim3(2 * pl.row_tiles, (pl.token_tiles + 1) / 2, pl.splits), kPgThreads,
+                               kP2SmemBytes, stream>>>(g, wmap);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if (marks && (e = cudaEventRecord(marks[2], stream)) != cudaSuccess) return e;
 
     PrefillFinishParams f;
     f.ws = w.ws;
@@ -125,10 +171,12 @@ cudaError_t lun_launch_prefill(const GemvParams &p, int count, int epilogue, con
     f.num_pages = p.num_pages;
     f.layer = p.layer;
     switch (epilogue) {
-    case kEpiStore: return launch_finish<kEpiStore>(f, stream);
-    case kEpiResidual: return launch_finish<kEpiResidual>(f, stream);
-    case kEpiQKV: return launch_finish<kEpiQKV>(f, stream);
-    case kEpiSwiGLU: return launch_finish<kEpiSwiGLU>(f, stream);
+    case kEpiStore: e = launch_finish<kEpiStore>(f, stream); break;
+    case kEpiResidual: e = launch_finish<kEpiResidual>(f, stream); break;
+    case kEpiQKV: e = launch_finish<kEpiQKV>(f, stream); break;
+    case kEpiSwiGLU: e = launch_finish<kEpiSwiGLU>(f, stream); break;
     default: return cudaErrorInvalidValue;
     }
+    if (e == cudaSuccess && marks) e = cudaEventRecord(marks[3], stream);
+    return e;
 }

@@ -1,4 +1,5 @@
-"""Decode GEMV microbenchmark on the current GPU.
+"""Decode GEMV microbenchmark on the current GPU, and the
+prefill GEMM microbenchmark (--prefill-gemm).
 
 Shapes: the model's FP8 linears q 3072->4096, k/v 3072->1024, o 4096->3072,
 gate/up 3072->9216, down 9216->3072, and the BF16 lm_head 3072->131072, at token
@@ -163,6 +164,62 @@ def decode_phases(checkpoint, steps=8, prompt=32):
     return out
 
 
+PREFILL_SHAPES = {"qkv": (6144, 3072), "o": (3072, 4096), "gateup": (18432, 3072), "down": (3072, 9216)}
+
+
+def tensor_peak():
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    try:
+        return float(json.load(open(path))["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def prefill_gemm(counts, iters):
+    """The tcgen05 prefill projections at the model's four shapes: mean device
+    time of the split, GEMM and finish kernels (CUDA events), weights rotated
+    over copies larger than 2x L2. `issued` TFLOP/s counts what the tensor core
+    executes (hi and lo passes over 128-token tiles and 256-row tiles),
+    `useful` the projection's own 2 * rows * cols * count."""
+    import ctypes
+    import torch
+    import lunelette_b200 as L
+    lib = L.library()
+    stream = torch.cuda.current_stream().cuda_stream
+    peak, kind = tensor_peak()
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    out = []
+    for name, (rows, cols) in PREFILL_SHAPES.items():
+        copies = max(1, min(8, (2 * L2_BYTES) // (rows * cols) + 1))
+        w = torch.randint(0, 256, (copies * rows * cols,), device="cuda", dtype=torch.uint8, generator=gen)
+        w[(w & 127) == 127] = 0
+        for count in counts:
+            x = torch.randn(count, cols, device="cuda", generator=gen)
+            y = torch.empty(count, rows, device="cuda")
+            ms = (ctypes.c_float * 3)()
+            # one warm-up pass, then the timed back-to-back runs
+            for reps in (copies, iters):
+                rc = lib.lunelette_cuda_gemm_fp8_timed(w.data_ptr(), copies, rows, cols, 1.0, x.data_ptr(), count,
+                                                       y.data_ptr(), reps, ms, stream)
+                assert rc == 0, (name, count)
+            tot = [ms[0], ms[1], ms[2]]
+            tt = (count + 127) // 128
+            # a CTA pair covers 256 tokens (two 128-token tiles) x 512 rows
+            issued = 2 * 2 * ((rows + 511) // 512 * 512) * ((cols + 63) // 64 * 64) * 256 * ((tt + 1) // 2)
+            useful = 2 * rows * cols * count
+            out.append({
+                "projection": name, "rows": rows, "cols": cols, "count": count,
+                "split_us": tot[0] * 1e3, "gemm_us": tot[1] * 1e3, "finish_us": tot[2] * 1e3,
+                "gemm_issued_tflops": issued / (tot[1] * 1e-3) / 1e12,
+                "gemm_useful_tflops": useful / (tot[1] * 1e-3) / 1e12,
+                "tensor_frac_issued": issued / (tot[1] * 1e-3) / 1e12 / peak,
+                "tensor_frac_useful": 2 * useful / (tot[1] * 1e-3) / 1e12 / peak, "peak_tflops": peak,
+                "peak_kind": kind,
+                "weight_gbs": rows * cols / (tot[1] * 1e-3) / 1e9,
+            })
+    return out
+
+
 def decode_tokens(checkpoint, steps, prompt=32):
     """A small profiling target: the C0 prompt, then `steps` greedy tokens through
     lunelette_metal_decode (one persistent-kernel launch each)."""
@@ -185,7 +242,13 @@ def main():
                     help="run the C0 prompt and N single-token decode launches (a profiling target)")
     ap.add_argument("--decode-phases", metavar="CHECKPOINT", default=None,
                     help="time the persistent decode kernel's phases on this checkpoint instead")
+    ap.add_argument("--prefill-gemm", metavar="COUNTS", default=None,
+                    help="time the tcgen05 prefill projections at these token counts (e.g. 256,32)")
     args = ap.parse_args()
+    if args.prefill_gemm:
+        for r in prefill_gemm([int(v) for v in args.prefill_gemm.split(",")], args.iters):
+            print(json.dumps(r))
+        return
     if args.decode_tokens:
         print(json.dumps({"last_token": decode_tokens(args.decode_tokens[0], int(args.decode_tokens[1]))}))
         return
