@@ -170,6 +170,180 @@ static __global__ void __launch_bounds__(128) attention_combine_kernel(AttnParam
     p.out[(size_t)t * kQuery + head * kHeadDim + d] = acc / l;
 }
 
+// ---- blocks of query tokens (prefill, append) ------------------------------------
+// One block per (8 query tokens, KV head): the 32 query rows (8 tokens x the
+// 4 query heads of the GQA group, row 4 * token + head) stream the causal K/V
+// range once, a 64-position page at a time, instead of once per token. K and V
+// tiles arrive by cp.async (a page of one head is 32 KB contiguous per kind);
+// the next tile's K loads during this tile's P V and the next V during the
+// next S, so one buffer each suffices. S = Q K^T and O += P V run as 4 x 4 and
+// 4 x 8 register tiles per thread: thread (rg, cg) owns rows 4rg..4rg+3, keys
+// cg + 16j (conflict-free 16-byte reads of the padded K rows) and dims
+// 8cg..8cg+7; the online softmax of a row lives in the 16 threads of a half
+// warp, the same in both phases.
+constexpr int kPfTokens = 8;                    // query tokens per block
+constexpr int kPfRows = 4 * kPfTokens;          // 32 query rows
+constexpr int kPfKeys = kPage;                  // positions per K/V tile (one page)
+constexpr int kPfRowStride = kHeadDim + 4;      // padded Q and K rows (floats)
+constexpr int kPfPStride = kPfRows + 4;         // P^T row
+constexpr int kPfThreads = 128;
+constexpr int kPfSmemFloats =
+    kPfRows * kPfRowStride + kPfKeys * kPfRowStride + kPfKeys * kHeadDim + kPfKeys * kPfPStride;
+constexpr int kPfSmemBytes = kPfSmemFloats * 4;
+
+// Copy rows [0, keys) of a 64 x 128 tile (zero the rest) into rows of `stride` floats.
+__device__ __forceinline__ void pf_issue_tile(float *dst, const float *src, int keys, int stride)
+{
+    for (int i = threadIdx.x; i < kPfKeys * (kHeadDim / 4); i += kPfThreads) {
+        const int row = i >> 5, c = i & 31;
+        const bool in = row < keys;
+        cp_async16(dst + row * stride + 4 * c, in ? src + (size_t)row * kHeadDim + 4 * c : src, in);
+    }
+    cp_async_commit();
+}
+
+// Grid (ceil(count / 8), 8 KV heads), 128 threads.
+static __global__ void __launch_bounds__(kPfThreads) attention_prefill_kernel(AttnParams p, int count)
+{
+    extern __shared__ float4 pf_smem4[];
+    float *qs = reinterpret_cast<float *>(pf_smem4);     // [32][kPfRowStride]
+    float *ks = qs + kPfRows * kPfRowStride;             // [64][kPfRowStride]
+    float *vs = ks + kPfKeys * kPfRowStride;             // [64][128]
+    float *pt = vs + kPfKeys * kHeadDim;                 // [64][kPfPStride]: P^T of the tile
+    const int kvh = blockIdx.y, t0 = blockIdx.x * kPfTokens, tid = threadIdx.x;
+    const int rg = tid >> 4, cg = tid & 15;
+    pdl_wait();
+    pdl_launch_dependents();
+    const int length = (p.step ? p.step->length : p.length) + p.token_offset;
+    const int last = min(t0 + kPfTokens, count) - 1;      // last query token of the block
+    const int total = length + last + 1;                  // keys the block needs
+    const int tiles = (total + kPfKeys - 1) / kPfKeys;
+
+    auto kv_tile = [&](int tile, int kind) {
+        const int page = p.page_table[tile];
+        return p.kv + kv_offset(p.layer, p.num_pages, page, kind, kvh, 0);
+    };
+    pf_issue_tile(ks, kv_tile(0, 0), min(kPfKeys, total), kPfRowStride);
+    pf_issue_tile(vs, kv_tile(0, 1), min(kPfKeys, total), kHeadDim);
+    for (int i = tid; i < kPfRows * kHeadDim / 4; i += kPfThreads) {
+        const int r = i >> 5, c = i & 31, tk = r >> 2, hh = r & 3;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t0 + tk < count)
+            v = *reinterpret_cast<const float4 *>(p.q + (size_t)(t0 + tk) * kQuery + (kvh * 4 + hh) * kHeadDim + 4 * c);
+        *reinterpret_cast<float4 *>(qs + r * kPfRowStride + 4 * c) = v;
+    }
+    // the causal limit of each of this thread's rows: key position <= length + token
+    int limit[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int tk = t0 + ((4 * rg + i) >> 2);
+        limit[i] = tk < count ? length + tk : -1;
+    }
+    float m_run[4], l_run[4], o[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        m_run[i] = -INFINITY;
+        l_run[i] = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; e++) o[i][e] = 0.0f;
+    }
+    for (int tile = 0; tile < tiles; tile++) {
+        const int p0 = tile * kPfKeys, keys = min(kPfKeys, total - p0);
+        cp_async_wait_one();  // K of this tile (its V may still be in flight)
+        __syncthreads();
+        // S = Q K^T for rows 4rg.., keys p0 + cg + 16j
+        float s[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) s[i][j] = 0.0f;
+#pragma unroll 4
+        for (int d = 0; d < kHeadDim; d += 4) {
+            float4 a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) a[i] = *reinterpret_cast<const float4 *>(qs + (4 * rg + i) * kPfRowStride + d);
+#pragma unroll
+            for (int j = 0; j < 4; j++) b[j] = *reinterpret_cast<const float4 *>(ks + (cg + 16 * j) * kPfRowStride + d);
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    s[i][j] = fmaf(a[i].x, b[j].x, s[i][j]);
+                    s[i][j] = fmaf(a[i].y, b[j].y, s[i][j]);
+                    s[i][j] = fmaf(a[i].z, b[j].z, s[i][j]);
+                    s[i][j] = fmaf(a[i].w, b[j].w, s[i][j]);
+                }
+        }
+        __syncthreads();  // K consumed: the next tile's K may load
+        if (tile + 1 < tiles)
+            pf_issue_tile(ks, kv_tile(tile + 1, 0), min(kPfKeys, total - p0 - kPfKeys), kPfRowStride);
+        else
+            cp_async_commit();
+        // online softmax per row over the 16 threads of the half warp
+        float prob[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int pos = p0 + cg + 16 * j;
+                s[i][j] = pos <= limit[i] ? s[i][j] * kScoreScale : -INFINITY;
+                mx = fmaxf(mx, s[i][j]);
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float m_new = fmaxf(m_run[i], mx);
+            const float corr = m_run[i] == -INFINITY ? 0.0f : expf(m_run[i] - m_new);
+            float sum = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                prob[i][j] = s[i][j] == -INFINITY ? 0.0f : expf(s[i][j] - m_new);
+                sum += prob[i][j];
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+            l_run[i] = l_run[i] * corr + sum;
+            m_run[i] = m_new;
+#pragma unroll
+            for (int e = 0; e < 8; e++) o[i][e] *= corr;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            *reinterpret_cast<float4 *>(pt + (cg + 16 * j) * kPfPStride + 4 * rg) =
+                make_float4(prob[0][j], prob[1][j], prob[2][j], prob[3][j]);
+        cp_async_wait_one();  // V of this tile (the next K may still be in flight)
+        __syncthreads();
+        // O += P V for rows 4rg.., dims 8cg..8cg+7
+#pragma unroll 4
+        for (int j = 0; j < keys; j++) {
+            const float4 pj = *reinterpret_cast<const float4 *>(pt + j * kPfPStride + 4 * rg);
+            const float4 v0 = *reinterpret_cast<const float4 *>(vs + j * kHeadDim + 8 * cg);
+            const float4 v1 = *reinterpret_cast<const float4 *>(vs + j * kHeadDim + 8 * cg + 4);
+            const float pv[4] = {pj.x, pj.y, pj.z, pj.w};
+            const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int e = 0; e < 8; e++) o[i][e] = fmaf(pv[i], vv[e], o[i][e]);
+        }
+        __syncthreads();  // V and P consumed: the next tile's V may load
+        if (tile + 1 < tiles)
+            pf_issue_tile(vs, kv_tile(tile + 1, 1), min(kPfKeys, total - p0 - kPfKeys), kHeadDim);
+        else
+            cp_async_commit();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int r = 4 * rg + i, tk = t0 + (r >> 2), head = kvh * 4 + (r & 3);
+        if (tk >= count) continue;
+        const float inv = 1.0f / l_run[i];
+        float *dst = p.out + (size_t)tk * kQuery + head * kHeadDim + 8 * cg;
+        *reinterpret_cast<float4 *>(dst) = make_float4(o[i][0] * inv, o[i][1] * inv, o[i][2] * inv, o[i][3] * inv);
+        *reinterpret_cast<float4 *>(dst + 4) =
+            make_float4(o[i][4] * inv, o[i][5] * inv, o[i][6] * inv, o[i][7] * inv);
+    }
+}
+
 // x[t][c] = widen(E[ids[t]][c]) for the call's tokens (src/metal_runtime.m:391-395).
 static __global__ void embed_kernel(const uint16_t *embedding, const StepParams *step, float *x,
                              int count)

@@ -203,6 +203,9 @@ cudaError_t lun_kernels_init()
     if ((e = cudaFuncSetAttribute(attention_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   kAttnSmemBytes)) != cudaSuccess)
         return e;
+    if ((e = cudaFuncSetAttribute(attention_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  kPfSmemBytes)) != cudaSuccess)
+        return e;
     if ((e = setup_epi<kEpiStore>()) != cudaSuccess) return e;
     if ((e = setup_epi<kEpiResidual>()) != cudaSuccess) return e;
     if ((e = setup_epi<kEpiQKV>()) != cudaSuccess) return e;
@@ -274,10 +277,13 @@ void lun_attention_plan(AttnParams *a, int total, int count, int sm_count, int s
 
 cudaError_t lun_launch_attention(const AttnParams &a, int count, cudaStream_t stream)
 {
-    if (a.splits < 1 || a.split_len < kTile || (a.split_len % kTile)) return cudaErrorInvalidValue;
-    dim3 grid(a.splits, kKVHeads, count);
     cudaError_t e = lun_kernels_ensure();
     if (e != cudaSuccess) return e;
+    if (count > kGemvMaxTokens)  // blocks of tokens: one pass over the keys per 8 query tokens
+        return launch(attention_prefill_kernel, dim3((count + kPfTokens - 1) / kPfTokens, kKVHeads), dim3(kPfThreads),
+                      kPfSmemBytes, stream, a, count);
+    if (a.splits < 1 || a.split_len < kTile || (a.split_len % kTile)) return cudaErrorInvalidValue;
+    dim3 grid(a.splits, kKVHeads, count);
     e = launch(attention_split_kernel, grid, dim3(128), kAttnSmemBytes, stream, a);
     if (e != cudaSuccess || a.splits == 1) return e;
     return launch(attention_combine_kernel, dim3(kQueryHeads, count), dim3(128), 0, stream, a);
