@@ -179,6 +179,32 @@ def traffic_per_launch(steps):
     return None if per_token is None else per_token * steps
 
 
+def prefill_gemm_roofline(lib, torch, count=256, reps=20):
+    """Device time of the tcgen05 prefill GEMM (prefill_gemm_pair_kernel) for
+    the gate/up projection of a 256-token block, from CUDA events on its
+    stream (lunelette_cuda_gemm_fp8_timed, back-to-back launches rotating 5
+    weight copies: 283 MB > L2). FLOPs: `issued` counts the tensor core's work
+    (hi and lo passes, 256-token pair tiles), `useful` the projection's own
+    2 * rows * cols * count."""
+    import ctypes
+    rows, cols, copies = 18432, 3072, 5
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    w = torch.randint(0, 256, (copies * rows * cols,), device="cuda", dtype=torch.uint8, generator=gen)
+    w[(w & 127) == 127] = 0
+    x = torch.randn(count, cols, device="cuda", generator=gen)
+    y = torch.empty(count, rows, device="cuda")
+    ms = (ctypes.c_float * 3)()
+    s = torch.cuda.current_stream().cuda_stream
+    for n in (copies, reps):
+        assert lib.lunelette_cuda_gemm_fp8_timed(w.data_ptr(), copies, rows, cols, 1.0, x.data_ptr(), count,
+                                                 y.data_ptr(), n, ms, s) == 0
+    tiles = (count + 255) // 256
+    issued = 2 * 2 * ((rows + 511) // 512 * 512) * cols * 256 * tiles
+    useful = 2 * rows * cols * count
+    return {"split_ms": ms[0], "gemm_ms": ms[1], "finish_ms": ms[2], "issued_flops": issued,
+            "useful_flops": useful}
+
+
 def cpu_baseline(checkpoint, prompt, decode_steps=6):
     """The CPU oracle (C restatement of the reference kernels, OpenMP) on this
     box's host cores: the C0 prompt, then `decode_steps` greedy decode steps."""
@@ -343,6 +369,7 @@ def run_ours(args, rank, world, local_rank):
 
     hbm, bf16, peak_kind = measured_peaks()
     gemv_ms, gemv_bytes = gateup_roofline(lib, torch, checkpoint)
+    pg = prefill_gemm_roofline(lib, torch)
     ms_per_step = device_ms / steps
     mean_ctx = PROMPT + (per_round + 1) / 2
     step_bytes = WEIGHT_BYTES_PER_TOKEN + KV_BYTES_PER_POSITION * mean_ctx
@@ -376,6 +403,15 @@ def run_ours(args, rank, world, local_rank):
                               "achieved": gemv_bytes / (gemv_ms / 1000) / 1e9, "unit": "GB/s",
                               "frac": gemv_bytes / (gemv_ms / 1000) / 1e9 / hbm, "algorithmic_bytes": gemv_bytes,
                               "avg_launch_ms": gemv_ms},
+            "prefill_roofline": {
+                "kernel": "prefill_gemm_pair_kernel (tcgen05 cta_group::2, FP16 hi + lo passes, gate/up "
+                          "18432x3072, 256 tokens, weights > L2)",
+                "bound": "tensor", "unit": "TFLOP/s", "peak": bf16, "peak_kind": peak_kind,
+                "achieved": pg["issued_flops"] / (pg["gemm_ms"] / 1e3) / 1e12,
+                "frac": pg["issued_flops"] / (pg["gemm_ms"] / 1e3) / 1e12 / bf16,
+                "useful_tflops": pg["useful_flops"] / (pg["gemm_ms"] / 1e3) / 1e12,
+                "avg_launch_ms": pg["gemm_ms"], "split_ms": pg["split_ms"], "finish_ms": pg["finish_ms"],
+                "note": "issued = 2 FP16 passes (hi, lo) x 2 x rows x cols x 256; useful = half of it"},
             "clocks": clocks.summary(),
             "gpu_launches": launches,
             "greedy_device_matches_host": same_tokens,

@@ -220,6 +220,26 @@ def prefill_gemm(counts, iters):
     return out
 
 
+def prefill_tokens(checkpoint, count):
+    """A profiling target: prefill `count` seeded ids once (warm-up), then again
+    between cudaProfilerStart and cudaProfilerStop (ncu --profile-from-start off)."""
+    import torch
+    import lunelette_b200 as L
+    if not os.path.exists(checkpoint):
+        L.synth_checkpoint(checkpoint, 0)
+    with L.Runtime(checkpoint) as rt:
+        ids = np.random.default_rng(3).integers(1000, 131072, count).astype(np.int64)
+        rt.reset()
+        rt.prefill(ids)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        rt.reset()
+        tok = int(np.argmax(rt.prefill(ids)))
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+    return tok
+
+
 def decode_tokens(checkpoint, steps, prompt=32):
     """A small profiling target: the C0 prompt, then `steps` greedy tokens through
     lunelette_metal_decode (one persistent-kernel launch each)."""
@@ -242,9 +262,14 @@ def main():
                     help="run the C0 prompt and N single-token decode launches (a profiling target)")
     ap.add_argument("--decode-phases", metavar="CHECKPOINT", default=None,
                     help="time the persistent decode kernel's phases on this checkpoint instead")
+    ap.add_argument("--prefill-tokens", nargs=2, metavar=("CHECKPOINT", "N"), default=None,
+                    help="prefill N ids twice, the second between cudaProfilerStart/Stop (a profiling target)")
     ap.add_argument("--prefill-gemm", metavar="COUNTS", default=None,
                     help="time the tcgen05 prefill projections at these token counts (e.g. 256,32)")
     args = ap.parse_args()
+    if args.prefill_tokens:
+        print(json.dumps({"first_token": prefill_tokens(args.prefill_tokens[0], int(args.prefill_tokens[1]))}))
+        return
     if args.prefill_gemm:
         for r in prefill_gemm([int(v) for v in args.prefill_gemm.split(",")], args.iters):
             print(json.dumps(r))
