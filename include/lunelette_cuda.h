@@ -131,6 +131,18 @@ int lunelette_cuda_attention_noalloc(const float *q, const float *kv_pool, const
 
 /* Keep every layer's output rows (which 0..25) and the final-norm rows (26) of
  * the most recent call; host copy of count*3072 floats. Host-synchronous. */
+/* KV prefix reuse across sequences: copies pages of the paged FP32 pool
+ * [layer][page][K|V][8 heads][64 slots][128]. For i < pairs, every layer's
+ * K and V of page src_pages[i] go to page dst_pages[i] (device int arrays);
+ * the last pair copies only its first last_slots (1..64) positions. A sequence
+ * forked from another's prefix shares the full pages through its page table
+ * and copies only the partial last page (copy on write), or copies the whole
+ * prefix. The reference keeps one sequence per context and restores a prefix
+ * by rewinding its length (src/metal_runtime.m:494-575); this is the device
+ * side of reusing that prefix in another sequence. */
+int lunelette_cuda_kv_copy(float *kv_pool, size_t num_pages, size_t layers, const int *src_pages,
+    const int *dst_pages, size_t pairs, size_t last_slots, void *stream);
+
 int lunelette_cuda_trace(lunelette_metal *context, int enable);
 int lunelette_cuda_trace_copy(lunelette_metal *context, int which, float *out, size_t floats);
 /* Device-resident greedy decode for throughput measurement: decode `first_token`

@@ -71,6 +71,7 @@ SIGNATURES = {
     "lunelette_cuda_gemm_fp8": (ctypes.c_int, [P, SZ, SZ, ctypes.c_float, P, P, SZ, P, P]),
     "lunelette_cuda_gemm_qkv_rope": (ctypes.c_int, [P, P, P, P, SZ, SZ, P, P, P, P, P, SZ, SZ, P]),
     "lunelette_cuda_gemm_gateup_swiglu": (ctypes.c_int, [P, ctypes.c_float, ctypes.c_float, P, P, SZ, P, P]),
+    "lunelette_cuda_kv_copy": (ctypes.c_int, [P, SZ, SZ, P, P, SZ, SZ, P]),
     "lunelette_cuda_gemm_fp8_timed": (ctypes.c_int, [P, SZ, SZ, SZ, ctypes.c_float, P, SZ, P, ctypes.c_int, P, P]),
     "lunelette_cuda_rmsnorm": (ctypes.c_int, [P, P, SZ, SZ, P, P]),
     "lunelette_cuda_head_bf16": (ctypes.c_int, [P, SZ, SZ, P, P, P, P, P]),

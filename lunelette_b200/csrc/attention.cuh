@@ -344,6 +344,32 @@ static __global__ void __launch_bounds__(kPfThreads) attention_prefill_kernel(At
     }
 }
 
+// ---- KV prefix copy / remap ---------------------------------------------------------
+// Copies KV pages of the pool: for pair i, every layer's K and V rows of page
+// src_pages[i] go to page dst_pages[i] (slots [0, 64), or [0, last_slots) for
+// the last pair). A sequence that forks from another shares its full pages
+// through the page table and copies only the partial last page (copy on write),
+// or copies its whole prefix to pages of its own. Grid (pairs, layers * 16):
+// one block per (pair, layer, kind, KV head) segment of up to 32 KB.
+struct KvCopyParams {
+    float *kv;
+    int num_pages;
+    const int *src_pages, *dst_pages;
+    int pairs, last_slots;
+};
+
+static __global__ void __launch_bounds__(256) kv_copy_kernel(KvCopyParams p)
+{
+    const int i = blockIdx.x, seg = blockIdx.y;
+    const int layer = seg >> 4, kind = (seg >> 3) & 1, head = seg & 7;
+    const int slots = i == p.pairs - 1 ? p.last_slots : kPage;
+    const float4 *src =
+        reinterpret_cast<const float4 *>(p.kv + kv_offset(layer, p.num_pages, p.src_pages[i], kind, head, 0));
+    float4 *dst = reinterpret_cast<float4 *>(p.kv + kv_offset(layer, p.num_pages, p.dst_pages[i], kind, head, 0));
+    const int n = slots * (kHeadDim / 4);
+    for (int j = threadIdx.x; j < n; j += blockDim.x) dst[j] = __ldcg(src + j);
+}
+
 // x[t][c] = widen(E[ids[t]][c]) for the call's tokens (src/metal_runtime.m:391-395).
 static __global__ void embed_kernel(const uint16_t *embedding, const StepParams *step, float *x,
                              int count)

@@ -363,3 +363,22 @@ LUN_API int lunelette_cuda_attention(const float *q, const float *kv_pool, const
     lun_attention_plan(&a, (int)(length + count), (int)count, sm_count_of_current(), (int)slots);
     return ok(lun_launch_attention(a, (int)count, (cudaStream_t)stream));
 }
+
+// KV prefix copy / remap: for i < pairs, all layers' K and V of page
+// src_pages[i] -> page dst_pages[i] (device arrays), the last pair only its
+// first last_slots positions.
+LUN_API int lunelette_cuda_kv_copy(float *kv_pool, size_t num_pages, size_t layers, const int *src_pages,
+                                   const int *dst_pages, size_t pairs, size_t last_slots, void *stream)
+{
+    if (!kv_pool || !src_pages || !dst_pages || !num_pages || !layers || layers > 1024 || !pairs ||
+        pairs > num_pages || !last_slots || last_slots > (size_t)kPage)
+        return -1;
+    KvCopyParams p;
+    p.kv = kv_pool;
+    p.num_pages = (int)num_pages;
+    p.src_pages = src_pages;
+    p.dst_pages = dst_pages;
+    p.pairs = (int)pairs;
+    p.last_slots = (int)last_slots;
+    return ok(lun_launch_kv_copy(p, (int)layers, (cudaStream_t)stream));
+}

@@ -315,3 +315,10 @@ cudaError_t lun_launch_fp8_decode(const uint8_t *codes, size_t n, float scale, f
     fp8_decode_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0, stream>>>(codes, n, scale, out);
     return cudaGetLastError();
 }
+
+cudaError_t lun_launch_kv_copy(const KvCopyParams &p, int layers, cudaStream_t stream)
+{
+    if (p.pairs <= 0 || layers <= 0 || p.last_slots <= 0 || p.last_slots > kPage) return cudaErrorInvalidValue;
+    kv_copy_kernel<<<dim3(p.pairs, layers * 2 * kKVHeads), 256, 0, stream>>>(p);
+    return cudaGetLastError();
+}

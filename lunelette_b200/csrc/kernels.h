@@ -26,6 +26,9 @@ cudaError_t lun_launch_head(const lun::HeadParams &p, int sm_count, cudaStream_t
 void lun_attention_plan(lun::AttnParams *a, int total, int count, int sm_count, int slots);
 cudaError_t lun_launch_attention(const lun::AttnParams &a, int count, cudaStream_t stream);
 
+// KV page copies (attention.cuh kv_copy_kernel) over `layers` layers of the pool.
+cudaError_t lun_launch_kv_copy(const lun::KvCopyParams &p, int layers, cudaStream_t stream);
+
 // x[t] = widen(embedding[step->ids[t]]) for t < count.
 cudaError_t lun_launch_embed(const uint16_t *embedding, const lun::StepParams *step, float *x, int count,
                              cudaStream_t stream);

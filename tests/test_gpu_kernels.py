@@ -414,3 +414,30 @@ def test_attention_random_matches_oracle(lib, oracle, torch_cuda, length, count,
     got = run_attention(lib, torch, q, pool, table, num_pages, layer, length, count, slots)
     want = oracle.attention(q, k, v, length)
     assert np.abs(got - want).max() < 1e-5 * max(1.0, np.abs(want).max())
+
+
+def test_kv_copy_fork_pages_bit_exact(lib, torch_cuda):
+    """KV prefix reuse: a forked sequence copies pages of the pool. Full pages
+    move whole; the last pair moves only its first last_slots positions; every
+    other page and layer is untouched."""
+    torch = torch_cuda
+    layers, num_pages = 26, 9
+    rng = np.random.default_rng(41)
+    pool = rng.standard_normal(layers * num_pages * 2 * 8 * 64 * 128).astype(np.float32)
+    src = np.array([4, 7, 2], np.int32)   # the source sequence's pages (positions 0..63, 64..127, 128..)
+    dst = np.array([1, 8, 5], np.int32)   # the forked sequence's own pages
+    last = 23                              # the prefix ends at position 128 + 23
+    d_pool = dev(torch, pool)
+    assert lib.lunelette_cuda_kv_copy(ptr(d_pool), num_pages, layers, ptr(dev(torch, src)), ptr(dev(torch, dst)),
+                                      3, last, stream(torch)) == 0
+    got = d_pool.cpu().numpy().reshape(layers, num_pages, 2, 8, 64, 128)
+    want = pool.reshape(layers, num_pages, 2, 8, 64, 128).copy()
+    for i, (a, b) in enumerate(zip(src, dst)):
+        n = last if i == 2 else 64
+        want[:, b, :, :, :n] = want[:, a, :, :, :n]
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    # argument checks
+    assert lib.lunelette_cuda_kv_copy(ptr(d_pool), num_pages, layers, ptr(dev(torch, src)), ptr(dev(torch, dst)),
+                                      3, 65, stream(torch)) == -1
+    assert lib.lunelette_cuda_kv_copy(ptr(d_pool), num_pages, layers, ptr(dev(torch, src)), ptr(dev(torch, dst)),
+                                      0, 5, stream(torch)) == -1

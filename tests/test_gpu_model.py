@@ -191,3 +191,77 @@ def test_long_context_decode_matches_multi_kernel_path(lib, checkpoint_path, mon
             runs.append(np.stack(steps))
     assert_close(runs[0], runs[1], "persistent vs multi-kernel decode at 700 positions")
     assert [int(np.argmax(s)) for s in runs[0]] == [int(np.argmax(s)) for s in runs[1]]
+
+
+@pytest.fixture(scope="module")
+def long_oracle(oracle, checkpoint_path):
+    m = oracle.open_model(checkpoint_path, 4352)
+    yield m
+    m.close()
+
+
+def test_c2_chunked_long_prefill_then_decode_matches_oracle(lib, checkpoint_path, long_oracle):
+    """Config 2 at reduced length: a 600-token prompt at context 4352 prefilled in
+    256-token chunks (tensor-core GEMM, tiled prefill attention, YaRN positions
+    past 256), then greedy decode; logits within the gate and the same tokens as
+    the oracle's unchunked forward."""
+    ids = prompt(2024, 600)
+    long_oracle.reset()
+    want, _, _ = long_oracle.forward(ids)
+    with L.Runtime(checkpoint_path, limits=(4352, 256)) as rt:
+        rt.prefill(ids[:256])
+        rt.append(ids[256:512])
+        got = rt.append(ids[512:]).copy()
+        assert_close(got, want, "600-token chunked prefill logits")
+        tok_gpu, tok_cpu = greedy(got), greedy(want)
+        assert tok_gpu == tok_cpu
+        for step in range(8):
+            got = rt.decode(tok_gpu).copy()
+            want, _, _ = long_oracle.forward([tok_cpu])
+            assert_close(got, want, "decode step %d after the long prompt" % step)
+            tok_gpu, tok_cpu = greedy(got), greedy(want)
+            assert tok_gpu == tok_cpu, "greedy divergence at step %d" % step
+        assert rt.length() == 608
+
+
+def test_c3_multi_turn_prefix_reuse_matches_oracle(lib, checkpoint_path, long_oracle):
+    """Config 3 at reduced length: a system prefix, then turns that each append
+    user tokens and decode greedily, with the session checkpointed after every
+    turn and restored before the next (the service's save/restore cycle), plus a
+    branch that restores the last saved turn and continues differently. Every logits
+    vector against the oracle run on the same token sequence."""
+    rng = np.random.default_rng(303)
+    prefix = rng.integers(1000, 131072, 96)
+    long_oracle.reset()
+    with L.Runtime(checkpoint_path, limits=(4352, 256)) as rt:
+        got = rt.prefill(prefix).copy()
+        want, _, _ = long_oracle.forward(prefix)
+        assert_close(got, want, "prefix")
+        cp = None
+        for turn in range(3):
+            if cp is not None:
+                cp.destroy()
+            cp = rt.checkpoint_create()  # the newest checkpoint replaces the previous one
+            rt.checkpoint_restore(cp)    # the session resumes from its saved state
+            start = rt.length()
+            user = rng.integers(1000, 131072, 40)
+            got = rt.append(user).copy()
+            want, _, _ = long_oracle.forward(user)
+            assert_close(got, want, "turn %d user tokens" % turn)
+            tok = greedy(got)
+            assert tok == greedy(want)
+            for step in range(4):
+                got = rt.decode(tok).copy()
+                want, _, _ = long_oracle.forward([tok])
+                assert_close(got, want, "turn %d decode %d" % (turn, step))
+                tok = greedy(got)
+                assert tok == greedy(want)
+        # branch: back to the state saved before the last turn, different user tokens
+        rt.checkpoint_restore(cp)
+        assert rt.length() == start
+        long_oracle.rewind(start)
+        user = rng.integers(1000, 131072, 33)
+        got = rt.append(user).copy()
+        want, _, _ = long_oracle.forward(user)
+        assert_close(got, want, "branch from the saved turn")
+        cp.destroy()
