@@ -52,6 +52,7 @@ constexpr int kMegaSmemBytes =
 constexpr unsigned kSpinLimit = 1u << 22;
 constexpr int kPhasesPerStep = kLayers * 4 + 1;  // 4 FP8 phases per layer, then the head
 constexpr int kAttnMaxRanges = 18;               // position ranges per KV head (8 x 18 <= CTAs)
+constexpr int kHeadModeMax = 112;                // positions up to which each query head gets a CTA
 constexpr int kQStride = 36;                     // floats per staged query quarter (32 + pad)
 constexpr int kCmbStride = 132;                  // floats per (warp, head) attention partial
 static_assert((16 * kQStride + 2 * kHeadDim + kMegaConsumerWarps * 4 * kCmbStride) * 4 <= kFragBytes,
@@ -324,12 +325,16 @@ __device__ __forceinline__ float stage_frag(uint32_t *frag, const float *src, co
     constexpr int kF4 = K / 4;
     constexpr int kPer = (kF4 + kMegaConsumers - 1) / kMegaConsumers;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float4 v[kPer];
+    const float4 *gain4 = reinterpret_cast<const float4 *>(gain);
+    // the row and the gain in one round of loads
+    float4 v[kPer], g[kPer];
 #pragma unroll
     for (int u = 0; u < kPer; u++) {
         const int idx = threadIdx.x + u * kMegaConsumers;
         v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        g[u] = make_float4(1.f, 1.f, 1.f, 1.f);
         if (idx < kF4) {
+            if (gain) g[u] = __ldg(gain4 + idx);
             if (emb) {
                 const uint2 e = *reinterpret_cast<const uint2 *>(emb + 4 * idx);
                 v[u] = make_float4(bf16_lo(e.x), bf16_hi(e.x), bf16_lo(e.y), bf16_hi(e.y));
@@ -338,7 +343,6 @@ __device__ __forceinline__ float stage_frag(uint32_t *frag, const float *src, co
             }
         }
     }
-    const float4 *gain4 = reinterpret_cast<const float4 *>(gain);
     float ss = 0.0f, mx = 0.0f;
 #pragma unroll
     for (int u = 0; u < kPer; u++) {
@@ -349,8 +353,8 @@ __device__ __forceinline__ float stage_frag(uint32_t *frag, const float *src, co
             ss += x.y * x.y;
             ss += x.z * x.z;
             ss += x.w * x.w;
-            const float4 g = gain ? __ldg(gain4 + idx) : make_float4(1.f, 1.f, 1.f, 1.f);
-            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(g.x * x.x), fabsf(g.y * x.y)), fmaxf(fabsf(g.z * x.z), fabsf(g.w * x.w))));
+            const float4 gg = g[u];
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(gg.x * x.x), fabsf(gg.y * x.y)), fmaxf(fabsf(gg.z * x.z), fabsf(gg.w * x.w))));
         }
     }
     ss = warp_sum(ss);
@@ -375,11 +379,11 @@ __device__ __forceinline__ float stage_frag(uint32_t *frag, const float *src, co
         if (idx < kF4) {
             float4 x = v[u];
             if (gain) {
-                const float4 g = __ldg(gain4 + idx);
-                x.x = g.x * (x.x * rs);
-                x.y = g.y * (x.y * rs);
-                x.z = g.z * (x.z * rs);
-                x.w = g.w * (x.w * rs);
+                const float4 gg = g[u];
+                x.x = gg.x * (x.x * rs);
+                x.y = gg.y * (x.y * rs);
+                x.z = gg.z * (x.z * rs);
+                x.w = gg.w * (x.w * rs);
             }
             uint32_t hi, lo;
             split_hilo(x.x * sc, x.y * sc, hi, lo);
@@ -528,8 +532,31 @@ __device__ __forceinline__ int attention_unit(int units)
     return (u < units && (int)((long long)u * G / units) == (int)b) ? u : -1;
 }
 
+// L2 prefetch of the K (kind 0) or V (kind 1) rows [begin, min(end, length))
+// of an attention unit: per page one contiguous run of this KV head's slots.
+__device__ __forceinline__ void attention_prefetch(const MegaParams &p, int layer, int length, int kvh, int range,
+                                                   int ranges, int kind)
+{
+    int per = (length + 1 + ranges - 1) / ranges;
+    per = (per + 7) & ~7;
+    const int begin = range * per, end = min(begin + per, length);
+    for (int p0 = begin; p0 < end;) {
+        const int slot = p0 % kPage, n = min(kPage - slot, end - p0);
+        const int page = p.page_table[p0 / kPage];
+        l2_prefetch(p.kv + kv_offset(layer, p.num_pages, page, kind, kvh, slot), (unsigned)n * kHeadDim * 4);
+        p0 += n;
+    }
+}
+
 // K (lanes = position x dim quarter) and V (lanes = dims) of one 8-position
 // sub-tile into registers; positions past `end` read as zero.
+__device__ __forceinline__ float4 ld_cg_f4(const float4 *p)
+{
+    float4 v;
+    asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
+}
+
 __device__ __forceinline__ void attention_load(const MegaParams &p, int layer, int kvh, int p0, int end, float4 (&kk)[8],
                                                float4 (&vv)[8])
 {
@@ -540,10 +567,10 @@ __device__ __forceinline__ void attention_load(const MegaParams &p, int layer, i
     const float *vb = p.kv + kv_offset(layer, p.num_pages, page, 1, kvh, p0 % kPage);
     const float4 *krow = reinterpret_cast<const float4 *>(kb + pp * kHeadDim + qd * 32);
 #pragma unroll
-    for (int c = 0; c < 8; c++) kk[c] = pp < n ? __ldcg(krow + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c = 0; c < 8; c++) kk[c] = pp < n ? ld_cg_f4(krow + c) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int t = 0; t < 8; t++)
-        vv[t] = t < n ? __ldcg(reinterpret_cast<const float4 *>(vb + t * kHeadDim) + lane)
+        vv[t] = t < n ? ld_cg_f4(reinterpret_cast<const float4 *>(vb + t * kHeadDim) + lane)
                       : make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
@@ -604,13 +631,13 @@ __device__ __forceinline__ void merge_ranges(const MegaParams &p, int kvh, int r
 // finishes a KV head's last range (ticket counter, `tickets` before this layer)
 // merges them in range order. Replaces scores + attend
 // (src/metal_kernels.metal:81-132).
-__device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, int length, int unit, int ranges,
-                                              unsigned epoch, unsigned tag, unsigned tickets, float *qs, float *cmb,
-                                              int *flag, bool rec)
+template <int HQ>
+__device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, int length, int kvh, int h0, int range,
+                                              int ranges, unsigned epoch, unsigned tag, unsigned tickets, float *qs,
+                                              float *cmb, int *flag, bool rec)
 {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, pp = lane >> 2, qd = lane & 3;
     const int total = length + 1;
-    const int kvh = unit / ranges, range = unit - kvh * ranges;
     int per = (total + ranges - 1) / ranges;
     per = (per + 7) & ~7;
     const int begin = range * per, end = min(begin + per, total);
@@ -624,14 +651,14 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
     {
         const unsigned long long *src;
         float *dst;
-        if (threadIdx.x < 128) {
+        if (threadIdx.x < 32 * HQ) {
             const int hq = threadIdx.x >> 5, d4 = threadIdx.x & 31;
-            src = p.qkvt + (size_t)(kvh * 4 + hq) * kHeadDim + 4 * d4;
+            src = p.qkvt + (size_t)(kvh * 4 + h0 + hq) * kHeadDim + 4 * d4;
             dst = qs + (hq * 4 + (d4 >> 3)) * kQStride + (d4 & 7) * 4;
-        } else if (threadIdx.x < 160) {
+        } else if (threadIdx.x >= 128 && threadIdx.x < 160) {
             src = p.qkvt + kQuery + kvh * kHeadDim + 4 * (threadIdx.x - 128);
             dst = kcur + 4 * (threadIdx.x - 128);
-        } else if (threadIdx.x < 192) {
+        } else if (threadIdx.x >= 160 && threadIdx.x < 192) {
             src = p.qkvt + kQuery + kKV + kvh * kHeadDim + 4 * (threadIdx.x - 160);
             dst = vcur + 4 * (threadIdx.x - 160);
         } else {
@@ -642,10 +669,10 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
     }
     consumers_sync();
     attention_patch(p0, length, kcur, vcur, kk, vv);
-    float m_run[4], l_run[4];
-    float4 o[4];
+    float m_run[HQ], l_run[HQ];
+    float4 o[HQ];
 #pragma unroll
-    for (int hq = 0; hq < 4; hq++) {
+    for (int hq = 0; hq < HQ; hq++) {
         m_run[hq] = -INFINITY;
         l_run[hq] = 0.0f;
         o[hq] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -656,9 +683,9 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
             attention_patch(p0, length, kcur, vcur, kk, vv);
         }
         const bool valid = pp < min(8, end - p0);
-        float pr[4];
+        float pr[HQ];
 #pragma unroll
-        for (int hq = 0; hq < 4; hq++) {
+        for (int hq = 0; hq < HQ; hq++) {
             const float4 *qv = reinterpret_cast<const float4 *>(qs + (hq * 4 + qd) * kQStride);
             float d = 0.0f;
 #pragma unroll
@@ -693,7 +720,7 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
 #pragma unroll
         for (int t = 0; t < 8; t++) {
 #pragma unroll
-            for (int hq = 0; hq < 4; hq++) {
+            for (int hq = 0; hq < HQ; hq++) {
                 const float pt = __shfl_sync(0xffffffffu, pr[hq], t * 4);
                 o[hq].x = fmaf(pt, vv[t].x, o[hq].x);
                 o[hq].y = fmaf(pt, vv[t].y, o[hq].y);
@@ -704,7 +731,7 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
     }
     // the warps' partials -> shared memory: [warp][head] o[128], m, l
 #pragma unroll
-    for (int hq = 0; hq < 4; hq++) {
+    for (int hq = 0; hq < HQ; hq++) {
         float *slot = cmb + (warp * 4 + hq) * kCmbStride;
         reinterpret_cast<float4 *>(slot)[lane] = o[hq];
         if (lane == 0) {
@@ -713,7 +740,7 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
         }
     }
     consumers_sync();
-    if (warp < 4) {
+    if (warp < HQ) {
         const int hq = warp;
         float M = -INFINITY;
         for (int w = 0; w < kMegaConsumerWarps; w++) {
@@ -735,7 +762,7 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
         }
         if (ranges == 1) {
             const float inv = 1.0f / L;
-            reinterpret_cast<float4 *>(p.attn + (size_t)(kvh * 4 + hq) * kHeadDim)[lane] =
+            reinterpret_cast<float4 *>(p.attn + (size_t)(kvh * 4 + h0 + hq) * kHeadDim)[lane] =
                 make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
         } else {
             const size_t at = (size_t)(kvh * ranges + range) * 4 + hq;
@@ -804,7 +831,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
     const uint4 *frag4 = reinterpret_cast<const uint4 *>(frag);
     float *xs_head = reinterpret_cast<float *>(frag);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    unsigned barrier = 0, taken = 0, seq = 0, tickets = 0;
+    unsigned barrier = 0, taken = 0, seq = 0, tickets = 0, attn_target = 0;
     for (int s = 0; s < p.steps; s++) {
         const bool rec = p.timeline && s == 0;
         const int length = __ldcg(&p.step->length);
@@ -813,8 +840,14 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
         for (int i = threadIdx.x; i < 2 * kHeadDim; i += kMegaConsumers)
             rope_s[i] = i < kHeadDim ? p.rope_cos[(size_t)length * kHeadDim + i]
                                      : p.rope_sin[(size_t)length * kHeadDim + i - kHeadDim];
-        const int ranges = attention_ranges(length + 1);
-        const int unit = attention_unit(kKVHeads * ranges);
+        // attention units: short contexts give each query head its own CTA
+        // (32 units); longer ones split each KV head's positions into ranges
+        const bool head_mode = length + 1 <= kHeadModeMax && (int)gridDim.x >= kQueryHeads;
+        const int ranges = head_mode ? 1 : attention_ranges(length + 1);
+        const int unit = attention_unit(head_mode ? kQueryHeads : kKVHeads * ranges);
+        const int akvh = unit < 0 ? 0 : (head_mode ? unit / 4 : unit / ranges);
+        const int ah0 = head_mode ? unit % 4 : 0, arange = head_mode ? 0 : unit - akvh * ranges;
+        const unsigned attn_signals = head_mode ? kQueryHeads : kKVHeads;
         for (int layer = 0; layer < kLayers; layer++) {
             const unsigned epoch = (unsigned)(s * kLayers + layer) + 1;  // layers run by the launch, this one included
             const float *sc = p.scales + layer * 7;
@@ -838,6 +871,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
             gp.qkv_tagged = p.qkvt;
             gp.ytag = p.tag_base + epoch - 1;
             const int mk = layer * kMarksPerLayer;
+            // the attention unit's K/V rows of earlier steps do not depend on
+            // this layer's qkv: start them towards L2 now
+            if (unit >= 0 && threadIdx.x < 2) attention_prefetch(p, layer, length, akvh, arange, ranges, threadIdx.x);
             float inv = stage_frag<kHidden>(frag, p.x, layer == 0 ? emb_row : nullptr,
                                             p.norms + (size_t)(2 * layer) * kHidden, red);
             if (threadIdx.x == 0) record_mark(p, rec, mk);
@@ -855,11 +891,16 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
             }
             if (unit >= 0) {
                 float *qs = reinterpret_cast<float *>(frag);
-                cta_attention(p, layer, length, unit, ranges, epoch, gp.ytag, tickets, qs,
-                              qs + 16 * kQStride + 2 * kHeadDim, &flag, rec);
+                if (head_mode)
+                    cta_attention<1>(p, layer, length, akvh, ah0, 0, 1, epoch, gp.ytag, tickets, qs,
+                                     qs + 16 * kQStride + 2 * kHeadDim, &flag, rec);
+                else
+                    cta_attention<4>(p, layer, length, akvh, 0, arange, ranges, epoch, gp.ytag, tickets, qs,
+                                     qs + 16 * kQStride + 2 * kHeadDim, &flag, rec);
                 consumers_sync();
             }
             if (ranges > 1) tickets += (unsigned)ranges;
+            attn_target += attn_signals;
             // o + residual (x)
             sp = phase_span(p, layer, kPhO);
             gp.rows = kHidden;
@@ -872,7 +913,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
             gp.y_stride = kHidden;
             stage_rows(res_s, p.x, gp.res_base, sp.items / (kQuery / kBlockCols / item_blocks(kPhO)) * kTileRows);
             // every KV head's attention output stored
-            if (threadIdx.x == 0) thread_wait(sync_word(p, kSyncAttn), (unsigned)kKVHeads * epoch, p.error);
+            if (threadIdx.x == 0) thread_wait(sync_word(p, kSyncAttn), attn_target, p.error);
             consumers_sync();
             inv = stage_frag<kQuery>(frag, p.attn, nullptr, nullptr, red);
             if (threadIdx.x == 0) record_mark(p, rec, mk + 4);

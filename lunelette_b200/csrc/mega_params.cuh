@@ -26,7 +26,8 @@ constexpr int kMegaTimelineHead = 1 + kMegaBarriersPerStep;
 // Synchronisation words of one launch, each on its own 128-byte line, zero at
 // launch and only ever increased (targets grow with the layers the launch ran):
 //   kSyncBarrier        grid barrier arrivals (gridDim per barrier)
-//   kSyncAttn           KV heads whose attention output is stored (8 per layer)
+//   kSyncAttn           attention units whose output is stored (8 per layer, or 32 when
+//                       each query head has its own unit)
 //   kSyncTicket + kvh   attention ranges of KV head kvh finished
 //   kSyncPick           CTAs done with the head (gridDim per step)
 constexpr int kSyncStride = 32;
