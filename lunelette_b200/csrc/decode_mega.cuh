@@ -938,16 +938,19 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
             consumers_sync();
             if (threadIdx.x == 0) record_mark(p, rec, mk + 8);
             fp8_epilogue<kEpiSwiGLU>(gp, sp, kHidden / kBlockCols / item_blocks(kPhGateUp), partial, inv);
+            // down's residual rows (h) are final since the o barrier: staged
+            // before this barrier, off the down phase's critical path
+            sp = phase_span(p, layer, kPhDown);
+            stage_rows(res_s, p.h, sp.first * kTileRows,
+                       sp.items / (kInner / kBlockCols / item_blocks(kPhDown)) * kTileRows);
             grid_sync(p, ++barrier, rec, mk + 9);
             // down + residual (h)
-            sp = phase_span(p, layer, kPhDown);
             gp.rows = kHidden;
             gp.cols = kInner;
             gp.scale[0] = gp.scale[1] = gp.scale[2] = sc[6];
             gp.res_base = sp.first * kTileRows;
             gp.y = p.x;
             gp.y_stride = kHidden;
-            stage_rows(res_s, p.h, gp.res_base, sp.items / (kInner / kBlockCols / item_blocks(kPhDown)) * kTileRows);
             inv = stage_frag<kInner>(frag, p.act, nullptr, nullptr, red);
             if (threadIdx.x == 0) record_mark(p, rec, mk + 10);
             consume_fp8<item_blocks(kPhDown), kInner / kBlockCols>(ring, sp, seq, taken, frag4, partial, p.error);
