@@ -131,6 +131,39 @@ int lunelette_cuda_attention_noalloc(const float *q, const float *kv_pool, const
 
 /* Keep every layer's output rows (which 0..25) and the final-norm rows (26) of
  * the most recent call; host copy of count*3072 floats. Host-synchronous. */
+/* ---------------- batched decode over many sessions (one weight replica) */
+
+/* One set of weights and a paged FP32 KV pool of pool_positions positions
+ * (rounded up to pages of 64) shared by up to max_sessions independent
+ * sessions of up to `context` (<= 4352) positions each; `block` (8..256)
+ * bounds the tokens of one append and the sessions of one decode step. The
+ * reference serves one sequence per context (src/metal_internal.h:29-50); this
+ * is the multi-session engine the service's many users share. Returns NULL
+ * with a diagnostic on failure. Single caller per batch context. */
+typedef struct lunelette_cuda_batch lunelette_cuda_batch;
+lunelette_cuda_batch *lunelette_cuda_batch_create(const char *path, size_t max_sessions, size_t context,
+    size_t pool_positions, size_t block, char *error, size_t capacity);
+void lunelette_cuda_batch_destroy(lunelette_cuda_batch *batch);
+/* A new empty session (its id into *session); -1 when all are in use. */
+int lunelette_cuda_batch_open(lunelette_cuda_batch *batch, int *session, char *error, size_t capacity);
+/* Return the session's pages to the pool. */
+int lunelette_cuda_batch_close(lunelette_cuda_batch *batch, int session);
+/* Prefill or extend one session by count (1..block) tokens, as
+ * lunelette_metal_prefill/append; *logits borrows the last token's 131072
+ * host logits until the next call. */
+int lunelette_cuda_batch_append(lunelette_cuda_batch *batch, int session, const int64_t *ids, size_t count,
+    const float **logits, char *error, size_t capacity);
+/* One greedy decode step for n (1..block) distinct non-empty sessions, token
+ * ids[i] of session sessions[i] at its current length: the projections run
+ * once for all n tokens (tcgen05 GEMMs), attention per token over its own
+ * pages. next[i] receives the greedy id (strict '>', lowest id on ties); when
+ * logits is not NULL it receives the n x 131072 logits. */
+int lunelette_cuda_batch_decode(lunelette_cuda_batch *batch, const int *sessions, const int64_t *ids, size_t n,
+    float *logits, int64_t *next, char *error, size_t capacity);
+/* Positions held by an open session (0 otherwise), and free pool positions. */
+size_t lunelette_cuda_batch_length(const lunelette_cuda_batch *batch, int session);
+size_t lunelette_cuda_batch_free_positions(const lunelette_cuda_batch *batch);
+
 /* KV prefix reuse across sequences: copies pages of the paged FP32 pool
  * [layer][page][K|V][8 heads][64 slots][128]. For i < pairs, every layer's
  * K and V of page src_pages[i] go to page dst_pages[i] (device int arrays);

@@ -71,6 +71,14 @@ SIGNATURES = {
     "lunelette_cuda_gemm_fp8": (ctypes.c_int, [P, SZ, SZ, ctypes.c_float, P, P, SZ, P, P]),
     "lunelette_cuda_gemm_qkv_rope": (ctypes.c_int, [P, P, P, P, SZ, SZ, P, P, P, P, P, SZ, SZ, P]),
     "lunelette_cuda_gemm_gateup_swiglu": (ctypes.c_int, [P, ctypes.c_float, ctypes.c_float, P, P, SZ, P, P]),
+    "lunelette_cuda_batch_create": (ctypes.c_void_p, [ctypes.c_char_p, SZ, SZ, SZ, SZ, ctypes.c_char_p, SZ]),
+    "lunelette_cuda_batch_destroy": (None, [P]),
+    "lunelette_cuda_batch_open": (ctypes.c_int, [P, P, ctypes.c_char_p, SZ]),
+    "lunelette_cuda_batch_close": (ctypes.c_int, [P, ctypes.c_int]),
+    "lunelette_cuda_batch_append": (ctypes.c_int, [P, ctypes.c_int, P, SZ, P, ctypes.c_char_p, SZ]),
+    "lunelette_cuda_batch_decode": (ctypes.c_int, [P, P, P, SZ, P, P, ctypes.c_char_p, SZ]),
+    "lunelette_cuda_batch_length": (SZ, [P, ctypes.c_int]),
+    "lunelette_cuda_batch_free_positions": (SZ, [P]),
     "lunelette_cuda_kv_copy": (ctypes.c_int, [P, SZ, SZ, P, P, SZ, SZ, P]),
     "lunelette_cuda_gemm_fp8_timed": (ctypes.c_int, [P, SZ, SZ, SZ, ctypes.c_float, P, SZ, P, ctypes.c_int, P, P]),
     "lunelette_cuda_rmsnorm": (ctypes.c_int, [P, P, SZ, SZ, P, P]),
@@ -256,3 +264,64 @@ class Runtime:
         if library().lunelette_cuda_trace_copy(self.handle, which, out.ctypes.data, out.size):
             raise LuneletteError("trace copy failed")
         return out
+
+
+class Batch:
+    """Many independent sessions over one weight replica and a paged KV pool
+    (lunelette_cuda_batch_*): per-session appends, batched greedy decode steps."""
+
+    def __init__(self, path, max_sessions, context=4352, pool_positions=None, block=256):
+        lib = library()
+        err = _error()
+        pool = pool_positions if pool_positions is not None else max_sessions * context
+        self.handle = lib.lunelette_cuda_batch_create(os.fsencode(path), max_sessions, context, pool, block, err, 512)
+        if not self.handle:
+            raise LuneletteError(err.value.decode())
+
+    def close(self):
+        if getattr(self, "handle", None):
+            library().lunelette_cuda_batch_destroy(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def open(self):
+        err = _error()
+        s = ctypes.c_int()
+        if library().lunelette_cuda_batch_open(self.handle, ctypes.byref(s), err, 512):
+            raise LuneletteError(err.value.decode())
+        return s.value
+
+    def close_session(self, session):
+        if library().lunelette_cuda_batch_close(self.handle, int(session)):
+            raise LuneletteError("close of a session that is not open")
+
+    def append(self, session, ids):
+        arr, p = _ids(ids)
+        err = _error()
+        out = ctypes.c_void_p()
+        if library().lunelette_cuda_batch_append(self.handle, int(session), p, arr.size, ctypes.byref(out), err, 512):
+            raise LuneletteError(err.value.decode())
+        return np.ctypeslib.as_array(ctypes.cast(out, ctypes.POINTER(ctypes.c_float)), shape=(VOCAB,))
+
+    def decode(self, sessions, ids, logits=False):
+        """One step: returns the greedy next ids (and the n x VOCAB logits)."""
+        ss = np.ascontiguousarray(np.asarray(sessions, np.int32))
+        arr, p = _ids(ids)
+        nxt = np.empty(ss.size, np.int64)
+        lg = np.empty((ss.size, VOCAB), np.float32) if logits else None
+        err = _error()
+        if library().lunelette_cuda_batch_decode(self.handle, ss.ctypes.data, p, ss.size,
+                                                 lg.ctypes.data if logits else None, nxt.ctypes.data, err, 512):
+            raise LuneletteError(err.value.decode())
+        return (nxt, lg) if logits else nxt
+
+    def length(self, session):
+        return library().lunelette_cuda_batch_length(self.handle, int(session))
+
+    def free_positions(self):
+        return library().lunelette_cuda_batch_free_positions(self.handle)

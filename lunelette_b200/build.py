@@ -23,7 +23,7 @@ NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 CC = "/usr/bin/gcc" if os.path.exists("/usr/bin/gcc") else "gcc"
 CXX = "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else "g++"
 
-C_SOURCES = ["st.c", "weights.c", "runtime.c", "synth.c"]
+C_SOURCES = ["st.c", "weights.c", "runtime.c", "synth.c", "batch.c"]
 CU_SOURCES = ["device.cu", "kernels.cu", "kernel_api.cu", "noalloc.cu", "mega.cu", "prefill.cu"]
 INCLUDES = ["-I" + os.path.join(REPO, "include"), "-I" + CSRC, "-I" + os.path.join(CUDA_HOME, "include")]
 CFLAGS = ["-std=c11", "-O2", "-fPIC", "-fvisibility=hidden", "-Wall", "-Wextra",

@@ -29,6 +29,12 @@ struct AttnParams {
     float *out;              // [count][4096] when splits == 1
     float *part_acc;         // [count][32][splits][128]
     float *part_ml;          // [count][32][splits][2]
+    // Batched decode over independent sessions: token t sits at position
+    // positions[t] of the session whose page table is page_table +
+    // token_table[t] * table_stride (nullptr: one sequence, positions
+    // length + token_offset + t over page_table).
+    const int *positions, *token_table;
+    int table_stride;
 };
 
 constexpr int kTile = 32;
@@ -48,8 +54,8 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 __device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 // Issue the copies of one 32-position K/V tile (2 x 16 KB) into a stage.
-__device__ __forceinline__ void attention_issue_tile(const AttnParams &p, float *stage, int kvh, int p0,
-                                                     int end)
+__device__ __forceinline__ void attention_issue_tile(const AttnParams &p, const int *table, float *stage, int kvh,
+                                                     int p0, int end)
 {
     float *ks = stage, *vs = stage + kTile * kKPad;
     for (int c = threadIdx.x; c < 2 * kTile * 32; c += blockDim.x) {
@@ -58,7 +64,7 @@ __device__ __forceinline__ void attention_issue_tile(const AttnParams &p, float 
         bool in = pos < end;
         const float *src = p.kv;
         if (in) {
-            int page = p.page_table[pos / kPage];
+            int page = table[pos / kPage];
             src = p.kv + kv_offset(p.layer, p.num_pages, page, kind, kvh, pos % kPage) + chunk * 4;
         }
         float *dst = kind == 0 ? ks + row * kKPad + chunk * 4 : vs + row * kHeadDim + chunk * 4;
@@ -80,11 +86,13 @@ static __global__ void __launch_bounds__(128) attention_split_kernel(AttnParams 
     const int head = kvh * 4 + warp;
     pdl_wait();  // q and the newest K/V rows come from the previous kernel
     pdl_launch_dependents();
-    const int total = (p.step ? p.step->length : p.length) + p.token_offset + t + 1;
+    const int total = p.positions ? p.positions[t] + 1
+                                  : (p.step ? p.step->length : p.length) + p.token_offset + t + 1;
+    const int *table = p.positions ? p.page_table + (size_t)p.token_table[t] * p.table_stride : p.page_table;
     const int begin = split * p.split_len;
     const int end = min(begin + p.split_len, total);
     const int tiles = end > begin ? (end - begin + kTile - 1) / kTile : 0;
-    if (tiles > 0) attention_issue_tile(p, stages, kvh, begin, end);
+    if (tiles > 0) attention_issue_tile(p, table, stages, kvh, begin, end);
 
     for (int i = threadIdx.x; i < 4 * kHeadDim; i += blockDim.x)
         qs[i] = p.q[(size_t)t * kQuery + kvh * 4 * kHeadDim + i];
@@ -93,7 +101,8 @@ static __global__ void __launch_bounds__(128) attention_split_kernel(AttnParams 
     float o[4] = {0.f, 0.f, 0.f, 0.f};
     for (int it = 0; it < tiles; it++) {
         const int p0 = begin + it * kTile;
-        if (it + 1 < tiles) attention_issue_tile(p, stages + ((it + 1) & 1) * kStageFloats, kvh, p0 + kTile, end);
+        if (it + 1 < tiles)
+            attention_issue_tile(p, table, stages + ((it + 1) & 1) * kStageFloats, kvh, p0 + kTile, end);
         else cp_async_commit();  // empty group keeps the wait count uniform
         cp_async_wait_one();
         __syncthreads();

@@ -37,7 +37,8 @@ struct lun_device {
     uint16_t *embedding = nullptr;
     float *norms = nullptr, *final_norm = nullptr;
     float *kv = nullptr;
-    int *page_table = nullptr;
+    int *page_table = nullptr;          // the table the kernels read (a session's row in batch mode)
+    int *own_table = nullptr;           // the identity table allocated with the device
     float *rope_cos = nullptr, *rope_sin = nullptr;
     StepParams *d_step = nullptr, *h_step = nullptr;
     float *x = nullptr, *h = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
@@ -72,6 +73,13 @@ struct lun_device {
     unsigned long long *timeline = nullptr;      // per-barrier timestamps (optional)
     bool record_timeline = false;
     lun_device_bytes owned = {};
+    size_t part_slots = kPartSlots;
+    // batched decode over sessions (lun_device_create_batch)
+    int max_sessions = 0, session_pages = 0;
+    int *session_tables = nullptr;      // [max_sessions][session_pages] page ids
+    int *d_meta = nullptr, *h_meta = nullptr;  // [block] positions, then [block] session of each token
+    float *batch_logits = nullptr;      // [block][vocab]
+    int *d_next = nullptr, *h_next = nullptr;
 };
 
 static int fail(char *error, size_t capacity, const char *what, cudaError_t e)
@@ -108,10 +116,15 @@ static cudaError_t dalloc(T **p, size_t bytes, uint64_t *counter)
     return e;
 }
 
-extern "C" lun_device *lun_device_create(size_t context, size_t block, char *error, size_t capacity)
+// context: positions of one sequence (RoPE table, bounds); kv_pages: pages of
+// the KV pool; part_slots: attention partial slots.
+static lun_device *create_device(size_t context, size_t kv_pages, size_t block, size_t part_slots, char *error,
+                                 size_t capacity)
 {
     lun_device_bytes plan;
     lun_device_plan(context, block, &plan);
+    plan.kv_bytes = (uint64_t)kLayers * kv_pages * 2 * kPageKind * sizeof(float);
+    plan.scratch_bytes += (uint64_t)(part_slots > kPartSlots ? part_slots - kPartSlots : 0) * (kHeadDim + 2) * 4;
     int ordinal = 0;
     cudaError_t e = cudaGetDevice(&ordinal);
     if (e != cudaSuccess) {
@@ -148,7 +161,8 @@ extern "C" lun_device *lun_device_create(size_t context, size_t block, char *err
     d->sm_count = prop.multiProcessorCount;
     d->context = context;
     d->block = block;
-    d->num_pages = (int)pages_for(context);
+    d->num_pages = (int)kv_pages;
+    d->part_slots = part_slots;
     uint64_t *wc = &d->owned.weight_bytes, *kc = &d->owned.kv_bytes, *sc = &d->owned.scratch_bytes;
     const char *what = "stream";
     if ((e = cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking)) != cudaSuccess) goto bad;
@@ -170,11 +184,11 @@ extern "C" lun_device *lun_device_create(size_t context, size_t block, char *err
         (e = dalloc(&d->attn, block * kQuery * 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->act, block * kInner * 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->logits, (size_t)kVocab * 4, sc)) != cudaSuccess ||
-        (e = dalloc(&d->part_acc, kPartSlots * kHeadDim * 4, sc)) != cudaSuccess ||
-        (e = dalloc(&d->part_ml, kPartSlots * 2 * 4, sc)) != cudaSuccess ||
+        (e = dalloc(&d->part_acc, part_slots * kHeadDim * 4, sc)) != cudaSuccess ||
+        (e = dalloc(&d->part_ml, part_slots * 2 * 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->rope_cos, context * kHeadDim * 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->rope_sin, context * kHeadDim * 4, sc)) != cudaSuccess ||
-        (e = dalloc(&d->page_table, (size_t)d->num_pages * 4, sc)) != cudaSuccess ||
+        (e = dalloc(&d->own_table, (size_t)d->num_pages * 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->d_flag, 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->d_scales, (size_t)kLayers * LUN_SLOT_COUNT * 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->mega_sync, kSyncWords * kSyncStride * sizeof(unsigned), sc)) != cudaSuccess ||
@@ -227,6 +241,7 @@ extern "C" lun_device *lun_device_create(size_t context, size_t block, char *err
             goto bad;
         }
         for (int i = 0; i < d->num_pages; i++) table[i] = i;
+        d->page_table = d->own_table;
         e = cudaMemcpy(d->page_table, table, (size_t)d->num_pages * 4, cudaMemcpyHostToDevice);
         free(table);
         if (e != cudaSuccess) goto bad;
@@ -238,6 +253,63 @@ bad:
     fail(error, capacity, what, e);
     lun_device_destroy(d);
     return nullptr;
+}
+
+extern "C" lun_device *lun_device_create(size_t context, size_t block, char *error, size_t capacity)
+{
+    return create_device(context, pages_for(context), block, kPartSlots, error, capacity);
+}
+
+extern "C" lun_device *lun_device_create_batch(size_t pool_pages, size_t session_context, size_t block,
+                                               size_t max_sessions, char *error, size_t capacity)
+{
+    if (!pool_pages || !session_context || block <= (size_t)kGemvMaxTokens || block > 256 || !max_sessions ||
+        max_sessions > 65536) {
+        if (error && capacity) snprintf(error, capacity, "batch: invalid pool, context, block or sessions");
+        return nullptr;
+    }
+    // partial slots for block tokens x 32 heads x up to 16 position splits
+    const size_t slots = block * kQueryHeads * 16 > kPartSlots ? block * kQueryHeads * 16 : kPartSlots;
+    lun_device *d = create_device(session_context, pool_pages, block, slots, error, capacity);
+    if (!d) return nullptr;
+    d->max_sessions = (int)max_sessions;
+    d->session_pages = (int)pages_for(session_context);
+    uint64_t *sc = &d->owned.scratch_bytes;
+    cudaError_t e;
+    const char *what = "batch tables";
+    if ((e = dalloc(&d->session_tables, (size_t)max_sessions * d->session_pages * sizeof(int), sc)) != cudaSuccess ||
+        (e = cudaMemset(d->session_tables, 0, (size_t)max_sessions * d->session_pages * sizeof(int))) !=
+            cudaSuccess ||
+        (e = dalloc(&d->d_meta, 2 * block * sizeof(int), sc)) != cudaSuccess || !d->pf.ws ||
+        (e = dalloc(&d->batch_logits, block * (size_t)kVocab * sizeof(float), sc)) != cudaSuccess ||
+        (e = dalloc(&d->d_next, block * sizeof(int), sc)) != cudaSuccess ||
+        (e = cudaMallocHost((void **)&d->h_meta, 2 * block * sizeof(int))) != cudaSuccess ||
+        (e = cudaMallocHost((void **)&d->h_next, block * sizeof(int))) != cudaSuccess) {
+        fail(error, capacity, what, e);
+        lun_device_destroy(d);
+        return nullptr;
+    }
+    return d;
+}
+
+extern "C" int lun_device_session_table(lun_device *d, int session, const int *pages, size_t n)
+{
+    if (!d->session_tables || session < 0 || session >= d->max_sessions || n > (size_t)d->session_pages) return -1;
+    for (size_t i = 0; i < n; i++)
+        if (pages[i] < 0 || pages[i] >= d->num_pages) return -1;
+    if (cudaSetDevice(d->ordinal) != cudaSuccess) return -1;
+    if (cudaStreamSynchronize(d->stream) != cudaSuccess) return -1;
+    return cudaMemcpy(d->session_tables + (size_t)session * d->session_pages, pages, n * sizeof(int),
+                      cudaMemcpyHostToDevice) == cudaSuccess
+               ? 0
+               : -1;
+}
+
+extern "C" int lun_device_use_session(lun_device *d, int session)
+{
+    if (!d->session_tables || session < 0 || session >= d->max_sessions) return -1;
+    d->page_table = d->session_tables + (size_t)session * d->session_pages;
+    return 0;
 }
 
 extern "C" void lun_device_destroy(lun_device *d)
@@ -259,13 +331,19 @@ extern "C" void lun_device_destroy(lun_device *d)
     cudaFree(d->part_ml);
     cudaFree(d->rope_cos);
     cudaFree(d->rope_sin);
-    cudaFree(d->page_table);
+    cudaFree(d->own_table);
     cudaFree(d->d_flag);
     cudaFree(d->trace_buf);
     cudaFree(d->d_tokens);
     cudaFree(d->d_partials);
     cudaFree(d->d_scales);
     cudaFree(d->mega_sync);
+    cudaFree(d->session_tables);
+    cudaFree(d->d_meta);
+    cudaFree(d->batch_logits);
+    cudaFree(d->d_next);
+    cudaFreeHost(d->h_meta);
+    cudaFreeHost(d->h_next);
     cudaFree(d->mega_qkvt);
     cudaFree(d->mega_error);
     cudaFree(d->arg_val);
@@ -456,10 +534,12 @@ static GemvParams layer_gemv(lun_device *d, int layer, int which)
 }
 
 // Launch `which` projection of `layer` over all `count` tokens in groups of <= 4.
-static cudaError_t run_projection(lun_device *d, int layer, int which, int count)
+// batched: tokens of independent sessions (batched decode): always the
+// tcgen05 path, whose QKV epilogue takes per-token positions and page tables.
+static cudaError_t run_projection(lun_device *d, int layer, int which, int count, bool batched = false)
 {
     static const int epi[4] = {kEpiQKV, kEpiResidual, kEpiSwiGLU, kEpiResidual};
-    const bool gemm = count > kGemvMaxTokens && d->use_gemm;
+    const bool gemm = batched || (count > kGemvMaxTokens && d->use_gemm);
     for (int t0 = 0; t0 < count; t0 += gemm ? count : kGemvMaxTokens) {
         int m = count - t0 < kGemvMaxTokens ? count - t0 : kGemvMaxTokens;
         GemvParams p = layer_gemv(d, layer, which);
@@ -496,6 +576,12 @@ static cudaError_t run_projection(lun_device *d, int layer, int which, int count
         }
         if (gemm) {
             p.prefetch = nullptr;  // the GEMM is tensor-bound; no next-matrix prefetch
+            if (batched) {
+                p.positions = d->d_meta;
+                p.token_table = d->d_meta + d->block;
+                p.table_stride = d->session_pages;
+                p.page_table = d->session_tables;
+            }
             return lun_launch_prefill(p, count, epi[which], d->pf, d->sm_count, d->stream);
         }
         cudaError_t e = lun_launch_gemv(p, m, epi[which], d->sm_count, d->stream);
@@ -521,7 +607,7 @@ static cudaError_t run_attention(lun_device *d, int layer, int count, size_t len
     // A captured graph serves every length, so it plans for the full context;
     // splits past the current length find no positions and contribute nothing.
     int total = fixed_plan ? (int)d->context : (int)(length + count);
-    lun_attention_plan(&a, total, count, d->sm_count, (int)kPartSlots);
+    lun_attention_plan(&a, total, count, d->sm_count, (int)d->part_slots);
     return lun_launch_attention(a, count, d->stream);
 }
 
@@ -589,7 +675,7 @@ static cudaError_t enqueue_decode_step(lun_device *d, int *launches)
             (e = run_projection(d, layer, 3, 1)) != cudaSuccess)
             break;
         AttnParams a;
-        lun_attention_plan(&a, (int)d->context, 1, d->sm_count, (int)kPartSlots);
+        lun_attention_plan(&a, (int)d->context, 1, d->sm_count, (int)d->part_slots);
         n += 5 + (a.splits > 1 ? 1 : 0);
     }
     if (e != cudaSuccess) return e;
@@ -791,6 +877,108 @@ extern "C" int lun_device_run(lun_device *d, const int64_t *ids, size_t count, s
     return 0;
 bad:
     return fail(error, capacity, what, e);
+}
+
+// One decode step for n tokens of n sessions: token i (id ids[i]) at position
+// positions[i] of session sessions[i]. The projections run on the tcgen05 path
+// for all n tokens at once (weights read once per step), attention per token
+// over its own session's pages, then the tied head over the rows and a greedy
+// id per row. Writes next[i] (host) and, when logits is not NULL, the n x 131072
+// logits (host).
+extern "C" int lun_device_batch_decode(lun_device *d, const int *sessions, const int64_t *ids, const int *positions,
+                                       size_t n, float *logits, int64_t *next, int *nonfinite, char *error,
+                                       size_t capacity)
+{
+    cudaError_t e = cudaSetDevice(d->ordinal);
+    if (e != cudaSuccess) return fail(error, capacity, "cudaSetDevice", e);
+    if (!d->session_tables || !n || n > d->block || !sessions || !ids || !positions) {
+        if (error && capacity) snprintf(error, capacity, "batch decode: invalid arguments");
+        return -1;
+    }
+    int longest = 0;
+    for (size_t i = 0; i < n; i++) {
+        if (sessions[i] < 0 || sessions[i] >= d->max_sessions || positions[i] < 0 ||
+            (size_t)positions[i] >= d->context || ids[i] < 0 || ids[i] >= kVocab) {
+            if (error && capacity) snprintf(error, capacity, "batch decode: token %zu out of range", i);
+            return -1;
+        }
+        d->h_step->ids[i] = (int)ids[i];
+        d->h_meta[i] = positions[i];
+        d->h_meta[d->block + i] = sessions[i];
+        longest = positions[i] + 1 > longest ? positions[i] + 1 : longest;
+    }
+    d->h_step->length = 0;
+    d->h_step->count = (int)n;
+    d->h_step->generated = 0;
+    const int count = (int)n;
+    const char *what = "batch upload";
+    if ((e = cudaMemcpyAsync(d->d_step, d->h_step, sizeof(StepParams), cudaMemcpyHostToDevice, d->stream)) !=
+            cudaSuccess ||
+        (e = cudaMemcpyAsync(d->d_meta, d->h_meta, 2 * d->block * sizeof(int), cudaMemcpyHostToDevice,
+                             d->stream)) != cudaSuccess ||
+        (e = cudaMemsetAsync(d->d_flag, 0, 4, d->stream)) != cudaSuccess)
+        return fail(error, capacity, what, e);
+    what = "batch kernels";
+    if ((e = lun_launch_embed(d->embedding, d->d_step, d->x, count, d->stream)) != cudaSuccess)
+        return fail(error, capacity, what, e);
+    for (int layer = 0; layer < kLayers; layer++) {
+        AttnParams a;
+        memset(&a, 0, sizeof a);
+        a.q = d->q;
+        a.kv = d->kv;
+        a.page_table = d->session_tables;
+        a.num_pages = d->num_pages;
+        a.layer = layer;
+        a.out = d->attn;
+        a.part_acc = d->part_acc;
+        a.part_ml = d->part_ml;
+        a.positions = d->d_meta;
+        a.token_table = d->d_meta + d->block;
+        a.table_stride = d->session_pages;
+        lun_attention_plan(&a, longest, count, d->sm_count, (int)d->part_slots);
+        if ((e = run_projection(d, layer, 0, count, true)) != cudaSuccess ||
+            (e = lun_launch_attention(a, count, d->stream)) != cudaSuccess ||
+            (e = run_projection(d, layer, 1, count, true)) != cudaSuccess ||
+            (e = run_projection(d, layer, 2, count, true)) != cudaSuccess ||
+            (e = run_projection(d, layer, 3, count, true)) != cudaSuccess)
+            return fail(error, capacity, what, e);
+    }
+    for (int t0 = 0; t0 < count; t0 += kHeadRows) {
+        HeadRowsParams hp;
+        hp.W = d->embedding;
+        hp.rows = kVocab;
+        hp.cols = kHidden;
+        hp.x = d->x + (size_t)t0 * kHidden;
+        hp.x_stride = kHidden;
+        hp.count = count - t0 < kHeadRows ? count - t0 : kHeadRows;
+        hp.gain = d->final_norm;
+        hp.logits = d->batch_logits + (size_t)t0 * kVocab;
+        hp.logits_stride = kVocab;
+        hp.nonfinite = d->d_flag;
+        if ((e = lun_launch_head_rows(hp, d->sm_count, d->stream)) != cudaSuccess)
+            return fail(error, capacity, what, e);
+    }
+    if ((e = lun_launch_argmax_rows(d->batch_logits, kVocab, kVocab, count, d->d_next, d->stream)) != cudaSuccess)
+        return fail(error, capacity, what, e);
+    what = "batch download";
+    if ((e = cudaMemcpyAsync(d->h_next, d->d_next, n * sizeof(int), cudaMemcpyDeviceToHost, d->stream)) !=
+            cudaSuccess ||
+        (e = cudaMemcpyAsync(d->h_flag, d->d_flag, 4, cudaMemcpyDeviceToHost, d->stream)) != cudaSuccess ||
+        (logits && (e = cudaMemcpyAsync(logits, d->batch_logits, n * (size_t)kVocab * sizeof(float),
+                                        cudaMemcpyDeviceToHost, d->stream)) != cudaSuccess))
+        return fail(error, capacity, what, e);
+    what = "batch execution";
+    if ((e = cudaStreamSynchronize(d->stream)) != cudaSuccess) return fail(error, capacity, what, e);
+    if (d->pf.error && (e = cudaMemcpy(d->h_pf_error, d->pf.error, 4, cudaMemcpyDeviceToHost)) == cudaSuccess &&
+        *d->h_pf_error) {
+        cudaMemset(d->pf.error, 0, sizeof(int));
+        if (error && capacity) snprintf(error, capacity, "batch decode: GEMM pipeline wait gave up");
+        return -1;
+    }
+    if (next)
+        for (size_t i = 0; i < n; i++) next[i] = d->h_next[i];
+    if (nonfinite) *nonfinite = *d->h_flag != 0;
+    return 0;
 }
 
 // CTA 0's barrier exits, then every CTA's marks (mega_params.cuh)

@@ -64,6 +64,21 @@ float *lun_device_host_logits(lun_device *d);
 int lun_device_decode_loop(lun_device *d, int64_t first_token, size_t length, size_t steps,
     int64_t *tokens, float *milliseconds, int *launches, char *error, size_t capacity);
 
+/* Batched decode over independent sessions. The KV pool has pool_pages pages
+ * of 64 positions; each of max_sessions sessions owns up to
+ * ceil(session_context / 64) of them through its row of a page-table array.
+ * block (8..256) bounds the tokens of one call. */
+lun_device *lun_device_create_batch(size_t pool_pages, size_t session_context, size_t block,
+    size_t max_sessions, char *error, size_t capacity);
+/* Write session `session`'s page ids (n <= its row length). */
+int lun_device_session_table(lun_device *d, int session, const int *pages, size_t n);
+/* Single-sequence calls (lun_device_run) run on this session's pages. */
+int lun_device_use_session(lun_device *d, int session);
+/* One decode step for n tokens of n sessions at their positions; greedy ids
+ * into next, logits (n x 131072) when not NULL. */
+int lun_device_batch_decode(lun_device *d, const int *sessions, const int64_t *ids, const int *positions,
+    size_t n, float *logits, int64_t *next, int *nonfinite, char *error, size_t capacity);
+
 /* Measurement: record %globaltimer at the start and after every grid barrier of
  * the first step of each persistent-kernel launch (133 entries). */
 int lun_device_timeline(lun_device *d, int enable);

@@ -279,7 +279,7 @@ cudaError_t lun_launch_attention(const AttnParams &a, int count, cudaStream_t st
 {
     cudaError_t e = lun_kernels_ensure();
     if (e != cudaSuccess) return e;
-    if (count > kGemvMaxTokens)  // blocks of tokens: one pass over the keys per 8 query tokens
+    if (count > kGemvMaxTokens && !a.positions)  // blocks of one sequence's tokens: one pass over the keys per 8
         return launch(attention_prefill_kernel, dim3((count + kPfTokens - 1) / kPfTokens, kKVHeads), dim3(kPfThreads),
                       kPfSmemBytes, stream, a, count);
     if (a.splits < 1 || a.split_len < kTile || (a.split_len % kTile)) return cudaErrorInvalidValue;
@@ -320,5 +320,80 @@ cudaError_t lun_launch_kv_copy(const KvCopyParams &p, int layers, cudaStream_t s
 {
     if (p.pairs <= 0 || layers <= 0 || p.last_slots <= 0 || p.last_slots > kPage) return cudaErrorInvalidValue;
     kv_copy_kernel<<<dim3(p.pairs, layers * 2 * kKVHeads), 256, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t lun_launch_head_rows(const HeadRowsParams &p, int sm_count, cudaStream_t stream)
+{
+    if (p.cols <= 0 || (p.cols & 7) || p.count < 1 || p.count > kHeadRows) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)kHeadRows * p.cols * 4;
+    static bool attr[128] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 128 && !attr[dev]) {
+        if ((e = cudaFuncSetAttribute(head_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) !=
+            cudaSuccess)
+            return e;
+        attr[dev] = true;
+    }
+    int per_sm = 0;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, head_rows_kernel, 256, smem)) != cudaSuccess)
+        return e;
+    if (per_sm < 1) per_sm = 1;
+    const int groups = (p.rows + 3) / 4;
+    int blocks = (groups + 7) / 8;
+    if (blocks > sm_count * per_sm) blocks = sm_count * per_sm;
+    return launch(head_rows_kernel, dim3(blocks), dim3(256), smem, stream, p);
+}
+
+// out[t] = argmax of logits row t (strict '>', lowest id on ties:
+// src/generation.c:8-34); one block of 1024 threads per row.
+__global__ void __launch_bounds__(1024) argmax_rows_kernel(const float *logits, int n, int stride, int *out)
+{
+    __shared__ float bv[32];
+    __shared__ int bi[32];
+    const float *row = logits + (size_t)blockIdx.x * stride;
+    float v = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float x = row[i];
+        if (x > v || (x == v && i < idx)) {
+            v = x;
+            idx = i;
+        }
+    }
+    for (int o = 16; o; o >>= 1) {
+        const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+        const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (v2 > v || (v2 == v && i2 < idx)) {
+            v = v2;
+            idx = i2;
+        }
+    }
+    if ((threadIdx.x & 31) == 0) {
+        bv[threadIdx.x >> 5] = v;
+        bi[threadIdx.x >> 5] = idx;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        v = bv[threadIdx.x];
+        idx = bi[threadIdx.x];
+        for (int o = 16; o; o >>= 1) {
+            const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+            const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+            if (v2 > v || (v2 == v && i2 < idx)) {
+                v = v2;
+                idx = i2;
+            }
+        }
+        if (threadIdx.x == 0) out[blockIdx.x] = idx < n ? idx : 0;
+    }
+}
+
+cudaError_t lun_launch_argmax_rows(const float *logits, int n, int stride, int rows, int *out, cudaStream_t stream)
+{
+    if (rows <= 0 || n <= 0) return cudaErrorInvalidValue;
+    argmax_rows_kernel<<<rows, 1024, 0, stream>>>(logits, n, stride, out);
     return cudaGetLastError();
 }

@@ -20,6 +20,10 @@ constexpr int kGemvMaxTokens = 4;
 cudaError_t lun_launch_gemv(const lun::GemvParams &p, int m, int epilogue, int sm_count,
                             cudaStream_t stream);
 cudaError_t lun_launch_head(const lun::HeadParams &p, int sm_count, cudaStream_t stream);
+// Tied head over 1..kHeadRows token rows (batched decode).
+cudaError_t lun_launch_head_rows(const lun::HeadRowsParams &p, int sm_count, cudaStream_t stream);
+// Greedy id of each of `rows` logits rows (stride floats apart).
+cudaError_t lun_launch_argmax_rows(const float *logits, int n, int stride, int rows, int *out, cudaStream_t stream);
 
 // Choose split_len/splits for `total` positions (max over the call's tokens),
 // `count` query tokens and `slots` partial slots available.

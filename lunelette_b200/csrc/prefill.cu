@@ -170,6 +170,9 @@ cudaError_t lun_launch_prefill_marked(const GemvParams &p, int count, int epilog
     f.page_table = p.page_table;
     f.num_pages = p.num_pages;
     f.layer = p.layer;
+    f.positions = p.positions;
+    f.token_table = p.token_table;
+    f.table_stride = p.table_stride;
     switch (epilogue) {
     case kEpiStore: e = launch_finish<kEpiStore>(f, stream); break;
     case kEpiResidual: e = launch_finish<kEpiResidual>(f, stream); break;

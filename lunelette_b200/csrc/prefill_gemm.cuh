@@ -565,6 +565,8 @@ struct PrefillFinishParams {
     float *kv;
     const int *page_table;
     int num_pages, layer;
+    const int *positions, *token_table;  // batched decode (GemvParams)
+    int table_stride;
 };
 
 __device__ __forceinline__ float finish_scale(const PrefillFinishParams &p, int r)
@@ -606,7 +608,7 @@ static __global__ void __launch_bounds__(256) prefill_finish_kernel(PrefillFinis
         const int ra = head * kHeadDim + j, rb = ra + 64;
         a *= finish_scale(p, ra);
         b *= finish_scale(p, rb);
-        const int pos = (p.step ? p.step->length : p.length) + t;
+        const int pos = p.positions ? p.positions[t] : (p.step ? p.step->length : p.length) + t;
         if (ra < kQuery + kKV) {
             const float *cs = p.rope_cos + (size_t)pos * 128, *sn = p.rope_sin + (size_t)pos * 128;
             const float lo = a * cs[j] + (-b) * sn[j];
@@ -621,7 +623,8 @@ static __global__ void __launch_bounds__(256) prefill_finish_kernel(PrefillFinis
         } else {
             const int kind = ra < kQuery + kKV ? 0 : 1;
             const int kvh = (ra - kQuery - kind * kKV) >> 7;
-            const int page = p.page_table[pos / kPage], slot = pos % kPage;
+            const int *table = p.positions ? p.page_table + (size_t)p.token_table[t] * p.table_stride : p.page_table;
+            const int page = table[pos / kPage], slot = pos % kPage;
             float *dst = p.kv + kv_offset(p.layer, p.num_pages, page, kind, kvh, slot);
             dst[j] = a;
             dst[j + 64] = b;

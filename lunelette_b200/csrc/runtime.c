@@ -178,6 +178,23 @@ static int upload_rope(lun_device *device, size_t context)
     return status;
 }
 
+/* Checkpoint -> device (FP8 compact admission), the YaRN table for
+ * rope_positions positions, then the upload's end; shared with batch.c. */
+int lun_runtime_load(lun_device *device, const char *path, size_t rope_positions, char *error, size_t capacity)
+{
+    lun_weights weights;
+    if (lun_weights_open(&weights, path, error, capacity)) {
+        return -1;
+    }
+    int status = upload(device, &weights, 1, error, capacity) || upload_rope(device, rope_positions) ||
+        lun_device_upload_finish(device, error, capacity);
+    if (status && !error[0]) {
+        snprintf(error, capacity, "weight upload failed");
+    }
+    lun_weights_close(&weights);
+    return status ? -1 : 0;
+}
+
 LUN_API lunelette_metal *lunelette_metal_create_configured(const char *path,
     const lunelette_metal_options *options, const lunelette_metal_limits *limits,
     char *error, size_t capacity)
