@@ -205,6 +205,81 @@ def prefill_gemm_roofline(lib, torch, count=256, reps=20):
             "useful_flops": useful}
 
 
+def config_lines(L, torch, checkpoint, seed, barrier, max_over_ranks, world):
+    """BASELINE configs 2-4 on one batch context (64 sessions x 4352 positions,
+    a paged FP32 KV pool of 59 GB): wall clock around host-synchronous calls.
+      C2: 4096 seeded ids in 16 chunks of 256 at context 4352, then 128 greedy
+          decode steps (persistent kernel);
+      C3: a 512-token prefix, then 8 turns of 200 appended ids + 64 greedy tokens
+          on the same session (its KV kept between turns); TTFT = the append;
+      C4: 64 sessions, prompts ~ U[256, 4096] (seeded), prefilled in 256-token
+          chunks, then 128 batched greedy decode steps over all 64 sessions.
+    Aggregates sum the ranks' work over the slowest rank's time."""
+    rng = np.random.default_rng(seed + 99)
+    out = {}
+    with L.Batch(checkpoint, max_sessions=64, context=4352, pool_positions=64 * 4352, block=256) as b:
+        # C2
+        s = b.open()
+        ids = rng.integers(1000, 131072, 4096).astype(np.int64)
+        barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for c in range(16):
+            logits = b.append(s, ids[256 * c:256 * (c + 1)])
+        t_prefill = max_over_ranks(time.perf_counter() - t0)
+        tok = int(np.argmax(logits))
+        t0 = time.perf_counter()
+        for _ in range(128):
+            tok = int(np.argmax(b.append(s, [tok])))
+        t_decode = max_over_ranks(time.perf_counter() - t0)
+        b.close_session(s)
+        out["c2"] = {"prefill_tok_s": world * 4096 / t_prefill, "decode_tok_s": world * 128 / t_decode,
+                     "note": "4096-token prompt in 16 x 256 chunks at context 4352, then 128 greedy steps"}
+        # C3
+        s = b.open()
+        prefix = rng.integers(1000, 131072, 512).astype(np.int64)
+        b.append(s, prefix[:256])
+        b.append(s, prefix[256:])
+        ttft, dec = [], []
+        for turn in range(8):
+            user = rng.integers(1000, 131072, 200).astype(np.int64)
+            t0 = time.perf_counter()
+            tok = int(np.argmax(b.append(s, user)))
+            ttft.append(time.perf_counter() - t0)
+            t0 = time.perf_counter()
+            for _ in range(63):
+                tok = int(np.argmax(b.append(s, [tok])))
+            dec.append(64 / (time.perf_counter() - t0))
+        b.close_session(s)
+        out["c3"] = {"ttft_ms_mean": 1e3 * max_over_ranks(float(np.mean(ttft))),
+                     "ttft_ms_last_turn": 1e3 * max_over_ranks(ttft[-1]),
+                     "decode_tok_s_per_turn_mean": float(np.mean(dec)),
+                     "note": "512-token prefix, 8 turns of 200 appended ids + 64 greedy tokens, KV kept"}
+        # C4
+        lengths = rng.integers(256, 4097, 64)
+        sessions = [b.open() for _ in range(64)]
+        barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        toks = []
+        for s, n in zip(sessions, lengths):
+            ids = rng.integers(1000, 131072, int(n)).astype(np.int64)
+            for c0 in range(0, int(n), 256):
+                logits = b.append(s, ids[c0:c0 + 256])
+            toks.append(int(np.argmax(logits)))
+        t_prefill = max_over_ranks(time.perf_counter() - t0)
+        t0 = time.perf_counter()
+        for _ in range(128):
+            toks = b.decode(sessions, toks).tolist()
+        t_decode = max_over_ranks(time.perf_counter() - t0)
+        out["c4"] = {"decode_tok_s_aggregate": world * 64 * 128 / t_decode,
+                     "prefill_tok_s_aggregate": world * float(lengths.sum()) / t_prefill,
+                     "ms_per_batched_step": 1e3 * t_decode / 128, "sessions_per_gpu": 64,
+                     "mean_prompt": float(lengths.mean()),
+                     "note": "64 ragged sessions per GPU, prompts U[256,4096], 128 batched greedy steps"}
+    return out
+
+
 def cpu_baseline(checkpoint, prompt, decode_steps=6):
     """The CPU oracle (C restatement of the reference kernels, OpenMP) on this
     box's host cores: the C0 prompt, then `decode_steps` greedy decode steps."""
@@ -367,6 +442,8 @@ def run_ours(args, rank, world, local_rank):
     cp.destroy()
     rt.close()
 
+    configs = None if args.no_configs else config_lines(L, torch, checkpoint, args.seed + rank, barrier,
+                                                         max_over_ranks, world)
     hbm, bf16, peak_kind = measured_peaks()
     gemv_ms, gemv_bytes = gateup_roofline(lib, torch, checkpoint)
     pg = prefill_gemm_roofline(lib, torch)
@@ -412,6 +489,7 @@ def run_ours(args, rank, world, local_rank):
                 "useful_tflops": pg["useful_flops"] / (pg["gemm_ms"] / 1e3) / 1e12,
                 "avg_launch_ms": pg["gemm_ms"], "split_ms": pg["split_ms"], "finish_ms": pg["finish_ms"],
                 "note": "issued = 2 FP16 passes (hi, lo) x 2 x rows x cols x 256; useful = half of it"},
+            "configs": configs,
             "clocks": clocks.summary(),
             "gpu_launches": launches,
             "greedy_device_matches_host": same_tokens,
@@ -435,6 +513,7 @@ def main():
     ap.add_argument("--checkpoint", default=os.path.join(tempfile.gettempdir(),
                                                          "lunelette_synth_seed0.safetensors"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the config 2-4 lines (batch context)")
     args = ap.parse_args()
     rank = env_int("RANK", 0)
     world = env_int("WORLD_SIZE", 1)

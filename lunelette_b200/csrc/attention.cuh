@@ -53,22 +53,23 @@ __device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool fu
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
-// Issue the copies of one 32-position K/V tile (2 x 16 KB) into a stage.
+// Issue the copies of one 32-position K/V tile (2 x 16 KB) into a stage. A tile
+// starts on a multiple of 32 and so lies in one page: the page lookup and the
+// row addresses are computed once per tile, not per 16-byte chunk.
 __device__ __forceinline__ void attention_issue_tile(const AttnParams &p, const int *table, float *stage, int kvh,
                                                      int p0, int end)
 {
     float *ks = stage, *vs = stage + kTile * kKPad;
-    for (int c = threadIdx.x; c < 2 * kTile * 32; c += blockDim.x) {
-        int kind = c >> 10, row = (c >> 5) & 31, chunk = c & 31;
-        int pos = p0 + row;
-        bool in = pos < end;
-        const float *src = p.kv;
-        if (in) {
-            int page = table[pos / kPage];
-            src = p.kv + kv_offset(p.layer, p.num_pages, page, kind, kvh, pos % kPage) + chunk * 4;
-        }
-        float *dst = kind == 0 ? ks + row * kKPad + chunk * 4 : vs + row * kHeadDim + chunk * 4;
-        cp_async16(dst, src, in);
+    const int page = table[p0 / kPage], slot0 = p0 % kPage;
+    const float *kb = p.kv + kv_offset(p.layer, p.num_pages, page, 0, kvh, slot0);
+    const float *vb = p.kv + kv_offset(p.layer, p.num_pages, page, 1, kvh, slot0);
+    const int rows = end - p0;
+#pragma unroll 4
+    for (int c = threadIdx.x; c < kTile * 32; c += blockDim.x) {
+        const int row = c >> 5, chunk = c & 31;
+        const bool in = row < rows;
+        cp_async16(ks + row * kKPad + chunk * 4, in ? kb + row * kHeadDim + chunk * 4 : kb, in);
+        cp_async16(vs + row * kHeadDim + chunk * 4, in ? vb + row * kHeadDim + chunk * 4 : vb, in);
     }
     cp_async_commit();
 }

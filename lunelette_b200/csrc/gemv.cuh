@@ -538,7 +538,7 @@ static __global__ void __launch_bounds__(256) head_bf16_kernel(HeadParams p)
 // logits[r][v] = E[v] . rmsnorm(x[r]) for r < count <= kHeadRows: every weight
 // row is read once per launch for all the rows, which sit normed in shared
 // memory (kHeadRows x cols floats, the per-row layout of head_bf16_kernel).
-constexpr int kHeadRows = 8;
+constexpr int kHeadRows = 16;
 struct HeadRowsParams {
     const uint16_t *W;
     int rows, cols;

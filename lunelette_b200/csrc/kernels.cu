@@ -255,9 +255,15 @@ cudaError_t lun_launch_head(const HeadParams &p, int sm_count, cudaStream_t stre
     return launch(head_bf16_kernel, dim3(blocks), dim3(256), smem, stream, p);
 }
 
+constexpr int kAttnMaxSplit = 512;
+
 void lun_attention_plan(AttnParams *a, int total, int count, int sm_count, int slots)
 {
     int wanted = (2 * sm_count + 8 * count - 1) / (8 * count);  // splits per (token, kv head)
+    // and no split longer than kAttnMaxSplit positions: a long sequence among
+    // many short ones (batched decode) must not stream its prefix serially
+    const int by_length = (total + kAttnMaxSplit - 1) / kAttnMaxSplit;
+    if (wanted < by_length) wanted = by_length;
     if (wanted < 1) wanted = 1;
     int split_len = (total + wanted - 1) / wanted;
     split_len = (split_len + kTile - 1) / kTile * kTile;

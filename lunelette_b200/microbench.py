@@ -240,6 +240,33 @@ def prefill_tokens(checkpoint, count):
     return tok
 
 
+def batch_step(checkpoint, sessions=64, seed=5, pool=None):
+    """A profiling target for config 4: `sessions` sessions with prompts ~
+    U[256, 4096] (seeded) prefilled, one warm-up batched decode step, then one
+    step between cudaProfilerStart and cudaProfilerStop."""
+    import torch
+    import lunelette_b200 as L
+    if not os.path.exists(checkpoint):
+        L.synth_checkpoint(checkpoint, 0)
+    rng = np.random.default_rng(seed)
+    pool = pool if pool is not None else sessions * 4352
+    with L.Batch(checkpoint, max_sessions=sessions, context=4352, pool_positions=pool, block=256) as b:
+        ss = [b.open() for _ in range(sessions)]
+        toks = []
+        for s in ss:
+            ids = rng.integers(1000, 131072, int(rng.integers(256, 4097))).astype(np.int64)
+            for c0 in range(0, ids.size, 256):
+                logits = b.append(s, ids[c0:c0 + 256])
+            toks.append(int(np.argmax(logits)))
+        toks = b.decode(ss, toks).tolist()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        toks = b.decode(ss, toks).tolist()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+    return toks[0]
+
+
 def decode_tokens(checkpoint, steps, prompt=32):
     """A small profiling target: the C0 prompt, then `steps` greedy tokens through
     lunelette_metal_decode (one persistent-kernel launch each)."""
@@ -264,9 +291,17 @@ def main():
                     help="time the persistent decode kernel's phases on this checkpoint instead")
     ap.add_argument("--prefill-tokens", nargs=2, metavar=("CHECKPOINT", "N"), default=None,
                     help="prefill N ids twice, the second between cudaProfilerStart/Stop (a profiling target)")
+    ap.add_argument("--batch-step", metavar="CHECKPOINT", default=None,
+                    help="one batched decode step of ragged sessions between cudaProfilerStart/Stop")
+    ap.add_argument("--batch-sessions", type=int, default=64)
     ap.add_argument("--prefill-gemm", metavar="COUNTS", default=None,
                     help="time the tcgen05 prefill projections at these token counts (e.g. 256,32)")
     args = ap.parse_args()
+    if args.batch_step:
+        n = args.batch_sessions
+        # the pool holds the sessions' prompts plus the two steps (pages of 64)
+        print(json.dumps({"first_token": batch_step(args.batch_step, n, pool=None if n >= 64 else n * 4160)}))
+        return
     if args.prefill_tokens:
         print(json.dumps({"first_token": prefill_tokens(args.prefill_tokens[0], int(args.prefill_tokens[1]))}))
         return
