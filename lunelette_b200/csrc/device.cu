@@ -534,6 +534,48 @@ static GemvParams layer_gemv(lun_device *d, int layer, int which)
 }
 
 // Launch `which` projection of `layer` over all `count` tokens in groups of <= 4.
+// Projection `which` of `layer` for the tokens from t0: weights, scales,
+// epilogue operands (x/y/res rows of the block's scratch).
+static cudaError_t run_attention(lun_device *d, int layer, int count, size_t length, bool fixed_plan = false);
+
+static GemvParams projection_params(lun_device *d, int layer, int which, int t0)
+{
+    GemvParams p = layer_gemv(d, layer, which);
+    p.token_offset = t0;
+    switch (which) {
+    case 0:
+        p.x = d->x + (size_t)t0 * kHidden;
+        p.x_stride = kHidden;
+        p.y = d->q + (size_t)t0 * kQuery;
+        p.y_stride = kQuery;
+        break;
+    case 1:
+        p.x = d->attn + (size_t)t0 * kQuery;
+        p.x_stride = kQuery;
+        p.res = d->x + (size_t)t0 * kHidden;
+        p.res_stride = kHidden;
+        p.y = d->h + (size_t)t0 * kHidden;
+        p.y_stride = kHidden;
+        break;
+    case 2:
+        p.x = d->h + (size_t)t0 * kHidden;
+        p.x_stride = kHidden;
+        p.y = d->act + (size_t)t0 * kInner;
+        p.y_stride = kInner;
+        break;
+    default:
+        p.x = d->act + (size_t)t0 * kInner;
+        p.x_stride = kInner;
+        p.res = d->h + (size_t)t0 * kHidden;
+        p.res_stride = kHidden;
+        p.y = d->x + (size_t)t0 * kHidden;
+        p.y_stride = kHidden;
+        break;
+    }
+    p.prefetch = nullptr;
+    return p;
+}
+
 // batched: tokens of independent sessions (batched decode): always the
 // tcgen05 path, whose QKV epilogue takes per-token positions and page tables.
 static cudaError_t run_projection(lun_device *d, int layer, int which, int count, bool batched = false)
@@ -542,40 +584,8 @@ static cudaError_t run_projection(lun_device *d, int layer, int which, int count
     const bool gemm = batched || (count > kGemvMaxTokens && d->use_gemm);
     for (int t0 = 0; t0 < count; t0 += gemm ? count : kGemvMaxTokens) {
         int m = count - t0 < kGemvMaxTokens ? count - t0 : kGemvMaxTokens;
-        GemvParams p = layer_gemv(d, layer, which);
-        p.token_offset = t0;
-        switch (which) {
-        case 0:
-            p.x = d->x + (size_t)t0 * kHidden;
-            p.x_stride = kHidden;
-            p.y = d->q + (size_t)t0 * kQuery;
-            p.y_stride = kQuery;
-            break;
-        case 1:
-            p.x = d->attn + (size_t)t0 * kQuery;
-            p.x_stride = kQuery;
-            p.res = d->x + (size_t)t0 * kHidden;
-            p.res_stride = kHidden;
-            p.y = d->h + (size_t)t0 * kHidden;
-            p.y_stride = kHidden;
-            break;
-        case 2:
-            p.x = d->h + (size_t)t0 * kHidden;
-            p.x_stride = kHidden;
-            p.y = d->act + (size_t)t0 * kInner;
-            p.y_stride = kInner;
-            break;
-        default:
-            p.x = d->act + (size_t)t0 * kInner;
-            p.x_stride = kInner;
-            p.res = d->h + (size_t)t0 * kHidden;
-            p.res_stride = kHidden;
-            p.y = d->x + (size_t)t0 * kHidden;
-            p.y_stride = kHidden;
-            break;
-        }
+        GemvParams p = projection_params(d, layer, which, t0);
         if (gemm) {
-            p.prefetch = nullptr;  // the GEMM is tensor-bound; no next-matrix prefetch
             if (batched) {
                 p.positions = d->d_meta;
                 p.token_table = d->d_meta + d->block;
@@ -584,14 +594,53 @@ static cudaError_t run_projection(lun_device *d, int layer, int which, int count
             }
             return lun_launch_prefill(p, count, epi[which], d->pf, d->sm_count, d->stream);
         }
+        if (!gemm) p.prefetch = layer_gemv(d, layer, which).prefetch;  // next-matrix L2 prefetch (GEMV)
         cudaError_t e = lun_launch_gemv(p, m, epi[which], d->sm_count, d->stream);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
 }
 
-static cudaError_t run_attention(lun_device *d, int layer, int count, size_t length,
-                                 bool fixed_plan = false)
+// Blocks of more than kGemvMaxTokens tokens of one sequence on the tcgen05
+// path, each finish fused with the next projection's split: per layer split
+// (attn), 4 GEMMs, the QKV finish, attention and three finish+split kernels.
+static cudaError_t run_prefill_layers(lun_device *d, int count, size_t length)
+{
+    cudaError_t e;
+    const int sms = d->sm_count;
+    if ((e = lun_launch_prefill_split(projection_params(d, 0, 0, 0), count, d->pf, sms, d->stream)) != cudaSuccess)
+        return e;
+    for (int layer = 0; layer < kLayers; layer++) {
+        const GemvParams qkv = projection_params(d, layer, 0, 0), o = projection_params(d, layer, 1, 0),
+                         gu = projection_params(d, layer, 2, 0), down = projection_params(d, layer, 3, 0);
+        if ((e = lun_launch_prefill_gemm(qkv, count, d->pf, sms, d->stream)) != cudaSuccess ||
+            (e = lun_launch_prefill_finish(qkv, count, kEpiQKV, d->pf, sms, d->stream)) != cudaSuccess ||
+            (e = run_attention(d, layer, count, length)) != cudaSuccess ||
+            (e = lun_launch_prefill_split(o, count, d->pf, sms, d->stream)) != cudaSuccess ||
+            (e = lun_launch_prefill_gemm(o, count, d->pf, sms, d->stream)) != cudaSuccess ||
+            (e = lun_launch_prefill_finish_split(o, count, kEpiResidual, d->pf, sms, gu.gain, gu.rows, true,
+                                                 d->stream)) != cudaSuccess ||
+            (e = lun_launch_prefill_gemm(gu, count, d->pf, sms, d->stream)) != cudaSuccess)
+            return e;
+        GemvParams gux = gu;
+        gux.y = nullptr;  // act feeds only the down projection's operand tiles
+        const bool last = layer + 1 == kLayers;
+        const float *next_gain = last ? nullptr : d->norms + (size_t)(2 * (layer + 1)) * kHidden;
+        if ((e = lun_launch_prefill_finish_split(gux, count, kEpiSwiGLU, d->pf, sms, nullptr, down.rows, true,
+                                                 d->stream)) != cudaSuccess ||
+            (e = lun_launch_prefill_gemm(down, count, d->pf, sms, d->stream)) != cudaSuccess ||
+            (e = lun_launch_prefill_finish_split(down, count, kEpiResidual, d->pf, sms, next_gain, kQKVRows, !last,
+                                                 d->stream)) != cudaSuccess)
+            return e;
+        if (d->trace && (e = cudaMemcpyAsync(d->trace_buf + (size_t)layer * count * kHidden, d->x,
+                                             (size_t)count * kHidden * 4, cudaMemcpyDeviceToDevice, d->stream)) !=
+                            cudaSuccess)
+            return e;
+    }
+    return cudaSuccess;
+}
+
+static cudaError_t run_attention(lun_device *d, int layer, int count, size_t length, bool fixed_plan)
 {
     AttnParams a;
     memset(&a, 0, sizeof a);
@@ -821,6 +870,9 @@ extern "C" int lun_device_run(lun_device *d, const int64_t *ids, size_t count, s
             goto bad;
     } else {
     if ((e = lun_launch_embed(d->embedding, d->d_step, d->x, n, d->stream)) != cudaSuccess) goto bad;
+    if (n > kGemvMaxTokens && d->use_gemm) {
+        if ((e = run_prefill_layers(d, n, length)) != cudaSuccess) goto bad;
+    } else
     for (int layer = 0; layer < kLayers; layer++) {
         if ((e = run_projection(d, layer, 0, n)) != cudaSuccess ||
             (e = run_attention(d, layer, n, length)) != cudaSuccess ||

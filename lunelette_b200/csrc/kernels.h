@@ -84,6 +84,20 @@ void lun_prefill_workspace_bytes(int max_count, int sm_count, size_t *xs_bytes, 
 // lun::GemvEpilogue, positions from p.step->length (or p.length + p.token_offset).
 cudaError_t lun_launch_prefill(const lun::GemvParams &p, int count, int epilogue, const PrefillWorkspace &w,
                                int sm_count, cudaStream_t stream);
+// The three steps separately, and the finish fused with the next projection's
+// split (residual or SwiGLU epilogue written to p.y when p.y is set; the row
+// then RMS-normed with next_gain (or not, nullptr) and split into the operand
+// tiles of a projection of next_rows rows; split == false stops after the
+// epilogue).
+cudaError_t lun_launch_prefill_split(const lun::GemvParams &p, int count, const PrefillWorkspace &w, int sm_count,
+                                     cudaStream_t stream);
+cudaError_t lun_launch_prefill_gemm(const lun::GemvParams &p, int count, const PrefillWorkspace &w, int sm_count,
+                                    cudaStream_t stream);
+cudaError_t lun_launch_prefill_finish(const lun::GemvParams &p, int count, int epilogue, const PrefillWorkspace &w,
+                                      int sm_count, cudaStream_t stream);
+cudaError_t lun_launch_prefill_finish_split(const lun::GemvParams &p, int count, int epilogue,
+                                            const PrefillWorkspace &w, int sm_count, const float *next_gain,
+                                            int next_rows, bool split, cudaStream_t stream);
 // The same with events recorded before the split, between the kernels and after
 // the finish (marks[0..3]), for per-kernel timing.
 cudaError_t lun_launch_prefill_marked(const lun::GemvParams &p, int count, int epilogue,

@@ -1,5 +1,6 @@
 // Launchers of the tcgen05 prefill projections (prefill_gemm.cuh).
 #include <cudaTypedefs.h>
+#include <string.h>
 
 #include "kernels.h"
 #include "prefill_gemm.cuh"
@@ -93,66 +94,36 @@ static cudaError_t launch_finish(const PrefillFinishParams &f, cudaStream_t stre
     return cudaGetLastError();
 }
 
-cudaError_t lun_launch_prefill(const GemvParams &p, int count, int epilogue, const PrefillWorkspace &w,
-                               int sm_count, cudaStream_t stream)
+static cudaError_t check_prefill(const GemvParams &p, int count, const PrefillPlan &pl, const PrefillWorkspace &w)
 {
-    return lun_launch_prefill_marked(p, count, epilogue, w, sm_count, stream, nullptr);
+    if (count <= 0 || p.rows <= 0 || (p.rows % kTileRows) || p.cols <= 0 || (p.cols & 15) || p.cols > kSplitMaxCols ||
+        !w.xs || !w.inv_scale || !w.ws || !w.error)
+        return cudaErrorInvalidValue;
+    if (pl.xs_bytes > w.xs_bytes || pl.inv_bytes > w.inv_bytes || pl.ws_bytes > w.ws_bytes) return cudaErrorInvalidValue;
+    return prefill_setup();
 }
 
-cudaError_t lun_launch_prefill_marked(const GemvParams &p, int count, int epilogue, const PrefillWorkspace &w,
-                                      int sm_count, cudaStream_t stream, cudaEvent_t *marks)
+static PrefillSplitParams split_params(const PrefillPlan &pl, int cols, int count, const PrefillWorkspace &w)
 {
-    if (count <= 0 || p.rows <= 0 || (p.rows % kTileRows) || p.cols <= 0 || (p.cols & 15) ||
-        p.cols > kSplitMaxCols || (p.x_stride & 3) || ((uintptr_t)p.x & 15) || ((uintptr_t)p.gain & 15) || !w.xs ||
-        !w.inv_scale || !w.ws || !w.error)
-        return cudaErrorInvalidValue;
-    if ((epilogue == kEpiQKV && (p.rows != kQKVRows || p.cols != kHidden)) || (epilogue == kEpiSwiGLU && (p.rows & 1)))
-        return cudaErrorInvalidValue;
-    const PrefillPlan pl = lun_prefill_plan(p.rows, p.cols, count, sm_count);
-    if (pl.xs_bytes > w.xs_bytes || pl.inv_bytes > w.inv_bytes || pl.ws_bytes > w.ws_bytes)
-        return cudaErrorInvalidValue;
-    cudaError_t e = prefill_setup();
-    if (e != cudaSuccess) return e;
-
     PrefillSplitParams sp;
-    sp.x = p.x;
-    sp.x_stride = p.x_stride;
-    sp.gain = p.gain;
-    sp.cols = p.cols;
+    memset(&sp, 0, sizeof sp);
+    sp.cols = cols;
     sp.kchunks = pl.kchunks;
     sp.count = count;
     sp.xs = w.xs;
     sp.inv_scale = w.inv_scale;
-    if (marks && (e = cudaEventRecord(marks[0], stream)) != cudaSuccess) return e;
-    prefill_split_kernel<<<pl.token_tiles * kPgM, kSplitThreads, 0, stream>>>(sp);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    if (marks && (e = cudaEventRecord(marks[1], stream)) != cudaSuccess) return e;
+    return sp;
+}
 
-    PrefillGemmParams g;
-    g.W = p.W;
-    g.rows = p.rows;
-    g.nb = (p.cols + kBlockCols - 1) / kBlockCols;
-    g.kchunks = pl.kchunks;
-    g.xs = w.xs;
-    g.token_tiles = pl.token_tiles;
-    g.count = count;
-    g.splits = pl.splits;
-    g.inv_scale = w.inv_scale;
-    g.ws = w.ws;
-    g.ws_rows = pl.row_tiles * kP2N;
-    g.error = w.error;
-    CUtensorMap wmap;
-    if ((e = weight_tensor_map(&wmap, p.W, p.rows, g.nb)) != cudaSuccess) return e;
-    prefill_gemm_pair_kernel<<<dim3(2 * pl.row_tiles, (pl.token_tiles + 1) / 2, pl.splits), kPgThreads,
-                               kP2SmemBytes, stream>>>(g, wmap);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    if (marks && (e = cudaEventRecord(marks[2], stream)) != cudaSuccess) return e;
-
+static PrefillFinishParams finish_params(const GemvParams &p, int count, const PrefillPlan &pl,
+                                         const PrefillWorkspace &w)
+{
     PrefillFinishParams f;
+    memset(&f, 0, sizeof f);
     f.ws = w.ws;
     f.splits = pl.splits;
     f.t_stride = pl.token_tiles * kPgM;
-    f.ws_rows = g.ws_rows;
+    f.ws_rows = pl.row_tiles * kP2N;
     f.rows = p.rows;
     f.count = count;
     for (int i = 0; i < 3; i++) f.scale[i] = p.scale[i];
@@ -173,13 +144,111 @@ cudaError_t lun_launch_prefill_marked(const GemvParams &p, int count, int epilog
     f.positions = p.positions;
     f.token_table = p.token_table;
     f.table_stride = p.table_stride;
+    return f;
+}
+
+cudaError_t lun_launch_prefill_split(const GemvParams &p, int count, const PrefillWorkspace &w, int sm_count,
+                                     cudaStream_t stream)
+{
+    const PrefillPlan pl = lun_prefill_plan(p.rows, p.cols, count, sm_count);
+    cudaError_t e = check_prefill(p, count, pl, w);
+    if (e != cudaSuccess) return e;
+    if ((p.x_stride & 3) || ((uintptr_t)p.x & 15) || ((uintptr_t)p.gain & 15)) return cudaErrorInvalidValue;
+    PrefillSplitParams sp = split_params(pl, p.cols, count, w);
+    sp.x = p.x;
+    sp.x_stride = p.x_stride;
+    sp.gain = p.gain;
+    prefill_split_kernel<<<pl.token_tiles * kPgM, kSplitThreads, 0, stream>>>(sp);
+    return cudaGetLastError();
+}
+
+cudaError_t lun_launch_prefill_gemm(const GemvParams &p, int count, const PrefillWorkspace &w, int sm_count,
+                                    cudaStream_t stream)
+{
+    const PrefillPlan pl = lun_prefill_plan(p.rows, p.cols, count, sm_count);
+    cudaError_t e = check_prefill(p, count, pl, w);
+    if (e != cudaSuccess) return e;
+    PrefillGemmParams g;
+    g.W = p.W;
+    g.rows = p.rows;
+    g.nb = (p.cols + kBlockCols - 1) / kBlockCols;
+    g.kchunks = pl.kchunks;
+    g.xs = w.xs;
+    g.token_tiles = pl.token_tiles;
+    g.count = count;
+    g.splits = pl.splits;
+    g.inv_scale = w.inv_scale;
+    g.ws = w.ws;
+    g.ws_rows = pl.row_tiles * kP2N;
+    g.error = w.error;
+    CUtensorMap wmap;
+    if ((e = weight_tensor_map(&wmap, p.W, p.rows, g.nb)) != cudaSuccess) return e;
+    prefill_gemm_pair_kernel<<<dim3(2 * pl.row_tiles, (pl.token_tiles + 1) / 2, pl.splits), kPgThreads,
+                               kP2SmemBytes, stream>>>(g, wmap);
+    return cudaGetLastError();
+}
+
+cudaError_t lun_launch_prefill_finish(const GemvParams &p, int count, int epilogue, const PrefillWorkspace &w,
+                                      int sm_count, cudaStream_t stream)
+{
+    const PrefillPlan pl = lun_prefill_plan(p.rows, p.cols, count, sm_count);
+    cudaError_t e = check_prefill(p, count, pl, w);
+    if (e != cudaSuccess) return e;
+    if ((epilogue == kEpiQKV && (p.rows != kQKVRows || p.cols != kHidden)) || (epilogue == kEpiSwiGLU && (p.rows & 1)))
+        return cudaErrorInvalidValue;
+    const PrefillFinishParams f = finish_params(p, count, pl, w);
     switch (epilogue) {
-    case kEpiStore: e = launch_finish<kEpiStore>(f, stream); break;
-    case kEpiResidual: e = launch_finish<kEpiResidual>(f, stream); break;
-    case kEpiQKV: e = launch_finish<kEpiQKV>(f, stream); break;
-    case kEpiSwiGLU: e = launch_finish<kEpiSwiGLU>(f, stream); break;
+    case kEpiStore: return launch_finish<kEpiStore>(f, stream);
+    case kEpiResidual: return launch_finish<kEpiResidual>(f, stream);
+    case kEpiQKV: return launch_finish<kEpiQKV>(f, stream);
+    case kEpiSwiGLU: return launch_finish<kEpiSwiGLU>(f, stream);
     default: return cudaErrorInvalidValue;
     }
-    if (e == cudaSuccess && marks) e = cudaEventRecord(marks[3], stream);
-    return e;
+}
+
+cudaError_t lun_launch_prefill_finish_split(const GemvParams &p, int count, int epilogue, const PrefillWorkspace &w,
+                                            int sm_count, const float *next_gain, int next_rows, bool split,
+                                            cudaStream_t stream)
+{
+    const PrefillPlan pl = lun_prefill_plan(p.rows, p.cols, count, sm_count);
+    cudaError_t e = check_prefill(p, count, pl, w);
+    if (e != cudaSuccess) return e;
+    const int width = epilogue == kEpiSwiGLU ? p.rows / 2 : p.rows;
+    if ((epilogue != kEpiResidual && epilogue != kEpiSwiGLU) || width > kSplitMaxCols || (width & 15) ||
+        (p.y && ((p.y_stride & 3) || ((uintptr_t)p.y & 15))) ||
+        (epilogue == kEpiResidual && (!p.res || (p.res_stride & 3) || ((uintptr_t)p.res & 15))) ||
+        ((uintptr_t)next_gain & 15))
+        return cudaErrorInvalidValue;
+    const PrefillFinishParams f = finish_params(p, count, pl, w);
+    // the next projection reads `width` columns: its plan sizes the operand tiles
+    const PrefillPlan next = lun_prefill_plan(next_rows > 0 ? next_rows : kTileRows, width, count, sm_count);
+    if (next.xs_bytes > w.xs_bytes) return cudaErrorInvalidValue;
+    PrefillSplitParams sp = split_params(next, width, count, w);
+    sp.gain = next_gain;
+    if (!split) sp.xs = nullptr;
+    if (epilogue == kEpiSwiGLU)
+        prefill_finish_split_kernel<kEpiSwiGLU><<<pl.token_tiles * kPgM, kFsThreads, 0, stream>>>(f, sp);
+    else
+        prefill_finish_split_kernel<kEpiResidual><<<pl.token_tiles * kPgM, kFsThreads, 0, stream>>>(f, sp);
+    return cudaGetLastError();
+}
+
+cudaError_t lun_launch_prefill(const GemvParams &p, int count, int epilogue, const PrefillWorkspace &w,
+                               int sm_count, cudaStream_t stream)
+{
+    return lun_launch_prefill_marked(p, count, epilogue, w, sm_count, stream, nullptr);
+}
+
+cudaError_t lun_launch_prefill_marked(const GemvParams &p, int count, int epilogue, const PrefillWorkspace &w,
+                                      int sm_count, cudaStream_t stream, cudaEvent_t *marks)
+{
+    cudaError_t e;
+    if (marks && (e = cudaEventRecord(marks[0], stream)) != cudaSuccess) return e;
+    if ((e = lun_launch_prefill_split(p, count, w, sm_count, stream)) != cudaSuccess) return e;
+    if (marks && (e = cudaEventRecord(marks[1], stream)) != cudaSuccess) return e;
+    if ((e = lun_launch_prefill_gemm(p, count, w, sm_count, stream)) != cudaSuccess) return e;
+    if (marks && (e = cudaEventRecord(marks[2], stream)) != cudaSuccess) return e;
+    if ((e = lun_launch_prefill_finish(p, count, epilogue, w, sm_count, stream)) != cudaSuccess) return e;
+    if (marks && (e = cudaEventRecord(marks[3], stream)) != cudaSuccess) return e;
+    return cudaSuccess;
 }

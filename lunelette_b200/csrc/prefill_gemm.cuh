@@ -137,29 +137,21 @@ struct PrefillSplitParams {
 constexpr int kSplitThreads = 256;
 constexpr int kSplitVec = 16;                                   // float4 per thread
 constexpr int kSplitMaxCols = kSplitThreads * 4 * kSplitVec;    // 16384
-static __global__ void __launch_bounds__(kSplitThreads) prefill_split_kernel(PrefillSplitParams p)
+// The split of one token row held in registers (v: the row, float4 slot
+// threadIdx.x + kSplitThreads * i; g: the gain, 1 without norm): the
+// statistics of gemv_stage (sum of squares of x, max of |gain * x|), the
+// exponent, and the hi/lo parts into the swizzled operand tiles.
+template <int THREADS, int VEC>
+__device__ __forceinline__ void split_emit(const PrefillSplitParams &p, int t, bool live, const float4 (&v)[VEC],
+                                           const float4 (&g)[VEC])
 {
-    __shared__ float red[2][kSplitThreads / 32];
-    const int t = blockIdx.x, tt = t >> 7, m = t & 127;
+    __shared__ float red[2][THREADS / 32];
+    const int tt = t >> 7, m = t & 127;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const bool live = t < p.count;
-    const float *xr = p.x + (size_t)(live ? t : 0) * p.x_stride;
     const int vecs = (p.kchunks * kPgK) / 4;  // float4 slots of the padded row
-    float4 v[kSplitVec], g[kSplitVec];
-#pragma unroll
-    for (int i = 0; i < kSplitVec; i++) {
-        const int c = 4 * (threadIdx.x + kSplitThreads * i);
-        v[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        g[i] = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
-        if (live && c < p.cols) {
-            v[i] = *reinterpret_cast<const float4 *>(xr + c);
-            if (p.gain) g[i] = *reinterpret_cast<const float4 *>(p.gain + c);
-        }
-    }
-    // the statistics of gemv_stage: sum of squares of x, max of |gain * x|
     float ss = 0.0f, mx = 0.0f;
 #pragma unroll
-    for (int i = 0; i < kSplitVec; i++) {
+    for (int i = 0; i < VEC; i++) {
         ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
         mx = fmaxf(mx, fmaxf(fmaxf(fabsf(g[i].x * v[i].x), fabsf(g[i].y * v[i].y)),
                              fmaxf(fabsf(g[i].z * v[i].z), fabsf(g[i].w * v[i].w))));
@@ -173,7 +165,7 @@ static __global__ void __launch_bounds__(kSplitThreads) prefill_split_kernel(Pre
     __syncthreads();
     float s = 0.0f, x = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kSplitThreads / 32; w++) {
+    for (int w = 0; w < THREADS / 32; w++) {
         s += red[0][w];
         x = fmaxf(x, red[1][w]);
     }
@@ -183,8 +175,8 @@ static __global__ void __launch_bounds__(kSplitThreads) prefill_split_kernel(Pre
     if (threadIdx.x == 0) p.inv_scale[t] = live ? exp2i(-e) : 0.0f;
     uint8_t *tile = p.xs + (size_t)tt * p.kchunks * 2 * kPgATile;
 #pragma unroll
-    for (int i = 0; i < kSplitVec; i++) {
-        const int slot = threadIdx.x + kSplitThreads * i;
+    for (int i = 0; i < VEC; i++) {
+        const int slot = threadIdx.x + THREADS * i;
         if (slot >= vecs) break;
         const int c = 4 * slot;
         float a0 = v[i].x, a1 = v[i].y, a2 = v[i].z, a3 = v[i].w;
@@ -204,6 +196,25 @@ static __global__ void __launch_bounds__(kSplitThreads) prefill_split_kernel(Pre
         *reinterpret_cast<uint2 *>(dst) = make_uint2(h0, h1);
         *reinterpret_cast<uint2 *>(dst + kPgATile) = make_uint2(l0, l1);
     }
+}
+
+static __global__ void __launch_bounds__(kSplitThreads) prefill_split_kernel(PrefillSplitParams p)
+{
+    const int t = blockIdx.x;
+    const bool live = t < p.count;
+    const float *xr = p.x + (size_t)(live ? t : 0) * p.x_stride;
+    float4 v[kSplitVec], g[kSplitVec];
+#pragma unroll
+    for (int i = 0; i < kSplitVec; i++) {
+        const int c = 4 * (threadIdx.x + kSplitThreads * i);
+        v[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        g[i] = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+        if (live && c < p.cols) {
+            v[i] = *reinterpret_cast<const float4 *>(xr + c);
+            if (p.gain) g[i] = *reinterpret_cast<const float4 *>(p.gain + c);
+        }
+    }
+    split_emit<kSplitThreads, kSplitVec>(p, t, live, v, g);
 }
 
 // ---- the GEMM ---------------------------------------------------------------------
@@ -630,6 +641,63 @@ static __global__ void __launch_bounds__(256) prefill_finish_kernel(PrefillFinis
             dst[j + 64] = b;
         }
     }
+}
+
+// ---- finish + the next projection's split, per token ----------------------------------
+// The residual (o, down) or SwiGLU (gate/up) epilogue of one token's row from
+// the K-range partials, in the same order as prefill_finish_kernel, kept in
+// registers; written to f.y when the row is needed later (h, x); then split
+// (RMS-normed with sp.gain) into the next projection's operand tiles. act,
+// which only the down projection reads, never goes to memory.
+constexpr int kFsThreads = 512;
+constexpr int kFsVec = kSplitMaxCols / (4 * kFsThreads);  // float4 per thread
+template <int EPI>
+static __global__ void __launch_bounds__(kFsThreads) prefill_finish_split_kernel(PrefillFinishParams f,
+                                                                                  PrefillSplitParams sp)
+{
+    const int t = blockIdx.x;
+    const bool live = t < f.count;
+    const int width = EPI == kEpiSwiGLU ? f.rows / 2 : f.rows;
+    const float *ws = f.ws + (size_t)(live ? t : 0) * f.ws_rows;
+    const size_t split_stride = (size_t)f.t_stride * f.ws_rows;
+    float4 v[kFsVec], g[kFsVec];
+#pragma unroll
+    for (int i = 0; i < kFsVec; i++) {
+        const int c = 4 * (threadIdx.x + kFsThreads * i);
+        v[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        g[i] = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+        if (live && c < width) {
+            if (sp.gain) g[i] = *reinterpret_cast<const float4 *>(sp.gain + c);
+            if constexpr (EPI == kEpiSwiGLU) {
+                // features c..c+3: gate at storage rows 2f, up at 2f + 1
+                float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+                for (int s = 0; s < f.splits; s++) {
+                    const float4 a = __ldcg(reinterpret_cast<const float4 *>(ws + s * split_stride + 2 * c));
+                    const float4 b = __ldcg(reinterpret_cast<const float4 *>(ws + s * split_stride + 2 * c + 4));
+                    lo.x += a.x; lo.y += a.y; lo.z += a.z; lo.w += a.w;
+                    hi.x += b.x; hi.y += b.y; hi.z += b.z; hi.w += b.w;
+                }
+                const float gv[4] = {lo.x * f.scale[0], lo.z * f.scale[0], hi.x * f.scale[0], hi.z * f.scale[0]};
+                const float uv[4] = {lo.y * f.scale[1], lo.w * f.scale[1], hi.y * f.scale[1], hi.w * f.scale[1]};
+                float o[4];
+#pragma unroll
+                for (int k = 0; k < 4; k++) o[k] = (gv[k] / (1.0f + expf(-gv[k]))) * uv[k];
+                v[i] = make_float4(o[0], o[1], o[2], o[3]);
+            } else {
+                float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int s = 0; s < f.splits; s++) {
+                    const float4 b = __ldcg(reinterpret_cast<const float4 *>(ws + s * split_stride + c));
+                    a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+                }
+                const float4 r = *reinterpret_cast<const float4 *>(f.res + (size_t)t * f.res_stride + c);
+                v[i] = make_float4(r.x + a.x * finish_scale(f, c), r.y + a.y * finish_scale(f, c + 1),
+                                   r.z + a.z * finish_scale(f, c + 2), r.w + a.w * finish_scale(f, c + 3));
+            }
+            if (f.y) *reinterpret_cast<float4 *>(f.y + (size_t)t * f.y_stride + c) = v[i];
+        }
+    }
+    if (!sp.xs) return;
+    split_emit<kFsThreads, kFsVec>(sp, t, live, v, g);
 }
 
 }  // namespace lun
