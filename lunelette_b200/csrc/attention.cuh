@@ -212,7 +212,10 @@ __device__ __forceinline__ void pf_issue_tile(float *dst, const float *src, int 
     cp_async_commit();
 }
 
-// Grid (ceil(count / 8), 8 KV heads), 128 threads.
+// Grid (ceil(count / 8), 8 KV heads, splits), 128 threads. Split s covers the
+// keys [s * split_len, (s + 1) * split_len) of the causal range (split_len a
+// multiple of 64); with one split the block writes the output, otherwise
+// (m, l, unnormalised o) per row for attention_combine_kernel.
 static __global__ void __launch_bounds__(kPfThreads) attention_prefill_kernel(AttnParams p, int count)
 {
     extern __shared__ float4 pf_smem4[];
@@ -226,15 +229,19 @@ static __global__ void __launch_bounds__(kPfThreads) attention_prefill_kernel(At
     pdl_launch_dependents();
     const int length = (p.step ? p.step->length : p.length) + p.token_offset;
     const int last = min(t0 + kPfTokens, count) - 1;      // last query token of the block
-    const int total = length + last + 1;                  // keys the block needs
-    const int tiles = (total + kPfKeys - 1) / kPfKeys;
+    const int split = blockIdx.z;
+    const int k0 = split * p.split_len;                   // first key of this split
+    const int total = min(length + last + 1, k0 + p.split_len);  // keys the block needs (end)
+    const int tiles = total > k0 ? (total - k0 + kPfKeys - 1) / kPfKeys : 0;
 
     auto kv_tile = [&](int tile, int kind) {
-        const int page = p.page_table[tile];
+        const int page = p.page_table[k0 / kPfKeys + tile];
         return p.kv + kv_offset(p.layer, p.num_pages, page, kind, kvh, 0);
     };
-    pf_issue_tile(ks, kv_tile(0, 0), min(kPfKeys, total), kPfRowStride);
-    pf_issue_tile(vs, kv_tile(0, 1), min(kPfKeys, total), kHeadDim);
+    if (tiles > 0) {
+        pf_issue_tile(ks, kv_tile(0, 0), min(kPfKeys, total - k0), kPfRowStride);
+        pf_issue_tile(vs, kv_tile(0, 1), min(kPfKeys, total - k0), kHeadDim);
+    }
     for (int i = tid; i < kPfRows * kHeadDim / 4; i += kPfThreads) {
         const int r = i >> 5, c = i & 31, tk = r >> 2, hh = r & 3;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -258,7 +265,7 @@ static __global__ void __launch_bounds__(kPfThreads) attention_prefill_kernel(At
         for (int e = 0; e < 8; e++) o[i][e] = 0.0f;
     }
     for (int tile = 0; tile < tiles; tile++) {
-        const int p0 = tile * kPfKeys, keys = min(kPfKeys, total - p0);
+        const int p0 = k0 + tile * kPfKeys, keys = min(kPfKeys, total - p0);
         cp_async_wait_one();  // K of this tile (its V may still be in flight)
         __syncthreads();
         // S = Q K^T for rows 4rg.., keys p0 + cg + 16j
@@ -346,11 +353,24 @@ static __global__ void __launch_bounds__(kPfThreads) attention_prefill_kernel(At
     for (int i = 0; i < 4; i++) {
         const int r = 4 * rg + i, tk = t0 + (r >> 2), head = kvh * 4 + (r & 3);
         if (tk >= count) continue;
-        const float inv = 1.0f / l_run[i];
-        float *dst = p.out + (size_t)tk * kQuery + head * kHeadDim + 8 * cg;
-        *reinterpret_cast<float4 *>(dst) = make_float4(o[i][0] * inv, o[i][1] * inv, o[i][2] * inv, o[i][3] * inv);
-        *reinterpret_cast<float4 *>(dst + 4) =
-            make_float4(o[i][4] * inv, o[i][5] * inv, o[i][6] * inv, o[i][7] * inv);
+        if (p.splits == 1) {
+            const float inv = 1.0f / l_run[i];
+            float *dst = p.out + (size_t)tk * kQuery + head * kHeadDim + 8 * cg;
+            *reinterpret_cast<float4 *>(dst) =
+                make_float4(o[i][0] * inv, o[i][1] * inv, o[i][2] * inv, o[i][3] * inv);
+            *reinterpret_cast<float4 *>(dst + 4) =
+                make_float4(o[i][4] * inv, o[i][5] * inv, o[i][6] * inv, o[i][7] * inv);
+        } else {
+            // a split past this token's causal range leaves l = 0 (the combine skips it)
+            const size_t slot = ((size_t)tk * kQueryHeads + head) * p.splits + split;
+            float *dst = p.part_acc + slot * kHeadDim + 8 * cg;
+            *reinterpret_cast<float4 *>(dst) = make_float4(o[i][0], o[i][1], o[i][2], o[i][3]);
+            *reinterpret_cast<float4 *>(dst + 4) = make_float4(o[i][4], o[i][5], o[i][6], o[i][7]);
+            if (cg == 0) {
+                p.part_ml[slot * 2] = m_run[i];
+                p.part_ml[slot * 2 + 1] = l_run[i];
+            }
+        }
     }
 }
 

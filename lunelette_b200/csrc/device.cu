@@ -97,7 +97,7 @@ extern "C" void lun_device_plan(size_t context, size_t block, lun_device_bytes *
     scratch += sizeof(StepParams);
     scratch += (uint64_t)block * (2 * kHidden + 2 * kQuery + kInner) * 4;  // x h q attn act
     scratch += (uint64_t)kVocab * 4;                                       // logits
-    scratch += (uint64_t)kPartSlots * (kHeadDim + 2) * 4;                  // attention partials
+    scratch += (uint64_t)kPartSlots * (kHeadDim + 2) * 4;                  // attention partials (decode)
     scratch += (uint64_t)context * kHeadDim * 2 * 4;                       // rope tables
     scratch += (uint64_t)pages_for(context) * 4 + 4;                        // page table + flag
     if (block > kGemvMaxTokens) {  // prefill GEMM workspace (sized for a 148-SM B200)
@@ -255,9 +255,17 @@ bad:
     return nullptr;
 }
 
+// Attention partial slots: the decode splits, and for blocks of tokens up to 17
+// key splits per (token, query head).
+static size_t part_slots_for(size_t block)
+{
+    const size_t prefill = block * kQueryHeads * 17;
+    return prefill > kPartSlots ? prefill : kPartSlots;
+}
+
 extern "C" lun_device *lun_device_create(size_t context, size_t block, char *error, size_t capacity)
 {
-    return create_device(context, pages_for(context), block, kPartSlots, error, capacity);
+    return create_device(context, pages_for(context), block, part_slots_for(block), error, capacity);
 }
 
 extern "C" lun_device *lun_device_create_batch(size_t pool_pages, size_t session_context, size_t block,
@@ -269,8 +277,7 @@ extern "C" lun_device *lun_device_create_batch(size_t pool_pages, size_t session
         return nullptr;
     }
     // partial slots for block tokens x 32 heads x up to 16 position splits
-    const size_t slots = block * kQueryHeads * 16 > kPartSlots ? block * kQueryHeads * 16 : kPartSlots;
-    lun_device *d = create_device(session_context, pool_pages, block, slots, error, capacity);
+    lun_device *d = create_device(session_context, pool_pages, block, part_slots_for(block), error, capacity);
     if (!d) return nullptr;
     d->max_sessions = (int)max_sessions;
     d->session_pages = (int)pages_for(session_context);

@@ -259,6 +259,20 @@ constexpr int kAttnMaxSplit = 512;
 
 void lun_attention_plan(AttnParams *a, int total, int count, int sm_count, int slots)
 {
+    if (count > kGemvMaxTokens && !a->positions) {
+        // blocks of one sequence's tokens (attention_prefill_kernel): key
+        // ranges of whole pages split so that about two waves of blocks run
+        const int qtiles = (count + kPfTokens - 1) / kPfTokens;
+        const int pages = (total + kPage - 1) / kPage;
+        int splits = (4 * sm_count + qtiles * kKVHeads - 1) / (qtiles * kKVHeads);
+        const int cap = slots / (count * kQueryHeads);
+        splits = splits > cap ? cap : splits;
+        splits = splits < 1 ? 1 : (splits > pages ? pages : splits);
+        const int per = (pages + splits - 1) / splits;
+        a->split_len = per * kPage;
+        a->splits = (pages + per - 1) / per;
+        return;
+    }
     int wanted = (2 * sm_count + 8 * count - 1) / (8 * count);  // splits per (token, kv head)
     // and no split longer than kAttnMaxSplit positions: a long sequence among
     // many short ones (batched decode) must not stream its prefix serially
@@ -285,9 +299,13 @@ cudaError_t lun_launch_attention(const AttnParams &a, int count, cudaStream_t st
 {
     cudaError_t e = lun_kernels_ensure();
     if (e != cudaSuccess) return e;
-    if (count > kGemvMaxTokens && !a.positions)  // blocks of one sequence's tokens: one pass over the keys per 8
-        return launch(attention_prefill_kernel, dim3((count + kPfTokens - 1) / kPfTokens, kKVHeads), dim3(kPfThreads),
-                      kPfSmemBytes, stream, a, count);
+    if (count > kGemvMaxTokens && !a.positions) {  // blocks of one sequence's tokens: key pages per 8 query tokens
+        if (a.splits < 1 || a.split_len < kPage || (a.split_len % kPage)) return cudaErrorInvalidValue;
+        e = launch(attention_prefill_kernel, dim3((count + kPfTokens - 1) / kPfTokens, kKVHeads, a.splits),
+                   dim3(kPfThreads), kPfSmemBytes, stream, a, count);
+        if (e != cudaSuccess || a.splits == 1) return e;
+        return launch(attention_combine_kernel, dim3(kQueryHeads, count), dim3(128), 0, stream, a);
+    }
     if (a.splits < 1 || a.split_len < kTile || (a.split_len % kTile)) return cudaErrorInvalidValue;
     dim3 grid(a.splits, kKVHeads, count);
     e = launch(attention_split_kernel, grid, dim3(128), kAttnSmemBytes, stream, a);
