@@ -31,6 +31,8 @@
 // Every wait is bounded (kSpinLimit polls): a CTA that gives up sets *error and
 // later waits return at once, so a failed launch ends and the host reports it.
 #pragma once
+#include <cuda.h>
+
 #include "async.cuh"
 #include "attention.cuh"
 #include "gemv.cuh"
@@ -55,6 +57,20 @@ constexpr int kAttnMaxRanges = 18;               // position ranges per KV head 
 constexpr int kHeadModeMax = 112;                // positions up to which each query head gets a CTA
 constexpr int kQStride = 36;                     // floats per staged query quarter (32 + pad)
 constexpr int kCmbStride = 132;                  // floats per (warp, head) attention partial
+// FFN in act slices: slice s (64 SwiGLU features, CTA s) takes the 16 gate/up
+// tiles that produce it, then the slice's 64 columns of down for all 3072 rows
+// as 16 items of 24 tile pieces (8 rows x 64 columns, 512 bytes each): items
+// as large as a slot, so the ring holds most of the slice's down before act
+// is ready (smaller items measured slower: fewer bytes in flight per warp).
+constexpr int kFfnSlices = kInner / 64;
+constexpr int kSliceTiles = kGateUpRows / kTileRows / kFfnSlices;
+constexpr int kDownItemTiles = 24;
+constexpr int kDownItems = kHidden / kTileRows / kDownItemTiles;
+constexpr int kActOffset = (kHidden / 64) * 256;  // act slice and down row sums after the gate/up fragments
+static_assert(kSliceTiles * kTileRows * kFfnSlices == kGateUpRows && kDownItemTiles * 512 <= kSlotBytes &&
+                  kDownItems * kDownItemTiles * kTileRows == kHidden,
+              "FFN slices cover gate/up and down, a down item fits a slot");
+static_assert(kActOffset + (64 + kHidden) * 4 <= kFragBytes, "act slice and down row sums fit the fragment area");
 static_assert((16 * kQStride + 2 * kHeadDim + kMegaConsumerWarps * 4 * kCmbStride) * 4 <= kFragBytes,
               "attention staging fits the fragment area");
 
@@ -93,12 +109,15 @@ enum { kPhQKV, kPhO, kPhGateUp, kPhDown, kPhHead };
 
 // This CTA's share of one phase: `items` consecutive items of `item_bytes`
 // starting at src. FP8 phases: whole 8-row tiles from tile `first`, each
-// split into K-chunks; head: 2-row items of the BF16 embedding from row `first`.
+// split into K-chunks; head: 2-row items of the BF16 embedding from row `first`;
+// down (tma = layer + 1): item i is the box {0, first, 24 i, layer} of the
+// down tensor map (act slice `first`, tiles 24 i .. 24 i + 23).
 struct PhaseSpan {
     const uint8_t *src;
     int items;
     int item_bytes;
     int first;
+    int tma;
 };
 
 __device__ __forceinline__ void cta_range(int units, int &u0, int &u1)
@@ -121,13 +140,19 @@ __device__ __forceinline__ PhaseSpan phase_span(const MegaParams &p, int layer, 
                 2 * kHidden * 2, 4 * g0};
     }
     const uint8_t *base = p.w8 + (size_t)layer * (lq + lo + lg + ld);
+    if (ph == kPhGateUp || ph == kPhDown) {
+        const int s = blockIdx.x;  // act slice of this CTA; CTAs past the last slice idle in the FFN
+        if (s >= kFfnSlices) return {base, 0, kSlotBytes, 0, 0};
+        if (ph == kPhDown) return {nullptr, kDownItems, kDownItemTiles * 512, s, layer + 1};
+        constexpr int nb = kHidden / kBlockCols, cb = item_blocks(kPhGateUp);
+        return {base + lq + lo + (size_t)s * kSliceTiles * nb * kBlockBytes, kSliceTiles * (nb / cb),
+                cb * kBlockBytes, s * kSliceTiles, 0};
+    }
     const uint8_t *m;
     int tiles, nb;
     switch (ph) {
     case kPhQKV: m = base; tiles = kQKVRows / kTileRows; nb = kHidden / kBlockCols; break;
-    case kPhO: m = base + lq; tiles = kHidden / kTileRows; nb = kQuery / kBlockCols; break;
-    case kPhGateUp: m = base + lq + lo; tiles = kGateUpRows / kTileRows; nb = kHidden / kBlockCols; break;
-    default: m = base + lq + lo + lg; tiles = kHidden / kTileRows; nb = kInner / kBlockCols; break;
+    default: m = base + lq; tiles = kHidden / kTileRows; nb = kQuery / kBlockCols; break;
     }
     const int cb = item_blocks(ph);
     int t0, t1;
@@ -185,8 +210,9 @@ __device__ __forceinline__ bool cursor_settle(const MegaParams &p, WarpCursor &c
 // it; the lanes issue independently, so a slow warp holds back only its own
 // stream. Each lane also keeps its next items (p.l2_ahead / 7 bytes) prefetched
 // into L2 while the layers run; the head streams without waits and reads
-// nothing ahead.
-__device__ __forceinline__ void produce(const MegaParams &p, const Ring &r, int w)
+// nothing ahead. Down items are tensor copies through down_map (24 pieces of
+// 512 bytes, one per tile, gathered into one slot).
+__device__ __forceinline__ void produce(const MegaParams &p, const Ring &r, int w, const void *down_map)
 {
     const int total = p.steps * kPhasesPerStep;
     WarpCursor rc = {0, w, 0u, stream_span(p, 0)}, pc = rc;
@@ -197,7 +223,12 @@ __device__ __forceinline__ void produce(const MegaParams &p, const Ring &r, int 
         const unsigned ahead = rc.k % kPhasesPerStep == kLayers * 4 ? 0u : budget;
         while (pf_more && pf_bytes < ring_bytes + ahead) {
             const unsigned n = (unsigned)pc.sp.item_bytes;
-            if (pf_bytes >= ring_bytes) l2_prefetch(pc.sp.src + (size_t)pc.i * n, n);  // not yet in the ring
+            if (pf_bytes >= ring_bytes) {  // not yet in the ring
+                if (pc.sp.tma)
+                    tma_prefetch_4d(down_map, 0, pc.sp.first, pc.i * kDownItemTiles, pc.sp.tma - 1);
+                else
+                    l2_prefetch(pc.sp.src + (size_t)pc.i * n, n);
+            }
             pf_bytes += n;
             pc.i += kMegaConsumerWarps;
             pf_more = cursor_settle(p, pc, w, total);
@@ -206,7 +237,11 @@ __device__ __forceinline__ void produce(const MegaParams &p, const Ring &r, int 
         if (use && !mbar_wait(&r.empty[slot], (use - 1) & 1, p.error)) return;
         const unsigned n = (unsigned)rc.sp.item_bytes;
         mbar_expect_tx(&r.full[slot], n);
-        bulk_g2s(r.slots + (size_t)slot * kSlotBytes, rc.sp.src + (size_t)rc.i * n, n, &r.full[slot]);
+        if (rc.sp.tma)
+            tma_load_4d(r.slots + (size_t)slot * kSlotBytes, down_map, 0, rc.sp.first, rc.i * kDownItemTiles,
+                        rc.sp.tma - 1, &r.full[slot]);
+        else
+            bulk_g2s(r.slots + (size_t)slot * kSlotBytes, rc.sp.src + (size_t)rc.i * n, n, &r.full[slot]);
         ring_bytes += n;
         rc.i += kMegaConsumerWarps;
         more = cursor_settle(p, rc, w, total);
@@ -306,21 +341,29 @@ __device__ __forceinline__ float consumers_sum(float v, float *red)
     return warp_sum(t);
 }
 
-// Rows [row0, row0 + n) of a vector another CTA wrote -> shared memory, for an
-// epilogue; the loads overlap the fragment staging that follows.
-__device__ __forceinline__ void stage_rows(float *dst, const float *src, int row0, int n)
+// 64-bit fixed point with 32 fraction bits: the last layer's output x is summed
+// in it (integer additions, so the sum does not depend on their order).
+__device__ __forceinline__ float fixed_to_float(long long v) { return (float)v * 0x1p-32f; }
+__device__ __forceinline__ long long float_to_fixed(float v) { return __float2ll_rn(v * 0x1p32f); }
+
+// Rows [row0, row0 + n) of the layer input x -> shared memory, for an
+// epilogue; the loads overlap the fragment staging that follows. x is the
+// embedding row (emb) or the fixed-point sum xfix that other CTAs wrote.
+__device__ __forceinline__ void stage_x_rows(float *dst, const long long *xfix, const uint16_t *emb, int row0, int n)
 {
-    for (int i = threadIdx.x; i < n; i += kMegaConsumers) dst[i] = __ldcg(&src[row0 + i]);
+    for (int i = threadIdx.x; i < n; i += kMegaConsumers)
+        dst[i] = emb ? bf16_lo((uint32_t)emb[row0 + i]) : fixed_to_float(__ldcg(&xfix[row0 + i]));
 }
 
 // Activation row -> hi/lo FP16 B fragments (lanes 0-7 of every half block, the
 // layout of gemv_stage with one token), optionally RMS-normalised, in one pass:
 // every consumer thread holds its float4s in registers while the sum of squares
 // and the magnitude bound are reduced. src is another CTA's output (read through
-// L2) or, with emb, the BF16 embedding row. Returns 2^-e, the inverse scale.
+// L2; or src64, the same in 64-bit fixed point) or, with emb, the BF16
+// embedding row. Returns 2^-e, the inverse scale.
 template <int K>
-__device__ __forceinline__ float stage_frag(uint32_t *frag, const float *src, const uint16_t *emb, const float *gain,
-                                            float *red)
+__device__ __forceinline__ float stage_frag(uint32_t *frag, const float *src, const long long *src64,
+                                            const uint16_t *emb, const float *gain, float *red)
 {
     constexpr int kF4 = K / 4;
     constexpr int kPer = (kF4 + kMegaConsumers - 1) / kMegaConsumers;
@@ -338,6 +381,10 @@ __device__ __forceinline__ float stage_frag(uint32_t *frag, const float *src, co
             if (emb) {
                 const uint2 e = *reinterpret_cast<const uint2 *>(emb + 4 * idx);
                 v[u] = make_float4(bf16_lo(e.x), bf16_hi(e.x), bf16_lo(e.y), bf16_hi(e.y));
+            } else if (src64) {
+                const longlong2 a = __ldcg(reinterpret_cast<const longlong2 *>(src64) + 2 * idx);
+                const longlong2 b = __ldcg(reinterpret_cast<const longlong2 *>(src64) + 2 * idx + 1);
+                v[u] = make_float4(fixed_to_float(a.x), fixed_to_float(a.y), fixed_to_float(b.x), fixed_to_float(b.y));
             } else {
                 v[u] = __ldcg(reinterpret_cast<const float4 *>(src) + idx);
             }
@@ -414,7 +461,7 @@ __device__ __forceinline__ void consume_fp8(const Ring &r, const PhaseSpan &sp, 
         mbar_wait(&r.full[slot], use & 1, error);
         const uint8_t *s = r.slots + (size_t)slot * kSlotBytes;
         const uint4 *xf = frag + (size_t)(i % kChunks) * CB * 32;  // two 64-column pieces per block
-        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        float c[4][4] = {};  // per k16 step j of a block: four independent accumulation chains
 #pragma unroll 4
         for (int b = 0; b < CB; b++) {
             const uint4 wa = *reinterpret_cast<const uint4 *>(s + b * kBlockBytes + lane * 16);
@@ -425,12 +472,13 @@ __device__ __forceinline__ void consume_fp8(const Ring &r, const PhaseSpan &sp, 
                 x0 = xf[(piece * 2) * 8 + (lane & 7)];
                 x1 = xf[(piece * 2 + 1) * 8 + (lane & 7)];
             }
-            mma_block(c, wa, wb, x0, x1);
+            mma_block4(c, wa, wb, x0, x1);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&r.empty[slot]);
         // lane (g, t4): t4 = 0 holds half 0 of row g (A rows g), t4 = 1 half 1 (A rows g + 8)
-        float v = (lane & 1) ? c[2] + c[3] : c[0] + c[1];
+        float v = (lane & 1) ? (c[0][2] + c[0][3]) + (c[1][2] + c[1][3]) + ((c[2][2] + c[2][3]) + (c[3][2] + c[3][3]))
+                             : (c[0][0] + c[0][1]) + (c[1][0] + c[1][1]) + ((c[2][0] + c[2][1]) + (c[3][0] + c[3][1]));
         v += __shfl_xor_sync(0xffffffffu, v, 1);
         if ((lane & 3) == 0) partial[i * 8 + (lane >> 2)] = v;
     }
@@ -455,6 +503,69 @@ __device__ __forceinline__ void fp8_epilogue(const GemvParams &gp, const PhaseSp
         }
         gemv_epilogue<1, EPI>(gp, (sp.first + tl) * 2 + gq, lane, acc);
     }
+}
+
+// Down items of this CTA's act slice (64 features, act_s in shared memory):
+// each item holds kDownItemTiles tile pieces (8 rows x the slice's 64 columns),
+// taken in pairs as the two 8-row halves of one m16n8k16 A tile, so every MMA
+// row is a weight row and the B operand's columns 0 and 1 are the slice's hi
+// and lo parts (same fragments for every pair; lanes 8-31 zero). The item's
+// row sums (rows 8 kDownItemTiles i ..), scaled by 2^-e and the tensor's scale,
+// go to rows_s[3072]; down_reduce then adds them into xfix.
+__device__ __forceinline__ void consume_down(const Ring &r, const PhaseSpan &sp, unsigned seq0, unsigned &taken,
+                                             const float *act_s, float *rows_s, float scale, int *error)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (first_item(seq0) >= sp.items) return;
+    const float a0 = act_s[lane], a1 = act_s[lane + 32];
+    const int e = frag_exponent(warp_max(fmaxf(fabsf(a0), fabsf(a1))) * 1.0001f);
+    const float sc = exp2i(e), out_scale = scale * exp2i(-e);
+    const int n = lane >> 2, t4 = lane & 3;
+    uint32_t b[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+    if (n < 2) {
+        // k-step j: b0 = columns 16j + 2 t4 (+1), b1 = columns 16j + 2 t4 + 8 (+9)
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            const int c = 16 * (q >> 1) + 2 * t4 + 8 * (q & 1);
+            uint32_t hi, lo;
+            split_hilo(act_s[c] * sc, act_s[c + 1] * sc, hi, lo);
+            b[q] = n == 0 ? hi : lo;
+        }
+    }
+    const uint4 x0 = make_uint4(b[0], b[1], b[2], b[3]), x1 = make_uint4(b[4], b[5], b[6], b[7]);
+    for (int i = first_item(seq0); i < sp.items; i += kMegaConsumerWarps) {
+        float *rows = rows_s + (size_t)i * kDownItemTiles * kTileRows;
+        const unsigned k = taken++;
+        const unsigned slot = slot_of(warp, k), use = k / kSlotsPerWarp;
+        mbar_wait(&r.full[slot], use & 1, error);
+        const uint8_t *s = r.slots + (size_t)slot * kSlotBytes;
+#pragma unroll 4
+        for (int q = 0; q < kDownItemTiles / 2; q++) {
+            const uint4 wa = *reinterpret_cast<const uint4 *>(s + q * 1024 + lane * 16);
+            const uint4 wb = *reinterpret_cast<const uint4 *>(s + q * 1024 + 512 + lane * 16);
+            float c[4][4] = {};
+            mma_block4(c, wa, wb, x0, x1);
+            // lane (g, 0): row g of the pair's first tile (c0 hi + c1 lo) and of its second (c2 + c3)
+            if (t4 == 0) {
+                rows[q * 16 + n] =
+                    ((c[0][0] + c[0][1]) + (c[1][0] + c[1][1]) + ((c[2][0] + c[2][1]) + (c[3][0] + c[3][1]))) *
+                    out_scale;
+                rows[q * 16 + 8 + n] =
+                    ((c[0][2] + c[0][3]) + (c[1][2] + c[1][3]) + ((c[2][2] + c[2][3]) + (c[3][2] + c[3][3]))) *
+                    out_scale;
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&r.empty[slot]);
+    }
+}
+
+// The CTA's 3072 down row sums (rows_s) added into xfix, the layer output x
+// in fixed point, with 64-bit integer reductions.
+__device__ __forceinline__ void down_reduce(const float *rows_s, long long *xfix)
+{
+    for (int v = threadIdx.x; v < kHidden; v += kMegaConsumers)
+        asm volatile("red.global.add.u64 [%0], %1;" ::"l"(xfix + v), "l"(float_to_fixed(rows_s[v])) : "memory");
 }
 
 __device__ __forceinline__ void arg_better(float &v, int &i, float v2, int i2)
@@ -797,7 +908,8 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
     }
 }
 
-__global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams p)
+__global__ void __launch_bounds__(kMegaThreads, 1)
+    decode_mega_kernel(MegaParams p, const __grid_constant__ CUtensorMap down_map)
 {
     extern __shared__ __align__(128) uint8_t mega_smem[];
     __shared__ float red[32];
@@ -824,7 +936,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
 
     if (threadIdx.x >= kMegaConsumers) {
         const int lane = threadIdx.x & 31;
-        if (lane < kMegaConsumerWarps) produce(p, ring, lane);
+        if (lane < kMegaConsumerWarps) produce(p, ring, lane, &down_map);
         return;
     }
 
@@ -871,14 +983,15 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
             gp.qkv_tagged = p.qkvt;
             gp.ytag = p.tag_base + epoch - 1;
             const int mk = layer * kMarksPerLayer;
+            // the layer input x: the embedding row, else the last layer's xfix
+            // (its h, stored by its o epilogue, plus every act slice's down rows)
+            const int cur = (layer & 1) * kHidden, prev = kHidden - cur;  // hbuf / xfix halves
             // the attention unit's K/V rows of earlier steps do not depend on
             // this layer's qkv: start them towards L2 now
             if (unit >= 0 && threadIdx.x < 2) attention_prefetch(p, layer, length, akvh, arange, ranges, threadIdx.x);
-            float inv = stage_frag<kHidden>(frag, p.x, layer == 0 ? emb_row : nullptr,
+            float inv = stage_frag<kHidden>(frag, nullptr, p.xfix + prev, layer == 0 ? emb_row : nullptr,
                                             p.norms + (size_t)(2 * layer) * kHidden, red);
             if (threadIdx.x == 0) record_mark(p, rec, mk);
-            if (layer == 0 && blockIdx.x == 0)
-                for (int c = threadIdx.x; c < kHidden; c += kMegaConsumers) p.x[c] = bf16_lo((uint32_t)emb_row[c]);
             consume_fp8<item_blocks(kPhQKV), kHidden / kBlockCols>(ring, sp, seq, taken, frag4, partial, p.error);
             seq += sp.items;
             consumers_sync();
@@ -909,13 +1022,17 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
             gp.bound[0] = gp.bound[1] = 1 << 30;
             gp.res_shared = res_s;
             gp.res_base = sp.first * kTileRows;
-            gp.y = p.h;
+            // h = x + o, as a float for the FFN's norm and as the starting
+            // value of this layer's xfix (read only after the FFN barrier)
+            gp.y = p.hbuf + cur;
+            gp.y_fixed = p.xfix + cur;
             gp.y_stride = kHidden;
-            stage_rows(res_s, p.x, gp.res_base, sp.items / (kQuery / kBlockCols / item_blocks(kPhO)) * kTileRows);
+            stage_x_rows(res_s, p.xfix + prev, layer == 0 ? emb_row : nullptr, gp.res_base,
+                         sp.items / (kQuery / kBlockCols / item_blocks(kPhO)) * kTileRows);
             // every KV head's attention output stored
             if (threadIdx.x == 0) thread_wait(sync_word(p, kSyncAttn), attn_target, p.error);
             consumers_sync();
-            inv = stage_frag<kQuery>(frag, p.attn, nullptr, nullptr, red);
+            inv = stage_frag<kQuery>(frag, p.attn, nullptr, nullptr, nullptr, red);
             if (threadIdx.x == 0) record_mark(p, rec, mk + 4);
             consume_fp8<item_blocks(kPhO), kQuery / kBlockCols>(ring, sp, seq, taken, frag4, partial, p.error);
             seq += sp.items;
@@ -923,56 +1040,56 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(MegaParams
             if (threadIdx.x == 0) record_mark(p, rec, mk + 5);
             fp8_epilogue<kEpiResidual>(gp, sp, kQuery / kBlockCols / item_blocks(kPhO), partial, inv);
             grid_sync(p, ++barrier, rec, mk + 6);
-            // post norm + gate/up + SwiGLU
+            // FFN of act slice s = blockIdx.x: post norm, the slice's 16 gate/up
+            // tiles and SwiGLU into shared memory (act never leaves the CTA), then
+            // the slice's 64 columns of down for every row, added into xfix;
+            // the next layer reads x from xfix after one barrier
             sp = phase_span(p, layer, kPhGateUp);
             gp.rows = kGateUpRows;
             gp.cols = kHidden;
             gp.scale[0] = sc[4];
             gp.scale[1] = sc[5];
-            gp.y = p.act;
+            gp.res_shared = nullptr;
+            gp.y_fixed = nullptr;
+            // features 64 s .. 64 s + 63 land in act_s[0 .. 63]
+            float *act_s = reinterpret_cast<float *>(mega_smem + (size_t)kRingSlots * kSlotBytes + kActOffset);
+            gp.y = act_s - (ptrdiff_t)blockIdx.x * 64;
             gp.y_stride = kInner;
-            inv = stage_frag<kHidden>(frag, p.h, nullptr, p.norms + (size_t)(2 * layer + 1) * kHidden, red);
+            inv = stage_frag<kHidden>(frag, p.hbuf + cur, nullptr, nullptr, p.norms + (size_t)(2 * layer + 1) * kHidden,
+                                      red);
             if (threadIdx.x == 0) record_mark(p, rec, mk + 7);
             consume_fp8<item_blocks(kPhGateUp), kHidden / kBlockCols>(ring, sp, seq, taken, frag4, partial, p.error);
             seq += sp.items;
             consumers_sync();
             if (threadIdx.x == 0) record_mark(p, rec, mk + 8);
             fp8_epilogue<kEpiSwiGLU>(gp, sp, kHidden / kBlockCols / item_blocks(kPhGateUp), partial, inv);
-            // down's residual rows (h) are final since the o barrier: staged
-            // before this barrier, off the down phase's critical path
+            consumers_sync();
+            if (threadIdx.x == 0) record_mark(p, rec, mk + 9);
             sp = phase_span(p, layer, kPhDown);
-            stage_rows(res_s, p.h, sp.first * kTileRows,
-                       sp.items / (kInner / kBlockCols / item_blocks(kPhDown)) * kTileRows);
-            grid_sync(p, ++barrier, rec, mk + 9);
-            // down + residual (h)
-            gp.rows = kHidden;
-            gp.cols = kInner;
-            gp.scale[0] = gp.scale[1] = gp.scale[2] = sc[6];
-            gp.res_base = sp.first * kTileRows;
-            gp.y = p.x;
-            gp.y_stride = kHidden;
-            inv = stage_frag<kInner>(frag, p.act, nullptr, nullptr, red);
-            if (threadIdx.x == 0) record_mark(p, rec, mk + 10);
-            consume_fp8<item_blocks(kPhDown), kInner / kBlockCols>(ring, sp, seq, taken, frag4, partial, p.error);
+            consume_down(ring, sp, seq, taken, act_s, act_s + 64, sc[6], p.error);
             seq += sp.items;
             consumers_sync();
+            if (sp.items) down_reduce(act_s + 64, p.xfix + cur);
             if (threadIdx.x == 0) record_mark(p, rec, mk + 11);
-            fp8_epilogue<kEpiResidual>(gp, sp, kInner / kBlockCols / item_blocks(kPhDown), partial, inv);
             grid_sync(p, ++barrier, rec, mk + 12);
         }
-        // final norm + tied head, 8-column staging
+        // final norm + tied head, 8-column staging; the last layer's x from xfix
+        // (CTA 0 also stores it, the step's final residual stream)
         {
+            const long long *xl = p.xfix + (size_t)((kLayers - 1) & 1) * kHidden;
             float ss = 0.0f;
             for (int c = threadIdx.x; c < kHidden; c += kMegaConsumers) {
-                float v = __ldcg(&p.x[c]);
+                const float v = fixed_to_float(__ldcg(&xl[c]));
                 ss += v * v;
             }
             ss = consumers_sum(ss, red);
             const float rs = rsqrtf(ss / (float)kHidden + kNormEps);
             const int NQ = kHidden >> 3;
-            for (int c = threadIdx.x; c < kHidden; c += kMegaConsumers)
-                xs_head[((size_t)((c >> 2) & 1) * NQ + (c >> 3)) * 4 + (c & 3)] =
-                    p.final_norm[c] * (__ldcg(&p.x[c]) * rs);
+            for (int c = threadIdx.x; c < kHidden; c += kMegaConsumers) {
+                const float v = fixed_to_float(__ldcg(&xl[c]));
+                if (blockIdx.x == 0) p.x[c] = v;
+                xs_head[((size_t)((c >> 2) & 1) * NQ + (c >> 3)) * 4 + (c & 3)] = p.final_norm[c] * (v * rs);
+            }
             consumers_sync();
         }
         float best = -INFINITY;

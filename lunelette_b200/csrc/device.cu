@@ -60,6 +60,9 @@ struct lun_device {
     float *d_scales = nullptr;          // [26][7]
     unsigned *mega_sync = nullptr;      // kSyncWords lines, zeroed before every launch
     unsigned long long *mega_qkvt = nullptr;  // tagged q/k/v words the persistent kernel exchanges
+    float *mega_ffn = nullptr;                // [2][3072] h, then [2][3072] 64-bit xfix (MegaParams::hbuf, xfix)
+    alignas(64) unsigned char down_map[128];  // tensor map of the down projections (lun_down_slice_map)
+    bool down_map_ready = false;
     unsigned mega_tag = 1;                    // tag of the next launch's first layer (never 0)
     unsigned l2_ahead = 0;              // persistent kernel's L2 lookahead (bytes per CTA)
     int *mega_error = nullptr, *h_error = nullptr;
@@ -193,6 +196,7 @@ static lun_device *create_device(size_t context, size_t kv_pages, size_t block, 
         (e = dalloc(&d->d_scales, (size_t)kLayers * LUN_SLOT_COUNT * 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->mega_sync, kSyncWords * kSyncStride * sizeof(unsigned), sc)) != cudaSuccess ||
         (e = dalloc(&d->mega_qkvt, (size_t)kQKVRows * sizeof(unsigned long long), sc)) != cudaSuccess ||
+        (e = dalloc(&d->mega_ffn, (size_t)6 * kHidden * sizeof(float), sc)) != cudaSuccess ||
         (e = dalloc(&d->mega_error, sizeof(int), sc)) != cudaSuccess ||
         (e = dalloc(&d->arg_val, (size_t)d->sm_count * 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->arg_idx, (size_t)d->sm_count * 4, sc)) != cudaSuccess ||
@@ -352,6 +356,7 @@ extern "C" void lun_device_destroy(lun_device *d)
     cudaFreeHost(d->h_meta);
     cudaFreeHost(d->h_next);
     cudaFree(d->mega_qkvt);
+    cudaFree(d->mega_ffn);
     cudaFree(d->mega_error);
     cudaFree(d->arg_val);
     cudaFree(d->arg_idx);
@@ -685,7 +690,8 @@ static cudaError_t launch_mega(lun_device *d, int steps)
     p.rope_sin = d->rope_sin;
     p.step = d->d_step;
     p.x = d->x;
-    p.h = d->h;
+    p.hbuf = d->mega_ffn;
+    p.xfix = reinterpret_cast<long long *>(d->mega_ffn + 2 * kHidden);
     // tags of this launch's layers: mega_tag .. mega_tag + 26 * steps - 1; a
     // wrap restarts from 1 over freshly zeroed words, so no old word matches
     const unsigned long long span = (unsigned long long)steps * kLayers;
@@ -698,7 +704,6 @@ static cudaError_t launch_mega(lun_device *d, int steps)
     p.tag_base = d->mega_tag;
     d->mega_tag += (unsigned)span;
     p.attn = d->attn;
-    p.act = d->act;
     p.part_acc = d->part_acc;
     p.part_ml = d->part_ml;
     p.logits = d->logits;
@@ -711,9 +716,16 @@ static cudaError_t launch_mega(lun_device *d, int steps)
     p.steps = steps;
     p.timeline = d->record_timeline ? d->timeline : nullptr;
     p.l2_ahead = d->l2_ahead;
-    cudaError_t e = cudaMemsetAsync(d->mega_sync, 0, kSyncWords * kSyncStride * sizeof(unsigned), d->stream);
+    cudaError_t e;
+    if (!d->down_map_ready) {
+        if ((e = lun_down_slice_map(d->down_map, layer_base(d, 0) + kLayerQKV + kLayerO + kLayerGateUp,
+                                    kLayerBytes)) != cudaSuccess)
+            return e;
+        d->down_map_ready = true;
+    }
+    e = cudaMemsetAsync(d->mega_sync, 0, kSyncWords * kSyncStride * sizeof(unsigned), d->stream);
     if (e != cudaSuccess) return e;
-    return lun_launch_decode_mega(p, d->sm_count, d->stream);
+    return lun_launch_decode_mega(p, d->down_map, d->sm_count, d->stream);
 }
 
 // One decode step reading length/ids from d_step, ending with device greedy

@@ -99,8 +99,7 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two_codes)
 __device__ __forceinline__ void mma_f16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                               uint32_t b0, uint32_t b1)
 {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
@@ -118,6 +117,22 @@ __device__ __forceinline__ void mma_block(float (&c)[4], const uint4 &wa, const 
     mma_f16_16816(c, e4m3x2_to_f16x2(wa.z), e4m3x2_to_f16x2(wb.z), e4m3x2_to_f16x2(wa.z >> 16),
                   e4m3x2_to_f16x2(wb.z >> 16), x1.x, x1.y);
     mma_f16_16816(c, e4m3x2_to_f16x2(wa.w), e4m3x2_to_f16x2(wb.w), e4m3x2_to_f16x2(wa.w >> 16),
+                  e4m3x2_to_f16x2(wb.w >> 16), x1.z, x1.w);
+}
+
+// The same four MMAs with k16 step j accumulating into c[j]: independent
+// accumulators let consecutive MMAs issue back to back instead of each waiting
+// for the previous one's result.
+__device__ __forceinline__ void mma_block4(float (&c)[4][4], const uint4 &wa, const uint4 &wb, const uint4 &x0,
+                                           const uint4 &x1)
+{
+    mma_f16_16816(c[0], e4m3x2_to_f16x2(wa.x), e4m3x2_to_f16x2(wb.x), e4m3x2_to_f16x2(wa.x >> 16),
+                  e4m3x2_to_f16x2(wb.x >> 16), x0.x, x0.y);
+    mma_f16_16816(c[1], e4m3x2_to_f16x2(wa.y), e4m3x2_to_f16x2(wb.y), e4m3x2_to_f16x2(wa.y >> 16),
+                  e4m3x2_to_f16x2(wb.y >> 16), x0.z, x0.w);
+    mma_f16_16816(c[2], e4m3x2_to_f16x2(wa.z), e4m3x2_to_f16x2(wb.z), e4m3x2_to_f16x2(wa.z >> 16),
+                  e4m3x2_to_f16x2(wb.z >> 16), x1.x, x1.y);
+    mma_f16_16816(c[3], e4m3x2_to_f16x2(wa.w), e4m3x2_to_f16x2(wb.w), e4m3x2_to_f16x2(wa.w >> 16),
                   e4m3x2_to_f16x2(wb.w >> 16), x1.z, x1.w);
 }
 
@@ -190,6 +205,9 @@ struct GemvParams {
     const float *rope_row;
     const float *res_shared;
     int res_base;
+    // kEpiResidual, one token: the output rows also as 64-bit fixed point
+    // (value * 2^32, rounded), or nullptr
+    long long *y_fixed;
     // One-token QKV epilogue for readers on other CTAs: q rows and the
     // position's k and v rows also go out as tagged words (store_tagged) to
     // qkv_tagged[0..4096) (q), [4096..5120) (k), [5120..6144) (v), tag ytag;
@@ -321,6 +339,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, int g, int la
                                               : __ldcg(&p.res[(size_t)m * p.res_stride + r])) +
                                 v;
                         p.y[(size_t)m * p.y_stride + r] = v;
+                        if (EPI == kEpiResidual && p.y_fixed) p.y_fixed[r] = __float2ll_rn(v * 0x1p32f);
                     }
                 }
             }

@@ -54,7 +54,12 @@ cudaError_t lun_launch_greedy(const float *logits, int n, int *partials, lun::St
 namespace lun {
 struct MegaParams;
 }
-cudaError_t lun_launch_decode_mega(const lun::MegaParams &p, int sm_count, cudaStream_t stream);
+cudaError_t lun_launch_decode_mega(const lun::MegaParams &p, const void *down_map, int sm_count,
+                                   cudaStream_t stream);
+// down_map (128 bytes, 64-byte aligned): the tensor map of every layer's down
+// projection that the persistent kernel's FFN reads in act slices; down0 is
+// layer 0's tiled down matrix, layer_stride the bytes between layers.
+cudaError_t lun_down_slice_map(void *map, const uint8_t *down0, size_t layer_stride);
 // Whether the persistent kernel's per-CTA work fits on a grid of sm_count CTAs.
 bool lun_mega_supported(int sm_count);
 

@@ -5,19 +5,20 @@
 
 namespace lun {
 
-// Grid barriers per decode step: three per layer (after o, once h is whole;
-// after gate/up; after down, once x is whole) and one after the head and the
-// pick. qkv -> attention goes through tagged words (the attention CTAs poll the
-// q, k and v values themselves), attention -> o through a counter (kSyncAttn).
-constexpr int kMegaBarriersPerStep = kLayers * 3 + 1;
+// Grid barriers per decode step: two per layer (after o, once h is whole;
+// after the FFN, once every act slice's down output is added into dsum) and
+// one after the head and the pick. qkv -> attention goes through tagged words
+// (the attention CTAs poll the q, k and v values themselves), attention -> o
+// through a counter (kSyncAttn); gate/up -> down stays inside each CTA.
+constexpr int kMegaBarriersPerStep = kLayers * 2 + 1;
 // Timeline of the first step of a launch: [0] start, [1 + k] CTA 0 leaving
 // barrier k, then from kMegaTimelineHead one entry per CTA b for each mark m at
 // kMegaTimelineHead + m * gridDim.x + b. Marks per layer L, at 13L + :
 //   0 qkv row staged, 1 qkv items done, 2 q/k/v stored (tagged),
 //   3 attention published (CTAs that own a unit, else 0),
 //   4 o row staged, 5 o items done, 6 arrival at the o barrier,
-//   7 gate/up row staged, 8 items done, 9 arrival at the gate/up barrier,
-//   10 down row staged, 11 items done, 12 arrival at the down barrier;
+//   7 gate/up row staged, 8 gate/up items done, 9 act slice stored,
+//   10 (unused), 11 down items done, 12 arrival at the FFN barrier;
 // mark 13 * 26 is the arrival at the barrier after the pick.
 constexpr int kMarksPerLayer = 13;
 constexpr int kMegaMarksPerStep = kLayers * kMarksPerLayer + 1;
@@ -50,7 +51,11 @@ struct MegaParams {
     int num_pages;
     const float *rope_cos, *rope_sin;
     StepParams *step;        // length and ids[0] advance on the device each step
-    float *x, *h, *attn, *act;
+    float *x;                // the step's final residual stream (written before the head)
+    float *attn;
+    float *hbuf;             // [2][3072]: layer L's h (x + o) in hbuf[L & 1]
+    long long *xfix;         // [2][3072]: layer L's output x in xfix[L & 1], 64-bit fixed point (2^-32):
+                             // its o epilogue stores h, then every act slice adds its down rows
     unsigned long long *qkvt;  // the step's q (4096) and k, v (1024 each) of the current layer, tagged
     unsigned tag_base;         // tag of this launch's first layer (step s, layer L: tag_base + 26 s + L)
     float *part_acc, *part_ml;  // [8 KV heads][ranges][4 query heads][128] and [..][2]

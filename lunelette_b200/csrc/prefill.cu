@@ -45,7 +45,7 @@ void lun_prefill_workspace_bytes(int max_count, int sm_count, size_t *xs_bytes, 
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link
 // against libcuda).
-static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
+PFN_cuTensorMapEncodeTiled_v12000 lun_tensor_map_encoder()
 {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
         void *f = nullptr;
@@ -61,7 +61,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
 // The tiled FP8 matrix as the GEMM's 4-D weight tensor (prefill_gemm_pair_kernel).
 static cudaError_t weight_tensor_map(CUtensorMap *map, const uint8_t *W, int rows, int nb)
 {
-    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    PFN_cuTensorMapEncodeTiled_v12000 encode = lun_tensor_map_encoder();
     if (!encode || ((uintptr_t)W & 15)) return cudaErrorInvalidValue;
     const cuuint64_t dims[4] = {256, 2, (cuuint64_t)(2 * nb), (cuuint64_t)(rows / kTileRows)};
     const cuuint64_t strides[3] = {256, 512, (cuuint64_t)nb * kBlockBytes};

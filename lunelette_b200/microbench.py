@@ -92,29 +92,29 @@ def run(shapes, ms_list, iters, warmup=3):
     return rows_out
 
 
-PHASE_BYTES = {"qkv": 6144 * 3072, "attn_o": (6144 + 4096) * 3072, "gate_up": 18432 * 3072, "down": 3072 * 9216,
-               "head": 131072 * 3072 * 2}
+PHASE_BYTES = {"attn_o": (6144 + 4096) * 3072, "ffn": 18432 * 3072 + 3072 * 9216, "head": 131072 * 3072 * 2}
 
 
 def decode_phases(checkpoint, steps=8, prompt=32):
     """Phase durations of the persistent decode kernel (single-token steps through
     lunelette_metal_decode), from its %globaltimer timeline, as means over `steps`
     steps and 26 layers. Barrier phases, from CTA 0 leaving one barrier to
-    leaving the next: `attn_o` (qkv, attention, o), `gate_up`, `down`, `head`
-    (head GEMV and greedy pick); with `<phase>_spread`, first to last CTA
-    arriving, and `<phase>_release`, last arrival to CTA 0 leaving. Milestones
-    within a layer, measured from the barrier that opened the phase to the last
-    CTA reaching them (`@max`) and to the median CTA (`@med`): row staged, items
-    done, q/k/v published, attention published."""
+    leaving the next: `attn_o` (qkv, attention, o), `ffn` (gate/up, SwiGLU and
+    down of every act slice), `head` (head GEMV and greedy pick); with
+    `<phase>_spread`, first to last CTA arriving, and `<phase>_release`, last
+    arrival to CTA 0 leaving. Milestones within a layer, measured from the
+    barrier that opened the phase to the last CTA reaching them (`@max`) and to
+    the median CTA (`@med`): row staged, items done, q/k/v published, attention
+    published, act slice stored."""
     import torch
     import lunelette_b200 as L
     peak, kind = hbm_peak()
     ctas = torch.cuda.get_device_properties(0).multi_processor_count
-    barriers, per_layer = 79, 13
+    barriers, per_layer = 53, 13
     marks = 26 * per_layer + 1
     milestones = {0: "qkv_staged", 1: "qkv_items", 2: "qkv_published", 3: "attention", 4: "o_staged",
-                  5: "o_items", 7: "gate_up_staged", 8: "gate_up_items", 10: "down_staged", 11: "down_items"}
-    closing = {6: "attn_o", 9: "gate_up", 12: "down"}
+                  5: "o_items", 7: "gate_up_staged", 8: "gate_up_items", 9: "act_stored", 11: "down_items"}
+    closing = {6: "attn_o", 12: "ffn"}
     rows = {}
 
     def add(name, v):
@@ -138,18 +138,18 @@ def decode_phases(checkpoint, steps=8, prompt=32):
                         arr = arr[arr > 0]
                         add(milestones[k] + "@max", arr.max() - opened)
                         add(milestones[k] + "@med", float(np.median(arr)) - opened)
-                    else:
-                        b = 3 * layer + (k - 6) // 3
+                    elif k in closing:
+                        b = 2 * layer + (k == 12)
                         name = closing[k]
                         add(name, exits[b] - opened)
                         add(name + "_spread", arr.max() - arr.min())
                         add(name + "_release", exits[b] - arr.max())
                         opened = exits[b]
             arr = mark[marks - 1]
-            add("head", exits[78] - opened)
+            add("head", exits[barriers - 1] - opened)
             add("head_spread", arr.max() - arr.min())
-            add("head_release", exits[78] - arr.max())
-            add("step", exits[78] - start)
+            add("head_release", exits[barriers - 1] - arr.max())
+            add("step", exits[barriers - 1] - start)
         rt.timeline(False)
     out = []
     for name, vals in rows.items():
