@@ -207,44 +207,64 @@ __device__ __forceinline__ bool cursor_settle(const MegaParams &p, WarpCursor &c
 
 // Producer lane w (one per consumer warp): every item of warp w in stream
 // order, each as one bulk copy into the warp's next slot once the warp released
-// it; the lanes issue independently, so a slow warp holds back only its own
-// stream. Each lane also keeps its next items (p.l2_ahead / 7 bytes) prefetched
-// into L2 while the layers run; the head streams without waits and reads
-// nothing ahead. Down items are tensor copies through down_map (24 pieces of
-// 512 bytes, one per tile, gathered into one slot).
+// it. The seven lanes share one warp, so none of them may block it: they run
+// one convergent loop in which each lane probes its next slot without waiting
+// (mbarrier test_wait) and issues when it is free, so a slow consumer warp
+// holds back only its own stream. Each lane also keeps its next items
+// (p.l2_ahead / 7 bytes) prefetched into L2 while the layers run; the head
+// reads nothing ahead. Down items are tensor copies through down_map (24
+// pieces of 512 bytes, one per tile, gathered into one slot). A lane that sees
+// no free slot for kSpinLimit probes sets *error and stops.
 __device__ __forceinline__ void produce(const MegaParams &p, const Ring &r, int w, const void *down_map)
 {
+    constexpr unsigned kLanes = (1u << kMegaConsumerWarps) - 1;
     const int total = p.steps * kPhasesPerStep;
     WarpCursor rc = {0, w, 0u, stream_span(p, 0)}, pc = rc;
     bool more = cursor_settle(p, rc, w, total), pf_more = cursor_settle(p, pc, w, total);
     const unsigned budget = p.l2_ahead / kMegaConsumerWarps;
     unsigned long long ring_bytes = 0, pf_bytes = 0;
-    for (unsigned u = 0; more; u++) {
-        const unsigned ahead = rc.k % kPhasesPerStep == kLayers * 4 ? 0u : budget;
-        while (pf_more && pf_bytes < ring_bytes + ahead) {
-            const unsigned n = (unsigned)pc.sp.item_bytes;
-            if (pf_bytes >= ring_bytes) {  // not yet in the ring
-                if (pc.sp.tma)
-                    tma_prefetch_4d(down_map, 0, pc.sp.first, pc.i * kDownItemTiles, pc.sp.tma - 1);
-                else
-                    l2_prefetch(pc.sp.src + (size_t)pc.i * n, n);
+    unsigned u = 0, idle = 0;
+    while (__any_sync(kLanes, more)) {
+        bool issued = false;
+        if (more) {
+            const unsigned ahead = rc.k % kPhasesPerStep == kLayers * 4 ? 0u : budget;
+            while (pf_more && pf_bytes < ring_bytes + ahead) {
+                const unsigned n = (unsigned)pc.sp.item_bytes;
+                if (pf_bytes >= ring_bytes) {  // not yet in the ring
+                    if (pc.sp.tma)
+                        tma_prefetch_4d(down_map, 0, pc.sp.first, pc.i * kDownItemTiles, pc.sp.tma - 1);
+                    else
+                        l2_prefetch(pc.sp.src + (size_t)pc.i * n, n);
+                }
+                pf_bytes += n;
+                pc.i += kMegaConsumerWarps;
+                pf_more = cursor_settle(p, pc, w, total);
             }
-            pf_bytes += n;
-            pc.i += kMegaConsumerWarps;
-            pf_more = cursor_settle(p, pc, w, total);
+            const unsigned slot = slot_of(w, u), use = u / kSlotsPerWarp;
+            if (!use || mbar_test_wait(&r.empty[slot], (use - 1) & 1)) {
+                const unsigned n = (unsigned)rc.sp.item_bytes;
+                mbar_expect_tx(&r.full[slot], n);
+                if (rc.sp.tma)
+                    tma_load_4d(r.slots + (size_t)slot * kSlotBytes, down_map, 0, rc.sp.first,
+                                rc.i * kDownItemTiles, rc.sp.tma - 1, &r.full[slot]);
+                else
+                    bulk_g2s(r.slots + (size_t)slot * kSlotBytes, rc.sp.src + (size_t)rc.i * n, n, &r.full[slot]);
+                ring_bytes += n;
+                rc.i += kMegaConsumerWarps;
+                more = cursor_settle(p, rc, w, total);
+                u++;
+                idle = 0;
+                issued = true;
+            } else if (++idle > kSpinLimit) {
+                atomicExch(p.error, 1);
+                more = false;
+            } else if ((idle & 255u) == 0 && *(volatile int *)p.error) {
+                more = false;
+            }
         }
-        const unsigned slot = slot_of(w, u), use = u / kSlotsPerWarp;
-        if (use && !mbar_wait(&r.empty[slot], (use - 1) & 1, p.error)) return;
-        const unsigned n = (unsigned)rc.sp.item_bytes;
-        mbar_expect_tx(&r.full[slot], n);
-        if (rc.sp.tma)
-            tma_load_4d(r.slots + (size_t)slot * kSlotBytes, down_map, 0, rc.sp.first, rc.i * kDownItemTiles,
-                        rc.sp.tma - 1, &r.full[slot]);
-        else
-            bulk_g2s(r.slots + (size_t)slot * kSlotBytes, rc.sp.src + (size_t)rc.i * n, n, &r.full[slot]);
-        ring_bytes += n;
-        rc.i += kMegaConsumerWarps;
-        more = cursor_settle(p, rc, w, total);
+        // no slot was free: back off briefly instead of taking the issue slots
+        // of the consumer warp that shares this scheduler
+        if (!__any_sync(kLanes, issued)) __nanosleep(64);
     }
 }
 
@@ -460,7 +480,9 @@ __device__ __forceinline__ void consume_fp8(const Ring &r, const PhaseSpan &sp, 
         const unsigned slot = slot_of(warp, k), use = k / kSlotsPerWarp;
         mbar_wait(&r.full[slot], use & 1, error);
         const uint8_t *s = r.slots + (size_t)slot * kSlotBytes;
+        __builtin_assume(__isShared(s));
         const uint4 *xf = frag + (size_t)(i % kChunks) * CB * 32;  // two 64-column pieces per block
+        __builtin_assume(__isShared(xf));
         float c[4][4] = {};  // per k16 step j of a block: four independent accumulation chains
 #pragma unroll 4
         for (int b = 0; b < CB; b++) {
@@ -539,21 +561,31 @@ __device__ __forceinline__ void consume_down(const Ring &r, const PhaseSpan &sp,
         const unsigned slot = slot_of(warp, k), use = k / kSlotsPerWarp;
         mbar_wait(&r.full[slot], use & 1, error);
         const uint8_t *s = r.slots + (size_t)slot * kSlotBytes;
-#pragma unroll 4
-        for (int q = 0; q < kDownItemTiles / 2; q++) {
-            const uint4 wa = *reinterpret_cast<const uint4 *>(s + q * 1024 + lane * 16);
-            const uint4 wb = *reinterpret_cast<const uint4 *>(s + q * 1024 + 512 + lane * 16);
-            float c[4][4] = {};
-            mma_block4(c, wa, wb, x0, x1);
-            // lane (g, 0): row g of the pair's first tile (c0 hi + c1 lo) and of its second (c2 + c3)
-            if (t4 == 0) {
-                rows[q * 16 + n] =
-                    ((c[0][0] + c[0][1]) + (c[1][0] + c[1][1]) + ((c[2][0] + c[2][1]) + (c[3][0] + c[3][1]))) *
-                    out_scale;
-                rows[q * 16 + 8 + n] =
-                    ((c[0][2] + c[0][3]) + (c[1][2] + c[1][3]) + ((c[2][2] + c[2][3]) + (c[3][2] + c[3][3]))) *
-                    out_scale;
+        __builtin_assume(__isShared(s));
+        // four pairs (64 rows) at a time: row 16 q + j of a group ends in lane
+        // (16 q + j) % 32, register q / 2, moved there by shuffles, and the group
+        // is stored once (a shared-memory store after every pair would hold the
+        // next pairs' loads behind it)
+#pragma unroll 1
+        for (int q0 = 0; q0 < kDownItemTiles / 2; q0 += 4) {
+            float res[2];
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const uint4 wa = *reinterpret_cast<const uint4 *>(s + (q0 + q) * 1024 + lane * 16);
+                const uint4 wb = *reinterpret_cast<const uint4 *>(s + (q0 + q) * 1024 + 512 + lane * 16);
+                float c[4][4] = {};
+                mma_block4(c, wa, wb, x0, x1);
+                // lane (g, 0): row g of the pair's first tile (c0 hi + c1 lo) and of its second (c2 + c3)
+                const float r0 =
+                    (c[0][0] + c[0][1]) + (c[1][0] + c[1][1]) + ((c[2][0] + c[2][1]) + (c[3][0] + c[3][1]));
+                const float r1 =
+                    (c[0][2] + c[0][3]) + (c[1][2] + c[1][3]) + ((c[2][2] + c[2][3]) + (c[3][2] + c[3][3]));
+                const int src = 4 * (lane & 7);
+                const float v0 = __shfl_sync(0xffffffffu, r0, src), v1 = __shfl_sync(0xffffffffu, r1, src);
+                if ((lane >> 4) == (q & 1)) res[q >> 1] = (lane & 8) ? v1 : v0;
             }
+            rows[q0 * 16 + lane] = res[0] * out_scale;
+            rows[q0 * 16 + 32 + lane] = res[1] * out_scale;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&r.empty[slot]);
