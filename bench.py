@@ -45,7 +45,7 @@ HEAD_BYTES = 131072 * 3072 * 2
 # DRAM read + write bytes of one C0 decode token: ncu capture of a one-token
 # launch of decode_mega_kernel at context 34 (profiles/decode_mega_c0_token.md:
 # 3,839,687,168 read + 7,772,160 written)
-DRAM_BYTES_PER_TOKEN = 3839687168 + 7772160
+DRAM_BYTES_PER_TOKEN = 3854483968 + 8470272
 
 
 def env_int(name, default):
