@@ -304,6 +304,36 @@ def cpu_baseline(checkpoint, prompt, decode_steps=6):
             "prefill_tok_s": len(prompt) / (t1 - t0)}
 
 
+class Ranks:
+    """Rank plumbing of the bench: one process per GPU, replicas only (no
+    data-path collective). `barrier` lines the ranks up around timed regions and
+    `max` takes the slowest rank's time; with no process group (N = 1) both are
+    no-ops. `device` is where the reduction tensor lives ("cuda" under NCCL,
+    "cpu" under gloo in the tests)."""
+
+    def __init__(self, dist=None, device="cpu"):
+        self.dist = dist
+        self.device = device
+
+    def barrier(self):
+        if self.dist is not None:
+            self.dist.barrier()
+
+    def max(self, v):
+        if self.dist is None:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64, device=self.device)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+
+def aggregate_rate(world, units_per_rank, slowest_seconds):
+    """Whole-job throughput: the units every rank processed over the slowest
+    rank's time (weak scaling: per-rank work is fixed)."""
+    return world * units_per_rank / slowest_seconds
+
+
 def run_reference(args, rank, world):
     """The reference's CPU implementation of the path: this repo's oracle port of
     its Metal kernels (the Metal runtime itself cannot run off Apple hardware)."""
@@ -366,17 +396,8 @@ def run_ours(args, rank, world, local_rank):
         import torch.distributed as dist
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local_rank))
-
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-
-    def max_over_ranks(v):
-        if dist is None:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    ranks = Ranks(dist, "cuda")
+    barrier, max_over_ranks = ranks.barrier, ranks.max
 
     lib = L.library()
     checkpoint = ensure_checkpoint(args.checkpoint, rank, world, barrier)
@@ -412,7 +433,7 @@ def run_ours(args, rank, world, local_rank):
         wall_ms = 1000 * (time.perf_counter() - t0)
     barrier()
     device_ms = max_over_ranks(device_ms)
-    value = world * steps / (device_ms / 1000)
+    value = aggregate_rate(world, steps, device_ms / 1000)
 
     # ---- e2e: the drop-in C-ABI with host buffers, host greedy each token
     barrier()
@@ -429,7 +450,7 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     barrier()
-    e2e_value = world * steps / e2e_s
+    e2e_value = aggregate_rate(world, steps, e2e_s)
     # the device loop and the host loop must generate the same greedy tokens
     same_tokens = list(e2e_tokens[1:per_round]) == [int(t) for t in tokens_seen[:per_round - 1]]
 
