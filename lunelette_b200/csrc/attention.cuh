@@ -180,195 +180,250 @@ static __global__ void __launch_bounds__(128) attention_combine_kernel(AttnParam
     p.out[(size_t)t * kQuery + head * kHeadDim + d] = acc / l;
 }
 
-// ---- blocks of query tokens (prefill, append) ------------------------------------
-// One block per (8 query tokens, KV head): the 32 query rows (8 tokens x the
-// 4 query heads of the GQA group, row 4 * token + head) stream the causal K/V
-// range once, a 64-position page at a time, instead of once per token. K and V
-// tiles arrive by cp.async (a page of one head is 32 KB contiguous per kind);
-// the next tile's K loads during this tile's P V and the next V during the
-// next S, so one buffer each suffices. S = Q K^T and O += P V run as 4 x 4 and
-// 4 x 8 register tiles per thread: thread (rg, cg) owns rows 4rg..4rg+3, keys
-// cg + 16j (conflict-free 16-byte reads of the padded K rows) and dims
-// 8cg..8cg+7; the online softmax of a row lives in the 16 threads of a half
-// warp, the same in both phases.
-constexpr int kPfTokens = 8;                    // query tokens per block
-constexpr int kPfRows = 4 * kPfTokens;          // 32 query rows
-constexpr int kPfKeys = kPage;                  // positions per K/V tile (one page)
-constexpr int kPfRowStride = kHeadDim + 4;      // padded Q and K rows (floats)
-constexpr int kPfPStride = kPfRows + 4;         // P^T row
-constexpr int kPfThreads = 128;
-constexpr int kPfSmemFloats =
-    kPfRows * kPfRowStride + kPfKeys * kPfRowStride + kPfKeys * kHeadDim + kPfKeys * kPfPStride;
-constexpr int kPfSmemBytes = kPfSmemFloats * 4;
+// ---- blocks of query tokens (prefill, append) on the tensor cores ----------------------
+// One block per (16 query tokens, KV head) and key range: the 64 query rows
+// (16 tokens x the 4 query heads of the GQA group) stream the causal K/V range
+// once, instead of once per token. Split s covers the keys [s * split_len,
+// (s + 1) * split_len) of the causal range (split_len a multiple of 64); with
+// one split the block writes the output, otherwise (m, l, unnormalised o) per
+// row for attention_combine_kernel. S = Q K^T and O += P V run on
+// mma.sync.m16n8k16 in FP16: every FP32 operand x is split into hi = fp16(x)
+// and lo = fp16(x - hi) (22 significant bits together) and each product takes
+// three MMAs (hi.hi + hi.lo + lo.hi, FP32 accumulation), so S and O keep
+// near-FP32 accuracy. Block: 4 warps x 16 rows (4 query tokens x the 4 query
+// heads of KV head blockIdx.y); keys stream in tiles of 32 (half a page): the
+// FP32 K and V rows are copied (cp.async), converted once per tile into FP16
+// hi/lo parts (K row-major, V transposed, both padded so the fragment loads are
+// conflict-free), and the next tile's copy overlaps this tile's MMAs. The
+// online softmax runs on the S fragments (a row's 32 keys sit in one lane
+// quad) exactly as in the FP32 kernel.
+constexpr int kPmTokens = 16;                                   // query tokens per block
+constexpr int kPmThreads = 128;
+constexpr int kPmKeys = 32;                                     // keys per tile
+constexpr int kPmKStride = kHeadDim + 8;                        // halves per K row
+constexpr int kPmVStride = kPmKeys + 8;                         // halves per V^T row
+constexpr int kPmStageBytes = 2 * kPmKeys * kHeadDim * 4;       // FP32 K and V of a tile
+constexpr int kPmKBytes = kPmKeys * kPmKStride * 2;             // one FP16 part of K
+constexpr int kPmVBytes = kHeadDim * kPmVStride * 2;            // one FP16 part of V^T
+constexpr int kPmSmemBytes = kPmStageBytes + 2 * kPmKBytes + 2 * kPmVBytes;
 
-// Copy rows [0, keys) of a 64 x 128 tile (zero the rest) into rows of `stride` floats.
-__device__ __forceinline__ void pf_issue_tile(float *dst, const float *src, int keys, int stride)
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void split_half2(float a, float b, uint32_t &hi, uint32_t &lo)
 {
-    for (int i = threadIdx.x; i < kPfKeys * (kHeadDim / 4); i += kPfThreads) {
-        const int row = i >> 5, c = i & 31;
-        const bool in = row < keys;
-        cp_async16(dst + row * stride + 4 * c, in ? src + (size_t)row * kHeadDim + 4 * c : src, in);
-    }
-    cp_async_commit();
+    const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+    const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
+    hi = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
+    lo = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
 }
 
-// Grid (ceil(count / 8), 8 KV heads, splits), 128 threads. Split s covers the
-// keys [s * split_len, (s + 1) * split_len) of the causal range (split_len a
-// multiple of 64); with one split the block writes the output, otherwise
-// (m, l, unnormalised o) per row for attention_combine_kernel.
-static __global__ void __launch_bounds__(kPfThreads) attention_prefill_kernel(AttnParams p, int count)
+__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
 {
-    extern __shared__ float4 pf_smem4[];
-    float *qs = reinterpret_cast<float *>(pf_smem4);     // [32][kPfRowStride]
-    float *ks = qs + kPfRows * kPfRowStride;             // [64][kPfRowStride]
-    float *vs = ks + kPfKeys * kPfRowStride;             // [64][128]
-    float *pt = vs + kPfKeys * kHeadDim;                 // [64][kPfPStride]: P^T of the tile
-    const int kvh = blockIdx.y, t0 = blockIdx.x * kPfTokens, tid = threadIdx.x;
-    const int rg = tid >> 4, cg = tid & 15;
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Grid (ceil(count / 16), 8 KV heads, splits), 128 threads, kPmSmemBytes.
+static __global__ void __launch_bounds__(kPmThreads) attention_prefill_mma_kernel(AttnParams p, int count)
+{
+    extern __shared__ __align__(16) uint8_t pm_smem[];
+    float *stage_k = reinterpret_cast<float *>(pm_smem);  // [32][128] FP32
+    float *stage_v = stage_k + kPmKeys * kHeadDim;        // [32][128] FP32
+    __half *kh = reinterpret_cast<__half *>(pm_smem + kPmStageBytes);  // [32][kPmKStride]
+    __half *kl = kh + kPmKeys * kPmKStride;
+    __half *vth = kl + kPmKeys * kPmKStride;  // [128][kPmVStride]: V^T
+    __half *vtl = vth + kHeadDim * kPmVStride;
+    const int kvh = blockIdx.y, t0 = blockIdx.x * kPmTokens, split = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
     pdl_wait();
     pdl_launch_dependents();
     const int length = (p.step ? p.step->length : p.length) + p.token_offset;
-    const int last = min(t0 + kPfTokens, count) - 1;      // last query token of the block
-    const int split = blockIdx.z;
-    const int k0 = split * p.split_len;                   // first key of this split
-    const int total = min(length + last + 1, k0 + p.split_len);  // keys the block needs (end)
-    const int tiles = total > k0 ? (total - k0 + kPfKeys - 1) / kPfKeys : 0;
+    const int last = min(t0 + kPmTokens, count) - 1;  // last query token of the block
+    const int k0 = split * p.split_len;               // first key of this split
+    const int total = min(length + last + 1, k0 + p.split_len);
+    const int tiles = total > k0 ? (total - k0 + kPmKeys - 1) / kPmKeys : 0;
 
-    auto kv_tile = [&](int tile, int kind) {
-        const int page = p.page_table[k0 / kPfKeys + tile];
-        return p.kv + kv_offset(p.layer, p.num_pages, page, kind, kvh, 0);
+    // rows [0, keys) of the 32-key tile at p0 (one page holds it), the rest zero
+    auto issue = [&](int p0) {
+        const int page = p.page_table[p0 / kPage], slot0 = p0 % kPage;
+        const float *kb = p.kv + kv_offset(p.layer, p.num_pages, page, 0, kvh, slot0);
+        const float *vb = p.kv + kv_offset(p.layer, p.num_pages, page, 1, kvh, slot0);
+        const int keys = min(kPmKeys, total - p0);
+#pragma unroll 4
+        for (int i = threadIdx.x; i < kPmKeys * (kHeadDim / 4); i += kPmThreads) {
+            const int row = i >> 5, c = i & 31;
+            const bool in = row < keys;
+            cp_async16(stage_k + row * kHeadDim + 4 * c, in ? kb + row * kHeadDim + 4 * c : kb, in);
+            cp_async16(stage_v + row * kHeadDim + 4 * c, in ? vb + row * kHeadDim + 4 * c : vb, in);
+        }
+        cp_async_commit();
     };
-    if (tiles > 0) {
-        pf_issue_tile(ks, kv_tile(0, 0), min(kPfKeys, total - k0), kPfRowStride);
-        pf_issue_tile(vs, kv_tile(0, 1), min(kPfKeys, total - k0), kHeadDim);
-    }
-    for (int i = tid; i < kPfRows * kHeadDim / 4; i += kPfThreads) {
-        const int r = i >> 5, c = i & 31, tk = r >> 2, hh = r & 3;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (t0 + tk < count)
-            v = *reinterpret_cast<const float4 *>(p.q + (size_t)(t0 + tk) * kQuery + (kvh * 4 + hh) * kHeadDim + 4 * c);
-        *reinterpret_cast<float4 *>(qs + r * kPfRowStride + 4 * c) = v;
-    }
-    // the causal limit of each of this thread's rows: key position <= length + token
-    int limit[4];
+    if (tiles > 0) issue(k0);
+
+    // this warp's rows: r = g (token ta) and g + 8 (token tb), head kvh * 4 + (g & 3)
+    const int head = kvh * 4 + (g & 3);
+    const int ta = t0 + 4 * warp + (g >> 2), tb = ta + 2;
+    const int limit_a = ta < count ? length + ta : -1, limit_b = tb < count ? length + tb : -1;
+    // Q as A fragments, hi and lo, per k16 step of the head dimension
+    uint32_t qh[8][4], ql[8][4];
+    {
+        const float *qa = p.q + (size_t)(ta < count ? ta : 0) * kQuery + head * kHeadDim;
+        const float *qb = p.q + (size_t)(tb < count ? tb : 0) * kQuery + head * kHeadDim;
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int tk = t0 + ((4 * rg + i) >> 2);
-        limit[i] = tk < count ? length + tk : -1;
-    }
-    float m_run[4], l_run[4], o[4][8];
+        for (int ks = 0; ks < 8; ks++) {
+            const int d = 16 * ks + 2 * t4;
+            float2 v[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+            if (ta < count) {
+                v[0] = *reinterpret_cast<const float2 *>(qa + d);
+                v[2] = *reinterpret_cast<const float2 *>(qa + d + 8);
+            }
+            if (tb < count) {
+                v[1] = *reinterpret_cast<const float2 *>(qb + d);
+                v[3] = *reinterpret_cast<const float2 *>(qb + d + 8);
+            }
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        m_run[i] = -INFINITY;
-        l_run[i] = 0.0f;
-#pragma unroll
-        for (int e = 0; e < 8; e++) o[i][e] = 0.0f;
+            for (int r = 0; r < 4; r++) split_half2(v[r].x, v[r].y, qh[ks][r], ql[ks][r]);
+        }
     }
+    float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.0f, l_b = 0.0f;
+    float o[16][4];
+#pragma unroll
+    for (int nb = 0; nb < 16; nb++) o[nb][0] = o[nb][1] = o[nb][2] = o[nb][3] = 0.0f;
+
     for (int tile = 0; tile < tiles; tile++) {
-        const int p0 = k0 + tile * kPfKeys, keys = min(kPfKeys, total - p0);
-        cp_async_wait_one();  // K of this tile (its V may still be in flight)
-        __syncthreads();
-        // S = Q K^T for rows 4rg.., keys p0 + cg + 16j
+        const int p0 = k0 + tile * kPmKeys;
+        cp_async_wait_all();
+        __syncthreads();  // the tile is staged; every warp is done with the last tile's FP16 parts
+        // K: [key][dim] hi/lo; V: transposed [dim][key] hi/lo, two keys per store
+        for (int i = threadIdx.x; i < kPmKeys * (kHeadDim / 4); i += kPmThreads) {
+            const int row = i >> 5, c = i & 31;
+            const float4 k4 = *reinterpret_cast<const float4 *>(stage_k + row * kHeadDim + 4 * c);
+            uint2 hi, lo;
+            split_half2(k4.x, k4.y, hi.x, lo.x);
+            split_half2(k4.z, k4.w, hi.y, lo.y);
+            *reinterpret_cast<uint2 *>(kh + row * kPmKStride + 4 * c) = hi;
+            *reinterpret_cast<uint2 *>(kl + row * kPmKStride + 4 * c) = lo;
+        }
+        for (int i = threadIdx.x; i < (kPmKeys / 2) * kHeadDim; i += kPmThreads) {
+            const int d = i & (kHeadDim - 1), kp = i >> 7;
+            uint32_t hi, lo;
+            split_half2(stage_v[(2 * kp) * kHeadDim + d], stage_v[(2 * kp + 1) * kHeadDim + d], hi, lo);
+            *reinterpret_cast<uint32_t *>(vth + d * kPmVStride + 2 * kp) = hi;
+            *reinterpret_cast<uint32_t *>(vtl + d * kPmVStride + 2 * kp) = lo;
+        }
+        __syncthreads();  // parts ready, staging free
+        if (tile + 1 < tiles) issue(p0 + kPmKeys);
+
+        // S = Q K^T: 4 key blocks of 8 x 8 k16 steps, three MMAs each
         float s[4][4];
 #pragma unroll
-        for (int i = 0; i < 4; i++)
+        for (int nb = 0; nb < 4; nb++) s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.0f;
 #pragma unroll
-            for (int j = 0; j < 4; j++) s[i][j] = 0.0f;
-#pragma unroll 4
-        for (int d = 0; d < kHeadDim; d += 4) {
-            float4 a[4], b[4];
+        for (int ks = 0; ks < 8; ks++) {
 #pragma unroll
-            for (int i = 0; i < 4; i++) a[i] = *reinterpret_cast<const float4 *>(qs + (4 * rg + i) * kPfRowStride + d);
-#pragma unroll
-            for (int j = 0; j < 4; j++) b[j] = *reinterpret_cast<const float4 *>(ks + (cg + 16 * j) * kPfRowStride + d);
-#pragma unroll
-            for (int i = 0; i < 4; i++)
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    s[i][j] = fmaf(a[i].x, b[j].x, s[i][j]);
-                    s[i][j] = fmaf(a[i].y, b[j].y, s[i][j]);
-                    s[i][j] = fmaf(a[i].z, b[j].z, s[i][j]);
-                    s[i][j] = fmaf(a[i].w, b[j].w, s[i][j]);
-                }
-        }
-        __syncthreads();  // K consumed: the next tile's K may load
-        if (tile + 1 < tiles)
-            pf_issue_tile(ks, kv_tile(tile + 1, 0), min(kPfKeys, total - p0 - kPfKeys), kPfRowStride);
-        else
-            cp_async_commit();
-        // online softmax per row over the 16 threads of the half warp
-        float prob[4][4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            float mx = -INFINITY;
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int pos = p0 + cg + 16 * j;
-                s[i][j] = pos <= limit[i] ? s[i][j] * kScoreScale : -INFINITY;
-                mx = fmaxf(mx, s[i][j]);
+            for (int nb = 0; nb < 4; nb++) {
+                const int off = (nb * 8 + g) * kPmKStride + 16 * ks + 2 * t4;
+                const uint32_t bh0 = *reinterpret_cast<const uint32_t *>(kh + off);
+                const uint32_t bh1 = *reinterpret_cast<const uint32_t *>(kh + off + 8);
+                const uint32_t bl0 = *reinterpret_cast<const uint32_t *>(kl + off);
+                const uint32_t bl1 = *reinterpret_cast<const uint32_t *>(kl + off + 8);
+                mma_16816(s[nb], qh[ks], bh0, bh1);
+                mma_16816(s[nb], qh[ks], bl0, bl1);
+                mma_16816(s[nb], ql[ks], bh0, bh1);
             }
+        }
+        // mask, scale, online softmax; lane quad (g, t4 = 0..3) holds rows g / g + 8, keys 8 nb + 2 t4 (+1)
+        float mx_a = -INFINITY, mx_b = -INFINITY;
 #pragma unroll
-            for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-            const float m_new = fmaxf(m_run[i], mx);
-            const float corr = m_run[i] == -INFINITY ? 0.0f : expf(m_run[i] - m_new);
-            float sum = 0.0f;
+        for (int nb = 0; nb < 4; nb++) {
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                prob[i][j] = s[i][j] == -INFINITY ? 0.0f : expf(s[i][j] - m_new);
-                sum += prob[i][j];
+            for (int e = 0; e < 2; e++) {
+                const int pos = p0 + 8 * nb + 2 * t4 + e;
+                s[nb][e] = pos <= limit_a ? s[nb][e] * kScoreScale : -INFINITY;
+                s[nb][2 + e] = pos <= limit_b ? s[nb][2 + e] * kScoreScale : -INFINITY;
+                mx_a = fmaxf(mx_a, s[nb][e]);
+                mx_b = fmaxf(mx_b, s[nb][2 + e]);
             }
-#pragma unroll
-            for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-            l_run[i] = l_run[i] * corr + sum;
-            m_run[i] = m_new;
-#pragma unroll
-            for (int e = 0; e < 8; e++) o[i][e] *= corr;
         }
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+        const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+        const float corr_a = m_a == -INFINITY ? 0.0f : expf(m_a - mn_a);
+        const float corr_b = m_b == -INFINITY ? 0.0f : expf(m_b - mn_b);
+        float sum_a = 0.0f, sum_b = 0.0f;
 #pragma unroll
-        for (int j = 0; j < 4; j++)
-            *reinterpret_cast<float4 *>(pt + (cg + 16 * j) * kPfPStride + 4 * rg) =
-                make_float4(prob[0][j], prob[1][j], prob[2][j], prob[3][j]);
-        cp_async_wait_one();  // V of this tile (the next K may still be in flight)
-        __syncthreads();
-        // O += P V for rows 4rg.., dims 8cg..8cg+7
-#pragma unroll 4
-        for (int j = 0; j < keys; j++) {
-            const float4 pj = *reinterpret_cast<const float4 *>(pt + j * kPfPStride + 4 * rg);
-            const float4 v0 = *reinterpret_cast<const float4 *>(vs + j * kHeadDim + 8 * cg);
-            const float4 v1 = *reinterpret_cast<const float4 *>(vs + j * kHeadDim + 8 * cg + 4);
-            const float pv[4] = {pj.x, pj.y, pj.z, pj.w};
-            const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        for (int nb = 0; nb < 4; nb++) {
 #pragma unroll
-            for (int i = 0; i < 4; i++)
-#pragma unroll
-                for (int e = 0; e < 8; e++) o[i][e] = fmaf(pv[i], vv[e], o[i][e]);
+            for (int e = 0; e < 2; e++) {
+                s[nb][e] = s[nb][e] == -INFINITY ? 0.0f : expf(s[nb][e] - mn_a);
+                s[nb][2 + e] = s[nb][2 + e] == -INFINITY ? 0.0f : expf(s[nb][2 + e] - mn_b);
+                sum_a += s[nb][e];
+                sum_b += s[nb][2 + e];
+            }
         }
-        __syncthreads();  // V and P consumed: the next tile's V may load
-        if (tile + 1 < tiles)
-            pf_issue_tile(vs, kv_tile(tile + 1, 1), min(kPfKeys, total - p0 - kPfKeys), kHeadDim);
-        else
-            cp_async_commit();
+        sum_a += __shfl_xor_sync(0xffffffffu, sum_a, 1);
+        sum_a += __shfl_xor_sync(0xffffffffu, sum_a, 2);
+        sum_b += __shfl_xor_sync(0xffffffffu, sum_b, 1);
+        sum_b += __shfl_xor_sync(0xffffffffu, sum_b, 2);
+        l_a = l_a * corr_a + sum_a;
+        l_b = l_b * corr_b + sum_b;
+        m_a = mn_a;
+        m_b = mn_b;
+#pragma unroll
+        for (int nb = 0; nb < 16; nb++) {
+            o[nb][0] *= corr_a;
+            o[nb][1] *= corr_a;
+            o[nb][2] *= corr_b;
+            o[nb][3] *= corr_b;
+        }
+        // O += P V: P's S fragments are the A fragments of two k16 steps of keys
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            uint32_t ph[4], pl[4];
+            split_half2(s[2 * j][0], s[2 * j][1], ph[0], pl[0]);
+            split_half2(s[2 * j][2], s[2 * j][3], ph[1], pl[1]);
+            split_half2(s[2 * j + 1][0], s[2 * j + 1][1], ph[2], pl[2]);
+            split_half2(s[2 * j + 1][2], s[2 * j + 1][3], ph[3], pl[3]);
+#pragma unroll
+            for (int nb = 0; nb < 16; nb++) {
+                const int off = (nb * 8 + g) * kPmVStride + 16 * j + 2 * t4;
+                const uint32_t bh0 = *reinterpret_cast<const uint32_t *>(vth + off);
+                const uint32_t bh1 = *reinterpret_cast<const uint32_t *>(vth + off + 8);
+                const uint32_t bl0 = *reinterpret_cast<const uint32_t *>(vtl + off);
+                const uint32_t bl1 = *reinterpret_cast<const uint32_t *>(vtl + off + 8);
+                mma_16816(o[nb], ph, bh0, bh1);
+                mma_16816(o[nb], ph, bl0, bl1);
+                mma_16816(o[nb], pl, bh0, bh1);
+            }
+        }
     }
+    // rows g (token ta) and g + 8 (token tb); lane holds dims 8 nb + 2 t4 (+1)
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int r = 4 * rg + i, tk = t0 + (r >> 2), head = kvh * 4 + (r & 3);
+    for (int half = 0; half < 2; half++) {
+        const int tk = half ? tb : ta;
         if (tk >= count) continue;
+        const float l = half ? l_b : l_a, m = half ? m_b : m_a;
         if (p.splits == 1) {
-            const float inv = 1.0f / l_run[i];
-            float *dst = p.out + (size_t)tk * kQuery + head * kHeadDim + 8 * cg;
-            *reinterpret_cast<float4 *>(dst) =
-                make_float4(o[i][0] * inv, o[i][1] * inv, o[i][2] * inv, o[i][3] * inv);
-            *reinterpret_cast<float4 *>(dst + 4) =
-                make_float4(o[i][4] * inv, o[i][5] * inv, o[i][6] * inv, o[i][7] * inv);
+            const float inv = 1.0f / l;
+            float *dst = p.out + (size_t)tk * kQuery + head * kHeadDim + 2 * t4;
+#pragma unroll
+            for (int nb = 0; nb < 16; nb++)
+                *reinterpret_cast<float2 *>(dst + 8 * nb) =
+                    make_float2(o[nb][2 * half] * inv, o[nb][2 * half + 1] * inv);
         } else {
             // a split past this token's causal range leaves l = 0 (the combine skips it)
             const size_t slot = ((size_t)tk * kQueryHeads + head) * p.splits + split;
-            float *dst = p.part_acc + slot * kHeadDim + 8 * cg;
-            *reinterpret_cast<float4 *>(dst) = make_float4(o[i][0], o[i][1], o[i][2], o[i][3]);
-            *reinterpret_cast<float4 *>(dst + 4) = make_float4(o[i][4], o[i][5], o[i][6], o[i][7]);
-            if (cg == 0) {
-                p.part_ml[slot * 2] = m_run[i];
-                p.part_ml[slot * 2 + 1] = l_run[i];
+            float *dst = p.part_acc + slot * kHeadDim + 2 * t4;
+#pragma unroll
+            for (int nb = 0; nb < 16; nb++)
+                *reinterpret_cast<float2 *>(dst + 8 * nb) = make_float2(o[nb][2 * half], o[nb][2 * half + 1]);
+            if (t4 == 0) {
+                p.part_ml[slot * 2] = m;
+                p.part_ml[slot * 2 + 1] = l;
             }
         }
     }

@@ -203,8 +203,8 @@ cudaError_t lun_kernels_init()
     if ((e = cudaFuncSetAttribute(attention_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   kAttnSmemBytes)) != cudaSuccess)
         return e;
-    if ((e = cudaFuncSetAttribute(attention_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  kPfSmemBytes)) != cudaSuccess)
+    if ((e = cudaFuncSetAttribute(attention_prefill_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  kPmSmemBytes)) != cudaSuccess)
         return e;
     if ((e = setup_epi<kEpiStore>()) != cudaSuccess) return e;
     if ((e = setup_epi<kEpiResidual>()) != cudaSuccess) return e;
@@ -260,9 +260,9 @@ constexpr int kAttnMaxSplit = 512;
 void lun_attention_plan(AttnParams *a, int total, int count, int sm_count, int slots)
 {
     if (count > kGemvMaxTokens && !a->positions) {
-        // blocks of one sequence's tokens (attention_prefill_kernel): key
+        // blocks of one sequence's tokens (attention_prefill_mma_kernel): key
         // ranges of whole pages split so that about two waves of blocks run
-        const int qtiles = (count + kPfTokens - 1) / kPfTokens;
+        const int qtiles = (count + kPmTokens - 1) / kPmTokens;
         const int pages = (total + kPage - 1) / kPage;
         int splits = (4 * sm_count + qtiles * kKVHeads - 1) / (qtiles * kKVHeads);
         const int cap = slots / (count * kQueryHeads);
@@ -301,8 +301,8 @@ cudaError_t lun_launch_attention(const AttnParams &a, int count, cudaStream_t st
     if (e != cudaSuccess) return e;
     if (count > kGemvMaxTokens && !a.positions) {  // blocks of one sequence's tokens: key pages per 8 query tokens
         if (a.splits < 1 || a.split_len < kPage || (a.split_len % kPage)) return cudaErrorInvalidValue;
-        e = launch(attention_prefill_kernel, dim3((count + kPfTokens - 1) / kPfTokens, kKVHeads, a.splits),
-                   dim3(kPfThreads), kPfSmemBytes, stream, a, count);
+        e = launch(attention_prefill_mma_kernel, dim3((count + kPmTokens - 1) / kPmTokens, kKVHeads, a.splits),
+                   dim3(kPmThreads), kPmSmemBytes, stream, a, count);
         if (e != cudaSuccess || a.splits == 1) return e;
         return launch(attention_combine_kernel, dim3(kQueryHeads, count), dim3(128), 0, stream, a);
     }
