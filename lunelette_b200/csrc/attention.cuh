@@ -181,8 +181,8 @@ static __global__ void __launch_bounds__(128) attention_combine_kernel(AttnParam
 }
 
 // ---- blocks of query tokens (prefill, append) on the tensor cores ----------------------
-// One block per (16 query tokens, KV head) and key range: the 64 query rows
-// (16 tokens x the 4 query heads of the GQA group) stream the causal K/V range
+// One block per (32 query tokens, KV head) and key range: the 128 query rows
+// (32 tokens x the 4 query heads of the GQA group) stream the causal K/V range
 // once, instead of once per token. Split s covers the keys [s * split_len,
 // (s + 1) * split_len) of the causal range (split_len a multiple of 64); with
 // one split the block writes the output, otherwise (m, l, unnormalised o) per
@@ -190,15 +190,17 @@ static __global__ void __launch_bounds__(128) attention_combine_kernel(AttnParam
 // mma.sync.m16n8k16 in FP16: every FP32 operand x is split into hi = fp16(x)
 // and lo = fp16(x - hi) (22 significant bits together) and each product takes
 // three MMAs (hi.hi + hi.lo + lo.hi, FP32 accumulation), so S and O keep
-// near-FP32 accuracy. Block: 4 warps x 16 rows (4 query tokens x the 4 query
+// near-FP32 accuracy. Block: 8 warps x 16 rows (4 query tokens x the 4 query
 // heads of KV head blockIdx.y); keys stream in tiles of 32 (half a page): the
 // FP32 K and V rows are copied (cp.async), converted once per tile into FP16
 // hi/lo parts (K row-major, V transposed, both padded so the fragment loads are
-// conflict-free), and the next tile's copy overlaps this tile's MMAs. The
-// online softmax runs on the S fragments (a row's 32 keys sit in one lane
-// quad) exactly as in the FP32 kernel.
-constexpr int kPmTokens = 16;                                   // query tokens per block
-constexpr int kPmThreads = 128;
+// conflict-free) shared by the block's 8 warps, and the next tile's copy
+// overlaps this tile's MMAs. The online softmax (running max, rescaled sum
+// and output, exp of the scaled scores) runs on the S fragments: a row's 32
+// keys sit in one lane quad.
+constexpr int kPmWarps = 8;                                     // 16 rows (4 tokens x 4 heads) each
+constexpr int kPmTokens = 4 * kPmWarps;                         // query tokens per block
+constexpr int kPmThreads = 32 * kPmWarps;
 constexpr int kPmKeys = 32;                                     // keys per tile
 constexpr int kPmKStride = kHeadDim + 8;                        // halves per K row
 constexpr int kPmVStride = kPmKeys + 8;                         // halves per V^T row
@@ -209,12 +211,14 @@ constexpr int kPmSmemBytes = kPmStageBytes + 2 * kPmKBytes + 2 * kPmVBytes;
 
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
+// (a, b) -> FP16x2 hi = round(a, b) and lo = round(a - hi, b - hi): packed conversions
 __device__ __forceinline__ void split_half2(float a, float b, uint32_t &hi, uint32_t &lo)
 {
-    const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
-    const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
-    hi = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
-    lo = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 back = __half22float2(h);
+    const __half2 l = __floats2half2_rn(a - back.x, b - back.y);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
 }
 
 __device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
@@ -225,7 +229,7 @@ __device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4],
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// Grid (ceil(count / 16), 8 KV heads, splits), 128 threads, kPmSmemBytes.
+// Grid (ceil(count / 32), 8 KV heads, splits), 256 threads, kPmSmemBytes.
 static __global__ void __launch_bounds__(kPmThreads) attention_prefill_mma_kernel(AttnParams p, int count)
 {
     extern __shared__ __align__(16) uint8_t pm_smem[];
@@ -316,23 +320,28 @@ static __global__ void __launch_bounds__(kPmThreads) attention_prefill_mma_kerne
         __syncthreads();  // parts ready, staging free
         if (tile + 1 < tiles) issue(p0 + kPmKeys);
 
-        // S = Q K^T: 4 key blocks of 8 x 8 k16 steps, three MMAs each
+        // S = Q K^T: 4 key blocks of 8 x 8 k16 steps, three MMAs each; the
+        // blocks interleave so consecutive MMAs never feed one another
         float s[4][4];
 #pragma unroll
         for (int nb = 0; nb < 4; nb++) s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.0f;
 #pragma unroll
         for (int ks = 0; ks < 8; ks++) {
+            uint32_t bh[4][2], bl[4][2];
 #pragma unroll
             for (int nb = 0; nb < 4; nb++) {
                 const int off = (nb * 8 + g) * kPmKStride + 16 * ks + 2 * t4;
-                const uint32_t bh0 = *reinterpret_cast<const uint32_t *>(kh + off);
-                const uint32_t bh1 = *reinterpret_cast<const uint32_t *>(kh + off + 8);
-                const uint32_t bl0 = *reinterpret_cast<const uint32_t *>(kl + off);
-                const uint32_t bl1 = *reinterpret_cast<const uint32_t *>(kl + off + 8);
-                mma_16816(s[nb], qh[ks], bh0, bh1);
-                mma_16816(s[nb], qh[ks], bl0, bl1);
-                mma_16816(s[nb], ql[ks], bh0, bh1);
+                bh[nb][0] = *reinterpret_cast<const uint32_t *>(kh + off);
+                bh[nb][1] = *reinterpret_cast<const uint32_t *>(kh + off + 8);
+                bl[nb][0] = *reinterpret_cast<const uint32_t *>(kl + off);
+                bl[nb][1] = *reinterpret_cast<const uint32_t *>(kl + off + 8);
             }
+#pragma unroll
+            for (int nb = 0; nb < 4; nb++) mma_16816(s[nb], qh[ks], bh[nb][0], bh[nb][1]);
+#pragma unroll
+            for (int nb = 0; nb < 4; nb++) mma_16816(s[nb], qh[ks], bl[nb][0], bl[nb][1]);
+#pragma unroll
+            for (int nb = 0; nb < 4; nb++) mma_16816(s[nb], ql[ks], bh[nb][0], bh[nb][1]);
         }
         // mask, scale, online softmax; lane quad (g, t4 = 0..3) holds rows g / g + 8, keys 8 nb + 2 t4 (+1)
         float mx_a = -INFINITY, mx_b = -INFINITY;
@@ -389,15 +398,22 @@ static __global__ void __launch_bounds__(kPmThreads) attention_prefill_mma_kerne
             split_half2(s[2 * j + 1][0], s[2 * j + 1][1], ph[2], pl[2]);
             split_half2(s[2 * j + 1][2], s[2 * j + 1][3], ph[3], pl[3]);
 #pragma unroll
-            for (int nb = 0; nb < 16; nb++) {
-                const int off = (nb * 8 + g) * kPmVStride + 16 * j + 2 * t4;
-                const uint32_t bh0 = *reinterpret_cast<const uint32_t *>(vth + off);
-                const uint32_t bh1 = *reinterpret_cast<const uint32_t *>(vth + off + 8);
-                const uint32_t bl0 = *reinterpret_cast<const uint32_t *>(vtl + off);
-                const uint32_t bl1 = *reinterpret_cast<const uint32_t *>(vtl + off + 8);
-                mma_16816(o[nb], ph, bh0, bh1);
-                mma_16816(o[nb], ph, bl0, bl1);
-                mma_16816(o[nb], pl, bh0, bh1);
+            for (int n0 = 0; n0 < 16; n0 += 4) {
+                uint32_t bh[4][2], bl[4][2];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int off = ((n0 + u) * 8 + g) * kPmVStride + 16 * j + 2 * t4;
+                    bh[u][0] = *reinterpret_cast<const uint32_t *>(vth + off);
+                    bh[u][1] = *reinterpret_cast<const uint32_t *>(vth + off + 8);
+                    bl[u][0] = *reinterpret_cast<const uint32_t *>(vtl + off);
+                    bl[u][1] = *reinterpret_cast<const uint32_t *>(vtl + off + 8);
+                }
+#pragma unroll
+                for (int u = 0; u < 4; u++) mma_16816(o[n0 + u], ph, bh[u][0], bh[u][1]);
+#pragma unroll
+                for (int u = 0; u < 4; u++) mma_16816(o[n0 + u], ph, bl[u][0], bl[u][1]);
+#pragma unroll
+                for (int u = 0; u < 4; u++) mma_16816(o[n0 + u], pl, bh[u][0], bh[u][1]);
             }
         }
     }

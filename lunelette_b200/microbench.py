@@ -222,19 +222,28 @@ def prefill_gemm(counts, iters):
 
 def prefill_tokens(checkpoint, count):
     """A profiling target: prefill `count` seeded ids once (warm-up), then again
-    between cudaProfilerStart and cudaProfilerStop (ncu --profile-from-start off)."""
+    between cudaProfilerStart and cudaProfilerStop (ncu --profile-from-start off).
+    Prompts longer than 256 ids go in 256-id chunks (prefill, then appends) at a
+    context of the prompt plus one chunk, as in config 2."""
     import torch
     import lunelette_b200 as L
     if not os.path.exists(checkpoint):
         L.synth_checkpoint(checkpoint, 0)
-    with L.Runtime(checkpoint) as rt:
+    context = 256 if count <= 256 else (count + 63) // 64 * 64 + 256
+    with L.Runtime(checkpoint, limits=(context, 256)) as rt:
         ids = np.random.default_rng(3).integers(1000, 131072, count).astype(np.int64)
-        rt.reset()
-        rt.prefill(ids)
+
+        def run():
+            rt.reset()
+            logits = rt.prefill(ids[:256])
+            for c in range(256, count, 256):
+                logits = rt.append(ids[c:c + 256])
+            return logits
+
+        run()
         torch.cuda.synchronize()
         torch.cuda.profiler.start()
-        rt.reset()
-        tok = int(np.argmax(rt.prefill(ids)))
+        tok = int(np.argmax(run()))
         torch.cuda.synchronize()
         torch.cuda.profiler.stop()
     return tok
