@@ -40,8 +40,8 @@ struct AttnParams {
 constexpr int kTile = 32;
 constexpr int kKPad = 132;  // padded K row (floats): conflict-free 16-byte reads across lanes
 constexpr int kStageFloats = kTile * kKPad + kTile * kHeadDim;
-// dynamic shared memory: q for 4 heads + two K/V tile stages
-constexpr int kAttnSmemBytes = (4 * kHeadDim + 2 * kStageFloats) * 4;
+// dynamic shared memory: the warps' merge area (4 x 4 x 128 o + 32 m/l) + two K/V tile stages
+constexpr int kAttnSmemBytes = (4 * 4 * kHeadDim + 32 + 2 * kStageFloats) * 4;
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool full)
 {
@@ -80,11 +80,10 @@ static __global__ void __launch_bounds__(128) attention_split_kernel(AttnParams 
 {
     extern __shared__ float4 attn_smem4[];
     float *sm = reinterpret_cast<float *>(attn_smem4);
-    float *qs = sm;  // [4][128]
-    float *stages = sm + 4 * kHeadDim;
+    float *merge = sm;                     // [4 warps][4 heads][128] partial o, then [4][4][2] (m, l)
+    float *stages = sm + 4 * kHeadDim * 4 + 32;
     const int split = blockIdx.x, kvh = blockIdx.y, t = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int head = kvh * 4 + warp;
     pdl_wait();  // q and the newest K/V rows come from the previous kernel
     pdl_launch_dependents();
     const int total = p.positions ? p.positions[t] + 1
@@ -95,11 +94,16 @@ static __global__ void __launch_bounds__(128) attention_split_kernel(AttnParams 
     const int tiles = end > begin ? (end - begin + kTile - 1) / kTile : 0;
     if (tiles > 0) attention_issue_tile(p, table, stages, kvh, begin, end);
 
-    for (int i = threadIdx.x; i < 4 * kHeadDim; i += blockDim.x)
-        qs[i] = p.q[(size_t)t * kQuery + kvh * 4 * kHeadDim + i];
-
-    float m_run = -INFINITY, l_run = 0.0f;
-    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    // every warp holds the four query heads of the group, lane l owning dims 4l..4l+3;
+    // warp w takes positions 8w..8w+7 of each tile, so K and V are read once per block
+    float4 q[4];
+#pragma unroll
+    for (int h = 0; h < 4; h++)
+        q[h] = *reinterpret_cast<const float4 *>(p.q + (size_t)t * kQuery + (kvh * 4 + h) * kHeadDim + 4 * lane);
+    float m_run = -INFINITY, l_run = 0.0f;  // of head lane & 3, over this warp's positions
+    float4 o[4];
+#pragma unroll
+    for (int h = 0; h < 4; h++) o[h] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int it = 0; it < tiles; it++) {
         const int p0 = begin + it * kTile;
         if (it + 1 < tiles)
@@ -109,50 +113,105 @@ static __global__ void __launch_bounds__(128) attention_split_kernel(AttnParams 
         __syncthreads();
         const float *ks = stages + (it & 1) * kStageFloats;
         const float *vs = ks + kTile * kKPad;
-        // scores: lane -> position p0 + lane
-        float s = -INFINITY;
-        if (p0 + lane < end) {
-            float dot = 0.0f;
+        // partial dots of (position j, head h) over this lane's dims, index 4 j + h
+        float d[32];
 #pragma unroll
-            for (int c = 0; c < 32; c++) {
-                float4 kk = *reinterpret_cast<const float4 *>(ks + lane * kKPad + c * 4);
-                float4 qa = *reinterpret_cast<const float4 *>(qs + warp * kHeadDim + c * 4);
-                dot = fmaf(qa.x, kk.x, dot);
-                dot = fmaf(qa.y, kk.y, dot);
-                dot = fmaf(qa.z, kk.z, dot);
-                dot = fmaf(qa.w, kk.w, dot);
-            }
-            s = dot * kScoreScale;
+        for (int j = 0; j < 8; j++) {
+            const float4 k4 = *reinterpret_cast<const float4 *>(ks + (8 * warp + j) * kKPad + 4 * lane);
+#pragma unroll
+            for (int h = 0; h < 4; h++)
+                d[4 * j + h] = fmaf(q[h].x, k4.x, fmaf(q[h].y, k4.y, fmaf(q[h].z, k4.z, q[h].w * k4.w)));
         }
-        float m_new = fmaxf(m_run, warp_max(s));
-        float correction = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
-        float prob = s == -INFINITY ? 0.0f : expf(s - m_new);
-        l_run = l_run * correction + warp_sum(prob);
-        m_run = m_new;
+        // reduce-scatter over the warp: lane l ends with the full dot of index l
 #pragma unroll
-        for (int d = 0; d < 4; d++) o[d] *= correction;
-        const int rows = min(kTile, end - p0);
-        for (int j = 0; j < rows; j++) {
-            float pj = __shfl_sync(0xffffffffu, prob, j);
-            float4 vv = *reinterpret_cast<const float4 *>(vs + j * kHeadDim + lane * 4);
-            o[0] = fmaf(pj, vv.x, o[0]);
-            o[1] = fmaf(pj, vv.y, o[1]);
-            o[2] = fmaf(pj, vv.z, o[2]);
-            o[3] = fmaf(pj, vv.w, o[3]);
+        for (int width = 16; width >= 1; width >>= 1) {
+            const bool upper = (lane & width) != 0;
+#pragma unroll
+            for (int i = 0; i < width; i++) {
+                const float mine = upper ? d[i + width] : d[i];
+                const float other = upper ? d[i] : d[i + width];
+                d[i] = mine + __shfl_xor_sync(0xffffffffu, other, width);
+            }
+        }
+        // lane l: position p0 + 8 warp + (l >> 2), head l & 3
+        const int pos = p0 + 8 * warp + (lane >> 2);
+        const float sc = pos < end ? d[0] * kScoreScale : -INFINITY;
+        float tmax = sc;
+        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
+        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
+        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
+        const float m_new = fmaxf(m_run, tmax);
+        const float corr = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
+        const float prob = sc == -INFINITY ? 0.0f : expf(sc - m_new);
+        float psum = prob;
+        psum += __shfl_xor_sync(0xffffffffu, psum, 4);
+        psum += __shfl_xor_sync(0xffffffffu, psum, 8);
+        psum += __shfl_xor_sync(0xffffffffu, psum, 16);
+        l_run = l_run * corr + psum;
+        m_run = m_new;
+        // O += P V for this warp's positions; head h's factors sit in lanes h, h + 4, ...
+#pragma unroll
+        for (int h = 0; h < 4; h++) {
+            const float c = __shfl_sync(0xffffffffu, corr, h);
+            o[h].x *= c;
+            o[h].y *= c;
+            o[h].z *= c;
+            o[h].w *= c;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const float4 v4 = *reinterpret_cast<const float4 *>(vs + (8 * warp + j) * kHeadDim + 4 * lane);
+#pragma unroll
+            for (int h = 0; h < 4; h++) {
+                const float pj = __shfl_sync(0xffffffffu, prob, 4 * j + h);
+                o[h].x = fmaf(pj, v4.x, o[h].x);
+                o[h].y = fmaf(pj, v4.y, o[h].y);
+                o[h].z = fmaf(pj, v4.z, o[h].z);
+                o[h].w = fmaf(pj, v4.w, o[h].w);
+            }
         }
         __syncthreads();  // this stage is refilled two iterations later
     }
+    // merge the four warps' (m, l, o) per head in warp order; warp h writes head h
+    float *ml = merge + 4 * 4 * kHeadDim;
+#pragma unroll
+    for (int h = 0; h < 4; h++)
+        *reinterpret_cast<float4 *>(merge + (warp * 4 + h) * kHeadDim + 4 * lane) = o[h];
+    if (lane < 4) {
+        ml[(warp * 4 + lane) * 2] = m_run;
+        ml[(warp * 4 + lane) * 2 + 1] = l_run;
+    }
+    __syncthreads();
+    const int h = warp, head = kvh * 4 + h;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; w++)
+        if (ml[(w * 4 + h) * 2 + 1] > 0.0f) M = fmaxf(M, ml[(w * 4 + h) * 2]);
+    float L = 0.0f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < 4; w++) {
+        const float lw = ml[(w * 4 + h) * 2 + 1];
+        if (!(lw > 0.0f)) continue;
+        const float wt = expf(ml[(w * 4 + h) * 2] - M);
+        const float4 v = *reinterpret_cast<const float4 *>(merge + (w * 4 + h) * kHeadDim + 4 * lane);
+        L = fmaf(wt, lw, L);
+        acc.x = fmaf(wt, v.x, acc.x);
+        acc.y = fmaf(wt, v.y, acc.y);
+        acc.z = fmaf(wt, v.z, acc.z);
+        acc.w = fmaf(wt, v.w, acc.w);
+    }
     if (p.splits == 1) {
-        float inv = 1.0f / l_run;
-        float4 r = make_float4(o[0] * inv, o[1] * inv, o[2] * inv, o[3] * inv);
-        *reinterpret_cast<float4 *>(&p.out[(size_t)t * kQuery + head * kHeadDim + lane * 4]) = r;
+        const float inv = 1.0f / L;
+        *reinterpret_cast<float4 *>(&p.out[(size_t)t * kQuery + head * kHeadDim + lane * 4]) =
+            make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
     } else {
+        // an empty split leaves l = 0 and m = -inf (the combine skips it)
         size_t slot = ((size_t)t * kQueryHeads + head) * p.splits + split;
-        *reinterpret_cast<float4 *>(&p.part_acc[slot * kHeadDim + lane * 4]) =
-            make_float4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<float4 *>(&p.part_acc[slot * kHeadDim + lane * 4]) = acc;
         if (lane == 0) {
-            p.part_ml[slot * 2] = m_run;
-            p.part_ml[slot * 2 + 1] = l_run;
+            p.part_ml[slot * 2] = M;
+            p.part_ml[slot * 2 + 1] = L;
         }
     }
 }
