@@ -82,6 +82,7 @@ struct lun_device {
     int *session_tables = nullptr;      // [max_sessions][session_pages] page ids
     int *d_meta = nullptr, *h_meta = nullptr;  // [block] positions, then [block] session of each token
     float *batch_logits = nullptr;      // [block][vocab]
+    uint16_t *head_stage = nullptr;     // B operand staging of the batched head (lun_launch_head_mma)
     int *d_next = nullptr, *h_next = nullptr;
 };
 
@@ -293,6 +294,7 @@ extern "C" lun_device *lun_device_create_batch(size_t pool_pages, size_t session
             cudaSuccess ||
         (e = dalloc(&d->d_meta, 2 * block * sizeof(int), sc)) != cudaSuccess || !d->pf.ws ||
         (e = dalloc(&d->batch_logits, block * (size_t)kVocab * sizeof(float), sc)) != cudaSuccess ||
+        (e = dalloc(&d->head_stage, lun_head_mma_stage_bytes(), sc)) != cudaSuccess ||
         (e = dalloc(&d->d_next, block * sizeof(int), sc)) != cudaSuccess ||
         (e = cudaMallocHost((void **)&d->h_meta, 2 * block * sizeof(int))) != cudaSuccess ||
         (e = cudaMallocHost((void **)&d->h_next, block * sizeof(int))) != cudaSuccess) {
@@ -352,6 +354,7 @@ extern "C" void lun_device_destroy(lun_device *d)
     cudaFree(d->session_tables);
     cudaFree(d->d_meta);
     cudaFree(d->batch_logits);
+    cudaFree(d->head_stage);
     cudaFree(d->d_next);
     cudaFreeHost(d->h_meta);
     cudaFreeHost(d->h_next);
@@ -1014,20 +1017,19 @@ extern "C" int lun_device_batch_decode(lun_device *d, const int *sessions, const
             (e = run_projection(d, layer, 3, count, true)) != cudaSuccess)
             return fail(error, capacity, what, e);
     }
-    for (int t0 = 0; t0 < count; t0 += kHeadRows) {
-        HeadRowsParams hp;
+    for (int t0 = 0; t0 < count; t0 += lun_head_mma_tokens()) {
+        HeadMmaParams hp;
         hp.W = d->embedding;
         hp.rows = kVocab;
-        hp.cols = kHidden;
         hp.x = d->x + (size_t)t0 * kHidden;
         hp.x_stride = kHidden;
-        hp.count = count - t0 < kHeadRows ? count - t0 : kHeadRows;
+        hp.count = count - t0 < lun_head_mma_tokens() ? count - t0 : lun_head_mma_tokens();
         hp.gain = d->final_norm;
+        hp.xb = d->head_stage;
         hp.logits = d->batch_logits + (size_t)t0 * kVocab;
         hp.logits_stride = kVocab;
         hp.nonfinite = d->d_flag;
-        if ((e = lun_launch_head_rows(hp, d->sm_count, d->stream)) != cudaSuccess)
-            return fail(error, capacity, what, e);
+        if ((e = lun_launch_head_mma(hp, d->stream)) != cudaSuccess) return fail(error, capacity, what, e);
     }
     if ((e = lun_launch_argmax_rows(d->batch_logits, kVocab, kVocab, count, d->d_next, d->stream)) != cudaSuccess)
         return fail(error, capacity, what, e);

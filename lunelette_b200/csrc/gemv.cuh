@@ -554,97 +554,18 @@ static __global__ void __launch_bounds__(256) head_bf16_kernel(HeadParams p)
 }
 
 // ---- tied head over several token rows (batched decode) -----------------------------
-// logits[r][v] = E[v] . rmsnorm(x[r]) for r < count <= kHeadRows: every weight
-// row is read once per launch for all the rows, which sit normed in shared
-// memory (kHeadRows x cols floats, the per-row layout of head_bf16_kernel).
-constexpr int kHeadRows = 16;
-struct HeadRowsParams {
-    const uint16_t *W;
-    int rows, cols;
+// Parameters of the tensor-core head of head_mma.cuh: logits[r][v] =
+// E[v] . rmsnorm(x[r]) for r < count (at most 64 rows per launch pair).
+struct HeadMmaParams {
+    const uint16_t *W;     // BF16 [rows][3072]
+    int rows;
     const float *x;        // [count][x_stride] hidden rows
-    int x_stride, count;
+    int x_stride, count;   // count <= kHmTokens
     const float *gain;
+    uint16_t *xb;          // kHmStageElems staged B operand
     float *logits;         // [count][logits_stride]
     int logits_stride;
     int *nonfinite;
 };
-
-static __global__ void __launch_bounds__(256) head_rows_kernel(HeadRowsParams p)
-{
-    extern __shared__ float4 xr4[];
-    __shared__ float red[32];
-    const int cols = p.cols, NQ = cols >> 3;
-    pdl_wait();
-    pdl_launch_dependents();
-    for (int r = 0; r < kHeadRows; r++) {
-        float *xf = reinterpret_cast<float *>(xr4) + (size_t)r * cols;
-        if (r >= p.count) {
-            for (int c = threadIdx.x; c < cols; c += blockDim.x) xf[c] = 0.0f;
-            continue;
-        }
-        const float *x = p.x + (size_t)r * p.x_stride;
-        float ss = 0.0f;
-        for (int c = threadIdx.x; c < cols; c += blockDim.x) ss += x[c] * x[c];
-        ss = block_sum(ss, red);
-        const float rs = rsqrtf(ss / (float)cols + kNormEps);
-        for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-            const int q = c >> 3, piece = (c >> 2) & 1, e = c & 3;
-            xf[((size_t)piece * NQ + q) * 4 + e] = p.gain[c] * (x[c] * rs);
-        }
-    }
-    __syncthreads();
-    const int lane = threadIdx.x & 31;
-    const int groups = (p.rows + 3) >> 2;
-    const int warps = gridDim.x * (blockDim.x >> 5);
-    int bad = 0;
-    for (int g = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); g < groups; g += warps) {
-        const uint16_t *wr[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int r = g * 4 + i;
-            wr[i] = p.W + (size_t)(r < p.rows ? r : p.rows - 1) * cols;
-        }
-        float acc[4][kHeadRows];
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-#pragma unroll
-            for (int t = 0; t < kHeadRows; t++) acc[i][t] = 0.0f;
-        for (int q = lane; q < NQ; q += 32) {
-            uint4 w[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) w[i] = ld_stream(wr[i] + (size_t)q * 8);
-#pragma unroll
-            for (int t = 0; t < kHeadRows; t++) {
-                const float4 x0 = xr4[(size_t)t * (cols >> 2) + q], x1 = xr4[(size_t)t * (cols >> 2) + NQ + q];
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    float a = acc[i][t];
-                    a = fmaf(bf16_lo(w[i].x), x0.x, a);
-                    a = fmaf(bf16_hi(w[i].x), x0.y, a);
-                    a = fmaf(bf16_lo(w[i].y), x0.z, a);
-                    a = fmaf(bf16_hi(w[i].y), x0.w, a);
-                    a = fmaf(bf16_lo(w[i].z), x1.x, a);
-                    a = fmaf(bf16_hi(w[i].z), x1.y, a);
-                    a = fmaf(bf16_lo(w[i].w), x1.z, a);
-                    a = fmaf(bf16_hi(w[i].w), x1.w, a);
-                    acc[i][t] = a;
-                }
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int r = g * 4 + i;
-#pragma unroll
-            for (int t = 0; t < kHeadRows; t++) {
-                const float v = warp_sum(acc[i][t]);
-                if (lane == t && r < p.rows && t < p.count) {
-                    p.logits[(size_t)t * p.logits_stride + r] = v;
-                    if (!isfinite(v)) bad = 1;
-                }
-            }
-        }
-    }
-    if (bad) atomicOr(p.nonfinite, 1);
-}
 
 }  // namespace lun

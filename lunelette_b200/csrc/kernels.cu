@@ -1,4 +1,5 @@
 #include "kernels.h"
+#include "head_mma.cuh"
 
 #include <stdlib.h>
 
@@ -347,29 +348,17 @@ cudaError_t lun_launch_kv_copy(const KvCopyParams &p, int layers, cudaStream_t s
     return cudaGetLastError();
 }
 
-cudaError_t lun_launch_head_rows(const HeadRowsParams &p, int sm_count, cudaStream_t stream)
+cudaError_t lun_launch_head_mma(const HeadMmaParams &p, cudaStream_t stream)
 {
-    if (p.cols <= 0 || (p.cols & 7) || p.count < 1 || p.count > kHeadRows) return cudaErrorInvalidValue;
-    const size_t smem = (size_t)kHeadRows * p.cols * 4;
-    static bool attr[128] = {};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    if (p.count < 1 || p.count > kHmTokens || p.rows < kHmRows || (p.rows % kHmRows) || !p.xb)
+        return cudaErrorInvalidValue;
+    cudaError_t e = launch(head_mma_split_kernel, dim3(kHmTokens), dim3(256), 0, stream, p);
     if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 128 && !attr[dev]) {
-        if ((e = cudaFuncSetAttribute(head_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) !=
-            cudaSuccess)
-            return e;
-        attr[dev] = true;
-    }
-    int per_sm = 0;
-    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, head_rows_kernel, 256, smem)) != cudaSuccess)
-        return e;
-    if (per_sm < 1) per_sm = 1;
-    const int groups = (p.rows + 3) / 4;
-    int blocks = (groups + 7) / 8;
-    if (blocks > sm_count * per_sm) blocks = sm_count * per_sm;
-    return launch(head_rows_kernel, dim3(blocks), dim3(256), smem, stream, p);
+    return launch(head_mma_kernel, dim3(p.rows / kHmRows), dim3(kHmThreads), kHmSmemBytes, stream, p);
 }
+
+size_t lun_head_mma_stage_bytes() { return kHmStageElems * sizeof(uint16_t); }
+int lun_head_mma_tokens() { return kHmTokens; }
 
 // out[t] = argmax of logits row t (strict '>', lowest id on ties:
 // src/generation.c:8-34); one block of 1024 threads per row.

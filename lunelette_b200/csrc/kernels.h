@@ -20,8 +20,11 @@ constexpr int kGemvMaxTokens = 4;
 cudaError_t lun_launch_gemv(const lun::GemvParams &p, int m, int epilogue, int sm_count,
                             cudaStream_t stream);
 cudaError_t lun_launch_head(const lun::HeadParams &p, int sm_count, cudaStream_t stream);
-// Tied head over 1..kHeadRows token rows (batched decode).
-cudaError_t lun_launch_head_rows(const lun::HeadRowsParams &p, int sm_count, cudaStream_t stream);
+// Batched tied head on the tensor cores (head_mma.cuh): up to lun_head_mma_tokens()
+// tokens per launch pair; p.xb holds lun_head_mma_stage_bytes() of staging.
+cudaError_t lun_launch_head_mma(const lun::HeadMmaParams &p, cudaStream_t stream);
+size_t lun_head_mma_stage_bytes();
+int lun_head_mma_tokens();
 // Greedy id of each of `rows` logits rows (stride floats apart).
 cudaError_t lun_launch_argmax_rows(const float *logits, int n, int stride, int rows, int *out, cudaStream_t stream);
 
