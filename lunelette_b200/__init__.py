@@ -167,6 +167,8 @@ class Runtime:
         if not self.handle:
             raise LuneletteError(err.value.decode())
         self._logits = ctypes.c_void_p()
+        self._err = _error()
+        self._view = None  # (address, array) of the last borrowed logits
 
     def close(self):
         if getattr(self, "handle", None):
@@ -180,13 +182,17 @@ class Runtime:
         self.close()
 
     def _borrowed(self):
-        # borrowed host logits: valid until the next mutating call
-        return np.ctypeslib.as_array(ctypes.cast(self._logits, ctypes.POINTER(ctypes.c_float)),
-                                     shape=(VOCAB,))
+        # borrowed host logits: valid until the next mutating call; the context
+        # reuses one host buffer, so the array over it is made once per address
+        address = self._logits.value
+        if self._view is None or self._view[0] != address:
+            arr = np.ctypeslib.as_array(ctypes.cast(self._logits, ctypes.POINTER(ctypes.c_float)), shape=(VOCAB,))
+            self._view = (address, arr)
+        return self._view[1]
 
     def _call(self, fn, *args):
-        err = _error()
-        self._logits = ctypes.c_void_p()
+        err = self._err
+        self._logits.value = None
         if fn(self.handle, *args, ctypes.byref(self._logits), err, 512):
             raise LuneletteError(err.value.decode())
         return self._borrowed()
