@@ -1085,7 +1085,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1)
             gp.y_fixed = nullptr;
             // features 64 s .. 64 s + 63 land in act_s[0 .. 63]
             float *act_s = reinterpret_cast<float *>(mega_smem + (size_t)kRingSlots * kSlotBytes + kActOffset);
-            gp.y = act_s - (ptrdiff_t)blockIdx.x * 64;
+            gp.y = act_s;
+            gp.y_base = blockIdx.x * 64;
             gp.y_stride = kInner;
             inv = stage_frag<kHidden>(frag, p.hbuf + cur, nullptr, nullptr, p.norms + (size_t)(2 * layer + 1) * kHidden,
                                       red);

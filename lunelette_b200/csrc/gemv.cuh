@@ -208,6 +208,9 @@ struct GemvParams {
     // kEpiResidual, one token: the output rows also as 64-bit fixed point
     // (value * 2^32, rounded), or nullptr
     long long *y_fixed;
+    // kEpiSwiGLU, one token: feature f goes to y[f - y_base] (a slice of the
+    // features staged in shared memory); 0 otherwise
+    int y_base;
     // One-token QKV epilogue for readers on other CTAs: q rows and the
     // position's k and v rows also go out as tagged words (store_tagged) to
     // qkv_tagged[0..4096) (q), [4096..5120) (k), [5120..6144) (v), tag ytag;
@@ -357,7 +360,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, int g, int la
                 // a = gate, b = up of feature 2g + pair
                 int f = 2 * g + pair;
                 float silu = a / (1.0f + expf(-a));
-                p.y[(size_t)m * p.y_stride + f] = silu * b;
+                p.y[(size_t)m * p.y_stride + f - p.y_base] = silu * b;
             } else {
                 // QKV: ra = head*128 + j (j < 64), rb = ra + 64
                 int pos = (p.step ? p.step->length : p.length) + p.token_offset + m;
