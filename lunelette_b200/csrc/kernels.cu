@@ -1,5 +1,6 @@
 #include "kernels.h"
 #include "head_mma.cuh"
+#include "launch.h"
 
 #include <stdlib.h>
 
@@ -8,34 +9,6 @@ using namespace lun;
 namespace {
 
 constexpr int kMaxGemvSmem = (kInner / 64) * 256 * 4;  // B fragments of 4 rows x 9216 columns
-
-// Programmatic dependent launch for every kernel of the decode/prefill sequence
-// (LUNELETTE_PDL=0 turns it off for comparisons).
-bool pdl_enabled()
-{
-    static const bool on = [] {
-        const char *v = getenv("LUNELETTE_PDL");
-        return !(v && v[0] == '0');
-    }();
-    return on;
-}
-
-template <typename... Params, typename... Args>
-cudaError_t launch(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
-                   cudaStream_t stream, Args &&...args)
-{
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...);
-}
 
 template <int M, int EPI>
 cudaError_t setup_one()

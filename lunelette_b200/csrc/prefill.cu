@@ -3,6 +3,7 @@
 #include <string.h>
 
 #include "kernels.h"
+#include "launch.h"
 #include "prefill_gemm.cuh"
 
 
@@ -90,8 +91,7 @@ template <int EPI>
 static cudaError_t launch_finish(const PrefillFinishParams &f, cudaStream_t stream)
 {
     const dim3 grid((unsigned)((f.rows / 2 + 255) / 256), (unsigned)f.count);
-    prefill_finish_kernel<EPI><<<grid, 256, 0, stream>>>(f);
-    return cudaGetLastError();
+    return launch(prefill_finish_kernel<EPI>, grid, dim3(256), 0, stream, f);
 }
 
 static cudaError_t check_prefill(const GemvParams &p, int count, const PrefillPlan &pl, const PrefillWorkspace &w)
@@ -158,8 +158,7 @@ cudaError_t lun_launch_prefill_split(const GemvParams &p, int count, const Prefi
     sp.x = p.x;
     sp.x_stride = p.x_stride;
     sp.gain = p.gain;
-    prefill_split_kernel<<<pl.token_tiles * kPgM, kSplitThreads, 0, stream>>>(sp);
-    return cudaGetLastError();
+    return launch(prefill_split_kernel, dim3(pl.token_tiles * kPgM), dim3(kSplitThreads), 0, stream, sp);
 }
 
 cudaError_t lun_launch_prefill_gemm(const GemvParams &p, int count, const PrefillWorkspace &w, int sm_count,
@@ -183,9 +182,8 @@ cudaError_t lun_launch_prefill_gemm(const GemvParams &p, int count, const Prefil
     g.error = w.error;
     CUtensorMap wmap;
     if ((e = weight_tensor_map(&wmap, p.W, p.rows, g.nb)) != cudaSuccess) return e;
-    prefill_gemm_pair_kernel<<<dim3(2 * pl.row_tiles, (pl.token_tiles + 1) / 2, pl.splits), kPgThreads,
-                               kP2SmemBytes, stream>>>(g, wmap);
-    return cudaGetLastError();
+    return launch(prefill_gemm_pair_kernel, dim3(2 * pl.row_tiles, (pl.token_tiles + 1) / 2, pl.splits),
+                  dim3(kPgThreads), kP2SmemBytes, stream, g, wmap);
 }
 
 cudaError_t lun_launch_prefill_finish(const GemvParams &p, int count, int epilogue, const PrefillWorkspace &w,
@@ -227,10 +225,10 @@ cudaError_t lun_launch_prefill_finish_split(const GemvParams &p, int count, int 
     sp.gain = next_gain;
     if (!split) sp.xs = nullptr;
     if (epilogue == kEpiSwiGLU)
-        prefill_finish_split_kernel<kEpiSwiGLU><<<pl.token_tiles * kPgM, kFsThreads, 0, stream>>>(f, sp);
-    else
-        prefill_finish_split_kernel<kEpiResidual><<<pl.token_tiles * kPgM, kFsThreads, 0, stream>>>(f, sp);
-    return cudaGetLastError();
+        return launch(prefill_finish_split_kernel<kEpiSwiGLU>, dim3(pl.token_tiles * kPgM), dim3(kFsThreads), 0,
+                      stream, f, sp);
+    return launch(prefill_finish_split_kernel<kEpiResidual>, dim3(pl.token_tiles * kPgM), dim3(kFsThreads), 0, stream,
+                  f, sp);
 }
 
 cudaError_t lun_launch_prefill(const GemvParams &p, int count, int epilogue, const PrefillWorkspace &w,

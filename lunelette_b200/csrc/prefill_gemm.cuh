@@ -200,6 +200,8 @@ __device__ __forceinline__ void split_emit(const PrefillSplitParams &p, int t, b
 
 static __global__ void __launch_bounds__(kSplitThreads) prefill_split_kernel(PrefillSplitParams p)
 {
+    pdl_wait();  // the rows come from the previous kernel, and the last GEMM read the operand tiles
+    pdl_launch_dependents();
     const int t = blockIdx.x;
     const bool live = t < p.count;
     const float *xr = p.x + (size_t)(live ? t : 0) * p.x_stride;
@@ -386,13 +388,27 @@ static __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPgThreads, 1
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // the weights do not depend on earlier kernels: their first stages are in
+    // flight before the wait for the previous kernel (programmatic launch); the
+    // activations, the partials this grid writes and the rest come after it
+    const int pre = min(nk, kP2WStages);
+    if (warp == 0 && lane == 0)
+        for (int iw = 0; iw < pre; iw++) {
+            uint8_t *dst = wring + iw * kP2W8;
+            mbar_expect_tx(&wfull[iw], kP2W8);
+            tma_load_4d(dst, &wmap, 0, 0, k0 + iw, tile0, &wfull[iw]);
+            tma_load_4d(dst + kP2W8 / 2, &wmap, 0, 0, k0 + iw, tile0 + kPgN / kTileRows, &wfull[iw]);
+        }
+    pdl_wait();
+    pdl_launch_dependents();
+
     if (warp == 0) {
         // ---- loads. Weights: per stage two tensor copies (the 16 tiles of each
         // 256-row half) into the weight ring; activations: the hi and lo atoms of
         // this CTA's tokens into the activation ring. Each stream goes as far
         // ahead as its ring allows; the warp issues whichever next copy has a
         // free slot (non-blocking probes, so one full ring never stalls the other).
-        int iw = 0, ia = 0;
+        int iw = pre, ia = 0;
         if (lane == 0) {
             unsigned idle = 0;
             while ((iw < nk || ia < nk) && !*abort_word) {
@@ -589,6 +605,8 @@ __device__ __forceinline__ float finish_scale(const PrefillFinishParams &p, int 
 template <int EPI>
 static __global__ void __launch_bounds__(256) prefill_finish_kernel(PrefillFinishParams p)
 {
+    pdl_wait();  // the partials come from the GEMM
+    pdl_launch_dependents();
     const int t = blockIdx.y;
     const int pr = blockIdx.x * blockDim.x + threadIdx.x;
     if (2 * pr >= p.rows) return;
@@ -655,6 +673,8 @@ template <int EPI>
 static __global__ void __launch_bounds__(kFsThreads) prefill_finish_split_kernel(PrefillFinishParams f,
                                                                                   PrefillSplitParams sp)
 {
+    pdl_wait();  // the partials come from the GEMM, which also read the operand tiles this kernel rewrites
+    pdl_launch_dependents();
     const int t = blockIdx.x;
     const bool live = t < f.count;
     const int width = EPI == kEpiSwiGLU ? f.rows / 2 : f.rows;
