@@ -6,7 +6,7 @@
 namespace lun {
 
 // Grid barriers per decode step: two per layer (after o, once h is whole;
-// after the FFN, once every act slice's down output is added into dsum) and
+// after the FFN, once every act slice's down output is added into xfix) and
 // one after the head and the pick. qkv -> attention goes through tagged words
 // (the attention CTAs poll the q, k and v values themselves), attention -> o
 // through a counter (kSyncAttn); gate/up -> down stays inside each CTA.
