@@ -2,17 +2,25 @@
 
 Workload ("C0"): the Ministral-3-3B-shaped decoder with a
 seeded random-init checkpoint, batch 1, a 32-token prompt of ids ~ U[1000,
-131072), greedy decode at context profile 256. A "step" is one greedy decode
-token. The timed region is R rounds of: restore the 32-token prompt checkpoint
-(host-only, no device work) and decode 31 greedy tokens on the device
-(lunelette_cuda_decode_loop: one launch of the persistent decode kernel for the
-31 tokens, argmax fed back on the GPU). `value` = decode tokens/s from CUDA
-events (max over ranks, all ranks' tokens summed); `e2e` = the same metric
-through the drop-in C-ABI with host buffers (lunelette_metal_decode + host
-greedy each token: one persistent-kernel launch per token, H2D of the step
-parameters and D2H of the 131072 logits inside the timed region). `roofline`
-is the persistent kernel's: the algorithmic bytes of a launch (FP8 linears,
-BF16 head, norm gains and the FP32 KV rows read) over its CUDA-event time.
+131072), then greedy decoding at context profile 256. One benchmark STEP is one
+C0 generation's decode phase: starting from the prompt's checkpoint (a host-only
+restore), 31 greedy decode tokens (the 32nd generated token comes from the
+prompt's logits). `--steps K` times exactly K such passes. `value` = decode
+tokens/s from CUDA events around lunelette_cuda_decode_loop (one launch of the
+persistent decode kernel per pass, argmax fed back on the GPU), all ranks'
+tokens over the slowest rank's device time. `e2e` = the same metric through
+the drop-in C-ABI with host buffers (lunelette_metal_decode + host greedy each
+token: H2D of the step parameters and D2H of the 131072 logits per token inside
+the timed region). `roofline` is the persistent kernel's: the algorithmic
+bytes of a launch (FP8 linears, BF16 head, norm gains and the FP32 KV rows
+read) over its CUDA-event time; `traffic` scales the ncu DRAM bytes of one
+token (profiles/decode_mega_c0_token.json) to a launch.
+
+`--impl reference` times the CPU reference of the same path (the oracle's FP32
+restatement of the reference's Metal kernels, all host threads) on the same
+`config`: each step is a bounded sample of the pass (REF_TOKENS_PER_STEP greedy
+tokens), and it never loads the product library (its checkpoint writer is
+oracle/libsynth.so).
 
 Multi-GPU: one process per GPU (torchrun), each an independent weight replica
 and session ("replicas only": the model has no collective), so scaling is weak.
@@ -38,14 +46,22 @@ sys.path.insert(0, REPO)
 METRIC = "decode tok/s (batch 1 and aggregate) + prefill tok/s, % of HBM/FP8 roofline"
 PROMPT = 32
 CONTEXT = 256
+PER_PASS = 31            # greedy decode tokens in one C0 pass (one bench step)
+REF_TOKENS_PER_STEP = 3  # CPU reference: greedy tokens sampled per step
 WEIGHT_BYTES_PER_TOKEN = 3026190336 + 805306368 + 53 * 3072 * 4  # FP8 linears + BF16 head + norms
 KV_BYTES_PER_POSITION = 26 * 2 * 1024 * 4                         # FP32 K and V, all layers
 GATEUP_BYTES = 18432 * 3072                                       # one fused gate/up launch
 HEAD_BYTES = 131072 * 3072 * 2
-# DRAM read + write bytes of one C0 decode token: ncu capture of a one-token
-# launch of decode_mega_kernel at context 34 (profiles/decode_mega_c0_token.md:
-# 3,839,687,168 read + 7,772,160 written)
-DRAM_BYTES_PER_TOKEN = 3854483968 + 8470272
+TRAFFIC_FILE = os.path.join(REPO, "profiles", "decode_mega_c0_token.json")
+
+# The workload both arms report (identical dicts, so the two lines compare).
+C0_CONFIG = {
+    "workload": "C0: batch-1 greedy decode after a 32-token prompt, context profile 256",
+    "prompt": PROMPT, "context": CONTEXT, "decode_tokens_per_step": PER_PASS,
+    "step": "one C0 generation's decode phase: restore the prompt checkpoint, then 31 greedy tokens",
+    "parallelism": "replicas (one weight replica and session per GPU)",
+    "l2": "inputs larger than L2: every token streams 3.83 GB of weights",
+}
 
 
 def env_int(name, default):
@@ -114,11 +130,12 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.samples)}
 
 
-def ensure_checkpoint(path, rank, world, barrier):
-    import lunelette_b200 as L
+def ensure_checkpoint(path, rank, barrier, writer):
+    """The seeded synthetic checkpoint at `path`, written once by rank 0 with
+    `writer(path, seed)` when absent (both arms' writers give identical bytes)."""
     if rank == 0 and not os.path.exists(path):
         tmp = path + ".partial%d" % os.getpid()
-        L.synth_checkpoint(tmp, 0)
+        writer(tmp, 0)
         os.replace(tmp, path)
     barrier()
     return path
@@ -170,13 +187,38 @@ def gateup_roofline(lib, torch, checkpoint, launches=40):
     return ms, algorithmic
 
 
-def traffic_per_launch(steps):
-    """DRAM bytes (read + write) of a persistent-kernel launch of `steps` tokens,
-    from the ncu capture summarised in profiles/ (one single-token launch on the
-    C0 workload, scaled by the token count: the kernel's traffic is per token),
-    or None when no capture has been summarised."""
-    per_token = DRAM_BYTES_PER_TOKEN
-    return None if per_token is None else per_token * steps
+def traffic_per_launch(tokens):
+    """DRAM bytes (read + write) of a persistent-kernel launch of `tokens` tokens:
+    the ncu capture of one single-token launch on the C0 workload, stored as data
+    in profiles/decode_mega_c0_token.json, times the tokens of the launch (every
+    token re-reads the weights); None when no capture is stored."""
+    try:
+        with open(TRAFFIC_FILE) as f:
+            d = json.load(f)
+        per_token = (int(d["dram_bytes_read"]) + int(d["dram_bytes_write"])) / int(d["tokens_per_launch"])
+    except Exception:
+        return None
+    return per_token * tokens
+
+
+def c0_bytes_per_token(context_before):
+    """Algorithmic bytes of one decode token at `context_before` positions:
+    weights, norms and the FP32 K/V rows of every position attended (the new one
+    included)."""
+    return WEIGHT_BYTES_PER_TOKEN + KV_BYTES_PER_POSITION * (context_before + 1)
+
+
+def c1_gemv(peak):
+    """every linear shape at token batch M = 1, 2, 4, 8 (the
+    BF16 head at M = 1) through the standalone GEMV kernels, GB/s of algorithmic
+    bytes and the fraction of the measured HBM peak, per shape and M."""
+    from lunelette_b200 import microbench
+    rows = microbench.run(list(microbench.SHAPES), [1, 2, 4, 8], iters=30)
+    out = {}
+    for r in rows:
+        out.setdefault(r["shape"], {})["m%d" % r["m"]] = {"us": round(r["us"], 2), "gbs": round(r["gbs"], 1),
+                                                          "frac": round(r["gbs"] / peak, 3)}
+    return out
 
 
 def prefill_gemm_roofline(lib, torch, count=256, reps=20):
@@ -205,36 +247,42 @@ def prefill_gemm_roofline(lib, torch, count=256, reps=20):
             "useful_flops": useful}
 
 
-def config_lines(L, torch, checkpoint, seed, barrier, max_over_ranks, world):
+def config_lines(L, torch, checkpoint, seed, barrier, max_over_ranks, world, hbm):
     """BASELINE configs 2-4 on one batch context (64 sessions x 4352 positions,
-    a paged FP32 KV pool of 59 GB): wall clock around host-synchronous calls.
+    a paged FP32 KV pool of 59 GB): wall clock around host-synchronous calls,
+    plus a device-timed C2 decode on a single-sequence context.
       C2: 4096 seeded ids in 16 chunks of 256 at context 4352, then 128 greedy
-          decode steps (persistent kernel);
+          decode steps (persistent kernel); `decode_device` repeats the decode
+          with lunelette_cuda_decode_loop (CUDA events, one launch) and carries
+          the roofline fraction of its algorithmic bytes;
       C3: a 512-token prefix, then 8 turns of 200 appended ids + 64 greedy tokens
           on the same session (its KV kept between turns); TTFT = the append;
       C4: 64 sessions, prompts ~ U[256, 4096] (seeded), prefilled in 256-token
-          chunks, then 128 batched greedy decode steps over all 64 sessions.
+          chunks, then 128 batched greedy decode steps over all 64 sessions; the
+          step's roofline counts the weights once plus every session's FP32 K/V
+          rows, over the wall-clock step time.
     Aggregates sum the ranks' work over the slowest rank's time."""
     rng = np.random.default_rng(seed + 99)
     out = {}
+    ids_c2 = rng.integers(1000, 131072, 4096).astype(np.int64)
     with L.Batch(checkpoint, max_sessions=64, context=4352, pool_positions=64 * 4352, block=256) as b:
         # C2
         s = b.open()
-        ids = rng.integers(1000, 131072, 4096).astype(np.int64)
         barrier()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         for c in range(16):
-            logits = b.append(s, ids[256 * c:256 * (c + 1)])
+            logits = b.append(s, ids_c2[256 * c:256 * (c + 1)])
         t_prefill = max_over_ranks(time.perf_counter() - t0)
-        tok = int(np.argmax(logits))
+        first_c2 = tok = int(np.argmax(logits))
         t0 = time.perf_counter()
         for _ in range(128):
             tok = int(np.argmax(b.append(s, [tok])))
         t_decode = max_over_ranks(time.perf_counter() - t0)
         b.close_session(s)
         out["c2"] = {"prefill_tok_s": world * 4096 / t_prefill, "decode_tok_s": world * 128 / t_decode,
-                     "note": "4096-token prompt in 16 x 256 chunks at context 4352, then 128 greedy steps"}
+                     "note": "4096-token prompt in 16 x 256 chunks at context 4352, then 128 greedy steps "
+                             "(wall clock around lunelette_cuda_batch_append)"}
         # C3
         s = b.open()
         prefix = rng.integers(1000, 131072, 512).astype(np.int64)
@@ -272,36 +320,85 @@ def config_lines(L, torch, checkpoint, seed, barrier, max_over_ranks, world):
         for _ in range(128):
             toks = b.decode(sessions, toks).tolist()
         t_decode = max_over_ranks(time.perf_counter() - t0)
+        step_s = t_decode / 128
+        # mean positions attended per session over the 128 steps (the new one included)
+        kv_positions = float(np.sum(lengths + 64.5))
+        step_bytes = WEIGHT_BYTES_PER_TOKEN + KV_BYTES_PER_POSITION * kv_positions
         out["c4"] = {"decode_tok_s_aggregate": world * 64 * 128 / t_decode,
                      "prefill_tok_s_aggregate": world * float(lengths.sum()) / t_prefill,
-                     "ms_per_batched_step": 1e3 * t_decode / 128, "sessions_per_gpu": 64,
+                     "ms_per_batched_step": 1e3 * step_s, "sessions_per_gpu": 64,
                      "mean_prompt": float(lengths.mean()),
+                     "roofline": {"bound": "hbm", "unit": "GB/s", "algorithmic_bytes_per_step": step_bytes,
+                                  "achieved": step_bytes / step_s / 1e9, "peak": hbm,
+                                  "frac": step_bytes / step_s / 1e9 / hbm,
+                                  "timing": "wall clock per batched step (host-synchronous calls)"},
                      "note": "64 ragged sessions per GPU, prompts U[256,4096], 128 batched greedy steps"}
+    # C2 decode on the device: the same prompt on a single-sequence context
+    with L.Runtime(checkpoint, limits=(4352, 256)) as rt:
+        rt.prefill(ids_c2[:256])
+        for c in range(1, 16):
+            rt.append(ids_c2[256 * c:256 * (c + 1)])
+        cp = rt.checkpoint_create()
+        rt.decode_loop(first_c2, 8)  # warm-up at this context
+        rt.checkpoint_restore(cp)
+        tokens, ms, launches = rt.decode_loop(first_c2, 128)
+        cp.destroy()
+    ms = max_over_ranks(ms)
+    launch_bytes = sum(c0_bytes_per_token(4096 + i) for i in range(128))
+    out["c2"]["decode_device"] = {
+        "tok_s": world * 128 / (ms / 1e3), "ms_per_token": ms / 128, "launches": launches,
+        "roofline": {"bound": "hbm", "unit": "GB/s", "algorithmic_bytes": launch_bytes,
+                     "achieved": launch_bytes / (ms / 1e3) / 1e9, "peak": hbm,
+                     "frac": launch_bytes / (ms / 1e3) / 1e9 / hbm,
+                     "kernel": "decode_mega_kernel, 128 greedy tokens at context 4096..4223 in one launch"}}
     return out
 
 
-def cpu_baseline(checkpoint, prompt, decode_steps=6):
-    """The CPU oracle (C restatement of the reference kernels, OpenMP) on this
-    box's host cores: the C0 prompt, then `decode_steps` greedy decode steps."""
-    from tests import oracle_lib
-    o = oracle_lib.load()
-    m = o.open_model(checkpoint, CONTEXT)
+def cpu_passes(oracle, checkpoint, prompt, steps, warmup, tokens_per_step):
+    """The CPU reference of a C0 pass on this box's host cores: the oracle's FP32
+    restatement of the reference kernels (OpenMP over all host threads). Each
+    step continues the greedy generation from the prompt by `tokens_per_step`
+    tokens, rewinding to the prompt after each pass of 31. Returns (seconds for
+    the timed steps, prefill seconds of the prompt)."""
+    m = oracle.open_model(checkpoint, CONTEXT)
     try:
         t0 = time.perf_counter()
         logits, _, _ = m.forward(prompt)
-        t1 = time.perf_counter()
-        tok = int(np.argmax(logits))
-        for _ in range(decode_steps):
-            logits, _, _ = m.forward([tok])
-            tok = int(np.argmax(logits))
-        t2 = time.perf_counter()
+        prefill_s = time.perf_counter() - t0
+        first = int(np.argmax(logits))
+        state = {"tok": first, "done": 0}
+
+        def step():
+            for _ in range(tokens_per_step):
+                if state["done"] == PER_PASS:
+                    m.rewind(len(prompt))
+                    state["tok"], state["done"] = first, 0
+                out, _, _ = m.forward([state["tok"]])
+                state["tok"] = int(np.argmax(out))
+                state["done"] += 1
+
+        for _ in range(warmup):
+            step()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            step()
+        elapsed = time.perf_counter() - t0
     finally:
         m.close()
-    return {"value": decode_steps / (t2 - t1), "unit": "tok/s", "cores": o.threads(), "kind": "port",
-            "sample": "C0 prompt of %d ids prefilled (%.2f s = %.1f tok/s), then %d greedy decode steps "
-                      "timed; oracle/oracle.c FP32, OpenMP" % (len(prompt), t1 - t0, len(prompt) / (t1 - t0),
-                                                                decode_steps),
-            "prefill_tok_s": len(prompt) / (t1 - t0)}
+    return elapsed, prefill_s
+
+
+def cpu_baseline(checkpoint, prompt, steps=2):
+    """cpu_baseline of our arm's line: a bounded sample of the C0 pass on the
+    host cores (rank 0 at N = 1)."""
+    from tests import oracle_lib
+    o = oracle_lib.load()
+    elapsed, prefill_s = cpu_passes(o, checkpoint, prompt, steps, 1, REF_TOKENS_PER_STEP)
+    n = steps * REF_TOKENS_PER_STEP
+    return {"value": n / elapsed, "unit": "tok/s", "cores": o.threads(), "kind": "port",
+            "sample": "%d greedy decode tokens of the C0 pass after the 32-token prompt (prefill %.2f s); "
+                      "oracle/oracle.c FP32 restatement of the reference's Metal kernels, OpenMP"
+                      % (n, prefill_s)}
 
 
 class Ranks:
@@ -335,53 +432,29 @@ def aggregate_rate(world, units_per_rank, slowest_seconds):
 
 
 def run_reference(args, rank, world):
-    """The reference's CPU implementation of the path: this repo's oracle port of
-    its Metal kernels (the Metal runtime itself cannot run off Apple hardware)."""
+    """The reference's CPU implementation of the path: this repository's oracle
+    port of its Metal kernels (the Metal runtime cannot run off Apple hardware),
+    on all host threads of rank 0. Loads only oracle/ libraries."""
     if rank != 0:
         return 0
-    import lunelette_b200 as L  # only for the synthetic checkpoint writer
-    checkpoint = ensure_checkpoint(args.checkpoint, 0, 1, lambda: None)
     from tests import oracle_lib
+    checkpoint = ensure_checkpoint(args.checkpoint, 0, lambda: None, oracle_lib.synth_checkpoint)
     o = oracle_lib.load()
     prompt = np.random.default_rng(args.seed).integers(1000, 131072, PROMPT).astype(np.int64)
-    # each step is one greedy token of the FP32 oracle on the host cores
-    # (~0.18 s): at most 256 timed steps keep the run within a few minutes
-    steps = min(args.steps, 256)
-    warmup = min(max(args.warmup, 3), 5)
-    m = o.open_model(checkpoint, CONTEXT)
-    try:
-        logits, _, _ = m.forward(prompt)
-        first = int(np.argmax(logits))
-        per_round = min(CONTEXT - PROMPT - 1, 31)
-
-        def decode(n):
-            # rounds of 31 greedy tokens from the prompt, as our arm's rounds
-            tok = first
-            m.rewind(PROMPT)
-            for i in range(n):
-                if i and i % per_round == 0:
-                    m.rewind(PROMPT)
-                    tok = first
-                logits, _, _ = m.forward([tok])
-                tok = int(np.argmax(logits))
-
-        decode(warmup)
-        t0 = time.perf_counter()
-        decode(steps)
-        elapsed = time.perf_counter() - t0
-    finally:
-        m.close()
-    value = steps / elapsed
+    steps, warmup = args.steps, max(args.warmup, 3)
+    elapsed, prefill_s = cpu_passes(o, checkpoint, prompt, steps, warmup, REF_TOKENS_PER_STEP)
+    tokens = steps * REF_TOKENS_PER_STEP
+    value = tokens / elapsed
+    sample = ("each step: %d greedy decode tokens of the C0 pass (a bounded sample of the 31-token pass), "
+              "continuing from the 32-token prompt; oracle/oracle.c FP32 restatement of the reference's "
+              "Metal kernels, OpenMP; prompt prefill %.2f s untimed" % (REF_TOKENS_PER_STEP, prefill_s))
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": steps, "warmup": warmup, "ms_per_step": 1000 * elapsed / steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded random-init checkpoint, seeded token ids)",
-            "config": {"workload": "C0: batch-1 greedy decode after a 32-token prompt, context 256",
-                       "prompt": PROMPT, "context": CONTEXT},
+            "data": "synthetic (seeded random-init checkpoint in the reference's tensor layout, seeded ids)",
+            "config": dict(C0_CONFIG),
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": o.threads(), "kind": "port",
-                             "sample": "%d greedy decode steps in rounds of 31 after the 32-token prompt "
-                                       "(bounded sample of C0); oracle/oracle.c FP32 restatement of the "
-                                       "reference's Metal kernels, OpenMP" % steps},
+                             "sample": sample},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
     return 0
@@ -400,22 +473,20 @@ def run_ours(args, rank, world, local_rank):
     barrier, max_over_ranks = ranks.barrier, ranks.max
 
     lib = L.library()
-    checkpoint = ensure_checkpoint(args.checkpoint, rank, world, barrier)
+    checkpoint = ensure_checkpoint(args.checkpoint, rank, barrier, L.synth_checkpoint)
     rt = L.Runtime(checkpoint)  # default options, profile C=256/B=256
     prompt = np.random.default_rng(args.seed + rank).integers(1000, 131072, PROMPT).astype(np.int64)
-    per_round = CONTEXT - PROMPT - 1
-    per_round = min(per_round, 31)  # C0: 32 greedy tokens, the first from the prefill
-    rounds = max(1, (args.steps + per_round - 1) // per_round)
-    steps = rounds * per_round
+    steps, warmup = args.steps, max(args.warmup, 3)
 
-    # ---- warm-up: untimed decode steps (also captures the decode graph)
+    # ---- warm-up: untimed passes
     rt.reset()
     first = int(np.argmax(rt.prefill(prompt)))
     cp = rt.checkpoint_create()
-    rt.decode_loop(first, max(args.warmup, 3))
-    rt.checkpoint_restore(cp)
+    for _ in range(warmup):
+        rt.decode_loop(first, PER_PASS)
+        rt.checkpoint_restore(cp)
 
-    # ---- value: device-resident decode, CUDA events
+    # ---- value: K passes on the device (one persistent launch each), CUDA events
     barrier()
     torch.cuda.synchronize()
     device_ms = 0.0
@@ -423,8 +494,8 @@ def run_ours(args, rank, world, local_rank):
     tokens_seen = None
     with ClockSampler(local_rank) as clocks:
         t0 = time.perf_counter()
-        for r in range(rounds):
-            tokens, ms, n = rt.decode_loop(first, per_round)
+        for _ in range(steps):
+            tokens, ms, n = rt.decode_loop(first, PER_PASS)
             device_ms += ms
             launches += n
             rt.checkpoint_restore(cp)
@@ -433,26 +504,27 @@ def run_ours(args, rank, world, local_rank):
         wall_ms = 1000 * (time.perf_counter() - t0)
     barrier()
     device_ms = max_over_ranks(device_ms)
-    value = aggregate_rate(world, steps, device_ms / 1000)
+    value = aggregate_rate(world, steps * PER_PASS, device_ms / 1000)
 
-    # ---- e2e: the drop-in C-ABI with host buffers, host greedy each token
+    # ---- e2e: K passes through the drop-in C-ABI with host buffers, host greedy each token
     barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     e2e_tokens = []
-    for r in range(rounds):
+    for _ in range(steps):
         logits = rt.checkpoint_restore(cp)
         tok = int(np.argmax(logits))
-        for i in range(per_round):
+        e2e_tokens = []
+        for i in range(PER_PASS):
             logits = rt.decode(tok)
             e2e_tokens.append(tok)
             tok = int(np.argmax(logits))
     torch.cuda.synchronize()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     barrier()
-    e2e_value = aggregate_rate(world, steps, e2e_s)
+    e2e_value = aggregate_rate(world, steps * PER_PASS, e2e_s)
     # the device loop and the host loop must generate the same greedy tokens
-    same_tokens = list(e2e_tokens[1:per_round]) == [int(t) for t in tokens_seen[:per_round - 1]]
+    same_tokens = list(e2e_tokens[1:]) == [int(t) for t in tokens_seen[:PER_PASS - 1]]
 
     # ---- prefill: 256-token chunk and the 32-token prompt through the C-ABI
     chunk = np.random.default_rng(args.seed + 17).integers(1000, 131072, 256).astype(np.int64)
@@ -474,39 +546,39 @@ def run_ours(args, rank, world, local_rank):
     cp.destroy()
     rt.close()
 
-    configs = None if args.no_configs else config_lines(L, torch, checkpoint, args.seed + rank, barrier,
-                                                         max_over_ranks, world)
     hbm, bf16, peak_kind = measured_peaks()
+    configs = None if args.no_configs else config_lines(L, torch, checkpoint, args.seed + rank, barrier,
+                                                         max_over_ranks, world, hbm)
+    gemv = c1_gemv(hbm) if not args.no_configs else None
     gemv_ms, gemv_bytes = gateup_roofline(lib, torch, checkpoint)
     pg = prefill_gemm_roofline(lib, torch)
     ms_per_step = device_ms / steps
-    mean_ctx = PROMPT + (per_round + 1) / 2
-    step_bytes = WEIGHT_BYTES_PER_TOKEN + KV_BYTES_PER_POSITION * mean_ctx
-    launch_ms = device_ms / launches            # one persistent-kernel launch per round
-    launch_bytes = step_bytes * steps / launches
+    launch_bytes = sum(c0_bytes_per_token(PROMPT + i) for i in range(PER_PASS))
+    launch_ms = device_ms / launches            # one persistent-kernel launch per pass
     achieved = launch_bytes / (launch_ms / 1000) / 1e9
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps,
-            "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True,
+            "warmup": warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None,
             "dtype": "fp8-e4m3 weights, fp32 activations/accumulation/kv",
             "data": "synthetic (seeded random-init checkpoint in the reference's tensor layout, seeded ids)",
-            "config": {"workload": "C0: batch-1 greedy decode after a 32-token prompt, context profile 256",
-                       "prompt": PROMPT, "decode_per_round": per_round, "rounds": rounds,
-                       "parallelism": "replicas (one weight replica and session per GPU)",
-                       "l2": "inputs larger than L2: each step streams %.2f GB of weights" % (step_bytes / 1e9)},
-            "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 1040,
-                    "d2h_bytes_per_step": 131072 * 4 + 4,
-                    "note": "lunelette_metal_decode per token, host greedy on the borrowed logits"},
+            "config": dict(C0_CONFIG),
+            "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 1040 * PER_PASS,
+                    "d2h_bytes_per_step": (131072 * 4 + 4) * PER_PASS,
+                    "note": "lunelette_metal_decode per token, host greedy on the borrowed logits; bytes per "
+                            "31-token step"},
             "prefill_tok_s": {"chunk_256": 256 / prefill_256, "prompt_32": PROMPT / prefill_32,
                               "note": "lunelette_metal_prefill wall time, host ids and logits"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "traffic": traffic_per_launch(per_round), "peak_kind": peak_kind,
-                         "kernel": "decode_mega_kernel (persistent: %d greedy tokens per launch)" % per_round,
+                         "frac": achieved / hbm, "traffic": traffic_per_launch(PER_PASS), "peak_kind": peak_kind,
+                         "kernel": "decode_mega_kernel (persistent: %d greedy tokens per launch)" % PER_PASS,
                          "algorithmic_bytes": launch_bytes, "avg_launch_ms": launch_ms,
-                         "bytes_per_token": step_bytes},
+                         "bytes_per_token": launch_bytes / PER_PASS,
+                         "traffic_source": "ncu DRAM read+write of one token (profiles/decode_mega_c0_token.json)"
+                                           " x the launch's tokens"},
+            "c1_gemv": gemv,
             "gemv_roofline": {"kernel": "gemv_tiled_kernel<1,kEpiSwiGLU> (fused norm + gate/up + SwiGLU, "
                                         "standalone launches, weights > L2)",
                               "achieved": gemv_bytes / (gemv_ms / 1000) / 1e9, "unit": "GB/s",
@@ -538,7 +610,7 @@ def run_ours(args, rank, world, local_rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=496)
+    ap.add_argument("--steps", type=int, default=20, help="C0 passes of 31 greedy tokens to time")
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seed", type=int, default=1234)

@@ -23,6 +23,17 @@ constexpr float kNormEps = 1e-5f;
 constexpr float kScoreScale = 0.08838834764831845f;  // 1/sqrt(128) as the reference rounds it
 constexpr int kQKVRows = kQuery + 2 * kKV;       // 6144
 constexpr int kGateUpRows = 2 * kInner;          // 18432: gate and up rows alternate (2f, 2f+1)
+// Bits of a step's flag word (the host reads it after the step):
+//   kFlagNonfinite    the head produced a NaN or infinite logit
+//   kFlagFixedRange   a term added into a 64-bit fixed-point sum (32 fraction
+//                     bits, range +-2^31) was non-finite or not below
+//                     kFixedTermLimit, so the sum cannot be trusted; the host
+//                     reruns the step on the FP32 path
+constexpr int kFlagNonfinite = 1;
+constexpr int kFlagFixedRange = 2;
+// At most 145 terms reach one fixed-point element per layer (h from the o
+// epilogue plus 144 act slices of down); 145 * 2^23 < 2^31.
+constexpr float kFixedTermLimit = 0x1p23f;
 
 // Per-call parameters that kernels read from device memory, so that one
 // captured graph serves every step: the sequence length before the call.

@@ -593,11 +593,18 @@ __device__ __forceinline__ void consume_down(const Ring &r, const PhaseSpan &sp,
 }
 
 // The CTA's 3072 down row sums (rows_s) added into xfix, the layer output x
-// in fixed point, with 64-bit integer reductions.
-__device__ __forceinline__ void down_reduce(const float *rows_s, long long *xfix)
+// in fixed point, with 64-bit integer reductions. A row sum the fixed point
+// cannot hold (non-finite, or too large for 145 terms to stay in range) sets
+// kFlagFixedRange, and the host reruns the step on the FP32 path.
+__device__ __forceinline__ void down_reduce(const float *rows_s, long long *xfix, int *flag)
 {
-    for (int v = threadIdx.x; v < kHidden; v += kMegaConsumers)
-        asm volatile("red.global.add.u64 [%0], %1;" ::"l"(xfix + v), "l"(float_to_fixed(rows_s[v])) : "memory");
+    bool out_of_range = false;
+    for (int v = threadIdx.x; v < kHidden; v += kMegaConsumers) {
+        const float r = rows_s[v];
+        out_of_range |= !(fabsf(r) < kFixedTermLimit);
+        asm volatile("red.global.add.u64 [%0], %1;" ::"l"(xfix + v), "l"(float_to_fixed(r)) : "memory");
+    }
+    if (__any_sync(0xffffffffu, out_of_range) && (threadIdx.x & 31) == 0) atomicOr(flag, kFlagFixedRange);
 }
 
 __device__ __forceinline__ void arg_better(float &v, int &i, float v2, int i2)
@@ -654,7 +661,7 @@ __device__ __forceinline__ void consume_head(const Ring &r, const PhaseSpan &sp,
             arg_better(best, best_i, v, row + rr);
         }
     }
-    if (bad) atomicOr(p.nonfinite, 1);
+    if (bad) atomicOr(p.nonfinite, kFlagNonfinite);
 }
 
 // Position ranges per KV head for `total` positions: at most 256 positions
@@ -1058,6 +1065,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1)
             // value of this layer's xfix (read only after the FFN barrier)
             gp.y = p.hbuf + cur;
             gp.y_fixed = p.xfix + cur;
+            gp.range_flag = p.nonfinite;
             gp.y_stride = kHidden;
             stage_x_rows(res_s, p.xfix + prev, layer == 0 ? emb_row : nullptr, gp.res_base,
                          sp.items / (kQuery / kBlockCols / item_blocks(kPhO)) * kTileRows);
@@ -1102,7 +1110,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1)
             consume_down(ring, sp, seq, taken, act_s, act_s + 64, sc[6], p.error);
             seq += sp.items;
             consumers_sync();
-            if (sp.items) down_reduce(act_s + 64, p.xfix + cur);
+            if (sp.items) down_reduce(act_s + 64, p.xfix + cur, p.nonfinite);
             if (threadIdx.x == 0) record_mark(p, rec, mk + 11);
             grid_sync(p, ++barrier, rec, mk + 12);
         }

@@ -792,11 +792,13 @@ extern "C" int lun_device_decode_loop(lun_device *d, int64_t first_token, size_t
         if ((e = cudaEventCreate(&start)) != cudaSuccess || (e = cudaEventCreate(&stop)) != cudaSuccess ||
             (e = cudaMemcpyAsync(d->d_step, d->h_step, sizeof(StepParams), cudaMemcpyHostToDevice,
                                  d->stream)) != cudaSuccess ||
+            (e = cudaMemsetAsync(d->d_flag, 0, 4, d->stream)) != cudaSuccess ||
             (e = cudaEventRecord(start, d->stream)) != cudaSuccess ||
             (e = launch_mega(d, (int)steps)) != cudaSuccess ||
             (e = cudaEventRecord(stop, d->stream)) != cudaSuccess ||
             (e = cudaMemcpyAsync(d->h_error, d->mega_error, 4, cudaMemcpyDeviceToHost, d->stream)) !=
                 cudaSuccess ||
+            (e = cudaMemcpyAsync(d->h_flag, d->d_flag, 4, cudaMemcpyDeviceToHost, d->stream)) != cudaSuccess ||
             (e = cudaStreamSynchronize(d->stream)) != cudaSuccess)
             goto bad;
         if (*d->h_error) {
@@ -804,6 +806,19 @@ extern "C" int lun_device_decode_loop(lun_device *d, int64_t first_token, size_t
             e = cudaErrorLaunchTimeout;
             what = "decode loop: grid barrier wait gave up";
             goto bad;
+        }
+        // the loop picks tokens on the device, so it cannot rerun a step on the
+        // FP32 path: a flagged step fails the call (lunelette_metal_decode
+        // handles such values)
+        if (*d->h_flag) {
+            if (error && capacity)
+                snprintf(error, capacity, "decode loop: %s",
+                         (*d->h_flag & kFlagNonfinite) ? "non-finite logit"
+                                                        : "hidden value outside the fixed-point range");
+            free(host_tokens);
+            cudaEventDestroy(start);
+            cudaEventDestroy(stop);
+            return -1;
         }
         if (milliseconds && (e = cudaEventElapsedTime(milliseconds, start, stop)) != cudaSuccess) goto bad;
         d->launches_per_step = 1;
@@ -862,6 +877,46 @@ bad:
     return fail(error, capacity, what, e);
 }
 
+// Embedding, the 26 layers on the per-projection kernels (GEMV for up to
+// kGemvMaxTokens tokens, tcgen05 GEMMs beyond), the optional trace copies and
+// the head over the last row, for the n tokens described by d_step.
+static cudaError_t enqueue_block(lun_device *d, int n, size_t length)
+{
+    cudaError_t e = lun_launch_embed(d->embedding, d->d_step, d->x, n, d->stream);
+    if (e != cudaSuccess) return e;
+    if (n > kGemvMaxTokens && d->use_gemm) {
+        if ((e = run_prefill_layers(d, n, length)) != cudaSuccess) return e;
+    } else {
+        for (int layer = 0; layer < kLayers; layer++) {
+            if ((e = run_projection(d, layer, 0, n)) != cudaSuccess ||
+                (e = run_attention(d, layer, n, length)) != cudaSuccess ||
+                (e = run_projection(d, layer, 1, n)) != cudaSuccess ||
+                (e = run_projection(d, layer, 2, n)) != cudaSuccess ||
+                (e = run_projection(d, layer, 3, n)) != cudaSuccess)
+                return e;
+            if (d->trace && (e = cudaMemcpyAsync(d->trace_buf + (size_t)layer * n * kHidden, d->x,
+                                                 (size_t)n * kHidden * 4, cudaMemcpyDeviceToDevice,
+                                                 d->stream)) != cudaSuccess)
+                return e;
+        }
+    }
+    if (d->trace) {
+        if ((e = lun_launch_rmsnorm(d->final_norm, d->x, d->trace_buf + (size_t)kLayers * n * kHidden, kHidden, n,
+                                    d->stream)) != cudaSuccess)
+            return e;
+        d->trace_count = (size_t)n;
+    }
+    HeadParams hp;
+    hp.W = d->embedding;
+    hp.rows = kVocab;
+    hp.cols = kHidden;
+    hp.x = d->x + (size_t)(n - 1) * kHidden;
+    hp.gain = d->final_norm;
+    hp.logits = d->logits;
+    hp.nonfinite = d->d_flag;
+    return lun_launch_head(hp, d->sm_count, d->stream);
+}
+
 extern "C" int lun_device_run(lun_device *d, const int64_t *ids, size_t count, size_t length,
                               const float **logits, int *nonfinite, char *error, size_t capacity)
 {
@@ -871,83 +926,61 @@ extern "C" int lun_device_run(lun_device *d, const int64_t *ids, size_t count, s
         if (error && capacity) snprintf(error, capacity, "device run: block/context exceeded");
         return -1;
     }
-    d->h_step->length = (int)length;
-    d->h_step->count = (int)count;
-    for (size_t i = 0; i < count; i++) d->h_step->ids[i] = (int)ids[i];
-    d->h_step->generated = 0;
     const int n = (int)count;
     // single-token calls run the persistent decode kernel (one launch); blocks of
-    // several tokens and traced calls run the per-projection kernels
-    const bool mega = count == 1 && !d->trace && d->use_mega;
+    // several tokens and traced calls run the per-projection kernels. A
+    // persistent step whose fixed-point residual sums left their range (a
+    // non-finite or huge hidden value) is run again on the FP32 kernels, which
+    // write the same KV rows and give the reference's answer for such values.
+    bool mega = count == 1 && !d->trace && d->use_mega;
     const char *what = "step upload";
-    if ((e = cudaMemcpyAsync(d->d_step, d->h_step, sizeof(StepParams), cudaMemcpyHostToDevice,
-                             d->stream)) != cudaSuccess ||
-        (e = cudaMemsetAsync(d->d_flag, 0, 4, d->stream)) != cudaSuccess)
-        goto bad;
-    what = "kernel launch";
-    if (mega) {
-        if ((e = launch_mega(d, 1)) != cudaSuccess ||
-            (e = cudaMemcpyAsync(d->h_error, d->mega_error, 4, cudaMemcpyDeviceToHost, d->stream)) !=
-                cudaSuccess)
+    for (;;) {
+        d->h_step->length = (int)length;
+        d->h_step->count = n;
+        for (size_t i = 0; i < count; i++) d->h_step->ids[i] = (int)ids[i];
+        d->h_step->generated = 0;
+        what = "step upload";
+        if ((e = cudaMemcpyAsync(d->d_step, d->h_step, sizeof(StepParams), cudaMemcpyHostToDevice,
+                                 d->stream)) != cudaSuccess ||
+            (e = cudaMemsetAsync(d->d_flag, 0, 4, d->stream)) != cudaSuccess)
             goto bad;
-    } else {
-    if ((e = lun_launch_embed(d->embedding, d->d_step, d->x, n, d->stream)) != cudaSuccess) goto bad;
-    if (n > kGemvMaxTokens && d->use_gemm) {
-        if ((e = run_prefill_layers(d, n, length)) != cudaSuccess) goto bad;
-    } else
-    for (int layer = 0; layer < kLayers; layer++) {
-        if ((e = run_projection(d, layer, 0, n)) != cudaSuccess ||
-            (e = run_attention(d, layer, n, length)) != cudaSuccess ||
-            (e = run_projection(d, layer, 1, n)) != cudaSuccess ||
-            (e = run_projection(d, layer, 2, n)) != cudaSuccess ||
-            (e = run_projection(d, layer, 3, n)) != cudaSuccess)
+        what = "kernel launch";
+        if (mega) {
+            if ((e = launch_mega(d, 1)) != cudaSuccess ||
+                (e = cudaMemcpyAsync(d->h_error, d->mega_error, 4, cudaMemcpyDeviceToHost, d->stream)) !=
+                    cudaSuccess)
+                goto bad;
+        } else if ((e = enqueue_block(d, n, length)) != cudaSuccess) {
             goto bad;
-        if (d->trace && (e = cudaMemcpyAsync(d->trace_buf + (size_t)layer * count * kHidden, d->x,
-                                             count * kHidden * 4, cudaMemcpyDeviceToDevice,
-                                             d->stream)) != cudaSuccess)
+        }
+        what = "logits download";
+        if ((e = cudaMemcpyAsync(d->h_logits, d->logits, (size_t)kVocab * 4, cudaMemcpyDeviceToHost,
+                                 d->stream)) != cudaSuccess ||
+            (e = cudaMemcpyAsync(d->h_flag, d->d_flag, 4, cudaMemcpyDeviceToHost, d->stream)) != cudaSuccess)
             goto bad;
-    }
-    if (d->trace) {
-        if ((e = lun_launch_rmsnorm(d->final_norm, d->x, d->trace_buf + (size_t)kLayers * count * kHidden,
-                                    kHidden, n, d->stream)) != cudaSuccess)
+        if (d->pf.error &&
+            (e = cudaMemcpyAsync(d->h_pf_error, d->pf.error, 4, cudaMemcpyDeviceToHost, d->stream)) != cudaSuccess)
             goto bad;
-        d->trace_count = count;
-    }
-    {
-        HeadParams hp;
-        hp.W = d->embedding;
-        hp.rows = kVocab;
-        hp.cols = kHidden;
-        hp.x = d->x + (size_t)(count - 1) * kHidden;
-        hp.gain = d->final_norm;
-        hp.logits = d->logits;
-        hp.nonfinite = d->d_flag;
-        if ((e = lun_launch_head(hp, d->sm_count, d->stream)) != cudaSuccess) goto bad;
-    }
-    }
-    what = "logits download";
-    if ((e = cudaMemcpyAsync(d->h_logits, d->logits, (size_t)kVocab * 4, cudaMemcpyDeviceToHost,
-                             d->stream)) != cudaSuccess ||
-        (e = cudaMemcpyAsync(d->h_flag, d->d_flag, 4, cudaMemcpyDeviceToHost, d->stream)) !=
-            cudaSuccess)
-        goto bad;
-    if (d->pf.error &&
-        (e = cudaMemcpyAsync(d->h_pf_error, d->pf.error, 4, cudaMemcpyDeviceToHost, d->stream)) != cudaSuccess)
-        goto bad;
-    what = "execution";
-    if ((e = cudaStreamSynchronize(d->stream)) != cudaSuccess) goto bad;
-    if (d->pf.error && *d->h_pf_error) {
-        cudaMemset(d->pf.error, 0, sizeof(int));
-        if (error && capacity) snprintf(error, capacity, "prefill: GEMM pipeline wait gave up");
-        return -1;
-    }
-    if (mega && *d->h_error) {
-        cudaMemset(d->mega_error, 0, sizeof(int));
-        if (error && capacity) snprintf(error, capacity, "decode: grid barrier wait gave up");
-        return -1;
+        what = "execution";
+        if ((e = cudaStreamSynchronize(d->stream)) != cudaSuccess) goto bad;
+        if (d->pf.error && *d->h_pf_error) {
+            cudaMemset(d->pf.error, 0, sizeof(int));
+            if (error && capacity) snprintf(error, capacity, "prefill: GEMM pipeline wait gave up");
+            return -1;
+        }
+        if (mega && *d->h_error) {
+            cudaMemset(d->mega_error, 0, sizeof(int));
+            if (error && capacity) snprintf(error, capacity, "decode: grid barrier wait gave up");
+            return -1;
+        }
+        if (mega && (*d->h_flag & kFlagFixedRange)) {
+            mega = false;
+            continue;
+        }
+        break;
     }
     *logits = d->h_logits;
-    *nonfinite = *d->h_flag != 0;
+    *nonfinite = (*d->h_flag & kFlagNonfinite) != 0;
     return 0;
 bad:
     return fail(error, capacity, what, e);

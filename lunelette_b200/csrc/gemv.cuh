@@ -206,8 +206,10 @@ struct GemvParams {
     const float *res_shared;
     int res_base;
     // kEpiResidual, one token: the output rows also as 64-bit fixed point
-    // (value * 2^32, rounded), or nullptr
+    // (value * 2^32, rounded), or nullptr; a value the fixed point cannot hold
+    // sets kFlagFixedRange in *range_flag
     long long *y_fixed;
+    int *range_flag;
     // kEpiSwiGLU, one token: feature f goes to y[f - y_base] (a slice of the
     // features staged in shared memory); 0 otherwise
     int y_base;
@@ -342,7 +344,10 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, int g, int la
                                               : __ldcg(&p.res[(size_t)m * p.res_stride + r])) +
                                 v;
                         p.y[(size_t)m * p.y_stride + r] = v;
-                        if (EPI == kEpiResidual && p.y_fixed) p.y_fixed[r] = __float2ll_rn(v * 0x1p32f);
+                        if (EPI == kEpiResidual && p.y_fixed) {
+                            p.y_fixed[r] = __float2ll_rn(v * 0x1p32f);
+                            if (!(fabsf(v) < kFixedTermLimit)) atomicOr(p.range_flag, kFlagFixedRange);
+                        }
                     }
                 }
             }

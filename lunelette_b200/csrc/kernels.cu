@@ -1,4 +1,8 @@
 #include "kernels.h"
+
+#include <atomic>
+#include <mutex>
+
 #include "head_mma.cuh"
 #include "launch.h"
 
@@ -186,16 +190,22 @@ cudaError_t lun_kernels_init()
     return setup_epi<kEpiSwiGLU>();
 }
 
-// Dynamic shared memory above 48 KB needs a per-device opt-in; do it on first use.
+// Dynamic shared memory above 48 KB needs a per-device opt-in; do it on first
+// use. Callers on several threads may arrive together: the flags are atomic and
+// the set-up itself runs under a lock, once per device.
 cudaError_t lun_kernels_ensure()
 {
-    static bool done[128] = {};
+    static std::atomic<bool> done[128];
+    static std::mutex setup;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 128 && done[dev]) return cudaSuccess;
+    if (dev < 0 || dev >= 128) return lun_kernels_init();
+    if (done[dev].load(std::memory_order_acquire)) return cudaSuccess;
+    std::lock_guard<std::mutex> lock(setup);
+    if (done[dev].load(std::memory_order_relaxed)) return cudaSuccess;
     e = lun_kernels_init();
-    if (e == cudaSuccess && dev >= 0 && dev < 128) done[dev] = true;
+    if (e == cudaSuccess) done[dev].store(true, std::memory_order_release);
     return e;
 }
 

@@ -2,6 +2,8 @@
 #include <cudaTypedefs.h>
 #include <string.h>
 
+#include <atomic>
+
 #include "decode_mega.cuh"
 #include "kernels.h"
 
@@ -45,16 +47,18 @@ cudaError_t lun_down_slice_map(void *map, const uint8_t *down0, size_t layer_str
 cudaError_t lun_launch_decode_mega(const MegaParams &p, const void *down_map, int sm_count, cudaStream_t stream)
 {
     if (!lun_mega_supported(sm_count)) return cudaErrorInvalidConfiguration;
-    static bool attribute_set[128] = {};
+    // the shared-memory opt-in, once per device (atomic flags: callers may be on
+    // several threads; setting the attribute twice is harmless)
+    static std::atomic<bool> attribute_set[128];
     int device = 0;
     cudaError_t e = cudaGetDevice(&device);
     if (e != cudaSuccess) return e;
     if (device < 0 || device >= 128) return cudaErrorInvalidDevice;
-    if (!attribute_set[device]) {
+    if (!attribute_set[device].load(std::memory_order_acquire)) {
         e = cudaFuncSetAttribute(decode_mega_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  kMegaSmemBytes);
         if (e != cudaSuccess) return e;
-        attribute_set[device] = true;
+        attribute_set[device].store(true, std::memory_order_release);
     }
     // every CTA must be resident at once (grid barriers): one per SM
     int per_sm = 0;

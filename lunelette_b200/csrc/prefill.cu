@@ -1,6 +1,7 @@
 // Launchers of the tcgen05 prefill projections (prefill_gemm.cuh).
 #include <cudaTypedefs.h>
 #include <string.h>
+#include <atomic>
 
 #include "kernels.h"
 #include "launch.h"
@@ -74,16 +75,18 @@ static cudaError_t weight_tensor_map(CUtensorMap *map, const uint8_t *W, int row
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// The GEMM's shared-memory opt-in, once per device (atomic flags: callers may
+// be on several threads; setting the attribute twice is harmless).
 static cudaError_t prefill_setup()
 {
-    static bool done[128] = {};
+    static std::atomic<bool> done[128];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
-    if (done[dev]) return cudaSuccess;
+    if (done[dev].load(std::memory_order_acquire)) return cudaSuccess;
     e = cudaFuncSetAttribute(prefill_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kP2SmemBytes);
-    if (e == cudaSuccess) done[dev] = true;
+    if (e == cudaSuccess) done[dev].store(true, std::memory_order_release);
     return e;
 }
 

@@ -1,10 +1,12 @@
 /* Host runtime (C11) behind include/metal.h for the B200 backend.
  *
- * Same contract and state machine as the reference's src/metal_runtime.m:
- * argument errors are rejected before any mutation; an execution, allocation or
- * non-finite failure leaves the sequence invalid until reset; checkpoints hold
- * host logits plus a length, guarded by a never-recycled context identity and a
- * per-context epoch. The device work goes through device.h.
+ * It serves the contract that include/metal.h states (the reference's
+ * include/metal.h:74-120, implemented there by src/metal_runtime.m:349-575):
+ * arguments are checked before anything changes; a failed or non-finite
+ * device step leaves the sequence unusable until reset; a checkpoint is the
+ * published length plus a host copy of its logits, accepted back only by the
+ * context and epoch that made it. The sequence is one state value (seq_state)
+ * and the device work goes through device.h.
  */
 #include "metal.h"
 
@@ -21,20 +23,32 @@
 
 #define LUN_API __attribute__((visibility("default")))
 
+/* Where a context's sequence stands. The contract in include/metal.h is a small
+ * state machine; keeping it as one explicit value (instead of separate flags)
+ * makes every transition visible at the place it happens:
+ *   SEQ_EMPTY        after create/reset: length 0, prefill allowed
+ *   SEQ_PUBLISHED    length > 0 and the host logits belong to the last position
+ *   SEQ_UNPUBLISHED  length > 0, KV valid, but the host logits are not the
+ *                    endpoint's (after lunelette_cuda_decode_loop)
+ *   SEQ_BROKEN       a device step failed or produced a non-finite logit; only
+ *                    reset leaves this state */
+typedef enum { SEQ_EMPTY, SEQ_PUBLISHED, SEQ_UNPUBLISHED, SEQ_BROKEN } seq_state;
+
 struct lunelette_metal {
     lun_device *device;
     lunelette_metal_limits limits;
     lunelette_metal_prefill_mode prefill;
     lunelette_metal_strategy strategy;
+    seq_state state;
     size_t length;
-    bool valid, endpoint_valid;
-    uint64_t identity, epoch;
-    lunelette_metal_checkpoint *active; /* borrowed; the caller owns handles */
-    float *logits;                      /* pinned host logits owned by the device layer */
+    uint64_t identity;  /* never reused within the process; 0 = exhausted */
+    uint64_t epoch;     /* bumped by every successful checkpoint create */
+    lunelette_metal_checkpoint *current; /* caller-owned; the only handle restore accepts */
+    float *logits;      /* pinned host logits owned by the device layer */
 };
 
 struct lunelette_metal_checkpoint {
-    lunelette_metal *owner;
+    lunelette_metal *context;
     uint64_t identity, epoch;
     size_t length;
     float logits[LUN_VOCAB];
@@ -199,10 +213,10 @@ LUN_API lunelette_metal *lunelette_metal_create_configured(const char *path,
     const lunelette_metal_options *options, const lunelette_metal_limits *limits,
     char *error, size_t capacity)
 {
-    char fallback[512];
+    char local[512];
     if (!error || !capacity) {
-        error = fallback;
-        capacity = sizeof fallback;
+        error = local;
+        capacity = sizeof local;
     }
     error[0] = 0;
     lunelette_metal_limits resolved = limits ? *limits : (lunelette_metal_limits){256, 256};
@@ -246,7 +260,7 @@ LUN_API lunelette_metal *lunelette_metal_create_configured(const char *path,
     context->limits = resolved;
     context->prefill = selected.prefill;
     context->strategy = selected.strategy;
-    context->valid = true;
+    context->state = SEQ_EMPTY;
     context->logits = lun_device_host_logits(device);
     return context;
 fail:
@@ -312,71 +326,112 @@ LUN_API int lunelette_metal_reset(lunelette_metal *context, char *error, size_t 
 {
     if (!context) {
         if (error && capacity) {
-            snprintf(error, capacity, "reset requires a context");
+            snprintf(error, capacity, "lunelette: reset needs a context");
         }
         return -1;
     }
-    context->active = NULL;
-    context->endpoint_valid = false;
+    /* Old KV rows stay in device memory but length 0 makes them unreachable;
+     * the current checkpoint no longer describes this sequence. */
+    context->state = SEQ_EMPTY;
     context->length = 0;
-    context->valid = true;
+    context->current = NULL;
     return 0;
 }
 
-static int execute(lunelette_metal *context, const int64_t *ids, size_t count, bool prefill,
-    const float **logits, char *error, size_t capacity)
+/* Kinds of model call; they differ only in which sequence states admit them. */
+typedef enum { CALL_PREFILL, CALL_APPEND } call_kind;
+
+/* Argument and state check of one model call. Returns NULL when the call may
+ * run, else the reason, written into `buffer`. Nothing is changed here: a
+ * rejected call leaves the context exactly as it was. */
+static const char *check_call(const lunelette_metal *context, const int64_t *ids, size_t count,
+    call_kind kind, const float *const *logits, char *buffer, size_t size)
 {
-    char fallback[512];
-    if (!error || !capacity) {
-        error = fallback;
-        capacity = sizeof fallback;
+    if (!context || !ids || !logits) {
+        return "lunelette: context, ids and logits output are required";
     }
-    if (logits) {
-        *logits = NULL;
+    if (context->state == SEQ_BROKEN) {
+        return "lunelette: sequence is invalid after a failed call; reset required";
     }
-    if (!context || !logits || !ids || !count || count > context->limits.block ||
-        count > context->limits.context || !context->valid ||
-        context->length > context->limits.context - count ||
-        (prefill ? context->length != 0 : context->length == 0)) {
-        snprintf(error, capacity, "sequence rejected: require reset/valid IDs and "
-            "configured block/context capacity");
-        return -1;
+    if (count == 0 || count > context->limits.block) {
+        snprintf(buffer, size, "lunelette: %zu ids in one call; the profile allows 1..%zu", count,
+            context->limits.block);
+        return buffer;
+    }
+    if (kind == CALL_PREFILL && context->state != SEQ_EMPTY) {
+        snprintf(buffer, size, "lunelette: prefill needs an empty sequence (length is %zu); reset first",
+            context->length);
+        return buffer;
+    }
+    if (kind == CALL_APPEND && context->state == SEQ_EMPTY) {
+        return "lunelette: append/decode needs a prefilled sequence";
+    }
+    if (count > context->limits.context || context->length > context->limits.context - count) {
+        snprintf(buffer, size, "lunelette: %zu + %zu positions exceed the context of %zu",
+            context->length, count, context->limits.context);
+        return buffer;
     }
     for (size_t i = 0; i < count; i++) {
         if (ids[i] < 0 || ids[i] >= LUN_VOCAB) {
-            snprintf(error, capacity, "invalid token ID at position %zu", i);
-            return -1;
+            snprintf(buffer, size, "lunelette: token id %lld at index %zu is outside [0, %d)",
+                (long long)ids[i], i, LUN_VOCAB);
+            return buffer;
         }
     }
-    /* Nothing is published until the device work and the finite check succeed;
-     * a failure also drops the checkpoint, a success keeps it. */
-    lunelette_metal_checkpoint *checkpoint = context->active;
-    context->active = NULL;
-    context->endpoint_valid = false;
-    context->valid = false;
-    const float *output = NULL;
-    int nonfinite = 0;
+    return NULL;
+}
+
+/* One model call (prefill, append or decode). The sequence is marked broken
+ * before the device runs, so every failure path below leaves it broken; only a
+ * finished step with finite logits moves it to SEQ_PUBLISHED. The current
+ * checkpoint survives a successful call (restore rewinds to it) and is dropped
+ * by a failed one. */
+static int run_call(lunelette_metal *context, const int64_t *ids, size_t count, call_kind kind,
+    const float **logits, char *error, size_t capacity)
+{
+    char local[512];
+    if (!error || !capacity) {
+        error = local;
+        capacity = sizeof local;
+    }
     error[0] = 0;
-    if (lun_device_run(context->device, ids, count, context->length, &output, &nonfinite, error,
-            capacity)) {
-        size_t used = strlen(error);
-        snprintf(error + used, capacity - used, "; reset required");
+    if (logits) {
+        *logits = NULL;
+    }
+    char reason[256];
+    const char *rejected = check_call(context, ids, count, kind, logits, reason, sizeof reason);
+    if (rejected) {
+        snprintf(error, capacity, "%s", rejected);
         return -1;
     }
-    if (nonfinite) {
-        for (size_t i = 0; i < LUN_VOCAB; i++) {
-            if (!isfinite(output[i])) {
-                snprintf(error, capacity, "nonfinite logit %zu; reset required", i);
-                return -1;
-            }
+    lunelette_metal_checkpoint *keep = context->current;
+    context->current = NULL;
+    context->state = SEQ_BROKEN;
+    const float *output = NULL;
+    int flagged = 0;
+    if (lun_device_run(context->device, ids, count, context->length, &output, &flagged, error,
+            capacity)) {
+        size_t used = strlen(error);
+        if (used + 1 < capacity) {
+            snprintf(error + used, capacity - used, "%sreset required", used ? "; " : "");
         }
-        snprintf(error, capacity, "nonfinite logit; reset required");
+        return -1;
+    }
+    if (flagged) {
+        size_t bad = 0;
+        while (bad < LUN_VOCAB && isfinite(output[bad])) {
+            bad++;
+        }
+        if (bad < LUN_VOCAB) {
+            snprintf(error, capacity, "lunelette: logit %zu is not finite; reset required", bad);
+        } else {
+            snprintf(error, capacity, "lunelette: the head reported a non-finite value; reset required");
+        }
         return -1;
     }
     context->length += count;
-    context->valid = true;
-    context->endpoint_valid = true;
-    context->active = checkpoint;
+    context->state = SEQ_PUBLISHED;
+    context->current = keep;
     *logits = output;
     return 0;
 }
@@ -384,61 +439,74 @@ static int execute(lunelette_metal *context, const int64_t *ids, size_t count, b
 LUN_API int lunelette_metal_prefill(lunelette_metal *context, const int64_t *ids, size_t count,
     const float **logits, char *error, size_t capacity)
 {
-    return execute(context, ids, count, true, logits, error, capacity);
+    return run_call(context, ids, count, CALL_PREFILL, logits, error, capacity);
 }
 
 LUN_API int lunelette_metal_decode(lunelette_metal *context, int64_t token,
     const float **logits, char *error, size_t capacity)
 {
-    return execute(context, &token, 1, false, logits, error, capacity);
+    return run_call(context, &token, 1, CALL_APPEND, logits, error, capacity);
 }
 
 LUN_API int lunelette_metal_append(lunelette_metal *context, const int64_t *ids, size_t count,
     const float **logits, char *error, size_t capacity)
 {
-    return execute(context, ids, count, false, logits, error, capacity);
+    return run_call(context, ids, count, CALL_APPEND, logits, error, capacity);
 }
 
+static void put_error(char *error, size_t capacity, const char *message)
+{
+    if (error && capacity) {
+        snprintf(error, capacity, "%s", message);
+    }
+}
+
+/* A checkpoint is the published endpoint: its length and a copy of its logits.
+ * No KV is copied, because a later restore only shortens the sequence, and the
+ * rows below the saved length are never rewritten while this handle is current
+ * (appends write at the end; reset drops the handle). */
 LUN_API int lunelette_metal_checkpoint_create(lunelette_metal *context,
     lunelette_metal_checkpoint **checkpoint, char *error, size_t capacity)
 {
     if (checkpoint) {
         *checkpoint = NULL;
     }
-    if (!context || !checkpoint || !context->identity || !context->valid ||
-        !context->endpoint_valid || !context->length ||
-        context->length > context->limits.context || context->epoch == UINT64_MAX) {
-        if (error && capacity) {
-            snprintf(error, capacity, "checkpoint requires valid endpoint/available epoch");
-        }
+    if (!context || !checkpoint) {
+        put_error(error, capacity, "checkpoint: context and output handle are required");
+        return -1;
+    }
+    if (context->state != SEQ_PUBLISHED || context->length == 0 ||
+        context->length > context->limits.context || context->identity == 0) {
+        put_error(error, capacity, "checkpoint: needs a valid sequence with published logits");
+        return -1;
+    }
+    if (context->epoch == UINT64_MAX) {
+        put_error(error, capacity, "checkpoint: epoch counter exhausted; handle not replaced");
         return -1;
     }
     for (size_t i = 0; i < LUN_VOCAB; i++) {
         if (!isfinite(context->logits[i])) {
             if (error && capacity) {
-                snprintf(error, capacity, "checkpoint nonfinite logit %zu", i);
+                snprintf(error, capacity, "checkpoint: endpoint logit %zu is not finite; reset required",
+                    i);
             }
-            context->valid = false;
-            context->endpoint_valid = false;
-            context->active = NULL;
+            context->state = SEQ_BROKEN;
+            context->current = NULL;
             return -1;
         }
     }
-    lunelette_metal_checkpoint *saved = malloc(sizeof *saved);
-    if (!saved) {
-        if (error && capacity) {
-            snprintf(error, capacity, "checkpoint allocation failed");
-        }
+    lunelette_metal_checkpoint *handle = malloc(sizeof *handle);
+    if (!handle) {
+        put_error(error, capacity, "checkpoint: out of host memory; previous handle kept");
         return -1;
     }
-    saved->owner = context;
-    saved->identity = context->identity;
-    saved->epoch = context->epoch + 1;
-    saved->length = context->length;
-    memcpy(saved->logits, context->logits, sizeof saved->logits);
-    context->epoch = saved->epoch;
-    context->active = saved;
-    *checkpoint = saved;
+    handle->context = context;
+    handle->identity = context->identity;
+    handle->epoch = ++context->epoch;
+    handle->length = context->length;
+    memcpy(handle->logits, context->logits, sizeof handle->logits);
+    context->current = handle;
+    *checkpoint = handle;
     return 0;
 }
 
@@ -449,18 +517,25 @@ LUN_API int lunelette_metal_checkpoint_restore(lunelette_metal *context,
     if (logits) {
         *logits = NULL;
     }
-    if (!context || !logits || !checkpoint || context->active != checkpoint ||
-        checkpoint->identity != context->identity || checkpoint->epoch != context->epoch ||
-        !context->valid || context->length > context->limits.context || !checkpoint->length ||
-        checkpoint->length > context->limits.context || checkpoint->length > context->length) {
-        if (error && capacity) {
-            snprintf(error, capacity, "checkpoint stale, invalid or wrong context");
-        }
+    const char *why = NULL;
+    if (!context || !checkpoint || !logits) {
+        why = "checkpoint: context, handle and logits output are required";
+    } else if (context->current != checkpoint || checkpoint->identity != context->identity ||
+        checkpoint->epoch != context->epoch) {
+        why = "checkpoint: handle is not this context's current checkpoint";
+    } else if (context->state == SEQ_BROKEN || context->state == SEQ_EMPTY) {
+        why = "checkpoint: sequence was reset or invalidated since the handle was made";
+    } else if (checkpoint->length == 0 || checkpoint->length > context->length ||
+        checkpoint->length > context->limits.context) {
+        why = "checkpoint: saved length does not fit the current sequence";
+    }
+    if (why) {
+        put_error(error, capacity, why);
         return -1;
     }
     memcpy(context->logits, checkpoint->logits, sizeof checkpoint->logits);
     context->length = checkpoint->length;
-    context->endpoint_valid = true;
+    context->state = SEQ_PUBLISHED;
     *logits = context->logits;
     return 0;
 }
@@ -470,8 +545,8 @@ LUN_API void lunelette_metal_checkpoint_destroy(lunelette_metal_checkpoint *chec
     if (!checkpoint) {
         return;
     }
-    if (checkpoint->owner->active == checkpoint) {
-        checkpoint->owner->active = NULL;
+    if (checkpoint->context && checkpoint->context->current == checkpoint) {
+        checkpoint->context->current = NULL;
     }
     free(checkpoint);
 }
@@ -481,10 +556,10 @@ LUN_API void lunelette_metal_checkpoint_destroy(lunelette_metal_checkpoint *chec
 LUN_API int lunelette_cuda_validate_checkpoint(const char *path,
     lunelette_metal_strategy strategy, char *error, size_t capacity)
 {
-    char fallback[512];
+    char local[512];
     if (!error || !capacity) {
-        error = fallback;
-        capacity = sizeof fallback;
+        error = local;
+        capacity = sizeof local;
     }
     error[0] = 0;
     if (strategy != LUNELETTE_METAL_RESIDENT_FP32 &&
@@ -545,31 +620,31 @@ LUN_API size_t lunelette_cuda_length(const lunelette_metal *context)
 LUN_API int lunelette_cuda_decode_loop(lunelette_metal *context, int64_t first_token, size_t steps,
     int64_t *tokens, float *milliseconds, int *launches, char *error, size_t capacity)
 {
-    char fallback[512];
+    char local[512];
     if (!error || !capacity) {
-        error = fallback;
-        capacity = sizeof fallback;
+        error = local;
+        capacity = sizeof local;
     }
-    if (!context || !tokens || !steps || !context->valid || !context->length ||
-        context->length > context->limits.context - steps || first_token < 0 ||
-        first_token >= LUN_VOCAB) {
-        snprintf(error, capacity, "decode loop rejected: require a valid non-empty sequence, "
-            "a valid token and room for every step");
+    error[0] = 0;
+    if (!context || !tokens || !steps || first_token < 0 || first_token >= LUN_VOCAB ||
+        (context->state != SEQ_PUBLISHED && context->state != SEQ_UNPUBLISHED) ||
+        steps > context->limits.context - context->length) {
+        snprintf(error, capacity, "decode loop: needs a prefilled valid sequence, a token id in "
+            "[0, %d) and room for %zu more positions", LUN_VOCAB, steps);
         return -1;
     }
-    lunelette_metal_checkpoint *checkpoint = context->active;
-    context->active = NULL;
-    context->endpoint_valid = false;
-    context->valid = false;
+    lunelette_metal_checkpoint *keep = context->current;
+    context->current = NULL;
+    context->state = SEQ_BROKEN;
     if (lun_device_decode_loop(context->device, first_token, context->length, steps, tokens,
             milliseconds, launches, error, capacity)) {
         return -1;
     }
-    /* The KV cache now holds `steps` more positions; the host logits were not
-     * refreshed, so there is no published endpoint until the next call. */
+    /* The KV cache holds `steps` more positions; the host logits were not
+     * refreshed, so no endpoint is published until the next model call. */
     context->length += steps;
-    context->valid = true;
-    context->active = checkpoint;
+    context->state = SEQ_UNPUBLISHED;
+    context->current = keep;
     return 0;
 }
 

@@ -140,6 +140,16 @@ int oracle_yarn(uint32_t position, float cosine[128], float sine[128])
 /* One output of `project` / `project_fp8`: lane-strided Kahan partials, then
  * simd_sum (src/metal_kernels.metal:7-27, 154-177). w holds already-scaled FP32
  * weights (weight(code, scale) in the FP8 case). */
+/* The oracle's hot loops are compiled for several vector widths and the widest
+ * the host supports is picked at load time; each lane's arithmetic is the same
+ * scalar FP32 sequence whatever the width (no contraction: -ffp-contract=off). */
+#if defined(__x86_64__) && defined(__GNUC__) && !defined(__clang__)
+#define ORACLE_CLONES __attribute__((target_clones("avx512f", "avx2", "default")))
+#else
+#define ORACLE_CLONES
+#endif
+
+ORACLE_CLONES
 static float kahan_dot(const float *w, const float *x, size_t cols)
 {
     float sum[LANES] = {0}, correction[LANES] = {0};
@@ -161,6 +171,45 @@ static float kahan_dot(const float *w, const float *x, size_t cols)
         sum[l] = next;
     }
     return lane_sum(sum);
+}
+
+/* kahan_dot for two inputs over the same weights: two independent chains per
+ * lane, each the exact operation sequence of kahan_dot, so each result equals
+ * kahan_dot's bit for bit (the weights are just read once for both). */
+ORACLE_CLONES
+static void kahan_dot_pair(const float *w, const float *x0, const float *x1, size_t cols, float *out0,
+    float *out1)
+{
+    float s0[LANES] = {0}, c0[LANES] = {0}, s1[LANES] = {0}, c1[LANES] = {0};
+    size_t full = cols / LANES * LANES;
+    for (size_t c = 0; c < full; c += LANES) {
+        for (int l = 0; l < LANES; l++) {
+            float p0 = w[c + l] * x0[c + l];
+            float v0 = p0 - c0[l];
+            float n0 = s0[l] + v0;
+            c0[l] = (n0 - s0[l]) - v0;
+            s0[l] = n0;
+            float p1 = w[c + l] * x1[c + l];
+            float v1 = p1 - c1[l];
+            float n1 = s1[l] + v1;
+            c1[l] = (n1 - s1[l]) - v1;
+            s1[l] = n1;
+        }
+    }
+    for (size_t l = 0; full + l < cols; l++) {
+        float p0 = w[full + l] * x0[full + l];
+        float v0 = p0 - c0[l];
+        float n0 = s0[l] + v0;
+        c0[l] = (n0 - s0[l]) - v0;
+        s0[l] = n0;
+        float p1 = w[full + l] * x1[full + l];
+        float v1 = p1 - c1[l];
+        float n1 = s1[l] + v1;
+        c1[l] = (n1 - s1[l]) - v1;
+        s1[l] = n1;
+    }
+    *out0 = lane_sum(s0);
+    *out1 = lane_sum(s1);
 }
 
 void oracle_project(const float *weights, const float *input, float *output,
@@ -193,7 +242,12 @@ void oracle_project_fp8(const unsigned char *packed, float scale, const float *i
             for (size_t c = 0; c < cols; c++) {
                 row_values[c] = table[codes[c]];
             }
-            for (size_t token = 0; token < count; token++) {
+            size_t token = 0;
+            for (; token + 1 < count; token += 2) {
+                kahan_dot_pair(row_values, input + token * cols, input + (token + 1) * cols, cols,
+                    &output[token * rows + row], &output[(token + 1) * rows + row]);
+            }
+            for (; token < count; token++) {
                 output[token * rows + row] = kahan_dot(row_values, input + token * cols, cols);
             }
         }
@@ -306,13 +360,19 @@ void oracle_attention(const float *query, const float *keys, const float *values
             if (probabilities) {
                 memcpy(probabilities + group * stride, row, stride * sizeof(float));
             }
-            for (size_t column = 0; column < 128; column++) {
-                float sum = 0;
-                for (size_t position = 0; position <= last; position++) {
-                    sum += row[position] * values[position * 1024 + (head / 4) * 128 + column];
+            /* every column accumulates over positions in ascending order, as
+             * the reference's per-column loop does; walking positions in the
+             * outer loop reads each value row contiguously and gives the same
+             * sums bit for bit */
+            float sums[128] = {0};
+            for (size_t position = 0; position <= last; position++) {
+                const float p = row[position];
+                const float *v = values + position * 1024 + (head / 4) * 128;
+                for (size_t column = 0; column < 128; column++) {
+                    sums[column] += p * v[column];
                 }
-                output[token * 4096 + head * 128 + column] = sum;
             }
+            memcpy(output + token * 4096 + head * 128, sums, sizeof sums);
         }
         free(row);
     }

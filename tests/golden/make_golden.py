@@ -1,9 +1,10 @@
 """Regenerate the committed golden fixtures in this directory.
 
-Run in a container that has the reference checkout (default /root/reference)
-and the reference checker built by `make -C oracle` (oracle/_ref/libref.so):
+Run where a reference checkout exists, with the reference checker built by
+`make -C oracle REF=<checkout>` (oracle/_ref/libref.so), naming the checkout:
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <checkout>
+    LUNELETTE_REFERENCE=<checkout> python tests/golden/make_golden.py
 
 Outputs (small JSON, committed so the GPU box needs no reference checkout):
   fp8_golden.json   all 256 E4M3FN codes -> FP32 bits, parsed as data from the
@@ -111,8 +112,11 @@ def greedy_cases(lib):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("LUNELETTE_REFERENCE"),
+                    help="reference checkout (default: $LUNELETTE_REFERENCE)")
     args = ap.parse_args()
+    if not args.ref or not os.path.isdir(args.ref):
+        ap.error("name the reference checkout with --ref or LUNELETTE_REFERENCE")
     lib = ctypes.CDLL(os.path.join(REPO, "oracle", "_ref", "libref.so"))
     fp8 = parse_fp8(args.ref)
     lib.st_f8_e4m3_to_f32.argtypes = [ctypes.c_ubyte]

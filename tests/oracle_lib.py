@@ -157,6 +157,26 @@ def load():
     return Oracle(ctypes.CDLL(PATH))
 
 
+SYNTH_PATH = os.path.join(ORACLE_DIR, "libsynth.so")
+
+
+def synth_checkpoint(path, seed=0):
+    """Write the seeded synthetic checkpoint with oracle/libsynth.so: the same
+    writer as the product library's lunelette_cuda_synth_checkpoint, compiled on
+    its own without CUDA, for callers that must not load the product library
+    (the benchmark's CPU reference leg)."""
+    if not os.path.exists(SYNTH_PATH):
+        subprocess.run(["make", "-C", ORACLE_DIR, "synth"], check=True, capture_output=True)
+    lib = ctypes.CDLL(SYNTH_PATH)
+    fn = lib.lunelette_cuda_synth_checkpoint
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_char_p, ctypes.c_uint64, ctypes.c_char_p, SZ]
+    err = ctypes.create_string_buffer(512)
+    if fn(os.fsencode(path), seed, err, 512):
+        raise RuntimeError(err.value.decode())
+    return path
+
+
 def greedy(logits):
     """argmax with strict '>' (lowest id wins ties), as src/generation.c:8-34."""
     return int(np.argmax(logits))

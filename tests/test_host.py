@@ -101,6 +101,42 @@ def test_product_yarn_bitwise_equals_reference(lib):
     assert lib.lunelette_cuda_yarn(262144, c.ctypes.data, s.ctypes.data) == -1
 
 
+def test_calls_without_a_context_fail_before_any_work(lib):
+    """The contract's argument rules on the host (include/metal.h:74-120): every
+    mutating call and checkpoint call rejects a NULL context, clears the logits
+    output and writes a diagnostic; NULL/0 error buffers are accepted."""
+    err = ctypes.create_string_buffer(512)
+    logits = ctypes.c_void_p(1)
+    ids = (ctypes.c_int64 * 2)(1, 2)
+    for call in (lambda: lib.lunelette_metal_append(None, ids, 2, ctypes.byref(logits), err, 512),
+                 lambda: lib.lunelette_metal_decode(None, 5, ctypes.byref(logits), err, 512),
+                 lambda: lib.lunelette_metal_prefill(None, ids, 2, ctypes.byref(logits), None, 0)):
+        logits.value = 1
+        assert call() == -1
+        assert logits.value is None
+    handle = ctypes.c_void_p(1)
+    assert lib.lunelette_metal_checkpoint_create(None, ctypes.byref(handle), err, 512) == -1
+    assert handle.value is None and err.value
+    logits.value = 1
+    assert lib.lunelette_metal_checkpoint_restore(None, None, ctypes.byref(logits), err, 512) == -1
+    assert logits.value is None and err.value
+    tokens = (ctypes.c_int64 * 4)()
+    assert lib.lunelette_cuda_decode_loop(None, 1, 4, tokens, None, None, err, 512) == -1
+    assert b"decode loop" in err.value
+
+
+def test_oracle_side_writer_matches_the_product_writer(checkpoint_path, tmp_path):
+    """The benchmark's CPU reference leg writes its input with oracle/libsynth.so
+    (no product library loaded): it must produce the product writer's file
+    byte for byte, so both legs read the same weights."""
+    import filecmp
+    from tests import oracle_lib
+    path = str(tmp_path / "synth.safetensors")
+    oracle_lib.synth_checkpoint(path, 0)
+    assert filecmp.cmp(path, checkpoint_path, shallow=False)
+    os.remove(path)
+
+
 def test_synthetic_checkpoint_admitted(checkpoint_path):
     for strategy in (L.RESIDENT_FP32, L.COMPACT_FP8_ARITHMETIC, L.COMPACT_FP8_LOOKUP):
         L.validate_checkpoint(checkpoint_path, strategy)

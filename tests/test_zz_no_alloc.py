@@ -30,7 +30,12 @@ def test_noalloc_matches_scratch_entry_point_twice(lib):
     torch.cuda.init()
     stream = torch.cuda.current_stream().cuda_stream
     err = ctypes.create_string_buffer(512)
-    cases = [(300, 1, 11), (1000, 5, 12)]  # both split over positions: the scratch is used
+    # (length, count, seed): one and five query rows split over positions (the
+    # scratch is used); 40 rows on the block path at a long context, where the
+    # split count is clamped to what the fixed scratch holds (3 splits x 40 x 32
+    # = 3840 of its 4096 slots); 100 and 128 rows, where the clamp leaves one
+    # split per key range
+    cases = [(300, 1, 11), (1000, 5, 12), (3000, 40, 13), (2500, 100, 14), (1200, 128, 15)]
     for length, count, seed in cases:
         rng = np.random.default_rng(seed)
         total = length + count
