@@ -161,6 +161,14 @@ int lunelette_cuda_batch_append(lunelette_cuda_batch *batch, int session, const 
 int lunelette_cuda_batch_decode(lunelette_cuda_batch *batch, const int *sessions, const int64_t *ids, size_t n,
     float *logits, int64_t *next, char *error, size_t capacity);
 /* Positions held by an open session (0 otherwise), and free pool positions. */
+/* Open a new session whose first `length` positions (1..the source's length)
+ * are the source session's: its full pages are shared (a page returns to the
+ * pool when its last session closes) and a partial last page is copied, so
+ * either session may append afterwards without affecting the other. Replaces
+ * re-prefilling a shared prefix; the reference reuses a prefix only within its
+ * one sequence, by rewinding (src/metal_runtime.m:494-575). */
+int lunelette_cuda_batch_fork(lunelette_cuda_batch *batch, int source, size_t length, int *session,
+    char *error, size_t capacity);
 size_t lunelette_cuda_batch_length(const lunelette_cuda_batch *batch, int session);
 size_t lunelette_cuda_batch_free_positions(const lunelette_cuda_batch *batch);
 

@@ -77,6 +77,7 @@ SIGNATURES = {
     "lunelette_cuda_batch_close": (ctypes.c_int, [P, ctypes.c_int]),
     "lunelette_cuda_batch_append": (ctypes.c_int, [P, ctypes.c_int, P, SZ, P, ctypes.c_char_p, SZ]),
     "lunelette_cuda_batch_decode": (ctypes.c_int, [P, P, P, SZ, P, P, ctypes.c_char_p, SZ]),
+    "lunelette_cuda_batch_fork": (ctypes.c_int, [P, ctypes.c_int, SZ, P, ctypes.c_char_p, SZ]),
     "lunelette_cuda_batch_length": (SZ, [P, ctypes.c_int]),
     "lunelette_cuda_batch_free_positions": (SZ, [P]),
     "lunelette_cuda_kv_copy": (ctypes.c_int, [P, SZ, SZ, P, P, SZ, SZ, P]),
@@ -325,6 +326,14 @@ class Batch:
                                                  lg.ctypes.data if logits else None, nxt.ctypes.data, err, 512):
             raise LuneletteError(err.value.decode())
         return (nxt, lg) if logits else nxt
+
+    def fork(self, source, length):
+        """A new session sharing the first `length` positions of `source`."""
+        err = _error()
+        s = ctypes.c_int()
+        if library().lunelette_cuda_batch_fork(self.handle, int(source), int(length), ctypes.byref(s), err, 512):
+            raise LuneletteError(err.value.decode())
+        return s.value
 
     def length(self, session):
         return library().lunelette_cuda_batch_length(self.handle, int(session))

@@ -75,6 +75,54 @@ __device__ __forceinline__ void l2_prefetch(const void *src, unsigned bytes)
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
+// L2 eviction policies (createpolicy): evict_first for bytes read once (after
+// the copy into shared memory the line is the first candidate for
+// replacement), evict_last for bytes fetched ahead of their use.
+__device__ __forceinline__ uint64_t l2_policy_evict_first()
+{
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_last()
+{
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
+}
+// bulk_g2s with an L2 cache policy
+__device__ __forceinline__ void bulk_g2s_hint(void *dst, const void *src, unsigned bytes, uint64_t *bar,
+                                              uint64_t policy)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+        "%4;" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+// tma_load_4d with an L2 cache policy (no multicast)
+__device__ __forceinline__ void tma_load_4d_hint(void *dst, const void *tmap, int c0, int c1, int c2, int c3,
+                                                 uint64_t *bar, uint64_t policy)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+        "{%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
+        "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ void l2_prefetch_hint(const void *src, unsigned bytes, uint64_t policy)
+{
+    asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(src), "r"(bytes), "l"(policy)
+                 : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_4d_hint(const void *tmap, int c0, int c1, int c2, int c3, uint64_t policy)
+{
+    asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile.L2::cache_hint [%0, {%1, %2, %3, %4}], %5;" ::"l"(
+                     tmap),
+                 "r"(c0), "r"(c1), "r"(c2), "r"(c3), "l"(policy)
+                 : "memory");
+}
+
 // Bounded wait on an mbarrier phase for one thread: polls until the phase with
 // `parity` completed, the CTA's abort word is set, or `limit` polls passed (then
 // it sets the abort word and *error). False when the wait did not see the phase.

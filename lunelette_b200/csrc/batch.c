@@ -9,7 +9,10 @@
  * Appends run one session at a time through the single-sequence path (the
  * tcgen05 GEMMs for blocks, the persistent kernel for one token); a decode step
  * takes one token of each of n sessions and runs the projections once for all
- * of them. Single caller per batch context, like lunelette_metal.
+ * of them. A session can be forked from a prefix of another: the new session
+ * shares the prefix's full pages (reference-counted; no session ever rewrites
+ * a position below its length) and gets its own copy of a partial last page.
+ * Single caller per batch context, like lunelette_metal.
  */
 #include "lunelette_cuda.h"
 
@@ -39,6 +42,7 @@ struct lunelette_cuda_batch {
     size_t context, block, max_sessions, pool_pages, row_pages;
     int *free_pages;
     size_t free_count;
+    unsigned *page_refs; /* sessions holding each pool page; 0 = on the free list */
     lun_session *sessions;
     int *meta_sessions, *meta_positions; /* per decode call */
 };
@@ -67,6 +71,7 @@ LUN_API void lunelette_cuda_batch_destroy(lunelette_cuda_batch *b)
     }
     free(b->sessions);
     free(b->free_pages);
+    free(b->page_refs);
     free(b->meta_sessions);
     free(b->meta_positions);
     free(b);
@@ -75,10 +80,10 @@ LUN_API void lunelette_cuda_batch_destroy(lunelette_cuda_batch *b)
 LUN_API lunelette_cuda_batch *lunelette_cuda_batch_create(const char *path, size_t max_sessions, size_t context,
     size_t pool_positions, size_t block, char *error, size_t capacity)
 {
-    char fallback[512];
+    char local[512];
     if (!error || !capacity) {
-        error = fallback;
-        capacity = sizeof fallback;
+        error = local;
+        capacity = sizeof local;
     }
     error[0] = 0;
     if (!path || !max_sessions || max_sessions > 65536 || !context || context > 4352 || block < 8 ||
@@ -97,10 +102,11 @@ LUN_API lunelette_cuda_batch *lunelette_cuda_batch_create(const char *path, size
     b->pool_pages = (pool_positions + LUN_PAGE - 1) / LUN_PAGE;
     b->row_pages = (context + LUN_PAGE - 1) / LUN_PAGE;
     b->free_pages = malloc(b->pool_pages * sizeof(int));
+    b->page_refs = calloc(b->pool_pages, sizeof(unsigned));
     b->sessions = calloc(max_sessions, sizeof(lun_session));
     b->meta_sessions = malloc(block * sizeof(int));
     b->meta_positions = malloc(block * sizeof(int));
-    if (!b->free_pages || !b->sessions || !b->meta_sessions || !b->meta_positions) {
+    if (!b->free_pages || !b->page_refs || !b->sessions || !b->meta_sessions || !b->meta_positions) {
         set_error(error, capacity, "batch: allocation failed");
         lunelette_cuda_batch_destroy(b);
         return NULL;
@@ -150,7 +156,10 @@ LUN_API int lunelette_cuda_batch_close(lunelette_cuda_batch *b, int session)
     }
     lun_session *s = &b->sessions[session];
     for (size_t i = s->npages; i > 0; i--) {
-        b->free_pages[b->free_count++] = s->pages[i - 1];
+        int page = s->pages[i - 1];
+        if (--b->page_refs[page] == 0) {
+            b->free_pages[b->free_count++] = page;
+        }
     }
     s->npages = 0;
     s->length = 0;
@@ -183,11 +192,59 @@ static int reserve(lunelette_cuda_batch *b, int session, size_t positions, char 
         return set_error(error, capacity, "batch: KV pool exhausted");
     }
     while (s->npages < need) {
-        s->pages[s->npages++] = b->free_pages[--b->free_count];
+        int page = b->free_pages[--b->free_count];
+        b->page_refs[page] = 1;
+        s->pages[s->npages++] = page;
     }
     if (lun_device_session_table(b->device, session, s->pages, s->npages)) {
         return set_error(error, capacity, "batch: page table upload failed");
     }
+    return 0;
+}
+
+LUN_API int lunelette_cuda_batch_fork(lunelette_cuda_batch *b, int source, size_t length, int *session,
+    char *error, size_t capacity)
+{
+    if (!b || !session || source < 0 || (size_t)source >= b->max_sessions || !b->sessions[source].open ||
+        length == 0 || length > b->sessions[source].length) {
+        return set_error(error, capacity, "batch fork: needs an open source session and 1..its length positions");
+    }
+    size_t slot = 0;
+    while (slot < b->max_sessions && b->sessions[slot].open) {
+        slot++;
+    }
+    if (slot == b->max_sessions) {
+        return set_error(error, capacity, "batch fork: every session is in use");
+    }
+    const lun_session *src = &b->sessions[source];
+    size_t shared = length / LUN_PAGE, partial = length % LUN_PAGE;
+    if (partial && b->free_count == 0) {
+        return set_error(error, capacity, "batch fork: KV pool exhausted");
+    }
+    lun_session *s = &b->sessions[slot];
+    for (size_t i = 0; i < shared; i++) {
+        s->pages[i] = src->pages[i];
+        b->page_refs[src->pages[i]]++;
+    }
+    s->npages = shared;
+    if (partial) {
+        int page = b->free_pages[--b->free_count];
+        b->page_refs[page] = 1;
+        s->pages[s->npages++] = page;
+        if (lun_device_copy_page(b->device, src->pages[shared], page, (int)partial)) {
+            s->open = true; /* let close return every page taken above */
+            lunelette_cuda_batch_close(b, (int)slot);
+            return set_error(error, capacity, "batch fork: partial page copy failed");
+        }
+    }
+    if (lun_device_session_table(b->device, (int)slot, s->pages, s->npages)) {
+        s->open = true;
+        lunelette_cuda_batch_close(b, (int)slot);
+        return set_error(error, capacity, "batch fork: page table upload failed");
+    }
+    s->open = true;
+    s->length = length;
+    *session = (int)slot;
     return 0;
 }
 

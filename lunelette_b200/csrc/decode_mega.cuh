@@ -222,6 +222,8 @@ __device__ __forceinline__ void produce(const MegaParams &p, const Ring &r, int 
     WarpCursor rc = {0, w, 0u, stream_span(p, 0)}, pc = rc;
     bool more = cursor_settle(p, rc, w, total), pf_more = cursor_settle(p, pc, w, total);
     const unsigned budget = p.l2_ahead / kMegaConsumerWarps;
+    const bool hint_ring = p.l2_hints & 1u, hint_ahead = p.l2_hints & 2u;
+    const uint64_t first_out = l2_policy_evict_first(), keep = l2_policy_evict_last();
     unsigned long long ring_bytes = 0, pf_bytes = 0;
     unsigned u = 0, idle = 0;
     while (__any_sync(kLanes, more)) {
@@ -231,10 +233,16 @@ __device__ __forceinline__ void produce(const MegaParams &p, const Ring &r, int 
             while (pf_more && pf_bytes < ring_bytes + ahead) {
                 const unsigned n = (unsigned)pc.sp.item_bytes;
                 if (pf_bytes >= ring_bytes) {  // not yet in the ring
-                    if (pc.sp.tma)
-                        tma_prefetch_4d(down_map, 0, pc.sp.first, pc.i * kDownItemTiles, pc.sp.tma - 1);
-                    else
+                    if (pc.sp.tma) {
+                        if (hint_ahead)
+                            tma_prefetch_4d_hint(down_map, 0, pc.sp.first, pc.i * kDownItemTiles, pc.sp.tma - 1, keep);
+                        else
+                            tma_prefetch_4d(down_map, 0, pc.sp.first, pc.i * kDownItemTiles, pc.sp.tma - 1);
+                    } else if (hint_ahead) {
+                        l2_prefetch_hint(pc.sp.src + (size_t)pc.i * n, n, keep);
+                    } else {
                         l2_prefetch(pc.sp.src + (size_t)pc.i * n, n);
+                    }
                 }
                 pf_bytes += n;
                 pc.i += kMegaConsumerWarps;
@@ -244,11 +252,19 @@ __device__ __forceinline__ void produce(const MegaParams &p, const Ring &r, int 
             if (!use || mbar_test_wait(&r.empty[slot], (use - 1) & 1)) {
                 const unsigned n = (unsigned)rc.sp.item_bytes;
                 mbar_expect_tx(&r.full[slot], n);
-                if (rc.sp.tma)
-                    tma_load_4d(r.slots + (size_t)slot * kSlotBytes, down_map, 0, rc.sp.first,
-                                rc.i * kDownItemTiles, rc.sp.tma - 1, &r.full[slot]);
-                else
-                    bulk_g2s(r.slots + (size_t)slot * kSlotBytes, rc.sp.src + (size_t)rc.i * n, n, &r.full[slot]);
+                uint8_t *dst = r.slots + (size_t)slot * kSlotBytes;
+                if (rc.sp.tma) {
+                    if (hint_ring)
+                        tma_load_4d_hint(dst, down_map, 0, rc.sp.first, rc.i * kDownItemTiles, rc.sp.tma - 1,
+                                         &r.full[slot], first_out);
+                    else
+                        tma_load_4d(dst, down_map, 0, rc.sp.first, rc.i * kDownItemTiles, rc.sp.tma - 1,
+                                    &r.full[slot]);
+                } else if (hint_ring) {
+                    bulk_g2s_hint(dst, rc.sp.src + (size_t)rc.i * n, n, &r.full[slot], first_out);
+                } else {
+                    bulk_g2s(dst, rc.sp.src + (size_t)rc.i * n, n, &r.full[slot]);
+                }
                 ring_bytes += n;
                 rc.i += kMegaConsumerWarps;
                 more = cursor_settle(p, rc, w, total);

@@ -65,6 +65,7 @@ struct lun_device {
     bool down_map_ready = false;
     unsigned mega_tag = 1;                    // tag of the next launch's first layer (never 0)
     unsigned l2_ahead = 0;              // persistent kernel's L2 lookahead (bytes per CTA)
+    unsigned l2_hints = 0;              // persistent kernel's L2 eviction hints (MegaParams::l2_hints)
     int *mega_error = nullptr, *h_error = nullptr;
     float *arg_val = nullptr;
     int *arg_idx = nullptr;
@@ -226,6 +227,9 @@ static lun_device *create_device(size_t context, size_t kv_pages, size_t block, 
         // lookaheads measured slower (prefetched lines evicted before use)
         const char *ahead = getenv("LUNELETTE_L2_AHEAD_KB");
         d->l2_ahead = (ahead ? (unsigned)strtoul(ahead, nullptr, 10) : 128u) << 10;
+        // L2 eviction hints of the persistent kernel's weight stream (MegaParams::l2_hints)
+        const char *hints = getenv("LUNELETTE_L2_HINTS");
+        d->l2_hints = hints ? (unsigned)strtoul(hints, nullptr, 10) : 0u;
     }
     what = "pinned host buffers";
     if ((e = cudaMallocHost((void **)&d->h_step, sizeof(StepParams))) != cudaSuccess ||
@@ -323,6 +327,26 @@ extern "C" int lun_device_use_session(lun_device *d, int session)
     if (!d->session_tables || session < 0 || session >= d->max_sessions) return -1;
     d->page_table = d->session_tables + (size_t)session * d->session_pages;
     return 0;
+}
+
+extern "C" int lun_device_copy_page(lun_device *d, int src_page, int dst_page, int slots)
+{
+    if (!d->d_meta || src_page < 0 || src_page >= d->num_pages || dst_page < 0 || dst_page >= d->num_pages ||
+        src_page == dst_page || slots < 1 || slots > kPage)
+        return -1;
+    if (cudaSetDevice(d->ordinal) != cudaSuccess || cudaStreamSynchronize(d->stream) != cudaSuccess) return -1;
+    // the pair goes through the batch metadata words (free between calls)
+    const int pair[2] = {src_page, dst_page};
+    if (cudaMemcpy(d->d_meta, pair, sizeof pair, cudaMemcpyHostToDevice) != cudaSuccess) return -1;
+    KvCopyParams p;
+    p.kv = d->kv;
+    p.num_pages = d->num_pages;
+    p.src_pages = d->d_meta;
+    p.dst_pages = d->d_meta + 1;
+    p.pairs = 1;
+    p.last_slots = slots;
+    if (lun_launch_kv_copy(p, kLayers, d->stream) != cudaSuccess) return -1;
+    return cudaStreamSynchronize(d->stream) == cudaSuccess ? 0 : -1;
 }
 
 extern "C" void lun_device_destroy(lun_device *d)
@@ -719,6 +743,7 @@ static cudaError_t launch_mega(lun_device *d, int steps)
     p.steps = steps;
     p.timeline = d->record_timeline ? d->timeline : nullptr;
     p.l2_ahead = d->l2_ahead;
+    p.l2_hints = d->l2_hints;
     cudaError_t e;
     if (!d->down_map_ready) {
         if ((e = lun_down_slice_map(d->down_map, layer_base(d, 0) + kLayerQKV + kLayerO + kLayerGateUp,

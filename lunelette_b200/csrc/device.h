@@ -74,6 +74,10 @@ lun_device *lun_device_create_batch(size_t pool_pages, size_t session_context, s
 int lun_device_session_table(lun_device *d, int session, const int *pages, size_t n);
 /* Single-sequence calls (lun_device_run) run on this session's pages. */
 int lun_device_use_session(lun_device *d, int session);
+/* Copy the first `slots` (1..64) positions of pool page src_page to dst_page,
+ * K and V of every layer (copy-on-write of a partial page when a session is
+ * forked from another's prefix). Synchronous. */
+int lun_device_copy_page(lun_device *d, int src_page, int dst_page, int slots);
 /* One decode step for n tokens of n sessions at their positions; greedy ids
  * into next, logits (n x 131072) when not NULL. */
 int lun_device_batch_decode(lun_device *d, const int *sessions, const int64_t *ids, const int *positions,

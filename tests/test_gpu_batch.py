@@ -104,3 +104,57 @@ def test_batch_decode_many_ragged_sessions(lib, checkpoint_path):
             assert_close(lg1[k], w1, "session %d step 1" % k)
             w2 = rt.decode(int(step1[k])).copy()
             assert_close(lg2[k], w2, "session %d step 2" % k)
+
+
+def test_forked_sessions_share_a_prefix_and_diverge(lib, checkpoint_path, oracle):
+    """lunelette_cuda_batch_fork: sessions forked from a 300-position prefix (a
+    partial last page: copied) and from its first 256 positions (whole pages:
+    shared) continue independently; every logits vector against the oracle on
+    the same full sequence, also after the source session is closed (its
+    shared pages stay alive while a fork holds them), and every page returns to
+    the pool at the end."""
+    rng = np.random.default_rng(505)
+    prefix = rng.integers(1000, 131072, 300)
+    users = [rng.integers(1000, 131072, n) for n in (40, 17, 33)]
+    with L.Batch(checkpoint_path, max_sessions=4, context=4352, pool_positions=2048, block=256) as b:
+        free0 = b.free_positions()
+        a = b.open()
+        b.append(a, prefix[:256])
+        b.append(a, prefix[256:])
+        full = b.fork(a, 300)   # pages 0-3 shared, page 4 (44 positions) copied
+        whole = b.fork(a, 256)  # pages 0-3 shared
+        assert b.length(full) == 300 and b.length(whole) == 256
+        # 5 pages for a, one more for the copied partial page
+        assert b.free_positions() == free0 - 6 * 64
+        got = {full: [b.append(full, users[0]).copy()], a: [b.append(a, users[1]).copy()],
+               whole: [b.append(whole, users[2]).copy()]}
+        toks = {s: greedy(v[0]) for s, v in got.items()}
+        order = [full, a, whole]
+        for _ in range(2):
+            nxt, lg = b.decode(order, [toks[s] for s in order], logits=True)
+            for i, s in enumerate(order):
+                got[s].append(lg[i].copy())
+                toks[s] = int(nxt[i])
+        b.close_session(a)
+        for _ in range(2):  # the forks keep decoding on the shared pages
+            nxt, lg = b.decode([full, whole], [toks[full], toks[whole]], logits=True)
+            for i, s in enumerate((full, whole)):
+                got[s].append(lg[i].copy())
+                toks[s] = int(nxt[i])
+        b.close_session(full)
+        b.close_session(whole)
+        assert b.free_positions() == free0
+    m = oracle.open_model(checkpoint_path, 4352)
+    try:
+        m.forward(prefix)
+        for s, start, user in ((full, 300, users[0]), (a, 300, users[1]), (whole, 256, users[2])):
+            m.rewind(start)
+            want, _, _ = m.forward(user)
+            seq = got[s]
+            assert_close(seq[0], want, "fork %d: appended block" % s)
+            for step, logits in enumerate(seq[1:]):
+                want, _, _ = m.forward([greedy(seq[step])])
+                assert_close(logits, want, "fork %d: decode step %d" % (s, step))
+                assert greedy(logits) == greedy(want)
+    finally:
+        m.close()

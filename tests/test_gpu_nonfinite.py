@@ -1,17 +1,23 @@
 """Non-finite and out-of-range hidden values on both decode paths, against the
 reference's contract (include/metal.h:79-86; src/metal_runtime.m:418-424 scans
-every logit and fails the call with "reset required"): a NaN anywhere in the
-step must fail it and leave the sequence unusable until reset, and a finite but
-huge hidden state must give the reference's finite logits.
+every logit and fails the call with "reset required"): a NaN must fail the
+call and leave the sequence unusable until reset, and a finite but huge hidden
+state must give the reference's finite logits.
 
 The persistent decode kernel sums each layer's output in 64-bit fixed point
-(range +-2^31). It flags a term it cannot hold and the host reruns that step
-on the FP32 kernels, so both paths must agree with the oracle here. The faults
-are made in the input file on the host (two embedding rows of a copy of the
-synthetic checkpoint are rewritten), never on the device:
-  BIG_TOKEN  its row times 2^30 (|x| ~ 2e7 > the fixed point's per-term limit
-             2^23): finite logits, compared with the oracle;
-  NAN_TOKEN  its row all NaN: the step fails, later calls fail until reset.
+(range +-2^31). It flags a term it cannot hold (non-finite, or not below 2^23)
+and the host reruns that step on the FP32 kernels, so both paths must agree
+with the oracle. The faults are made in the input file on the host, in copies
+of the synthetic checkpoint, never on the device:
+  huge  layer 0's post-attention norm gain set to 4096 (BF16 0x4580): the FFN
+        output, and so every later hidden state, is ~1e7..1e9 (above the fixed
+        point's per-term limit) but finite, at every position; logits stay
+        finite and are compared with the oracle on both paths;
+  nan   one embedding row set to NaN. The embedding is also the tied head, so
+        that token's logit is NaN in every call: the first call (a prefill, on
+        the FP32 kernels) must fail and leave the sequence invalid until reset.
+The persistent kernel's flag test is `!(fabsf(v) < 2^23)`, true for NaN and
+infinities as for huge values, so the huge case exercises the same check.
 """
 import json
 import os
@@ -25,7 +31,7 @@ from tests.oracle_lib import greedy
 
 pytestmark = pytest.mark.gpu
 
-BIG_TOKEN, NAN_TOKEN = 4242, 4343
+NAN_TOKEN = 4343
 MAX_ABS, REL_L2 = 2e-2, 1e-2
 
 
@@ -33,78 +39,100 @@ def rel_l2(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
-@pytest.fixture(scope="module")
-def patched_checkpoint(checkpoint_path, tmp_path_factory):
-    path = str(tmp_path_factory.mktemp("nonfinite") / "patched.safetensors")
-    shutil.copyfile(checkpoint_path, path)
-    with open(path, "r+b") as f:
+def patched_copy(src, dst, patch):
+    """Copy the checkpoint and rewrite bytes of named tensors: patch(name) ->
+    (byte offset within the tensor, bytes) or None."""
+    shutil.copyfile(src, dst)
+    with open(dst, "r+b") as f:
         n = int.from_bytes(f.read(8), "little")
         header = json.loads(f.read(n))
-        begin, _ = header["language_model.model.embed_tokens.weight"]["data_offsets"]
-        row_bytes = 3072 * 2
-        at = 8 + n + begin + BIG_TOKEN * row_bytes
-        f.seek(at)
-        row = np.frombuffer(f.read(row_bytes), np.uint16).copy()
-        normal = (row & 0x7F80) != 0  # zero and subnormal values keep their bits
-        row[normal] = row[normal] + np.uint16(30 << 7)  # exponent + 30: the value times 2^30, exactly
-        f.seek(at)
-        f.write(row.tobytes())
-        f.seek(8 + n + begin + NAN_TOKEN * row_bytes)
-        f.write(np.full(3072, 0x7FC0, np.uint16).tobytes())
+        for name, info in header.items():
+            if name == "__metadata__":
+                continue
+            change = patch(name)
+            if change is not None:
+                offset, data = change
+                f.seek(8 + n + info["data_offsets"][0] + offset)
+                f.write(data)
+    return dst
+
+
+def test_nan_logit_fails_the_call_until_reset(checkpoint_path, tmp_path, oracle, monkeypatch):
+    path = patched_copy(checkpoint_path, str(tmp_path / "nan.safetensors"), lambda name: (
+        NAN_TOKEN * 3072 * 2, np.full(3072, 0x7FC0, np.uint16).tobytes())
+        if name == "language_model.model.embed_tokens.weight" else None)
+    try:
+        ids = np.random.default_rng(57).integers(1000, 131072, 6).astype(np.int64)
+        for mega in ("1", "0"):
+            monkeypatch.setenv("LUNELETTE_MEGA", mega)
+            with L.Runtime(path) as rt:
+                with pytest.raises(L.LuneletteError, match="logit %d is not finite; reset required" % NAN_TOKEN):
+                    rt.prefill(ids)
+                with pytest.raises(L.LuneletteError, match="reset required"):
+                    rt.prefill(ids)  # the failed call left the sequence invalid
+                assert rt.length() == 0
+                rt.reset()
+                with pytest.raises(L.LuneletteError, match="not finite"):
+                    rt.prefill(ids[:1])
+        m = oracle.open_model(path, 256)
+        try:
+            with pytest.raises(RuntimeError, match="nonfinite logit %d" % NAN_TOKEN):
+                m.forward(ids)  # the reference arithmetic fails the same call
+        finally:
+            m.close()
+    finally:
+        os.remove(path)
+
+
+@pytest.fixture(scope="module")
+def huge_checkpoint(checkpoint_path, tmp_path_factory):
+    path = patched_copy(checkpoint_path, str(tmp_path_factory.mktemp("huge") / "huge.safetensors"),
+                        lambda name: (0, np.full(3072, 0x4580, np.uint16).tobytes())
+                        if name == "language_model.model.layers.0.post_attention_layernorm.weight" else None)
     yield path
     os.remove(path)
 
 
 @pytest.fixture(scope="module")
-def patched_oracle(oracle, patched_checkpoint):
-    m = oracle.open_model(patched_checkpoint, 256)
+def huge_oracle(oracle, huge_checkpoint):
+    m = oracle.open_model(huge_checkpoint, 256)
     yield m
     m.close()
 
 
 @pytest.mark.parametrize("mega", ["1", "0"])
-def test_huge_and_nan_hidden_values_follow_the_reference(patched_checkpoint, patched_oracle, monkeypatch,
-                                                         mega):
+def test_huge_hidden_values_match_the_oracle_on_both_paths(huge_checkpoint, huge_oracle, monkeypatch, mega):
     monkeypatch.setenv("LUNELETTE_MEGA", mega)
     ids = np.random.default_rng(55).integers(1000, 131072, 12).astype(np.int64)
-    patched_oracle.reset()
-    with L.Runtime(patched_checkpoint) as rt:
+    huge_oracle.reset()
+    with L.Runtime(huge_checkpoint) as rt:
+        rt.trace(True)
         got = rt.prefill(ids).copy()
-        want, _, _ = patched_oracle.forward(ids)
+        hidden = rt.trace_copy(0, len(ids))
+        rt.trace(False)
+        assert np.abs(hidden).max() > 2.0 ** 23  # the layer-0 output really is out of the fixed range
+        want, _, _ = huge_oracle.forward(ids)
         assert np.abs(got - want).max() <= MAX_ABS
-        # a finite step whose hidden state leaves the fixed-point range
-        for token in (BIG_TOKEN, int(greedy(want))):
-            got = rt.decode(token).copy()
-            want, _, _ = patched_oracle.forward([token])
+        tok = greedy(want)
+        for step in range(4):
+            got = rt.decode(tok).copy()
+            want, _, _ = huge_oracle.forward([tok])
             assert np.all(np.isfinite(got))
             err, rel = float(np.abs(got - want).max()), rel_l2(got, want)
-            assert err <= MAX_ABS and rel <= REL_L2, (token, err, rel)
+            assert err <= MAX_ABS and rel <= REL_L2, (step, err, rel)
             assert greedy(got) == greedy(want)
-        length = rt.length()
-        # a NaN step fails and the sequence stays invalid until reset
-        with pytest.raises(L.LuneletteError, match="reset required"):
-            rt.decode(NAN_TOKEN)
-        with pytest.raises(L.LuneletteError, match="reset required"):
-            rt.decode(int(ids[0]))
-        with pytest.raises(L.LuneletteError):
-            rt.checkpoint_create()
-        assert rt.length() == length
-        rt.reset()
-        again = rt.prefill(ids).copy()
-        assert np.all(np.isfinite(again))
-    # the oracle itself rejects the NaN step, as the reference does
-    with pytest.raises(RuntimeError, match="nonfinite"):
-        patched_oracle.forward([NAN_TOKEN])
+            tok = greedy(want)
 
 
-def test_decode_loop_reports_a_flagged_step(patched_checkpoint, monkeypatch):
+def test_decode_loop_reports_a_flagged_step(huge_checkpoint, monkeypatch):
     """The device-greedy loop cannot rerun a step on the FP32 kernels, so a step
-    whose hidden values leave the fixed-point range fails the call."""
+    whose hidden values leave the fixed-point range fails the call and leaves
+    the sequence invalid."""
     monkeypatch.setenv("LUNELETTE_MEGA", "1")
     ids = np.random.default_rng(56).integers(1000, 131072, 8).astype(np.int64)
-    with L.Runtime(patched_checkpoint) as rt:
-        rt.prefill(ids)
-        with pytest.raises(L.LuneletteError, match="fixed-point range|non-finite"):
-            rt.decode_loop(BIG_TOKEN, 4)
-        with pytest.raises(L.LuneletteError):
-            rt.decode(int(ids[0]))  # the failed loop left the sequence invalid
+    with L.Runtime(huge_checkpoint) as rt:
+        first = greedy(rt.prefill(ids))
+        with pytest.raises(L.LuneletteError, match="fixed-point range"):
+            rt.decode_loop(first, 4)
+        with pytest.raises(L.LuneletteError, match="reset required"):
+            rt.decode(first)
