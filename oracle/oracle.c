@@ -173,43 +173,41 @@ static float kahan_dot(const float *w, const float *x, size_t cols)
     return lane_sum(sum);
 }
 
-/* kahan_dot for two inputs over the same weights: two independent chains per
+/* kahan_dot for four inputs over the same weights: four independent chains per
  * lane, each the exact operation sequence of kahan_dot, so each result equals
- * kahan_dot's bit for bit (the weights are just read once for both). */
+ * kahan_dot's bit for bit. The Kahan update is a chain of four dependent
+ * additions per step; interleaving four inputs keeps the vector units busy
+ * instead of waiting on that chain (and reads each weight once for all four). */
+#define ORACLE_GROUP 4
 ORACLE_CLONES
-static void kahan_dot_pair(const float *w, const float *x0, const float *x1, size_t cols, float *out0,
-    float *out1)
+static void kahan_dot_group(const float *w, const float *x, size_t stride, size_t cols, float *out,
+    size_t out_stride)
 {
-    float s0[LANES] = {0}, c0[LANES] = {0}, s1[LANES] = {0}, c1[LANES] = {0};
+    float s[ORACLE_GROUP][LANES] = {{0}}, c[ORACLE_GROUP][LANES] = {{0}};
     size_t full = cols / LANES * LANES;
-    for (size_t c = 0; c < full; c += LANES) {
-        for (int l = 0; l < LANES; l++) {
-            float p0 = w[c + l] * x0[c + l];
-            float v0 = p0 - c0[l];
-            float n0 = s0[l] + v0;
-            c0[l] = (n0 - s0[l]) - v0;
-            s0[l] = n0;
-            float p1 = w[c + l] * x1[c + l];
-            float v1 = p1 - c1[l];
-            float n1 = s1[l] + v1;
-            c1[l] = (n1 - s1[l]) - v1;
-            s1[l] = n1;
+    for (size_t k = 0; k < full; k += LANES) {
+        for (int g = 0; g < ORACLE_GROUP; g++) {
+            const float *xg = x + g * stride + k;
+            for (int l = 0; l < LANES; l++) {
+                float product = w[k + l] * xg[l];
+                float value = product - c[g][l];
+                float next = s[g][l] + value;
+                c[g][l] = (next - s[g][l]) - value;
+                s[g][l] = next;
+            }
         }
     }
-    for (size_t l = 0; full + l < cols; l++) {
-        float p0 = w[full + l] * x0[full + l];
-        float v0 = p0 - c0[l];
-        float n0 = s0[l] + v0;
-        c0[l] = (n0 - s0[l]) - v0;
-        s0[l] = n0;
-        float p1 = w[full + l] * x1[full + l];
-        float v1 = p1 - c1[l];
-        float n1 = s1[l] + v1;
-        c1[l] = (n1 - s1[l]) - v1;
-        s1[l] = n1;
+    for (int g = 0; g < ORACLE_GROUP; g++) {
+        const float *xg = x + g * stride;
+        for (size_t l = 0; full + l < cols; l++) {
+            float product = w[full + l] * xg[full + l];
+            float value = product - c[g][l];
+            float next = s[g][l] + value;
+            c[g][l] = (next - s[g][l]) - value;
+            s[g][l] = next;
+        }
+        out[g * out_stride] = lane_sum(s[g]);
     }
-    *out0 = lane_sum(s0);
-    *out1 = lane_sum(s1);
 }
 
 void oracle_project(const float *weights, const float *input, float *output,
@@ -243,9 +241,9 @@ void oracle_project_fp8(const unsigned char *packed, float scale, const float *i
                 row_values[c] = table[codes[c]];
             }
             size_t token = 0;
-            for (; token + 1 < count; token += 2) {
-                kahan_dot_pair(row_values, input + token * cols, input + (token + 1) * cols, cols,
-                    &output[token * rows + row], &output[(token + 1) * rows + row]);
+            for (; token + ORACLE_GROUP <= count; token += ORACLE_GROUP) {
+                kahan_dot_group(row_values, input + token * cols, cols, cols, &output[token * rows + row],
+                    rows);
             }
             for (; token < count; token++) {
                 output[token * rows + row] = kahan_dot(row_values, input + token * cols, cols);

@@ -90,6 +90,8 @@ def test_reference_native_harness_capture_then_check(lib, checkpoint_path, tmp_p
                               capture_output=True, text=True, timeout=900)
         assert proc.returncode == 0, (mode, proc.stdout[-2000:], proc.stderr[-2000:])
         assert ("PASS native %s" % mode) in proc.stdout
-    # check compared 4 prompts x 8 steps x 2 reset cycles, every one bitwise exact
+    # check compared 4 prompts x 8 steps x 2 reset cycles, every one bitwise
+    # exact (its capture-file validation prints further exact=1 lines)
     assert "steps=64 cycles=2" in proc.stdout
-    assert proc.stdout.count("exact=1") == 64
+    assert "exact=0" not in proc.stdout
+    assert len([l for l in proc.stdout.splitlines() if l.startswith("check mode=mps cycle=")]) == 64
