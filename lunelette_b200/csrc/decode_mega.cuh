@@ -54,19 +54,7 @@ constexpr int kMegaSmemBytes =
 constexpr unsigned kSpinLimit = 1u << 22;
 constexpr int kPhasesPerStep = kLayers * 4 + 1;  // 4 FP8 phases per layer, then the head
 constexpr int kAttnMaxRanges = 18;               // position ranges per KV head (8 x 18 <= CTAs)
-constexpr int kHeadModeMax = 112;                // positions up to which attention runs per query head
-// Up to kHeadModeMax positions, attention and o are fused: CTA c < 128 computes
-// the attention of query head c / 4 and multiplies it by that head's 128
-// columns of o for the rows of quarter c % 4 (768 rows), reading those weights
-// as kOSliceItems items of kOSliceTiles tiles x one 1 KB block (a tensor-map
-// gather), and adds the 768 partial sums into the layer's fixed-point h.
-constexpr int kFusedCtas = kQueryHeads * 4;
-constexpr int kOSliceTiles = 12;
-constexpr int kOSliceRows = kHidden / 4;
-constexpr int kOSliceItems = kOSliceRows / kTileRows / kOSliceTiles;
-// floats into the fragment area where the fused path keeps the head's attention
-// output and the o row sums (past the attention's query and merge staging)
-constexpr int kFusedHeadOffset = 5120;
+constexpr int kHeadModeMax = 112;                // positions up to which each query head gets a CTA
 constexpr int kQStride = 36;                     // floats per staged query quarter (32 + pad)
 constexpr int kCmbStride = 132;                  // floats per (warp, head) attention partial
 // FFN in act slices: slice s (64 SwiGLU features, CTA s) takes the 16 gate/up
@@ -83,13 +71,8 @@ static_assert(kSliceTiles * kTileRows * kFfnSlices == kGateUpRows && kDownItemTi
                   kDownItems * kDownItemTiles * kTileRows == kHidden,
               "FFN slices cover gate/up and down, a down item fits a slot");
 static_assert(kActOffset + (64 + kHidden) * 4 <= kFragBytes, "act slice and down row sums fit the fragment area");
-static_assert(kOSliceItems * kOSliceTiles * kTileRows == kOSliceRows && kOSliceTiles * kBlockBytes <= kSlotBytes,
-              "o slices cover a quarter of the rows, an item fits a slot");
 static_assert((16 * kQStride + 2 * kHeadDim + kMegaConsumerWarps * 4 * kCmbStride) * 4 <= kFragBytes,
               "attention staging fits the fragment area");
-static_assert(16 * kQStride + 2 * kHeadDim + kMegaConsumerWarps * 4 * kCmbStride <= kFusedHeadOffset &&
-                  (kFusedHeadOffset + kHeadDim + kOSliceRows) * 4 <= kFragBytes,
-              "the fused path's head output and o row sums fit past the attention staging");
 
 // ---- small PTX wrappers (the mbarrier and bulk-copy ones are in async.cuh) ----
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p)
@@ -127,20 +110,14 @@ enum { kPhQKV, kPhO, kPhGateUp, kPhDown, kPhHead };
 // This CTA's share of one phase: `items` consecutive items of `item_bytes`
 // starting at src. FP8 phases: whole 8-row tiles from tile `first`, each
 // split into K-chunks; head: 2-row items of the BF16 embedding from row `first`;
-// tensor-map phases (map != kMapNone) gather item i through a 4-D map:
-//   kMapDown: box {0, first, 24 i, layer} of the down map (act slice `first`,
-//             tiles 24 i .. 24 i + 23);
-//   kMapO:    box {0, first, tile0 + 12 i, layer} of the o map (block `first`
-//             = the query head's 128 columns, tiles tile0 + 12 i ..).
-enum { kMapNone, kMapDown, kMapO };
+// down (tma = layer + 1): item i is the box {0, first, 24 i, layer} of the
+// down tensor map (act slice `first`, tiles 24 i .. 24 i + 23).
 struct PhaseSpan {
     const uint8_t *src;
     int items;
     int item_bytes;
     int first;
-    int map;
-    int layer;
-    int tile0;
+    int tma;
 };
 
 __device__ __forceinline__ void cta_range(int units, int &u0, int &u1)
@@ -152,11 +129,7 @@ __device__ __forceinline__ void cta_range(int units, int &u0, int &u1)
 // blocks per item: qkv, o, gate/up, down
 __host__ __device__ constexpr int item_blocks(int ph) { return ph == kPhO ? 8 : 12; }
 
-// Steps of a launch that run the fused attention + o path (the consumers'
-// choice, from the step's length, and the producers', from length0 + s).
-__device__ __forceinline__ bool fused_step(int length) { return length + 1 <= kHeadModeMax && gridDim.x >= kFusedCtas; }
-
-__device__ __forceinline__ PhaseSpan phase_span(const MegaParams &p, int layer, int ph, bool fused)
+__device__ __forceinline__ PhaseSpan phase_span(const MegaParams &p, int layer, int ph)
 {
     constexpr size_t lq = (size_t)kQKVRows * kHidden, lo = (size_t)kHidden * kQuery,
                      lg = (size_t)kGateUpRows * kHidden, ld = (size_t)kHidden * kInner;
@@ -164,21 +137,16 @@ __device__ __forceinline__ PhaseSpan phase_span(const MegaParams &p, int layer, 
         int g0, g1;
         cta_range(kVocab / 4, g0, g1);  // 4-row groups, two items each
         return {reinterpret_cast<const uint8_t *>(p.embedding) + (size_t)g0 * 4 * kHidden * 2, 2 * (g1 - g0),
-                2 * kHidden * 2, 4 * g0, kMapNone, 0, 0};
-    }
-    if (ph == kPhO && fused) {
-        if ((int)blockIdx.x >= kFusedCtas) return {nullptr, 0, kSlotBytes, 0, kMapNone, 0, 0};
-        return {nullptr, kOSliceItems, kOSliceTiles * kBlockBytes, (int)blockIdx.x >> 2, kMapO, layer,
-                ((int)blockIdx.x & 3) * (kOSliceRows / kTileRows)};
+                2 * kHidden * 2, 4 * g0};
     }
     const uint8_t *base = p.w8 + (size_t)layer * (lq + lo + lg + ld);
     if (ph == kPhGateUp || ph == kPhDown) {
         const int s = blockIdx.x;  // act slice of this CTA; CTAs past the last slice idle in the FFN
-        if (s >= kFfnSlices) return {base, 0, kSlotBytes, 0, kMapNone, 0, 0};
-        if (ph == kPhDown) return {nullptr, kDownItems, kDownItemTiles * 512, s, kMapDown, layer, 0};
+        if (s >= kFfnSlices) return {base, 0, kSlotBytes, 0, 0};
+        if (ph == kPhDown) return {nullptr, kDownItems, kDownItemTiles * 512, s, layer + 1};
         constexpr int nb = kHidden / kBlockCols, cb = item_blocks(kPhGateUp);
         return {base + lq + lo + (size_t)s * kSliceTiles * nb * kBlockBytes, kSliceTiles * (nb / cb),
-                cb * kBlockBytes, s * kSliceTiles, kMapNone, 0, 0};
+                cb * kBlockBytes, s * kSliceTiles, 0};
     }
     const uint8_t *m;
     int tiles, nb;
@@ -189,17 +157,15 @@ __device__ __forceinline__ PhaseSpan phase_span(const MegaParams &p, int layer, 
     const int cb = item_blocks(ph);
     int t0, t1;
     cta_range(tiles, t0, t1);
-    return {m + (size_t)t0 * nb * kBlockBytes, (t1 - t0) * (nb / cb), cb * kBlockBytes, t0, kMapNone, 0, 0};
+    return {m + (size_t)t0 * nb * kBlockBytes, (t1 - t0) * (nb / cb), cb * kBlockBytes, t0};
 }
 
-// Phase k of the launch's stream (steps repeat the same weights; step s runs
-// at length length0 + s, which decides whether its o phase is fused).
+// Phase k of the launch's stream (steps repeat the same weights).
 __device__ __forceinline__ PhaseSpan stream_span(const MegaParams &p, int k)
 {
-    const bool fused = fused_step(p.length0 + k / kPhasesPerStep);
     k %= kPhasesPerStep;
-    if (k == kLayers * 4) return phase_span(p, 0, kPhHead, false);
-    return phase_span(p, k >> 2, k & 3, fused);
+    if (k == kLayers * 4) return phase_span(p, 0, kPhHead);
+    return phase_span(p, k >> 2, k & 3);
 }
 
 struct Ring {
@@ -249,8 +215,7 @@ __device__ __forceinline__ bool cursor_settle(const MegaParams &p, WarpCursor &c
 // reads nothing ahead. Down items are tensor copies through down_map (24
 // pieces of 512 bytes, one per tile, gathered into one slot). A lane that sees
 // no free slot for kSpinLimit probes sets *error and stops.
-__device__ __forceinline__ void produce(const MegaParams &p, const Ring &r, int w, const void *down_map,
-                                        const void *o_map)
+__device__ __forceinline__ void produce(const MegaParams &p, const Ring &r, int w, const void *down_map)
 {
     constexpr unsigned kLanes = (1u << kMegaConsumerWarps) - 1;
     const int total = p.steps * kPhasesPerStep;
@@ -268,14 +233,11 @@ __device__ __forceinline__ void produce(const MegaParams &p, const Ring &r, int 
             while (pf_more && pf_bytes < ring_bytes + ahead) {
                 const unsigned n = (unsigned)pc.sp.item_bytes;
                 if (pf_bytes >= ring_bytes) {  // not yet in the ring
-                    if (pc.sp.map != kMapNone) {
-                        const bool down = pc.sp.map == kMapDown;
-                        const void *map = down ? down_map : o_map;
-                        const int c2 = down ? pc.i * kDownItemTiles : pc.sp.tile0 + pc.i * kOSliceTiles;
+                    if (pc.sp.tma) {
                         if (hint_ahead)
-                            tma_prefetch_4d_hint(map, 0, pc.sp.first, c2, pc.sp.layer, keep);
+                            tma_prefetch_4d_hint(down_map, 0, pc.sp.first, pc.i * kDownItemTiles, pc.sp.tma - 1, keep);
                         else
-                            tma_prefetch_4d(map, 0, pc.sp.first, c2, pc.sp.layer);
+                            tma_prefetch_4d(down_map, 0, pc.sp.first, pc.i * kDownItemTiles, pc.sp.tma - 1);
                     } else if (hint_ahead) {
                         l2_prefetch_hint(pc.sp.src + (size_t)pc.i * n, n, keep);
                     } else {
@@ -291,14 +253,13 @@ __device__ __forceinline__ void produce(const MegaParams &p, const Ring &r, int 
                 const unsigned n = (unsigned)rc.sp.item_bytes;
                 mbar_expect_tx(&r.full[slot], n);
                 uint8_t *dst = r.slots + (size_t)slot * kSlotBytes;
-                if (rc.sp.map != kMapNone) {
-                    const bool down = rc.sp.map == kMapDown;
-                    const void *map = down ? down_map : o_map;
-                    const int c2 = down ? rc.i * kDownItemTiles : rc.sp.tile0 + rc.i * kOSliceTiles;
+                if (rc.sp.tma) {
                     if (hint_ring)
-                        tma_load_4d_hint(dst, map, 0, rc.sp.first, c2, rc.sp.layer, &r.full[slot], first_out);
+                        tma_load_4d_hint(dst, down_map, 0, rc.sp.first, rc.i * kDownItemTiles, rc.sp.tma - 1,
+                                         &r.full[slot], first_out);
                     else
-                        tma_load_4d(dst, map, 0, rc.sp.first, c2, rc.sp.layer, &r.full[slot]);
+                        tma_load_4d(dst, down_map, 0, rc.sp.first, rc.i * kDownItemTiles, rc.sp.tma - 1,
+                                    &r.full[slot]);
                 } else if (hint_ring) {
                     bulk_g2s_hint(dst, rc.sp.src + (size_t)rc.i * n, n, &r.full[slot], first_out);
                 } else {
@@ -423,11 +384,11 @@ __device__ __forceinline__ long long float_to_fixed(float v) { return __float2ll
 
 // Rows [row0, row0 + n) of the layer input x -> shared memory, for an
 // epilogue; the loads overlap the fragment staging that follows. x is the
-// embedding row (emb) or the fixed-point sum fix that other CTAs wrote.
-__device__ __forceinline__ void stage_x_rows(float *dst, const long long *fix, const uint16_t *emb, int row0, int n)
+// embedding row (emb) or the fixed-point sum xfix that other CTAs wrote.
+__device__ __forceinline__ void stage_x_rows(float *dst, const long long *xfix, const uint16_t *emb, int row0, int n)
 {
     for (int i = threadIdx.x; i < n; i += kMegaConsumers)
-        dst[i] = emb ? bf16_lo((uint32_t)emb[row0 + i]) : fixed_to_float(__ldcg(&fix[row0 + i]));
+        dst[i] = emb ? bf16_lo((uint32_t)emb[row0 + i]) : fixed_to_float(__ldcg(&xfix[row0 + i]));
 }
 
 // Activation row -> hi/lo FP16 B fragments (lanes 0-7 of every half block, the
@@ -588,7 +549,7 @@ __device__ __forceinline__ void fp8_epilogue(const GemvParams &gp, const PhaseSp
 // row is a weight row and the B operand's columns 0 and 1 are the slice's hi
 // and lo parts (same fragments for every pair; lanes 8-31 zero). The item's
 // row sums (rows 8 kDownItemTiles i ..), scaled by 2^-e and the tensor's scale,
-// go to rows_s[3072]; down_reduce then adds them into the layer's fix_x.
+// go to rows_s[3072]; down_reduce then adds them into xfix.
 __device__ __forceinline__ void consume_down(const Ring &r, const PhaseSpan &sp, unsigned seq0, unsigned &taken,
                                              const float *act_s, float *rows_s, float scale, int *error)
 {
@@ -647,115 +608,17 @@ __device__ __forceinline__ void consume_down(const Ring &r, const PhaseSpan &sp,
     }
 }
 
-__device__ __forceinline__ void red_add_u64(long long *dst, long long v)
+// The CTA's 3072 down row sums (rows_s) added into xfix, the layer output x
+// in fixed point, with 64-bit integer reductions. A row sum the fixed point
+// cannot hold (non-finite, or too large for 145 terms to stay in range) sets
+// kFlagFixedRange, and the host reruns the step on the FP32 path.
+__device__ __forceinline__ void down_reduce(const float *rows_s, long long *xfix, int *flag)
 {
-    asm volatile("red.global.add.u64 [%0], %1;" ::"l"(dst), "l"(v) : "memory");
-}
-
-// The CTA's 3072 down row sums (rows_s) added into fix_x, the layer output x
-// in fixed point, with 64-bit integer reductions; act slice s also adds h
-// (fix_h, exact integers) for its share of the rows, so fix_x = h + down. A
-// row sum the fixed point cannot hold (non-finite, or too large for 145 terms
-// to stay in range) sets kFlagFixedRange, and the host reruns the step on the
-// FP32 path.
-__device__ __forceinline__ void down_reduce(const float *rows_s, long long *fix_x, const long long *fix_h, int slice,
-                                            int *flag)
-{
-    const int h0 = kHidden * slice / kFfnSlices, h1 = kHidden * (slice + 1) / kFfnSlices;
     bool out_of_range = false;
     for (int v = threadIdx.x; v < kHidden; v += kMegaConsumers) {
         const float r = rows_s[v];
         out_of_range |= !(fabsf(r) < kFixedTermLimit);
-        long long add = float_to_fixed(r);
-        if (v >= h0 && v < h1) add += __ldcg(&fix_h[v]);
-        red_add_u64(fix_x + v, add);
-    }
-    if (__any_sync(0xffffffffu, out_of_range) && (threadIdx.x & 31) == 0) atomicOr(flag, kFlagFixedRange);
-}
-
-// Fused path: the attention output of one query head (128 values in shared
-// memory) as hi/lo FP16 B fragments of two 64-column pieces (the layout of
-// stage_frag); returns 2^-e, the inverse of the split's scale.
-__device__ __forceinline__ float stage_head_frag(uint32_t *frag, const float *head_s, float *red)
-{
-    if (threadIdx.x < 32) {
-        const int lane = threadIdx.x;
-        const float4 x = reinterpret_cast<const float4 *>(head_s)[lane];
-        const float mx = warp_max(fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
-        const int e = frag_exponent(mx * 1.0001f);
-        const float sc = exp2i(e);
-        uint32_t hi, lo;
-        split_hilo(x.x * sc, x.y * sc, hi, lo);
-        frag_store_pair(frag, 8, 4 * lane, 0, hi);
-        frag_store_pair(frag, 8, 4 * lane, 1, lo);
-        split_hilo(x.z * sc, x.w * sc, hi, lo);
-        frag_store_pair(frag, 8, 4 * lane + 2, 0, hi);
-        frag_store_pair(frag, 8, 4 * lane + 2, 1, lo);
-        if (lane == 0) red[0] = exp2i(-e);
-    }
-    consumers_sync();
-    return red[0];
-}
-
-// Fused path: this CTA's o-slice items (kOSliceTiles tiles x the query head's
-// one 1 KB block each: 8 rows x 128 columns), every block against the same
-// head fragments. Row sums (scaled by out_scale) go to rows_s[768]: item i,
-// tile b, row g at 96 i + 8 b + g.
-__device__ __forceinline__ void consume_oslice(const Ring &r, const PhaseSpan &sp, unsigned seq0, unsigned &taken,
-                                               const uint4 *frag, float *rows_s, float out_scale, int *error)
-{
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (first_item(seq0) >= sp.items) return;
-    uint4 x0 = make_uint4(0, 0, 0, 0), x1 = x0;
-    if (lane < 16) {
-        const int piece = lane >> 3;
-        x0 = frag[(piece * 2) * 8 + (lane & 7)];
-        x1 = frag[(piece * 2 + 1) * 8 + (lane & 7)];
-    }
-    for (int i = first_item(seq0); i < sp.items; i += kMegaConsumerWarps) {
-        const unsigned k = taken++;
-        const unsigned slot = slot_of(warp, k), use = k / kSlotsPerWarp;
-        mbar_wait(&r.full[slot], use & 1, error);
-        const uint8_t *s = r.slots + (size_t)slot * kSlotBytes;
-        __builtin_assume(__isShared(s));
-#pragma unroll 4
-        for (int b = 0; b < kOSliceTiles; b++) {
-            const uint4 wa = *reinterpret_cast<const uint4 *>(s + b * kBlockBytes + lane * 16);
-            const uint4 wb = *reinterpret_cast<const uint4 *>(s + b * kBlockBytes + 512 + lane * 16);
-            float c[4][4] = {};
-            mma_block4(c, wa, wb, x0, x1);
-            // lane (g, t4): t4 = 0 holds half 0 of row g, t4 = 1 half 1
-            float v = (lane & 1) ? (c[0][2] + c[0][3]) + (c[1][2] + c[1][3]) + ((c[2][2] + c[2][3]) + (c[3][2] + c[3][3]))
-                                 : (c[0][0] + c[0][1]) + (c[1][0] + c[1][1]) + ((c[2][0] + c[2][1]) + (c[3][0] + c[3][1]));
-            v += __shfl_xor_sync(0xffffffffu, v, 1);
-            if ((lane & 3) == 0) rows_s[(i * kOSliceTiles + b) * kTileRows + (lane >> 2)] = v * out_scale;
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&r.empty[slot]);
-    }
-}
-
-// Fused path: the quarter's 768 o partial sums added into fix_h; the quarter
-// CTAs of query head 0 also add the layer input x (exactly: the previous
-// layer's fixed-point output, or the embedding row), so fix_h = x + o.
-__device__ __forceinline__ void oslice_reduce(const float *rows_s, long long *fix_h, int row0, bool add_x,
-                                              const long long *fix_x_prev, const uint16_t *emb, int *flag)
-{
-    bool out_of_range = false;
-    for (int v = threadIdx.x; v < kOSliceRows; v += kMegaConsumers) {
-        const float r = rows_s[v];
-        out_of_range |= !(fabsf(r) < kFixedTermLimit);
-        long long add = float_to_fixed(r);
-        if (add_x) {
-            if (emb) {
-                const float xe = bf16_lo((uint32_t)emb[row0 + v]);
-                out_of_range |= !(fabsf(xe) < kFixedTermLimit);
-                add += float_to_fixed(xe);
-            } else {
-                add += __ldcg(&fix_x_prev[row0 + v]);
-            }
-        }
-        red_add_u64(fix_h + row0 + v, add);
+        asm volatile("red.global.add.u64 [%0], %1;" ::"l"(xfix + v), "l"(float_to_fixed(r)) : "memory");
     }
     if (__any_sync(0xffffffffu, out_of_range) && (threadIdx.x & 31) == 0) atomicOr(flag, kFlagFixedRange);
 }
@@ -937,7 +800,7 @@ __device__ __forceinline__ void merge_ranges(const MegaParams &p, int kvh, int r
 template <int HQ>
 __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, int length, int kvh, int h0, int range,
                                               int ranges, unsigned epoch, unsigned tag, unsigned tickets, float *qs,
-                                              float *cmb, int *flag, bool rec, float *out_s = nullptr)
+                                              float *cmb, int *flag, bool rec)
 {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, pp = lane >> 2, qd = lane & 3;
     const int total = length + 1;
@@ -1065,8 +928,8 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
         }
         if (ranges == 1) {
             const float inv = 1.0f / L;
-            float *dst = out_s ? out_s : p.attn + (size_t)(kvh * 4 + h0 + hq) * kHeadDim;
-            reinterpret_cast<float4 *>(dst)[lane] = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+            reinterpret_cast<float4 *>(p.attn + (size_t)(kvh * 4 + h0 + hq) * kHeadDim)[lane] =
+                make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
         } else {
             const size_t at = (size_t)(kvh * ranges + range) * 4 + hq;
             reinterpret_cast<float4 *>(p.part_acc + at * kHeadDim)[lane] = acc;
@@ -1079,7 +942,7 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
     consumers_sync();
     if (ranges == 1) {
         if (threadIdx.x == 0) {
-            if (!out_s) signal_word(sync_word(p, kSyncAttn), 1);
+            signal_word(sync_word(p, kSyncAttn), 1);
             record_mark(p, rec, layer * kMarksPerLayer + 3);
         }
         return;
@@ -1101,8 +964,7 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
 }
 
 __global__ void __launch_bounds__(kMegaThreads, 1)
-    decode_mega_kernel(MegaParams p, const __grid_constant__ CUtensorMap down_map,
-                       const __grid_constant__ CUtensorMap o_map)
+    decode_mega_kernel(MegaParams p, const __grid_constant__ CUtensorMap down_map)
 {
     extern __shared__ __align__(128) uint8_t mega_smem[];
     __shared__ float red[32];
@@ -1129,16 +991,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1)
 
     if (threadIdx.x >= kMegaConsumers) {
         const int lane = threadIdx.x & 31;
-        if (lane < kMegaConsumerWarps) produce(p, ring, lane, &down_map, &o_map);
+        if (lane < kMegaConsumerWarps) produce(p, ring, lane, &down_map);
         return;
     }
 
     const uint4 *frag4 = reinterpret_cast<const uint4 *>(frag);
     float *xs_head = reinterpret_cast<float *>(frag);
-    // fused path, in the fragment area past the attention staging: the head's
-    // attention output and the quarter's 768 o row sums
-    float *head_s = reinterpret_cast<float *>(frag) + kFusedHeadOffset;
-    float *orows_s = head_s + kHeadDim;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     unsigned barrier = 0, taken = 0, seq = 0, tickets = 0, attn_target = 0;
     for (int s = 0; s < p.steps; s++) {
@@ -1149,45 +1007,17 @@ __global__ void __launch_bounds__(kMegaThreads, 1)
         for (int i = threadIdx.x; i < 2 * kHeadDim; i += kMegaConsumers)
             rope_s[i] = i < kHeadDim ? p.rope_cos[(size_t)length * kHeadDim + i]
                                      : p.rope_sin[(size_t)length * kHeadDim + i - kHeadDim];
-        // attention units: short contexts run fused with o (CTA c < 128: query
-        // head c / 4, o rows of quarter c % 4); longer ones split each KV head's
-        // positions into ranges and o waits for all heads
-        const bool fused = fused_step(length);
+        // attention units: short contexts give each query head its own CTA
+        // (32 units); longer ones split each KV head's positions into ranges
         const bool head_mode = length + 1 <= kHeadModeMax && (int)gridDim.x >= kQueryHeads;
         const int ranges = head_mode ? 1 : attention_ranges(length + 1);
-        int unit, akvh, ah0, arange;
-        if (fused) {
-            unit = (int)blockIdx.x < kFusedCtas ? (int)blockIdx.x : -1;
-            akvh = unit < 0 ? 0 : unit >> 4;
-            ah0 = unit < 0 ? 0 : (unit >> 2) & 3;
-            arange = 0;
-        } else {
-            unit = attention_unit(head_mode ? kQueryHeads : kKVHeads * ranges);
-            akvh = unit < 0 ? 0 : (head_mode ? unit / 4 : unit / ranges);
-            ah0 = head_mode ? unit % 4 : 0;
-            arange = head_mode ? 0 : unit - akvh * ranges;
-        }
-        const unsigned attn_signals = fused ? 0u : (head_mode ? kQueryHeads : kKVHeads);
+        const int unit = attention_unit(head_mode ? kQueryHeads : kKVHeads * ranges);
+        const int akvh = unit < 0 ? 0 : (head_mode ? unit / 4 : unit / ranges);
+        const int ah0 = head_mode ? unit % 4 : 0, arange = head_mode ? 0 : unit - akvh * ranges;
+        const unsigned attn_signals = head_mode ? kQueryHeads : kKVHeads;
         for (int layer = 0; layer < kLayers; layer++) {
             const unsigned epoch = (unsigned)(s * kLayers + layer) + 1;  // layers run by the launch, this one included
             const float *sc = p.scales + layer * 7;
-            // this layer's fixed-point buffers (g counts the launch's layers)
-            const int g = s * kLayers + layer;
-            long long *fix_h = p.fix + (size_t)((2 * g) & 3) * kHidden;
-            long long *fix_x = p.fix + (size_t)((2 * g + 1) & 3) * kHidden;
-            const long long *fix_x_prev = p.fix + (size_t)((2 * g + 3) & 3) * kHidden;  // layer g - 1's x
-            {
-                // zero this layer's x and the next layer's h (their previous
-                // contents, x of layer g - 2 and h of layer g - 1, were last read
-                // before the barrier this layer started from)
-                long long *next_h = p.fix + (size_t)((2 * g + 2) & 3) * kHidden;
-                int r0, r1;
-                cta_range(kHidden, r0, r1);
-                for (int v = r0 + threadIdx.x; v < r1; v += kMegaConsumers) {
-                    fix_x[v] = 0;
-                    next_h[v] = 0;
-                }
-            }
             GemvParams gp;
             memset(&gp, 0, sizeof gp);
             gp.kv = p.kv;
@@ -1197,7 +1027,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1)
             gp.rope_row = rope_s;
             gp.length = length;
             // qkv: input norm, RoPE, KV store
-            PhaseSpan sp = phase_span(p, layer, kPhQKV, fused);
+            PhaseSpan sp = phase_span(p, layer, kPhQKV);
             gp.rows = kQKVRows;
             gp.cols = kHidden;
             gp.scale[0] = sc[0];
@@ -1208,11 +1038,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1)
             gp.qkv_tagged = p.qkvt;
             gp.ytag = p.tag_base + epoch - 1;
             const int mk = layer * kMarksPerLayer;
+            // the layer input x: the embedding row, else the last layer's xfix
+            // (its h, stored by its o epilogue, plus every act slice's down rows)
+            const int cur = (layer & 1) * kHidden, prev = kHidden - cur;  // hbuf / xfix halves
             // the attention unit's K/V rows of earlier steps do not depend on
             // this layer's qkv: start them towards L2 now
             if (unit >= 0 && threadIdx.x < 2) attention_prefetch(p, layer, length, akvh, arange, ranges, threadIdx.x);
-            // the layer input x: the embedding row, else the previous layer's x
-            float inv = stage_frag<kHidden>(frag, nullptr, fix_x_prev, layer == 0 ? emb_row : nullptr,
+            float inv = stage_frag<kHidden>(frag, nullptr, p.xfix + prev, layer == 0 ? emb_row : nullptr,
                                             p.norms + (size_t)(2 * layer) * kHidden, red);
             if (threadIdx.x == 0) record_mark(p, rec, mk);
             consume_fp8<item_blocks(kPhQKV), kHidden / kBlockCols>(ring, sp, seq, taken, frag4, partial, p.error);
@@ -1226,65 +1058,49 @@ __global__ void __launch_bounds__(kMegaThreads, 1)
                 if (threadIdx.x == 0) record_mark(p, rec, mk + 2);
             }
             if (unit >= 0) {
-                // fused: the head's output goes to head_s, nothing is signalled
                 float *qs = reinterpret_cast<float *>(frag);
                 if (head_mode)
                     cta_attention<1>(p, layer, length, akvh, ah0, 0, 1, epoch, gp.ytag, tickets, qs,
-                                     qs + 16 * kQStride + 2 * kHeadDim, &flag, rec, fused ? head_s : nullptr);
+                                     qs + 16 * kQStride + 2 * kHeadDim, &flag, rec);
                 else
                     cta_attention<4>(p, layer, length, akvh, 0, arange, ranges, epoch, gp.ytag, tickets, qs,
                                      qs + 16 * kQStride + 2 * kHeadDim, &flag, rec);
                 consumers_sync();
             }
-            if (fused) {
-                // the query head's attention straight into its o columns:
-                // h = x + sum over heads of o_head, in fixed point
-                sp = phase_span(p, layer, kPhO, true);
-                if (unit >= 0) {
-                    const float inv_o = stage_head_frag(frag, head_s, red);
-                    if (threadIdx.x == 0) record_mark(p, rec, mk + 4);
-                    consume_oslice(ring, sp, seq, taken, frag4, orows_s, inv_o * sc[3], p.error);
-                    consumers_sync();
-                    if (threadIdx.x == 0) record_mark(p, rec, mk + 5);
-                    oslice_reduce(orows_s, fix_h, (unit & 3) * kOSliceRows, (unit >> 2) == 0, fix_x_prev,
-                                  layer == 0 ? emb_row : nullptr, p.nonfinite);
-                }
-                seq += sp.items;
-            } else {
-                if (ranges > 1) tickets += (unsigned)ranges;
-                attn_target += attn_signals;
-                // o + residual (x), whole rows: h = x + o stored into fix_h
-                sp = phase_span(p, layer, kPhO, false);
-                gp.rows = kHidden;
-                gp.cols = kQuery;
-                gp.scale[0] = gp.scale[1] = gp.scale[2] = sc[3];
-                gp.bound[0] = gp.bound[1] = 1 << 30;
-                gp.res_shared = res_s;
-                gp.res_base = sp.first * kTileRows;
-                gp.y = nullptr;
-                gp.y_fixed = fix_h;
-                gp.range_flag = p.nonfinite;
-                gp.y_stride = kHidden;
-                stage_x_rows(res_s, fix_x_prev, layer == 0 ? emb_row : nullptr, gp.res_base,
-                             sp.items / (kQuery / kBlockCols / item_blocks(kPhO)) * kTileRows);
-                // every KV head's attention output stored
-                if (threadIdx.x == 0) thread_wait(sync_word(p, kSyncAttn), attn_target, p.error);
-                consumers_sync();
-                inv = stage_frag<kQuery>(frag, p.attn, nullptr, nullptr, nullptr, red);
-                if (threadIdx.x == 0) record_mark(p, rec, mk + 4);
-                consume_fp8<item_blocks(kPhO), kQuery / kBlockCols>(ring, sp, seq, taken, frag4, partial, p.error);
-                seq += sp.items;
-                consumers_sync();
-                if (threadIdx.x == 0) record_mark(p, rec, mk + 5);
-                fp8_epilogue<kEpiResidual>(gp, sp, kQuery / kBlockCols / item_blocks(kPhO), partial, inv);
-            }
+            if (ranges > 1) tickets += (unsigned)ranges;
+            attn_target += attn_signals;
+            // o + residual (x)
+            sp = phase_span(p, layer, kPhO);
+            gp.rows = kHidden;
+            gp.cols = kQuery;
+            gp.scale[0] = gp.scale[1] = gp.scale[2] = sc[3];
+            gp.bound[0] = gp.bound[1] = 1 << 30;
+            gp.res_shared = res_s;
+            gp.res_base = sp.first * kTileRows;
+            // h = x + o, as a float for the FFN's norm and as the starting
+            // value of this layer's xfix (read only after the FFN barrier)
+            gp.y = p.hbuf + cur;
+            gp.y_fixed = p.xfix + cur;
+            gp.range_flag = p.nonfinite;
+            gp.y_stride = kHidden;
+            stage_x_rows(res_s, p.xfix + prev, layer == 0 ? emb_row : nullptr, gp.res_base,
+                         sp.items / (kQuery / kBlockCols / item_blocks(kPhO)) * kTileRows);
+            // every KV head's attention output stored
+            if (threadIdx.x == 0) thread_wait(sync_word(p, kSyncAttn), attn_target, p.error);
+            consumers_sync();
+            inv = stage_frag<kQuery>(frag, p.attn, nullptr, nullptr, nullptr, red);
+            if (threadIdx.x == 0) record_mark(p, rec, mk + 4);
+            consume_fp8<item_blocks(kPhO), kQuery / kBlockCols>(ring, sp, seq, taken, frag4, partial, p.error);
+            seq += sp.items;
+            consumers_sync();
+            if (threadIdx.x == 0) record_mark(p, rec, mk + 5);
+            fp8_epilogue<kEpiResidual>(gp, sp, kQuery / kBlockCols / item_blocks(kPhO), partial, inv);
             grid_sync(p, ++barrier, rec, mk + 6);
             // FFN of act slice s = blockIdx.x: post norm, the slice's 16 gate/up
             // tiles and SwiGLU into shared memory (act never leaves the CTA), then
-            // the slice's 64 columns of down for every row, added into fix_x
-            // (with h for the slice's share of the rows); the next layer reads x
-            // from fix_x after one barrier
-            sp = phase_span(p, layer, kPhGateUp, fused);
+            // the slice's 64 columns of down for every row, added into xfix;
+            // the next layer reads x from xfix after one barrier
+            sp = phase_span(p, layer, kPhGateUp);
             gp.rows = kGateUpRows;
             gp.cols = kHidden;
             gp.scale[0] = sc[4];
@@ -1296,7 +1112,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1)
             gp.y = act_s;
             gp.y_base = blockIdx.x * 64;
             gp.y_stride = kInner;
-            inv = stage_frag<kHidden>(frag, nullptr, fix_h, nullptr, p.norms + (size_t)(2 * layer + 1) * kHidden,
+            inv = stage_frag<kHidden>(frag, p.hbuf + cur, nullptr, nullptr, p.norms + (size_t)(2 * layer + 1) * kHidden,
                                       red);
             if (threadIdx.x == 0) record_mark(p, rec, mk + 7);
             consume_fp8<item_blocks(kPhGateUp), kHidden / kBlockCols>(ring, sp, seq, taken, frag4, partial, p.error);
@@ -1306,18 +1122,18 @@ __global__ void __launch_bounds__(kMegaThreads, 1)
             fp8_epilogue<kEpiSwiGLU>(gp, sp, kHidden / kBlockCols / item_blocks(kPhGateUp), partial, inv);
             consumers_sync();
             if (threadIdx.x == 0) record_mark(p, rec, mk + 9);
-            sp = phase_span(p, layer, kPhDown, fused);
+            sp = phase_span(p, layer, kPhDown);
             consume_down(ring, sp, seq, taken, act_s, act_s + 64, sc[6], p.error);
             seq += sp.items;
             consumers_sync();
-            if (sp.items) down_reduce(act_s + 64, fix_x, fix_h, blockIdx.x, p.nonfinite);
+            if (sp.items) down_reduce(act_s + 64, p.xfix + cur, p.nonfinite);
             if (threadIdx.x == 0) record_mark(p, rec, mk + 11);
             grid_sync(p, ++barrier, rec, mk + 12);
         }
-        // final norm + tied head, 8-column staging; the last layer's x from its
-        // fixed-point buffer (CTA 0 also stores it, the step's final residual stream)
+        // final norm + tied head, 8-column staging; the last layer's x from xfix
+        // (CTA 0 also stores it, the step's final residual stream)
         {
-            const long long *xl = p.fix + (size_t)((2 * (s * kLayers + kLayers - 1) + 1) & 3) * kHidden;
+            const long long *xl = p.xfix + (size_t)((kLayers - 1) & 1) * kHidden;
             float ss = 0.0f;
             for (int c = threadIdx.x; c < kHidden; c += kMegaConsumers) {
                 const float v = fixed_to_float(__ldcg(&xl[c]));
@@ -1335,7 +1151,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1)
         }
         float best = -INFINITY;
         int bi = 0x7fffffff;
-        const PhaseSpan hs = phase_span(p, 0, kPhHead, false);
+        const PhaseSpan hs = phase_span(p, 0, kPhHead);
         consume_head(ring, hs, seq, taken, p, reinterpret_cast<const float4 *>(xs_head), best, bi, p.error);
         seq += hs.items;
         if (lane == 0) {

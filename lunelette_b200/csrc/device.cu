@@ -60,9 +60,8 @@ struct lun_device {
     float *d_scales = nullptr;          // [26][7]
     unsigned *mega_sync = nullptr;      // kSyncWords lines, zeroed before every launch
     unsigned long long *mega_qkvt = nullptr;  // tagged q/k/v words the persistent kernel exchanges
-    long long *mega_fix = nullptr;            // [4][3072] fixed-point residual buffers (MegaParams::fix)
+    float *mega_ffn = nullptr;                // [2][3072] h, then [2][3072] 64-bit xfix (MegaParams::hbuf, xfix)
     alignas(64) unsigned char down_map[128];  // tensor map of the down projections (lun_down_slice_map)
-    alignas(64) unsigned char o_map[128];     // tensor map of the o projections (lun_o_slice_map)
     bool down_map_ready = false;
     unsigned mega_tag = 1;                    // tag of the next launch's first layer (never 0)
     unsigned l2_ahead = 0;              // persistent kernel's L2 lookahead (bytes per CTA)
@@ -199,7 +198,7 @@ static lun_device *create_device(size_t context, size_t kv_pages, size_t block, 
         (e = dalloc(&d->d_scales, (size_t)kLayers * LUN_SLOT_COUNT * 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->mega_sync, kSyncWords * kSyncStride * sizeof(unsigned), sc)) != cudaSuccess ||
         (e = dalloc(&d->mega_qkvt, (size_t)kQKVRows * sizeof(unsigned long long), sc)) != cudaSuccess ||
-        (e = dalloc(&d->mega_fix, (size_t)4 * kHidden * sizeof(long long), sc)) != cudaSuccess ||
+        (e = dalloc(&d->mega_ffn, (size_t)6 * kHidden * sizeof(float), sc)) != cudaSuccess ||
         (e = dalloc(&d->mega_error, sizeof(int), sc)) != cudaSuccess ||
         (e = dalloc(&d->arg_val, (size_t)d->sm_count * 4, sc)) != cudaSuccess ||
         (e = dalloc(&d->arg_idx, (size_t)d->sm_count * 4, sc)) != cudaSuccess ||
@@ -388,7 +387,7 @@ extern "C" void lun_device_destroy(lun_device *d)
     cudaFreeHost(d->h_meta);
     cudaFreeHost(d->h_next);
     cudaFree(d->mega_qkvt);
-    cudaFree(d->mega_fix);
+    cudaFree(d->mega_ffn);
     cudaFree(d->mega_error);
     cudaFree(d->arg_val);
     cudaFree(d->arg_idx);
@@ -705,9 +704,8 @@ static cudaError_t run_attention(lun_device *d, int layer, int count, size_t len
 }
 
 // The persistent decode kernel for `steps` batch-1 steps starting from d_step
-// (its length must be `length`, and ids[0]); it advances d_step and logs the
-// greedy ids in d_tokens.
-static cudaError_t launch_mega(lun_device *d, int steps, size_t length)
+// (length and ids[0]); it advances d_step and logs the greedy ids in d_tokens.
+static cudaError_t launch_mega(lun_device *d, int steps)
 {
     MegaParams p;
     memset(&p, 0, sizeof p);
@@ -723,8 +721,8 @@ static cudaError_t launch_mega(lun_device *d, int steps, size_t length)
     p.rope_sin = d->rope_sin;
     p.step = d->d_step;
     p.x = d->x;
-    p.length0 = (int)length;
-    p.fix = d->mega_fix;
+    p.hbuf = d->mega_ffn;
+    p.xfix = reinterpret_cast<long long *>(d->mega_ffn + 2 * kHidden);
     // tags of this launch's layers: mega_tag .. mega_tag + 26 * steps - 1; a
     // wrap restarts from 1 over freshly zeroed words, so no old word matches
     const unsigned long long span = (unsigned long long)steps * kLayers;
@@ -753,16 +751,13 @@ static cudaError_t launch_mega(lun_device *d, int steps, size_t length)
     cudaError_t e;
     if (!d->down_map_ready) {
         if ((e = lun_down_slice_map(d->down_map, layer_base(d, 0) + kLayerQKV + kLayerO + kLayerGateUp,
-                                    kLayerBytes)) != cudaSuccess ||
-            (e = lun_o_slice_map(d->o_map, layer_base(d, 0) + kLayerQKV, kLayerBytes)) != cudaSuccess)
+                                    kLayerBytes)) != cudaSuccess)
             return e;
         d->down_map_ready = true;
     }
-    if ((e = cudaMemsetAsync(d->mega_sync, 0, kSyncWords * kSyncStride * sizeof(unsigned), d->stream)) !=
-            cudaSuccess ||
-        (e = cudaMemsetAsync(d->mega_fix, 0, (size_t)4 * kHidden * sizeof(long long), d->stream)) != cudaSuccess)
-        return e;
-    return lun_launch_decode_mega(p, d->down_map, d->o_map, d->sm_count, d->stream);
+    e = cudaMemsetAsync(d->mega_sync, 0, kSyncWords * kSyncStride * sizeof(unsigned), d->stream);
+    if (e != cudaSuccess) return e;
+    return lun_launch_decode_mega(p, d->down_map, d->sm_count, d->stream);
 }
 
 // One decode step reading length/ids from d_step, ending with device greedy
@@ -828,7 +823,7 @@ extern "C" int lun_device_decode_loop(lun_device *d, int64_t first_token, size_t
                                  d->stream)) != cudaSuccess ||
             (e = cudaMemsetAsync(d->d_flag, 0, 4, d->stream)) != cudaSuccess ||
             (e = cudaEventRecord(start, d->stream)) != cudaSuccess ||
-            (e = launch_mega(d, (int)steps, length)) != cudaSuccess ||
+            (e = launch_mega(d, (int)steps)) != cudaSuccess ||
             (e = cudaEventRecord(stop, d->stream)) != cudaSuccess ||
             (e = cudaMemcpyAsync(d->h_error, d->mega_error, 4, cudaMemcpyDeviceToHost, d->stream)) !=
                 cudaSuccess ||
@@ -980,7 +975,7 @@ extern "C" int lun_device_run(lun_device *d, const int64_t *ids, size_t count, s
             goto bad;
         what = "kernel launch";
         if (mega) {
-            if ((e = launch_mega(d, 1, length)) != cudaSuccess ||
+            if ((e = launch_mega(d, 1)) != cudaSuccess ||
                 (e = cudaMemcpyAsync(d->h_error, d->mega_error, 4, cudaMemcpyDeviceToHost, d->stream)) !=
                     cudaSuccess)
                 goto bad;

@@ -183,7 +183,7 @@ struct GemvParams {
     const float *gain;   // RMSNorm gain (FP32) fused as prologue, or nullptr
     float scale[3];      // per-tensor scales by row range
     int bound[2];        // rows < bound[0] -> scale[0]; < bound[1] -> scale[1]; else scale[2]
-    float *y;            // output rows [M][y_stride] (kEpiStore/kEpiResidual: may be nullptr with y_fixed)
+    float *y;            // output rows [M][y_stride]
     int y_stride;
     const float *res;    // residual rows [M][res_stride] (kEpiResidual)
     int res_stride;
@@ -343,7 +343,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, int g, int la
                             v = (p.res_shared ? p.res_shared[r - p.res_base]
                                               : __ldcg(&p.res[(size_t)m * p.res_stride + r])) +
                                 v;
-                        if (p.y) p.y[(size_t)m * p.y_stride + r] = v;
+                        p.y[(size_t)m * p.y_stride + r] = v;
                         if (EPI == kEpiResidual && p.y_fixed) {
                             p.y_fixed[r] = __float2ll_rn(v * 0x1p32f);
                             if (!(fabsf(v) < kFixedTermLimit)) atomicOr(p.range_flag, kFlagFixedRange);

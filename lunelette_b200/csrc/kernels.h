@@ -57,16 +57,12 @@ cudaError_t lun_launch_greedy(const float *logits, int n, int *partials, lun::St
 namespace lun {
 struct MegaParams;
 }
-cudaError_t lun_launch_decode_mega(const lun::MegaParams &p, const void *down_map, const void *o_map, int sm_count,
+cudaError_t lun_launch_decode_mega(const lun::MegaParams &p, const void *down_map, int sm_count,
                                    cudaStream_t stream);
 // down_map (128 bytes, 64-byte aligned): the tensor map of every layer's down
 // projection that the persistent kernel's FFN reads in act slices; down0 is
 // layer 0's tiled down matrix, layer_stride the bytes between layers.
 cudaError_t lun_down_slice_map(void *map, const uint8_t *down0, size_t layer_stride);
-// o_map (same size and alignment): the tensor map of every layer's o projection
-// that the fused attention + o path reads one query head's columns from; o0 is
-// layer 0's tiled o matrix.
-cudaError_t lun_o_slice_map(void *map, const uint8_t *o0, size_t layer_stride);
 // Whether the persistent kernel's per-CTA work fits on a grid of sm_count CTAs.
 bool lun_mega_supported(int sm_count);
 

@@ -44,28 +44,7 @@ cudaError_t lun_down_slice_map(void *map, const uint8_t *down0, size_t layer_str
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-// The o projections of all layers as one 4-D tensor of 32-bit elements: {256
-// (one 1 KB block: 8 rows x 128 columns of one tile), 32 blocks per tile (block
-// j = query head j's columns), 384 tiles, 26 layers}; the box {256, 1, 12, 1}
-// is one o-slice item of the fused path (12 tiles of one head's block).
-cudaError_t lun_o_slice_map(void *map, const uint8_t *o0, size_t layer_stride)
-{
-    PFN_cuTensorMapEncodeTiled_v12000 encode = lun_tensor_map_encoder();
-    if (!encode || ((uintptr_t)o0 & 15) || (layer_stride & 15)) return cudaErrorInvalidValue;
-    const cuuint64_t dims[4] = {256, (cuuint64_t)(kQuery / kBlockCols), (cuuint64_t)(kHidden / kTileRows),
-                                (cuuint64_t)kLayers};
-    const cuuint64_t strides[3] = {(cuuint64_t)kBlockBytes, (cuuint64_t)(kQuery / kBlockCols) * kBlockBytes,
-                                   layer_stride};
-    const cuuint32_t box[4] = {256, 1, kOSliceTiles, 1};
-    const cuuint32_t elem[4] = {1, 1, 1, 1};
-    CUresult r = encode(reinterpret_cast<CUtensorMap *>(map), CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (void *)o0, dims,
-                        strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
-}
-
-cudaError_t lun_launch_decode_mega(const MegaParams &p, const void *down_map, const void *o_map, int sm_count,
-                                   cudaStream_t stream)
+cudaError_t lun_launch_decode_mega(const MegaParams &p, const void *down_map, int sm_count, cudaStream_t stream)
 {
     if (!lun_mega_supported(sm_count)) return cudaErrorInvalidConfiguration;
     // the shared-memory opt-in, once per device (atomic flags: callers may be on
@@ -88,10 +67,9 @@ cudaError_t lun_launch_decode_mega(const MegaParams &p, const void *down_map, co
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
     MegaParams copy = p;
-    CUtensorMap map, omap;
+    CUtensorMap map;
     memcpy(&map, down_map, sizeof map);
-    memcpy(&omap, o_map, sizeof omap);
-    void *args[] = {&copy, &map, &omap};
+    void *args[] = {&copy, &map};
     return cudaLaunchCooperativeKernel((const void *)decode_mega_kernel, dim3(sm_count),
                                        dim3(kMegaThreads), args, kMegaSmemBytes, stream);
 }

@@ -51,16 +51,11 @@ struct MegaParams {
     int num_pages;
     const float *rope_cos, *rope_sin;
     StepParams *step;        // length and ids[0] advance on the device each step
-    int length0;             // step->length at launch: step s runs at length0 + s
     float *x;                // the step's final residual stream (written before the head)
     float *attn;
-    // [4][3072] 64-bit fixed point (value * 2^32): the residual stream, summed
-    // with integer adds. Layer g of the launch (g = 26 s + L) accumulates
-    // h = x + o in fix_h(g) = fix[(2g) & 3] and its output x = h + down in
-    // fix_x(g) = fix[(2g + 1) & 3]; a buffer is zeroed (at the start of layer
-    // g, the two that layer g and g + 1 will accumulate into next) only after
-    // its last reader has passed a grid barrier. Zero at launch.
-    long long *fix;
+    float *hbuf;             // [2][3072]: layer L's h (x + o) in hbuf[L & 1]
+    long long *xfix;         // [2][3072]: layer L's output x in xfix[L & 1], 64-bit fixed point (2^-32):
+                             // its o epilogue stores h, then every act slice adds its down rows
     unsigned long long *qkvt;  // the step's q (4096) and k, v (1024 each) of the current layer, tagged
     unsigned tag_base;         // tag of this launch's first layer (step s, layer L: tag_base + 26 s + L)
     float *part_acc, *part_ml;  // [8 KV heads][ranges][4 query heads][128] and [..][2]

@@ -15,11 +15,14 @@
 
 #include <cuda_runtime_api.h>
 #include <math.h>
+#include <pthread.h>
 #include <stdatomic.h>
+#include <stdint.h>
 #include <stdbool.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <unistd.h>
 
 #define LUN_API __attribute__((visibility("default")))
 
@@ -97,8 +100,95 @@ static int resolve_options(const lunelette_metal_options *options, lunelette_met
     return 0;
 }
 
+/* Parallel read (and FP8 admission scan) of one tensor's bytes into pinned
+ * staging: the range is cut into chunks that worker threads pread and scan at
+ * the same time, so a 3.8 GB checkpoint in the page cache loads at memory
+ * speed rather than one thread's copy rate. The first failing chunk (in file
+ * order) supplies the diagnostic. */
+enum { READ_CHUNK = 4 << 20, READ_MAX_THREADS = 16 };
+
+typedef struct {
+    const lun_weights *w;
+    const lun_tensor *tensor;
+    size_t index;              /* weight index, for the admission scan */
+    const lun_admission *table; /* NULL: no scan (BF16 payloads) */
+    uint64_t offset;           /* byte offset of dst[0] within the tensor */
+    unsigned char *dst;
+    size_t bytes;
+    _Atomic size_t next_chunk;
+    size_t failed_chunk;       /* lowest failing chunk, SIZE_MAX if none */
+    pthread_mutex_t lock;
+    char error[512];
+} read_job;
+
+static void *read_worker(void *arg)
+{
+    read_job *job = arg;
+    size_t chunks = (job->bytes + READ_CHUNK - 1) / READ_CHUNK;
+    for (;;) {
+        size_t c = atomic_fetch_add(&job->next_chunk, 1);
+        if (c >= chunks) {
+            break;
+        }
+        size_t at = c * (size_t)READ_CHUNK, n = job->bytes - at < READ_CHUNK ? job->bytes - at : READ_CHUNK;
+        char message[512] = "";
+        int bad = lun_st_read(&job->w->file, job->tensor, job->offset + at, job->dst + at, n);
+        if (bad) {
+            snprintf(message, sizeof message, "tensor %s: bounded payload read failed", job->tensor->name);
+        } else if (job->table) {
+            bad = lun_admit_codes(job->w, job->index, job->table, job->dst + at, n, job->offset + at,
+                job->w->w[job->index].scale, message, sizeof message);
+        }
+        if (bad) {
+            pthread_mutex_lock(&job->lock);
+            if (c < job->failed_chunk) {
+                job->failed_chunk = c;
+                snprintf(job->error, sizeof job->error, "%s", message);
+            }
+            pthread_mutex_unlock(&job->lock);
+        }
+    }
+    return NULL;
+}
+
+static int read_threads(void)
+{
+    long n = sysconf(_SC_NPROCESSORS_ONLN);
+    return n < 1 ? 1 : (n > READ_MAX_THREADS ? READ_MAX_THREADS : (int)n);
+}
+
+static int parallel_read(const lun_weights *w, size_t index, const lun_admission *table, uint64_t offset,
+    unsigned char *dst, size_t bytes, char *error, size_t capacity)
+{
+    read_job job = {w, w->w[index].tensor, index, table, offset, dst, bytes, 0, SIZE_MAX,
+        PTHREAD_MUTEX_INITIALIZER, ""};
+    size_t chunks = (bytes + READ_CHUNK - 1) / READ_CHUNK;
+    int threads = read_threads();
+    if ((size_t)threads > chunks) {
+        threads = (int)chunks;
+    }
+    pthread_t tid[READ_MAX_THREADS];
+    int started = 0;
+    for (int t = 1; t < threads; t++) {
+        if (pthread_create(&tid[started], NULL, read_worker, &job) == 0) {
+            started++;
+        }
+    }
+    read_worker(&job); /* the calling thread works too; it finishes what others did not take */
+    for (int t = 0; t < started; t++) {
+        pthread_join(tid[t], NULL);
+    }
+    pthread_mutex_destroy(&job.lock);
+    if (job.failed_chunk != SIZE_MAX) {
+        snprintf(error, capacity, "%s", job.error);
+        return -1;
+    }
+    return 0;
+}
+
 /* Stream every tensor into device memory through the two pinned staging
- * buffers, checking FP8 admission on the bytes as they pass. */
+ * buffers, checking FP8 admission on the bytes as they pass (parallel_read);
+ * the device copies and tiling of one buffer overlap the reads of the next. */
 static int upload(lun_device *device, lun_weights *w, int compact, char *error, size_t capacity)
 {
     size_t staging = lun_device_staging_bytes();
@@ -122,13 +212,7 @@ static int upload(lun_device *device, lun_weights *w, int compact, char *error, 
                 return -1;
             }
             unsigned char *dst = lun_device_staging(device, buffer);
-            if (lun_st_read(&w->file, t, 0, dst, bytes)) {
-                snprintf(error, capacity, "compact tensor %s: compact bounded payload read failed",
-                    t->name);
-                return -1;
-            }
-            if (lun_admit_codes(w, index, &table, dst, bytes, 0, w->w[index].scale, error,
-                    capacity) ||
+            if (parallel_read(w, index, &table, 0, dst, bytes, error, capacity) ||
                 lun_device_upload_linear(device, buffer, (int)layer, slot_of[b],
                     lun_block_weights[b].rows, lun_block_weights[b].cols, w->w[index].scale)) {
                 if (!error[0]) {
@@ -144,7 +228,7 @@ static int upload(lun_device *device, lun_weights *w, int compact, char *error, 
     for (size_t offset = 0; offset < total; offset += staging) {
         size_t bytes = total - offset < staging ? total - offset : staging;
         if (lun_device_staging_wait(device, buffer) ||
-            lun_st_read(&w->file, embedding, offset, lun_device_staging(device, buffer), bytes) ||
+            parallel_read(w, 0, NULL, offset, lun_device_staging(device, buffer), bytes, error, capacity) ||
             lun_device_upload_embedding(device, buffer, offset, bytes)) {
             snprintf(error, capacity, "weight decode/read failed: %s", embedding->name);
             return -1;
@@ -572,28 +656,27 @@ LUN_API int lunelette_cuda_validate_checkpoint(const char *path,
     if (lun_weights_open(&weights, path, error, capacity)) {
         return -1;
     }
-    enum { CHUNK = 1 << 20 };
-    unsigned char *buffer = malloc(CHUNK);
+    /* every FP8 tensor read and scanned whole, by the same parallel reader
+     * the upload uses (the largest tensor is 9216 x 3072 bytes) */
+    size_t largest = 0;
+    for (size_t index = 0; index < LUN_WEIGHT_COUNT; index++) {
+        if (weights.w[index].tensor->dtype == LUN_F8_E4M3 && weights.w[index].elements > largest) {
+            largest = weights.w[index].elements;
+        }
+    }
+    unsigned char *buffer = malloc(largest ? largest : 1);
     int status = buffer ? 0 : -1;
+    if (!buffer) {
+        snprintf(error, capacity, "validate: out of host memory");
+    }
     for (size_t index = 0; !status && index < LUN_WEIGHT_COUNT; index++) {
         if (weights.w[index].tensor->dtype != LUN_F8_E4M3) {
             continue;
         }
         lun_admission table;
         status = lun_weights_admission(&weights, index, strategy != LUNELETTE_METAL_RESIDENT_FP32,
-            &table, error, capacity);
-        size_t total = weights.w[index].elements;
-        for (size_t offset = 0; !status && offset < total; offset += CHUNK) {
-            size_t n = total - offset < CHUNK ? total - offset : CHUNK;
-            if (lun_st_read(&weights.file, weights.w[index].tensor, offset, buffer, n)) {
-                snprintf(error, capacity, "compact tensor %s: compact bounded payload read failed",
-                    weights.w[index].tensor->name);
-                status = -1;
-            } else {
-                status = lun_admit_codes(&weights, index, &table, buffer, n, offset,
-                    weights.w[index].scale, error, capacity);
-            }
-        }
+            &table, error, capacity) ||
+            parallel_read(&weights, index, &table, 0, buffer, weights.w[index].elements, error, capacity);
     }
     free(buffer);
     lun_weights_close(&weights);
