@@ -222,6 +222,7 @@ __device__ __forceinline__ void produce(const MegaParams &p, const Ring &r, int 
     WarpCursor rc = {0, w, 0u, stream_span(p, 0)}, pc = rc;
     bool more = cursor_settle(p, rc, w, total), pf_more = cursor_settle(p, pc, w, total);
     const unsigned budget = p.l2_ahead / kMegaConsumerWarps;
+    const unsigned budget_ffn = p.l2_ahead_ffn / kMegaConsumerWarps;
     const bool hint_ring = p.l2_hints & 1u, hint_ahead = p.l2_hints & 2u;
     const uint64_t first_out = l2_policy_evict_first(), keep = l2_policy_evict_last();
     unsigned long long ring_bytes = 0, pf_bytes = 0;
@@ -229,7 +230,11 @@ __device__ __forceinline__ void produce(const MegaParams &p, const Ring &r, int 
     while (__any_sync(kLanes, more)) {
         bool issued = false;
         if (more) {
-            const unsigned ahead = rc.k % kPhasesPerStep == kLayers * 4 ? 0u : budget;
+            // the lookahead while the ring feeds the FFN (the layer's longest
+            // stretch of pure weight streaming) may differ from the one while it
+            // feeds qkv and o, whose phases wait on other CTAs
+            const int kk = rc.k % kPhasesPerStep;
+            const unsigned ahead = kk == kLayers * 4 ? 0u : ((kk & 3) >= kPhGateUp ? budget_ffn : budget);
             while (pf_more && pf_bytes < ring_bytes + ahead) {
                 const unsigned n = (unsigned)pc.sp.item_bytes;
                 if (pf_bytes >= ring_bytes) {  // not yet in the ring

@@ -65,6 +65,7 @@ struct lun_device {
     bool down_map_ready = false;
     unsigned mega_tag = 1;                    // tag of the next launch's first layer (never 0)
     unsigned l2_ahead = 0;              // persistent kernel's L2 lookahead (bytes per CTA)
+    unsigned l2_ahead_ffn = 0;          // the same while the ring is filled with FFN items
     unsigned l2_hints = 0;              // persistent kernel's L2 eviction hints (MegaParams::l2_hints)
     int *mega_error = nullptr, *h_error = nullptr;
     float *arg_val = nullptr;
@@ -229,6 +230,8 @@ static lun_device *create_device(size_t context, size_t kv_pages, size_t block, 
         // lengthen the latency of the phases' cross-CTA exchanges
         const char *ahead = getenv("LUNELETTE_L2_AHEAD_KB");
         d->l2_ahead = (ahead ? (unsigned)strtoul(ahead, nullptr, 10) : 128u) << 10;
+        const char *ahead_ffn = getenv("LUNELETTE_L2_AHEAD_FFN_KB");
+        d->l2_ahead_ffn = ahead_ffn ? (unsigned)strtoul(ahead_ffn, nullptr, 10) << 10 : d->l2_ahead;
         // L2 eviction hints of the persistent kernel's weight stream
         // (MegaParams::l2_hints): ring copies evict_first measured +1.8 % on C0
         // (1002 against 984 tok/s); evict_last on the prefetches gained nothing
@@ -747,6 +750,7 @@ static cudaError_t launch_mega(lun_device *d, int steps)
     p.steps = steps;
     p.timeline = d->record_timeline ? d->timeline : nullptr;
     p.l2_ahead = d->l2_ahead;
+    p.l2_ahead_ffn = d->l2_ahead_ffn;
     p.l2_hints = d->l2_hints;
     cudaError_t e;
     if (!d->down_map_ready) {

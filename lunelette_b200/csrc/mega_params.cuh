@@ -68,6 +68,7 @@ struct MegaParams {
     int *error;
     int steps;
     unsigned l2_ahead;          // bytes of a CTA's weight stream kept prefetched into L2 ahead of its ring
+    unsigned l2_ahead_ffn;      // the same while the ring is filled with FFN (gate/up, down) items
     unsigned l2_hints;          // bit 0: ring copies mark their lines evict_first (read once per step);
                                 // bit 1: L2 prefetches mark theirs evict_last (kept until the copy)
     unsigned long long *timeline;  // optional %globaltimer (ns) record, layout above

@@ -24,7 +24,6 @@ import pytest
 
 from tests.oracle_lib import greedy
 
-pytestmark = pytest.mark.gpu
 
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 REF_BIN = os.path.join(REPO, "oracle", "_ref")
@@ -37,6 +36,7 @@ def binary(name):
     return path
 
 
+@pytest.mark.gpu
 def test_reference_generation_loop_drives_the_runtime(lib, checkpoint_path, oracle):
     prompt = np.random.default_rng(4321).integers(1000, 131072, 32).astype(np.int64)
     proc = subprocess.run([binary("generate_metal_next"), checkpoint_path, "32"] + [str(int(i)) for i in prompt],
@@ -73,6 +73,7 @@ def write_generated_fixture(path, forced):
         f.write(data)
 
 
+@pytest.mark.gpu
 def test_reference_native_harness_capture_then_check(lib, checkpoint_path, tmp_path):
     rng = np.random.default_rng(606)
     pairs = []
@@ -95,3 +96,66 @@ def test_reference_native_harness_capture_then_check(lib, checkpoint_path, tmp_p
     assert "steps=64 cycles=2" in proc.stdout
     assert "exact=0" not in proc.stdout
     assert len([l for l in proc.stdout.splitlines() if l.startswith("check mode=mps cycle=")]) == 64
+
+
+@pytest.mark.gpu
+def test_reference_service_generator_runs_multi_turn_sessions(lib, checkpoint_path, oracle, tmp_path):
+    """service/native.c (the reference's native service generator, compiled
+    unchanged on Linux with a SHA-256 stand-in for CommonCrypto) drives the
+    runtime through config 3's turn shape: a 512-id system prefix, then 2 turns
+    of 200 user ids and 64 greedy ids each, the prefix reused between turns
+    (appends after it) and the last turn's prompt checkpointed, restored and
+    generated again. Every generated id against the oracle on the same
+    sequence."""
+    prefix_len, turns, user_len, gen = 512, 2, 200, 64
+    rng = np.random.default_rng(909)
+    prefix = rng.integers(1000, 131072, prefix_len)
+    users = [rng.integers(1000, 131072, user_len) for _ in range(turns)]
+    ids_path = tmp_path / "ids.txt"
+    ids_path.write_text(" ".join(str(int(i)) for i in np.concatenate([prefix] + users)) + "\n")
+    proc = subprocess.run([binary("service_native_turns"), checkpoint_path, str(ids_path), str(prefix_len),
+                           str(turns), str(user_len), str(gen)],
+                          capture_output=True, text=True, timeout=900, cwd=str(tmp_path))
+    assert proc.returncode == 0, (proc.stdout[-2000:], proc.stderr[-2000:])
+    lines = dict(line.split(":", 1) for line in proc.stdout.strip().splitlines())
+    got = [[int(t) for t in lines["turn %d" % t].split()] for t in range(turns)]
+    replay = [int(t) for t in lines["replay"].split()]
+    m = oracle.open_model(checkpoint_path, 4352)
+    try:
+        m.forward(prefix)
+        pending = []
+        for t in range(turns):
+            logits, _, _ = m.forward(np.concatenate([np.asarray(pending, np.int64), users[t]]).astype(np.int64))
+            want = [greedy(logits)]
+            while len(want) < gen:
+                logits, _, _ = m.forward([want[-1]])
+                want.append(greedy(logits))
+            assert got[t] == want, "turn %d" % t
+            pending = [want[-1]]  # generated but not yet fed: opens the next turn
+    finally:
+        m.close()
+    assert replay == got[-1]
+
+
+def test_commoncrypto_stand_in_matches_sha256(tmp_path):
+    """The SHA-256 stand-in (tests/c_drivers/CommonCrypto/CommonDigest.h) that
+    lets service/native.c fingerprint its files on Linux, against hashlib on
+    lengths around the 64-byte block and padding boundaries."""
+    import hashlib
+    src = tmp_path / "sha.c"
+    src.write_text(
+        "#include <CommonCrypto/CommonDigest.h>\n#include <stdio.h>\n"
+        "int main(int c, char **v) { FILE *f = fopen(v[1], \"rb\"); CC_SHA256_CTX x; CC_SHA256_Init(&x);"
+        " unsigned char b[777], d[32]; size_t n; while ((n = fread(b, 1, sizeof b, f)))"
+        " CC_SHA256_Update(&x, b, (CC_LONG)n); CC_SHA256_Final(d, &x);"
+        " for (int i = 0; i < 32; i++) printf(\"%02x\", d[i]); return 0; }\n")
+    exe = tmp_path / "sha"
+    subprocess.run(["gcc", "-std=c11", "-O2", "-I", os.path.join(REPO, "tests", "c_drivers"), str(src), "-o", str(exe)],
+                   check=True)
+    rng = np.random.default_rng(3)
+    for n in (0, 1, 55, 56, 63, 64, 65, 119, 120, 777, 778, 5000):
+        data = rng.integers(0, 256, n).astype(np.uint8).tobytes()
+        path = tmp_path / ("m%d" % n)
+        path.write_bytes(data)
+        out = subprocess.run([str(exe), str(path)], capture_output=True, text=True, check=True).stdout
+        assert out == hashlib.sha256(data).hexdigest(), n
