@@ -75,6 +75,7 @@ cudaError_t lun_launch_fp8_decode(const uint8_t *codes, size_t n, float scale, f
 struct PrefillPlan {
     int row_tiles, token_tiles, kchunks, splits;  // 512-row tiles, 128-token tiles, 64-column chunks, K ranges
     size_t xs_bytes, inv_bytes, ws_bytes;         // workspace this projection needs
+    bool tmem_a;  // small blocks: the GEMM with the weights as tensor-memory A (128 rows per CTA)
 };
 PrefillPlan lun_prefill_plan(int rows, int cols, int count, int sm_count);
 struct PrefillWorkspace {

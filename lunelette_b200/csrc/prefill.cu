@@ -6,9 +6,23 @@
 #include "kernels.h"
 #include "launch.h"
 #include "prefill_gemm.cuh"
+#include "prefill_gemm_tmem.cuh"
+
+#include <stdlib.h>
 
 
 using namespace lun;
+
+// Blocks of up to kTmMaxTokens tokens run the tensor-memory-A GEMM
+// (prefill_gemm_tmem.cuh) unless LUNELETTE_TMEM_GEMM=0.
+static bool tmem_gemm_enabled()
+{
+    static const int on = [] {
+        const char *v = getenv("LUNELETTE_TMEM_GEMM");
+        return v && v[0] == '0' ? 0 : 1;
+    }();
+    return on != 0;
+}
 
 PrefillPlan lun_prefill_plan(int rows, int cols, int count, int sm_count)
 {
@@ -16,10 +30,12 @@ PrefillPlan lun_prefill_plan(int rows, int cols, int count, int sm_count)
     pl.row_tiles = (rows + kP2N - 1) / kP2N;
     pl.token_tiles = (count + kPgM - 1) / kPgM;
     pl.kchunks = (cols + kPgK - 1) / kPgK;
+    pl.tmem_a = count <= kTmMaxTokens && tmem_gemm_enabled();
     // K ranges fill the SMs when the output tiles alone do not (a CTA pair per
-    // 512 rows x 256 tokens); every range keeps at least two stages
-    const int pairs = pl.row_tiles * ((pl.token_tiles + 1) / 2);
-    int splits = sm_count / (2 * (pairs > 0 ? pairs : 1));
+    // 512 rows x 256 tokens, or a CTA per 128 rows for small blocks); every
+    // range keeps at least two stages
+    const int ctas = pl.tmem_a ? (rows + kTmRows - 1) / kTmRows : 2 * pl.row_tiles * ((pl.token_tiles + 1) / 2);
+    int splits = sm_count / (ctas > 0 ? ctas : 1);
     splits = splits < 1 ? 1 : splits;
     const int max_splits = pl.kchunks / 2 > 0 ? pl.kchunks / 2 : 1;
     pl.splits = splits > max_splits ? max_splits : splits;
@@ -86,6 +102,8 @@ static cudaError_t prefill_setup()
     if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
     if (done[dev].load(std::memory_order_acquire)) return cudaSuccess;
     e = cudaFuncSetAttribute(prefill_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kP2SmemBytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(prefill_gemm_tmem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTmSmemBytes);
     if (e == cudaSuccess) done[dev].store(true, std::memory_order_release);
     return e;
 }
@@ -185,6 +203,21 @@ cudaError_t lun_launch_prefill_gemm(const GemvParams &p, int count, const Prefil
     g.error = w.error;
     CUtensorMap wmap;
     if ((e = weight_tensor_map(&wmap, p.W, p.rows, g.nb)) != cudaSuccess) return e;
+    if (pl.tmem_a) {
+        TmGemmParams t;
+        t.rows = p.rows;
+        t.kchunks = pl.kchunks;
+        t.count = count;
+        t.splits = pl.splits;
+        t.xs = w.xs;
+        t.inv_scale = w.inv_scale;
+        t.ws = w.ws;
+        t.t_stride = pl.token_tiles * kPgM;
+        t.ws_rows = pl.row_tiles * kP2N;
+        t.error = w.error;
+        return launch(prefill_gemm_tmem_kernel, dim3((p.rows + kTmRows - 1) / kTmRows, 1, pl.splits),
+                      dim3(kPgThreads), kTmSmemBytes, stream, t, wmap);
+    }
     return launch(prefill_gemm_pair_kernel, dim3(2 * pl.row_tiles, (pl.token_tiles + 1) / 2, pl.splits),
                   dim3(kPgThreads), kP2SmemBytes, stream, g, wmap);
 }

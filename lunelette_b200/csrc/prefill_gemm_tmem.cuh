@@ -1,0 +1,281 @@
+// Projections of small token blocks (decode batches over many sessions, short
+// prompts) on the tcgen05 tensor cores with the weights as the MMA's A operand
+// in tensor memory.
+//
+// For a block of up to kTmMaxTokens tokens the work of a projection is the
+// weight stream itself: 116 MB of FP8 per layer, which the pair GEMM
+// (prefill_gemm.cuh) converts to FP16 through shared memory, tiles 256 tokens
+// per MMA whatever the block holds and so runs about as long at 64 tokens as
+// at 256. Here one CTA owns 128 weight rows and a K range for all the block's
+// tokens (MMA M = 128 rows, N = the tokens rounded up to 16):
+//   warp 0      tensor copies of the FP8 weight stages (128 rows x 64 columns,
+//               the 4-D map of the pair GEMM) and bulk copies of the split
+//               activations' hi and lo operand tiles;
+//   warp 1      allocates tensor memory; one lane issues the MMAs
+//               (tcgen05.mma.cta_group::1.kind::f16 with A in tensor memory,
+//               B = activations in shared memory) and commits;
+//   warps 2-5   convert: thread = weight row (its warp's quarter of the TMEM
+//               lanes), the row's 64 FP8 bytes of a stage to 32 FP16 pairs in
+//               registers, one tcgen05.st into that stage's A buffer; then the
+//               epilogue: the accumulator (row x token) times the token's 2^-e
+//               into the FP32 partials of its K range, which the finish kernels
+//               add in order as for the pair GEMM.
+// The FP16 weights never touch shared memory, and the MMA does no work for
+// token tiles the block does not have.
+//
+// Tensor-memory A operand (kind::f16, M = 128, cta_group::1): row r in lane r,
+// K element k of a 16-element step in 32-bit column k / 2 (low half even k),
+// consecutive steps in consecutive 8-column groups.
+#pragma once
+#include "prefill_gemm.cuh"
+
+namespace lun {
+
+constexpr int kTmMaxTokens = 64;                      // tokens of a block this GEMM takes
+constexpr int kTmRows = 128;                          // weight rows per CTA (MMA M, TMEM lanes)
+constexpr int kTmWStages = 8;                         // FP8 weight stages in shared memory
+constexpr int kTmAStages = 4;                         // activation stages in shared memory
+constexpr int kTmTStages = 4;                         // A stages in tensor memory
+constexpr int kTmW8 = kTmRows * kPgK;                 // 8192: one stage of FP8 weights
+constexpr int kTmABytes = (kTmMaxTokens / 8) * 1024;  // 8192: one part (hi or lo) of a stage's activations
+constexpr int kTmStageCols = kPgK / 2;                // 32 TMEM columns: one stage's A (64 FP16 per row)
+constexpr int kTmAccCols = 64;                        // accumulator columns (>= tokens rounded to 16)
+constexpr int kTmTmemCols = 256;                      // accumulator + A stages, a power of two
+constexpr int kTmWOffset = 0;
+constexpr int kTmAOffset = kTmWOffset + kTmWStages * kTmW8;
+constexpr int kTmBarOffset = kTmAOffset + kTmAStages * 2 * kTmABytes;
+constexpr int kTmSmemBytes = 1024 + kTmBarOffset + 512;
+static_assert(kTmAccCols + kTmTStages * kTmStageCols <= kTmTmemCols && kTmAccCols >= kTmMaxTokens,
+              "accumulator and A stages fit the allocation");
+static_assert(kTmSmemBytes <= 232448, "small GEMM shared memory");
+
+// One thread: D[tmem] (+)= A[tmem] * B[smem]^T.
+__device__ __forceinline__ void tc_mma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                                  bool accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate)
+        : "memory");
+}
+
+// Whole warp: 32 consecutive 32-bit columns of this warp's 32 TMEM lanes, one
+// register per column, then wait for the stores.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32])
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+        "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+        "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+struct TmGemmParams {
+    int rows, kchunks, count, splits;
+    const uint8_t *xs;        // split activations: [kchunks][hi, lo][kPgATile] of token tile 0
+    const float *inv_scale;   // [128]: 2^-e per token
+    float *ws;                // [splits][t_stride][ws_rows] FP32 partials
+    int t_stride, ws_rows;
+    int *error;
+};
+
+// Grid (ceil(rows / 128), 1, splits), 192 threads. wmap: the weight map of the
+// pair GEMM (a box is one 64-column half block of 16 tiles = 128 rows).
+static __global__ void __launch_bounds__(kPgThreads, 1)
+    prefill_gemm_tmem_kernel(TmGemmParams p, const __grid_constant__ CUtensorMap wmap)
+{
+    extern __shared__ __align__(1024) uint8_t tm_raw[];
+    const uint32_t raw = smem_u32(tm_raw);
+    uint8_t *base = tm_raw + (((raw + 1023u) & ~1023u) - raw);
+    uint8_t *wring = base + kTmWOffset, *aring = base + kTmAOffset;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(base + kTmBarOffset);
+    uint64_t *wfull = bars, *wempty = wfull + kTmWStages;
+    uint64_t *afull = wempty + kTmWStages, *aempty = afull + kTmAStages;
+    uint64_t *tfull = aempty + kTmAStages, *tempty = tfull + kTmTStages;
+    uint64_t *accf = tempty + kTmTStages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accf + 1);
+    volatile int *abort_word = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int split = blockIdx.z;
+    const int k0 = (int)((long long)split * p.kchunks / p.splits);
+    const int nk = (int)((long long)(split + 1) * p.kchunks / p.splits) - k0;
+    const int tile0 = blockIdx.x * (kTmRows / kTileRows);
+    const int count = min(p.count, kTmMaxTokens);
+    const int n = (count + 15) & ~15;                            // MMA N
+    const uint32_t abytes = (uint32_t)((count + 7) / 8) * 1024;  // 8-token atoms of a part
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kTmWStages; s++) {
+            mbar_init(&wfull[s], 1);
+            mbar_init(&wempty[s], 4);  // the converter warps
+        }
+        for (int s = 0; s < kTmAStages; s++) {
+            mbar_init(&afull[s], 1);
+            mbar_init(&aempty[s], 1);
+        }
+        for (int s = 0; s < kTmTStages; s++) {
+            mbar_init(&tfull[s], 4);   // the converter warps, after their tensor-memory stores
+            mbar_init(&tempty[s], 1);
+        }
+        mbar_init(accf, 1);
+        *abort_word = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, kTmTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    // the weights depend on no earlier kernel: the first stages are in flight
+    // before the wait for the previous kernel (programmatic launch)
+    const int pre = min(nk, kTmWStages);
+    if (warp == 0 && lane == 0)
+        for (int iw = 0; iw < pre; iw++) {
+            mbar_expect_tx(&wfull[iw], kTmW8);
+            tma_load_4d(wring + iw * kTmW8, &wmap, 0, 0, k0 + iw, tile0, &wfull[iw]);
+        }
+    pdl_wait();
+    pdl_launch_dependents();
+
+    if (warp == 0) {
+        // ---- loads: weights into their ring, activations into theirs, each as
+        // far ahead as its ring allows (non-blocking probes)
+        int iw = pre, ia = 0;
+        if (lane == 0) {
+            unsigned idle = 0;
+            while ((iw < nk || ia < nk) && !*abort_word) {
+                bool progressed = false;
+                if (iw < nk) {
+                    const int s = iw % kTmWStages, u = iw / kTmWStages;
+                    if (u == 0 || mbar_test_wait(&wempty[s], (u - 1) & 1)) {
+                        mbar_expect_tx(&wfull[s], kTmW8);
+                        tma_load_4d(wring + s * kTmW8, &wmap, 0, 0, k0 + iw, tile0, &wfull[s]);
+                        iw++;
+                        progressed = true;
+                    }
+                }
+                if (ia < nk) {
+                    const int s = ia % kTmAStages, u = ia / kTmAStages;
+                    if (u == 0 || mbar_test_wait(&aempty[s], (u - 1) & 1)) {
+                        uint8_t *st = aring + s * 2 * kTmABytes;
+                        const uint8_t *a = p.xs + ((size_t)(k0 + ia) * 2) * kPgATile;
+                        mbar_expect_tx(&afull[s], 2 * abytes);
+                        bulk_g2s(st, a, abytes, &afull[s]);
+                        bulk_g2s(st + kTmABytes, a + kPgATile, abytes, &afull[s]);
+                        ia++;
+                        progressed = true;
+                    }
+                }
+                if (progressed) {
+                    idle = 0;
+                } else if (++idle > 64u * kPgSpinLimit) {
+                    *abort_word = 1;
+                    atomicExch(p.error, 1);
+                    break;
+                }
+            }
+        }
+        iw = __shfl_sync(0xffffffffu, iw, 0);
+        ia = __shfl_sync(0xffffffffu, ia, 0);
+        // every copy issued has landed before the CTA ends
+        for (int i = max(0, iw - kTmWStages); i < iw; i++)
+            mbar_wait_bounded(&wfull[i % kTmWStages], (i / kTmWStages) & 1, abort_word, p.error, kPgSpinLimit);
+        for (int i = max(0, ia - kTmAStages); i < ia; i++)
+            mbar_wait_bounded(&afull[i % kTmAStages], (i / kTmAStages) & 1, abort_word, p.error, kPgSpinLimit);
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = f16_idesc(kTmRows, n);
+            bool ok = true;
+            for (int i = 0; i < nk && ok; i++) {
+                const int s = i % kTmAStages, t = i % kTmTStages;
+                ok = mbar_wait_bounded(&tfull[t], (i / kTmTStages) & 1, abort_word, p.error, kPgSpinLimit) &&
+                     mbar_wait_bounded(&afull[s], (i / kTmAStages) & 1, abort_word, p.error, kPgSpinLimit);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t b0 = smem_u32(aring + s * 2 * kTmABytes);
+                const uint32_t a_cols = tmem + (uint32_t)(kTmAccCols + t * kTmStageCols);
+#pragma unroll
+                for (int k = 0; k < kPgK / 16; k++)
+#pragma unroll
+                    for (int part = 0; part < 2; part++)
+                        tc_mma_f16_tmem_a(tmem, a_cols + (uint32_t)(k * 8), sw128_desc(b0 + part * kTmABytes + k * 32),
+                                          idesc, (i | k | part) != 0);
+                tc_commit(&aempty[s]);
+                tc_commit(&tempty[t]);
+            }
+            tc_commit(accf);
+            mbar_wait_bounded(accf, 0, abort_word, p.error, kPgSpinLimit);
+        }
+        __syncwarp();
+    } else {
+        // ---- converters: thread = weight row 32 q + lane of the CTA's 128, in
+        // TMEM lane quarter q = warp % 4 (the quarter this warp may access)
+        const int q = warp & 3, r = 32 * q + lane;
+        const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        int done = 0;
+        for (int i = 0; i < nk; i++) {
+            const int s = i % kTmWStages, t = i % kTmTStages, ut = i / kTmTStages;
+            if (!warp_wait(&wfull[s], (i / kTmWStages) & 1, abort_word, p.error)) break;
+            if (ut > 0 && !warp_wait(&tempty[t], (ut - 1) & 1, abort_word, p.error)) break;
+            // tile r >> 3 of the stage holds the 64 columns of its 8 rows in 512
+            // bytes; row g's four 16-byte chunks (lanes 4 g .. 4 g + 3 of the
+            // fragment layout) are contiguous: chunk c, word j carries columns
+            // 16 j + 2 c + {0, 1} (low half) and 16 j + 2 c + {8, 9} (high half)
+            const uint8_t *src = wring + s * kTmW8 + (r >> 3) * 512 + (r & 7) * 64;
+            uint32_t a[32];
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const uint4 w = *reinterpret_cast<const uint4 *>(src + 16 * c);
+                const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    a[8 * j + c] = e4m3x2_to_f16x2(words[j]);
+                    a[8 * j + c + 4] = e4m3x2_to_f16x2(words[j] >> 16);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&wempty[s]);  // the FP8 slot may refill
+            tmem_st32(tmem + lane_base + (uint32_t)(kTmAccCols + t * kTmStageCols), a);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tfull[t]);
+            done = i + 1;
+        }
+        // the MMAs of the last A stages completed before the CTA ends
+        for (int i = max(0, done - kTmTStages); i < done; i++)
+            warp_wait(&tempty[i % kTmTStages], (i / kTmTStages) & 1, abort_word, p.error);
+        if (warp_wait(accf, 0, abort_word, p.error) && !*abort_word) {
+            tc_fence_after();
+            // accumulator: lane = weight row, column = token
+            const int row = blockIdx.x * kTmRows + r;
+            for (int cb = 0; cb < n; cb += 32) {
+                uint32_t d[32];
+                tmem_ld32(tmem + lane_base + (uint32_t)cb, d);
+                if (row < p.rows)
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        const int tok = cb + j;
+                        if (tok < count)
+                            __stcg(p.ws + ((size_t)split * p.t_stride + tok) * p.ws_rows + row,
+                                   __uint_as_float(d[j]) * p.inv_scale[tok]);
+                    }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmTmemCols);
+    }
+}
+
+}  // namespace lun

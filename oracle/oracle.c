@@ -231,22 +231,37 @@ void oracle_project_fp8(const unsigned char *packed, float scale, const float *i
     for (int code = 0; code < 256; code++) {
         table[code] = oracle_fp8_decode((unsigned char)code) * scale;
     }
+    /* Blocks of ORACLE_ROWS decoded rows against blocks of ORACLE_TOKENS input
+     * rows, so a block of inputs stays in cache while every row of the block
+     * uses it (a long prompt's inputs are tens of MB). Each output is still one
+     * kahan_dot sequence over all columns, so the results do not change. */
+    enum { ORACLE_ROWS = 32, ORACLE_TOKENS = 32 };
+    size_t blocks = (rows + ORACLE_ROWS - 1) / ORACLE_ROWS;
     #pragma omp parallel
     {
-        float *row_values = malloc(cols * sizeof(float));
-        #pragma omp for schedule(static)
-        for (size_t row = 0; row < rows; row++) {
-            const unsigned char *codes = packed + row * cols;
-            for (size_t c = 0; c < cols; c++) {
-                row_values[c] = table[codes[c]];
+        float *row_values = malloc((size_t)ORACLE_ROWS * cols * sizeof(float));
+        #pragma omp for schedule(dynamic, 1)
+        for (size_t block = 0; block < blocks; block++) {
+            size_t r0 = block * ORACLE_ROWS;
+            size_t nr = rows - r0 < ORACLE_ROWS ? rows - r0 : ORACLE_ROWS;
+            for (size_t r = 0; r < nr; r++) {
+                const unsigned char *codes = packed + (r0 + r) * cols;
+                for (size_t c = 0; c < cols; c++) {
+                    row_values[r * cols + c] = table[codes[c]];
+                }
             }
-            size_t token = 0;
-            for (; token + ORACLE_GROUP <= count; token += ORACLE_GROUP) {
-                kahan_dot_group(row_values, input + token * cols, cols, cols, &output[token * rows + row],
-                    rows);
-            }
-            for (; token < count; token++) {
-                output[token * rows + row] = kahan_dot(row_values, input + token * cols, cols);
+            for (size_t t0 = 0; t0 < count; t0 += ORACLE_TOKENS) {
+                size_t t1 = t0 + ORACLE_TOKENS < count ? t0 + ORACLE_TOKENS : count;
+                for (size_t r = 0; r < nr; r++) {
+                    const float *w = row_values + r * cols;
+                    size_t token = t0;
+                    for (; token + ORACLE_GROUP <= t1; token += ORACLE_GROUP) {
+                        kahan_dot_group(w, input + token * cols, cols, cols, &output[token * rows + r0 + r], rows);
+                    }
+                    for (; token < t1; token++) {
+                        output[token * rows + r0 + r] = kahan_dot(w, input + token * cols, cols);
+                    }
+                }
             }
         }
         free(row_values);

@@ -143,6 +143,16 @@ def test_gemm_fp8_matches_oracle(lib, oracle, torch_cuda, rows, cols, count):
                entry="lunelette_cuda_gemm_fp8")
 
 
+# Blocks of up to 64 tokens run the GEMM with the weights as tensor-memory A
+# (prefill_gemm_tmem.cuh): the model's shapes at the decode-batch sizes, a
+# token count that is not a multiple of 16, and K ranges split across CTAs.
+@pytest.mark.parametrize("rows,cols,count", [
+    (6144, 3072, 64), (18432, 3072, 64), (3072, 4096, 33), (3072, 9216, 16), (128, 3072, 63), (136, 3072, 2)])
+def test_small_block_gemm_matches_oracle(lib, oracle, torch_cuda, rows, cols, count):
+    gemv_check(lib, oracle, torch_cuda, rows, cols, count, seed=rows * 3 + cols + count,
+               entry="lunelette_cuda_gemm_fp8")
+
+
 def test_gemm_fp8_residual(lib, oracle, torch_cuda):
     gemv_check(lib, oracle, torch_cuda, 3072, 4096, 77, seed=12, residual=True, entry="lunelette_cuda_gemm_fp8")
 
