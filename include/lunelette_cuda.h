@@ -127,10 +127,6 @@ int lunelette_cuda_attention_noalloc(const float *q, const float *kv_pool, const
     size_t num_pages, size_t layer, size_t length, size_t count, float *out, void *stream,
     char *error, size_t capacity);
 
-/* ---------------- model-level test support */
-
-/* Keep every layer's output rows (which 0..25) and the final-norm rows (26) of
- * the most recent call; host copy of count*3072 floats. Host-synchronous. */
 /* ---------------- batched decode over many sessions (one weight replica) */
 
 /* One set of weights and a paged FP32 KV pool of pool_positions positions
@@ -184,8 +180,23 @@ size_t lunelette_cuda_batch_free_positions(const lunelette_cuda_batch *batch);
 int lunelette_cuda_kv_copy(float *kv_pool, size_t num_pages, size_t layers, const int *src_pages,
     const int *dst_pages, size_t pairs, size_t last_slots, void *stream);
 
+/* ---------------- model-level test support */
+
+/* Keep every layer's output rows (which 0..25) and the final-norm rows (26) of
+ * the most recent call; host copy of count*3072 floats. Host-synchronous.
+ * While enabled, calls run the per-projection kernels (not the persistent
+ * decode kernel). Setting LUNELETTE_CUDA_TRACE=1 in the environment enables it
+ * for every context created afterwards. */
 int lunelette_cuda_trace(lunelette_metal *context, int enable);
 int lunelette_cuda_trace_copy(lunelette_metal *context, int which, float *out, size_t floats);
+/* Borrowed host rows of the most recent successful call while tracing: the
+ * layer-25 output (normalized 0) or the final-norm rows (normalized 1), one row
+ * per token of that call, valid until the next call on the context; NULL when
+ * tracing is off or the sequence holds no published result. The reference's
+ * test hook test_metal_snapshot (tests/metal_snapshot.m:5-8) returns the same
+ * two buffers of its Metal runtime; tests/c_drivers/metal_snapshot_cuda.c
+ * defines that hook on this function so tests/compare_metal.c links unchanged. */
+const float *lunelette_cuda_snapshot(lunelette_metal *context, int normalized);
 /* Device-resident greedy decode for throughput measurement: decode `first_token`
  * and then keep feeding each step's argmax (strict '>', lowest id on ties, as
  * src/generation.c:8-34) back on the GPU, `steps` steps in all, with no host

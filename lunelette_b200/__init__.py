@@ -88,6 +88,7 @@ SIGNATURES = {
     "lunelette_cuda_attention_noalloc": (ctypes.c_int, [P, P, P, SZ, SZ, SZ, SZ, P, P, ERR, SZ]),
     "lunelette_cuda_trace": (ctypes.c_int, [P, ctypes.c_int]),
     "lunelette_cuda_trace_copy": (ctypes.c_int, [P, ctypes.c_int, P, SZ]),
+    "lunelette_cuda_snapshot": (P, [P, ctypes.c_int]),
     "lunelette_cuda_length": (SZ, [P]),
     "lunelette_cuda_decode_loop": (ctypes.c_int, [P, ctypes.c_int64, SZ, P, P, P, ERR, SZ]),
     "lunelette_cuda_yarn": (ctypes.c_int, [ctypes.c_uint32, P, P]),

@@ -1155,6 +1155,11 @@ extern "C" int lun_device_trace(lun_device *d, int enable)
     return 0;
 }
 
+extern "C" size_t lun_device_trace_rows(const lun_device *d)
+{
+    return d->trace && d->trace_buf ? d->trace_count : 0;
+}
+
 extern "C" int lun_device_trace_copy(lun_device *d, int which, float *out, size_t floats)
 {
     if (!d->trace_buf || which < 0 || which > kLayers || floats != d->trace_count * kHidden)

@@ -93,6 +93,8 @@ int lun_device_timeline_copy(lun_device *d, unsigned long long *out, size_t entr
 int lun_device_trace(lun_device *d, int enable);
 /* which: 0..25 = layer output [count][3072]; 26 = final norm [count][3072]. */
 int lun_device_trace_copy(lun_device *d, int which, float *out, size_t floats);
+/* Rows the most recent traced call kept (0 while tracing is off). */
+size_t lun_device_trace_rows(const lun_device *d);
 
 #ifdef __cplusplus
 }

@@ -48,6 +48,7 @@ struct lunelette_metal {
     uint64_t epoch;     /* bumped by every successful checkpoint create */
     lunelette_metal_checkpoint *current; /* caller-owned; the only handle restore accepts */
     float *logits;      /* pinned host logits owned by the device layer */
+    float *snapshot[2]; /* lunelette_cuda_snapshot: last block's layer-25 / final-norm rows */
 };
 
 struct lunelette_metal_checkpoint {
@@ -331,6 +332,14 @@ LUN_API lunelette_metal *lunelette_metal_create_configured(const char *path,
     if (!device) {
         goto fail;
     }
+    /* test support: LUNELETTE_CUDA_TRACE=1 keeps every call's layer outputs
+     * (lunelette_cuda_snapshot), for harnesses that cannot call
+     * lunelette_cuda_trace between create and their first step */
+    const char *trace = getenv("LUNELETTE_CUDA_TRACE");
+    if (trace && trace[0] && strcmp(trace, "0") != 0 && lun_device_trace(device, 1)) {
+        snprintf(error, capacity, "trace buffer allocation failed");
+        goto fail;
+    }
     int compact = selected.strategy != LUNELETTE_METAL_RESIDENT_FP32;
     if (upload(device, &weights, compact, error, capacity) || upload_rope(device, resolved.context) ||
         lun_device_upload_finish(device, error, capacity)) {
@@ -403,6 +412,8 @@ LUN_API void lunelette_metal_destroy(lunelette_metal *context)
         cudaSetDevice(lun_device_ordinal(context->device));
     }
     lun_device_destroy(context->device);
+    free(context->snapshot[0]);
+    free(context->snapshot[1]);
     free(context);
 }
 
@@ -693,6 +704,27 @@ LUN_API int lunelette_cuda_trace_copy(lunelette_metal *context, int which, float
 {
     return context && context->device && out ?
         lun_device_trace_copy(context->device, which, out, floats) : -1;
+}
+
+LUN_API const float *lunelette_cuda_snapshot(lunelette_metal *context, int normalized)
+{
+    if (!context || !context->device || context->state != SEQ_PUBLISHED) {
+        return NULL;
+    }
+    const size_t rows = lun_device_trace_rows(context->device);
+    const int kind = normalized != 0;
+    if (!rows) {
+        return NULL;
+    }
+    if (!context->snapshot[kind] &&
+        !(context->snapshot[kind] = malloc(context->limits.block * (size_t)LUN_HIDDEN * sizeof(float)))) {
+        return NULL;
+    }
+    if (lun_device_trace_copy(context->device, kind ? LUN_LAYERS : LUN_LAYERS - 1, context->snapshot[kind],
+            rows * (size_t)LUN_HIDDEN)) {
+        return NULL;
+    }
+    return context->snapshot[kind];
 }
 
 LUN_API size_t lunelette_cuda_length(const lunelette_metal *context)

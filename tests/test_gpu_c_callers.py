@@ -6,6 +6,13 @@ into oracle/_ref/) and linked against liblunelette_cuda.so unchanged.
                         with the CLI's logits callback (src/main.c:48-67):
                         its 32 greedy tokens after a 32-id prompt must equal
                         the oracle's greedy tokens.
+  compare_metal_cuda    the reference's real-weight comparator
+                        (tests/compare_metal.c) with its snapshot hook
+                        (tests/c_drivers/metal_snapshot_cuda.c): logits, the
+                        layer-25 output and the final-norm rows of every
+                        teacher-forced step against a fixture the oracle
+                        writes, in its own element bound 2e-4 + 1e-4|ref|,
+                        over two reset cycles.
   compare_native_cuda   the reference's native regression harness
                         (tests/compare_native.c:348-450): `capture` records 8
                         teacher-forced steps after prompts of 6/24/150/248 ids,
@@ -71,6 +78,74 @@ def write_generated_fixture(path, forced):
         f.write(struct.pack("<Q", len(header)))
         f.write(header)
         f.write(data)
+
+
+def write_safetensors(path, tensors):
+    """A safetensors file of (name, array) pairs in order (I64 or F32)."""
+    import json
+    header, blobs, offset = {}, [], 0
+    for name, array in tensors:
+        array = np.ascontiguousarray(array)
+        dtype = {np.dtype(np.int64): "I64", np.dtype(np.float32): "F32"}[array.dtype]
+        data = array.tobytes()
+        header[name] = {"dtype": dtype, "shape": list(array.shape), "data_offsets": [offset, offset + len(data)]}
+        blobs.append(data)
+        offset += len(data)
+    text = json.dumps(header, separators=(",", ":")).encode()
+    text += b" " * ((8 - len(text) % 8) % 8)
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(text)))
+        f.write(text)
+        for data in blobs:
+            f.write(data)
+
+
+def oracle_metal_fixtures(oracle, checkpoint_path, tmp_path, cases, seed):
+    """ids files and comparator fixtures the oracle captures: the greedy ids it
+    generates, its logits, layer-25 output rows and final-norm rows for the
+    prompt and each decode step (the tensor names tests/compare_metal.c reads)."""
+    rng = np.random.default_rng(seed)
+    pairs = []
+    m = oracle.open_model(checkpoint_path, 256)
+    try:
+        for count, steps in cases:
+            ids = rng.integers(1000, 131072, count).astype(np.int64)
+            ids_path = tmp_path / ("ids%d.txt" % count)
+            ids_path.write_text(" ".join(str(int(i)) for i in ids) + "\n")
+            m.reset()
+            tensors, generated, feed = [], [], ids
+            for step in range(steps):
+                logits, trace, final = m.forward(feed, trace=True, final_norm=True)
+                rows = len(feed)
+                tensors += [("logits_%d" % step, logits.reshape(1, -1)),
+                            ("block_25_%d" % step, trace[25].reshape(1, rows, -1)),
+                            ("final_norm_%d" % step, final.reshape(1, rows, -1))]
+                generated.append(greedy(logits))
+                feed = [generated[-1]]
+            fixture = tmp_path / ("oracle%d.safetensors" % count)
+            write_safetensors(fixture, [("generated", np.asarray(generated, np.int64))] + tensors)
+            pairs += [str(ids_path), str(fixture)]
+    finally:
+        m.close()
+    return pairs
+
+
+@pytest.mark.gpu
+def test_reference_metal_comparator_against_oracle_fixtures(lib, checkpoint_path, oracle, tmp_path):
+    """tests/compare_metal.c, the reference's comparator for a runtime against
+    captures of an independent reference, here with fixtures the oracle
+    captures. The comparator teacher-forces the fixture's ids, requires every
+    element within 2e-4 + 1e-4|ref| and the same argmax, runs both prompts twice
+    over reset cycles, fills the 256-position context (248 + 8) and checks that
+    the next decode is rejected, then destroys and recreates the runtime."""
+    pairs = oracle_metal_fixtures(oracle, checkpoint_path, tmp_path, ((6, 4), (248, 8)), 2718)
+    env = dict(os.environ, LUNELETTE_CUDA_TRACE="1")
+    proc = subprocess.run([binary("compare_metal_cuda"), checkpoint_path] + pairs,
+                          capture_output=True, text=True, timeout=900, env=env)
+    assert proc.returncode == 0, (proc.stdout[-3000:], proc.stderr[-2000:])
+    assert "PASS steps24 cycles2" in proc.stdout
+    assert proc.stdout.count("PASS capacity256 append then reject") == 2
+    assert "PASS destroy/recreate" in proc.stdout
 
 
 @pytest.mark.gpu
