@@ -120,9 +120,13 @@ def decode_phases(checkpoint, steps=8, prompt=32):
     def add(name, v):
         rows.setdefault(name, []).append(v)
 
-    with L.Runtime(checkpoint) as rt:
+    # prompts beyond 248 ids run on the (4352, 256) profile, prefilled in 256-id chunks
+    with L.Runtime(checkpoint, limits=(4352, 256) if prompt > 248 else None) as rt:
         ids = np.random.default_rng(7).integers(1000, 131072, prompt)
-        tok = int(np.argmax(rt.prefill(ids)))
+        logits = rt.prefill(ids[:256])
+        for c in range(256, prompt, 256):
+            logits = rt.append(ids[c:c + 256])
+        tok = int(np.argmax(logits))
         rt.timeline(True)
         for _ in range(steps):
             tok = int(np.argmax(rt.decode(tok)))
@@ -298,6 +302,8 @@ def main():
                     help="run the C0 prompt and N single-token decode launches (a profiling target)")
     ap.add_argument("--decode-phases", metavar="CHECKPOINT", default=None,
                     help="time the persistent decode kernel's phases on this checkpoint instead")
+    ap.add_argument("--phases-prompt", type=int, default=32,
+                    help="prompt length before the timed decode steps of --decode-phases (4096: config 2)")
     ap.add_argument("--prefill-tokens", nargs=2, metavar=("CHECKPOINT", "N"), default=None,
                     help="prefill N ids twice, the second between cudaProfilerStart/Stop (a profiling target)")
     ap.add_argument("--batch-step", metavar="CHECKPOINT", default=None,
@@ -322,7 +328,7 @@ def main():
         print(json.dumps({"last_token": decode_tokens(args.decode_tokens[0], int(args.decode_tokens[1]))}))
         return
     if args.decode_phases:
-        for r in decode_phases(args.decode_phases):
+        for r in decode_phases(args.decode_phases, prompt=args.phases_prompt):
             print(json.dumps(r))
         return
     out = run(args.shapes.split(","), [int(v) for v in args.m.split(",")], args.iters, args.warmup)
