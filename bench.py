@@ -210,7 +210,8 @@ def c0_bytes_per_token(context_before):
 
 def c1_gemv(peak):
     """every linear shape at token batch M = 1, 2, 4, 8 (the
-    BF16 head at M = 1) through the standalone GEMV kernels, GB/s of algorithmic
+    BF16 head at M = 1) through the kernels the runtime runs for that many
+    tokens (the GEMV up to 4, the tcgen05 GEMM beyond), GB/s of algorithmic
     bytes and the fraction of the measured HBM peak, per shape and M."""
     from lunelette_b200 import microbench
     rows = microbench.run(list(microbench.SHAPES), [1, 2, 4, 8], iters=30)

@@ -126,12 +126,29 @@ __device__ __forceinline__ void tma_prefetch_4d_hint(const void *tmap, int c0, i
 // Bounded wait on an mbarrier phase for one thread: polls until the phase with
 // `parity` completed, the CTA's abort word is set, or `limit` polls passed (then
 // it sets the abort word and *error). False when the wait did not see the phase.
+__device__ __forceinline__ unsigned long long wait_clock_ns()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+constexpr unsigned long long kWaitLimitNs = 1000000000ull;  // one second
+
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, unsigned parity, volatile int *abort_word,
                                                   int *error, unsigned limit)
 {
+    // mbarrier.try_wait may suspend the thread for a system-defined time per
+    // poll, so the poll count alone does not bound the wait: a clock does too
     unsigned spins = 0;
+    unsigned long long start = 0;
     while (!mbar_try_wait(bar, parity)) {
-        if (++spins > limit) {
+        ++spins;
+        if ((spins & 255u) == 1) {
+            const unsigned long long now = wait_clock_ns();
+            if (spins == 1) start = now;
+            else if (now - start > kWaitLimitNs) spins = limit + 1;
+        }
+        if (spins > limit) {
             *abort_word = 1;
             atomicExch(error, 1);
             return false;
@@ -139,6 +156,16 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, unsigned parity
         if ((spins & 63u) == 0 && *abort_word) return false;
     }
     return true;
+}
+
+// Polls of one bounded mbarrier wait in the tensor-core kernels.
+constexpr unsigned kWaitSpinLimit = 1u << 20;
+
+// Warp-uniform bounded wait: every lane polls; the warp goes on only if all saw the phase.
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, unsigned parity, volatile int *abort_word, int *error)
+{
+    const bool ok = mbar_wait_bounded(bar, parity, abort_word, error, kWaitSpinLimit);
+    return __all_sync(0xffffffffu, ok);
 }
 
 // Make this thread's generic-proxy shared-memory writes visible to the async

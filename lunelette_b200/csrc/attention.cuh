@@ -35,6 +35,7 @@ struct AttnParams {
     // length + token_offset + t over page_table).
     const int *positions, *token_table;
     int table_stride;
+    int *error;  // set when the tensor-core kernel's bounded waits give up (nullptr: not reported)
 };
 
 constexpr int kTile = 32;

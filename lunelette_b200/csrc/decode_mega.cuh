@@ -1101,6 +1101,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1)
             if (threadIdx.x == 0) record_mark(p, rec, mk + 5);
             fp8_epilogue<kEpiResidual>(gp, sp, kQuery / kBlockCols / item_blocks(kPhO), partial, inv);
             grid_sync(p, ++barrier, rec, mk + 6);
+            // long contexts: the next layer's K/V rows of this CTA's attention
+            // unit start towards L2 while the FFN streams its weights, so that
+            // the next attention reads L2 instead of waiting on HBM
+            if (p.kv_early && !head_mode && unit >= 0 && threadIdx.x < 2 && layer + 1 < kLayers)
+                attention_prefetch(p, layer + 1, length, akvh, arange, ranges, threadIdx.x);
             // FFN of act slice s = blockIdx.x: post norm, the slice's 16 gate/up
             // tiles and SwiGLU into shared memory (act never leaves the CTA), then
             // the slice's 64 columns of down for every row, added into xfix;

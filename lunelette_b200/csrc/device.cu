@@ -67,6 +67,7 @@ struct lun_device {
     unsigned l2_ahead = 0;              // persistent kernel's L2 lookahead (bytes per CTA)
     unsigned l2_ahead_ffn = 0;          // the same while the ring is filled with FFN items
     unsigned l2_hints = 0;              // persistent kernel's L2 eviction hints (MegaParams::l2_hints)
+    bool kv_early = true;               // persistent kernel: next layer's K/V into L2 during the FFN
     int *mega_error = nullptr, *h_error = nullptr;
     float *arg_val = nullptr;
     int *arg_idx = nullptr;
@@ -235,6 +236,8 @@ static lun_device *create_device(size_t context, size_t kv_pages, size_t block, 
         // L2 eviction hints of the persistent kernel's weight stream
         // (MegaParams::l2_hints): ring copies evict_first measured +1.8 % on C0
         // (1002 against 984 tok/s); evict_last on the prefetches gained nothing
+        const char *early = getenv("LUNELETTE_KV_EARLY");
+        d->kv_early = !(early && early[0] == '0');
         const char *hints = getenv("LUNELETTE_L2_HINTS");
         d->l2_hints = hints ? (unsigned)strtoul(hints, nullptr, 10) : 1u;
     }
@@ -699,6 +702,7 @@ static cudaError_t run_attention(lun_device *d, int layer, int count, size_t len
     a.out = d->attn;
     a.part_acc = d->part_acc;
     a.part_ml = d->part_ml;
+    a.error = d->pf.error;  // the tcgen05 kernel's bounded waits report here, as the GEMM's do
     // A captured graph serves every length, so it plans for the full context;
     // splits past the current length find no positions and contribute nothing.
     int total = fixed_plan ? (int)d->context : (int)(length + count);
@@ -752,6 +756,7 @@ static cudaError_t launch_mega(lun_device *d, int steps)
     p.l2_ahead = d->l2_ahead;
     p.l2_ahead_ffn = d->l2_ahead_ffn;
     p.l2_hints = d->l2_hints;
+    p.kv_early = d->kv_early ? 1u : 0u;
     cudaError_t e;
     if (!d->down_map_ready) {
         if ((e = lun_down_slice_map(d->down_map, layer_base(d, 0) + kLayerQKV + kLayerO + kLayerGateUp,

@@ -28,6 +28,7 @@
 // CUDA-core instructions per four weights with two conversions and a quarter MMA.
 #pragma once
 #include "common.cuh"
+#include "async.cuh"
 
 namespace lun {
 
@@ -417,6 +418,14 @@ __global__ void __launch_bounds__(256) gemv_tiled_kernel(GemvParams p)
     __shared__ float part[8][8][M];
     __shared__ float inv_scale[M];
     __shared__ float red[16 * M];
+    // this block's first tiles (contiguous NB KB each) start towards L2 before
+    // the activation row is staged: the weights depend on no earlier kernel
+    {
+        const int NB = (p.cols + 127) >> 7, tiles = (p.rows + 7) >> 3;
+        const int tile = blockIdx.x + (int)threadIdx.x * (int)gridDim.x;
+        if (threadIdx.x < 4 && tile < tiles)
+            l2_prefetch(p.W + (size_t)tile * NB * kBlockBytes, (unsigned)(NB * kBlockBytes));
+    }
     l2_prefetch_share(p.prefetch, p.prefetch_bytes);
     pdl_wait();
     pdl_launch_dependents();

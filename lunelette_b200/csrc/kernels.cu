@@ -3,6 +3,7 @@
 #include <atomic>
 #include <mutex>
 
+#include "attention_tc.cuh"
 #include "head_mma.cuh"
 #include "launch.h"
 
@@ -184,6 +185,9 @@ cudaError_t lun_kernels_init()
     if ((e = cudaFuncSetAttribute(attention_prefill_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   kPmSmemBytes)) != cudaSuccess)
         return e;
+    if ((e = cudaFuncSetAttribute(attention_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  kTaSmemBytes)) != cudaSuccess)
+        return e;
     if ((e = setup_epi<kEpiStore>()) != cudaSuccess) return e;
     if ((e = setup_epi<kEpiResidual>()) != cudaSuccess) return e;
     if ((e = setup_epi<kEpiQKV>()) != cudaSuccess) return e;
@@ -241,14 +245,28 @@ cudaError_t lun_launch_head(const HeadParams &p, int sm_count, cudaStream_t stre
 
 constexpr int kAttnMaxSplit = 512;
 
+// Blocks of more than kGemvMaxTokens tokens of one sequence run the tcgen05
+// attention (attention_tc.cuh) unless LUNELETTE_TC_ATTENTION=0 selects the
+// mma.sync kernel (attention.cuh).
+static bool tc_attention_enabled()
+{
+    static const bool on = [] {
+        const char *v = getenv("LUNELETTE_TC_ATTENTION");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
 void lun_attention_plan(AttnParams *a, int total, int count, int sm_count, int slots)
 {
     if (count > kGemvMaxTokens && !a->positions) {
         // blocks of one sequence's tokens (attention_prefill_mma_kernel): key
         // ranges of whole pages split so that about two waves of blocks run
+        // (the tcgen05 kernel holds a whole SM: about one wave of its blocks)
         const int qtiles = (count + kPmTokens - 1) / kPmTokens;
         const int pages = (total + kPage - 1) / kPage;
-        int splits = (4 * sm_count + qtiles * kKVHeads - 1) / (qtiles * kKVHeads);
+        const int target = tc_attention_enabled() ? sm_count : 4 * sm_count;
+        int splits = (target + qtiles * kKVHeads - 1) / (qtiles * kKVHeads);
         const int cap = slots / (count * kQueryHeads);
         splits = splits > cap ? cap : splits;
         splits = splits < 1 ? 1 : (splits > pages ? pages : splits);
@@ -285,8 +303,11 @@ cudaError_t lun_launch_attention(const AttnParams &a, int count, cudaStream_t st
     if (e != cudaSuccess) return e;
     if (count > kGemvMaxTokens && !a.positions) {  // blocks of one sequence's tokens: key pages per 8 query tokens
         if (a.splits < 1 || a.split_len < kPage || (a.split_len % kPage)) return cudaErrorInvalidValue;
-        e = launch(attention_prefill_mma_kernel, dim3((count + kPmTokens - 1) / kPmTokens, kKVHeads, a.splits),
-                   dim3(kPmThreads), kPmSmemBytes, stream, a, count);
+        const dim3 grid((count + kPmTokens - 1) / kPmTokens, kKVHeads, a.splits);
+        if (tc_attention_enabled())
+            e = launch(attention_prefill_tc_kernel, grid, dim3(kTaThreads), kTaSmemBytes, stream, a, count);
+        else
+            e = launch(attention_prefill_mma_kernel, grid, dim3(kPmThreads), kPmSmemBytes, stream, a, count);
         if (e != cudaSuccess || a.splits == 1) return e;
         return launch(attention_combine_kernel, dim3(kQueryHeads, count), dim3(128), 0, stream, a);
     }

@@ -216,7 +216,7 @@ cudaError_t lun_launch_prefill_gemm(const GemvParams &p, int count, const Prefil
         t.ws_rows = pl.row_tiles * kP2N;
         t.error = w.error;
         return launch(prefill_gemm_tmem_kernel, dim3((p.rows + kTmRows - 1) / kTmRows, 1, pl.splits),
-                      dim3(kPgThreads), kTmSmemBytes, stream, t, wmap);
+                      dim3(kTmThreads), kTmSmemBytes, stream, t, wmap);
     }
     return launch(prefill_gemm_pair_kernel, dim3(2 * pl.row_tiles, (pl.token_tiles + 1) / 2, pl.splits),
                   dim3(kPgThreads), kP2SmemBytes, stream, g, wmap);

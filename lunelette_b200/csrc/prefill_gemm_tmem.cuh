@@ -14,12 +14,15 @@
 //   warp 1      allocates tensor memory; one lane issues the MMAs
 //               (tcgen05.mma.cta_group::1.kind::f16 with A in tensor memory,
 //               B = activations in shared memory) and commits;
-//   warps 2-5   convert: thread = weight row (its warp's quarter of the TMEM
-//               lanes), the row's 64 FP8 bytes of a stage to 32 FP16 pairs in
-//               registers, one tcgen05.st into that stage's A buffer; then the
-//               epilogue: the accumulator (row x token) times the token's 2^-e
-//               into the FP32 partials of its K range, which the finish kernels
-//               add in order as for the pair GEMM.
+//   warps 2-9   convert: thread = weight row (its warp's quarter of the TMEM
+//               lanes), two warps per quarter, each taking half of the row's 64
+//               FP8 bytes of a stage (32 columns) to 16 FP16 pairs in registers
+//               and one tcgen05.st into that stage's A buffer; the 8-byte reads
+//               start at a chunk rotated by lane so that a warp's reads spread
+//               over the shared-memory banks (4 wavefronts instead of 16); then
+//               the epilogue: the accumulator (row x token) times the token's
+//               2^-e into the FP32 partials of its K range, which the finish
+//               kernels add in order as for the pair GEMM.
 // The FP16 weights never touch shared memory, and the MMA does no work for
 // token tiles the block does not have.
 //
@@ -32,6 +35,8 @@
 namespace lun {
 
 constexpr int kTmMaxTokens = 64;                      // tokens of a block this GEMM takes
+constexpr int kTmConverters = 8;                      // converter warps (two per TMEM lane quarter)
+constexpr int kTmThreads = 32 * (2 + kTmConverters);  // load warp, MMA warp, converters
 constexpr int kTmRows = 128;                          // weight rows per CTA (MMA M, TMEM lanes)
 constexpr int kTmWStages = 8;                         // FP8 weight stages in shared memory
 constexpr int kTmAStages = 4;                         // activation stages in shared memory
@@ -49,33 +54,6 @@ static_assert(kTmAccCols + kTmTStages * kTmStageCols <= kTmTmemCols && kTmAccCol
               "accumulator and A stages fit the allocation");
 static_assert(kTmSmemBytes <= 232448, "small GEMM shared memory");
 
-// One thread: D[tmem] (+)= A[tmem] * B[smem]^T.
-__device__ __forceinline__ void tc_mma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
-                                                  bool accumulate)
-{
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate)
-        : "memory");
-}
-
-// Whole warp: 32 consecutive 32-bit columns of this warp's 32 TMEM lanes, one
-// register per column, then wait for the stores.
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32])
-{
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
-        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
-        "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
-        "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
-        : "memory");
-    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
-
 struct TmGemmParams {
     int rows, kchunks, count, splits;
     const uint8_t *xs;        // split activations: [kchunks][hi, lo][kPgATile] of token tile 0
@@ -85,9 +63,9 @@ struct TmGemmParams {
     int *error;
 };
 
-// Grid (ceil(rows / 128), 1, splits), 192 threads. wmap: the weight map of the
-// pair GEMM (a box is one 64-column half block of 16 tiles = 128 rows).
-static __global__ void __launch_bounds__(kPgThreads, 1)
+// Grid (ceil(rows / 128), 1, splits), kTmThreads threads. wmap: the weight map
+// of the pair GEMM (a box is one 64-column half block of 16 tiles = 128 rows).
+static __global__ void __launch_bounds__(kTmThreads, 1)
     prefill_gemm_tmem_kernel(TmGemmParams p, const __grid_constant__ CUtensorMap wmap)
 {
     extern __shared__ __align__(1024) uint8_t tm_raw[];
@@ -114,14 +92,14 @@ static __global__ void __launch_bounds__(kPgThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTmWStages; s++) {
             mbar_init(&wfull[s], 1);
-            mbar_init(&wempty[s], 4);  // the converter warps
+            mbar_init(&wempty[s], kTmConverters);
         }
         for (int s = 0; s < kTmAStages; s++) {
             mbar_init(&afull[s], 1);
             mbar_init(&aempty[s], 1);
         }
         for (int s = 0; s < kTmTStages; s++) {
-            mbar_init(&tfull[s], 4);   // the converter warps, after their tensor-memory stores
+            mbar_init(&tfull[s], kTmConverters);  // after the converters' tensor-memory stores
             mbar_init(&tempty[s], 1);
         }
         mbar_init(accf, 1);
@@ -217,9 +195,11 @@ static __global__ void __launch_bounds__(kPgThreads, 1)
         __syncwarp();
     } else {
         // ---- converters: thread = weight row 32 q + lane of the CTA's 128, in
-        // TMEM lane quarter q = warp % 4 (the quarter this warp may access)
-        const int q = warp & 3, r = 32 * q + lane;
+        // TMEM lane quarter q = warp % 4 (the quarter this warp may access);
+        // half hf of the stage's columns (words j = 2 hf, 2 hf + 1 of each chunk)
+        const int q = warp & 3, hf = (warp - 2) >> 2, r = 32 * q + lane;
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        const int rot = (lane >> 1) & 3;  // first chunk this lane reads
         int done = 0;
         for (int i = 0; i < nk; i++) {
             const int s = i % kTmWStages, t = i % kTmTStages, ut = i / kTmTStages;
@@ -229,21 +209,24 @@ static __global__ void __launch_bounds__(kPgThreads, 1)
             // bytes; row g's four 16-byte chunks (lanes 4 g .. 4 g + 3 of the
             // fragment layout) are contiguous: chunk c, word j carries columns
             // 16 j + 2 c + {0, 1} (low half) and 16 j + 2 c + {8, 9} (high half)
-            const uint8_t *src = wring + s * kTmW8 + (r >> 3) * 512 + (r & 7) * 64;
-            uint32_t a[32];
+            const uint8_t *src = wring + s * kTmW8 + (r >> 3) * 512 + (r & 7) * 64 + 8 * hf;
+            uint2 w[4];
 #pragma unroll
-            for (int c = 0; c < 4; c++) {
-                const uint4 w = *reinterpret_cast<const uint4 *>(src + 16 * c);
-                const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    a[8 * j + c] = e4m3x2_to_f16x2(words[j]);
-                    a[8 * j + c + 4] = e4m3x2_to_f16x2(words[j] >> 16);
-                }
-            }
+            for (int k = 0; k < 4; k++) w[k] = *reinterpret_cast<const uint2 *>(src + 16 * ((k + rot) & 3));
             __syncwarp();
             if (lane == 0) mbar_arrive(&wempty[s]);  // the FP8 slot may refill
-            tmem_st32(tmem + lane_base + (uint32_t)(kTmAccCols + t * kTmStageCols), a);
+            uint32_t a[16];
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                // chunk c was read in step (c - rot) & 3
+                const int d = (c - rot) & 3;
+                const uint2 v = d == 0 ? w[0] : d == 1 ? w[1] : d == 2 ? w[2] : w[3];
+                a[c] = e4m3x2_to_f16x2(v.x);
+                a[c + 4] = e4m3x2_to_f16x2(v.x >> 16);
+                a[8 + c] = e4m3x2_to_f16x2(v.y);
+                a[8 + c + 4] = e4m3x2_to_f16x2(v.y >> 16);
+            }
+            tmem_st16(tmem + lane_base + (uint32_t)(kTmAccCols + t * kTmStageCols + 16 * hf), a);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tfull[t]);
@@ -252,22 +235,22 @@ static __global__ void __launch_bounds__(kPgThreads, 1)
         // the MMAs of the last A stages completed before the CTA ends
         for (int i = max(0, done - kTmTStages); i < done; i++)
             warp_wait(&tempty[i % kTmTStages], (i / kTmTStages) & 1, abort_word, p.error);
-        if (warp_wait(accf, 0, abort_word, p.error) && !*abort_word) {
+        // (the tensor-memory load below is warp-collective: a warp-uniform test)
+        if (__all_sync(0xffffffffu, warp_wait(accf, 0, abort_word, p.error) && !*abort_word) && 32 * hf < n) {
             tc_fence_after();
-            // accumulator: lane = weight row, column = token
-            const int row = blockIdx.x * kTmRows + r;
-            for (int cb = 0; cb < n; cb += 32) {
-                uint32_t d[32];
-                tmem_ld32(tmem + lane_base + (uint32_t)cb, d);
-                if (row < p.rows)
+            // accumulator: lane = weight row, column = token; half hf takes
+            // tokens 32 hf .. 32 hf + 31
+            const int row = blockIdx.x * kTmRows + r, cb = 32 * hf;
+            uint32_t d[32];
+            tmem_ld32(tmem + lane_base + (uint32_t)cb, d);
+            if (row < p.rows)
 #pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        const int tok = cb + j;
-                        if (tok < count)
-                            __stcg(p.ws + ((size_t)split * p.t_stride + tok) * p.ws_rows + row,
-                                   __uint_as_float(d[j]) * p.inv_scale[tok]);
-                    }
-            }
+                for (int j = 0; j < 32; j++) {
+                    const int tok = cb + j;
+                    if (tok < count)
+                        __stcg(p.ws + ((size_t)split * p.t_stride + tok) * p.ws_rows + row,
+                               __uint_as_float(d[j]) * p.inv_scale[tok]);
+                }
         }
     }
     tc_fence_before();

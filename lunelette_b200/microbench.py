@@ -9,8 +9,10 @@ size); several copies rotate so that the working set exceeds L2; activations
 N(0,1). Time per launch from CUDA
 events on the launching stream; GB/s counts weight bytes + activations in and
 outputs once per launch (the algorithmic bytes), against the measured HBM peak.
-M = 8 runs as two launches of 4 rows (weights are streamed twice) — the GB/s
-reported is still algorithmic bytes over total time.
+M <= 4 runs the GEMV kernel; M = 8 runs the path the runtime takes for blocks
+of more than four tokens: the activation split, the tcgen05 GEMM with the
+weights as tensor-memory A and the ordered K-range finish (the sum of the three
+kernels' device times, lunelette_cuda_gemm_fp8_timed).
 
     python -m lunelette_b200.microbench [--shapes q,gate,...] [--m 1,2,4,8] [--iters N]
 """
@@ -47,7 +49,7 @@ def run(shapes, ms_list, iters, warmup=3):
         rows, cols = SHAPES[name]
         bf16 = name == "lm_head"
         wbytes = rows * cols * (2 if bf16 else 1)
-        copies = max(1, min(8, (2 * L2_BYTES) // wbytes + 1))
+        copies = max(1, min(128, (2 * L2_BYTES) // wbytes + 1))  # rotated copies > 2x L2
         ws = []
         for _ in range(copies):
             if bf16:
@@ -63,6 +65,9 @@ def run(shapes, ms_list, iters, warmup=3):
                 continue
             x = torch.randn(m, cols, device="cuda", generator=gen)
             y = torch.empty(m, rows, device="cuda")
+            if m > GEMV_MAX_TOKENS and not bf16:
+                rows_out.append(gemm_row(lib, torch, name, rows, cols, m, copies, x, y, iters, peak, kind, gen))
+                continue
 
             def launch(i):
                 w = ws[i % copies]
@@ -90,6 +95,27 @@ def run(shapes, ms_list, iters, warmup=3):
                              "algorithmic_bytes": nbytes, "gbs": gbs, "frac_hbm": gbs / peak,
                              "peak_gbs": peak, "peak_kind": kind})
     return rows_out
+
+
+GEMV_MAX_TOKENS = 4  # blocks of more tokens run the tcgen05 GEMM (kGemvMaxTokens in csrc/kernels.h)
+
+
+def gemm_row(lib, torch, name, rows, cols, m, copies, x, y, iters, peak, kind, gen):
+    """One C1 row on the tcgen05 path: split + GEMM + finish device time."""
+    import ctypes
+    w = torch.randint(0, 256, (copies * rows * cols,), device="cuda", dtype=torch.uint8, generator=gen)
+    w[(w & 127) == 127] = 0
+    ms = (ctypes.c_float * 3)()
+    stream = torch.cuda.current_stream().cuda_stream
+    for reps in (copies, iters):
+        assert lib.lunelette_cuda_gemm_fp8_timed(w.data_ptr(), copies, rows, cols, 1e-3, x.data_ptr(), m,
+                                                 y.data_ptr(), reps, ms, stream) == 0
+    ms_total = ms[0] + ms[1] + ms[2]
+    nbytes = rows * cols + m * cols * 4 + m * rows * 4
+    gbs = nbytes / (ms_total / 1000) / 1e9
+    return {"shape": name, "rows": rows, "cols": cols, "m": m, "us": ms_total * 1000, "algorithmic_bytes": nbytes,
+            "gbs": gbs, "frac_hbm": gbs / peak, "peak_gbs": peak, "peak_kind": kind,
+            "path": "split %.2f + tcgen05 GEMM %.2f + finish %.2f us" % (ms[0] * 1e3, ms[1] * 1e3, ms[2] * 1e3)}
 
 
 PHASE_BYTES = {"attn_o": (6144 + 4096) * 3072, "ffn": 18432 * 3072 + 3072 * 9216, "head": 131072 * 3072 * 2}

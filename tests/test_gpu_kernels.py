@@ -409,7 +409,8 @@ def test_attention_long_causal_sentinel(lib, torch_cuda):
 
 @pytest.mark.parametrize("length,count,slots", [(0, 1, 8192), (255, 1, 8192), (300, 1, 8192),
                                                 (4351, 1, 8192), (100, 37, 8192), (0, 256, 8192),
-                                                (1000, 5, 160), (2000, 3, 96)])
+                                                (1000, 5, 160), (2000, 3, 96), (4000, 64, 16384),
+                                                (4096, 256, 65536), (63, 65, 8192)])
 def test_attention_random_matches_oracle(lib, oracle, torch_cuda, length, count, slots):
     torch = torch_cuda
     rng = np.random.default_rng(length * 3 + count)
@@ -424,6 +425,31 @@ def test_attention_random_matches_oracle(lib, oracle, torch_cuda, length, count,
     got = run_attention(lib, torch, q, pool, table, num_pages, layer, length, count, slots)
     want = oracle.attention(q, k, v, length)
     assert np.abs(got - want).max() < 1e-5 * max(1.0, np.abs(want).max())
+
+
+def test_attention_block_ignores_stale_pool_rows(lib, oracle, torch_cuda):
+    """Blocks of tokens (the tensor-core kernel) copy whole pages of the pool:
+    slots past the sequence's last position and every other page hold NaN here
+    (stale or never-written rows) and must not reach the output, whose key
+    ranges end inside a page and are split across CTAs."""
+    torch = torch_cuda
+    rng = np.random.default_rng(77)
+    for length, count in ((150, 40), (1200, 90)):
+        total = length + count
+        num_pages = (total + 63) // 64 + 2
+        table = rng.permutation(num_pages).astype(np.int32)
+        k = rng.standard_normal((total, 1024)).astype(np.float32)
+        v = rng.standard_normal((total, 1024)).astype(np.float32)
+        q = rng.standard_normal((count, 4096)).astype(np.float32)
+        pool = np.full((2, num_pages, 2, 8, 64, 128), np.nan, np.float32)
+        for pos in range(total):
+            page = table[pos // 64]
+            pool[1, page, 0, :, pos % 64, :] = k[pos].reshape(8, 128)
+            pool[1, page, 1, :, pos % 64, :] = v[pos].reshape(8, 128)
+        got = run_attention(lib, torch, q, pool.reshape(-1), table, num_pages, 1, length, count)
+        want = oracle.attention(q, k, v, length)
+        assert np.all(np.isfinite(got)), (length, count)
+        assert np.abs(got - want).max() < 1e-5 * max(1.0, np.abs(want).max()), (length, count)
 
 
 def test_kv_copy_fork_pages_bit_exact(lib, torch_cuda):
