@@ -6,15 +6,18 @@
 // One CTA owns 128 query rows (32 tokens x the 4 query heads of one KV head)
 // and a page-aligned key range (split) of the paged FP32 pool; it streams the
 // range in tiles of 64 keys (one page):
-//   warp 0     bulk copies of a tile's FP32 K and V rows (32 KB each, one page
-//              of one KV head) into a two-stage ring;
+//   warp 0     bulk copies of a tile's FP32 K rows and V rows (32 KB each, one
+//              page of one KV head) into two separate two-stage rings, each
+//              copy issued as soon as its slot is free (non-blocking probes);
 //   warp 1     allocates tensor memory; one lane issues the MMAs
 //              (tcgen05.mma.cta_group::1.kind::f16, A in tensor memory) and
 //              commits: S = Q K^T into one of two S buffers, O += P V;
-//   warps 2-5  convert a staged tile into FP16 hi + lo parts in shared memory
-//              (K as [64 keys x 128 dims], V transposed as [128 dims x 64 keys],
-//              both K-major with the 128-byte swizzle); V rows past the valid
-//              keys become zeros;
+//   warps 2-3  convert a staged K tile into FP16 hi + lo parts in shared
+//              memory ([64 keys x 128 dims], K-major, 128-byte swizzle);
+//   warps 4-5  convert a staged V tile, transposed ([128 dims x 64 keys]), into
+//              one of two buffers; V rows past the valid keys become zeros;
+//              with two V buffers and separate rings the next tiles' loads and
+//              conversions never wait for the current P V;
 //   warps 6-9  one thread per query row (TMEM lane quarter = query head): Q's
 //              hi + lo parts into tensor memory once; per tile the row's 64
 //              scores from tensor memory, causal mask, online softmax with the
@@ -42,13 +45,14 @@ namespace lun {
 
 constexpr int kTaKeys = 64;                                   // keys per tile (one page)
 constexpr int kTaThreads = 320;                               // 10 warps
-constexpr int kTaStageBytes = 2 * kTaKeys * kHeadDim * 4;     // FP32 K and V of a tile: 65536
 constexpr int kTaKPart = kTaKeys * kHeadDim * 2;              // one FP16 part of K: 16384 (two 8 KB chunks)
 constexpr int kTaVPart = kHeadDim * kTaKeys * 2;              // one FP16 part of V^T: 16384
-constexpr int kTaStageOffset = 0;
-constexpr int kTaKOffset = kTaStageOffset + 2 * kTaStageBytes;
-constexpr int kTaVOffset = kTaKOffset + 2 * kTaKPart;
-constexpr int kTaBarOffset = kTaVOffset + 2 * kTaVPart;
+constexpr int kTaRowBytes = kTaKeys * kHeadDim * 4;          // one FP32 K (or V) page of a head: 32768
+constexpr int kTaKStageOffset = 0;                             // K ring: 2 x 32 KB
+constexpr int kTaVStageOffset = kTaKStageOffset + 2 * kTaRowBytes;  // V ring: 2 x 32 KB
+constexpr int kTaKOffset = kTaVStageOffset + 2 * kTaRowBytes;  // K hi | lo
+constexpr int kTaVOffset = kTaKOffset + 2 * kTaKPart;          // two V buffers, each hi | lo
+constexpr int kTaBarOffset = kTaVOffset + 4 * kTaVPart;
 constexpr int kTaSmemBytes = 1024 + kTaBarOffset + 256;
 static_assert(kTaSmemBytes <= 232448, "tensor-core attention shared memory");
 constexpr uint32_t kTaQCol = 0, kTaSCol = 128, kTaOCol = 256, kTaTmemCols = 512;
@@ -66,13 +70,13 @@ static __global__ void __launch_bounds__(kTaThreads, 1) attention_prefill_tc_ker
     extern __shared__ __align__(1024) uint8_t ta_raw[];
     const uint32_t raw = smem_u32(ta_raw);
     uint8_t *base = ta_raw + (((raw + 1023u) & ~1023u) - raw);
-    uint8_t *stage = base + kTaStageOffset;
-    uint8_t *kc = base + kTaKOffset, *vc = base + kTaVOffset;  // [hi | lo] each
+    uint8_t *kstage = base + kTaKStageOffset, *vstage = base + kTaVStageOffset;
+    uint8_t *kc = base + kTaKOffset, *vc = base + kTaVOffset;  // K [hi | lo]; V buffer b at b * 2 parts
     uint64_t *bars = reinterpret_cast<uint64_t *>(base + kTaBarOffset);
-    uint64_t *stage_full = bars, *stage_empty = bars + 2;
-    uint64_t *k_ready = bars + 4, *k_free = bars + 5, *v_ready = bars + 6, *v_free = bars + 7;
-    uint64_t *s_full = bars + 8, *p_ready = bars + 10, *o_done = bars + 12, *q_ready = bars + 13;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 14);
+    uint64_t *kst_full = bars, *kst_empty = bars + 2, *vst_full = bars + 4, *vst_empty = bars + 6;
+    uint64_t *k_ready = bars + 8, *k_free = bars + 9, *v_ready = bars + 10, *v_free = bars + 12;
+    uint64_t *s_full = bars + 14, *p_ready = bars + 16, *o_done = bars + 18, *q_ready = bars + 19;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 20);
     volatile int *abort_word = reinterpret_cast<volatile int *>(tmem_slot + 1);
     int *error = p.error ? p.error : &tc_attention_error_sink;
 
@@ -80,15 +84,17 @@ static __global__ void __launch_bounds__(kTaThreads, 1) attention_prefill_tc_ker
     const int kvh = blockIdx.y, t0 = blockIdx.x * kPmTokens, split = blockIdx.z;
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2; i++) {
-            mbar_init(&stage_full[i], 1);
-            mbar_init(&stage_empty[i], 4);  // converter warps
+            mbar_init(&kst_full[i], 1);
+            mbar_init(&kst_empty[i], 2);  // K converter warps
+            mbar_init(&vst_full[i], 1);
+            mbar_init(&vst_empty[i], 2);  // V converter warps
+            mbar_init(&v_ready[i], 2);
+            mbar_init(&v_free[i], 1);
             mbar_init(&s_full[i], 1);
-            mbar_init(&p_ready[i], 4);      // softmax warps
+            mbar_init(&p_ready[i], 4);    // softmax warps
         }
-        mbar_init(k_ready, 4);
+        mbar_init(k_ready, 2);
         mbar_init(k_free, 1);
-        mbar_init(v_ready, 4);
-        mbar_init(v_free, 1);
         mbar_init(o_done, 1);
         mbar_init(q_ready, 4);
         *abort_word = 0;
@@ -109,26 +115,43 @@ static __global__ void __launch_bounds__(kTaThreads, 1) attention_prefill_tc_ker
     const int tiles = total > k0 ? (total - k0 + kTaKeys - 1) / kTaKeys : 0;
 
     if (warp == 0) {
-        // ---- loads: tile j's K and V pages of this KV head into stage j % 2
+        // ---- loads: tile j's K page into K slot j % 2 and its V page into V
+        // slot j % 2, each as soon as the converters released the slot
         if (lane == 0) {
-            int issued = 0;
-            for (int j = 0; j < tiles; j++) {
-                const int s = j & 1;
-                if (j >= 2 && !mbar_wait_bounded(&stage_empty[s], ((j >> 1) - 1) & 1, abort_word, error,
-                                                 kWaitSpinLimit))
+            int ik = 0, iv = 0;
+            unsigned idle = 0;
+            const unsigned long long start = wait_clock_ns();
+            while ((ik < tiles || iv < tiles) && !*abort_word) {
+                bool progressed = false;
+                if (ik < tiles && (ik < 2 || mbar_test_wait(&kst_empty[ik & 1], ((ik >> 1) - 1) & 1))) {
+                    const int page = p.page_table[(k0 + ik * kTaKeys) / kPage];
+                    mbar_expect_tx(&kst_full[ik & 1], kTaRowBytes);
+                    bulk_g2s(kstage + (ik & 1) * kTaRowBytes, p.kv + kv_offset(p.layer, p.num_pages, page, 0, kvh, 0),
+                             kTaRowBytes, &kst_full[ik & 1]);
+                    ik++;
+                    progressed = true;
+                }
+                if (iv < tiles && (iv < 2 || mbar_test_wait(&vst_empty[iv & 1], ((iv >> 1) - 1) & 1))) {
+                    const int page = p.page_table[(k0 + iv * kTaKeys) / kPage];
+                    mbar_expect_tx(&vst_full[iv & 1], kTaRowBytes);
+                    bulk_g2s(vstage + (iv & 1) * kTaRowBytes, p.kv + kv_offset(p.layer, p.num_pages, page, 1, kvh, 0),
+                             kTaRowBytes, &vst_full[iv & 1]);
+                    iv++;
+                    progressed = true;
+                }
+                if (progressed) {
+                    idle = 0;
+                } else if ((++idle & 1023u) == 0 && wait_clock_ns() - start > kWaitLimitNs) {
+                    *abort_word = 1;
+                    atomicExch(error, 1);
                     break;
-                const int page = p.page_table[(k0 + j * kTaKeys) / kPage];
-                uint8_t *dst = stage + s * kTaStageBytes;
-                mbar_expect_tx(&stage_full[s], kTaStageBytes);
-                bulk_g2s(dst, p.kv + kv_offset(p.layer, p.num_pages, page, 0, kvh, 0), kTaStageBytes / 2,
-                         &stage_full[s]);
-                bulk_g2s(dst + kTaStageBytes / 2, p.kv + kv_offset(p.layer, p.num_pages, page, 1, kvh, 0),
-                         kTaStageBytes / 2, &stage_full[s]);
-                issued = j + 1;
+                }
             }
             // every copy issued has landed before the CTA ends
-            for (int j = max(0, issued - 2); j < issued; j++)
-                mbar_wait_bounded(&stage_full[j & 1], (j >> 1) & 1, abort_word, error, kWaitSpinLimit);
+            for (int j = max(0, ik - 2); j < ik; j++)
+                mbar_wait_bounded(&kst_full[j & 1], (j >> 1) & 1, abort_word, error, kWaitSpinLimit);
+            for (int j = max(0, iv - 2); j < iv; j++)
+                mbar_wait_bounded(&vst_full[j & 1], (j >> 1) & 1, abort_word, error, kWaitSpinLimit);
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -155,40 +178,38 @@ static __global__ void __launch_bounds__(kTaThreads, 1) attention_prefill_tc_ker
                     tc_commit(&s_full[j & 1]);
                 }
                 if (j >= 1) {
-                    const int jj = j - 1;
-                    if (!(ok = mbar_wait_bounded(&p_ready[jj & 1], (jj >> 1) & 1, abort_word, error, kWaitSpinLimit) &&
-                               mbar_wait_bounded(v_ready, jj & 1, abort_word, error, kWaitSpinLimit)))
+                    const int jj = j - 1, vb = jj & 1;
+                    if (!(ok = mbar_wait_bounded(&p_ready[vb], (jj >> 1) & 1, abort_word, error, kWaitSpinLimit) &&
+                               mbar_wait_bounded(&v_ready[vb], (jj >> 1) & 1, abort_word, error, kWaitSpinLimit)))
                         break;
                     tc_fence_after();
-                    const uint32_t pa = tmem + kTaSCol + 64u * (uint32_t)(jj & 1);
+                    const uint32_t pa = tmem + kTaSCol + 64u * (uint32_t)vb;
+                    const uint32_t v0 = vc0 + (uint32_t)vb * 2 * kTaVPart;
 #pragma unroll
                     for (int ks = 0; ks < kTaKeys / 16; ks++)
 #pragma unroll
                         for (int term = 0; term < 3; term++) {
                             const uint32_t a = pa + (term == 2 ? 32u : 0u) + 8u * (uint32_t)ks;
-                            const uint32_t b = vc0 + (term == 1 ? kTaVPart : 0) + ks * 32;
+                            const uint32_t b = v0 + (term == 1 ? kTaVPart : 0) + ks * 32;
                             tc_mma_f16_tmem_a(tmem + kTaOCol, a, sw128_desc(b), idesc_o, (jj | ks | term) != 0);
                         }
-                    tc_commit(v_free);
+                    tc_commit(&v_free[vb]);
                     tc_commit(o_done);
                 }
             }
         }
         __syncwarp();
-    } else if (warp < 6) {
-        // ---- converters: staged FP32 K / V -> FP16 hi + lo operand tiles
-        const int ct = threadIdx.x - 64;  // 0..127
+    } else if (warp < 4) {
+        // ---- K converters: staged FP32 K -> FP16 hi + lo operand tile
+        const int ct = threadIdx.x - 64;  // 0..63
         for (int j = 0; j < tiles; j++) {
-            const int s = j & 1;
-            const float *sk = reinterpret_cast<const float *>(stage + s * kTaStageBytes);
-            const float *sv = sk + kTaKeys * kHeadDim;
-            const int valid = min(kTaKeys, total - (k0 + j * kTaKeys));
-            if (!warp_wait(&stage_full[s], (j >> 1) & 1, abort_word, error)) break;
+            const float *sk = reinterpret_cast<const float *>(kstage + (j & 1) * kTaRowBytes);
+            if (!warp_wait(&kst_full[j & 1], (j >> 1) & 1, abort_word, error)) break;
             if (j >= 1 && !warp_wait(k_free, (j - 1) & 1, abort_word, error)) break;
-            // K: unit g = (key, 8 dims); a warp reads two whole 512-byte rows
-#pragma unroll 2
-            for (int it = 0; it < 8; it++) {
-                const int g = ct + 128 * it, key = g >> 4, grp = g & 15;
+            // unit g = (key, 8 dims); a warp reads two whole 512-byte rows
+#pragma unroll 4
+            for (int it = 0; it < 16; it++) {
+                const int g = ct + 64 * it, key = g >> 4, grp = g & 15;
                 const float4 a = *reinterpret_cast<const float4 *>(sk + key * kHeadDim + 8 * grp);
                 const float4 b = *reinterpret_cast<const float4 *>(sk + key * kHeadDim + 8 * grp + 4);
                 uint4 hi, lo;
@@ -202,32 +223,47 @@ static __global__ void __launch_bounds__(kTaThreads, 1) attention_prefill_tc_ker
             }
             fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(k_ready);
-            if (j >= 1 && !warp_wait(v_free, (j - 1) & 1, abort_word, error)) break;
-            // V^T: unit (dim d = ct, keys 8 it .. 8 it + 7); keys past the valid
-            // ones are zeros (their stale pool rows must not reach P V)
+            if (lane == 0) {
+                mbar_arrive(k_ready);
+                mbar_arrive(&kst_empty[j & 1]);
+            }
+        }
+    } else if (warp < 6) {
+        // ---- V converters: staged FP32 V -> transposed FP16 hi + lo tile in
+        // buffer j % 2; keys past the valid ones are zeros (their stale pool
+        // rows must not reach P V)
+        const int ct = threadIdx.x - 128;  // 0..63
+        for (int j = 0; j < tiles; j++) {
+            const int vb = j & 1;
+            const float *sv = reinterpret_cast<const float *>(vstage + vb * kTaRowBytes);
+            uint8_t *vdst = vc + vb * 2 * kTaVPart;
+            const int valid = min(kTaKeys, total - (k0 + j * kTaKeys));
+            if (!warp_wait(&vst_full[vb], (j >> 1) & 1, abort_word, error)) break;
+            if (j >= 2 && !warp_wait(&v_free[vb], ((j >> 1) - 1) & 1, abort_word, error)) break;
+            // unit (dim d, keys 8 kg .. 8 kg + 7): d = ct + 64 (it & 1), kg = it >> 1
 #pragma unroll 2
-            for (int it = 0; it < 8; it++) {
+            for (int it = 0; it < 16; it++) {
+                const int d = ct + 64 * (it & 1), kg = it >> 1;
                 float v[8];
 #pragma unroll
                 for (int e = 0; e < 8; e++) {
-                    const int key = 8 * it + e;
-                    v[e] = key < valid ? sv[key * kHeadDim + ct] : 0.0f;
+                    const int key = 8 * kg + e;
+                    v[e] = key < valid ? sv[key * kHeadDim + d] : 0.0f;
                 }
                 uint4 hi, lo;
                 split_half2(v[0], v[1], hi.x, lo.x);
                 split_half2(v[2], v[3], hi.y, lo.y);
                 split_half2(v[4], v[5], hi.z, lo.z);
                 split_half2(v[6], v[7], hi.w, lo.w);
-                const uint32_t off = sw128_offset(ct, 8 * it);
-                *reinterpret_cast<uint4 *>(vc + off) = hi;
-                *reinterpret_cast<uint4 *>(vc + kTaVPart + off) = lo;
+                const uint32_t off = sw128_offset(d, 8 * kg);
+                *reinterpret_cast<uint4 *>(vdst + off) = hi;
+                *reinterpret_cast<uint4 *>(vdst + kTaVPart + off) = lo;
             }
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(v_ready);
-                mbar_arrive(&stage_empty[s]);
+                mbar_arrive(&v_ready[vb]);
+                mbar_arrive(&vst_empty[vb]);
             }
         }
     } else {

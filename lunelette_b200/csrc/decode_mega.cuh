@@ -745,6 +745,44 @@ __device__ __forceinline__ void attention_load(const MegaParams &p, int layer, i
                       : make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
+// K and V of one 8-position sub-tile with lanes = dims (lane l holds dims
+// 4 l .. 4 l + 3 of each position): every load instruction reads one whole
+// 512-byte row; positions past `end` read as zero.
+__device__ __forceinline__ void attention_load_rows(const MegaParams &p, int layer, int kvh, int p0, int end,
+                                                    float4 (&kk)[8], float4 (&vv)[8])
+{
+    const int lane = threadIdx.x & 31;
+    const int n = min(8, end - p0);
+    const int page = p.page_table[p0 / kPage];
+    const float *kb = p.kv + kv_offset(layer, p.num_pages, page, 0, kvh, p0 % kPage);
+    const float *vb = p.kv + kv_offset(layer, p.num_pages, page, 1, kvh, p0 % kPage);
+#pragma unroll
+    for (int t = 0; t < 8; t++) {
+        kk[t] = t < n ? ld_cg_f4(reinterpret_cast<const float4 *>(kb + t * kHeadDim) + lane)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+        vv[t] = t < n ? ld_cg_f4(reinterpret_cast<const float4 *>(vb + t * kHeadDim) + lane)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
+__device__ __forceinline__ void attention_patch_rows(int p0, int cur, const float *kcur, const float *vcur,
+                                                     float4 (&kk)[8], float4 (&vv)[8])
+{
+    if (cur < p0 || cur >= p0 + 8) return;
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int t = 0; t < 8; t++)
+        if (p0 + t == cur) {
+            kk[t] = reinterpret_cast<const float4 *>(kcur)[lane];
+            vv[t] = reinterpret_cast<const float4 *>(vcur)[lane];
+        }
+}
+
+__device__ __forceinline__ float pick4(const float (&v)[4], int i)
+{
+    return i == 0 ? v[0] : i == 1 ? v[1] : i == 2 ? v[2] : v[3];
+}
+
 // The step's own position `cur` inside the sub-tile at p0: its k/v rows come
 // from shared memory (staged from the tagged words), not from the pool.
 __device__ __forceinline__ void attention_patch(int p0, int cur, const float *kcur, const float *vcur, float4 (&kk)[8],
@@ -816,7 +854,11 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
     // K/V of earlier steps' positions are in memory already: loaded first
     int p0 = begin + 8 * warp;
     float4 kk[8], vv[8];
-    if (p0 < end) attention_load(p, layer, kvh, p0, end, kk, vv);
+    const bool rows = HQ == 4 && p.attn_rows;
+    if (p0 < end) {
+        if (rows) attention_load_rows(p, layer, kvh, p0, end, kk, vv);
+        else attention_load(p, layer, kvh, p0, end, kk, vv);
+    }
     // this layer's q rows of the four query heads and the position's k, v rows,
     // polled from the tagged words the qkv epilogues write (224 threads, 4 words each)
     {
@@ -839,7 +881,8 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
         if (src) *reinterpret_cast<float4 *>(dst) = poll_tagged4(src, tag, p.error);
     }
     consumers_sync();
-    attention_patch(p0, length, kcur, vcur, kk, vv);
+    if (rows) attention_patch_rows(p0, length, kcur, vcur, kk, vv);
+    else attention_patch(p0, length, kcur, vcur, kk, vv);
     float m_run[HQ], l_run[HQ];
     float4 o[HQ];
 #pragma unroll
@@ -848,6 +891,79 @@ __device__ __forceinline__ void cta_attention(const MegaParams &p, int layer, in
         l_run[hq] = 0.0f;
         o[hq] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    if (rows) {
+        // lanes = dims: this lane's 4 dims of the four query heads
+        float4 qv[4];
+#pragma unroll
+        for (int hq = 0; hq < 4; hq++)
+            qv[hq] = *reinterpret_cast<const float4 *>(qs + (hq * 4 + (lane >> 3)) * kQStride + (lane & 7) * 4);
+        const int my_h = lane & 3, my_t = lane >> 2;
+        for (; p0 < end; p0 += 8 * kMegaConsumerWarps) {
+            if (p0 != begin + 8 * warp) {
+                attention_load_rows(p, layer, kvh, p0, end, kk, vv);
+                attention_patch_rows(p0, length, kcur, vcur, kk, vv);
+            }
+            // partial dots over this lane's 4 dims, index i = 4 t + hq
+            float part[32];
+#pragma unroll
+            for (int t = 0; t < 8; t++)
+#pragma unroll
+                for (int hq = 0; hq < 4; hq++) {
+                    float d = qv[hq].x * kk[t].x;
+                    d = fmaf(qv[hq].y, kk[t].y, d);
+                    d = fmaf(qv[hq].z, kk[t].z, d);
+                    d = fmaf(qv[hq].w, kk[t].w, d);
+                    part[4 * t + hq] = d;
+                }
+            // reduce-scatter over the warp: lane l ends with the full dot of index l
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) {
+                const bool upper = (lane & off) != 0;
+#pragma unroll
+                for (int k = 0; k < off; k++) {
+                    const float send = upper ? part[k] : part[k + off];
+                    const float keep = upper ? part[k + off] : part[k];
+                    part[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+                }
+            }
+            const bool valid = my_t < min(8, end - p0);
+            const float sc = valid ? part[0] * kScoreScale : -INFINITY;
+            float tmax = sc;
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
+            float m_new[4], corr[4];
+#pragma unroll
+            for (int hq = 0; hq < 4; hq++) {
+                m_new[hq] = fmaxf(m_run[hq], __shfl_sync(0xffffffffu, tmax, hq));
+                corr[hq] = m_run[hq] == -INFINITY ? 0.0f : expf(m_run[hq] - m_new[hq]);
+            }
+            const float pr = valid ? expf(sc - pick4(m_new, my_h)) : 0.0f;
+            float ps = pr;
+            ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+#pragma unroll
+            for (int hq = 0; hq < 4; hq++) {
+                l_run[hq] = l_run[hq] * corr[hq] + __shfl_sync(0xffffffffu, ps, hq);
+                m_run[hq] = m_new[hq];
+                o[hq].x *= corr[hq];
+                o[hq].y *= corr[hq];
+                o[hq].z *= corr[hq];
+                o[hq].w *= corr[hq];
+            }
+#pragma unroll
+            for (int t = 0; t < 8; t++)
+#pragma unroll
+                for (int hq = 0; hq < 4; hq++) {
+                    const float pt = __shfl_sync(0xffffffffu, pr, 4 * t + hq);
+                    o[hq].x = fmaf(pt, vv[t].x, o[hq].x);
+                    o[hq].y = fmaf(pt, vv[t].y, o[hq].y);
+                    o[hq].z = fmaf(pt, vv[t].z, o[hq].z);
+                    o[hq].w = fmaf(pt, vv[t].w, o[hq].w);
+                }
+        }
+    } else
     for (; p0 < end; p0 += 8 * kMegaConsumerWarps) {
         if (p0 != begin + 8 * warp) {
             attention_load(p, layer, kvh, p0, end, kk, vv);

@@ -757,6 +757,10 @@ static cudaError_t launch_mega(lun_device *d, int steps)
     p.l2_ahead_ffn = d->l2_ahead_ffn;
     p.l2_hints = d->l2_hints;
     p.kv_early = d->kv_early ? 1u : 0u;
+    {
+        const char *rows = getenv("LUNELETTE_ATTN_ROWS");
+        p.attn_rows = !(rows && rows[0] == '0');
+    }
     cudaError_t e;
     if (!d->down_map_ready) {
         if ((e = lun_down_slice_map(d->down_map, layer_base(d, 0) + kLayerQKV + kLayerO + kLayerGateUp,

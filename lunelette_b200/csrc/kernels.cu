@@ -262,11 +262,11 @@ void lun_attention_plan(AttnParams *a, int total, int count, int sm_count, int s
     if (count > kGemvMaxTokens && !a->positions) {
         // blocks of one sequence's tokens (attention_prefill_mma_kernel): key
         // ranges of whole pages split so that about two waves of blocks run
-        // (the tcgen05 kernel holds a whole SM: about one wave of its blocks)
+        // (the tcgen05 kernel holds a whole SM: at most one wave of its blocks)
         const int qtiles = (count + kPmTokens - 1) / kPmTokens;
         const int pages = (total + kPage - 1) / kPage;
-        const int target = tc_attention_enabled() ? sm_count : 4 * sm_count;
-        int splits = (target + qtiles * kKVHeads - 1) / (qtiles * kKVHeads);
+        int splits = tc_attention_enabled() ? sm_count / (qtiles * kKVHeads)
+                                            : (4 * sm_count + qtiles * kKVHeads - 1) / (qtiles * kKVHeads);
         const int cap = slots / (count * kQueryHeads);
         splits = splits > cap ? cap : splits;
         splits = splits < 1 ? 1 : (splits > pages ? pages : splits);

@@ -71,6 +71,7 @@ struct MegaParams {
     unsigned l2_ahead_ffn;      // the same while the ring is filled with FFN (gate/up, down) items
     unsigned l2_hints;          // bit 0: ring copies mark their lines evict_first (read once per step);
                                 // bit 1: L2 prefetches mark theirs evict_last (kept until the copy)
+    unsigned attn_rows;         // range-mode attention with lanes = dims (row-coalesced K loads)
     unsigned kv_early;          // long contexts: prefetch layer L + 1's K/V rows into L2 during layer L's FFN
     unsigned long long *timeline;  // optional %globaltimer (ns) record, layout above
 };
