@@ -38,7 +38,7 @@ constexpr int kTmMaxTokens = 64;                      // tokens of a block this 
 constexpr int kTmConverters = 8;                      // converter warps (two per TMEM lane quarter)
 constexpr int kTmThreads = 32 * (2 + kTmConverters);  // load warp, MMA warp, converters
 constexpr int kTmRows = 128;                          // weight rows per CTA (MMA M, TMEM lanes)
-constexpr int kTmWStages = 8;                         // FP8 weight stages in shared memory
+constexpr int kTmWStages = 16;                        // FP8 weight stages in shared memory
 constexpr int kTmAStages = 4;                         // activation stages in shared memory
 constexpr int kTmTStages = 4;                         // A stages in tensor memory
 constexpr int kTmW8 = kTmRows * kPgK;                 // 8192: one stage of FP8 weights
