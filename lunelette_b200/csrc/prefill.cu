@@ -91,6 +91,25 @@ static cudaError_t weight_tensor_map(CUtensorMap *map, const uint8_t *W, int row
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// The same matrix as 8-byte elements in three dimensions, {64 (one 512-byte
+// piece: 8 rows x 64 columns), 2 * nb pieces per tile row, tiles}, for
+// prefill_gemm_tmem_kernel: a box of {64, 1, 16} lands the same 8 KB (one
+// piece of each of 16 tiles) as the 4-D map's box, in 16 box rows of 512 bytes
+// instead of 32 of 256.
+static cudaError_t weight_tensor_map_wide(CUtensorMap *map, const uint8_t *W, int rows, int nb)
+{
+    PFN_cuTensorMapEncodeTiled_v12000 encode = lun_tensor_map_encoder();
+    if (!encode || ((uintptr_t)W & 15)) return cudaErrorInvalidValue;
+    const cuuint64_t dims[3] = {64, (cuuint64_t)(2 * nb), (cuuint64_t)(rows / kTileRows)};
+    const cuuint64_t strides[2] = {512, (cuuint64_t)nb * kBlockBytes};
+    const cuuint32_t box[3] = {64, 1, kTmRows / kTileRows};
+    const cuuint32_t elem[3] = {1, 1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, (void *)W, dims, strides, box, elem,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 // The GEMM's shared-memory opt-in, once per device (atomic flags: callers may
 // be on several threads; setting the attribute twice is harmless).
 static cudaError_t prefill_setup()
@@ -215,8 +234,10 @@ cudaError_t lun_launch_prefill_gemm(const GemvParams &p, int count, const Prefil
         t.t_stride = pl.token_tiles * kPgM;
         t.ws_rows = pl.row_tiles * kP2N;
         t.error = w.error;
+        CUtensorMap wide;
+        if ((e = weight_tensor_map_wide(&wide, p.W, p.rows, g.nb)) != cudaSuccess) return e;
         return launch(prefill_gemm_tmem_kernel, dim3((p.rows + kTmRows - 1) / kTmRows, 1, pl.splits),
-                      dim3(kTmThreads), kTmSmemBytes, stream, t, wmap);
+                      dim3(kTmThreads), kTmSmemBytes, stream, t, wide);
     }
     return launch(prefill_gemm_pair_kernel, dim3(2 * pl.row_tiles, (pl.token_tiles + 1) / 2, pl.splits),
                   dim3(kPgThreads), kP2SmemBytes, stream, g, wmap);

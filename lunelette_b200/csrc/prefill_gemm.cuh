@@ -46,7 +46,7 @@ constexpr int kPgN = 256;                           // N of one MMA (TMEM column
 constexpr int kPgK = 64;                            // K columns per stage
 constexpr int kPgThreads = 192;                     // warp 0 loads, warp 1 MMA, warps 2-5 convert + epilogue
 constexpr int kPgATile = kPgM * kPgK * 2;           // 16384: one activation part of a stage
-constexpr unsigned kPgSpinLimit = kWaitSpinLimit;
+constexpr unsigned kPgSpinLimit = 1u << 20;  // polls of a bounded wait; the loaders idle up to 64x this
 
 // ---- activation split --------------------------------------------------------------
 struct PrefillSplitParams {

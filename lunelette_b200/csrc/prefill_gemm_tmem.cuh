@@ -38,19 +38,23 @@ constexpr int kTmMaxTokens = 64;                      // tokens of a block this 
 constexpr int kTmConverters = 8;                      // converter warps (two per TMEM lane quarter)
 constexpr int kTmThreads = 32 * (2 + kTmConverters);  // load warp, MMA warp, converters
 constexpr int kTmRows = 128;                          // weight rows per CTA (MMA M, TMEM lanes)
-constexpr int kTmWStages = 16;                        // FP8 weight stages in shared memory
-constexpr int kTmAStages = 4;                         // activation stages in shared memory
-constexpr int kTmTStages = 4;                         // A stages in tensor memory
+constexpr int kTmWStages = 8;                         // FP8 weight stages in shared memory
+constexpr int kTmAStages = 8;                         // activation stages in shared memory
+constexpr int kTmTStages = 8;                         // A stages in tensor memory
 constexpr int kTmW8 = kTmRows * kPgK;                 // 8192: one stage of FP8 weights
 constexpr int kTmABytes = (kTmMaxTokens / 8) * 1024;  // 8192: one part (hi or lo) of a stage's activations
 constexpr int kTmStageCols = kPgK / 2;                // 32 TMEM columns: one stage's A (64 FP16 per row)
-constexpr int kTmAccCols = 64;                        // accumulator columns (>= tokens rounded to 16)
-constexpr int kTmTmemCols = 256;                      // accumulator + A stages, a power of two
+constexpr int kTmAccCols = 64;                        // columns of one accumulator (>= tokens rounded to 16)
+// MMAs that accumulate into one TMEM tile run one after another (each waits for
+// the previous result), so a stage's 8 MMAs rotate over kTmAccs independent
+// accumulators, which the epilogue adds in a fixed order
+constexpr int kTmAccs = 4;
+constexpr int kTmTmemCols = 512;                      // accumulator + A stages, a power of two
 constexpr int kTmWOffset = 0;
 constexpr int kTmAOffset = kTmWOffset + kTmWStages * kTmW8;
 constexpr int kTmBarOffset = kTmAOffset + kTmAStages * 2 * kTmABytes;
 constexpr int kTmSmemBytes = 1024 + kTmBarOffset + 512;
-static_assert(kTmAccCols + kTmTStages * kTmStageCols <= kTmTmemCols && kTmAccCols >= kTmMaxTokens,
+static_assert(kTmAccs * kTmAccCols + kTmTStages * kTmStageCols <= kTmTmemCols && kTmAccCols >= kTmMaxTokens,
               "accumulator and A stages fit the allocation");
 static_assert(kTmSmemBytes <= 232448, "small GEMM shared memory");
 
@@ -63,8 +67,9 @@ struct TmGemmParams {
     int *error;
 };
 
-// Grid (ceil(rows / 128), 1, splits), kTmThreads threads. wmap: the weight map
-// of the pair GEMM (a box is one 64-column half block of 16 tiles = 128 rows).
+// Grid (ceil(rows / 128), 1, splits), kTmThreads threads. wmap: the weight
+// matrix as 8-byte elements {64, 2 nb, tiles} (a box {64, 1, 16} is one
+// 64-column piece of 16 tiles = 128 rows, in 16 rows of 512 bytes).
 static __global__ void __launch_bounds__(kTmThreads, 1)
     prefill_gemm_tmem_kernel(TmGemmParams p, const __grid_constant__ CUtensorMap wmap)
 {
@@ -92,14 +97,14 @@ static __global__ void __launch_bounds__(kTmThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTmWStages; s++) {
             mbar_init(&wfull[s], 1);
-            mbar_init(&wempty[s], kTmConverters);
+            mbar_init(&wempty[s], 4);  // the converter group of the stage (one warp per quarter)
         }
         for (int s = 0; s < kTmAStages; s++) {
             mbar_init(&afull[s], 1);
             mbar_init(&aempty[s], 1);
         }
         for (int s = 0; s < kTmTStages; s++) {
-            mbar_init(&tfull[s], kTmConverters);  // after the converters' tensor-memory stores
+            mbar_init(&tfull[s], 4);   // after that group's tensor-memory stores
             mbar_init(&tempty[s], 1);
         }
         mbar_init(accf, 1);
@@ -118,7 +123,7 @@ static __global__ void __launch_bounds__(kTmThreads, 1)
     if (warp == 0 && lane == 0)
         for (int iw = 0; iw < pre; iw++) {
             mbar_expect_tx(&wfull[iw], kTmW8);
-            tma_load_4d(wring + iw * kTmW8, &wmap, 0, 0, k0 + iw, tile0, &wfull[iw]);
+            tma_load_3d(wring + iw * kTmW8, &wmap, 0, k0 + iw, tile0, &wfull[iw]);
         }
     pdl_wait();
     pdl_launch_dependents();
@@ -135,7 +140,7 @@ static __global__ void __launch_bounds__(kTmThreads, 1)
                     const int s = iw % kTmWStages, u = iw / kTmWStages;
                     if (u == 0 || mbar_test_wait(&wempty[s], (u - 1) & 1)) {
                         mbar_expect_tx(&wfull[s], kTmW8);
-                        tma_load_4d(wring + s * kTmW8, &wmap, 0, 0, k0 + iw, tile0, &wfull[s]);
+                        tma_load_3d(wring + s * kTmW8, &wmap, 0, k0 + iw, tile0, &wfull[s]);
                         iw++;
                         progressed = true;
                     }
@@ -179,13 +184,16 @@ static __global__ void __launch_bounds__(kTmThreads, 1)
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t b0 = smem_u32(aring + s * 2 * kTmABytes);
-                const uint32_t a_cols = tmem + (uint32_t)(kTmAccCols + t * kTmStageCols);
+                const uint32_t a_cols = tmem + (uint32_t)(kTmAccs * kTmAccCols + t * kTmStageCols);
 #pragma unroll
                 for (int k = 0; k < kPgK / 16; k++)
 #pragma unroll
-                    for (int part = 0; part < 2; part++)
-                        tc_mma_f16_tmem_a(tmem, a_cols + (uint32_t)(k * 8), sw128_desc(b0 + part * kTmABytes + k * 32),
-                                          idesc, (i | k | part) != 0);
+                    for (int part = 0; part < 2; part++) {
+                        const int acc = (2 * k + part) % kTmAccs;
+                        tc_mma_f16_tmem_a(tmem + (uint32_t)(acc * kTmAccCols), a_cols + (uint32_t)(k * 8),
+                                          sw128_desc(b0 + part * kTmABytes + k * 32), idesc,
+                                          i > 0 || 2 * k + part >= kTmAccs);
+                    }
                 tc_commit(&aempty[s]);
                 tc_commit(&tempty[t]);
             }
@@ -196,60 +204,66 @@ static __global__ void __launch_bounds__(kTmThreads, 1)
     } else {
         // ---- converters: thread = weight row 32 q + lane of the CTA's 128, in
         // TMEM lane quarter q = warp % 4 (the quarter this warp may access);
-        // half hf of the stage's columns (words j = 2 hf, 2 hf + 1 of each chunk)
-        const int q = warp & 3, hf = (warp - 2) >> 2, r = 32 * q + lane;
+        // two groups of four warps take alternating stages, so that one
+        // group's tensor-memory stores are in flight while the other converts
+        const int q = warp & 3, grp = (warp - 2) >> 2, r = 32 * q + lane;
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
         const int rot = (lane >> 1) & 3;  // first chunk this lane reads
-        int done = 0;
-        for (int i = 0; i < nk; i++) {
+        for (int i = grp; i < nk; i += 2) {
             const int s = i % kTmWStages, t = i % kTmTStages, ut = i / kTmTStages;
             if (!warp_wait(&wfull[s], (i / kTmWStages) & 1, abort_word, p.error)) break;
             if (ut > 0 && !warp_wait(&tempty[t], (ut - 1) & 1, abort_word, p.error)) break;
             // tile r >> 3 of the stage holds the 64 columns of its 8 rows in 512
             // bytes; row g's four 16-byte chunks (lanes 4 g .. 4 g + 3 of the
             // fragment layout) are contiguous: chunk c, word j carries columns
-            // 16 j + 2 c + {0, 1} (low half) and 16 j + 2 c + {8, 9} (high half)
-            const uint8_t *src = wring + s * kTmW8 + (r >> 3) * 512 + (r & 7) * 64 + 8 * hf;
-            uint2 w[4];
+            // 16 j + 2 c + {0, 1} (low half) and 16 j + 2 c + {8, 9} (high half);
+            // lanes start at chunk rot so a warp's reads spread over the banks
+            const uint8_t *src = wring + s * kTmW8 + (r >> 3) * 512 + (r & 7) * 64;
+            uint4 w[4];
 #pragma unroll
-            for (int k = 0; k < 4; k++) w[k] = *reinterpret_cast<const uint2 *>(src + 16 * ((k + rot) & 3));
+            for (int k = 0; k < 4; k++) w[k] = *reinterpret_cast<const uint4 *>(src + 16 * ((k + rot) & 3));
             __syncwarp();
             if (lane == 0) mbar_arrive(&wempty[s]);  // the FP8 slot may refill
-            uint32_t a[16];
+            uint32_t a[32];
 #pragma unroll
             for (int c = 0; c < 4; c++) {
-                // chunk c was read in step (c - rot) & 3
-                const int d = (c - rot) & 3;
-                const uint2 v = d == 0 ? w[0] : d == 1 ? w[1] : d == 2 ? w[2] : w[3];
-                a[c] = e4m3x2_to_f16x2(v.x);
-                a[c + 4] = e4m3x2_to_f16x2(v.x >> 16);
-                a[8 + c] = e4m3x2_to_f16x2(v.y);
-                a[8 + c + 4] = e4m3x2_to_f16x2(v.y >> 16);
+                const int d = (c - rot) & 3;  // chunk c was read in step d
+                const uint4 v = d == 0 ? w[0] : d == 1 ? w[1] : d == 2 ? w[2] : w[3];
+                const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    a[8 * j + c] = e4m3x2_to_f16x2(words[j]);
+                    a[8 * j + c + 4] = e4m3x2_to_f16x2(words[j] >> 16);
+                }
             }
-            tmem_st16(tmem + lane_base + (uint32_t)(kTmAccCols + t * kTmStageCols + 16 * hf), a);
+            tmem_st32(tmem + lane_base + (uint32_t)(kTmAccs * kTmAccCols + t * kTmStageCols), a);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tfull[t]);
-            done = i + 1;
         }
-        // the MMAs of the last A stages completed before the CTA ends
-        for (int i = max(0, done - kTmTStages); i < done; i++)
-            warp_wait(&tempty[i % kTmTStages], (i / kTmTStages) & 1, abort_word, p.error);
-        // (the tensor-memory load below is warp-collective: a warp-uniform test)
+        const int hf = grp;  // the epilogue: group g takes tokens 32 g .. 32 g + 31
+        // accf completes once every MMA of the CTA did (the A stages in tensor
+        // memory are free then too). The tensor-memory load below is
+        // warp-collective: a warp-uniform test
         if (__all_sync(0xffffffffu, warp_wait(accf, 0, abort_word, p.error) && !*abort_word) && 32 * hf < n) {
             tc_fence_after();
             // accumulator: lane = weight row, column = token; half hf takes
             // tokens 32 hf .. 32 hf + 31
             const int row = blockIdx.x * kTmRows + r, cb = 32 * hf;
-            uint32_t d[32];
-            tmem_ld32(tmem + lane_base + (uint32_t)cb, d);
+            float sum[32];
+#pragma unroll 1
+            for (int acc = 0; acc < kTmAccs; acc++) {
+                uint32_t d[32];
+                tmem_ld32(tmem + lane_base + (uint32_t)(acc * kTmAccCols + cb), d);
+#pragma unroll
+                for (int j = 0; j < 32; j++) sum[j] = acc ? sum[j] + __uint_as_float(d[j]) : __uint_as_float(d[j]);
+            }
             if (row < p.rows)
 #pragma unroll
                 for (int j = 0; j < 32; j++) {
                     const int tok = cb + j;
                     if (tok < count)
-                        __stcg(p.ws + ((size_t)split * p.t_stride + tok) * p.ws_rows + row,
-                               __uint_as_float(d[j]) * p.inv_scale[tok]);
+                        __stcg(p.ws + ((size_t)split * p.t_stride + tok) * p.ws_rows + row, sum[j] * p.inv_scale[tok]);
                 }
         }
     }

@@ -279,6 +279,50 @@ def prefill_tokens(checkpoint, count):
     return tok
 
 
+def attention_block(length, count, reps=20):
+    """Blocks of `count` query rows at positions length..length+count-1 (the
+    prefill/append attention) through lunelette_cuda_attention on a random
+    paged pool: mean device time (CUDA events) of `reps` back-to-back calls after
+    one untimed call (an ncu target with -s 1 -c 1). FLOPs: QK and PV per query
+    row and causally visible key (`useful`), times 3 for the hi/lo terms the
+    tensor cores execute (`issued`)."""
+    import torch
+    import lunelette_b200 as L
+    lib = L.library()
+    total = length + count
+    num_pages = (total + 63) // 64
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    pool = torch.randn(num_pages * 2 * 8 * 64 * 128, device="cuda", generator=gen)
+    table = torch.arange(num_pages, dtype=torch.int32, device="cuda")
+    q = torch.randn(count, 4096, device="cuda", generator=gen)
+    out = torch.empty(count, 4096, device="cuda")
+    slots = 65536
+    acc = torch.empty(slots * 128, device="cuda")
+    ml = torch.empty(slots * 2, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def call():
+        assert lib.lunelette_cuda_attention(q.data_ptr(), pool.data_ptr(), table.data_ptr(), num_pages, 0, length,
+                                            count, out.data_ptr(), acc.data_ptr(), ml.data_ptr(), slots,
+                                            stream.cuda_stream) == 0
+
+    call()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(reps):
+        call()
+    stop.record(stream)
+    torch.cuda.synchronize()
+    us = start.elapsed_time(stop) * 1000 / reps
+    keys = sum(length + t + 1 for t in range(count))
+    useful = 2 * 2 * 32 * 128 * keys
+    peak, kind = tensor_peak()
+    return {"length": length, "count": count, "us": us, "useful_tflops": useful / us / 1e6,
+            "issued_tflops": 3 * useful / us / 1e6, "frac_issued": 3 * useful / us / 1e6 / peak,
+            "peak_tflops": peak, "peak_kind": kind}
+
+
 def batch_step(checkpoint, sessions=64, seed=5, pool=None):
     """A profiling target for config 4: `sessions` sessions with prompts ~
     U[256, 4096] (seeded) prefilled, one warm-up batched decode step, then one
@@ -332,6 +376,9 @@ def main():
                     help="prompt length before the timed decode steps of --decode-phases (4096: config 2)")
     ap.add_argument("--prefill-tokens", nargs=2, metavar=("CHECKPOINT", "N"), default=None,
                     help="prefill N ids twice, the second between cudaProfilerStart/Stop (a profiling target)")
+    ap.add_argument("--attention", metavar="LENGTH,COUNT", default=None,
+                    help="time the block attention (tcgen05 kernel) of COUNT queries at LENGTH positions")
+    ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--batch-step", metavar="CHECKPOINT", default=None,
                     help="one batched decode step of ragged sessions between cudaProfilerStart/Stop")
     ap.add_argument("--batch-sessions", type=int, default=64)
@@ -342,6 +389,10 @@ def main():
         n = args.batch_sessions
         # the pool holds the sessions' prompts plus the two steps (pages of 64)
         print(json.dumps({"first_token": batch_step(args.batch_step, n, pool=None if n >= 64 else n * 4160)}))
+        return
+    if args.attention:
+        length, count = (int(v) for v in args.attention.split(","))
+        print(json.dumps(attention_block(length, count, args.reps)))
         return
     if args.prefill_tokens:
         print(json.dumps({"first_token": prefill_tokens(args.prefill_tokens[0], int(args.prefill_tokens[1]))}))
