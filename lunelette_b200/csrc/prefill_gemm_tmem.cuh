@@ -44,11 +44,13 @@ constexpr int kTmTStages = 8;                         // A stages in tensor memo
 constexpr int kTmW8 = kTmRows * kPgK;                 // 8192: one stage of FP8 weights
 constexpr int kTmABytes = (kTmMaxTokens / 8) * 1024;  // 8192: one part (hi or lo) of a stage's activations
 constexpr int kTmStageCols = kPgK / 2;                // 32 TMEM columns: one stage's A (64 FP16 per row)
-constexpr int kTmAccCols = 64;                        // columns of one accumulator (>= tokens rounded to 16)
-// MMAs that accumulate into one TMEM tile run one after another (each waits for
-// the previous result), so a stage's 8 MMAs rotate over kTmAccs independent
-// accumulators, which the epilogue adds in a fixed order
-constexpr int kTmAccs = 4;
+// A stage's activations are one B operand of N = 2 n rows: the hi tile's n
+// token rows followed by the lo tile's (n = tokens rounded up to 16), so one
+// MMA per k-step covers both parts (MMA issue, not tensor work, is what a
+// stage of this small GEMM spends); D column t is W.hi_t and column n + t is
+// W.lo_t. The k-steps alternate between two accumulators, added in the epilogue.
+constexpr int kTmAccCols = 2 * kTmMaxTokens;          // columns of one accumulator (2 n)
+constexpr int kTmAccs = 2;
 constexpr int kTmTmemCols = 512;                      // accumulator + A stages, a power of two
 constexpr int kTmWOffset = 0;
 constexpr int kTmAOffset = kTmWOffset + kTmWStages * kTmW8;
@@ -92,7 +94,7 @@ static __global__ void __launch_bounds__(kTmThreads, 1)
     const int tile0 = blockIdx.x * (kTmRows / kTileRows);
     const int count = min(p.count, kTmMaxTokens);
     const int n = (count + 15) & ~15;                            // MMA N
-    const uint32_t abytes = (uint32_t)((count + 7) / 8) * 1024;  // 8-token atoms of a part
+    const uint32_t nbytes = (uint32_t)(n / 8) * 1024;             // 8-token atoms of a part (n rows)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTmWStages; s++) {
@@ -150,9 +152,9 @@ static __global__ void __launch_bounds__(kTmThreads, 1)
                     if (u == 0 || mbar_test_wait(&aempty[s], (u - 1) & 1)) {
                         uint8_t *st = aring + s * 2 * kTmABytes;
                         const uint8_t *a = p.xs + ((size_t)(k0 + ia) * 2) * kPgATile;
-                        mbar_expect_tx(&afull[s], 2 * abytes);
-                        bulk_g2s(st, a, abytes, &afull[s]);
-                        bulk_g2s(st + kTmABytes, a + kPgATile, abytes, &afull[s]);
+                        mbar_expect_tx(&afull[s], 2 * nbytes);
+                        bulk_g2s(st, a, nbytes, &afull[s]);                   // hi: B rows 0 .. n - 1
+                        bulk_g2s(st + nbytes, a + kPgATile, nbytes, &afull[s]);  // lo: B rows n .. 2 n - 1
                         ia++;
                         progressed = true;
                     }
@@ -175,7 +177,7 @@ static __global__ void __launch_bounds__(kTmThreads, 1)
             mbar_wait_bounded(&afull[i % kTmAStages], (i / kTmAStages) & 1, abort_word, p.error, kPgSpinLimit);
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t idesc = f16_idesc(kTmRows, n);
+            const uint32_t idesc = f16_idesc(kTmRows, 2 * n);
             bool ok = true;
             for (int i = 0; i < nk && ok; i++) {
                 const int s = i % kTmAStages, t = i % kTmTStages;
@@ -186,14 +188,11 @@ static __global__ void __launch_bounds__(kTmThreads, 1)
                 const uint32_t b0 = smem_u32(aring + s * 2 * kTmABytes);
                 const uint32_t a_cols = tmem + (uint32_t)(kTmAccs * kTmAccCols + t * kTmStageCols);
 #pragma unroll
-                for (int k = 0; k < kPgK / 16; k++)
-#pragma unroll
-                    for (int part = 0; part < 2; part++) {
-                        const int acc = (2 * k + part) % kTmAccs;
-                        tc_mma_f16_tmem_a(tmem + (uint32_t)(acc * kTmAccCols), a_cols + (uint32_t)(k * 8),
-                                          sw128_desc(b0 + part * kTmABytes + k * 32), idesc,
-                                          i > 0 || 2 * k + part >= kTmAccs);
-                    }
+                for (int k = 0; k < kPgK / 16; k++) {
+                    const int acc = k % kTmAccs;
+                    tc_mma_f16_tmem_a(tmem + (uint32_t)(acc * kTmAccCols), a_cols + (uint32_t)(k * 8),
+                                      sw128_desc(b0 + k * 32), idesc, i > 0 || k >= kTmAccs);
+                }
                 tc_commit(&aempty[s]);
                 tc_commit(&tempty[t]);
             }
@@ -250,13 +249,20 @@ static __global__ void __launch_bounds__(kTmThreads, 1)
             // accumulator: lane = weight row, column = token; half hf takes
             // tokens 32 hf .. 32 hf + 31
             const int row = blockIdx.x * kTmRows + r, cb = 32 * hf;
+            // (acc 0 + acc 1) of the hi column plus the same of the lo column
             float sum[32];
 #pragma unroll 1
-            for (int acc = 0; acc < kTmAccs; acc++) {
-                uint32_t d[32];
-                tmem_ld32(tmem + lane_base + (uint32_t)(acc * kTmAccCols + cb), d);
+            for (int part = 0; part < 2; part++) {
+                float ps[32];
+#pragma unroll 1
+                for (int acc = 0; acc < kTmAccs; acc++) {
+                    uint32_t d[32];
+                    tmem_ld32(tmem + lane_base + (uint32_t)(acc * kTmAccCols + part * n + cb), d);
 #pragma unroll
-                for (int j = 0; j < 32; j++) sum[j] = acc ? sum[j] + __uint_as_float(d[j]) : __uint_as_float(d[j]);
+                    for (int j = 0; j < 32; j++) ps[j] = acc ? ps[j] + __uint_as_float(d[j]) : __uint_as_float(d[j]);
+                }
+#pragma unroll
+                for (int j = 0; j < 32; j++) sum[j] = part ? sum[j] + ps[j] : ps[j];
             }
             if (row < p.rows)
 #pragma unroll
