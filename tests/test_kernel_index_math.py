@@ -1,9 +1,11 @@
-"""CPU restatements of the index arithmetic of three kernels, checked against
+"""CPU restatements of the index arithmetic of the kernels, checked against
 the dense operation they implement (no GPU): the persistent decode kernel's
 down slices (one 4-D tensor copy gathers 24 tile pieces of a 64-column slice,
 paired into m16n8k16 A tiles), the batched head's column order (A fragments
-read straight from row-major BF16 rows, B rows staged in the same order), and
-the split attention's warp reduce-scatter (lane l ends with the sum of index l).
+read straight from row-major BF16 rows, B rows staged in the same order), the
+split attention's warp reduce-scatter (lane l ends with the sum of index l),
+the small-block tcgen05 GEMM's converter reads and joint hi|lo operand, and
+the tcgen05 block attention's swizzled K and V^T operand tiles.
 """
 import numpy as np
 
@@ -111,3 +113,77 @@ def test_reduce_scatter_leaves_lane_l_with_index_l():
         d = new
         width //= 2
     assert np.allclose([d[lane][0] for lane in range(32)], vals.sum(axis=0))
+
+
+def sw128_offset(r, k):
+    """Byte offset of FP16 element (row r, k < 64) in a K-major 128-byte-swizzle
+    tile (8-row atoms of 1024 bytes): the operand layout of the tcgen05 kernels."""
+    return (r >> 3) * 1024 + (r & 7) * 128 + ((((k >> 3) ^ (r & 7)) & 7) << 4) + (k & 7) * 2
+
+
+def test_small_block_gemm_converters_rebuild_each_weight_row():
+    """prefill_gemm_tmem.cuh: a stage is one 512-byte piece (8 rows x 64
+    columns) of each of 16 tiles; thread r reads its row's four 16-byte chunks
+    starting at chunk (lane >> 1) & 3, undoes the rotation and stores words
+    a[8 j + c] (columns 16 j + 2 c + {0, 1}) and a[8 j + c + 4] (+ {8, 9}) into
+    tensor-memory columns 0..31, column m holding K elements 2 m and 2 m + 1."""
+    rng = np.random.default_rng(8)
+    rows, cols = 128, 3072
+    codes = rng.integers(0, 256, (rows, cols), dtype=np.uint8)
+    tiled = tile_reference(codes)
+    nb = cols // 128
+    for chunk in (0, 5, 47):
+        stage = np.concatenate([tiled[t * nb * 1024 + chunk * 512: t * nb * 1024 + chunk * 512 + 512]
+                                for t in range(16)])
+        for r in range(rows):
+            lane = r & 31
+            rot = (lane >> 1) & 3
+            base = (r >> 3) * 512 + (r & 7) * 64
+            reads = [stage[base + 16 * ((k + rot) & 3): base + 16 * ((k + rot) & 3) + 16] for k in range(4)]
+            cols_of_word = np.zeros(32 * 2, np.uint8)  # TMEM column m -> K elements 2m, 2m+1
+            for c in range(4):
+                chunk_bytes = reads[(c - rot) & 3]
+                for j in range(4):
+                    word = chunk_bytes[4 * j: 4 * j + 4]
+                    for half, m in ((0, 8 * j + c), (1, 8 * j + c + 4)):
+                        cols_of_word[2 * m: 2 * m + 2] = word[2 * half: 2 * half + 2]
+            assert np.array_equal(cols_of_word, codes[r, 64 * chunk: 64 * chunk + 64]), (chunk, r)
+
+
+def test_small_block_gemm_hi_and_lo_tiles_form_one_operand():
+    """One MMA per k-step reads B rows 0..n-1 from the hi tile and n..2n-1 from
+    the lo tile copied right after it (n a multiple of 16): row n + r of the
+    joint operand is row r of the lo part."""
+    for n in (16, 32, 48, 64):
+        nbytes = n // 8 * 1024
+        for r in range(n):
+            for k in (0, 7, 8, 33, 63):
+                assert sw128_offset(n + r, k) == nbytes + sw128_offset(r, k)
+
+
+def test_tc_attention_operand_tiles_cover_their_buffers_once():
+    """attention_tc.cuh converters: K unit g = (key g >> 4, dims 8 (g & 15) ..)
+    goes to chunk (g & 15) >> 3 (8 KB each) at sw128_offset(key, 8 (g & 7));
+    V^T unit (dim d, keys 8 kg ..) to sw128_offset(d, 8 kg). Every FP16 element
+    of the 16 KB parts is written exactly once, where the K-major swizzled
+    layout puts element (row, k)."""
+    k_seen = np.zeros(16384, np.int32)
+    for ct in range(64):
+        for it in range(16):
+            g = ct + 64 * it
+            key, grp = g >> 4, g & 15
+            off = (grp >> 3) * 8192 + sw128_offset(key, (grp & 7) * 8)
+            for e in range(8):
+                dim = 8 * grp + e
+                assert off + 2 * e == (dim // 64) * 8192 + sw128_offset(key, dim % 64)
+                k_seen[off + 2 * e: off + 2 * e + 2] += 1
+    assert np.all(k_seen == 1)
+    v_seen = np.zeros(16384, np.int32)
+    for ct in range(64):
+        for it in range(16):
+            d, kg = ct + 64 * (it & 1), it >> 1
+            off = sw128_offset(d, 8 * kg)
+            for e in range(8):
+                assert off + 2 * e == sw128_offset(d, 8 * kg + e)
+                v_seen[off + 2 * e: off + 2 * e + 2] += 1
+    assert np.all(v_seen == 1)
