@@ -517,56 +517,6 @@ struct PrefillFinishParams {
     int table_stride;
 };
 
-// Sum over the K ranges of one float4 of partials, ranges in order (the same
-// additions as a plain loop, so the result does not change), with the loads
-// of four ranges issued together.
-__device__ __forceinline__ float4 sum_ranges4(const float *p, size_t stride, int splits)
-{
-    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-    int s = 0;
-    for (; s + 4 <= splits; s += 4) {
-        float4 b[4];
-#pragma unroll
-        for (int k = 0; k < 4; k++) b[k] = __ldcg(reinterpret_cast<const float4 *>(p + (size_t)(s + k) * stride));
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            a.x += b[k].x;
-            a.y += b[k].y;
-            a.z += b[k].z;
-            a.w += b[k].w;
-        }
-    }
-    for (; s < splits; s++) {
-        const float4 b = __ldcg(reinterpret_cast<const float4 *>(p + (size_t)s * stride));
-        a.x += b.x;
-        a.y += b.y;
-        a.z += b.z;
-        a.w += b.w;
-    }
-    return a;
-}
-__device__ __forceinline__ float2 sum_ranges2(const float *p, size_t stride, int splits)
-{
-    float2 a = make_float2(0.f, 0.f);
-    int s = 0;
-    for (; s + 4 <= splits; s += 4) {
-        float2 b[4];
-#pragma unroll
-        for (int k = 0; k < 4; k++) b[k] = __ldcg(reinterpret_cast<const float2 *>(p + (size_t)(s + k) * stride));
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            a.x += b[k].x;
-            a.y += b[k].y;
-        }
-    }
-    for (; s < splits; s++) {
-        const float2 b = __ldcg(reinterpret_cast<const float2 *>(p + (size_t)s * stride));
-        a.x += b.x;
-        a.y += b.y;
-    }
-    return a;
-}
-
 __device__ __forceinline__ float finish_scale(const PrefillFinishParams &p, int r)
 {
     return r < p.bound[0] ? p.scale[0] : (r < p.bound[1] ? p.scale[1] : p.scale[2]);
@@ -581,8 +531,12 @@ static __global__ void __launch_bounds__(256) prefill_finish_kernel(PrefillFinis
     const int t = blockIdx.y;
     const int pr = blockIdx.x * blockDim.x + threadIdx.x;
     if (2 * pr >= p.rows) return;
-    const float2 sum = sum_ranges2(p.ws + (size_t)t * p.ws_rows + 2 * pr, (size_t)p.t_stride * p.ws_rows, p.splits);
-    float a = sum.x, b = sum.y;
+    float a = 0.0f, b = 0.0f;
+    for (int s = 0; s < p.splits; s++) {
+        const float2 v = __ldcg(reinterpret_cast<const float2 *>(p.ws + ((size_t)s * p.t_stride + t) * p.ws_rows) + pr);
+        a += v.x;
+        b += v.y;
+    }
     if constexpr (EPI == kEpiStore || EPI == kEpiResidual) {
         const int r = 2 * pr;
         a *= finish_scale(p, r);
@@ -657,8 +611,13 @@ static __global__ void __launch_bounds__(kFsThreads) prefill_finish_split_kernel
             if (sp.gain) g[i] = *reinterpret_cast<const float4 *>(sp.gain + c);
             if constexpr (EPI == kEpiSwiGLU) {
                 // features c..c+3: gate at storage rows 2f, up at 2f + 1
-                const float4 lo = sum_ranges4(ws + 2 * c, split_stride, f.splits);
-                const float4 hi = sum_ranges4(ws + 2 * c + 4, split_stride, f.splits);
+                float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+                for (int s = 0; s < f.splits; s++) {
+                    const float4 a = __ldcg(reinterpret_cast<const float4 *>(ws + s * split_stride + 2 * c));
+                    const float4 b = __ldcg(reinterpret_cast<const float4 *>(ws + s * split_stride + 2 * c + 4));
+                    lo.x += a.x; lo.y += a.y; lo.z += a.z; lo.w += a.w;
+                    hi.x += b.x; hi.y += b.y; hi.z += b.z; hi.w += b.w;
+                }
                 const float gv[4] = {lo.x * f.scale[0], lo.z * f.scale[0], hi.x * f.scale[0], hi.z * f.scale[0]};
                 const float uv[4] = {lo.y * f.scale[1], lo.w * f.scale[1], hi.y * f.scale[1], hi.w * f.scale[1]};
                 float o[4];
@@ -666,7 +625,11 @@ static __global__ void __launch_bounds__(kFsThreads) prefill_finish_split_kernel
                 for (int k = 0; k < 4; k++) o[k] = (gv[k] / (1.0f + expf(-gv[k]))) * uv[k];
                 v[i] = make_float4(o[0], o[1], o[2], o[3]);
             } else {
-                const float4 a = sum_ranges4(ws + c, split_stride, f.splits);
+                float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int s = 0; s < f.splits; s++) {
+                    const float4 b = __ldcg(reinterpret_cast<const float4 *>(ws + s * split_stride + c));
+                    a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+                }
                 const float4 r = *reinterpret_cast<const float4 *>(f.res + (size_t)t * f.res_stride + c);
                 v[i] = make_float4(r.x + a.x * finish_scale(f, c), r.y + a.y * finish_scale(f, c + 1),
                                    r.z + a.z * finish_scale(f, c + 2), r.w + a.w * finish_scale(f, c + 3));
