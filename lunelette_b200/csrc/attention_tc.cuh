@@ -30,6 +30,9 @@
 // FP32 accumulation, as the mma.sync kernel in attention.cuh does; the softmax
 // runs in base 2 (scores scaled by log2 e).
 //
+// The CTA takes all 512 tensor-memory columns of its SM: its 225 KB of shared
+// memory leave no room for a second CTA of this or any other tcgen05 kernel of
+// this library (each needs more than 128 KB), so the allocation never waits.
 // Tensor memory (512 columns): Q hi [0, 64), Q lo [64, 128) (FP16 pairs),
 // S/P buffers [128, 192) and [192, 256) (64 FP32 scores, then P hi in the first
 // 32 columns and P lo in the next 32), O [256, 384) (128 FP32 dims). The MMAs of

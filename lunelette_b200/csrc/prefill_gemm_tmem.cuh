@@ -7,24 +7,32 @@
 // (prefill_gemm.cuh) converts to FP16 through shared memory, tiles 256 tokens
 // per MMA whatever the block holds and so runs about as long at 64 tokens as
 // at 256. Here one CTA owns 128 weight rows and a K range for all the block's
-// tokens (MMA M = 128 rows, N = the tokens rounded up to 16):
-//   warp 0      tensor copies of the FP8 weight stages (128 rows x 64 columns,
-//               the 4-D map of the pair GEMM) and bulk copies of the split
-//               activations' hi and lo operand tiles;
+// tokens (MMA M = 128 rows, N = 2 x the tokens rounded up to 16: the hi and
+// the lo activation tiles side by side, one MMA per k-step for both):
+//   warp 0      tensor copies of the FP8 weight stages (128 rows x 64 columns:
+//               one 512-byte piece of each of 16 tiles, a 3-D map of 8-byte
+//               elements) and bulk copies of the split activations' hi and lo
+//               operand tiles, each into its own ring;
 //   warp 1      allocates tensor memory; one lane issues the MMAs
 //               (tcgen05.mma.cta_group::1.kind::f16 with A in tensor memory,
-//               B = activations in shared memory) and commits;
-//   warps 2-9   convert: thread = weight row (its warp's quarter of the TMEM
-//               lanes), two warps per quarter, each taking half of the row's 64
-//               FP8 bytes of a stage (32 columns) to 16 FP16 pairs in registers
-//               and one tcgen05.st into that stage's A buffer; the 8-byte reads
-//               start at a chunk rotated by lane so that a warp's reads spread
-//               over the shared-memory banks (4 wavefronts instead of 16); then
-//               the epilogue: the accumulator (row x token) times the token's
-//               2^-e into the FP32 partials of its K range, which the finish
-//               kernels add in order as for the pair GEMM.
+//               B = activations in shared memory), alternating between two
+//               accumulators, and commits;
+//   warps 2-9   convert, in two groups of four (one warp per TMEM lane
+//               quarter) that take alternating stages: thread = weight row,
+//               its 64 FP8 bytes of the stage to 32 FP16 pairs in registers
+//               and one tcgen05.st into that stage's A buffer; the 16-byte
+//               reads start at a chunk rotated by lane so a warp's reads
+//               spread over the shared-memory banks; then the epilogue (group g
+//               takes tokens 32 g .. 32 g + 31): the accumulators' hi and lo
+//               columns added, times the token's 2^-e, into the FP32 partials
+//               of its K range, which the finish kernels add in order as for
+//               the pair GEMM.
 // The FP16 weights never touch shared memory, and the MMA does no work for
 // token tiles the block does not have.
+//
+// The CTA takes all 512 tensor-memory columns of its SM; its 198 KB of shared
+// memory keep any other tcgen05 kernel of this library off that SM meanwhile,
+// so the allocation never waits.
 //
 // Tensor-memory A operand (kind::f16, M = 128, cta_group::1): row r in lane r,
 // K element k of a 16-element step in 32-bit column k / 2 (low half even k),
