@@ -181,3 +181,52 @@ def test_greedy_rule_matches_reference(oracle):
             assert not np.all(np.isfinite(v))
         else:
             assert greedy(v) == case["token"]
+
+
+def test_operators_match_float64_on_random_inputs(oracle):
+    """Beyond the reference's analytic cases: the oracle's projection (FP32 and
+    FP8), RMSNorm, RoPE and attention on random inputs against independent
+    float64 restatements of the same formulas, within bounds set by FP32
+    rounding (the oracle sums in FP32 with per-lane Kahan compensation)."""
+    rng = np.random.default_rng(2024)
+    # FP32 projection, an awkward shape: |error| <= 1e-6 x sum |w x|
+    w = rng.standard_normal((67, 515)).astype(np.float32)
+    x = rng.standard_normal((3, 515)).astype(np.float32)
+    got = oracle.project(w, x)
+    want = x.astype(np.float64) @ w.astype(np.float64).T
+    bound = np.abs(x).astype(np.float64) @ np.abs(w).astype(np.float64).T
+    assert np.all(np.abs(got - want) <= 1e-6 * bound + 1e-30)
+    # FP8 projection: decode (bit-exact, pinned above) x scale x input
+    codes = rng.integers(0, 256, (40, 3072)).astype(np.uint8)
+    codes[(codes & 127) == 127] = 0
+    decoded = np.array([oracle.fp8_decode(int(c)) for c in range(256)], np.float64)[codes]
+    scale = 0.00123
+    xs = rng.standard_normal((2, 3072)).astype(np.float32)
+    got = oracle.project_fp8(codes, scale, xs)
+    want = (xs.astype(np.float64) @ decoded.T) * scale
+    bound = (np.abs(xs).astype(np.float64) @ np.abs(decoded).T) * scale
+    assert np.all(np.abs(got - want) <= 1e-6 * bound + 1e-30)
+    # RMSNorm over the model width
+    gain = rng.uniform(0.5, 1.5, 3072).astype(np.float32)
+    xn = (rng.standard_normal((4, 3072)) * 3).astype(np.float32)
+    got = oracle.norm(gain, xn)
+    xd = xn.astype(np.float64)
+    want = gain * (xd / np.sqrt((xd * xd).mean(axis=1, keepdims=True) + 1e-5))
+    assert np.abs(got - want).max() <= 4e-6 * np.abs(want).max()
+    # RoPE (split-half rotation, query scale) at random positions
+    positions = rng.integers(0, 4352, 6).astype(np.uint32)
+    xr = rng.standard_normal((6, 128)).astype(np.float32)
+    cos = np.stack([oracle.yarn(int(p))[0] for p in positions])
+    sin = np.stack([oracle.yarn(int(p))[1] for p in positions])
+    for query in (0, 1):
+        got = oracle.rope(xr, cos, sin, positions, query)
+        rot = np.concatenate([-xr[:, 64:], xr[:, :64]], axis=1).astype(np.float64)
+        want = xr * cos.astype(np.float64) + rot * sin
+        assert np.abs(got - want).max() <= 2e-6 * np.abs(want).max()
+    # causal GQA attention, random rows, a prefix that is not a tile multiple
+    count, prefix = 5, 70
+    q = rng.standard_normal((count, 4096)).astype(np.float32)
+    k = rng.standard_normal((prefix + count, 1024)).astype(np.float32)
+    v = rng.standard_normal((prefix + count, 1024)).astype(np.float32)
+    got = oracle.attention(q, k, v, prefix)
+    assert np.abs(got - attention_reference(q, k, v, prefix)).max() <= 1e-5
