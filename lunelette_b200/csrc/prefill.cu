@@ -220,8 +220,6 @@ cudaError_t lun_launch_prefill_gemm(const GemvParams &p, int count, const Prefil
     g.ws = w.ws;
     g.ws_rows = pl.row_tiles * kP2N;
     g.error = w.error;
-    CUtensorMap wmap;
-    if ((e = weight_tensor_map(&wmap, p.W, p.rows, g.nb)) != cudaSuccess) return e;
     if (pl.tmem_a) {
         TmGemmParams t;
         t.rows = p.rows;
@@ -239,6 +237,8 @@ cudaError_t lun_launch_prefill_gemm(const GemvParams &p, int count, const Prefil
         return launch(prefill_gemm_tmem_kernel, dim3((p.rows + kTmRows - 1) / kTmRows, 1, pl.splits),
                       dim3(kTmThreads), kTmSmemBytes, stream, t, wide);
     }
+    CUtensorMap wmap;
+    if ((e = weight_tensor_map(&wmap, p.W, p.rows, g.nb)) != cudaSuccess) return e;
     return launch(prefill_gemm_pair_kernel, dim3(2 * pl.row_tiles, (pl.token_tiles + 1) / 2, pl.splits),
                   dim3(kPgThreads), kP2SmemBytes, stream, g, wmap);
 }
