@@ -273,6 +273,16 @@ class Runtime:
             raise LuneletteError("trace copy failed")
         return out
 
+    def snapshot(self, count, normalized=False):
+        """The last call's layer-25 output rows (or its final-norm rows) while
+        tracing is on: a copy of the `count` rows lunelette_cuda_snapshot
+        borrows (the hook the reference's comparator reads)."""
+        ptr = library().lunelette_cuda_snapshot(self.handle, 1 if normalized else 0)
+        if not ptr:
+            raise LuneletteError("no snapshot: tracing is off or the sequence holds no published result")
+        view = np.ctypeslib.as_array(ctypes.cast(ptr, ctypes.POINTER(ctypes.c_float)), shape=(count, HIDDEN))
+        return view.copy()
+
 
 class Batch:
     """Many independent sessions over one weight replica and a paged KV pool

@@ -64,6 +64,9 @@ def test_c0_prefill_per_layer_and_greedy_32(runtime, oracle_model):
     try:
         logits = runtime.prefill(ids).copy()
         layers = [runtime.trace_copy(l, len(ids)) for l in range(27)]
+        # the comparator hook's view of the same call: layer 25 and final norm
+        assert np.array_equal(runtime.snapshot(len(ids)), layers[25])
+        assert np.array_equal(runtime.snapshot(len(ids), normalized=True), layers[26])
     finally:
         runtime.trace(False)
     want, trace, final = oracle_model.forward(ids, trace=True, final_norm=True)

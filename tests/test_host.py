@@ -123,6 +123,7 @@ def test_calls_without_a_context_fail_before_any_work(lib):
     tokens = (ctypes.c_int64 * 4)()
     assert lib.lunelette_cuda_decode_loop(None, 1, 4, tokens, None, None, err, 512) == -1
     assert b"decode loop" in err.value
+    assert not lib.lunelette_cuda_snapshot(None, 0) and not lib.lunelette_cuda_snapshot(None, 1)
 
 
 def test_oracle_side_writer_matches_the_product_writer(checkpoint_path, tmp_path):
