@@ -1007,7 +1007,7 @@ extern "C" int lun_device_run(lun_device *d, const int64_t *ids, size_t count, s
         if ((e = cudaStreamSynchronize(d->stream)) != cudaSuccess) goto bad;
         if (d->pf.error && *d->h_pf_error) {
             cudaMemset(d->pf.error, 0, sizeof(int));
-            if (error && capacity) snprintf(error, capacity, "prefill: GEMM pipeline wait gave up");
+            if (error && capacity) snprintf(error, capacity, "prefill: tensor-core pipeline wait gave up (GEMM or block attention)");
             return -1;
         }
         if (mega && *d->h_error) {
