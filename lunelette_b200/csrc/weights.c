@@ -2,6 +2,7 @@
 #include "weights.h"
 
 #include <math.h>
+#include <stdlib.h>
 #include <stdio.h>
 #include <string.h>
 
@@ -17,115 +18,187 @@ const lun_block_weight lun_block_weights[LUN_BLOCK_WEIGHTS] = {
     {"mlp.down_proj.weight", LUN_HIDDEN, LUN_INNER},
 };
 
-static const char *companions[2] = {"weight_scale_inv", "activation_scale"};
+/* The checkpoint contract as a catalogue: every tensor the decoder reads
+ * (embedding, final norm, 26 x 9 block tensors) and the two rank-0 BF16 scalars
+ * beside each FP8 linear ("<stem>.weight_scale_inv", "<stem>.activation_scale"),
+ * each with its dtype and shape, listed in the order failures are reported:
+ * the embedding, the final norm, then layer by layer each tensor followed by its
+ * scalars. One pass over the file's "language_model." tensors finds every
+ * entry by binary search over the names and remembers the first tensor the
+ * contract does not list; tensors outside "language_model." (a vision tower,
+ * a projector) are not this backend's concern. */
+enum { ENTRY_TENSOR, ENTRY_SCALE, ENTRY_ACTIVATION_SCALE };
+enum { CONTRACT_ENTRIES = LUN_WEIGHT_COUNT + 2 * LUN_LAYERS * 7 };  /* 7 FP8 linears a layer */
 
-/* "<prefix>.weight" -> "<prefix>.<suffix>" */
-static void companion_name(char *out, size_t capacity, const char *name, const char *suffix)
+typedef struct {
+    char name[LUN_ST_MAX_NAME + 32];
+    lun_dtype dtype;
+    size_t rows, cols;  /* cols == 0: a vector of rows elements */
+    int kind;           /* ENTRY_* */
+    size_t weight;      /* index into lun_weights.w (of the owning tensor for a scalar) */
+    const lun_tensor *found;
+} contract_entry;
+
+static const char *dtype_name(lun_dtype dtype)
 {
-    size_t stem = strlen(name) - strlen("weight");
-    snprintf(out, capacity, "%.*s%s", (int)stem, name, suffix);
+    return dtype == LUN_F8_E4M3 ? "F8_E4M3" : "BF16";
 }
 
-static int expect(lun_weights *weights, size_t index, const char *name, size_t rows,
-    size_t cols, char *error, size_t capacity)
+static size_t contract_add(contract_entry *c, size_t n, const char *name, lun_dtype dtype, size_t rows,
+    size_t cols, int kind, size_t weight)
 {
-    const lun_tensor *t = lun_st_find(&weights->file, name);
-    lun_dtype want = (cols && index != 0) ? LUN_F8_E4M3 : LUN_BF16;
-    if (!t || t->dtype != want || t->rank != (cols ? 2u : 1u) || t->shape[0] != rows ||
-        (cols && t->shape[1] != cols)) {
-        if (cols) {
-            snprintf(error, capacity, "tensor %s: expected %s [%zu,%zu]", name,
-                want == LUN_BF16 ? "BF16" : "F8_E4M3", rows, cols);
-        } else {
-            snprintf(error, capacity, "tensor %s: expected BF16 [%zu]", name, rows);
-        }
-        return -1;
-    }
-    if (want == LUN_F8_E4M3) {
-        for (int i = 0; i < 2; i++) {
-            char scalar[LUN_ST_MAX_NAME + 32];
-            companion_name(scalar, sizeof scalar, name, companions[i]);
-            const lun_tensor *s = lun_st_find(&weights->file, scalar);
-            if (!s || s->dtype != LUN_BF16 || s->rank != 0 || s->end - s->begin != 2) {
-                snprintf(error, capacity, "scalar %s: expected BF16 rank0", scalar);
-                return -1;
+    snprintf(c[n].name, sizeof c[n].name, "%s", name);
+    c[n].dtype = dtype;
+    c[n].rows = rows;
+    c[n].cols = cols;
+    c[n].kind = kind;
+    c[n].weight = weight;
+    c[n].found = NULL;
+    return n + 1;
+}
+
+static size_t contract_build(contract_entry *c)
+{
+    size_t n = 0;
+    n = contract_add(c, n, "language_model.model.embed_tokens.weight", LUN_BF16, LUN_VOCAB, LUN_HIDDEN,
+        ENTRY_TENSOR, 0);
+    n = contract_add(c, n, "language_model.model.norm.weight", LUN_BF16, LUN_HIDDEN, 0, ENTRY_TENSOR, 1);
+    for (size_t layer = 0; layer < LUN_LAYERS; layer++) {
+        for (size_t slot = 0; slot < LUN_BLOCK_WEIGHTS; slot++) {
+            const lun_block_weight *b = &lun_block_weights[slot];
+            const size_t index = 2 + layer * LUN_BLOCK_WEIGHTS + slot;
+            char name[LUN_ST_MAX_NAME];
+            snprintf(name, sizeof name, "language_model.model.layers.%zu.%s", layer, b->suffix);
+            const int fp8 = b->cols != 0;  /* linears are FP8, norm gains BF16 */
+            n = contract_add(c, n, name, fp8 ? LUN_F8_E4M3 : LUN_BF16, b->rows, b->cols, ENTRY_TENSOR, index);
+            if (fp8) {
+                /* "<stem>.weight" -> "<stem>.weight_scale_inv" / "<stem>.activation_scale" */
+                const int stem = (int)(strlen(name) - strlen("weight"));
+                char scalar[LUN_ST_MAX_NAME + 32];
+                snprintf(scalar, sizeof scalar, "%.*sweight_scale_inv", stem, name);
+                n = contract_add(c, n, scalar, LUN_BF16, 0, 0, ENTRY_SCALE, index);
+                snprintf(scalar, sizeof scalar, "%.*sactivation_scale", stem, name);
+                n = contract_add(c, n, scalar, LUN_BF16, 0, 0, ENTRY_ACTIVATION_SCALE, index);
             }
         }
     }
-    weights->w[index].tensor = t;
-    weights->w[index].scale = 1.0f;
-    weights->w[index].elements = rows * (cols ? cols : 1);
+    return n;
+}
+
+static int entry_by_name(const void *a, const void *b)
+{
+    return strcmp((*(contract_entry *const *)a)->name, (*(contract_entry *const *)b)->name);
+}
+
+static int name_to_entry(const void *key, const void *item)
+{
+    return strcmp((const char *)key, (*(contract_entry *const *)item)->name);
+}
+
+/* 0 when the file's tensor matches the entry, else -1 with the reason. */
+static int entry_check(const contract_entry *e, char *error, size_t capacity)
+{
+    const lun_tensor *t = e->found;
+    if (e->kind != ENTRY_TENSOR) {
+        if (!t || t->dtype != LUN_BF16 || t->rank != 0 || t->end - t->begin != 2) {
+            snprintf(error, capacity, "scalar %s: an FP8 tensor needs this rank-0 BF16 value beside it", e->name);
+            return -1;
+        }
+        return 0;
+    }
+    char want[64];
+    if (e->cols) {
+        snprintf(want, sizeof want, "%s [%zu,%zu]", dtype_name(e->dtype), e->rows, e->cols);
+    } else {
+        snprintf(want, sizeof want, "%s [%zu]", dtype_name(e->dtype), e->rows);
+    }
+    if (!t) {
+        snprintf(error, capacity, "tensor %s: not in the checkpoint (the decoder reads %s)", e->name, want);
+        return -1;
+    }
+    const unsigned rank = e->cols ? 2u : 1u;
+    if (t->dtype != e->dtype || t->rank != rank || t->shape[0] != e->rows || (e->cols && t->shape[1] != e->cols)) {
+        snprintf(error, capacity, "tensor %s: the decoder reads %s here", e->name, want);
+        return -1;
+    }
     return 0;
 }
 
 static int validate(lun_weights *weights, char *error, size_t capacity)
 {
-    if (expect(weights, 0, "language_model.model.embed_tokens.weight", LUN_VOCAB, LUN_HIDDEN,
-            error, capacity) ||
-        expect(weights, 1, "language_model.model.norm.weight", LUN_HIDDEN, 0, error, capacity)) {
+    contract_entry *contract = calloc(CONTRACT_ENTRIES, sizeof *contract);
+    contract_entry **sorted = calloc(CONTRACT_ENTRIES, sizeof *sorted);
+    if (!contract || !sorted) {
+        free(contract);
+        free(sorted);
+        snprintf(error, capacity, "checkpoint contract: out of host memory");
         return -1;
     }
-    for (size_t layer = 0; layer < LUN_LAYERS; layer++) {
-        for (size_t slot = 0; slot < LUN_BLOCK_WEIGHTS; slot++) {
-            char name[LUN_ST_MAX_NAME];
-            const lun_block_weight *b = &lun_block_weights[slot];
-            snprintf(name, sizeof name, "language_model.model.layers.%zu.%s", layer, b->suffix);
-            if (expect(weights, 2 + layer * LUN_BLOCK_WEIGHTS + slot, name, b->rows, b->cols,
-                    error, capacity)) {
-                return -1;
-            }
-        }
+    const size_t n = contract_build(contract);
+    for (size_t i = 0; i < n; i++) {
+        sorted[i] = &contract[i];
     }
-    /* Every "language_model." tensor must be a known weight or companion;
-     * other prefixes (vision, projector) are left alone. */
+    qsort(sorted, n, sizeof *sorted, entry_by_name);
+    const char *stranger = NULL;
     for (size_t i = 0; i < weights->file.count; i++) {
-        const char *name = weights->file.tensors[i].name;
-        if (strncmp(name, "language_model.", 15) != 0) {
+        const lun_tensor *t = &weights->file.tensors[i];
+        if (strncmp(t->name, "language_model.", 15) != 0) {
             continue;
         }
-        int known = 0;
-        for (size_t j = 0; j < LUN_WEIGHT_COUNT && !known; j++) {
-            const lun_tensor *t = weights->w[j].tensor;
-            known = !strcmp(name, t->name);
-            if (!known && t->dtype == LUN_F8_E4M3) {
-                for (int k = 0; k < 2 && !known; k++) {
-                    char scalar[LUN_ST_MAX_NAME + 32];
-                    companion_name(scalar, sizeof scalar, t->name, companions[k]);
-                    known = !strcmp(name, scalar);
-                }
-            }
-        }
-        if (!known) {
-            snprintf(error, capacity, "Unexpected text tensor: %s", name);
-            return -1;
+        contract_entry **hit = bsearch(t->name, sorted, n, sizeof *sorted, name_to_entry);
+        if (hit) {
+            (*hit)->found = t;
+        } else if (!stranger) {
+            stranger = t->name;
         }
     }
-    return 0;
+    int status = 0;
+    for (size_t i = 0; i < n && !status; i++) {
+        status = entry_check(&contract[i], error, capacity);
+    }
+    if (!status && stranger) {
+        snprintf(error, capacity, "tensor %s: not part of the text model this backend runs", stranger);
+        status = -1;
+    }
+    for (size_t i = 0; i < n && !status; i++) {
+        const contract_entry *e = &contract[i];
+        if (e->kind == ENTRY_TENSOR) {
+            weights->w[e->weight].tensor = e->found;
+            weights->w[e->weight].scale = 1.0f;
+            weights->w[e->weight].elements = e->rows * (e->cols ? e->cols : 1);
+        } else if (e->kind == ENTRY_SCALE) {
+            weights->w[e->weight].scale_tensor = e->found;
+        } else {
+            weights->w[e->weight].activation_tensor = e->found;
+        }
+    }
+    free(sorted);
+    free(contract);
+    return status;
 }
 
+/* Both scalars of every FP8 tensor must be positive and finite; the weight
+ * scale becomes the tensor's dequantisation factor. The activation scale is
+ * only checked: activations are never quantised statically here. */
 static int read_scales(lun_weights *weights, char *error, size_t capacity)
 {
     for (size_t i = 0; i < LUN_WEIGHT_COUNT; i++) {
-        const lun_tensor *t = weights->w[i].tensor;
-        if (t->dtype != LUN_F8_E4M3) {
+        const lun_tensor *pair[2] = {weights->w[i].scale_tensor, weights->w[i].activation_tensor};
+        if (weights->w[i].tensor->dtype != LUN_F8_E4M3) {
             continue;
         }
         for (int k = 0; k < 2; k++) {
-            char scalar[LUN_ST_MAX_NAME + 32];
-            companion_name(scalar, sizeof scalar, t->name, companions[k]);
-            const lun_tensor *s = lun_st_find(&weights->file, scalar);
             unsigned char raw[2];
-            if (lun_st_read(&weights->file, s, 0, raw, 2)) {
-                snprintf(error, capacity, "scalar %s: read failed", scalar);
+            if (lun_st_read(&weights->file, pair[k], 0, raw, 2)) {
+                snprintf(error, capacity, "scalar %s: read failed", pair[k]->name);
                 return -1;
             }
-            float value = lun_bf16_to_f32((uint16_t)(raw[0] | raw[1] << 8));
+            const float value = lun_bf16_to_f32((uint16_t)(raw[0] | raw[1] << 8));
             if (!isfinite(value) || value <= 0) {
-                snprintf(error, capacity, "scalar %s: expected positive finite BF16", scalar);
+                snprintf(error, capacity, "scalar %s: holds %g, where an FP8 tensor's scalars must be positive finite BF16",
+                    pair[k]->name, value);
                 return -1;
             }
-            /* activation_scale is checked and then unused: weights are
-             * dequantised, activations are never statically quantised. */
             if (k == 0) {
                 weights->w[i].scale = value;
             }
@@ -161,7 +234,7 @@ int lun_weights_admission(const lun_weights *weights, size_t index, int compact,
 {
     const lun_tensor *t = index < LUN_WEIGHT_COUNT ? weights->w[index].tensor : NULL;
     if (!t || t->dtype != LUN_F8_E4M3) {
-        snprintf(error, capacity, "compact tensor %s: expected exact compact F8 element count",
+        snprintf(error, capacity, "tensor %s: code admission applies to F8_E4M3 tensors only",
             t ? t->name : "(invalid index)");
         return -1;
     }
@@ -171,8 +244,8 @@ int lun_weights_admission(const lun_weights *weights, size_t index, int compact,
         memcpy(&bits, &scale, sizeof bits);
         if (!(scale > 0) || !isnormal(scale) || (bits & 0xffffu)) {
             snprintf(error, capacity,
-                "compact tensor %s: compact scale must be positive FP32-normal widened BF16",
-                t->name);
+                "tensor %s: the compact strategies need a positive scale that is an FP32-normal widened BF16 "
+                "(got %g)", t->name, scale);
             return -1;
         }
     }
@@ -191,10 +264,9 @@ int lun_admit_codes(const lun_weights *weights, size_t index, const lun_admissio
 {
     for (size_t i = 0; i < count; i++) {
         if (!table->allowed[codes[i]]) {
-            snprintf(error, capacity, "compact tensor %s byte %llu code 0x%02x: "
-                "NaN or non-normal/overflow reconstructed product (scale %.9g)",
-                weights->w[index].tensor->name, (unsigned long long)(offset + i), codes[i],
-                scale);
+            snprintf(error, capacity, "tensor %s byte %llu code 0x%02x: code x scale %.9g is not admitted "
+                "(NaN, an overflow or a non-normal product)",
+                weights->w[index].tensor->name, (unsigned long long)(offset + i), codes[i], scale);
             return -1;
         }
     }

@@ -35,6 +35,9 @@ typedef struct {
         const lun_tensor *tensor;
         float scale; /* widened BF16 weight_scale_inv; 1 for BF16 tensors */
         size_t elements;
+        /* FP8 tensors: their rank-0 BF16 companions weight_scale_inv and
+         * activation_scale (NULL for BF16 tensors) */
+        const lun_tensor *scale_tensor, *activation_tensor;
     } w[LUN_WEIGHT_COUNT];
 } lun_weights;
 

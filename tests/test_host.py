@@ -226,11 +226,21 @@ def test_admission_rejects_planted_faults(corrupt_copy):
             L.validate_checkpoint(corrupt_copy, L.RESIDENT_FP32)
     finally:
         patch(corrupt_copy, at, old)
+    # a companion scalar under another name: the FP8 tensor lacks it (reported
+    # before the stray name, in the contract's order)
+    n, header = header_of(corrupt_copy)
+    at = 8 + header.index(act) + len(act) - 1
+    old = patch(corrupt_copy, at, b"f")
+    try:
+        with pytest.raises(L.LuneletteError, match="scalar " + act.replace(".", r"\.") + ": an FP8 tensor needs"):
+            L.validate_checkpoint(corrupt_copy, L.COMPACT_FP8_ARITHMETIC)
+    finally:
+        patch(corrupt_copy, at, old)
     n, header = header_of(corrupt_copy)
     at = 8 + header.index("embed_tokens") + len("embed_token")
     old = patch(corrupt_copy, at, b"z")
     try:
-        with pytest.raises(L.LuneletteError, match="embed_tokens.weight: expected BF16"):
+        with pytest.raises(L.LuneletteError, match="embed_tokens.weight: not in the checkpoint"):
             L.validate_checkpoint(corrupt_copy, L.COMPACT_FP8_ARITHMETIC)
     finally:
         patch(corrupt_copy, at, old)
