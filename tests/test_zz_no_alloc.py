@@ -1,8 +1,9 @@
 """The allocation-free attention entry point, for callers that cannot call
 cudaMalloc (an engine that has reserved the whole device for its own pool, or a
 loop where an allocation would synchronise the device): it must give the same
-output as lunelette_cuda_attention, which takes caller scratch, on two calls in a
-row (the second call finds the first call's partial results in the shared array).
+output as lunelette_cuda_attention, which takes caller scratch, and as the FP32
+oracle, on two calls in a row (the second call finds the first call's partial
+results in the shared array).
 
 Collected last on purpose (file name), and self-contained so it also passes
 alone in a fresh process."""
@@ -25,7 +26,7 @@ def pool_from_rows(k_rows, v_rows, table, num_pages, layer, layers):
     return pool.reshape(-1)
 
 
-def test_noalloc_matches_scratch_entry_point_twice(lib):
+def test_noalloc_matches_scratch_entry_point_twice(lib, oracle):
     import torch
     torch.cuda.init()
     stream = torch.cuda.current_stream().cuda_stream
@@ -53,6 +54,9 @@ def test_noalloc_matches_scratch_entry_point_twice(lib):
         assert lib.lunelette_cuda_attention(d_q.data_ptr(), d_pool.data_ptr(), d_table.data_ptr(),
                                             num_pages, 1, length, count, want.data_ptr(),
                                             acc.data_ptr(), ml.data_ptr(), SLOTS, stream) == 0
+        # the FP32 oracle on the same rows, so the fixed-scratch path is pinned to
+        # the restatement directly and not only through the scratch-taking one
+        exact = oracle.attention(q, k, v, length)
         for call in range(2):
             got = torch.full((count, 4096), float("nan"), dtype=torch.float32, device="cuda")
             rc = lib.lunelette_cuda_attention_noalloc(d_q.data_ptr(), d_pool.data_ptr(),
@@ -64,6 +68,8 @@ def test_noalloc_matches_scratch_entry_point_twice(lib):
             assert np.all(np.isfinite(a))
             # the tolerance of the attention parity tests
             assert np.abs(a - b).max() < 1e-5 * max(1.0, np.abs(b).max()), (length, count, call)
+            assert np.abs(a - exact).max() < 1e-5 * max(1.0, np.abs(exact).max()), \
+                (length, count, call)
 
 
 def test_noalloc_rejects_counts_beyond_its_scratch(lib):
