@@ -72,6 +72,15 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const void *tmap, int c0,
         "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
         : "memory");
 }
+// Tiled 2-D tensor load (no multicast) of the box at {c0, c1}, completing on *bar.
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int c0, int c1, uint64_t *bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(dst)),
+        "l"(tmap), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
 // L2 prefetch of the box at {c0, c1, c2, c3} of a 4-D tensor map.
 __device__ __forceinline__ void tma_prefetch_4d(const void *tmap, int c0, int c1, int c2, int c3)
 {

@@ -68,6 +68,7 @@ struct lun_device {
     unsigned l2_ahead_ffn = 0;          // the same while the ring is filled with FFN items
     unsigned l2_hints = 0;              // persistent kernel's L2 eviction hints (MegaParams::l2_hints)
     bool kv_early = true;               // persistent kernel: next layer's K/V into L2 during the FFN
+    bool head_tc = true;                // batched head on tcgen05 (head_tc.cuh) instead of mma.sync
     int *mega_error = nullptr, *h_error = nullptr;
     float *arg_val = nullptr;
     int *arg_idx = nullptr;
@@ -240,6 +241,12 @@ static lun_device *create_device(size_t context, size_t kv_pages, size_t block, 
         d->kv_early = !(early && early[0] == '0');
         const char *hints = getenv("LUNELETTE_L2_HINTS");
         d->l2_hints = hints ? (unsigned)strtoul(hints, nullptr, 10) : 1u;
+        // the batched head's kernel: tcgen05 (its bounded waits report through
+        // the GEMM's error word) unless LUNELETTE_HEAD_TC=0 selects the mma.sync
+        // kernel for comparison (64-session step at short contexts: 3.00 against
+        // 3.28 ms)
+        const char *head = getenv("LUNELETTE_HEAD_TC");
+        d->head_tc = !(head && head[0] == '0') && d->pf.error;
     }
     what = "pinned host buffers";
     if ((e = cudaMallocHost((void **)&d->h_step, sizeof(StepParams))) != cudaSuccess ||
@@ -1104,7 +1111,9 @@ extern "C" int lun_device_batch_decode(lun_device *d, const int *sessions, const
         hp.logits = d->batch_logits + (size_t)t0 * kVocab;
         hp.logits_stride = kVocab;
         hp.nonfinite = d->d_flag;
-        if ((e = lun_launch_head_mma(hp, d->stream)) != cudaSuccess) return fail(error, capacity, what, e);
+        hp.error = d->pf.error;
+        if ((e = d->head_tc ? lun_launch_head_tc(hp, d->stream) : lun_launch_head_mma(hp, d->stream)) != cudaSuccess)
+            return fail(error, capacity, what, e);
     }
     if ((e = lun_launch_argmax_rows(d->batch_logits, kVocab, kVocab, count, d->d_next, d->stream)) != cudaSuccess)
         return fail(error, capacity, what, e);
@@ -1120,7 +1129,7 @@ extern "C" int lun_device_batch_decode(lun_device *d, const int *sessions, const
     if (d->pf.error && (e = cudaMemcpy(d->h_pf_error, d->pf.error, 4, cudaMemcpyDeviceToHost)) == cudaSuccess &&
         *d->h_pf_error) {
         cudaMemset(d->pf.error, 0, sizeof(int));
-        if (error && capacity) snprintf(error, capacity, "batch decode: GEMM pipeline wait gave up");
+        if (error && capacity) snprintf(error, capacity, "batch decode: tensor-core pipeline wait gave up (GEMM or head)");
         return -1;
     }
     if (next)

@@ -583,6 +583,7 @@ struct HeadMmaParams {
     float *logits;         // [count][logits_stride]
     int logits_stride;
     int *nonfinite;
+    int *error;            // set when a bounded wait of the tcgen05 head gives up
 };
 
 }  // namespace lun

@@ -3,8 +3,11 @@
 #include <atomic>
 #include <mutex>
 
+#include <cudaTypedefs.h>
+
 #include "attention_tc.cuh"
 #include "head_mma.cuh"
+#include "head_tc.cuh"
 #include "launch.h"
 
 #include <stdlib.h>
@@ -188,6 +191,9 @@ cudaError_t lun_kernels_init()
     if ((e = cudaFuncSetAttribute(attention_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   kTaSmemBytes)) != cudaSuccess)
         return e;
+    if ((e = cudaFuncSetAttribute(head_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kHtSmemBytes)) !=
+        cudaSuccess)
+        return e;
     if ((e = setup_epi<kEpiStore>()) != cudaSuccess) return e;
     if ((e = setup_epi<kEpiResidual>()) != cudaSuccess) return e;
     if ((e = setup_epi<kEpiQKV>()) != cudaSuccess) return e;
@@ -359,6 +365,38 @@ cudaError_t lun_launch_head_mma(const HeadMmaParams &p, cudaStream_t stream)
     cudaError_t e = launch(head_mma_split_kernel, dim3(kHmTokens), dim3(256), 0, stream, p);
     if (e != cudaSuccess) return e;
     return launch(head_mma_kernel, dim3(p.rows / kHmRows), dim3(kHmThreads), kHmSmemBytes, stream, p);
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 lun_tensor_map_encoder();
+
+// The embedding as a 2-D BF16 tensor {3072, rows}: a box {64, 128} is one
+// chunk of a CTA's 128 rows, landed in the 128-byte-swizzled K-major order the
+// tensor core reads (head_tc_kernel).
+static cudaError_t embedding_tensor_map(CUtensorMap *map, const uint16_t *E, int rows)
+{
+    PFN_cuTensorMapEncodeTiled_v12000 encode = lun_tensor_map_encoder();
+    if (!encode || ((uintptr_t)E & 15)) return cudaErrorInvalidValue;
+    const cuuint64_t dims[2] = {(cuuint64_t)kHidden, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)kHidden * 2};
+    const cuuint32_t box[2] = {kHtChunk, kHtRows};
+    const cuuint32_t elem[2] = {1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void *)E, dims, strides, box, elem,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+cudaError_t lun_launch_head_tc(const HeadMmaParams &p, cudaStream_t stream)
+{
+    if (p.count < 1 || p.count > kHmTokens || p.rows < kHtRows || (p.rows % kHtRows) || !p.xb || !p.error ||
+        ((uintptr_t)p.xb & 15))
+        return cudaErrorInvalidValue;
+    cudaError_t e = lun_kernels_ensure();
+    if (e != cudaSuccess) return e;
+    CUtensorMap emap;
+    if ((e = embedding_tensor_map(&emap, p.W, p.rows)) != cudaSuccess) return e;
+    if ((e = launch(head_tc_split_kernel, dim3(kHmTokens), dim3(256), 0, stream, p)) != cudaSuccess) return e;
+    return launch(head_tc_kernel, dim3(p.rows / kHtRows), dim3(kHtThreads), kHtSmemBytes, stream, p, emap);
 }
 
 size_t lun_head_mma_stage_bytes() { return kHmStageElems * sizeof(uint16_t); }

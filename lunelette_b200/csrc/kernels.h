@@ -23,6 +23,9 @@ cudaError_t lun_launch_head(const lun::HeadParams &p, int sm_count, cudaStream_t
 // Batched tied head on the tensor cores (head_mma.cuh): up to lun_head_mma_tokens()
 // tokens per launch pair; p.xb holds lun_head_mma_stage_bytes() of staging.
 cudaError_t lun_launch_head_mma(const lun::HeadMmaParams &p, cudaStream_t stream);
+// The same on tcgen05 (head_tc.cuh), same staging size, same logits; p.error
+// receives a bounded wait that gave up.
+cudaError_t lun_launch_head_tc(const lun::HeadMmaParams &p, cudaStream_t stream);
 size_t lun_head_mma_stage_bytes();
 int lun_head_mma_tokens();
 // Greedy id of each of `rows` logits rows (stride floats apart).

@@ -350,6 +350,34 @@ def batch_step(checkpoint, sessions=64, seed=5, pool=None):
     return toks[0]
 
 
+def batch_head_ab(checkpoint, sessions=64, steps=20, seed=9):
+    """Batched decode steps of `sessions` sessions with 8-token prompts (short
+    contexts: the step is the projections and the head) with the mma.sync head
+    and with the tcgen05 head (LUNELETTE_HEAD_TC, read when the context is
+    created); wall-clock ms per step after three warm-up steps."""
+    import time
+    import lunelette_b200 as L
+    if not os.path.exists(checkpoint):
+        L.synth_checkpoint(checkpoint, 0)
+    rng = np.random.default_rng(seed)
+    prompts = [rng.integers(1000, 131072, 8) for _ in range(sessions)]
+    out = {}
+    for name, head in (("mma_ms", "0"), ("tc_ms", "1")):
+        os.environ["LUNELETTE_HEAD_TC"] = head
+        with L.Batch(checkpoint, max_sessions=sessions, context=4352, pool_positions=sessions * 128,
+                     block=256) as b:
+            ss = [b.open() for _ in range(sessions)]
+            toks = [int(np.argmax(b.append(s, p))) for s, p in zip(ss, prompts)]
+            for _ in range(3):
+                toks = b.decode(ss, toks).tolist()
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                toks = b.decode(ss, toks).tolist()
+            out[name] = (time.perf_counter() - t0) / steps * 1e3
+    os.environ.pop("LUNELETTE_HEAD_TC", None)
+    return out
+
+
 def decode_tokens(checkpoint, steps, prompt=32):
     """A small profiling target: the C0 prompt, then `steps` greedy tokens through
     lunelette_metal_decode (one persistent-kernel launch each)."""
@@ -382,9 +410,14 @@ def main():
     ap.add_argument("--batch-step", metavar="CHECKPOINT", default=None,
                     help="one batched decode step of ragged sessions between cudaProfilerStart/Stop")
     ap.add_argument("--batch-sessions", type=int, default=64)
+    ap.add_argument("--batch-head", metavar="CHECKPOINT", default=None,
+                    help="batched step with the mma.sync and the tcgen05 head, ms per step")
     ap.add_argument("--prefill-gemm", metavar="COUNTS", default=None,
                     help="time the tcgen05 prefill projections at these token counts (e.g. 256,32)")
     args = ap.parse_args()
+    if args.batch_head:
+        print(json.dumps(batch_head_ab(args.batch_head, args.batch_sessions)))
+        return
     if args.batch_step:
         n = args.batch_sessions
         # the pool holds the sessions' prompts plus the two steps (pages of 64)

@@ -158,3 +158,43 @@ def test_forked_sessions_share_a_prefix_and_diverge(lib, checkpoint_path, oracle
                 assert greedy(logits) == greedy(want)
     finally:
         m.close()
+
+
+def test_tcgen05_head_matches_mma_head_and_oracle(lib, checkpoint_path, oracle, monkeypatch):
+    """The batched head on tcgen05 (head_tc.cuh, the default; LUNELETTE_HEAD_TC=1)
+    against the mma.sync head (LUNELETTE_HEAD_TC=0) on the same tokens: 70 sessions, so the head runs as a
+    pass of 64 tokens and a pass of 6; the logits agree to FP32 accumulation
+    order, the greedy ids follow from them, and one session of the second pass
+    against the oracle."""
+    rng = np.random.default_rng(606)
+    prompts = [rng.integers(1000, 131072, n) for n in rng.integers(5, 40, 70)]
+    runs = {}
+    feed = None
+    for head in ("0", "1"):
+        monkeypatch.setenv("LUNELETTE_HEAD_TC", head)
+        with L.Batch(checkpoint_path, max_sessions=70, context=4352, pool_positions=70 * 128, block=256) as b:
+            sessions = [b.open() for _ in prompts]
+            firsts = [greedy(b.append(s, p).copy()) for s, p in zip(sessions, prompts)]
+            toks = firsts if feed is None else feed[0]
+            nxt1, lg1 = b.decode(sessions, toks, logits=True)
+            assert [greedy(r) for r in lg1] == nxt1.tolist()
+            toks2 = nxt1.tolist() if feed is None else feed[1]
+            nxt2, lg2 = b.decode(sessions, toks2, logits=True)
+            assert [greedy(r) for r in lg2] == nxt2.tolist()
+            if feed is None:
+                feed = (firsts, toks2)
+            runs[head] = (lg1.copy(), lg2.copy())
+    for step in range(2):
+        got, want = runs["1"][step], runs["0"][step]
+        assert np.all(np.isfinite(got))
+        err = float(np.abs(got - want).max())
+        rel = float(np.linalg.norm((got - want).ravel()) / np.linalg.norm(want.ravel()))
+        assert err <= 1e-3 and rel <= 1e-5, "step %d: max-abs %.3g rel-L2 %.3g" % (step, err, rel)
+    k = 66
+    m = oracle.open_model(checkpoint_path, 4352)
+    try:
+        m.forward(prompts[k])
+        want, _, _ = m.forward([feed[0][k]])
+        assert_close(runs["1"][0][k], want, "session %d step 1 (tcgen05 head) vs oracle" % k)
+    finally:
+        m.close()

@@ -187,3 +187,72 @@ def test_tc_attention_operand_tiles_cover_their_buffers_once():
                 assert off + 2 * e == sw128_offset(d, 8 * kg + e)
                 v_seen[off + 2 * e: off + 2 * e + 2] += 1
     assert np.all(v_seen == 1)
+
+
+def bf16_bits(v):
+    """Round-to-nearest-even FP32 -> BF16 bit patterns (finite inputs)."""
+    u = np.asarray(v, np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def bf16_value(bits):
+    return (np.asarray(bits, np.uint32) << 16).view(np.float32)
+
+
+def test_tcgen05_head_operands_and_epilogue_give_the_tied_head():
+    """head_tc.cuh on two CTAs of 128 vocabulary rows: the split kernel's B rows
+    2 t (hi) and 2 t + 1 (lo) at head_tc_b_offset, one 16 KB tile per 64-column
+    chunk; the embedding tile as the 2-D tensor copy lands it with the 128-byte
+    swizzle (box row r at 128 r bytes, 16-byte chunk j moved to j ^ (r % 8));
+    the MMA's K-major swizzled reads (four K = 16 steps per chunk at start
+    offsets 32 k); and the epilogue's column 32 cb + 2 j (+ 1) = token
+    16 cb + j, hi (lo). The result is E times (hi + lo) for every token below
+    count, whatever the stale B rows of the other tokens hold."""
+    rng = np.random.default_rng(21)
+    rows, hidden, n_rows, chunk = 256, 3072, 128, 64
+    count = 37
+    emb = bf16_bits(rng.standard_normal((rows, hidden)).astype(np.float32) * 0.02)
+    v = rng.standard_normal((64, hidden)).astype(np.float32)
+    hi = bf16_bits(v)
+    lo = bf16_bits(v - bf16_value(hi))
+    # B operand: rows 2 t and 2 t + 1, tokens >= count zeroed by the split kernel
+    b_rows = np.zeros((n_rows, hidden), np.uint16)
+    b_rows[0:2 * count:2] = hi[:count]
+    b_rows[1:2 * count:2] = lo[:count]
+    xb = np.zeros(hidden // chunk * 16384 // 2, np.uint16)
+    cols = np.arange(hidden)
+    for n in range(n_rows):
+        off = (cols // chunk) * 16384 + sw128_offset(n, cols % chunk)
+        xb[off // 2] = b_rows[n]
+    k = np.arange(chunk)
+    r = np.arange(n_rows)[:, None]
+    read_idx = sw128_offset(r, k[None, :]) // 2  # the MMA's K-major swizzled reads
+    logits = np.zeros((count, rows))
+    for cta in range(rows // n_rows):
+        row0 = cta * n_rows
+        acc = np.zeros((n_rows, n_rows))
+        for c in range(hidden // chunk):
+            box = emb[row0:row0 + n_rows, c * chunk:(c + 1) * chunk]
+            tile_a = np.zeros(8192, np.uint16)
+            for rr in range(n_rows):
+                for j in range(8):
+                    dst = rr * 64 + ((j ^ (rr % 8)) * 8)
+                    tile_a[dst:dst + 8] = box[rr, 8 * j:8 * j + 8]
+            tile_b = xb[c * 8192:(c + 1) * 8192]
+            for ks in range(chunk // 16):
+                a = bf16_value(tile_a[read_idx[:, 16 * ks:16 * ks + 16]]).astype(np.float64)
+                b = bf16_value(tile_b[read_idx[:, 16 * ks:16 * ks + 16]]).astype(np.float64)
+                acc += a @ b.T
+        for q in range(4):
+            for lane in range(32):
+                m = 32 * q + lane
+                for cb in range(4):
+                    if 16 * cb >= count:
+                        break
+                    for j in range(16):
+                        tok = 16 * cb + j
+                        if tok < count:
+                            logits[tok, row0 + m] = acc[m, 32 * cb + 2 * j] + acc[m, 32 * cb + 2 * j + 1]
+    want = (bf16_value(hi[:count]).astype(np.float64) + bf16_value(lo[:count]).astype(np.float64)) @ \
+        bf16_value(emb).astype(np.float64).T
+    assert np.allclose(logits, want, rtol=1e-12, atol=1e-12)
