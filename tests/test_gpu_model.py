@@ -85,6 +85,44 @@ def test_c0_prefill_per_layer_and_greedy_32(runtime, oracle_model):
         assert tokens_gpu == tokens_cpu, "greedy divergence at step %d" % step
 
 
+def test_prefill_per_layer_matches_transformers_fixture(runtime, checkpoint_path):
+    """The CUDA runtime against an implementation independent of this
+    repository: tests/golden/transformers_model.json holds Transformers'
+    Ministral3ForCausalLM (CPU FP32) on the same synthetic weights and an 8-id
+    prompt, the fixture the oracle matches to FP32 rounding on the CPU. A
+    traced prefill of that prompt: every layer's hidden state at every token
+    (its norm and its projections on the fixture's eight directions, within
+    the relative L2 gate), the last token's layer-25 and final-norm rows, and
+    the last position's logits at the 16 largest and 256 sampled entries,
+    within the gate, with the same greedy id."""
+    import json
+    import os
+    from tests.golden.make_transformers_golden import directions, fingerprint, sample_indices
+    with open(os.path.join(os.path.dirname(__file__), "golden", "transformers_model.json")) as f:
+        fx = json.load(f)
+    assert fingerprint(checkpoint_path) == fx["checkpoint"], "the fixture was made from other weights"
+    ids = np.array(fx["ids"], np.int64)
+    runtime.reset()
+    runtime.trace(True)
+    try:
+        logits = runtime.prefill(ids).copy()
+        layers = [runtime.trace_copy(l, len(ids)).astype(np.float64) for l in range(27)]
+    finally:
+        runtime.trace(False)
+    hidden = np.stack(layers[:26])  # [layer][token][3072]
+    want_norms = np.array(fx["hidden_norms"])
+    assert np.abs(np.linalg.norm(hidden, axis=2) / want_norms - 1).max() <= REL_L2
+    proj = np.einsum("ltc,dc->ltd", hidden, directions())
+    assert (np.abs(proj - np.array(fx["hidden_projections"])) / want_norms[:, :, None]).max() <= REL_L2
+    assert_close(hidden[25, -1], np.array(fx["last_hidden"]["25"]), "layer 25, last token")
+    assert_close(layers[26][-1], np.array(fx["last_final_norm"]), "final norm, last token")
+    top = fx["top_logits"][-1]
+    got = np.concatenate([logits[top["ids"]], logits[sample_indices()]])
+    want = np.concatenate([np.array(top["values"]), np.array(fx["sampled_logits"][-1])])
+    assert_close(got, want, "last-position logits")
+    assert greedy(logits) == top["ids"][0]
+
+
 def test_reset_cycles_are_bitwise_identical(runtime):
     ids = prompt(77, 24)
     runs = []
