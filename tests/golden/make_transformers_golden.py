@@ -76,12 +76,9 @@ def fingerprint(path):
             "layer0_q_first64k_sha256": hashlib.sha256(codes).hexdigest()}
 
 
-def build_model(path):
-    import torch
-    from safetensors import safe_open
-    from transformers import Ministral3Config, Ministral3ForCausalLM
-    from transformers.models.ministral3.modeling_ministral3 import Ministral3RotaryEmbedding
-
+def model_config():
+    """Ministral3Config with the reference's model facts (eager attention)."""
+    from transformers import Ministral3Config
     config = Ministral3Config(
         vocab_size=131072, hidden_size=3072, intermediate_size=9216, num_hidden_layers=26,
         num_attention_heads=32, num_key_value_heads=8, head_dim=128, max_position_embeddings=262144,
@@ -90,6 +87,16 @@ def build_model(path):
                          "original_max_position_embeddings": 16384, "beta_fast": 32.0, "beta_slow": 1.0,
                          "mscale": 1.0, "mscale_all_dim": 1.0, "llama_4_scaling_beta": 0.1})
     config._attn_implementation = "eager"
+    return config
+
+
+def build_model(path):
+    import torch
+    from safetensors import safe_open
+    from transformers import Ministral3ForCausalLM
+    from transformers.models.ministral3.modeling_ministral3 import Ministral3RotaryEmbedding
+
+    config = model_config()
     with torch.device("meta"):
         model = Ministral3ForCausalLM(config)
     state = {}

@@ -280,3 +280,36 @@ def test_oracle_model_matches_transformers(oracle, checkpoint_path):
         assert np.abs(lg[top["ids"]] - np.array(top["values"])).max() < 1e-4, pos
         assert np.abs(lg[samples] - np.array(fx["sampled_logits"][pos])).max() < 1e-4, pos
         assert int(np.argmax(lg)) == top["ids"][0], pos
+
+
+def test_rope_and_query_scale_match_transformers_at_far_positions(oracle):
+    """Beyond the reference's RoPE golden (positions up to 16385, no query
+    scale): the oracle's YaRN table and its rotation with the query scale
+    1 + 0.1 ln(1 + floor(p / 16384)) against Transformers' Ministral3 rotary
+    embedding and its llama-4 attention scale, configured from the reference's
+    model facts, at positions across the scale's steps up to the last one the
+    model takes (observed: tables within 3.6e-7, the rotated and scaled rows
+    identical when both use the same table)."""
+    import torch
+    from transformers.models.ministral3.modeling_ministral3 import (Ministral3RotaryEmbedding,
+                                                                    apply_rotary_pos_emb,
+                                                                    get_llama_4_attn_scale)
+    from tests.golden.make_transformers_golden import model_config
+    positions = np.array([0, 1, 4351, 16383, 16384, 16385, 32767, 32768, 49152, 100000, 262143], np.int64)
+    x = np.random.default_rng(3).standard_normal((len(positions), 128)).astype(np.float32)
+    rotary = Ministral3RotaryEmbedding(model_config())
+    assert rotary.attention_scaling == 1.0
+    xt = torch.from_numpy(x)[None, None]
+    pos_t = torch.from_numpy(positions)[None]
+    cos, sin = rotary(xt, pos_t)
+    q, _ = apply_rotary_pos_emb(xt, xt, cos, sin)
+    q = (q * get_llama_4_attn_scale(pos_t, 0.1, 16384).to(q.dtype))[0, 0].numpy()
+    cos, sin = cos[0].numpy(), sin[0].numpy()
+    own_cos = np.stack([oracle.yarn(int(p))[0] for p in positions])
+    own_sin = np.stack([oracle.yarn(int(p))[1] for p in positions])
+    assert np.abs(own_cos - cos).max() < 1e-6
+    assert np.abs(own_sin - sin).max() < 1e-6
+    same_table = oracle.rope(x, cos, sin, positions.astype(np.uint32), 1)
+    assert np.abs(same_table - q).max() <= 1e-6 * np.abs(q).max()
+    own_table = oracle.rope(x, own_cos, own_sin, positions.astype(np.uint32), 1)
+    assert np.abs(own_table - q).max() <= 4e-6 * np.abs(q).max()
