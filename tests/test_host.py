@@ -304,3 +304,117 @@ def test_parser_corpus(lib, case, request):
             assert st_open_verdicts(ref, path) == accepted
     finally:
         os.unlink(path)
+
+
+FUZZ_TOKENS = [b'{', b'}', b'[', b']', b',', b':', b'"', b'\\', b'0', b'-1', b'1e3', b'18446744073709551615',
+               b'18446744073709551616', b'9223372036854775807', b'"dtype"', b'"shape"', b'"data_offsets"',
+               b'"BF16"', b'"F8_E4M3"', b'"F32"', b'"I64"', b'"__metadata__"', b' ', b'\n', b'\x00', b'\xff',
+               b'null', b'true', b'1.0', b'\\u0000', b'\\ud800', b'01', b'+1']
+
+
+def fuzz_file(rng, directory):
+    """One seeded mutation of a corpus case: up to three edits of its header
+    (byte deleted, JSON token inserted, byte replaced, cut, span replaced), the
+    data sometimes cut or padded, and the 8-byte header size sometimes wrong
+    (too long, too short, or a huge value)."""
+    header, data, _ = rng.choice(PARSER_CASES)
+    h = bytearray(header.encode())
+    for _ in range(rng.randint(1, 3)):
+        if not h:
+            h = bytearray(b'{')
+        op, i = rng.randrange(5), rng.randrange(len(h) + 1)
+        if op == 0 and len(h) > 1:
+            del h[min(i, len(h) - 1)]
+        elif op == 1:
+            h[i:i] = rng.choice(FUZZ_TOKENS)
+        elif op == 2 and i < len(h):
+            h[i] = rng.randrange(256)
+        elif op == 3:
+            h = h[:i]
+        elif op == 4:
+            j = rng.randrange(len(h) + 1)
+            h[min(i, j):max(i, j)] = rng.choice(FUZZ_TOKENS)
+    if rng.random() < 0.2:
+        data = data[:rng.randrange(len(data) + 1)] + b'\0' * rng.randrange(3)
+    size, r = len(h), rng.random()
+    if r < 0.05:
+        size = len(h) + rng.randrange(1, 64)
+    elif r < 0.10:
+        size = max(0, len(h) - rng.randrange(1, 16))
+    elif r < 0.12:
+        size = rng.choice([0, 2 ** 63, 2 ** 64 - 1, 100_000_001, 2 ** 32])
+    fd, path = tempfile.mkstemp(suffix=".safetensors", dir=directory)
+    with os.fdopen(fd, "wb") as f:
+        f.write(struct.pack("<Q", size) + bytes(h) + data)
+    return path
+
+
+FUZZ_DTYPES = {"BF16": 2, "F16": 2, "F32": 4, "F8_E4M3": 1, "I64": 8, "U8": 1, "BOOL": 1, "F64": 8,
+               "bf16": 1, "F8_E5M2": 1}
+
+
+def structured_file(rng, directory):
+    """A well-formed header built at random: up to four tensors (names with
+    escapes, empty or repeated names), dtypes the parser knows and some it does
+    not, shapes of 0 to 9 dimensions, offsets that are contiguous or off by a
+    byte, keys and fields in shuffled order, optional metadata (string and
+    non-string values), whitespace between tokens, and data of the declared
+    length or one byte off: about a fifth of these files are valid."""
+    entries, off = [], 0
+    for i in range(rng.randrange(0, 5)):
+        name = rng.choice(["w", "a", "b", "x.y", "a\\u0041", "\\n", "", "w"]) + (str(i) if rng.random() < 0.7 else "")
+        dtype = rng.choice(list(FUZZ_DTYPES))
+        shape = [rng.choice([0, 1, 2, 3, 4]) for _ in range(rng.choice([0, 1, 1, 2, 2, 3, 8, 9]))]
+        nbytes = int(np.prod(shape, dtype=np.int64)) * FUZZ_DTYPES[dtype]
+        start = off if rng.random() < 0.85 else off + rng.choice([-1, 1, 2])
+        end = start + nbytes if rng.random() < 0.85 else start + nbytes + rng.choice([-1, 1])
+        entries.append((name, dtype, shape, max(0, start), max(0, end)))
+        off = max(off, end)
+    if rng.random() < 0.3:
+        rng.shuffle(entries)
+    ws = lambda: rng.choice(["", "", " ", "\n", "\t"])
+    parts = []
+    if rng.random() < 0.3:
+        parts.append('"__metadata__":%s%s' % (ws(), rng.choice(['{"a":"b"}', '{}', '{"a":1}', '{"a":"b","c":"d"}'])))
+    for name, dtype, shape, start, end in entries:
+        fields = ['"dtype":%s"%s"' % (ws(), dtype), '"shape":[%s]' % ",".join(map(str, shape)),
+                  '"data_offsets":[%d,%d]' % (start, end)]
+        if rng.random() < 0.3:
+            rng.shuffle(fields)
+        parts.append('%s"%s"%s:%s{%s}' % (ws(), name, ws(), ws(), ",".join(fields)))
+    header = ("{" + ",".join(parts) + "}" + rng.choice(["", "", " ", "  "])).encode()
+    total = max([e[4] for e in entries] + [0])
+    data = b"\0" * (total if rng.random() < 0.85 else max(0, total + rng.choice([-1, 1])))
+    fd, path = tempfile.mkstemp(suffix=".safetensors", dir=directory)
+    with os.fdopen(fd, "wb") as f:
+        f.write(struct.pack("<Q", len(header)) + header + data)
+    return path
+
+
+def test_parser_agrees_with_reference_on_random_files(lib, tmp_path):
+    """Differential fuzzing of the checkpoint parser against the reference's
+    st_open (src/safetensors.c, compiled from its sources into oracle/_ref):
+    800 seeded mutations of the corpus above (almost all malformed) and 800
+    well-formed random headers (about a fifth valid) get the same
+    accept/reject verdict from both, and neither crashes."""
+    import random
+    libref = os.path.join(REPO, "oracle", "_ref", "libref.so")
+    if not os.path.exists(libref):
+        pytest.skip("the reference's parser is not built here (oracle/Makefile with a reference checkout)")
+    ref = ctypes.CDLL(libref)
+    rng = random.Random(20261202)
+    accepted = 0
+    for case in range(1600):
+        make = fuzz_file if case % 2 == 0 else structured_file
+        path = make(rng, str(tmp_path))
+        try:
+            err = ctypes.create_string_buffer(512)
+            lib.lunelette_cuda_validate_checkpoint(path.encode(), 1, err, 512)
+            mine = b"tensor language_model.model.embed_tokens.weight" in err.value
+            with open(path, "rb") as f:
+                raw = f.read()
+            assert mine == st_open_verdicts(ref, path), (case, raw[:200], err.value)
+            accepted += mine
+        finally:
+            os.unlink(path)
+    assert accepted > 100  # the structured half reaches the parser's semantic checks
