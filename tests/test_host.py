@@ -418,3 +418,72 @@ def test_parser_agrees_with_reference_on_random_files(lib, tmp_path):
         finally:
             os.unlink(path)
     assert accepted > 100  # the structured half reaches the parser's semantic checks
+
+
+def reference_admission(ref_lib, path, index):
+    """The reference loader's verdicts on a checkpoint (src/metal_weights.c):
+    open (names, shapes, dtypes, every scalar read and checked) and, for the
+    weight at `index`, its compact raw admission and its resident FP32 load.
+    Returns (compact admitted, resident admitted)."""
+    ref_lib.lunelette_metal_weights_open.argtypes = [ctypes.c_void_p, ctypes.c_char_p,
+                                                     ctypes.c_char_p, ctypes.c_size_t]
+    ref_lib.lunelette_metal_weights_load_raw.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                                                         ctypes.c_size_t, ctypes.c_char_p, ctypes.c_size_t]
+    ref_lib.lunelette_metal_weights_load.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                                                     ctypes.c_size_t]
+    ref_lib.lunelette_metal_weights_close.argtypes = [ctypes.c_void_p]
+    state = ctypes.create_string_buffer(1 << 16)  # sizeof(lunelette_metal_weights) is 5704 bytes
+    err = ctypes.create_string_buffer(512)
+    if ref_lib.lunelette_metal_weights_open(state, path.encode(), err, 512) != 0:
+        return False, False
+    try:
+        if index is None:
+            return True, True
+        rows, cols = {1: (4096, 3072), 8: (3072, 9216)}[(index - 2) % 9]
+        raw = np.empty(rows * cols, np.uint8)
+        compact = ref_lib.lunelette_metal_weights_load_raw(state, index, raw.ctypes.data, raw.size, err, 512) == 0
+        wide = np.empty(rows * cols, np.float32)
+        resident = ref_lib.lunelette_metal_weights_load(state, index, wide.ctypes.data, wide.size) == 0
+        return compact, resident
+    finally:
+        ref_lib.lunelette_metal_weights_close(state)
+
+
+def test_admission_verdicts_match_reference_loader(corrupt_copy, ref_lib):
+    """The same planted faults through this library's admission and the
+    reference's loader (compiled from its sources): for each, both strategies
+    admit or reject alike. Faults: NaN codes in the first and the last FP8
+    tensor of a layer, a subnormal, zero, infinite and negative weight scale, a
+    NaN and a negative activation scale, a renamed companion scalar, a renamed
+    embedding."""
+    q = "language_model.model.layers.3.self_attn.q_proj.weight"
+    down = "language_model.model.layers.25.mlp.down_proj.weight"
+    q_index, down_index = 2 + 3 * 9 + 1, 2 + 25 * 9 + 8
+    n, header = header_of(corrupt_copy)
+    act = q[:-6] + "activation_scale"
+    faults = [  # (offset, bytes, index of the affected weight or None)
+        (tensor_offset(corrupt_copy, q) + 1000, b"\x7f", q_index),
+        (tensor_offset(corrupt_copy, down) + 12345, b"\xff", down_index),
+        (tensor_offset(corrupt_copy, q[:-6] + "weight_scale_inv"), struct.pack("<H", 0x0001), q_index),
+        (tensor_offset(corrupt_copy, q[:-6] + "weight_scale_inv"), struct.pack("<H", 0x0000), q_index),
+        (tensor_offset(corrupt_copy, down[:-6] + "weight_scale_inv"), struct.pack("<H", 0x7F80), down_index),
+        (tensor_offset(corrupt_copy, down[:-6] + "weight_scale_inv"), struct.pack("<H", 0xBC00), down_index),
+        (tensor_offset(corrupt_copy, act), struct.pack("<H", 0x7FC0), None),
+        (tensor_offset(corrupt_copy, act), struct.pack("<H", 0xBF80), None),
+        (8 + header.index(act) + len(act) - 1, b"f", None),
+        (8 + header.index("embed_tokens") + len("embed_token"), b"z", None),
+    ]
+    for offset, data, index in faults:
+        old = patch(corrupt_copy, offset, data)
+        try:
+            ours = []
+            for strategy in (L.COMPACT_FP8_ARITHMETIC, L.RESIDENT_FP32):
+                try:
+                    L.validate_checkpoint(corrupt_copy, strategy)
+                    ours.append(True)
+                except L.LuneletteError:
+                    ours.append(False)
+            assert tuple(ours) == reference_admission(ref_lib, corrupt_copy, index), (offset, data)
+        finally:
+            patch(corrupt_copy, offset, old)
+    assert reference_admission(ref_lib, corrupt_copy, q_index) == (True, True)
