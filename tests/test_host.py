@@ -487,3 +487,48 @@ def test_admission_verdicts_match_reference_loader(corrupt_copy, ref_lib):
         finally:
             patch(corrupt_copy, offset, old)
     assert reference_admission(ref_lib, corrupt_copy, q_index) == (True, True)
+
+
+def test_parser_and_admission_memory_safe_under_sanitizers(checkpoint_path, tmp_path):
+    """The checkpoint parser and admission catalogue (csrc/st.c, csrc/weights.c)
+    built on their own with the address, undefined-behaviour and leak
+    sanitizers (tests/c_drivers/open_checkpoints.c) and run over 2000 seeded
+    random files of the two fuzz generators above, the synthetic checkpoint and
+    three truncations of it: no sanitizer report, the checkpoint admitted, every
+    truncation rejected."""
+    import random
+    import subprocess
+    csrc = os.path.join(REPO, "lunelette_b200", "csrc")
+    exe = str(tmp_path / "open_checkpoints")
+    build = subprocess.run(["gcc", "-std=c11", "-g", "-O1", "-fsanitize=address,undefined",
+                            "-fno-sanitize-recover=undefined", "-fno-omit-frame-pointer", "-I" + csrc,
+                            "-I" + os.path.join(REPO, "include"), os.path.join(csrc, "st.c"),
+                            os.path.join(csrc, "weights.c"),
+                            os.path.join(REPO, "tests", "c_drivers", "open_checkpoints.c"),
+                            "-o", exe, "-lm", "-lpthread"], capture_output=True, text=True)
+    if build.returncode and "asan" in build.stderr.lower():
+        pytest.skip("no sanitizer runtime here: " + build.stderr.strip()[:200])
+    assert build.returncode == 0, build.stderr
+    env = dict(os.environ, ASAN_OPTIONS="detect_leaks=1:abort_on_error=0", UBSAN_OPTIONS="print_stacktrace=1")
+    files = tmp_path / "files"
+    files.mkdir()
+    rng = random.Random(7)
+    for i in range(2000):
+        (structured_file if i % 2 else fuzz_file)(rng, str(files))
+    run = subprocess.run([exe, str(files)], capture_output=True, text=True, env=env, timeout=600)
+    assert run.returncode == 0 and "runtime error" not in run.stderr and "Sanitizer" not in run.stderr, \
+        run.stderr[-2000:]
+    assert len(run.stdout.splitlines()) == 2000
+    n, _ = header_of(checkpoint_path)
+    with open(checkpoint_path, "rb") as f:
+        head = f.read(8 + n + (1 << 20))
+    cuts = []
+    for name, size in (("header_only", 8 + n), ("header_1mb", len(head)), ("header_cut", 8 + n // 2)):
+        path = tmp_path / (name + ".safetensors")
+        path.write_bytes(head[:size])
+        cuts.append(str(path))
+    run = subprocess.run([exe, checkpoint_path] + cuts, capture_output=True, text=True, env=env, timeout=600)
+    assert run.returncode == 0 and "runtime error" not in run.stderr and "Sanitizer" not in run.stderr, \
+        run.stderr[-2000:]
+    verdicts = [line.split(" ", 1)[0] for line in run.stdout.splitlines()]
+    assert verdicts == ["0", "-1", "-1", "-1"], run.stdout
