@@ -410,3 +410,80 @@ def test_host_runtime_contract_under_sanitizers(checkpoint_path, tmp_path):
     run = subprocess.run([sys.executable, "-c", code, lib, checkpoint_path], cwd=REPO, env=env,
                          capture_output=True, text=True, timeout=900)
     assert run.returncode == 0 and "runtime error" not in run.stderr, run.stderr[-3000:]
+
+
+REF_FAKE = os.path.join(REPO, "oracle", "_ref", "fake")
+
+
+def fake_binary(name):
+    path = os.path.join(REF_FAKE, name)
+    if not os.path.exists(path):
+        pytest.skip("%s not built (make -C oracle REF=<reference checkout>)" % name)
+    return path
+
+
+def test_reference_callers_over_fake_device(checkpoint_path, tmp_path):
+    """The reference's own C callers of include/metal.h (compiled from its
+    sources by oracle/Makefile into oracle/_ref/fake/, linked against the host
+    runtime over the CPU stand-in): its generation loop (src/generation.c with
+    the CLI's callback) generates the stand-in's greedy chain; its native
+    regression harness (tests/compare_native.c) captures 8 teacher-forced steps
+    after prompts of 6/24/150/248 ids and checks them bitwise over two reset
+    cycles in a second process; its service generator (service/native.c) runs
+    config 3's turn shape (512-id prefix, 2 turns of 200 + 64) with prefix reuse
+    and a checkpointed replay of the last turn, every id the stand-in's chain."""
+    from tests.test_gpu_c_callers import write_generated_fixture
+    lib = bind(fake_binary("liblunelette_cuda.so"))
+    rng = np.random.default_rng(4321)
+    # the generation loop: greedy until id 2 or 32 tokens
+    prompt = [int(i) for i in rng.integers(1000, 131072, 32)]
+    proc = subprocess.run([fake_binary("generate_metal_next"), checkpoint_path, "32"] + [str(i) for i in prompt],
+                          capture_output=True, text=True, timeout=600)
+    assert proc.returncode == 0, proc.stderr
+    lines = dict(line.split(":", 1) for line in proc.stdout.strip().splitlines())
+    got = [int(t) for t in lines["tokens"].split()]
+    seq, want = list(prompt), []
+    while True:
+        tok = greedy(reference(lib, seq))
+        want.append(tok)
+        if tok == 2 or len(want) == 32:
+            break
+        seq.append(tok)
+    assert got == want and int(lines["calls"]) == len(got)
+    # the native regression harness: capture, then check in another process
+    pairs = []
+    for count in (6, 24, 150, 248):
+        ids_path = tmp_path / ("ids%d.txt" % count)
+        ids_path.write_text(" ".join(str(int(i)) for i in rng.integers(1000, 131072, count)) + "\n")
+        fixture = tmp_path / ("forced%d.safetensors" % count)
+        write_generated_fixture(fixture, rng.integers(1000, 131072, 8))
+        pairs += [str(ids_path), str(fixture)]
+    out_dir = tmp_path / "capture"
+    out_dir.mkdir()
+    for mode in ("capture", "check"):
+        proc = subprocess.run([fake_binary("compare_native"), mode, checkpoint_path, "mps", str(out_dir)] + pairs,
+                              capture_output=True, text=True, timeout=600)
+        assert proc.returncode == 0, (mode, proc.stdout[-2000:], proc.stderr[-2000:])
+        assert ("PASS native %s" % mode) in proc.stdout
+    assert "steps=64 cycles=2" in proc.stdout and "exact=0" not in proc.stdout
+    # the service generator over config 3's turn shape
+    prefix_len, turns, user_len, gen = 512, 2, 200, 64
+    prefix = [int(i) for i in rng.integers(1000, 131072, prefix_len)]
+    users = [[int(i) for i in rng.integers(1000, 131072, user_len)] for _ in range(turns)]
+    ids_path = tmp_path / "turns.txt"
+    ids_path.write_text(" ".join(str(i) for i in prefix + sum(users, [])) + "\n")
+    proc = subprocess.run([fake_binary("service_native_turns"), checkpoint_path, str(ids_path), str(prefix_len),
+                           str(turns), str(user_len), str(gen)],
+                          capture_output=True, text=True, timeout=600, cwd=str(tmp_path))
+    assert proc.returncode == 0, (proc.stdout[-2000:], proc.stderr[-2000:])
+    lines = dict(line.split(":", 1) for line in proc.stdout.strip().splitlines())
+    seq, pending = list(prefix), []
+    for t in range(turns):
+        seq += pending + users[t]
+        want = [greedy(reference(lib, seq))]
+        while len(want) < gen:
+            seq.append(want[-1])
+            want.append(greedy(reference(lib, seq)))
+        assert [int(x) for x in lines["turn %d" % t].split()] == want, "turn %d" % t
+        pending = [want[-1]]  # generated but not yet fed: opens the next turn
+    assert [int(x) for x in lines["replay"].split()] == want
