@@ -394,6 +394,20 @@ def check_batch(lib, path):
         assert b"exhausted" in err.value
         length = lib.lunelette_cuda_batch_length(b, s)
         assert length in (before, before + 256)
+        # argument errors: forks of no positions, of more than the source holds, of
+        # a closed session; calls on a closed session; too many tokens at once
+        child = ctypes.c_int(-1)
+        free_before = lib.lunelette_cuda_batch_free_positions(b)
+        for source, length in ((order[1], 0), (order[1], len(seqs[order[1]]) + 1), (src_a, 10), (99, 10)):
+            assert lib.lunelette_cuda_batch_fork(b, source, length, ctypes.byref(child), err, 512) != 0
+        assert append(src_a, [1])[0] != 0 and decode([src_a], [1])[0] != 0
+        assert lib.lunelette_cuda_batch_close(b, src_a) != 0  # already closed
+        assert append(order[1], [1] * 257)[0] != 0
+        assert decode(list(range(6)) * 43, [1] * 258)[0] != 0
+        assert lib.lunelette_cuda_batch_free_positions(b) == free_before
+        rc, lg, _ = decode([order[1]], [904])  # the rejected calls changed nothing
+        seqs[order[1]].append(904)
+        assert rc == 0 and np.array_equal(lg[0], reference(lib, seqs[order[1]]))
         # every page returns to the pool once every session is closed
         for s in (order[1], order[2], fork_a.value, fork_b.value):
             assert lib.lunelette_cuda_batch_close(b, s) == 0
