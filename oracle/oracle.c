@@ -27,7 +27,9 @@
 /* Precision-study knobs (default 0 = the reference's FP32 everywhere). They let
  * tests measure what a narrower storage format for KV rows (kv_rounding) or for
  * projection inputs (input_rounding) does to per-layer drift: 1 rounds to BF16,
- * 2 to FP16, both round-to-nearest-even. Never used as a reference result. */
+ * 2 to FP16, both round-to-nearest-even; for inputs, 3 and 4 write each row as
+ * the sum of two or three scaled FP16 terms (round_inputs). Never used as a
+ * reference result. */
 static int kv_rounding, input_rounding;
 
 void oracle_set_rounding(int kv, int input)
@@ -55,6 +57,42 @@ static void round_rows(float *v, size_t n, int mode)
     if (mode) {
         for (size_t i = 0; i < n; i++) {
             v[i] = round_to(v[i], mode);
+        }
+    }
+}
+
+/* Projection inputs as the CUDA kernels' tensor-core operands carry them
+ * (input modes 3 and 4): each row scaled by the power of two that brings its
+ * largest magnitude into [2^14, 2^15), then written as a sum of FP16 terms,
+ * each the round-to-nearest-even of what the earlier terms left: two terms
+ * (hi + lo, mode 3) or three (mode 4). Other modes round element by element. */
+static void round_inputs(float *v, size_t count, size_t width, int mode)
+{
+    if (mode != 3 && mode != 4) {
+        round_rows(v, count * width, mode);
+        return;
+    }
+    for (size_t r = 0; r < count; r++) {
+        float *row = v + r * width;
+        float peak = 0.0f;
+        for (size_t c = 0; c < width; c++) {
+            peak = fmaxf(peak, fabsf(row[c]));
+        }
+        if (peak == 0.0f || !isfinite(peak)) {
+            continue;
+        }
+        int e;
+        frexpf(peak, &e);  /* peak = m * 2^e, m in [0.5, 1) */
+        const int shift = 15 - e;  /* peak * 2^shift in [2^14, 2^15) */
+        for (size_t c = 0; c < width; c++) {
+            const float y = ldexpf(row[c], shift);
+            float left = y, sum = 0.0f;
+            for (int term = 0; term < mode - 1; term++) {
+                const float part = (float)(_Float16)left;
+                sum += part;
+                left = y - sum;
+            }
+            row[c] = ldexpf(sum, -shift);
         }
     }
 }
@@ -707,7 +745,7 @@ int oracle_forward(oracle_model *m, const int64_t *ids, size_t count, float *log
         float *keys = m->keys + (size_t)layer * m->context * KV;
         float *values = m->values + (size_t)layer * m->context * KV;
         oracle_norm(m->norms[layer][0], x, normed, H, count);
-        round_rows(normed, count * H, input_rounding);
+        round_inputs(normed, count, H, input_rounding);
         oracle_project_fp8(m->linear[layer][0], m->scale[layer][0], normed, q, Q, H, count);
         oracle_project_fp8(m->linear[layer][1], m->scale[layer][1], normed, k, KV, H, count);
         oracle_project_fp8(m->linear[layer][2], m->scale[layer][2], normed, v, KV, H, count);
@@ -717,16 +755,16 @@ int oracle_forward(oracle_model *m, const int64_t *ids, size_t count, float *log
         round_rows(keys + m->length * KV, count * KV, kv_rounding);
         round_rows(values + m->length * KV, count * KV, kv_rounding);
         oracle_attention(rq, keys, values, attn, count, m->length, NULL);
-        round_rows(attn, count * Q, input_rounding);
+        round_inputs(attn, count, Q, input_rounding);
         oracle_project_fp8(m->linear[layer][3], m->scale[layer][3], attn, o, H, Q, count);
         oracle_element(x, o, residual, count * H, 0);
         oracle_norm(m->norms[layer][1], residual, normed, H, count);
-        round_rows(normed, count * H, input_rounding);
+        round_inputs(normed, count, H, input_rounding);
         oracle_project_fp8(m->linear[layer][4], m->scale[layer][4], normed, gate, F, H, count);
         oracle_project_fp8(m->linear[layer][5], m->scale[layer][5], normed, up, F, H, count);
         oracle_element(gate, gate, gated, count * F, 1);
         oracle_element(gated, up, gated, count * F, 2);
-        round_rows(gated, count * F, input_rounding);
+        round_inputs(gated, count, F, input_rounding);
         oracle_project_fp8(m->linear[layer][6], m->scale[layer][6], gated, down, H, F, count);
         oracle_element(residual, down, x, count * H, 0);
         if (trace) {
