@@ -248,6 +248,52 @@ static void kahan_dot_group(const float *w, const float *x, size_t stride, size_
     }
 }
 
+/* Precision-study knob (default 0: the Kahan lane sums above). A positive
+ * value n models a tensor core's FP32 accumulation as measured on earlier
+ * NVIDIA parts (Fasi, Higham, Mikaitis, Pranesh, "Numerical behavior of
+ * NVIDIA tensor cores", PeerJ Computer Science 7:e330, 2021): products exact,
+ * each block of 16 products added to the accumulator and the sum truncated
+ * toward zero to FP32, over chains of n blocks (the kernels split K over CTAs
+ * and accumulators) whose results are added in FP32. A model for studies
+ * only, not a statement of how a B200 rounds. */
+static int accumulation_study;
+
+void oracle_set_accumulation(int mode)
+{
+    accumulation_study = mode;
+}
+
+static float toward_zero(double s)
+{
+    float f = (float)s;
+    if (fabs((double)f) > fabs(s)) {
+        f = nextafterf(f, 0.0f);
+    }
+    return f;
+}
+
+/* Chains of `chain` blocks of 16 products, each accumulated as above; the
+ * chains' results added in FP32 (round to nearest) in order. */
+static float truncated_dot(const float *w, const float *x, size_t cols, size_t chain)
+{
+    float total = 0.0f;
+    const size_t span = 16 * chain;
+    for (size_t k0 = 0; k0 < cols; k0 += span) {
+        size_t k1 = k0 + span < cols ? k0 + span : cols;
+        float acc = 0.0f;
+        for (size_t c0 = k0; c0 < k1; c0 += 16) {
+            size_t c1 = c0 + 16 < k1 ? c0 + 16 : k1;
+            double s = acc;
+            for (size_t c = c0; c < c1; c++) {
+                s += (double)w[c] * (double)x[c];
+            }
+            acc = toward_zero(s);
+        }
+        total += acc;
+    }
+    return total;
+}
+
 void oracle_project(const float *weights, const float *input, float *output,
     size_t rows, size_t cols, size_t count)
 {
@@ -293,6 +339,12 @@ void oracle_project_fp8(const unsigned char *packed, float scale, const float *i
                 for (size_t r = 0; r < nr; r++) {
                     const float *w = row_values + r * cols;
                     size_t token = t0;
+                    if (accumulation_study) {
+                        for (; token < t1; token++) {
+                            output[token * rows + r0 + r] = truncated_dot(w, input + token * cols, cols,
+                                (size_t)accumulation_study);
+                        }
+                    }
                     for (; token + ORACLE_GROUP <= t1; token += ORACLE_GROUP) {
                         kahan_dot_group(w, input + token * cols, cols, cols, &output[token * rows + r0 + r], rows);
                     }

@@ -51,6 +51,7 @@ int oracle_threads(void);
 /* Precision study only (default 0,0 = FP32 as the reference): round stored KV
  * rows and/or projection inputs to 1 = BF16 or 2 = FP16 to measure drift. */
 void oracle_set_rounding(int kv, int input);
+void oracle_set_accumulation(int mode);
 
 /* ---- model level ---- */
 typedef struct oracle_model oracle_model;

@@ -30,6 +30,7 @@ class Oracle:
             "oracle_attention": (None, [P, P, P, P, SZ, SZ, P]),
             "oracle_set_threads": (None, [ctypes.c_int]),
             "oracle_set_rounding": (None, [ctypes.c_int, ctypes.c_int]),
+            "oracle_set_accumulation": (None, [ctypes.c_int]),
             "oracle_threads": (ctypes.c_int, []),
             "oracle_open": (P, [ctypes.c_char_p, SZ, ctypes.c_char_p, SZ]),
             "oracle_close": (None, [P]),

@@ -354,3 +354,30 @@ def test_fp16_hi_lo_inputs_meet_the_comparator_bound(oracle, checkpoint_path):
             assert misses > total // 2, (mode, misses, total)
         else:
             assert misses == 0, (mode, misses, total)
+
+
+def test_accumulation_study_model_truncates_toward_zero(oracle):
+    """The oracle's tensor-core accumulation model (oracle_set_accumulation,
+    a study knob that is off by default): on positive terms every result is at
+    most the exact dot product (blocks of 16 truncated toward zero), a single
+    chain over 9216 columns loses more than chains of 12 blocks, and with the
+    knob off the projection is the usual Kahan sum."""
+    rng = np.random.default_rng(5)
+    codes = rng.integers(0x30, 0x50, (64, 9216)).astype(np.uint8)
+    scale = np.float32(0.0011)
+    x = rng.uniform(0.5, 2.0, (3, 9216)).astype(np.float32)
+    w = np.array([oracle.fp8_decode(c) for c in range(256)], np.float32)[codes] * scale
+    exact = x.astype(np.float64) @ w.astype(np.float64).T
+    try:
+        plain = oracle.project_fp8(codes, scale, x)
+        oracle.lib.oracle_set_accumulation(1 << 30)
+        one_chain = oracle.project_fp8(codes, scale, x)
+        oracle.lib.oracle_set_accumulation(12)
+        short = oracle.project_fp8(codes, scale, x)
+    finally:
+        oracle.lib.oracle_set_accumulation(0)
+    assert np.abs(plain - exact).max() <= 1e-6 * exact.max()
+    assert np.all(one_chain <= exact) and np.all(short <= exact * (1 + 1e-7))
+    long_error = (exact - one_chain) / exact
+    short_error = np.abs(exact - short) / exact
+    assert long_error.mean() > 4 * short_error.mean() and long_error.max() < 1e-3
