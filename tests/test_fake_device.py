@@ -544,3 +544,66 @@ def test_reference_callers_over_fake_device(checkpoint_path, tmp_path):
         assert [int(x) for x in lines["turn %d" % t].split()] == want, "turn %d" % t
         pending = [want[-1]]  # generated but not yet fed: opens the next turn
     assert [int(x) for x in lines["replay"].split()] == want
+
+
+def history_hash(ids):
+    """fake_device.c's hash of a token history (FNV-1a over id + 1, 64-bit)."""
+    h = 1469598103934665603
+    for i in ids:
+        h = ((h ^ (int(i) + 1)) * 1099511628211) % (1 << 64)
+    return h
+
+
+def mix64(x):
+    """fake_device.c's mix64 over a uint64 array."""
+    with np.errstate(over="ignore"):
+        x = x + np.uint64(0x9E3779B97F4A7C15)
+        x = (x ^ (x >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        x = (x ^ (x >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+    return x ^ (x >> np.uint64(31))
+
+
+def trace_rows(h, which, rows):
+    """fake_device.c's traced rows of a call whose history hash is h."""
+    i = np.arange(rows * 3072, dtype=np.uint64)
+    key = np.uint64(h) ^ (np.uint64(which) << np.uint64(40)) ^ i
+    return ((mix64(key) >> np.uint64(40)).astype(np.float64) * 2.0 ** -24).astype(np.float32)
+
+
+def test_reference_comparator_over_fake_device(checkpoint_path, tmp_path):
+    """The reference's real-weight comparator (tests/compare_metal.c, with
+    the snapshot hook over lunelette_cuda_snapshot) over the CPU stand-in, on
+    fixtures that hold the stand-in's own logits, layer-25 rows and final-norm
+    rows: its whole protocol (teacher-forced steps, two reset cycles, the
+    256-position capacity check, destroy and recreate) passes and every
+    tensor matches exactly."""
+    from tests.test_gpu_c_callers import write_safetensors
+    lib = bind(fake_binary("liblunelette_cuda.so"))
+    rng = np.random.default_rng(2718)
+    pairs = []
+    for count, steps in ((6, 4), (248, 8)):
+        ids = [int(i) for i in rng.integers(1000, 131072, count)]
+        ids_path = tmp_path / ("ids%d.txt" % count)
+        ids_path.write_text(" ".join(str(i) for i in ids) + "\n")
+        history, feed, generated, tensors = [], ids, [], []
+        for step in range(steps):
+            history += feed
+            logits = reference(lib, history)
+            h = history_hash(history)
+            tensors += [("logits_%d" % step, logits.reshape(1, -1)),
+                        ("block_25_%d" % step, trace_rows(h, 25, len(feed)).reshape(1, len(feed), -1)),
+                        ("final_norm_%d" % step, trace_rows(h, 26, len(feed)).reshape(1, len(feed), -1))]
+            generated.append(greedy(logits))
+            feed = [generated[-1]]
+        fixture = tmp_path / ("fake%d.safetensors" % count)
+        write_safetensors(fixture, [("generated", np.asarray(generated, np.int64))] + tensors)
+        pairs += [str(ids_path), str(fixture)]
+    env = dict(os.environ, LUNELETTE_CUDA_TRACE="1")
+    proc = subprocess.run([fake_binary("compare_metal"), checkpoint_path] + pairs,
+                          capture_output=True, text=True, timeout=600, env=env)
+    assert proc.returncode == 0, (proc.stdout[-3000:], proc.stderr[-2000:])
+    out = proc.stdout
+    assert len([l for l in out.splitlines() if l.startswith("PASS /")]) == 24, out[-3000:]
+    metrics = [l for l in out.splitlines() if l.startswith("metrics ")]
+    assert len(metrics) == 72 and all(" mismatches0 " in l for l in metrics), out[-3000:]
+    assert out.count("PASS capacity256 append then reject") == 2 and "PASS destroy/recreate" in out
