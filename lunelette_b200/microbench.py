@@ -15,6 +15,7 @@ weights as tensor-memory A and the ordered K-range finish (the sum of the three
 kernels' device times, lunelette_cuda_gemm_fp8_timed).
 
     python -m lunelette_b200.microbench [--shapes q,gate,...] [--m 1,2,4,8] [--iters N]
+    python -m lunelette_b200.microbench --accumulation-probe   # tensor-core accumulation rounding
 """
 import argparse
 import json
@@ -350,6 +351,64 @@ def batch_step(checkpoint, sessions=64, seed=5, pool=None):
     return toks[0]
 
 
+def e4m3_values():
+    """The 256 E4M3FN codes as float64 (sign, 4 exponent bits with bias 7, 3
+    mantissa bits; exponent 0 subnormal; S.1111.111 NaN)."""
+    v = np.empty(256)
+    for c in range(256):
+        sign, e, m = (-1.0 if c & 0x80 else 1.0), (c >> 3) & 15, c & 7
+        if e == 15 and m == 7:
+            v[c] = np.nan
+        elif e == 0:
+            v[c] = sign * m / 8 * 2.0 ** -6
+        else:
+            v[c] = sign * (1 + m / 8) * 2.0 ** (e - 7)
+    return v
+
+
+def accumulation_probe(rows=18432, cols=9216, seed=3):
+    """How the tensor cores round the FP32 accumulation, measured through the
+    FP8 projection entry points on operands whose every product is exact:
+    positive codes 0x30..0x4F (0.5 .. 7.5), scale 1, activations k / 1024 with
+    k in [1024, 2048) (exact FP16 after the kernels' power-of-two row scale, so
+    the lo part is zero). The float64 dot product is then exact, and each
+    output's signed error in units of its FP32 ulp shows the rounding:
+    truncation toward zero leaves every error <= 0 and a mean of minus about
+    half an ulp per accumulation step; round to nearest, errors of both signs
+    around zero. Shapes: the small-block tcgen05 GEMM (16 tokens: one K range
+    per CTA, 144 chunks of 64 over two alternating accumulators), the CTA-pair
+    GEMM (128 tokens: two K ranges added in FP32 by the finish kernel) and the
+    mma.sync GEMV (4 tokens)."""
+    import torch
+    import lunelette_b200 as L
+    lib = L.library()
+    rng = np.random.default_rng(seed)
+    codes = rng.integers(0x30, 0x50, (rows, cols)).astype(np.uint8)
+    w = e4m3_values()[codes]
+    stream = torch.cuda.current_stream().cuda_stream
+    raw = torch.from_numpy(codes).cuda()
+    tiled = torch.zeros(-(-rows // 8) * 8 * (-(-cols // 128) * 128), dtype=torch.uint8, device="cuda")
+    assert lib.lunelette_cuda_tile_fp8(raw.data_ptr(), rows, cols, 0, tiled.data_ptr(), stream) == 0
+    out = {}
+    for name, entry, count in (("tcgen05 small-block GEMM", "lunelette_cuda_gemm_fp8", 16),
+                               ("tcgen05 CTA-pair GEMM", "lunelette_cuda_gemm_fp8", 128),
+                               ("mma.sync GEMV", "lunelette_cuda_gemv_fp8", 4)):
+        x = (rng.integers(1024, 2048, (count, cols)) / 1024.0).astype(np.float32)
+        d_x = torch.from_numpy(x).cuda()
+        y = torch.empty((count, rows), dtype=torch.float32, device="cuda")
+        assert getattr(lib, entry)(tiled.data_ptr(), rows, cols, 1.0, d_x.data_ptr(), None, count, y.data_ptr(),
+                                   stream) == 0
+        torch.cuda.synchronize()
+        exact = x.astype(np.float64) @ w.T
+        got = y.cpu().numpy().astype(np.float64)
+        ulp = np.spacing(exact.astype(np.float32)).astype(np.float64)
+        err = (got - exact) / ulp
+        out[name] = {"tokens": count, "outputs": int(err.size), "mean_ulp": float(err.mean()),
+                     "min_ulp": float(err.min()), "max_ulp": float(err.max()),
+                     "below": float((err < 0).mean()), "above": float((err > 0).mean())}
+    return out
+
+
 def batch_head_ab(checkpoint, sessions=64, steps=20, seed=9):
     """Batched decode steps of `sessions` sessions with 8-token prompts (short
     contexts: the step is the projections and the head) with the mma.sync head
@@ -410,11 +469,16 @@ def main():
     ap.add_argument("--batch-step", metavar="CHECKPOINT", default=None,
                     help="one batched decode step of ragged sessions between cudaProfilerStart/Stop")
     ap.add_argument("--batch-sessions", type=int, default=64)
+    ap.add_argument("--accumulation-probe", action="store_true",
+                    help="signed errors of the FP8 projections on exact-product operands (accumulation rounding)")
     ap.add_argument("--batch-head", metavar="CHECKPOINT", default=None,
                     help="batched step with the mma.sync and the tcgen05 head, ms per step")
     ap.add_argument("--prefill-gemm", metavar="COUNTS", default=None,
                     help="time the tcgen05 prefill projections at these token counts (e.g. 256,32)")
     args = ap.parse_args()
+    if args.accumulation_probe:
+        print(json.dumps(accumulation_probe()))
+        return
     if args.batch_head:
         print(json.dumps(batch_head_ab(args.batch_head, args.batch_sessions)))
         return
