@@ -381,3 +381,17 @@ def test_accumulation_study_model_truncates_toward_zero(oracle):
     long_error = (exact - one_chain) / exact
     short_error = np.abs(exact - short) / exact
     assert long_error.mean() > 4 * short_error.mean() and long_error.max() < 1e-3
+
+
+def test_accumulation_probe_decode_table_matches_frozen_pytorch_table():
+    """The E4M3 table the accumulation probe (lunelette_b200/microbench.py)
+    computes its exact products from equals the reference's frozen PyTorch
+    table bit for bit, NaN codes included."""
+    from lunelette_b200.microbench import e4m3_values
+    g = load("fp8_golden.json")
+    values = e4m3_values()
+    for code in range(256):
+        if code in g["nan_codes"]:
+            assert np.isnan(values[code])
+        else:
+            assert bits(np.float32(values[code])) == g["bits"][code], code
