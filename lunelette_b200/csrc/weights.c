@@ -249,19 +249,47 @@ int lun_weights_admission(const lun_weights *weights, size_t index, int compact,
             return -1;
         }
     }
+    table->nan_only = 1;
     for (unsigned code = 0; code < 256; code++) {
         float decoded = lun_e4m3_to_f32((unsigned char)code);
         float product = decoded * scale;
         table->allowed[code] = compact ? (isfinite(product) && (decoded == 0 || isnormal(product)))
                                        : isfinite(product);
+        table->nan_only &= table->allowed[code] == ((code & 0x7Fu) != 0x7Fu);
     }
     return 0;
+}
+
+/* Whether any byte has its low seven bits all ones (an E4M3 NaN code), eight
+ * bytes at a time: a byte of y = (w & 0x7F..) ^ 0x7F.. is zero exactly for such
+ * a code, and (y - 0x01..) & ~y & 0x80.. is nonzero exactly when some byte of y
+ * is zero (no byte of y has its top bit set). Branch-free, so it vectorizes. */
+static int has_nan_code(const unsigned char *p, size_t n)
+{
+    const uint64_t low7 = 0x7F7F7F7F7F7F7F7Full, ones = 0x0101010101010101ull, tops = 0x8080808080808080ull;
+    uint64_t found = 0;
+    size_t i = 0;
+    for (; i + 8 <= n; i += 8) {
+        uint64_t w;
+        memcpy(&w, p + i, 8);
+        const uint64_t y = (w & low7) ^ low7;
+        found |= (y - ones) & ~y & tops;
+    }
+    for (; i < n; i++) {
+        found |= (p[i] & 0x7Fu) == 0x7Fu;
+    }
+    return found != 0;
 }
 
 int lun_admit_codes(const lun_weights *weights, size_t index, const lun_admission *table,
     const unsigned char *codes, size_t count, uint64_t offset, float scale,
     char *error, size_t capacity)
 {
+    /* the usual table (only NaN codes rejected): a word-wide scan, and the byte
+     * loop below only to name the first rejected byte */
+    if (table->nan_only && !has_nan_code(codes, count)) {
+        return 0;
+    }
     for (size_t i = 0; i < count; i++) {
         if (!table->allowed[codes[i]]) {
             snprintf(error, capacity, "tensor %s byte %llu code 0x%02x: code x scale %.9g is not admitted "

@@ -54,6 +54,7 @@ void lun_weights_close(lun_weights *weights);
  * Builds the 256-entry table once per call of lun_weights_admission(). */
 typedef struct {
     unsigned char allowed[256];
+    int nan_only; /* the rejected codes are exactly the two NaN codes 0x7F and 0xFF */
 } lun_admission;
 int lun_weights_admission(const lun_weights *weights, size_t index, int compact,
     lun_admission *table, char *error, size_t capacity);

@@ -532,3 +532,22 @@ def test_parser_and_admission_memory_safe_under_sanitizers(checkpoint_path, tmp_
         run.stderr[-2000:]
     verdicts = [line.split(" ", 1)[0] for line in run.stdout.splitlines()]
     assert verdicts == ["0", "-1", "-1", "-1"], run.stdout
+
+
+def test_admission_finds_nan_codes_at_every_word_position(corrupt_copy):
+    """The admission scan tests eight bytes at a time when only the NaN codes
+    are rejected: a NaN code (0x7F or 0xFF) at each position of an 8-byte word,
+    at a tensor's first and last byte and in the bytes after its last whole
+    word is still found and named by its byte offset."""
+    q = "language_model.model.layers.7.mlp.down_proj.weight"
+    base = tensor_offset(corrupt_copy, q)
+    size = 3072 * 9216
+    for offset, code in [(8 * 1000 + k, 0x7F if k % 2 else 0xFF) for k in range(8)] + \
+                        [(0, 0xFF), (size - 1, 0x7F), (size - 3, 0xFF), (4 << 20, 0x7F), ((4 << 20) - 1, 0xFF)]:
+        old = patch(corrupt_copy, base + offset, bytes([code]))
+        try:
+            with pytest.raises(L.LuneletteError, match="byte %d code 0x%02x" % (offset, code)):
+                L.validate_checkpoint(corrupt_copy, L.COMPACT_FP8_ARITHMETIC)
+        finally:
+            patch(corrupt_copy, base + offset, old)
+    L.validate_checkpoint(corrupt_copy, L.COMPACT_FP8_ARITHMETIC)
